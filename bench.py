@@ -1,0 +1,397 @@
+"""Benchmark of the jax4j B200 engine's hot path (one JSON line on rank 0).
+
+Workload (the metric's "Q8_0 dequant-GEMV GB/s"): y[8, 4096] = W x with W a
+4096 x 4096 weight drawn 0.02*N(0,1) by the engine's own counter PRNG (PrngKey(0).split(2)[1])
+and quantised Q8_0 on the device, x [8, 4096] ~ N(0,1) (split(2)[0]). A step is one GEMV call;
+`value` is algorithmic bytes (GGUF weight bytes + x + y) per second over all GPUs.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl engine|reference]
+                  [--config q8_0_b8|q4_k_b1|q4_k_b16]
+
+N > 1 (launched by torchrun, one rank per GPU): each rank owns a 4096-row slab of a (4096 N)-row
+weight (weak scaling), computes its y slab and all-gathers the slabs over NCCL each step.
+
+Timing: W untimed warm-up steps, then exactly K steps replayed from a CUDA graph, bracketed by a
+barrier and device synchronisation, timed with CUDA events on the launching stream, max over
+ranks. The weights rotate over enough identical copies (>= 2x L2) that every step streams its
+weight from HBM. nvidia-smi samples clocks during the timed region.
+"""
+from __future__ import annotations
+
+import argparse
+import concurrent.futures
+import ctypes
+import json
+import math
+import os
+import re
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+CONFIGS = {
+    # name: (ggml type, rows per rank, cols, batch, label)
+    "q8_0_b8": (8, 4096, 4096, 8, "BASELINE configs[1]: GGUF Q8_0 matmul x[8,4096] . W[4096x4096]"),
+    "q4_k_b1": (12, 14336, 4096, 1, "BASELINE configs[2]: Q4_K decode GEMV B=1, W[14336x4096]"),
+    "q4_k_b16": (12, 14336, 4096, 16, "BASELINE configs[2]: Q4_K decode GEMV B=16, W[14336x4096]"),
+}
+TYPE_NAME = {8: "Q8_0", 12: "Q4_K", 2: "Q4_0", 42: "Q2_0"}
+BLOCK = {8: (32, 34), 12: (256, 144), 2: (32, 18), 42: (128, 34)}
+METRIC = "Q4_K/Q8_0 dequant-GEMV GB/s vs HBM peak; fused-JIT tape steps/s at 1/2/4/8 B200"
+
+
+def alg_bytes(qtype, rows, cols, batch):
+    be, bb = BLOCK[qtype]
+    return rows * cols // be * bb + batch * cols * 4 + batch * rows * 4
+
+
+def measured_peaks():
+    path = os.path.join(HERE, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def profiled_traffic(cfg):
+    """Per-launch DRAM bytes of the GEMV kernel from the committed ncu summary, if any."""
+    path = os.path.join(HERE, "profiles", f"qgemv_{cfg}.md")
+    if not os.path.exists(path):
+        return None
+    m = re.search(r"traffic_bytes_per_launch:\s*([0-9]+)", open(path).read())
+    return int(m.group(1)) if m else None
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons while the GPU is busy."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "50"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sms, maxes, reasons = [], [], set()
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sms.append(float(parts[1]))
+                maxes.append(float(parts[2]))
+            except ValueError:
+                continue
+            names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        if not sms:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sms), "sm_max_mhz": max(maxes),
+                "reasons": sorted(reasons), "samples": len(sms)}
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+# ------------------------------------------------------------------------------------------------
+# CPU side: the oracle restatement of the reference's CPU path (baseline and --impl reference)
+# ------------------------------------------------------------------------------------------------
+
+def cpu_matvec_rate(qtype, rows, cols, batch, threads, budget_s, blob=None, x=None):
+    """Times the oracle's float-sequential quantMatvec (reference loop style) on a bounded row
+    sample split over `threads` host threads. Returns (GB/s of algorithmic bytes, sample text)."""
+    import numpy as np
+    sys.path.insert(0, HERE)
+    from oracle import oracle as o
+    if blob is None:
+        rng = np.random.default_rng(0)
+        w = (rng.standard_normal((rows, cols)) * 0.02).astype(np.float32)
+        blob = o.quantize(qtype, w)
+        x = rng.standard_normal((batch, cols)).astype(np.float32)
+    rb = o.quant_row_bytes(qtype, cols)
+    # calibrate: one row-block of 16 rows single-threaded
+    t0 = time.perf_counter()
+    o.quant_matvec(qtype, blob[:16 * rb], 16, cols, x)
+    per_row = (time.perf_counter() - t0) / 16
+    sample_rows = max(threads, min(rows, int(budget_s * threads / max(per_row, 1e-9))))
+    chunks = [(i * sample_rows // threads, (i + 1) * sample_rows // threads) for i in range(threads)]
+
+    def work(c):
+        r0, r1 = c
+        if r1 > r0:
+            o.quant_matvec(qtype, blob[r0 * rb:r1 * rb], r1 - r0, cols, x)
+
+    t0 = time.perf_counter()
+    if threads == 1:
+        work(chunks[0])
+    else:
+        with concurrent.futures.ThreadPoolExecutor(threads) as ex:
+            list(ex.map(work, chunks))
+    dt = time.perf_counter() - t0
+    nbytes = alg_bytes(qtype, sample_rows, cols, batch)
+    sample = (f"{sample_rows} of {rows} rows x {cols} cols, batch {batch}, "
+              f"{TYPE_NAME[qtype]} float-sequential oracle port, {threads} thread(s)")
+    return nbytes / dt / 1e9, sample, dt
+
+
+def run_reference(args):
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return 0
+    qtype, rows, cols, batch, label = CONFIGS[args.config]
+    threads = os.cpu_count() or 1
+    total_steps = args.steps + args.warmup
+    budget = max(0.05, min(2.0, 90.0 / max(total_steps, 1)))  # whole run within ~1.5 minutes
+    import numpy as np
+    sys.path.insert(0, HERE)
+    from oracle import oracle as o
+    rng = np.random.default_rng(0)
+    w = (rng.standard_normal((rows, cols)) * 0.02).astype(np.float32)
+    blob = o.quantize(qtype, w)
+    x = rng.standard_normal((batch, cols)).astype(np.float32)
+    for _ in range(args.warmup):
+        cpu_matvec_rate(qtype, rows, cols, batch, threads, budget, blob, x)
+    rates, times, sample = [], [], ""
+    for _ in range(args.steps):
+        r, sample, dt = cpu_matvec_rate(qtype, rows, cols, batch, threads, budget, blob, x)
+        rates.append(r)
+        times.append(dt)
+    value = statistics.median(rates)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1e3 * statistics.median(times), 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": label, "batch": batch, "rows": rows, "cols": cols,
+                   "quant": TYPE_NAME[qtype]},
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads,
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------------------------------------
+# engine arm
+# ------------------------------------------------------------------------------------------------
+
+def run_engine(args):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    sys.path.insert(0, HERE)
+    from jax4j_b200 import _lib
+    from jax4j_b200.backend import B200Backend
+    from jax4j_b200.prng import PrngKey
+
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    be = B200Backend(local)
+    qtype, rows, cols, batch, label = CONFIGS[args.config]
+    per_call = alg_bytes(qtype, rows, cols, batch)
+    dev = torch.device("cuda", local)
+
+    # ---- synthetic inputs, generated on the device by the engine ----
+    kx, kw = PrngKey.of(0).split(2)
+    x = be.random_normal(kx.seed, kx.counter, (batch, cols))
+    w32 = be.random_normal(kw.seed, kw.counter + rank * rows * cols, (rows, cols))
+    w32 = be.scalar("MUL", w32, 0.02)
+    blob = be.quantize(w32, qtype)
+    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
+    copies = max(2, math.ceil(2 * l2 / blob.numel()))
+    weights = [be.upload_quantized(blob, qtype, (rows, cols)) for _ in range(copies)]
+    del w32, blob
+    y = torch.empty(batch * rows, dtype=torch.float32, device=dev)
+    y_all = torch.empty(world * batch * rows, dtype=torch.float32, device=dev) if world > 1 else None
+    torch.cuda.synchronize()
+
+    def gemv(i, stream):
+        _lib.call("j4b_quant_matvec", ctypes.c_void_p(weights[i % copies].handle), x.ptr, 0,
+                  y.data_ptr(), batch, stream)
+
+    def step(i, with_collective=True):
+        s = torch.cuda.current_stream().cuda_stream
+        gemv(i, s)
+        if world > 1 and with_collective:
+            dist.all_gather_into_tensor(y_all, y)
+
+    def capture(n, with_collective=True):
+        g = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            step(0, with_collective)  # warm the path on the capture stream
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        with torch.cuda.graph(g):
+            for i in range(n):
+                step(i, with_collective)
+        return g
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def timed(g, n_rep=1):
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        start.record()
+        for _ in range(n_rep):
+            g.replay()
+        end.record()
+        barrier()
+        ms = start.elapsed_time(end)
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    K, W = args.steps, max(3, args.warmup)
+    warm = capture(W)
+    main = capture(K)
+    kernel_only = capture(K, with_collective=False) if world > 1 else main
+    # soak ~0.5 s so clocks are at their loaded state, then time K steps while sampling clocks
+    warm.replay()
+    torch.cuda.synchronize()
+    soak_t0 = time.perf_counter()
+    with ClockSampler(local) as clocks:
+        while time.perf_counter() - soak_t0 < 0.5:
+            warm.replay()
+            torch.cuda.synchronize()
+        ms = timed(main)
+        kernel_ms = timed(kernel_only) if world > 1 else ms
+        # keep sampling for a short tail so short timed regions still get samples
+        tail = time.perf_counter()
+        while time.perf_counter() - tail < 0.3:
+            main.replay()
+            torch.cuda.synchronize()
+    clk = clocks.summary()
+
+    value = world * per_call * K / (ms * 1e-3) / 1e9
+    kernel_avg_us = kernel_ms * 1e3 / K
+    achieved = per_call / (kernel_avg_us * 1e-6) / 1e9
+    peak, peak_kind = measured_peaks()
+
+    # ---- end to end through the public API, host buffers, copies inside the timed region ----
+    x_host = torch.from_numpy(np.ascontiguousarray(be.download(x))).pin_memory()
+    y_host = torch.empty(batch * rows, dtype=torch.float32).pin_memory()
+    e2e_steps = min(K, 2000)
+    xin = be.full(0.0, (batch, cols))
+    stream = torch.cuda.current_stream().cuda_stream
+    barrier()
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_start.record()
+    for i in range(e2e_steps):
+        _lib.call("j4b_h2d", xin.ptr, ctypes.c_void_p(x_host.data_ptr()), x_host.numel() * 4, stream)
+        out = be.quant_matvec(weights[i % copies], xin)
+        _lib.call("j4b_d2h", ctypes.c_void_p(y_host.data_ptr()), out.ptr, y_host.numel() * 4, stream)
+    e_end.record()
+    barrier()
+    e_ms = e_start.elapsed_time(e_end)
+    if world > 1:
+        t = torch.tensor([e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e_ms = float(t.item())
+    e2e_value = world * per_call * e2e_steps / (e_ms * 1e-3) / 1e9
+
+    # ---- CPU baseline (rank 0, N = 1 only) ----
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rate, sample, _ = cpu_matvec_rate(qtype, rows, cols, batch, 1, 10.0)
+        cpu = {"value": round(rate, 4), "unit": "GB/s", "cores": 1, "kind": "port",
+               "sample": sample + f" (host has {os.cpu_count()} cores)"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": K, "warmup": W, "ms_per_step": round(ms / K, 6), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {
+                "workload": label, "quant": TYPE_NAME[qtype], "batch": batch,
+                "rows_per_gpu": rows, "cols": cols, "bytes_per_step_per_gpu": per_call,
+                "compute": "Q8/Q4 codes -> fp16 mma.sync, x split fp16 hi+lo, fp32 accumulate",
+                "l2": f"weights rotate over {copies} copies ({copies * per_call / 1e6:.0f} MB > 2x L2)",
+                "parallelism": "replica" if world == 1 else f"row-shard x{world} + NCCL all-gather",
+                "timing": "CUDA graph of K GEMV calls, CUDA events, max over ranks",
+            },
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "traffic": profiled_traffic(args.config),
+                         "peak_source": f"{peak_kind} MEASURED_PEAKS.json hbm_gbs" if peak_kind == "measured" else "fallback 6.65 TB/s",
+                         "kernel": "qgemv_kernel", "kernel_avg_us": round(kernel_avg_us, 3)},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e_value, 3), "unit": "GB/s",
+                    "h2d_bytes_per_step": batch * cols * 4, "d2h_bytes_per_step": batch * rows * 4},
+            "gpu_launches": K,
+            "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"],
+                       "reasons": clk["reasons"], "samples": clk["samples"]},
+        }
+        print(json.dumps(line), flush=True)
+    del main, warm, kernel_only
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20000)
+    p.add_argument("--warmup", type=int, default=200)
+    p.add_argument("--impl", choices=["engine", "reference"], default="engine")
+    p.add_argument("--config", choices=sorted(CONFIGS), default="q8_0_b8")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    args = p.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_engine(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,186 @@
+/*
+ * jax4j_b200 -- C ABI of the B200 (sm_100a) engine behind JAX4J's engine SPI.
+ *
+ * One entry point per reference SPI operation. A thin binding (Java FFM in the JAX4J tree, or
+ * ctypes here) maps each ComputeBackend / QuantizedOps method to one call below, as the
+ * reference's CudaRuntime maps its methods onto cu* driver calls. Reference interfaces are cited
+ * by their path inside the jax4j project, with these prefixes:
+ *   core/ = jax4j-core/src/main/java/com/nablatensor/jax4j/
+ *   cuda/ = jax4j-engine-cuda/src/main/java/com/nablatensor/jax4j/
+ *
+ * Conventions
+ *   - Every function returns an int status (J4B_OK == 0). On failure j4b_last_error() returns a
+ *     message for the calling thread. J4B_EINVAL is raised for shape/argument violations before
+ *     any launch (the reference's IllegalArgumentException), J4B_EUNSUPPORTED for unsupported
+ *     types (UnsupportedOperationException), J4B_ECUDA for driver/runtime failures
+ *     (RuntimeException "<op> failed: <CUDA error>").
+ *   - Device buffers are plain device addresses carried as uint64_t (j4b_buf). Any allocator may
+ *     produce them (j4b_alloc, or a framework such as PyTorch); f32 tensors are dense row-major.
+ *   - Launches are asynchronous on the given stream (a cudaStream_t passed as void*). A NULL
+ *     stream selects the engine's own per-device non-blocking stream created by j4b_init.
+ *   - Shapes are (const int64_t* dims, int rank); rank <= 8.
+ */
+#ifndef JAX4J_B200_H
+#define JAX4J_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define J4B_OK 0
+#define J4B_EINVAL 1
+#define J4B_ENOMEM 2
+#define J4B_ECUDA 3
+#define J4B_EUNSUPPORTED 4
+#define J4B_ENOTINIT 5
+#define J4B_ETIMEOUT 6
+
+typedef uint64_t j4b_buf;          /* device address of a dense f32 buffer */
+typedef void* j4b_stream;          /* cudaStream_t; NULL = engine stream of the device */
+typedef struct j4b_qweight* j4b_qweight_t; /* opaque quantized matrix (QuantizedOps buffer) */
+
+/* GGUF type ids: core/tensor/QuantType.java:4-13 */
+#define J4B_Q4_0 2
+#define J4B_Q8_0 8
+#define J4B_Q4_K 12
+#define J4B_Q2_0 42
+
+/* Op codes: the ordinal order of core/tensor/Op.java:19-23 (the reference's CUDA kernels
+ * switch on the same enum, cuda/backend/cuda/CudaBackend.java:1053-1079). */
+#define J4B_ADD 0
+#define J4B_SUB 1
+#define J4B_MUL 2
+#define J4B_DIV 3
+#define J4B_MAX 4
+#define J4B_MIN 5
+#define J4B_NEG 6
+#define J4B_EXP 7
+#define J4B_LOG 8
+#define J4B_SQRT 9
+#define J4B_RSQRT 10
+#define J4B_TANH 11
+#define J4B_SIGMOID 12
+#define J4B_RELU 13
+#define J4B_ABS 14
+#define J4B_SIGN 15
+
+/* Engine counters; the names follow the reference GPU backends' diagnostics() records
+ * (core/tensor/spi/GpuTensorBackend.java, read by core/tensor/bench/GpuComparison.java:35-56). */
+typedef struct j4b_diagnostics {
+  uint64_t dispatches;    /* kernel launches issued by the engine */
+  uint64_t allocations;   /* device allocations made by the engine */
+  uint64_t releases;      /* device frees made by the engine */
+  uint64_t h2d_bytes;     /* host->device bytes copied by j4b_h2d / uploads */
+  uint64_t d2h_bytes;     /* device->host bytes copied by j4b_d2h */
+  uint64_t compilations;  /* runtime kernel compilations (fused tapes) */
+} j4b_diagnostics;
+
+/* ---- lifecycle: cuda/backend/cuda/CudaRuntime.java:140-211 (cuInit, context on device 0) --- */
+
+/* Initialises the listed devices (NULL/0 = device 0). Idempotent. */
+int j4b_init(const int* devices, int n);
+/* ComputeBackend.isAvailable (core/tensor/spi/ComputeBackend.java:43): never fails; count 0
+ * when no usable GPU exists. */
+int j4b_device_count(int* count);
+int j4b_device_name(int dev, char* buf, size_t len);
+int j4b_sm_count(int dev, int* count);
+int j4b_get_stream(int dev, j4b_stream* stream);
+/* ComputeBackend.sync (core/tensor/spi/ComputeBackend.java:276-277) */
+int j4b_sync(int dev);
+int j4b_last_error(char* buf, size_t len);
+int j4b_get_diagnostics(j4b_diagnostics* out);
+
+/* ---- memory: CudaRuntime.java:252-290 (malloc/pool), :432-485 (HtoD/DtoH) ---- */
+
+int j4b_alloc(int dev, size_t bytes, j4b_buf* out);
+/* Stream-ordered free on the device's engine stream: safe to call from any thread, and on a
+ * value of 0 (no-op). Replaces the reference's pending-free queue (CudaRuntime.java:407-430). */
+int j4b_free(j4b_buf buf);
+/* ComputeBackend.upload (ComputeBackend.java:48) */
+int j4b_h2d(j4b_buf dst, const void* src, size_t bytes, j4b_stream stream);
+/* ComputeBackend.download (ComputeBackend.java:87): synchronises the stream first. */
+int j4b_d2h(void* dst, j4b_buf src, size_t bytes, j4b_stream stream);
+int j4b_d2d(j4b_buf dst, j4b_buf src, size_t bytes, j4b_stream stream);
+
+/* ---- dense SPI primitives (core/tensor/spi/ComputeBackend.java:48-280) ---- */
+
+/* full: ComputeBackend.java:78-85 */
+int j4b_fill(j4b_buf out, int64_t n, float value, j4b_stream s);
+/* binary: ComputeBackend.java:89 (equal element counts; CpuBackend.java:61-94 semantics) */
+int j4b_binary(int op, j4b_buf a, j4b_buf b, j4b_buf out, int64_t n, j4b_stream s);
+/* scalar: ComputeBackend.java:91 (value cast to float first, CpuBackend.java:101) */
+int j4b_scalar(int op, j4b_buf a, double value, j4b_buf out, int64_t n, j4b_stream s);
+/* unary: ComputeBackend.java:93 */
+int j4b_unary(int op, j4b_buf a, j4b_buf out, int64_t n, j4b_stream s);
+/* transpose: ComputeBackend.java:95 (rank 2) */
+int j4b_transpose(j4b_buf a, j4b_buf out, int64_t rows, int64_t cols, j4b_stream s);
+/* reduceSum / reduceMax: ComputeBackend.java:150-153 (out is one float) */
+int j4b_reduce_sum(j4b_buf a, int64_t n, j4b_buf out, j4b_stream s);
+int j4b_reduce_max(j4b_buf a, int64_t n, j4b_buf out, j4b_stream s);
+/* sumAxis / maxAxis / argMaxAxis: ComputeBackend.java:158-172, the tensor viewed as
+ * [outer, axis, inner]; out is [outer, inner] (keepDims only changes the shape). sumAxis0
+ * (ComputeBackend.java:156) is outer = 1. */
+int j4b_sum_axis(j4b_buf a, int64_t outer, int64_t axis, int64_t inner, j4b_buf out,
+                 j4b_stream s);
+int j4b_max_axis(j4b_buf a, int64_t outer, int64_t axis, int64_t inner, j4b_buf out,
+                 j4b_stream s);
+int j4b_argmax_axis(j4b_buf a, int64_t outer, int64_t axis, int64_t inner, j4b_buf out,
+                    j4b_stream s);
+/* maxAxisBackward: ComputeBackend.java:174-177 */
+int j4b_max_axis_backward(j4b_buf upstream, j4b_buf input, int64_t outer, int64_t axis,
+                          int64_t inner, j4b_buf out, j4b_stream s);
+/* broadcastTo: ComputeBackend.java:205-206 (numpy rules, any rank <= 8) */
+int j4b_broadcast_to(j4b_buf a, const int64_t* src_dims, int src_rank, const int64_t* dst_dims,
+                     int dst_rank, j4b_buf out, j4b_stream s);
+/* reindex / scatterAdd: ComputeBackend.java:247-274. map is a device int32 array; -1 means
+ * zero (reindex) or discard (scatterAdd). The kernels treat entries outside [-1, n) as -1; the
+ * binding validates the static map once, on the host, when it uploads it (the reference's
+ * "index out of bounds" check, ComputeBackend.java:254-255, 269-270). */
+int j4b_reindex(j4b_buf a, int64_t n_src, j4b_buf map, int64_t n_dst, j4b_buf out,
+                j4b_stream s);
+int j4b_scatter_add(j4b_buf a, int64_t n_src, j4b_buf map, int64_t n_dst, j4b_buf out,
+                    j4b_stream s);
+/* reluBackward: ComputeBackend.java:202-203 */
+int j4b_relu_backward(j4b_buf upstream, j4b_buf input, j4b_buf out, int64_t n, j4b_stream s);
+/* randomUniform / randomNormal: ComputeBackend.java:50-76 (bit-exact uniforms) */
+int j4b_random_uniform(int64_t seed, int64_t counter, j4b_buf out, int64_t n, j4b_stream s);
+int j4b_random_normal(int64_t seed, int64_t counter, j4b_buf out, int64_t n, j4b_stream s);
+/* matmul / batchedMatmul: ComputeBackend.java:97-101. out[b] = a[b] (m x k) . b[b] (k x n),
+ * row-major f32. precision 0 = fp32-accurate (rel 1e-4), 1 = bf16 tensor-core operands. */
+int j4b_matmul(j4b_buf a, j4b_buf b, j4b_buf out, int64_t batch, int64_t m, int64_t k,
+               int64_t n, int precision, j4b_stream s);
+
+/* ---- QuantizedOps: core/tensor/spi/QuantizedOps.java:19-34 ---- */
+
+/* supportedQuantTypes (QuantizedOps.java:21): writes up to cap ids, returns the count in *n. */
+int j4b_quant_supported(int* ids, int cap, int* n);
+/* Bytes of a rows x cols matrix in GGUF blocks (QuantType.byteSizeFor, QuantType.java:46-53). */
+int j4b_quant_bytes(int ggml_type, int64_t rows, int64_t cols, int64_t* bytes);
+/* uploadQuantized (QuantizedOps.java:23-24): copies a host GGUF blob to the device and repacks
+ * it into the engine's tensor-core fragment layout (same byte count). */
+int j4b_quant_upload(int dev, const void* blocks, size_t bytes, int ggml_type, int64_t rows,
+                     int64_t cols, j4b_qweight_t* out);
+/* Same, from a GGUF blob already resident on the device (e.g. written by j4b_quantize). */
+int j4b_quant_upload_device(int dev, j4b_buf blocks, size_t bytes, int ggml_type, int64_t rows,
+                            int64_t cols, j4b_qweight_t* out);
+int j4b_quant_free(j4b_qweight_t w);
+int j4b_quant_shape(j4b_qweight_t w, int* ggml_type, int64_t* rows, int64_t* cols);
+/* quantMatvec / quantMatvecAdd (QuantizedOps.java:26-30), batched: x [batch, cols] f32,
+ * add [batch, rows] f32 or 0, y [batch, rows] f32. batch = 1 is the reference call. */
+int j4b_quant_matvec(j4b_qweight_t w, j4b_buf x, j4b_buf add, j4b_buf y, int64_t batch,
+                     j4b_stream s);
+/* quantGatherRow (QuantizedOps.java:32-33): bit-exact dequantised row, out [cols] f32. */
+int j4b_quant_gather_row(j4b_qweight_t w, int64_t row, j4b_buf out, j4b_stream s);
+/* Encoder (no reference counterpart; producers of GGUF data): w [rows, cols] f32 on the device
+ * -> GGUF blocks on the device. Byte-identical to the published block encoders restated in the
+ * oracle. */
+int j4b_quantize(int ggml_type, j4b_buf w, int64_t rows, int64_t cols, j4b_buf out_blocks,
+                 j4b_stream s);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,75 @@
+// Internal helpers shared by the engine's translation units: status/error plumbing, the
+// per-device context table and launch bookkeeping.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <string>
+
+#include "../../include/jax4j_b200.h"
+
+namespace j4b {
+
+constexpr int kMaxDevices = 16;
+
+struct DeviceCtx {
+  bool ready = false;
+  int sm_count = 0;
+  cudaStream_t stream = nullptr;
+  char name[256] = {0};
+};
+
+DeviceCtx* device_ctx(int dev);          // nullptr if dev is out of range
+int ensure_device(int dev);              // lazily initialises dev; returns status
+int device_of(const void* ptr, int* dev);  // device owning a device pointer
+cudaStream_t resolve_stream(int dev, j4b_stream s);
+
+// Sets the calling thread's last error and returns code.
+int set_error(int code, const char* fmt, ...);
+int cuda_error(cudaError_t e, const char* what);
+
+struct Counters {
+  std::atomic<uint64_t> dispatches{0}, allocations{0}, releases{0}, h2d{0}, d2h{0},
+      compilations{0};
+};
+Counters& counters();
+
+inline void count_launch(uint64_t n = 1) { counters().dispatches += n; }
+
+// RAII guard restoring the caller's current device.
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+}  // namespace j4b
+
+#define J4B_CHECK_LAUNCH(what)                                 \
+  do {                                                         \
+    cudaError_t e_ = cudaGetLastError();                       \
+    if (e_ != cudaSuccess) return ::j4b::cuda_error(e_, what); \
+    ::j4b::count_launch();                                     \
+  } while (0)
+
+#define J4B_CUDA(call, what)                                   \
+  do {                                                         \
+    cudaError_t e_ = (call);                                   \
+    if (e_ != cudaSuccess) return ::j4b::cuda_error(e_, what); \
+  } while (0)
+
+#define J4B_REQUIRE(cond, ...)                                   \
+  do {                                                           \
+    if (!(cond)) return ::j4b::set_error(J4B_EINVAL, __VA_ARGS__); \
+  } while (0)

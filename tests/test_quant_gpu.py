@@ -1,0 +1,130 @@
+"""GPU parity of the quantized path (QuantizedOps) against the C oracle.
+
+Bars (stated per test): dequantised weights and encoded blocks bit-exact; GEMV outputs within a
+normwise relative error of 1e-4 of the exact (float64) product of the dequantised weights --
+max|y - y_exact| / max|y_exact| <= 1e-4 -- the fp32-accumulate bar.
+"""
+import numpy as np
+import pytest
+import torch
+
+Q4_0, Q8_0, Q4_K, Q2_0 = 2, 8, 12, 42
+TYPES = [Q8_0, Q4_0, Q4_K, Q2_0]
+REL = 1e-4
+
+pytestmark = pytest.mark.gpu
+
+
+def make(oracle, qtype, rows, cols, seed, scale=0.02):
+    rng = np.random.default_rng(seed)
+    w = (rng.standard_normal((rows, cols)) * scale).astype(np.float32)
+    return w, oracle.quantize(qtype, w)
+
+
+def normwise(y, y64):
+    return float(np.abs(y.astype(np.float64) - y64).max() / max(np.abs(y64).max(), 1e-30))
+
+
+# ragged shapes: rows not a multiple of the 16-row tile, columns not a multiple of the 128/1024
+# column chunks, a single row, a single block
+SHAPES = {
+    Q8_0: [(37, 96), (1, 32), (64, 1056), (130, 2080)],
+    Q4_0: [(37, 96), (1, 32), (64, 1056), (130, 2080)],
+    Q4_K: [(21, 256), (1, 512), (48, 1280), (130, 2304)],
+    Q2_0: [(37, 128), (1, 384), (64, 1152), (130, 2176)],
+}
+
+
+@pytest.mark.parametrize("qtype", TYPES)
+def test_gather_row_bit_exact(backend, oracle, qtype):
+    for i, (rows, cols) in enumerate(SHAPES[qtype]):
+        _, blob = make(oracle, qtype, rows, cols, 100 + i)
+        w = backend.upload_quantized(blob, qtype, (rows, cols))
+        for r in sorted({0, rows // 2, rows - 1}):
+            got = backend.download(backend.quant_gather_row(w, r))
+            want = oracle.gather_row(qtype, blob, rows, cols, r)
+            assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), (rows, cols, r)
+
+
+@pytest.mark.parametrize("qtype", TYPES)
+def test_device_encoder_byte_identical(backend, oracle, qtype):
+    for i, (rows, cols) in enumerate(SHAPES[qtype]):
+        w, blob = make(oracle, qtype, rows, cols, 200 + i)
+        dev = backend.quantize(backend.upload(w, w.shape), qtype)
+        assert np.array_equal(dev.cpu().numpy(), blob), (rows, cols)
+
+
+@pytest.mark.parametrize("qtype", TYPES)
+@pytest.mark.parametrize("batch", [1, 3, 8, 9, 16, 21])
+def test_matvec_within_tolerance(backend, oracle, qtype, batch):
+    for i, (rows, cols) in enumerate(SHAPES[qtype]):
+        _, blob = make(oracle, qtype, rows, cols, 300 + i)
+        w = backend.upload_quantized(blob, qtype, (rows, cols))
+        x = np.random.default_rng(i).standard_normal((batch, cols)).astype(np.float32)
+        y = backend.download(backend.quant_matvec(w, backend.upload(x, x.shape)))
+        y64 = oracle.quant_matvec_f64(qtype, blob, rows, cols, x)
+        assert normwise(y, y64) <= REL, (rows, cols, batch, normwise(y, y64))
+
+
+def test_reference_shaped_call_and_add(backend, oracle):
+    """Rank-1 x is the reference's quantMatvec / quantMatvecAdd (CpuBackend.java:707-736)."""
+    rows, cols = 48, 512
+    _, blob = make(oracle, Q4_0, rows, cols, 7)
+    w = backend.upload_quantized(blob, Q4_0, (rows, cols))
+    x = np.random.default_rng(1).standard_normal(cols).astype(np.float32)
+    add = np.random.default_rng(2).standard_normal(rows).astype(np.float32)
+    y = backend.download(backend.quant_matvec(w, backend.upload(x, (cols,))))
+    assert y.shape == (rows,)
+    ref = oracle.quant_matvec(Q4_0, blob, rows, cols, x)[0]  # the reference's float order
+    y64 = oracle.quant_matvec_f64(Q4_0, blob, rows, cols, x)[0]
+    assert normwise(y, y64) <= REL and normwise(ref, y64) <= REL
+    ya = backend.download(backend.quant_matvec_add(w, backend.upload(x, (cols,)),
+                                                   backend.upload(add, (rows,))))
+    assert normwise(ya - add, y64) <= REL
+    with pytest.raises(ValueError, match="quantMatvec shape mismatch"):
+        backend.quant_matvec(w, backend.upload(np.zeros(cols - 32, np.float32), (cols - 32,)))
+
+
+def test_repeated_calls_are_deterministic(backend, oracle):
+    """The split-K arrival counters reset themselves: back-to-back calls agree bit for bit."""
+    rows, cols = 160, 4096  # 4 K ranges
+    _, blob = make(oracle, Q8_0, rows, cols, 11)
+    w = backend.upload_quantized(blob, Q8_0, (rows, cols))
+    x = backend.upload(np.random.default_rng(3).standard_normal((8, cols)).astype(np.float32),
+                       (8, cols))
+    first = backend.download(backend.quant_matvec(w, x))
+    for _ in range(5):
+        again = backend.download(backend.quant_matvec(w, x))
+        assert np.array_equal(first, again)
+
+
+def test_invalid_geometry_rejected(backend, oracle):
+    with pytest.raises(ValueError, match="invalid quant dimensions"):
+        backend.upload_quantized(np.zeros(34, np.uint8), Q8_0, (1, 33))
+    with pytest.raises(ValueError, match="bytes"):
+        backend.upload_quantized(np.zeros(30, np.uint8), Q8_0, (1, 32))
+    with pytest.raises(NotImplementedError):
+        backend.upload_quantized(np.zeros(210, np.uint8), 14, (1, 256))
+
+
+@pytest.mark.parametrize("qtype,rows,cols,batch", [
+    (Q8_0, 4096, 4096, 8),
+    (Q4_K, 14336, 4096, 1),    # BASELINE config 3, decode
+    (Q4_K, 14336, 4096, 16),   # BASELINE config 3, batch 16
+    (Q4_0, 4096, 14336, 4),    # config 5 down-projection shape
+])
+def test_baseline_sizes(backend, oracle, qtype, rows, cols, batch):
+    """Full BASELINE shapes: device-encoded weights, checked against the float64 oracle."""
+    g = torch.Generator(device="cuda").manual_seed(rows + cols)
+    wt = torch.randn(rows, cols, device="cuda", generator=g) * 0.02
+    blob_dev = backend.quantize(backend.wrap(wt), qtype)
+    blob = blob_dev.cpu().numpy()
+    w = backend.upload_quantized(blob_dev, qtype, (rows, cols))
+    x = np.random.default_rng(5).standard_normal((batch, cols)).astype(np.float32)
+    y = backend.download(backend.quant_matvec(w, backend.upload(x, x.shape)))
+    y64 = oracle.quant_matvec_f64(qtype, blob, rows, cols, x)
+    assert normwise(y, y64) <= REL
+    # dequantised rows of the full matrix stay bit-exact
+    for r in (0, rows - 1):
+        got = backend.download(backend.quant_gather_row(w, r))
+        assert np.array_equal(got, oracle.gather_row(qtype, blob, rows, cols, r))
