@@ -220,7 +220,7 @@ def run_engine(args):
     import torch.distributed as dist
     sys.path.insert(0, HERE)
     from jax4j_b200 import _lib
-    from jax4j_b200.backend import B200Backend
+    from jax4j_b200.backend import B200Backend, torch_stream
     from jax4j_b200.prng import PrngKey
 
     world, rank, local = dist_env()
@@ -253,7 +253,7 @@ def run_engine(args):
                   y.data_ptr(), batch, stream)
 
     def step(i, with_collective=True):
-        s = torch.cuda.current_stream().cuda_stream
+        s = torch_stream()
         gemv(i, s)
         if world > 1 and with_collective:
             dist.all_gather_into_tensor(y_all, y)
@@ -322,7 +322,7 @@ def run_engine(args):
     y_host = torch.empty(batch * rows, dtype=torch.float32).pin_memory()
     e2e_steps = min(K, 2000)
     xin = be.full(0.0, (batch, cols))
-    stream = torch.cuda.current_stream().cuda_stream
+    stream = torch_stream()
     barrier()
     e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e_start.record()

@@ -17,7 +17,8 @@
  *   - Device buffers are plain device addresses carried as uint64_t (j4b_buf). Any allocator may
  *     produce them (j4b_alloc, or a framework such as PyTorch); f32 tensors are dense row-major.
  *   - Launches are asynchronous on the given stream (a cudaStream_t passed as void*). A NULL
- *     stream selects the engine's own per-device non-blocking stream created by j4b_init.
+ *     stream selects the engine's own per-device non-blocking stream created by j4b_init; pass
+ *     cudaStreamLegacy ((void*)1) to mean the legacy default stream.
  *   - Shapes are (const int64_t* dims, int rank); rank <= 8.
  */
 #ifndef JAX4J_B200_H

@@ -25,6 +25,15 @@ def _prod(dims) -> int:
     return n
 
 
+CUDA_STREAM_LEGACY = 1  # cudaStreamLegacy
+
+
+def torch_stream(device=None) -> int:
+    """Handle of PyTorch's current stream, in the C ABI's convention."""
+    s = torch.cuda.current_stream(device).cuda_stream
+    return s if s else CUDA_STREAM_LEGACY
+
+
 def broadcast_shape(a: tuple, b: tuple) -> tuple:
     """Shape.broadcast (core/tensor/Shape.java:105-121)."""
     rank = max(len(a), len(b))
@@ -106,7 +115,9 @@ class B200Backend:
     # ---- plumbing ----
     @property
     def stream(self) -> int:
-        return torch.cuda.current_stream(self._torch_device).cuda_stream
+        """PyTorch's current stream; its default stream (handle 0) is passed as cudaStreamLegacy,
+        since a NULL stream selects the engine's own stream in the C ABI."""
+        return torch_stream(self._torch_device)
 
     def _new(self, shape) -> DeviceBuffer:
         t = torch.empty(max(_prod(shape), 1), dtype=torch.float32, device=self._torch_device)

@@ -1,0 +1,564 @@
+// Batched dequant-GEMV kernel (included by quant.cu inside namespace j4b::<anonymous>).
+//
+// Two CTAs per SM. A CTA owns one 1024-column K range ("split") of a run of 16-row tiles. For
+// each tile, the K range's quant bytes and scale bytes are contiguous in the repacked layout, so
+// one elected thread streams them into a ring of shared-memory stages with 1-D TMA bulk copies
+// (cp.async.bulk, completion counted on an mbarrier); the eight warps decode their 128-column
+// slice from shared memory into fp16 mma.m16n8k16 fragments, multiply them by the x fragments
+// they keep in registers for the whole run, and fold the per-block scales in fp32. Warp partials
+// of a tile are summed through shared memory; the K splits of a tile group are combined by the
+// last CTA of the group to finish (one arrival counter per group, partials in the weight's
+// scratch), which also applies `add`.
+//
+// Launches use programmatic dependent launch: the weight prefetch of one GEMV overlaps the tail
+// of the kernel before it (see the comment at the prefetch).
+//
+// Every mbarrier wait is bounded: on timeout the CTA records an error code in the weight's
+// status word, waits (bounded) for its copies in flight, and returns.
+
+constexpr int kGemvThreads = 256;
+constexpr uint32_t kWaitLimit = 1u << 26;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void fence_proxy_async() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+// 1-D bulk copy global -> this CTA's shared memory (no multicast). 16-byte aligned, size % 16 == 0.
+__device__ __forceinline__ void tma_load_1d(void* dst, const void* src, uint32_t bytes,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t phase) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, "
+      "0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(phase)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t phase) {
+  for (uint32_t it = 0; it < kWaitLimit; ++it)
+    if (mbar_try_wait(bar, phase)) return true;
+  return false;
+}
+
+// Programmatic dependent launch: let the next kernel in the stream start its prologue early /
+// wait until the previous kernel's writes are visible.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t rotr(uint32_t v, int s) { return __funnelshift_r(v, v, s); }
+__device__ __forceinline__ uint32_t lop_or(uint32_t v, uint32_t mask, uint32_t bias) {
+  return (v & mask) | bias;
+}
+__device__ __forceinline__ uint32_t h2sub(uint32_t a, uint32_t b) {
+  __half2 r = __hsub2(*reinterpret_cast<__half2*>(&a), *reinterpret_cast<__half2*>(&b));
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+// Q8_0: 4 bytes (a0..a3 or a4..a7) -> two half2 holding the exact integer codes.
+__device__ __forceinline__ void q8_pairs(uint32_t w, uint32_t& p0, uint32_t& p1) {
+  const uint32_t kBias = 0x64806480u;  // half2(1152, 1152): 1024 + the 0x80 code offset
+  p0 = h2sub(__byte_perm(w, 0x64646464u, 0x4140), kBias);
+  p1 = h2sub(__byte_perm(w, 0x64646464u, 0x4342), kBias);
+}
+// 4-bit: one word -> four half2 of (1 + q/16).
+__device__ __forceinline__ void q4_pairs(uint32_t w, uint32_t (&a)[4]) {
+  const uint32_t kMask = 0x03C003C0u, kOne = 0x3C003C00u;
+  a[0] = lop_or(w, kMask, kOne);
+  a[1] = lop_or(rotr(w, 4), kMask, kOne);
+  a[2] = lop_or(rotr(w, 8), kMask, kOne);
+  a[3] = lop_or(rotr(w, 12), kMask, kOne);
+}
+// 2-bit: one word -> eight half2 of (1 + c/4); pairs 0..3 are k-step 0, 4..7 k-step 1.
+__device__ __forceinline__ uint32_t q2_pair(uint32_t w, int p) {
+  return lop_or(rotr(w, 2 * p), 0x03000300u, 0x3C003C00u);
+}
+
+// Tiles per bulk copy (one copy of ~35 KB: bulk-copy throughput grows with the copy size), the
+// copies kept in flight, and the per-stage warp-partial buffer.
+template <int QT>
+struct GemvTraits {
+  static constexpr int kQ = QT == J4B_Q8_0 ? 512 : (QT == J4B_Q2_0 ? 128 : 256);
+  static constexpr int kM = QT == J4B_Q2_0 ? 8 : 32;
+  static constexpr int kChunk = 32 * (kQ + kM);  // bytes of one full tile chunk
+  static constexpr int kTilesPerCopy = QT == J4B_Q8_0 ? 2 : 4;
+  static constexpr int kStages = 2;
+};
+
+struct GemvArgs {
+  const uint8_t* data;
+  Layout L;
+  int64_t rows, cols, kpad, rt;
+  const float* x;
+  const float* add;
+  float* y;
+  int batch;  // batch rows handled by this launch (<= 8 * NT)
+  int ksplit;
+  int tiles_per_cta;
+  float* partials;     // [ksplit][rt][256]
+  unsigned* arrivals;  // one counter per tile group
+  int* status;         // nonzero after a bounded wait gave up
+};
+
+template <int QT, int NT>
+__host__ __device__ constexpr int gemv_smem_bytes() {
+  return GemvTraits<QT>::kStages * GemvTraits<QT>::kTilesPerCopy * GemvTraits<QT>::kChunk +
+         GemvTraits<QT>::kTilesPerCopy * 8 * NT * 128 * 4 + GemvTraits<QT>::kStages * 8 + 16;
+}
+
+template <int QT>
+constexpr int kXBlocks = QT == J4B_Q2_0 ? 1 : 4;  // x block sums per warp chunk
+
+// One warp's contribution to one 16-row tile: its 128-column slice of the tile's chunk (quants at
+// sq, scales at sm) times the x fragments, accumulated into acc (C-fragment layout: rows g and
+// g+8, batch columns 2t and 2t+1 of each n-tile). hi and lo halves of x accumulate separately so
+// each dependent chain is two mma long.
+template <int QT, int NT>
+__device__ __forceinline__ void tile_compute(const uint8_t* __restrict__ sq,
+                                             const uint8_t* __restrict__ sm, int warp, int lane,
+                                             const uint32_t (&bh)[NT][8][2],
+                                             const uint32_t (&bl)[NT][8][2],
+                                             const float (&xblk)[NT][kXBlocks<QT>][2],
+                                             float (&acc)[NT][4]) {
+  const int g = lane >> 2, t = lane & 3;
+  if constexpr (QT == J4B_Q8_0) {
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      const uint4 line = *reinterpret_cast<const uint4*>(sq + (warp * 4 + q) * 512 + lane * 16);
+      const uint32_t sc = *reinterpret_cast<const uint32_t*>(sm + (warp * 4 + q) * 32 + g * 4);
+      float th[NT][4] = {}, tl[NT][4] = {};
+      const uint32_t wv[4] = {line.x, line.y, line.z, line.w};
+#pragma unroll
+      for (int ks = 0; ks < 2; ks++) {
+        uint32_t a0, a1, a2, a3;
+        q8_pairs(wv[2 * ks], a0, a1);
+        q8_pairs(wv[2 * ks + 1], a2, a3);
+        const int j = 2 * q + ks;
+#pragma unroll
+        for (int n = 0; n < NT; n++) {
+          mma16816(th[n], a0, a1, a2, a3, bh[n][j][0], bh[n][j][1]);
+          mma16816(tl[n], a0, a1, a2, a3, bl[n][j][0], bl[n][j][1]);
+        }
+      }
+      const float2 d = __half22float2(*reinterpret_cast<const __half2*>(&sc));
+#pragma unroll
+      for (int n = 0; n < NT; n++) {
+        acc[n][0] = fmaf(d.x, th[n][0] + tl[n][0], acc[n][0]);
+        acc[n][1] = fmaf(d.x, th[n][1] + tl[n][1], acc[n][1]);
+        acc[n][2] = fmaf(d.y, th[n][2] + tl[n][2], acc[n][2]);
+        acc[n][3] = fmaf(d.y, th[n][3] + tl[n][3], acc[n][3]);
+      }
+    }
+  } else if constexpr (QT == J4B_Q4_0) {
+    const uint4 l0 = *reinterpret_cast<const uint4*>(sq + warp * 1024 + lane * 16);
+    const uint4 l1 = *reinterpret_cast<const uint4*>(sq + warp * 1024 + 512 + lane * 16);
+    const uint32_t wv[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      const uint32_t sc = *reinterpret_cast<const uint32_t*>(sm + (warp * 4 + q) * 32 + g * 4);
+      float th[NT][4] = {}, tl[NT][4] = {};
+#pragma unroll
+      for (int ks = 0; ks < 2; ks++) {
+        uint32_t av[4];
+        q4_pairs(wv[2 * q + ks], av);
+        const int j = 2 * q + ks;
+#pragma unroll
+        for (int n = 0; n < NT; n++) {
+          mma16816(th[n], av[0], av[1], av[2], av[3], bh[n][j][0], bh[n][j][1]);
+          mma16816(tl[n], av[0], av[1], av[2], av[3], bl[n][j][0], bl[n][j][1]);
+        }
+      }
+      // sum w x = d (16 C' - 24 X), C' = sum (1 + q/16) x
+      const float2 d = __half22float2(*reinterpret_cast<const __half2*>(&sc));
+      const float c0 = 16.f * d.x, c1 = 16.f * d.y, x0 = -24.f * d.x, x1 = -24.f * d.y;
+#pragma unroll
+      for (int n = 0; n < NT; n++) {
+        acc[n][0] += fmaf(c0, th[n][0] + tl[n][0], x0 * xblk[n][q][0]);
+        acc[n][1] += fmaf(c0, th[n][1] + tl[n][1], x0 * xblk[n][q][1]);
+        acc[n][2] += fmaf(c1, th[n][2] + tl[n][2], x1 * xblk[n][q][0]);
+        acc[n][3] += fmaf(c1, th[n][3] + tl[n][3], x1 * xblk[n][q][1]);
+      }
+    }
+  } else if constexpr (QT == J4B_Q2_0) {
+    const uint4 line = *reinterpret_cast<const uint4*>(sq + warp * 512 + lane * 16);
+    const uint32_t sc = *reinterpret_cast<const uint32_t*>(sm + warp * 32 + g * 4);
+    const uint32_t wv[4] = {line.x, line.y, line.z, line.w};
+    float th[NT][4] = {}, tl[NT][4] = {};
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+#pragma unroll
+      for (int ks = 0; ks < 2; ks++) {
+        const uint32_t a0 = q2_pair(wv[q], 4 * ks), a1 = q2_pair(wv[q], 4 * ks + 1);
+        const uint32_t a2 = q2_pair(wv[q], 4 * ks + 2), a3 = q2_pair(wv[q], 4 * ks + 3);
+        const int j = 2 * q + ks;
+#pragma unroll
+        for (int n = 0; n < NT; n++) {
+          mma16816(th[n], a0, a1, a2, a3, bh[n][j][0], bh[n][j][1]);
+          mma16816(tl[n], a0, a1, a2, a3, bl[n][j][0], bl[n][j][1]);
+        }
+      }
+    }
+    // sum w x = d (4 C' - 5 X), C' = sum (1 + c/4) x
+    const float2 d = __half22float2(*reinterpret_cast<const __half2*>(&sc));
+    const float c0 = 4.f * d.x, c1 = 4.f * d.y, x0 = -5.f * d.x, x1 = -5.f * d.y;
+#pragma unroll
+    for (int n = 0; n < NT; n++) {
+      acc[n][0] += fmaf(c0, th[n][0] + tl[n][0], x0 * xblk[n][0][0]);
+      acc[n][1] += fmaf(c0, th[n][1] + tl[n][1], x0 * xblk[n][0][1]);
+      acc[n][2] += fmaf(c1, th[n][2] + tl[n][2], x1 * xblk[n][0][0]);
+      acc[n][3] += fmaf(c1, th[n][3] + tl[n][3], x1 * xblk[n][0][1]);
+    }
+  } else {  // Q4_K: warp w holds half (w & 1) of super-block w / 2 of the CTA's K range
+    const int h = warp & 1;
+    const uint4 l0 = *reinterpret_cast<const uint4*>(sq + warp * 1024 + lane * 32);
+    const uint4 l1 = *reinterpret_cast<const uint4*>(sq + warp * 1024 + lane * 32 + 16);
+    const uint8_t* mp = sm + (warp >> 1) * 256 + g * 32;
+    const uint4 mm[2] = {*reinterpret_cast<const uint4*>(mp), *reinterpret_cast<const uint4*>(mp + 16)};
+    // Lane t decodes sub-block 4h+t for rows g and g+8: coefficients 16 d sc and
+    // -(16 d sc + dmin m); the four lanes of the group then exchange them.
+    float cs[2], cx[2];
+#pragma unroll
+    for (int r = 0; r < 2; r++) {
+      const uint32_t w0 = mm[r].x, w1 = mm[r].y, w2 = mm[r].z, w3 = mm[r].w;
+      const float d = __half2float(__ushort_as_half((uint16_t)(w0 & 0xFFFF)));
+      const float dmin = __half2float(__ushort_as_half((uint16_t)(w0 >> 16)));
+      const int j = 4 * h + t;
+      int sc, mn;
+      if (j < 4) {
+        sc = (w1 >> (8 * j)) & 63;
+        mn = (w2 >> (8 * j)) & 63;
+      } else {
+        const int jj = j - 4;
+        const uint32_t qj4 = (w3 >> (8 * jj)) & 0xFF;  // q[j+4]
+        sc = (qj4 & 0xF) | (((w1 >> (8 * jj + 6)) & 3) << 4);
+        mn = (qj4 >> 4) | (((w2 >> (8 * jj + 6)) & 3) << 4);
+      }
+      const float ds = d * (float)sc;
+      cs[r] = 16.f * ds;
+      cx[r] = -fmaf(16.f, ds, dmin * (float)mn);
+    }
+    const uint32_t wv[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      float th[NT][4] = {}, tl[NT][4] = {};
+#pragma unroll
+      for (int ks = 0; ks < 2; ks++) {
+        uint32_t av[4];
+        q4_pairs(wv[2 * q + ks], av);
+        const int j = 2 * q + ks;
+#pragma unroll
+        for (int n = 0; n < NT; n++) {
+          mma16816(th[n], av[0], av[1], av[2], av[3], bh[n][j][0], bh[n][j][1]);
+          mma16816(tl[n], av[0], av[1], av[2], av[3], bl[n][j][0], bl[n][j][1]);
+        }
+      }
+      const int src = (lane & ~3) | q;
+      const float s0 = __shfl_sync(0xffffffffu, cs[0], src);
+      const float s1 = __shfl_sync(0xffffffffu, cs[1], src);
+      const float z0 = __shfl_sync(0xffffffffu, cx[0], src);
+      const float z1 = __shfl_sync(0xffffffffu, cx[1], src);
+#pragma unroll
+      for (int n = 0; n < NT; n++) {
+        acc[n][0] += fmaf(s0, th[n][0] + tl[n][0], z0 * xblk[n][q][0]);
+        acc[n][1] += fmaf(s0, th[n][1] + tl[n][1], z0 * xblk[n][q][1]);
+        acc[n][2] += fmaf(s1, th[n][2] + tl[n][2], z1 * xblk[n][q][0]);
+        acc[n][3] += fmaf(s1, th[n][3] + tl[n][3], z1 * xblk[n][q][1]);
+      }
+    }
+  }
+}
+
+// Output element v (0 .. NT*128) of a tile's 16 x (8 NT) block -> (row in tile, batch column).
+__device__ __forceinline__ void out_coord(int v, int& row, int& bcol) {
+  const int nc = v >> 5, ln = v & 31, n = nc >> 2, c = nc & 3;
+  row = (ln >> 2) + 8 * (c >> 1);
+  bcol = 8 * n + 2 * (ln & 3) + (c & 1);
+}
+
+template <int QT, int NT>
+__global__ void __launch_bounds__(kGemvThreads, 2) qgemv_kernel(GemvArgs a) {
+  using T = GemvTraits<QT>;
+  constexpr int kStages = T::kStages, kM = T::kTilesPerCopy;
+  constexpr int kStageBytes = kM * T::kChunk;
+  constexpr int kVals = NT * 128;  // outputs of one tile
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t* stage_base = smem;
+  float* red = reinterpret_cast<float*>(smem + kStages * kStageBytes);  // [kM][8 warps][kVals]
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes + kM * 8 * kVals * 4);
+  __shared__ int last_flag;
+
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int g = lane >> 2, t = lane & 3;
+  const int split = blockIdx.x % a.ksplit;
+  const int group = blockIdx.x / a.ksplit;
+  const int64_t tile0 = (int64_t)group * a.tiles_per_cta;
+  const int64_t tile1 = min(tile0 + a.tiles_per_cta, a.rt);
+  const int ntiles = (int)(tile1 - tile0);
+  const int ncopies = (ntiles + kM - 1) / kM;
+  const int64_t k0 = (int64_t)split * 1024 + warp * 128;  // this warp's 128-column chunk
+  const bool active = k0 < a.kpad;
+  const int groups_here = a.L.groups_in_split(split);
+  const uint32_t chunk = (uint32_t)a.L.chunk_bytes(split);  // bytes of one tile of this split
+  const uint32_t meta_off = (uint32_t)(groups_here * T::kQ);
+
+  // copy c brings tiles [c*kM, min((c+1)*kM, ntiles)) into stage c % kStages
+  auto issue = [&](int c) {
+    const int first = c * kM, count = min(kM, ntiles - first);
+    const uint32_t bytes = (uint32_t)count * chunk;
+    uint64_t* bar = &full[c % kStages];
+    mbar_expect_tx(bar, bytes);
+    tma_load_1d(stage_base + (c % kStages) * kStageBytes,
+                a.data + a.L.chunk_offset(split, tile0 + first), bytes, bar);
+  };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; s++) mbar_init(&full[s], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  // Weights are immutable once uploaded, so they stream in before this kernel waits on the one
+  // before it in the stream; x, add, y and the split-K scratch are touched only after the wait.
+  int issued = 0;  // copies thread 0 has issued (only thread 0 tracks it)
+  if (threadIdx.x == 0)
+    for (; issued < kStages && issued < ncopies; issued++) issue(issued);
+  pdl_launch_dependents();
+  pdl_wait();
+
+  // ---- x fragments of this warp's 128-column chunk: hi/lo fp16, per n-tile and k-step ----
+  // Addresses are clamped into the tensor and out-of-range lanes select zero, so all loads are
+  // unconditional and issue back to back.
+  uint32_t bh[NT][8][2], bl[NT][8][2];
+  float xs[NT][8];
+#pragma unroll
+  for (int n = 0; n < NT; n++) {
+    const int b = 8 * n + g;
+    const bool brow = active && b < a.batch;
+    const float* xr = a.x + (int64_t)min(b, a.batch - 1) * a.cols;
+    float2 p0[8], p1[8];
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      const int64_t k = k0 + 16 * j + 2 * t;
+      p0[j] = __ldg(reinterpret_cast<const float2*>(xr + min(k, a.cols - 2)));
+      p1[j] = __ldg(reinterpret_cast<const float2*>(xr + min(k + 8, a.cols - 2)));
+    }
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      const int64_t k = k0 + 16 * j + 2 * t;
+      const bool v0ok = brow && k < a.cols, v1ok = brow && k + 8 < a.cols;
+      const float v[4] = {v0ok ? p0[j].x : 0.f, v0ok ? p0[j].y : 0.f, v1ok ? p1[j].x : 0.f,
+                          v1ok ? p1[j].y : 0.f};
+      __half2 h0 = __floats2half2_rn(v[0], v[1]);
+      __half2 h1 = __floats2half2_rn(v[2], v[3]);
+      const float2 f0 = __half22float2(h0), f1 = __half22float2(h1);
+      __half2 l0 = __floats2half2_rn(v[0] - f0.x, v[1] - f0.y);
+      __half2 l1 = __floats2half2_rn(v[2] - f1.x, v[3] - f1.y);
+      bh[n][j][0] = *reinterpret_cast<uint32_t*>(&h0);
+      bh[n][j][1] = *reinterpret_cast<uint32_t*>(&h1);
+      bl[n][j][0] = *reinterpret_cast<uint32_t*>(&l0);
+      bl[n][j][1] = *reinterpret_cast<uint32_t*>(&l1);
+      const float2 g0 = __half22float2(l0), g1 = __half22float2(l1);
+      xs[n][j] = (f0.x + g0.x) + (f0.y + g0.y) + (f1.x + g1.x) + (f1.y + g1.y);
+    }
+  }
+  // Block sums of x for the output columns this lane holds (batch 2t, 2t+1 of each n-tile).
+  constexpr int kXB = kXBlocks<QT>;
+  float xblk[NT][kXB][2] = {};
+  if constexpr (QT != J4B_Q8_0) {
+#pragma unroll
+    for (int n = 0; n < NT; n++) {
+#pragma unroll
+      for (int q = 0; q < kXB; q++) {
+        float s = 0.f;
+        constexpr int kSteps = 8 / kXB;
+#pragma unroll
+        for (int j = 0; j < kSteps; j++) s += xs[n][q * kSteps + j];
+        s += __shfl_xor_sync(0xffffffffu, s, 1);
+        s += __shfl_xor_sync(0xffffffffu, s, 2);
+        xblk[n][q][0] = __shfl_sync(0xffffffffu, s, 4 * (2 * t));
+        xblk[n][q][1] = __shfl_sync(0xffffffffu, s, 4 * (2 * t + 1));
+      }
+    }
+  }
+
+  bool failed = false;
+  int consumed = 0;  // copies fully consumed
+  for (int c = 0; c < ncopies; c++) {
+    const int s = c % kStages;
+    const int count = min(kM, ntiles - c * kM);
+    if (!mbar_wait_bounded(&full[s], (uint32_t)((c / kStages) & 1))) failed = true;
+    float acc[kM][NT][4] = {};
+    if (active && !failed) {
+      const uint8_t* st = stage_base + s * kStageBytes;
+      // all kM tiles are computed so their mma chains interleave; tiles past `count` read
+      // stale stage bytes and are discarded
+#pragma unroll
+      for (int j = 0; j < kM; j++)
+        tile_compute<QT, NT>(st + j * chunk, st + j * chunk + meta_off, warp, lane, bh, bl, xblk, acc[j]);
+    }
+#pragma unroll
+    for (int j = 0; j < kM; j++)
+#pragma unroll
+      for (int n = 0; n < NT; n++)
+#pragma unroll
+        for (int cc = 0; cc < 4; cc++) red[(j * 8 + warp) * kVals + (n * 4 + cc) * 32 + lane] = acc[j][n][cc];
+    if (__syncthreads_or(failed)) {
+      failed = true;
+      break;
+    }
+    consumed = c + 1;
+    if (threadIdx.x == 0 && c + kStages < ncopies) {
+      fence_proxy_async();  // generic-proxy reads of stage s happen before the async refill
+      issue(c + kStages);
+      issued++;
+    }
+    for (int idx = threadIdx.x; idx < count * kVals; idx += kGemvThreads) {
+      const int j = idx / kVals, v = idx % kVals;
+      float total = 0.f;
+#pragma unroll
+      for (int w = 0; w < 8; w++) total += red[(j * 8 + w) * kVals + v];
+      const int64_t tile = tile0 + c * kM + j;
+      if (a.ksplit == 1) {
+        int row, bcol;
+        out_coord(v, row, bcol);
+        const int64_t r = tile * 16 + row;
+        if (r < a.rows && bcol < a.batch) {
+          if (a.add) total += a.add[(int64_t)bcol * a.rows + r];
+          a.y[(int64_t)bcol * a.rows + r] = total;
+        }
+      } else {
+        a.partials[((int64_t)split * a.rt + tile) * 256 + v] = total;
+      }
+    }
+    __syncthreads();  // red is rewritten by the next stage
+  }
+
+  if (failed) {
+    // Let copies still in flight land before the CTA's shared memory is released.
+    if (threadIdx.x == 0) {
+      atomicExch(a.status, 1);
+      for (int cc = consumed; cc < issued; cc++)  // bounded wait for each copy still in flight
+        mbar_wait_bounded(&full[cc % kStages], (uint32_t)((cc / kStages) & 1));
+    }
+    return;
+  }
+
+  if (a.ksplit > 1) {
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) last_flag = atomicAdd(a.arrivals + group, 1u) == (unsigned)(a.ksplit - 1);
+    __syncthreads();
+    if (!last_flag) return;
+    __threadfence();
+    // The last CTA of the group folds the K splits in split order (deterministic); four outputs
+    // per thread per pass keep all their loads in flight together.
+    const int nv = ntiles * kVals;
+    for (int i0 = threadIdx.x; i0 < nv; i0 += 4 * kGemvThreads) {
+      float tot[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int sp = 0; sp < a.ksplit; sp++) {
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+          const int idx = min(i0 + u * kGemvThreads, nv - 1);
+          const int64_t tile = tile0 + idx / kVals;
+          tot[u] += __ldcg(a.partials + ((int64_t)sp * a.rt + tile) * 256 + idx % kVals);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        const int idx = i0 + u * kGemvThreads;
+        if (idx >= nv) break;
+        const int64_t tile = tile0 + idx / kVals;
+        int row, bcol;
+        out_coord(idx % kVals, row, bcol);
+        const int64_t r = tile * 16 + row;
+        if (r < a.rows && bcol < a.batch) {
+          float v = tot[u];
+          if (a.add) v += a.add[(int64_t)bcol * a.rows + r];
+          a.y[(int64_t)bcol * a.rows + r] = v;
+        }
+      }
+    }
+    if (threadIdx.x == 0) a.arrivals[group] = 0u;
+  }
+}
+
+template <int QT, int NT>
+cudaError_t launch_gemv(const j4b_qweight* w, const float* x, const float* add, float* y,
+                        int batch, int sms, cudaStream_t stream) {
+  static bool configured = false;  // one attribute call per instantiation
+  constexpr int smem = gemv_smem_bytes<QT, NT>();
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(qgemv_kernel<QT, NT>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  GemvArgs a;
+  a.data = w->data;
+  a.L = layout_of(w);
+  a.rows = w->rows;
+  a.cols = w->cols;
+  a.kpad = w->kpad;
+  a.rt = w->rt;
+  a.x = x;
+  a.add = add;
+  a.y = y;
+  a.batch = batch;
+  a.ksplit = w->ksplit;
+  a.partials = w->partials;
+  a.arrivals = w->arrivals;
+  a.status = w->status;
+  // Two CTAs per SM (16 warps to hide the mma / shared-memory latencies): as many tile groups as
+  // fit next to the K splits, tiles shared out evenly.
+  const int64_t groups_fit = std::max<int64_t>(1, 2ll * sms / w->ksplit);
+  const int64_t tiles = (w->rt + groups_fit - 1) / groups_fit;
+  a.tiles_per_cta = (int)tiles;
+  const int64_t groups = (w->rt + tiles - 1) / tiles;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(groups * w->ksplit));
+  cfg.blockDim = dim3(kGemvThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, qgemv_kernel<QT, NT>, a);
+}
+
+template <int QT>
+cudaError_t gemv_dispatch(const j4b_qweight* w, const float* x, const float* add, float* y,
+                          int batch, int sms, cudaStream_t stream) {
+  if (batch <= 8) return launch_gemv<QT, 1>(w, x, add, y, batch, sms, stream);
+  return launch_gemv<QT, 2>(w, x, add, y, batch, sms, stream);
+}

@@ -40,11 +40,11 @@ struct j4b_qweight {
   int64_t rt;     // row tiles of 16
   int64_t kpad;   // K rounded up to the 128-column warp chunk
   int ksplit;     // K ranges of 1024 columns
-  uint8_t* quants;
-  uint8_t* meta;
-  size_t quant_bytes, meta_bytes;
+  uint8_t* data;       // repacked plane (split-major, see Layout)
+  size_t data_bytes;   // equal to the GGUF blob size when rows % 16 == 0 and cols % 128 == 0
   float* partials;     // [ksplit][rt][256] split-K scratch
-  unsigned* arrivals;  // [rt] arrival counters, zero between launches
+  unsigned* arrivals;  // [rt] arrival counters (one per tile group), zero between launches
+  int* status;         // set to nonzero by a kernel whose bounded wait gave up
 };
 
 namespace j4b {
@@ -125,49 +125,95 @@ __device__ inline int raw_code(int type, const uint8_t* blob, int64_t rows, int6
 }
 
 // ---------------------------------------------------------------------------------------------
-// repack kernels
+// repacked layout ("split-major"): one plane holding, for each 1024-column K range ("split") s
+// and each 16-row tile t, one contiguous chunk [quant bytes of the split's 32-column groups |
+// scale bytes of those groups]. A CTA that owns split s of tiles t0..t1 therefore streams one
+// contiguous byte range. Within a chunk, group gl (0..groups_here) occupies, per type:
+//   Q8_0: quants gl*512 + lane*16 (k-step ks, element e at byte 8ks+e, code ^ 0x80);
+//         scales gl*32 + g*4 + which*2 (f16 d of row g / row g+8 of the tile)
+//   Q4_0: quants (gl/2)*512 + lane*16 + (gl%2)*8 (two words, k-steps 0/1, nibbles at nib_pos);
+//         scales as Q8_0
+//   Q4_K: quants (gl/4)*1024 + lane*32 + (gl%4)*8; scales (gl/8)*256 + (g*2+which)*16, the
+//         row's 16 GGUF bytes (d, dmin, 12 packed 6-bit scales/mins) per super-block
+//   Q2_0: quants (gl/4)*512 + lane*16 + (gl%4)*4 (one word, crumbs at crumb_pos);
+//         scales (gl/4)*32 + g*4 + which*2
 // ---------------------------------------------------------------------------------------------
+__host__ __device__ inline int group_quant_bytes(int t) {
+  return t == J4B_Q8_0 ? 512 : (t == J4B_Q2_0 ? 128 : 256);
+}
+__host__ __device__ inline int group_meta_bytes(int t) { return t == J4B_Q2_0 ? 8 : 32; }
+
+struct Layout {
+  int type;
+  int64_t rt, kpad;
+  __host__ __device__ int groups_in_split(int64_t s) const {
+    const int64_t rem = (kpad - s * 1024) / 32;
+    return (int)(rem < 32 ? rem : 32);
+  }
+  __host__ __device__ int64_t chunk_bytes(int64_t s) const {
+    return (int64_t)groups_in_split(s) * (group_quant_bytes(type) + group_meta_bytes(type));
+  }
+  __host__ __device__ int64_t chunk_offset(int64_t s, int64_t tile) const {
+    return s * rt * 32 * (group_quant_bytes(type) + group_meta_bytes(type)) + tile * chunk_bytes(s);
+  }
+  __host__ __device__ int64_t total_bytes() const {
+    const int64_t splits = (kpad + 1023) / 1024;
+    return chunk_offset(splits - 1, rt);
+  }
+  // byte offset of lane `lane`'s quant data for global 32-column group G of `tile`
+  __host__ __device__ int64_t quant_offset(int64_t tile, int64_t G, int lane) const {
+    const int64_t s = G / 32;
+    const int gl = (int)(G % 32);
+    const int64_t base = chunk_offset(s, tile);
+    switch (type) {
+      case J4B_Q8_0: return base + gl * 512 + lane * 16;
+      case J4B_Q4_0: return base + (gl / 2) * 512 + lane * 16 + (gl % 2) * 8;
+      case J4B_Q4_K: return base + (gl / 4) * 1024 + lane * 32 + (gl % 4) * 8;
+      default: return base + (gl / 4) * 512 + lane * 16 + (gl % 4) * 4;
+    }
+  }
+  // byte offset of the scale data of row (g, which) of `tile` for global group G
+  __host__ __device__ int64_t meta_offset(int64_t tile, int64_t G, int g, int which) const {
+    const int64_t s = G / 32;
+    const int gl = (int)(G % 32);
+    const int64_t base = chunk_offset(s, tile) + (int64_t)groups_in_split(s) * group_quant_bytes(type);
+    switch (type) {
+      case J4B_Q4_K: return base + (gl / 8) * 256 + (g * 2 + which) * 16;
+      case J4B_Q2_0: return base + (gl / 4) * 32 + g * 4 + which * 2;
+      default: return base + gl * 32 + g * 4 + which * 2;
+    }
+  }
+};
 
 // One thread per (row tile, 32-column group, lane): writes that lane's quant bytes.
-__global__ void repack_quants_kernel(int type, const uint8_t* __restrict__ blob, int64_t rows,
-                                     int64_t cols, int64_t rt, int64_t kpad,
-                                     uint8_t* __restrict__ out) {
-  int64_t groups = kpad / 32;
-  int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= rt * groups * 32) return;
-  int lane = (int)(idx % 32);
-  int64_t grp = (idx / 32) % groups;
-  int64_t tile = idx / 32 / groups;
-  int64_t r0 = tile * 16, k0 = grp * 32;
+__global__ void repack_quants_kernel(Layout L, const uint8_t* __restrict__ blob, int64_t rows,
+                                     int64_t cols, uint8_t* __restrict__ out) {
+  const int type = L.type;
+  const int64_t groups = L.kpad / 32;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= L.rt * groups * 32) return;
+  const int lane = (int)(idx % 32);
+  const int64_t grp = (idx / 32) % groups;
+  const int64_t tile = idx / 32 / groups;
+  const int64_t r0 = tile * 16, k0 = grp * 32;
+  uint8_t* dst = out + L.quant_offset(tile, grp, lane);
   bool in;
   if (type == J4B_Q8_0) {
-    // [tile][grp][lane][16 bytes]: kstep ks, element e at byte 8*ks + e, value q ^ 0x80.
-    uint8_t bytes[16];
     for (int ks = 0; ks < 2; ks++)
       for (int e = 0; e < 8; e++) {
-        int q = raw_code(type, blob, rows, cols, r0 + frag_row(lane, e), k0 + 16 * ks + frag_col(lane, e), &in);
-        bytes[8 * ks + e] = (uint8_t)((q & 0xFF) ^ 0x80);
+        const int q = raw_code(type, blob, rows, cols, r0 + frag_row(lane, e), k0 + 16 * ks + frag_col(lane, e), &in);
+        dst[8 * ks + e] = (uint8_t)((q & 0xFF) ^ 0x80);
       }
-    uint8_t* dst = out + ((tile * groups + grp) * 32 + lane) * 16;
-    for (int i = 0; i < 16; i++) dst[i] = bytes[i];
   } else if (type == J4B_Q4_0 || type == J4B_Q4_K) {
-    // Two 32-bit words (k-steps 0, 1) per lane per group. Q4_0 groups are paired into one
-    // 16-byte line per lane ([tile][grp/2][lane][grp&1][8 bytes]); Q4_K half super-blocks of 4
-    // groups form one 32-byte line per lane ([tile][grp/4][lane][grp&3][8 bytes]).
     uint32_t words[2] = {0, 0};
     for (int ks = 0; ks < 2; ks++)
       for (int e = 0; e < 8; e++) {
-        int q = raw_code(type, blob, rows, cols, r0 + frag_row(lane, e), k0 + 16 * ks + frag_col(lane, e), &in);
+        const int q = raw_code(type, blob, rows, cols, r0 + frag_row(lane, e), k0 + 16 * ks + frag_col(lane, e), &in);
         words[ks] |= rotl32((uint32_t)(q & 0xF), nib_pos(e));
       }
-    int per_line = type == J4B_Q4_0 ? 2 : 4;
-    int64_t line = grp / per_line;
-    int slot = (int)(grp % per_line);
-    uint32_t* dst = (uint32_t*)(out + ((tile * (groups / per_line) + line) * 32 + lane) * (8 * per_line) + 8 * slot);
-    dst[0] = words[0];
-    dst[1] = words[1];
+    reinterpret_cast<uint32_t*>(dst)[0] = words[0];
+    reinterpret_cast<uint32_t*>(dst)[1] = words[1];
   } else if (type == J4B_Q2_0) {
-    // One word per lane per group; the 4 groups of a 128-block form one 16-byte line.
     uint32_t word = 0;
     for (int ks = 0; ks < 2; ks++)
       for (int e = 0; e < 8; e++) {
@@ -175,460 +221,100 @@ __global__ void repack_quants_kernel(int type, const uint8_t* __restrict__ blob,
         if (!in) c = 1;  // padding decodes to 0
         word |= rotl32((uint32_t)(c & 3), crumb_pos(4 * ks + (e >> 1), e & 1));
       }
-    int64_t line = grp / 4;
-    int slot = (int)(grp % 4);
-    uint32_t* dst = (uint32_t*)(out + ((tile * (groups / 4) + line) * 32 + lane) * 16 + 4 * slot);
-    dst[0] = word;
+    reinterpret_cast<uint32_t*>(dst)[0] = word;
   }
 }
 
-// Scale planes. Q8_0/Q4_0/Q2_0: [tile][block][8 groups][2 halves: row g, row g+8].
-// Q4_K: [tile][super-block][8 groups][2 rows][16 bytes: d, dmin, 12 packed scale bytes].
-__global__ void repack_meta_kernel(int type, const uint8_t* __restrict__ blob, int64_t rows,
-                                   int64_t cols, int64_t rt, int64_t kpad,
-                                   uint8_t* __restrict__ out) {
-  int be = block_elems(type), bb = block_bytes(type);
-  int64_t blocks = kpad / be;
-  int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // (tile, block, row-in-tile)
-  if (idx >= rt * blocks * 16) return;
-  int rr = (int)(idx % 16);
-  int64_t blk = (idx / 16) % blocks;
-  int64_t tile = idx / 16 / blocks;
-  int64_t r = tile * 16 + rr;
-  bool in = r < rows && blk * be < cols;
+// One thread per (row tile, GGUF block, row in tile): copies the row's scale bytes.
+__global__ void repack_meta_kernel(Layout L, const uint8_t* __restrict__ blob, int64_t rows,
+                                   int64_t cols, uint8_t* __restrict__ out) {
+  const int type = L.type;
+  const int be = block_elems(type), bb = block_bytes(type);
+  const int64_t blocks = L.kpad / be;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= L.rt * blocks * 16) return;
+  const int rr = (int)(idx % 16);
+  const int64_t blk = (idx / 16) % blocks;
+  const int64_t tile = idx / 16 / blocks;
+  const int64_t r = tile * 16 + rr;
+  const bool in = r < rows && blk * be < cols;
   const uint8_t* src = in ? blob + (r * (cols / be) + blk) * bb : nullptr;
-  int g = rr & 7, which = rr >> 3;
-  if (type == J4B_Q4_K) {
-    uint8_t* dst = out + (((tile * blocks + blk) * 8 + g) * 2 + which) * 16;
-    for (int i = 0; i < 16; i++) dst[i] = in ? src[i] : 0;
-  } else {
-    uint8_t* dst = out + (((tile * blocks + blk) * 8 + g) * 2 + which) * 2;
-    dst[0] = in ? src[0] : 0;
-    dst[1] = in ? src[1] : 0;
-  }
+  const int g = rr & 7, which = rr >> 3;
+  const int64_t G = blk * be / 32;  // first 32-column group of the block
+  uint8_t* dst = out + L.meta_offset(tile, G, g, which);
+  const int n = type == J4B_Q4_K ? 16 : 2;
+  for (int i = 0; i < n; i++) dst[i] = in ? src[i] : 0;
 }
 
 // ---------------------------------------------------------------------------------------------
 // bit-exact gather (quantGatherRow) from the repacked layout
 // ---------------------------------------------------------------------------------------------
-__device__ inline int repacked_code(const j4b_qweight& w, int64_t r, int64_t k) {
-  int64_t tile = r / 16;
-  int rr = (int)(r % 16);
-  int64_t grp = k / 32, groups = w.kpad / 32;
-  int kk = (int)(k % 32), ks = kk / 16, k16 = kk % 16;
-  int g = rr & 7, hi8 = rr >> 3;
-  int t = (k16 & 7) >> 1;
-  int lane = 4 * g + t;
-  int e = (k16 & 1) + 2 * hi8 + 4 * (k16 >> 3);
-  if (w.type == J4B_Q8_0) {
-    const uint8_t* p = w.quants + ((tile * groups + grp) * 32 + lane) * 16;
-    return (int)(int8_t)(p[8 * ks + e] ^ 0x80);
-  }
-  if (w.type == J4B_Q4_0 || w.type == J4B_Q4_K) {
-    int per_line = w.type == J4B_Q4_0 ? 2 : 4;
-    const uint32_t* p = (const uint32_t*)(w.quants + ((tile * (groups / per_line) + grp / per_line) * 32 + lane) * (8 * per_line) + 8 * (grp % per_line));
-    return rotr32(p[ks], nib_pos(e)) & 0xF;
-  }
-  const uint32_t* p = (const uint32_t*)(w.quants + ((tile * (groups / 4) + grp / 4) * 32 + lane) * 16 + 4 * (grp % 4));
-  return rotr32(p[0], crumb_pos(4 * ks + (e >> 1), e & 1)) & 3;
+__device__ inline int repacked_code(const Layout& L, const uint8_t* data, int64_t r, int64_t k) {
+  const int64_t tile = r / 16;
+  const int rr = (int)(r % 16);
+  const int64_t grp = k / 32;
+  const int kk = (int)(k % 32), ks = kk / 16, k16 = kk % 16;
+  const int g = rr & 7, hi8 = rr >> 3;
+  const int t = (k16 & 7) >> 1;
+  const int lane = 4 * g + t;
+  const int e = (k16 & 1) + 2 * hi8 + 4 * (k16 >> 3);
+  const uint8_t* p = data + L.quant_offset(tile, grp, lane);
+  if (L.type == J4B_Q8_0) return (int)(int8_t)(p[8 * ks + e] ^ 0x80);
+  if (L.type == J4B_Q4_0 || L.type == J4B_Q4_K)
+    return rotr32(reinterpret_cast<const uint32_t*>(p)[ks], nib_pos(e)) & 0xF;
+  return rotr32(reinterpret_cast<const uint32_t*>(p)[0], crumb_pos(4 * ks + (e >> 1), e & 1)) & 3;
 }
 
-__global__ void gather_row_kernel(j4b_qweight w, int64_t row, float* __restrict__ out) {
-  int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (k >= w.cols) return;
-  int64_t tile = row / 16;
-  int rr = (int)(row % 16), g = rr & 7, which = rr >> 3;
-  int q = repacked_code(w, row, k);
+__global__ void gather_row_kernel(Layout L, const uint8_t* __restrict__ data, int64_t cols,
+                                  int64_t row, float* __restrict__ out) {
+  const int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (k >= cols) return;
+  const int64_t tile = row / 16;
+  const int rr = (int)(row % 16), g = rr & 7, which = rr >> 3;
+  const int q = repacked_code(L, data, row, k);
+  const uint8_t* m = data + L.meta_offset(tile, k / 32, g, which);
   float v;
-  if (w.type == J4B_Q4_K) {
-    int64_t sb = k / 256;
-    const uint8_t* m = w.meta + (((tile * (w.kpad / 256) + sb) * 8 + g) * 2 + which) * 16;
-    float d = __half2float(__ushort_as_half(rd16(m)));
-    float dmin = __half2float(__ushort_as_half(rd16(m + 2)));
-    int j = (int)((k % 256) / 32), sc, mn;
+  if (L.type == J4B_Q4_K) {
+    const float d = __half2float(__ushort_as_half(rd16(m)));
+    const float dmin = __half2float(__ushort_as_half(rd16(m + 2)));
+    const int j = (int)((k % 256) / 32);
+    int sc, mn;
     q4k_scale_min(j, m + 4, &sc, &mn);
-    float d1 = __fmul_rn(d, (float)sc), m1 = __fmul_rn(dmin, (float)mn);
+    const float d1 = __fmul_rn(d, (float)sc), m1 = __fmul_rn(dmin, (float)mn);
     v = __fsub_rn(__fmul_rn(d1, (float)q), m1);  // d1*q is exact; one rounding, as the oracle
   } else {
-    int be = block_elems(w.type);
-    int64_t blk = k / be;
-    const uint8_t* m = w.meta + (((tile * (w.kpad / be) + blk) * 8 + g) * 2 + which) * 2;
-    float d = __half2float(__ushort_as_half(rd16(m)));
-    int code = w.type == J4B_Q8_0 ? q : (w.type == J4B_Q4_0 ? q - 8 : q - 1);
+    const float d = __half2float(__ushort_as_half(rd16(m)));
+    const int code = L.type == J4B_Q8_0 ? q : (L.type == J4B_Q4_0 ? q - 8 : q - 1);
     v = __fmul_rn(d, (float)code);
   }
   out[k] = v;
 }
 
-// ---------------------------------------------------------------------------------------------
-// GEMV
-// ---------------------------------------------------------------------------------------------
-struct GemvArgs {
-  const uint8_t* quants;
-  const uint8_t* meta;
-  int64_t rows, cols, kpad, rt;
-  const float* x;
-  const float* add;
-  float* y;
-  int batch;  // batch rows handled by this launch (<= 8 * NT)
-  int ksplit;
-  int tiles_per_cta;
-  float* partials;
-  unsigned* arrivals;
-};
-
-__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
-                                         uint32_t a3, uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};\n"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+Layout layout_of(const j4b_qweight* w) {
+  Layout L;
+  L.type = w->type;
+  L.rt = w->rt;
+  L.kpad = w->kpad;
+  return L;
 }
 
-__device__ __forceinline__ uint32_t rotr(uint32_t v, int s) { return __funnelshift_r(v, v, s); }
-__device__ __forceinline__ uint32_t lop_or(uint32_t v, uint32_t mask, uint32_t bias) {
-  return (v & mask) | bias;
-}
-__device__ __forceinline__ uint32_t h2sub(uint32_t a, uint32_t b) {
-  __half2 r = __hsub2(*reinterpret_cast<__half2*>(&a), *reinterpret_cast<__half2*>(&b));
-  return *reinterpret_cast<uint32_t*>(&r);
-}
-
-// Q8_0: 4 bytes (a0..a3 or a4..a7) -> two half2 holding the exact integer codes.
-__device__ __forceinline__ void q8_pairs(uint32_t w, uint32_t& p0, uint32_t& p1) {
-  const uint32_t kBias = 0x64806480u;  // half2(1152, 1152): 1024 + the 0x80 code offset
-  p0 = h2sub(__byte_perm(w, 0x64646464u, 0x4140), kBias);
-  p1 = h2sub(__byte_perm(w, 0x64646464u, 0x4342), kBias);
-}
-// 4-bit: one word -> four half2 of (1 + q/16).
-__device__ __forceinline__ void q4_pairs(uint32_t w, uint32_t (&a)[4]) {
-  const uint32_t kMask = 0x03C003C0u, kOne = 0x3C003C00u;
-  a[0] = lop_or(w, kMask, kOne);
-  a[1] = lop_or(rotr(w, 4), kMask, kOne);
-  a[2] = lop_or(rotr(w, 8), kMask, kOne);
-  a[3] = lop_or(rotr(w, 12), kMask, kOne);
-}
-// 2-bit: one word -> eight half2 of (1 + c/4); pairs 0..3 are k-step 0, 4..7 k-step 1.
-__device__ __forceinline__ uint32_t q2_pair(uint32_t w, int p) {
-  return lop_or(rotr(w, 2 * p), 0x03000300u, 0x3C003C00u);
-}
-
-template <int QT, int NT>
-__global__ void __launch_bounds__(256, 2) qgemv_kernel(GemvArgs a) {
-  __shared__ float red[2][kWarps][NT * 4][32];
-  __shared__ int last_flag;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int g = lane >> 2, t = lane & 3;
-  const int split = blockIdx.x % a.ksplit;
-  const int64_t tile0 = (int64_t)(blockIdx.x / a.ksplit) * a.tiles_per_cta;
-  const int64_t tile1 = min(tile0 + a.tiles_per_cta, a.rt);
-  const int64_t k0 = (int64_t)split * kCtaCols + warp * kWarpCols;
-  const bool active = k0 < a.kpad;
-  const int groups_total = (int)(a.kpad / 32);
-
-  // ---- x fragments of this warp's 128-column chunk: hi/lo fp16, per n-tile and k-step ----
-  uint32_t bh[NT][8][2], bl[NT][8][2];
-  float xs[NT][8];  // per-lane partial sums of x over its fragment columns, per 16-col k-step
-#pragma unroll
-  for (int n = 0; n < NT; n++) {
-    const int b = 8 * n + g;
-#pragma unroll
-    for (int j = 0; j < 8; j++) {
-      float v[4] = {0.f, 0.f, 0.f, 0.f};
-      const int64_t k = k0 + 16 * j + 2 * t;
-      if (active && b < a.batch) {
-        const float* xr = a.x + (int64_t)b * a.cols;
-        if (k < a.cols) {
-          float2 p = *reinterpret_cast<const float2*>(xr + k);
-          v[0] = p.x;
-          v[1] = p.y;
-        }
-        if (k + 8 < a.cols) {
-          float2 p = *reinterpret_cast<const float2*>(xr + k + 8);
-          v[2] = p.x;
-          v[3] = p.y;
-        }
-      }
-      __half2 h0 = __floats2half2_rn(v[0], v[1]);
-      __half2 h1 = __floats2half2_rn(v[2], v[3]);
-      float2 f0 = __half22float2(h0), f1 = __half22float2(h1);
-      __half2 l0 = __floats2half2_rn(v[0] - f0.x, v[1] - f0.y);
-      __half2 l1 = __floats2half2_rn(v[2] - f1.x, v[3] - f1.y);
-      bh[n][j][0] = *reinterpret_cast<uint32_t*>(&h0);
-      bh[n][j][1] = *reinterpret_cast<uint32_t*>(&h1);
-      bl[n][j][0] = *reinterpret_cast<uint32_t*>(&l0);
-      bl[n][j][1] = *reinterpret_cast<uint32_t*>(&l1);
-      float2 g0 = __half22float2(l0), g1 = __half22float2(l1);
-      xs[n][j] = (f0.x + g0.x) + (f0.y + g0.y) + (f1.x + g1.x) + (f1.y + g1.y);
-    }
-  }
-  // Block sums of x for the output columns this lane holds (batch 2t, 2t+1 of each n-tile).
-  // Q4_0 / Q4_K: per 32-col block (4 per chunk); Q2_0: one 128-col block.
-  constexpr int kXB = (QT == J4B_Q2_0) ? 1 : 4;
-  float xblk[NT][kXB][2];
-  if constexpr (QT != J4B_Q8_0) {
-#pragma unroll
-    for (int n = 0; n < NT; n++) {
-#pragma unroll
-      for (int q = 0; q < kXB; q++) {
-        float s = 0.f;
-        constexpr int kSteps = 8 / kXB;
-#pragma unroll
-        for (int j = 0; j < kSteps; j++) s += xs[n][q * kSteps + j];
-        s += __shfl_xor_sync(0xffffffffu, s, 1);
-        s += __shfl_xor_sync(0xffffffffu, s, 2);  // block sum of x for batch 8n+g
-        xblk[n][q][0] = __shfl_sync(0xffffffffu, s, 4 * (2 * t));
-        xblk[n][q][1] = __shfl_sync(0xffffffffu, s, 4 * (2 * t + 1));
-      }
-    }
-  }
-
-  int buf = 0;
-  for (int64_t tile = tile0; tile < tile1; tile++) {
-    float acc[NT][4];
-#pragma unroll
-    for (int n = 0; n < NT; n++) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
-
-    if (active) {
-      const int64_t gbase = tile * groups_total + k0 / 32;  // first 32-col group of the chunk
-      if constexpr (QT == J4B_Q8_0) {
-        const uint4* qp = reinterpret_cast<const uint4*>(a.quants + (gbase * 32) * 16) ;
-        uint4 line[4];
-        uint32_t sc[4];
-#pragma unroll
-        for (int q = 0; q < 4; q++) line[q] = __ldg(qp + q * 32 + lane);
-#pragma unroll
-        for (int q = 0; q < 4; q++)
-          sc[q] = __ldg(reinterpret_cast<const uint32_t*>(a.meta + ((gbase + q) * 8 + g) * 4));
-#pragma unroll
-        for (int q = 0; q < 4; q++) {
-          float tmp[NT][4];
-#pragma unroll
-          for (int n = 0; n < NT; n++) tmp[n][0] = tmp[n][1] = tmp[n][2] = tmp[n][3] = 0.f;
-          const uint32_t wv[4] = {line[q].x, line[q].y, line[q].z, line[q].w};
-#pragma unroll
-          for (int ks = 0; ks < 2; ks++) {
-            uint32_t a0, a1, a2, a3;
-            q8_pairs(wv[2 * ks], a0, a1);
-            q8_pairs(wv[2 * ks + 1], a2, a3);
-            const int j = 2 * q + ks;
-#pragma unroll
-            for (int n = 0; n < NT; n++) {
-              mma16816(tmp[n], a0, a1, a2, a3, bh[n][j][0], bh[n][j][1]);
-              mma16816(tmp[n], a0, a1, a2, a3, bl[n][j][0], bl[n][j][1]);
-            }
-          }
-          const float2 d = __half22float2(*reinterpret_cast<const __half2*>(&sc[q]));
-#pragma unroll
-          for (int n = 0; n < NT; n++) {
-            acc[n][0] = fmaf(d.x, tmp[n][0], acc[n][0]);
-            acc[n][1] = fmaf(d.x, tmp[n][1], acc[n][1]);
-            acc[n][2] = fmaf(d.y, tmp[n][2], acc[n][2]);
-            acc[n][3] = fmaf(d.y, tmp[n][3], acc[n][3]);
-          }
-        }
-      } else if constexpr (QT == J4B_Q4_0) {
-        const uint4* qp = reinterpret_cast<const uint4*>(a.quants + gbase * 32 * 8);
-        uint4 line[2];
-        uint32_t sc[4];
-#pragma unroll
-        for (int q = 0; q < 2; q++) line[q] = __ldg(qp + q * 32 + lane);
-#pragma unroll
-        for (int q = 0; q < 4; q++)
-          sc[q] = __ldg(reinterpret_cast<const uint32_t*>(a.meta + ((gbase + q) * 8 + g) * 4));
-        const uint32_t wv[8] = {line[0].x, line[0].y, line[0].z, line[0].w,
-                                line[1].x, line[1].y, line[1].z, line[1].w};
-#pragma unroll
-        for (int q = 0; q < 4; q++) {
-          float tmp[NT][4];
-#pragma unroll
-          for (int n = 0; n < NT; n++) tmp[n][0] = tmp[n][1] = tmp[n][2] = tmp[n][3] = 0.f;
-#pragma unroll
-          for (int ks = 0; ks < 2; ks++) {
-            uint32_t av[4];
-            q4_pairs(wv[2 * q + ks], av);
-            const int j = 2 * q + ks;
-#pragma unroll
-            for (int n = 0; n < NT; n++) {
-              mma16816(tmp[n], av[0], av[1], av[2], av[3], bh[n][j][0], bh[n][j][1]);
-              mma16816(tmp[n], av[0], av[1], av[2], av[3], bl[n][j][0], bl[n][j][1]);
-            }
-          }
-          // sum w x = d (16 C' - 24 X)
-          const float2 d = __half22float2(*reinterpret_cast<const __half2*>(&sc[q]));
-          const float c0 = 16.f * d.x, c1 = 16.f * d.y, x0 = -24.f * d.x, x1 = -24.f * d.y;
-#pragma unroll
-          for (int n = 0; n < NT; n++) {
-            acc[n][0] += fmaf(c0, tmp[n][0], x0 * xblk[n][q][0]);
-            acc[n][1] += fmaf(c0, tmp[n][1], x0 * xblk[n][q][1]);
-            acc[n][2] += fmaf(c1, tmp[n][2], x1 * xblk[n][q][0]);
-            acc[n][3] += fmaf(c1, tmp[n][3], x1 * xblk[n][q][1]);
-          }
-        }
-      } else if constexpr (QT == J4B_Q2_0) {
-        const uint4 line = __ldg(reinterpret_cast<const uint4*>(a.quants + gbase * 32 * 4) + lane);
-        const uint32_t sc = __ldg(reinterpret_cast<const uint32_t*>(a.meta + ((gbase / 4) * 8 + g) * 4));
-        const uint32_t wv[4] = {line.x, line.y, line.z, line.w};
-        float tmp[NT][4];
-#pragma unroll
-        for (int n = 0; n < NT; n++) tmp[n][0] = tmp[n][1] = tmp[n][2] = tmp[n][3] = 0.f;
-#pragma unroll
-        for (int q = 0; q < 4; q++) {
-#pragma unroll
-          for (int ks = 0; ks < 2; ks++) {
-            const uint32_t a0 = q2_pair(wv[q], 4 * ks), a1 = q2_pair(wv[q], 4 * ks + 1);
-            const uint32_t a2 = q2_pair(wv[q], 4 * ks + 2), a3 = q2_pair(wv[q], 4 * ks + 3);
-            const int j = 2 * q + ks;
-#pragma unroll
-            for (int n = 0; n < NT; n++) {
-              mma16816(tmp[n], a0, a1, a2, a3, bh[n][j][0], bh[n][j][1]);
-              mma16816(tmp[n], a0, a1, a2, a3, bl[n][j][0], bl[n][j][1]);
-            }
-          }
-        }
-        // sum w x = d (4 C' - 5 X)
-        const float2 d = __half22float2(*reinterpret_cast<const __half2*>(&sc));
-        const float c0 = 4.f * d.x, c1 = 4.f * d.y, x0 = -5.f * d.x, x1 = -5.f * d.y;
-#pragma unroll
-        for (int n = 0; n < NT; n++) {
-          acc[n][0] = fmaf(c0, tmp[n][0], x0 * xblk[n][0][0]);
-          acc[n][1] = fmaf(c0, tmp[n][1], x0 * xblk[n][0][1]);
-          acc[n][2] = fmaf(c1, tmp[n][2], x1 * xblk[n][0][0]);
-          acc[n][3] = fmaf(c1, tmp[n][3], x1 * xblk[n][0][1]);
-        }
-      } else {  // Q4_K: this chunk is half h of super-block sb
-        const int64_t sb = k0 / 256;
-        const int h = (int)((k0 / 128) & 1);
-        const int64_t sbs = a.kpad / 256;
-        const uint4* qp = reinterpret_cast<const uint4*>(
-            a.quants + (((tile * sbs + sb) * 2 + h) * 32 + lane) * 32);
-        const uint4 l0 = __ldg(qp), l1 = __ldg(qp + 1);
-        const uint8_t* mp = a.meta + ((tile * sbs + sb) * 8 + g) * 32;
-        const uint4 m0 = __ldg(reinterpret_cast<const uint4*>(mp));
-        const uint4 m1 = __ldg(reinterpret_cast<const uint4*>(mp + 16));
-        // Lane t decodes sub-block 4h+t for rows g and g+8: coefficients 16 d sc and
-        // -(16 d sc + dmin m); the group's four lanes then exchange them.
-        float cs[2], cx[2];
-        {
-          const uint4 mm[2] = {m0, m1};
-#pragma unroll
-          for (int r = 0; r < 2; r++) {
-            const uint32_t w0 = mm[r].x, w1 = mm[r].y, w2 = mm[r].z, w3 = mm[r].w;
-            const float d = __half2float(__ushort_as_half((uint16_t)(w0 & 0xFFFF)));
-            const float dmin = __half2float(__ushort_as_half((uint16_t)(w0 >> 16)));
-            // scale bytes q[0..11] are w1 (q0..3), w2 (q4..7), w3 (q8..11)
-            const int j = 4 * h + t;
-            int sc, mn;
-            if (j < 4) {
-              sc = (w1 >> (8 * j)) & 63;
-              mn = (w2 >> (8 * j)) & 63;
-            } else {
-              const int jj = j - 4;
-              const uint32_t qj4 = (w3 >> (8 * jj)) & 0xFF;  // q[j+4]
-              sc = (qj4 & 0xF) | (((w1 >> (8 * jj + 6)) & 3) << 4);
-              mn = (qj4 >> 4) | (((w2 >> (8 * jj + 6)) & 3) << 4);
-            }
-            const float ds = d * (float)sc;
-            cs[r] = 16.f * ds;
-            cx[r] = -fmaf(16.f, ds, dmin * (float)mn);
-          }
-        }
-        const uint32_t wv[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
-#pragma unroll
-        for (int q = 0; q < 4; q++) {
-          float tmp[NT][4];
-#pragma unroll
-          for (int n = 0; n < NT; n++) tmp[n][0] = tmp[n][1] = tmp[n][2] = tmp[n][3] = 0.f;
-#pragma unroll
-          for (int ks = 0; ks < 2; ks++) {
-            uint32_t av[4];
-            q4_pairs(wv[2 * q + ks], av);
-            const int j = 2 * q + ks;
-#pragma unroll
-            for (int n = 0; n < NT; n++) {
-              mma16816(tmp[n], av[0], av[1], av[2], av[3], bh[n][j][0], bh[n][j][1]);
-              mma16816(tmp[n], av[0], av[1], av[2], av[3], bl[n][j][0], bl[n][j][1]);
-            }
-          }
-          const int src = (lane & ~3) | q;
-          const float s0 = __shfl_sync(0xffffffffu, cs[0], src);
-          const float s1 = __shfl_sync(0xffffffffu, cs[1], src);
-          const float z0 = __shfl_sync(0xffffffffu, cx[0], src);
-          const float z1 = __shfl_sync(0xffffffffu, cx[1], src);
-#pragma unroll
-          for (int n = 0; n < NT; n++) {
-            acc[n][0] += fmaf(s0, tmp[n][0], z0 * xblk[n][q][0]);
-            acc[n][1] += fmaf(s0, tmp[n][1], z0 * xblk[n][q][1]);
-            acc[n][2] += fmaf(s1, tmp[n][2], z1 * xblk[n][q][0]);
-            acc[n][3] += fmaf(s1, tmp[n][3], z1 * xblk[n][q][1]);
-          }
-        }
-      }
-    }
-
-    // ---- sum the 8 warp partials of this row tile ----
-#pragma unroll
-    for (int n = 0; n < NT; n++)
-#pragma unroll
-      for (int c = 0; c < 4; c++) red[buf][warp][n * 4 + c][lane] = acc[n][c];
-    __syncthreads();
-    const int v = threadIdx.x;  // one (n, c, lane) value per thread
-    float total = 0.f;
-    int row = 0, bcol = 0;
-    const bool owner = v < NT * 4 * 32;
-    if (owner) {
-      const int nc = v / 32, ln = v % 32, n = nc / 4, c = nc % 4;
-#pragma unroll
-      for (int w = 0; w < kWarps; w++) total += red[buf][w][nc][ln];
-      row = (ln >> 2) + 8 * (c >> 1);
-      bcol = 8 * n + 2 * (ln & 3) + (c & 1);
-    }
-    if (a.ksplit == 1) {
-      if (owner) {
-        const int64_t r = tile * 16 + row;
-        if (r < a.rows && bcol < a.batch) {
-          if (a.add) total += a.add[(int64_t)bcol * a.rows + r];
-          a.y[(int64_t)bcol * a.rows + r] = total;
-        }
-      }
-    } else {
-      float* part = a.partials + ((int64_t)split * a.rt + tile) * 256;
-      if (owner) part[v] = total;
-      __threadfence();
-      __syncthreads();
-      if (threadIdx.x == 0) {
-        const unsigned prev = atomicAdd(a.arrivals + tile, 1u);
-        last_flag = prev == (unsigned)(a.ksplit - 1);
-      }
-      __syncthreads();
-      if (last_flag) {
-        __threadfence();
-        if (owner) {
-          float s = 0.f;
-          for (int sp = 0; sp < a.ksplit; sp++)
-            s += __ldcg(a.partials + ((int64_t)sp * a.rt + tile) * 256 + v);
-          const int64_t r = tile * 16 + row;
-          if (r < a.rows && bcol < a.batch) {
-            if (a.add) s += a.add[(int64_t)bcol * a.rows + r];
-            a.y[(int64_t)bcol * a.rows + r] = s;
-          }
-        }
-        if (threadIdx.x == 0) a.arrivals[tile] = 0u;
-      }
-    }
-    buf ^= 1;
-  }
-}
+#include "qgemv.cuh"
 
 // ---------------------------------------------------------------------------------------------
 // device encoder: byte-identical to the published block encoders the oracle restates
 // ---------------------------------------------------------------------------------------------
-__device__ inline void wr16(uint8_t* p, uint16_t v) {
-  p[0] = (uint8_t)(v & 0xff);
-  p[1] = (uint8_t)(v >> 8);
-}
 __device__ inline uint16_t f2h(float f) { return __half_as_ushort(__float2half_rn(f)); }
+
+// A block is assembled in a register array of 32-bit words, then written out byte by byte.
+struct BlockBytes {
+  uint32_t w[36] = {};
+  __device__ void put(int i, uint32_t v) { w[i >> 2] |= (v & 0xffu) << (8 * (i & 3)); }
+  __device__ void put16(int i, uint16_t v) {
+    put(i, v & 0xffu);
+    put(i + 1, v >> 8);
+  }
+  __device__ uint8_t get(int i) const { return (uint8_t)(w[i >> 2] >> (8 * (i & 3))); }
+};
 
 __global__ void quantize_kernel(int type, const float* __restrict__ w, int64_t rows, int64_t cols,
                                 uint8_t* __restrict__ out) {
@@ -637,17 +323,17 @@ __global__ void quantize_kernel(int type, const float* __restrict__ w, int64_t r
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= nblk) return;
   const float* src = w + idx * be;  // row-major: blocks of a row are consecutive
-  uint8_t* blk = out + idx * bb;
+  BlockBytes blk;
   if (type == J4B_Q8_0) {
     float amax = 0.f;
     for (int i = 0; i < 32; i++) amax = fmaxf(amax, fabsf(src[i]));
     const float d = __fdiv_rn(amax, 127.0f);
     const float id = d != 0.f ? __fdiv_rn(1.0f, d) : 0.f;
-    wr16(blk, f2h(d));
+    blk.put16(0, f2h(d));
     for (int i = 0; i < 32; i++) {
       int q = (int)roundf(__fmul_rn(src[i], id));
       q = max(-127, min(127, q));
-      blk[2 + i] = (uint8_t)(int8_t)q;
+      blk.put(2 + i, (uint32_t)(q & 0xff));
     }
   } else if (type == J4B_Q4_0) {
     float amax = 0.f, m = 0.f;
@@ -658,19 +344,19 @@ __global__ void quantize_kernel(int type, const float* __restrict__ w, int64_t r
       }
     const float d = __fdiv_rn(m, -8.0f);
     const float id = d != 0.f ? __fdiv_rn(1.0f, d) : 0.f;
-    wr16(blk, f2h(d));
+    blk.put16(0, f2h(d));
     for (int j = 0; j < 16; j++) {
       int q0 = (int)__fadd_rn(__fmul_rn(src[j], id), 8.5f);
       int q1 = (int)__fadd_rn(__fmul_rn(src[j + 16], id), 8.5f);
       q0 = max(0, min(15, q0));
       q1 = max(0, min(15, q1));
-      blk[2 + j] = (uint8_t)(q0 | (q1 << 4));
+      blk.put(2 + j, (uint32_t)(q0 | (q1 << 4)));
     }
   } else if (type == J4B_Q2_0) {
     float amax = 0.f;
     for (int i = 0; i < 128; i++) amax = fmaxf(amax, fabsf(src[i]));
     const float id = amax != 0.f ? __fdiv_rn(1.0f, amax) : 0.f;
-    wr16(blk, f2h(amax));
+    blk.put16(0, f2h(amax));
     for (int p = 0; p < 32; p++) {
       int byte = 0;
       for (int s = 0; s < 4; s++) {
@@ -678,7 +364,7 @@ __global__ void quantize_kernel(int type, const float* __restrict__ w, int64_t r
         q = max(-1, min(1, q));
         byte |= (q + 1) << (2 * s);
       }
-      blk[2 + p] = (uint8_t)byte;
+      blk.put(2 + p, (uint32_t)byte);
     }
   } else if (type == J4B_Q4_K) {
     float scale[8], mins[8], max_scale = 0.f, max_min = 0.f;
@@ -704,15 +390,13 @@ __global__ void quantize_kernel(int type, const float* __restrict__ w, int64_t r
       sc[j] = max(0, min(63, s));
       m[j] = max(0, min(63, mm));
     }
-    wr16(blk, dh);
-    wr16(blk + 2, mh);
-    uint8_t* sbp = blk + 4;
+    blk.put16(0, dh);
+    blk.put16(2, mh);
     for (int j = 0; j < 4; j++) {
-      sbp[j] = (uint8_t)((sc[j] & 63) | ((sc[j + 4] >> 4) << 6));
-      sbp[j + 4] = (uint8_t)((m[j] & 63) | ((m[j + 4] >> 4) << 6));
-      sbp[j + 8] = (uint8_t)((sc[j + 4] & 0xF) | ((m[j + 4] & 0xF) << 4));
+      blk.put(4 + j, (uint32_t)((sc[j] & 63) | ((sc[j + 4] >> 4) << 6)));
+      blk.put(8 + j, (uint32_t)((m[j] & 63) | ((m[j + 4] >> 4) << 6)));
+      blk.put(12 + j, (uint32_t)((sc[j + 4] & 0xF) | ((m[j + 4] & 0xF) << 4)));
     }
-    uint8_t* qs = blk + 16;
     for (int c = 0; c < 4; c++)
       for (int l = 0; l < 32; l++) {
         int q[2];
@@ -723,9 +407,11 @@ __global__ void quantize_kernel(int type, const float* __restrict__ w, int64_t r
           const int qq = ds > 0.f ? (int)roundf(__fdiv_rn(v, ds)) : 0;
           q[hh] = max(0, min(15, qq));
         }
-        qs[32 * c + l] = (uint8_t)(q[0] | (q[1] << 4));
+        blk.put(16 + 32 * c + l, (uint32_t)(q[0] | (q[1] << 4)));
       }
   }
+  uint8_t* dst = out + idx * bb;
+  for (int i = 0; i < bb; i++) dst[i] = blk.get(i);
 }
 
 int qtype_ok(int t) { return block_elems(t) > 0; }
@@ -742,29 +428,26 @@ int upload_common(int dev, const uint8_t* dblob, int type, int64_t rows, int64_t
   w->kpad = (cols + kWarpCols - 1) / kWarpCols * kWarpCols;
   if (type == J4B_Q4_K) w->kpad = (cols + 255) / 256 * 256;
   w->ksplit = (int)((w->kpad + kCtaCols - 1) / kCtaCols);
-  const int64_t groups = w->kpad / 32;
-  w->quant_bytes = (size_t)(w->rt * groups * 32) * (type == J4B_Q8_0 ? 16 : (type == J4B_Q2_0 ? 4 : 8));
-  const int be = block_elems(type);
-  w->meta_bytes = (size_t)(w->rt * (w->kpad / be) * 16) * (type == J4B_Q4_K ? 16 : 2);
-  cudaError_t e = cudaMalloc(&w->quants, w->quant_bytes);
-  if (e == cudaSuccess) e = cudaMalloc(&w->meta, w->meta_bytes);
-  if (e == cudaSuccess && w->ksplit > 1) {
+  const Layout L = layout_of(w);
+  w->data_bytes = (size_t)L.total_bytes();
+  cudaError_t e = cudaMalloc(&w->data, w->data_bytes);
+  if (e == cudaSuccess && w->ksplit > 1)
     e = cudaMalloc(&w->partials, (size_t)w->ksplit * w->rt * 256 * sizeof(float));
-    if (e == cudaSuccess) e = cudaMalloc(&w->arrivals, (size_t)w->rt * sizeof(unsigned));
-    if (e == cudaSuccess) e = cudaMemsetAsync(w->arrivals, 0, (size_t)w->rt * sizeof(unsigned), stream);
-  }
+  if (e == cudaSuccess) e = cudaMalloc(&w->arrivals, (size_t)(w->rt + 1) * sizeof(unsigned));
+  if (e == cudaSuccess)
+    e = cudaMemsetAsync(w->arrivals, 0, (size_t)(w->rt + 1) * sizeof(unsigned), stream);
+  if (e == cudaSuccess) w->status = (int*)(w->arrivals + w->rt);
   if (e != cudaSuccess) {
-    cudaFree(w->quants);
-    cudaFree(w->meta);
+    cudaFree(w->data);
     cudaFree(w->partials);
     cudaFree(w->arrivals);
     delete w;
     return cuda_error(e, "quantized weight allocation");
   }
-  counters().allocations += w->ksplit > 1 ? 4 : 2;
+  counters().allocations += w->ksplit > 1 ? 3 : 2;
   {
-    const int64_t n = w->rt * groups * 32;
-    repack_quants_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(type, dblob, rows, cols, w->rt, w->kpad, w->quants);
+    const int64_t n = w->rt * (w->kpad / 32) * 32;
+    repack_quants_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(L, dblob, rows, cols, w->data);
     cudaError_t le = cudaGetLastError();
     if (le != cudaSuccess) {
       j4b_quant_free(w);
@@ -773,8 +456,8 @@ int upload_common(int dev, const uint8_t* dblob, int type, int64_t rows, int64_t
     count_launch();
   }
   {
-    const int64_t n = w->rt * (w->kpad / be) * 16;
-    repack_meta_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(type, dblob, rows, cols, w->rt, w->kpad, w->meta);
+    const int64_t n = w->rt * (w->kpad / block_elems(type)) * 16;
+    repack_meta_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(L, dblob, rows, cols, w->data);
     cudaError_t le = cudaGetLastError();
     if (le != cudaSuccess) {
       j4b_quant_free(w);
@@ -796,40 +479,6 @@ int check_geometry(int type, int64_t rows, int64_t cols, size_t bytes) {
   if ((int64_t)bytes != need)
     return set_error(J4B_EINVAL, "quant blob is %zu bytes, shape needs %lld", bytes, (long long)need);
   return J4B_OK;
-}
-
-template <int QT, int NT>
-cudaError_t launch_gemv(const j4b_qweight* w, const float* x, const float* add, float* y,
-                        int batch, int sms, cudaStream_t stream) {
-  GemvArgs a;
-  a.quants = w->quants;
-  a.meta = w->meta;
-  a.rows = w->rows;
-  a.cols = w->cols;
-  a.kpad = w->kpad;
-  a.rt = w->rt;
-  a.x = x;
-  a.add = add;
-  a.y = y;
-  a.batch = batch;
-  a.ksplit = w->ksplit;
-  a.partials = w->partials;
-  a.arrivals = w->arrivals;
-  // Aim at two resident CTAs per SM in a single wave.
-  const int64_t slots = 2ll * sms;
-  int64_t tiles = (w->rt * w->ksplit + slots - 1) / slots;
-  if (tiles < 1) tiles = 1;
-  a.tiles_per_cta = (int)tiles;
-  const int64_t grid = (w->rt + tiles - 1) / tiles * w->ksplit;
-  qgemv_kernel<QT, NT><<<(unsigned)grid, 256, 0, stream>>>(a);
-  return cudaGetLastError();
-}
-
-template <int QT>
-cudaError_t gemv_dispatch(const j4b_qweight* w, const float* x, const float* add, float* y,
-                          int batch, int sms, cudaStream_t stream) {
-  if (batch <= 8) return launch_gemv<QT, 1>(w, x, add, y, batch, sms, stream);
-  return launch_gemv<QT, 2>(w, x, add, y, batch, sms, stream);
 }
 
 }  // namespace
@@ -895,11 +544,10 @@ extern "C" int j4b_quant_upload_device(int dev, j4b_buf blocks, size_t bytes, in
 extern "C" int j4b_quant_free(j4b_qweight_t w) {
   if (!w) return J4B_OK;
   DeviceGuard guard(w->dev);
-  cudaFree(w->quants);
-  cudaFree(w->meta);
+  cudaFree(w->data);
   cudaFree(w->partials);
   cudaFree(w->arrivals);
-  counters().releases += w->partials ? 4 : 2;
+  counters().releases += w->partials ? 3 : 2;
   delete w;
   return J4B_OK;
 }
@@ -946,7 +594,8 @@ extern "C" int j4b_quant_gather_row(j4b_qweight_t w, int64_t row, j4b_buf out, j
   J4B_REQUIRE(out, "quantGatherRow needs an output buffer");
   DeviceGuard guard(w->dev);
   cudaStream_t stream = resolve_stream(w->dev, s);
-  gather_row_kernel<<<(unsigned)((w->cols + 255) / 256), 256, 0, stream>>>(*w, row, (float*)(uintptr_t)out);
+  gather_row_kernel<<<(unsigned)((w->cols + 255) / 256), 256, 0, stream>>>(
+      layout_of(w), w->data, w->cols, row, (float*)(uintptr_t)out);
   J4B_CHECK_LAUNCH("gather_row_kernel");
   return J4B_OK;
 }
