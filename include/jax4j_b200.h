@@ -144,6 +144,15 @@ int j4b_reindex(j4b_buf a, int64_t n_src, j4b_buf map, int64_t n_dst, j4b_buf ou
                 j4b_stream s);
 int j4b_scatter_add(j4b_buf a, int64_t n_src, j4b_buf map, int64_t n_dst, j4b_buf out,
                     j4b_stream s);
+/* Full sum that allocates nothing (no counterpart in the reference). For callers that cannot
+ * allocate device memory while they run -- code inside CUDA stream capture in global capture
+ * mode, or a host that fixes its device-memory budget up front -- where j4b_reduce_sum would
+ * allocate its block partials. Same result as j4b_reduce_sum (double accumulation, one float
+ * out) within the sums' rounding. Its scratch is a static device array of 512 KiB per GPU that
+ * loads the library, held until exit, so n is limited to 134,217,728 elements (J4B_EINVAL
+ * above that). The first call on a device looks the array up and zeroes its counter, so make
+ * it before any stream capture. All calls share the array: calls that overlap on the GPU race. */
+int j4b_reduce_sum_noalloc(j4b_buf a, int64_t n, j4b_buf out, j4b_stream s);
 /* reluBackward: ComputeBackend.java:202-203 */
 int j4b_relu_backward(j4b_buf upstream, j4b_buf input, j4b_buf out, int64_t n, j4b_stream s);
 /* randomUniform / randomNormal: ComputeBackend.java:50-76 (bit-exact uniforms) */

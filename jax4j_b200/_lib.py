@@ -59,6 +59,7 @@ SIGNATURES = {
     "j4b_transpose": [_u64, _u64, _i64, _i64, _vp],
     "j4b_reduce_sum": [_u64, _i64, _u64, _vp],
     "j4b_reduce_max": [_u64, _i64, _u64, _vp],
+    "j4b_reduce_sum_noalloc": [_u64, _i64, _u64, _vp],
     "j4b_sum_axis": [_u64, _i64, _i64, _i64, _u64, _vp],
     "j4b_max_axis": [_u64, _i64, _i64, _i64, _u64, _vp],
     "j4b_argmax_axis": [_u64, _i64, _i64, _i64, _u64, _vp],

@@ -9,6 +9,7 @@
 #include <cuda_runtime.h>
 
 #include <cstring>
+#include <mutex>
 
 #include "j4b_internal.h"
 #include "j4b_math.cuh"
@@ -602,5 +603,108 @@ extern "C" int j4b_matmul(j4b_buf a, j4b_buf b, j4b_buf out, int64_t batch, int6
   sgemm_kernel<<<grid, 256, 0, stream>>>((const float*)(uintptr_t)a, (const float*)(uintptr_t)b,
                                          (float*)(uintptr_t)out, m, k, n);
   J4B_CHECK_LAUNCH("sgemm_kernel");
+  return J4B_OK;
+}
+
+// ---------------------------------------------------------------------------------------------
+// Full sum without any allocation.
+//
+// Some callers cannot allocate device memory when they reduce: code that runs inside CUDA stream
+// capture in global capture mode (where allocation calls are errors), and hosts that reserve a
+// fixed device-memory budget up front and forbid growth afterwards (a JVM that hands the engine
+// a pre-sized arena, a serving loop that must not take allocator locks). j4b_reduce_sum above
+// allocates its block partials on every call; this variant keeps them in the static array below,
+// which every GPU that loads the library holds until the process exits (512 KiB + 256 bytes).
+//
+// Layout of the array: one double per 2048-element chunk of the input (at most 65536 chunks,
+// so at most 134,217,728 elements per call), then one 64-bit arrival counter. Each call rewrites
+// the partials it uses; the counter must start at zero, is zeroed at set-up and is reset by the
+// last block of every call. All calls share the array: calls that overlap on the GPU (on
+// different streams, or from different threads without ordering) race and give wrong sums.
+// ---------------------------------------------------------------------------------------------
+namespace j4b {
+namespace {
+
+constexpr int64_t kNoallocChunk = 2048;      // elements per block (256 threads x 8)
+constexpr int64_t kNoallocMaxChunks = 65536;  // partials the static array holds
+static __device__ __align__(256) double g_reduce_noalloc_scratch[kNoallocMaxChunks + 32];
+
+std::mutex g_noalloc_mu;
+double* g_noalloc_ptr[kMaxDevices] = {};
+
+// Device address of the static scratch on `dev`, looked up (and its counter zeroed) on the first
+// call for that device, with the device current.
+int noalloc_scratch(int dev, cudaStream_t stream, double** out) {
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    J4B_CUDA(cudaGetSymbolAddress(&p, g_reduce_noalloc_scratch), "cudaGetSymbolAddress");
+    J4B_CUDA(cudaMemsetAsync((double*)p + kNoallocMaxChunks, 0, sizeof(double), stream),
+             "cudaMemsetAsync(reduce scratch counter)");
+    g_noalloc_ptr[dev] = (double*)p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return J4B_OK;
+}
+
+__global__ void reduce_sum_noalloc_kernel(const float* __restrict__ a, int64_t n,
+                                          double* __restrict__ scratch, float* __restrict__ out) {
+  __shared__ double sh[32];
+  __shared__ bool last;
+  unsigned long long* counter = reinterpret_cast<unsigned long long*>(scratch + kNoallocMaxChunks);
+  const int64_t base = (int64_t)blockIdx.x * kNoallocChunk;
+  double acc = 0.0;
+#pragma unroll
+  for (int i = 0; i < 8; i++) {
+    const int64_t k = base + i * 256 + threadIdx.x;
+    if (k < n) acc += a[k];
+  }
+  acc = warp_sum(acc);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) sh[warp] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double v = 0.0;
+    for (int w = 0; w < 8; w++) v += sh[w];
+    scratch[blockIdx.x] = v;
+    __threadfence();
+    last = atomicAdd(counter, 1ull) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  // The last block folds the partials: thread t takes partials t, t+256, ... in order, then the
+  // warps and the block combine in a fixed order, so the result does not depend on timing.
+  double v = 0.0;
+  for (int64_t b = threadIdx.x; b < gridDim.x; b += 256) v += __ldcg(scratch + b);
+  v = warp_sum(v);
+  if (lane == 0) sh[warp] = v;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double total = 0.0;
+    for (int w = 0; w < 8; w++) total += sh[w];
+    out[0] = (float)total;
+    *counter = 0ull;
+  }
+}
+
+}  // namespace
+}  // namespace j4b
+
+extern "C" int j4b_reduce_sum_noalloc(j4b_buf a, int64_t n, j4b_buf out, j4b_stream s) {
+  J4B_REQUIRE(n >= 0, "negative element count");
+  J4B_REQUIRE(n <= kNoallocChunk * kNoallocMaxChunks,
+              "reduce_sum_noalloc sums at most %lld elements (its static scratch holds %lld "
+              "partials of %lld elements); got %lld",
+              (long long)(kNoallocChunk * kNoallocMaxChunks), (long long)kNoallocMaxChunks,
+              (long long)kNoallocChunk, (long long)n);
+  J4B_DEVICE_OF(out);
+  double* scratch = nullptr;
+  int st = noalloc_scratch(dev, stream, &scratch);
+  if (st) return st;
+  const int64_t chunks = n == 0 ? 1 : (n + kNoallocChunk - 1) / kNoallocChunk;
+  reduce_sum_noalloc_kernel<<<(unsigned)chunks, 256, 0, stream>>>((const float*)(uintptr_t)a, n,
+                                                                   scratch, (float*)(uintptr_t)out);
+  J4B_CHECK_LAUNCH("reduce_sum_noalloc_kernel");
   return J4B_OK;
 }
