@@ -10,7 +10,7 @@
 #include <cstdio>
 #include <string>
 
-#include "../../include/jax4j_b200.h"
+#include "jax4j_b200.h"
 
 namespace j4b {
 

@@ -1,6 +1,6 @@
 // Batched dequant-GEMV kernel (included by quant.cu inside namespace j4b::<anonymous>).
 //
-// Two CTAs per SM. A CTA owns one 1024-column K range ("split") of a run of 16-row tiles. For
+// One CTA of 16 warps per SM. A CTA owns one 1024-column K range ("split") of a run of 16-row tiles. For
 // each tile, the K range's quant bytes and scale bytes are contiguous in the repacked layout, so
 // one elected thread streams them into a ring of shared-memory stages with 1-D TMA bulk copies
 // (cp.async.bulk, completion counted on an mbarrier); the eight warps decode their 128-column
@@ -16,7 +16,7 @@
 // Every mbarrier wait is bounded: on timeout the CTA records an error code in the weight's
 // status word, waits (bounded) for its copies in flight, and returns.
 
-constexpr int kGemvThreads = 256;
+constexpr int kGemvThreads = 512;
 constexpr uint32_t kWaitLimit = 1u << 26;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -104,16 +104,19 @@ __device__ __forceinline__ uint32_t q2_pair(uint32_t w, int p) {
   return lop_or(rotr(w, 2 * p), 0x03000300u, 0x3C003C00u);
 }
 
-// Tiles per bulk copy (one copy of ~35 KB: bulk-copy throughput grows with the copy size), the
-// copies kept in flight, and the per-stage warp-partial buffer.
+// Bytes of one tile chunk, and the tiles per bulk copy: as many as two stages, the staged x and
+// the warp-partial buffer leave room for in shared memory (a copy of 35-147 KB; bulk-copy
+// throughput grows with the copy size, and more tiles per stage means fewer barriers and more
+// independent mma chains per warp).
 template <int QT>
 struct GemvTraits {
   static constexpr int kQ = QT == J4B_Q8_0 ? 512 : (QT == J4B_Q2_0 ? 128 : 256);
   static constexpr int kM = QT == J4B_Q2_0 ? 8 : 32;
   static constexpr int kChunk = 32 * (kQ + kM);  // bytes of one full tile chunk
-  static constexpr int kTilesPerCopy = QT == J4B_Q8_0 ? 2 : 4;
   static constexpr int kStages = 2;
 };
+template <int QT, int NT>
+constexpr int kTilesPerCopy = QT == J4B_Q8_0 ? (NT == 1 ? 4 : 2) : (QT == J4B_Q2_0 ? 8 : (NT == 1 ? 8 : 4));
 
 struct GemvArgs {
   const uint8_t* data;
@@ -125,15 +128,21 @@ struct GemvArgs {
   int batch;  // batch rows handled by this launch (<= 8 * NT)
   int ksplit;
   int tiles_per_cta;
-  float* partials;     // [ksplit][rt][256]
+  int cluster;         // 1: the ksplit CTAs of a tile group form a cluster and fold through DSMEM
+  float* partials;     // [ksplit][rt][256] (global split-K fold only)
   unsigned* arrivals;  // one counter per tile group
   int* status;         // nonzero after a bounded wait gave up
 };
 
+constexpr int kXStride = 1024 + 4;  // floats per staged x row (padding spreads the banks)
+
+// Shared memory: [stages | warp partials | staged x | stage barriers | (cluster mode) this CTA's
+// per-tile totals]. The cluster fold reuses the bytes from offset 0 as the leader's landing area.
 template <int QT, int NT>
-__host__ __device__ constexpr int gemv_smem_bytes() {
-  return GemvTraits<QT>::kStages * GemvTraits<QT>::kTilesPerCopy * GemvTraits<QT>::kChunk +
-         GemvTraits<QT>::kTilesPerCopy * 8 * NT * 128 * 4 + GemvTraits<QT>::kStages * 8 + 16;
+__host__ __device__ constexpr int gemv_smem_base() {
+  return GemvTraits<QT>::kStages * kTilesPerCopy<QT, NT> * GemvTraits<QT>::kChunk +
+         kTilesPerCopy<QT, NT> * 8 * NT * 128 * 4 + 8 * NT * kXStride * 4 +
+         GemvTraits<QT>::kStages * 8 + 16;
 }
 
 template <int QT>
@@ -145,7 +154,7 @@ constexpr int kXBlocks = QT == J4B_Q2_0 ? 1 : 4;  // x block sums per warp chunk
 // each dependent chain is two mma long.
 template <int QT, int NT>
 __device__ __forceinline__ void tile_compute(const uint8_t* __restrict__ sq,
-                                             const uint8_t* __restrict__ sm, int warp, int lane,
+                                             const uint8_t* __restrict__ sm, int warp, int lane,  // warp = K chunk 0..7
                                              const uint32_t (&bh)[NT][8][2],
                                              const uint32_t (&bl)[NT][8][2],
                                              const float (&xblk)[NT][kXBlocks<QT>][2],
@@ -298,6 +307,22 @@ __device__ __forceinline__ void tile_compute(const uint8_t* __restrict__ sq,
   }
 }
 
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Full cluster barrier with release/acquire ordering of shared::cluster accesses.
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Store to the same shared-memory offset in CTA `rank` of the cluster.
+__device__ __forceinline__ void st_cluster_f32(const void* local, uint32_t rank, float v) {
+  uint32_t raddr;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(raddr) : "r"(smem_u32(local)), "r"(rank));
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(raddr), "f"(v) : "memory");
+}
+
 // Output element v (0 .. NT*128) of a tile's 16 x (8 NT) block -> (row in tile, batch column).
 __device__ __forceinline__ void out_coord(int v, int& row, int& bcol) {
   const int nc = v >> 5, ln = v & 31, n = nc >> 2, c = nc & 3;
@@ -306,18 +331,23 @@ __device__ __forceinline__ void out_coord(int v, int& row, int& bcol) {
 }
 
 template <int QT, int NT>
-__global__ void __launch_bounds__(kGemvThreads, 2) qgemv_kernel(GemvArgs a) {
+__global__ void __launch_bounds__(kGemvThreads, 1) qgemv_kernel(GemvArgs a) {
   using T = GemvTraits<QT>;
-  constexpr int kStages = T::kStages, kM = T::kTilesPerCopy;
+  constexpr int kStages = T::kStages, kM = kTilesPerCopy<QT, NT>;
   constexpr int kStageBytes = kM * T::kChunk;
   constexpr int kVals = NT * 128;  // outputs of one tile
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* stage_base = smem;
-  float* red = reinterpret_cast<float*>(smem + kStages * kStageBytes);  // [kM][8 warps][kVals]
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes + kM * 8 * kVals * 4);
+  float* red = reinterpret_cast<float*>(smem + kStages * kStageBytes);  // [kM][8 chunks][kVals]
+  float* xstage = red + kM * 8 * kVals;                                  // [8 NT][kXStride]
+  uint64_t* full = reinterpret_cast<uint64_t*>(xstage + 8 * NT * kXStride);
+  float* mine = reinterpret_cast<float*>(smem + gemv_smem_base<QT, NT>());  // cluster mode only
   __shared__ int last_flag;
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  // 16 warps: warp w works on the 128-column chunk w % 8 of the CTA's K range, for the tiles of
+  // each stage whose index has the parity w / 8.
+  const int chunk = warp & 7, sub = warp >> 3;
   const int g = lane >> 2, t = lane & 3;
   const int split = blockIdx.x % a.ksplit;
   const int group = blockIdx.x / a.ksplit;
@@ -325,16 +355,17 @@ __global__ void __launch_bounds__(kGemvThreads, 2) qgemv_kernel(GemvArgs a) {
   const int64_t tile1 = min(tile0 + a.tiles_per_cta, a.rt);
   const int ntiles = (int)(tile1 - tile0);
   const int ncopies = (ntiles + kM - 1) / kM;
-  const int64_t k0 = (int64_t)split * 1024 + warp * 128;  // this warp's 128-column chunk
+  const int64_t kc0 = (int64_t)split * 1024;
+  const int64_t k0 = kc0 + chunk * 128;  // this warp's 128-column chunk
   const bool active = k0 < a.kpad;
   const int groups_here = a.L.groups_in_split(split);
-  const uint32_t chunk = (uint32_t)a.L.chunk_bytes(split);  // bytes of one tile of this split
+  const uint32_t chunk_bytes = (uint32_t)a.L.chunk_bytes(split);  // one tile of this split
   const uint32_t meta_off = (uint32_t)(groups_here * T::kQ);
 
   // copy c brings tiles [c*kM, min((c+1)*kM, ntiles)) into stage c % kStages
   auto issue = [&](int c) {
     const int first = c * kM, count = min(kM, ntiles - first);
-    const uint32_t bytes = (uint32_t)count * chunk;
+    const uint32_t bytes = (uint32_t)count * chunk_bytes;
     uint64_t* bar = &full[c % kStages];
     mbar_expect_tx(bar, bytes);
     tma_load_1d(stage_base + (c % kStages) * kStageBytes,
@@ -354,29 +385,37 @@ __global__ void __launch_bounds__(kGemvThreads, 2) qgemv_kernel(GemvArgs a) {
   pdl_launch_dependents();
   pdl_wait();
 
+  // ---- x: the CTA's 1024-column slice of every batch row, staged once in shared memory with
+  // coalesced 128-bit loads (columns past K and rows past the batch are zeros) ----
+  {
+    constexpr int kPer = 8 * NT * 256 / kGemvThreads;  // float4s per thread
+    float4 v[kPer];
+#pragma unroll
+    for (int u = 0; u < kPer; u++) {  // all loads first: one round trip, not kPer
+      const int idx = threadIdx.x + u * kGemvThreads, b = idx >> 8, c4 = idx & 255;
+      const int64_t k = kc0 + 4 * c4;
+      const bool ok = b < a.batch && k < a.cols;
+      v[u] = __ldg(reinterpret_cast<const float4*>(a.x + (ok ? (int64_t)b * a.cols + k : 0)));
+      if (!ok) v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int u = 0; u < kPer; u++) {
+      const int idx = threadIdx.x + u * kGemvThreads, b = idx >> 8, c4 = idx & 255;
+      *reinterpret_cast<float4*>(xstage + b * kXStride + 4 * c4) = v[u];
+    }
+  }
+  __syncthreads();
   // ---- x fragments of this warp's 128-column chunk: hi/lo fp16, per n-tile and k-step ----
-  // Addresses are clamped into the tensor and out-of-range lanes select zero, so all loads are
-  // unconditional and issue back to back.
   uint32_t bh[NT][8][2], bl[NT][8][2];
   float xs[NT][8];
 #pragma unroll
   for (int n = 0; n < NT; n++) {
-    const int b = 8 * n + g;
-    const bool brow = active && b < a.batch;
-    const float* xr = a.x + (int64_t)min(b, a.batch - 1) * a.cols;
-    float2 p0[8], p1[8];
+    const float* xr = xstage + (8 * n + g) * kXStride + chunk * 128 + 2 * t;
 #pragma unroll
     for (int j = 0; j < 8; j++) {
-      const int64_t k = k0 + 16 * j + 2 * t;
-      p0[j] = __ldg(reinterpret_cast<const float2*>(xr + min(k, a.cols - 2)));
-      p1[j] = __ldg(reinterpret_cast<const float2*>(xr + min(k + 8, a.cols - 2)));
-    }
-#pragma unroll
-    for (int j = 0; j < 8; j++) {
-      const int64_t k = k0 + 16 * j + 2 * t;
-      const bool v0ok = brow && k < a.cols, v1ok = brow && k + 8 < a.cols;
-      const float v[4] = {v0ok ? p0[j].x : 0.f, v0ok ? p0[j].y : 0.f, v1ok ? p1[j].x : 0.f,
-                          v1ok ? p1[j].y : 0.f};
+      const float2 p0 = *reinterpret_cast<const float2*>(xr + 16 * j);
+      const float2 p1 = *reinterpret_cast<const float2*>(xr + 16 * j + 8);
+      const float v[4] = {p0.x, p0.y, p1.x, p1.y};
       __half2 h0 = __floats2half2_rn(v[0], v[1]);
       __half2 h1 = __floats2half2_rn(v[2], v[3]);
       const float2 f0 = __half22float2(h0), f1 = __half22float2(h1);
@@ -416,21 +455,24 @@ __global__ void __launch_bounds__(kGemvThreads, 2) qgemv_kernel(GemvArgs a) {
     const int s = c % kStages;
     const int count = min(kM, ntiles - c * kM);
     if (!mbar_wait_bounded(&full[s], (uint32_t)((c / kStages) & 1))) failed = true;
-    float acc[kM][NT][4] = {};
+    constexpr int kMine = kM / 2;  // tiles of the stage this warp computes: sub, sub + 2, ...
+    float acc[kMine][NT][4] = {};
     if (active && !failed) {
       const uint8_t* st = stage_base + s * kStageBytes;
-      // all kM tiles are computed so their mma chains interleave; tiles past `count` read
-      // stale stage bytes and are discarded
+      // tiles past `count` read stale stage bytes and are discarded
 #pragma unroll
-      for (int j = 0; j < kM; j++)
-        tile_compute<QT, NT>(st + j * chunk, st + j * chunk + meta_off, warp, lane, bh, bl, xblk, acc[j]);
+      for (int jj = 0; jj < kMine; jj++) {
+        const int j = sub + 2 * jj;
+        tile_compute<QT, NT>(st + j * chunk_bytes, st + j * chunk_bytes + meta_off, chunk, lane, bh, bl, xblk, acc[jj]);
+      }
     }
 #pragma unroll
-    for (int j = 0; j < kM; j++)
+    for (int jj = 0; jj < kMine; jj++)
 #pragma unroll
       for (int n = 0; n < NT; n++)
 #pragma unroll
-        for (int cc = 0; cc < 4; cc++) red[(j * 8 + warp) * kVals + (n * 4 + cc) * 32 + lane] = acc[j][n][cc];
+        for (int cc = 0; cc < 4; cc++)
+          red[((sub + 2 * jj) * 8 + chunk) * kVals + (n * 4 + cc) * 32 + lane] = acc[jj][n][cc];
     if (__syncthreads_or(failed)) {
       failed = true;
       break;
@@ -455,6 +497,8 @@ __global__ void __launch_bounds__(kGemvThreads, 2) qgemv_kernel(GemvArgs a) {
           if (a.add) total += a.add[(int64_t)bcol * a.rows + r];
           a.y[(int64_t)bcol * a.rows + r] = total;
         }
+      } else if (a.cluster) {
+        mine[(c * kM + j) * kVals + v] = total;
       } else {
         a.partials[((int64_t)split * a.rt + tile) * 256 + v] = total;
       }
@@ -463,11 +507,40 @@ __global__ void __launch_bounds__(kGemvThreads, 2) qgemv_kernel(GemvArgs a) {
   }
 
   if (failed) {
-    // Let copies still in flight land before the CTA's shared memory is released.
+    // Let copies still in flight land before the CTA's shared memory is reused or released.
     if (threadIdx.x == 0) {
       atomicExch(a.status, 1);
       for (int cc = consumed; cc < issued; cc++)  // bounded wait for each copy still in flight
         mbar_wait_bounded(&full[cc % kStages], (uint32_t)((cc / kStages) & 1));
+    }
+    __syncthreads();
+    if (!a.cluster) return;  // cluster members still take both cluster barriers below
+  }
+
+  if (a.cluster) {
+    // Split-K fold inside the cluster: every CTA is past its main loop (barrier 1), CTAs 1.. push
+    // their per-tile totals into CTA 0's shared memory from offset 0, where its stages were
+    // (barrier 2), and CTA 0 adds them in split order, so the result is deterministic.
+    const uint32_t rank = cluster_ctarank();
+    const int nv = ntiles * kVals;
+    float* landing = reinterpret_cast<float*>(smem);  // [ksplit - 1][nv] in CTA 0
+    cluster_sync();
+    if (rank != 0)
+      for (int i = threadIdx.x; i < nv; i += kGemvThreads)
+        st_cluster_f32(landing + (rank - 1) * nv + i, 0, mine[i]);
+    cluster_sync();
+    if (rank == 0 && !failed) {
+      for (int i = threadIdx.x; i < nv; i += kGemvThreads) {
+        float total = mine[i];
+        for (int sp = 1; sp < a.ksplit; sp++) total += landing[(sp - 1) * nv + i];
+        int row, bcol;
+        out_coord(i % kVals, row, bcol);
+        const int64_t r = (tile0 + i / kVals) * 16 + row;
+        if (r < a.rows && bcol < a.batch) {
+          if (a.add) total += a.add[(int64_t)bcol * a.rows + r];
+          a.y[(int64_t)bcol * a.rows + r] = total;
+        }
+      }
     }
     return;
   }
@@ -514,13 +587,23 @@ __global__ void __launch_bounds__(kGemvThreads, 2) qgemv_kernel(GemvArgs a) {
 template <int QT, int NT>
 cudaError_t launch_gemv(const j4b_qweight* w, const float* x, const float* add, float* y,
                         int batch, int sms, cudaStream_t stream) {
-  static bool configured = false;  // one attribute call per instantiation
-  constexpr int smem = gemv_smem_bytes<QT, NT>();
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(qgemv_kernel<QT, NT>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  // Largest dynamic shared memory a CTA may request: the device's opt-in limit minus the
+  // kernel's static shared memory (set once per instantiation).
+  static int64_t kMaxSmem = -1;
+  constexpr int base = gemv_smem_base<QT, NT>();
+  constexpr int kVals = NT * 128;
+  if (kMaxSmem < 0) {
+    int dev = 0, optin = 0;
+    cudaGetDevice(&dev);
+    cudaError_t e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    cudaFuncAttributes fa;
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, qgemv_kernel<QT, NT>);
     if (e != cudaSuccess) return e;
-    configured = true;
+    const int64_t lim = (int64_t)optin - (int64_t)fa.sharedSizeBytes;
+    if (lim < base) return cudaErrorInvalidConfiguration;
+    e = cudaFuncSetAttribute(qgemv_kernel<QT, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)lim);
+    if (e != cudaSuccess) return e;
+    kMaxSmem = lim;
   }
   GemvArgs a;
   a.data = w->data;
@@ -537,22 +620,62 @@ cudaError_t launch_gemv(const j4b_qweight* w, const float* x, const float* add, 
   a.partials = w->partials;
   a.arrivals = w->arrivals;
   a.status = w->status;
-  // Two CTAs per SM (16 warps to hide the mma / shared-memory latencies): as many tile groups as
-  // fit next to the K splits, tiles shared out evenly.
-  const int64_t groups_fit = std::max<int64_t>(1, 2ll * sms / w->ksplit);
-  const int64_t tiles = (w->rt + groups_fit - 1) / groups_fit;
+  // One 16-warp CTA per SM: as many tile groups as fit next to the K splits, tiles shared out
+  // evenly.
+  int64_t groups_fit = std::max<int64_t>(1, (int64_t)sms / w->ksplit);
+  int64_t tiles = (w->rt + groups_fit - 1) / groups_fit;
+  int64_t groups = (w->rt + tiles - 1) / tiles;
+  // Cluster split-K fold when the splits fit one portable cluster, the per-tile totals fit next
+  // to the base layout, the landing area fits below them, and every cluster is co-resident.
+  int64_t smem = base;
+  a.cluster = 0;
+  if (w->ksplit >= 2 && w->ksplit <= 8) {
+    const int64_t need = base + tiles * kVals * 4;
+    const int64_t landing = (w->ksplit - 1) * tiles * kVals * 4;
+    if (need <= kMaxSmem && landing <= base) {
+      cudaLaunchConfig_t occ = {};
+      occ.gridDim = dim3((unsigned)(groups * w->ksplit));
+      occ.blockDim = dim3(kGemvThreads);
+      occ.dynamicSmemBytes = (size_t)need;
+      cudaLaunchAttribute ca[1];
+      ca[0].id = cudaLaunchAttributeClusterDimension;
+      ca[0].val.clusterDim.x = (unsigned)w->ksplit;
+      ca[0].val.clusterDim.y = 1;
+      ca[0].val.clusterDim.z = 1;
+      occ.attrs = ca;
+      occ.numAttrs = 1;
+      int max_clusters = 0;
+      if (cudaOccupancyMaxActiveClusters(&max_clusters, qgemv_kernel<QT, NT>, &occ) == cudaSuccess &&
+          max_clusters >= 1) {
+        if (groups > max_clusters) {  // keep one wave
+          tiles = (w->rt + max_clusters - 1) / max_clusters;
+          groups = (w->rt + tiles - 1) / tiles;
+        }
+        const int64_t need2 = base + tiles * kVals * 4;
+        if (need2 <= kMaxSmem && (w->ksplit - 1) * tiles * kVals * 4 <= base) {
+          a.cluster = 1;
+          smem = need2;
+        }
+      } else {
+        cudaGetLastError();
+      }
+    }
+  }
   a.tiles_per_cta = (int)tiles;
-  const int64_t groups = (w->rt + tiles - 1) / tiles;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(groups * w->ksplit));
   cfg.blockDim = dim3(kGemvThreads);
-  cfg.dynamicSmemBytes = smem;
+  cfg.dynamicSmemBytes = (size_t)smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = a.cluster ? (unsigned)w->ksplit : 1u;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = a.cluster ? 2 : 1;
   return cudaLaunchKernelEx(&cfg, qgemv_kernel<QT, NT>, a);
 }
 

@@ -565,7 +565,8 @@ extern "C" int j4b_quant_matvec(j4b_qweight_t w, j4b_buf x, j4b_buf add, j4b_buf
   if (!w) return set_error(J4B_EINVAL, "null quantized weight");
   J4B_REQUIRE(batch >= 1, "quantMatvec batch must be positive, got %lld", (long long)batch);
   J4B_REQUIRE(x && y, "quantMatvec needs x and y buffers");
-  J4B_REQUIRE(((x | y | add) & 7) == 0, "quantMatvec buffers must be 8-byte aligned");
+  J4B_REQUIRE((x & 15) == 0 && ((y | add) & 3) == 0,
+              "quantMatvec needs x 16-byte aligned and y/add 4-byte aligned");
   DeviceGuard guard(w->dev);
   cudaStream_t stream = resolve_stream(w->dev, s);
   const int sms = device_ctx(w->dev)->sm_count;
