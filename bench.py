@@ -39,6 +39,11 @@ CONFIGS = {
     "q4_k_b1": (12, 14336, 4096, 1, "BASELINE configs[2]: Q4_K decode GEMV B=1, W[14336x4096]"),
     "q4_k_b16": (12, 14336, 4096, 16, "BASELINE configs[2]: Q4_K decode GEMV B=16, W[14336x4096]"),
 }
+TAPE_CONFIGS = {
+    # name: (rows per rank, cols, label)
+    "rms_swiglu": (4096, 8192, "BASELINE configs[3]: vmap-batched JIT-fused RMSNorm+SwiGLU tape with "
+                   "its grad, x[4096,8192], g[8192]"),
+}
 TYPE_NAME = {8: "Q8_0", 12: "Q4_K", 2: "Q4_0", 42: "Q2_0"}
 BLOCK = {8: (32, 34), 12: (256, 144), 2: (32, 18), 42: (128, 34)}
 METRIC = "Q4_K/Q8_0 dequant-GEMV GB/s vs HBM peak; fused-JIT tape steps/s at 1/2/4/8 B200"
@@ -59,8 +64,9 @@ def measured_peaks():
 
 
 def profiled_traffic(cfg):
-    """Per-launch DRAM bytes of the GEMV kernel from the committed ncu summary, if any."""
-    path = os.path.join(HERE, "profiles", f"qgemv_{cfg}.md")
+    """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary, if any."""
+    name = f"tape_{cfg}.md" if cfg in TAPE_CONFIGS else f"qgemv_{cfg}.md"
+    path = os.path.join(HERE, "profiles", name)
     if not os.path.exists(path):
         return None
     m = re.search(r"traffic_bytes_per_launch:\s*([0-9]+)", open(path).read())
@@ -171,7 +177,91 @@ def cpu_matvec_rate(qtype, rows, cols, batch, threads, budget_s, blob=None, x=No
     return nbytes / dt / 1e9, sample, dt
 
 
+def tape_alg_bytes(rows, cols):
+    """Read x and g, write dx, dg and the loss (f32)."""
+    return 4 * (2 * rows * cols + 2 * cols + 1)
+
+
+def rms_inputs_host(rows, cols, seed=0):
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((rows, cols)).astype(np.float32)
+    g = (1 + 0.1 * rng.standard_normal(cols)).astype(np.float32)
+    return x, g
+
+
+def cpu_tape_rate(rows, cols, threads, budget_s, x=None, g=None):
+    """Times the oracle's call-by-call replay of the tape (the reference CPU backend's
+    primitives, single-threaded each) on a bounded row sample, split over `threads` host
+    threads (row chunks; their column sums and losses combine). Returns (steps/s of the full
+    workload, sample text, seconds)."""
+    sys.path.insert(0, HERE)
+    from jax4j_b200 import jit as J, nn
+    from oracle.backend import run_tape
+    if x is None:
+        x, g = rms_inputs_host(rows, cols)
+    # calibrate on 8 rows
+    t8 = J.trace(nn.rms_swiglu_value_and_grad, [(8, cols), (cols,)])
+    t0 = time.perf_counter()
+    run_tape(t8, [x[:8], g])
+    per_row = (time.perf_counter() - t0) / 8
+    sample_rows = max(threads, min(rows, int(budget_s * threads / max(per_row, 1e-9))))
+    chunk = -(-sample_rows // threads)
+    sample_rows = chunk * threads
+    tape = J.trace(nn.rms_swiglu_value_and_grad, [(chunk, cols), (cols,)])
+
+    def work(i):
+        r0 = (i * chunk) % max(rows - chunk + 1, 1)
+        return run_tape(tape, [x[r0:r0 + chunk], g])
+
+    t0 = time.perf_counter()
+    if threads == 1:
+        work(0)
+    else:
+        with concurrent.futures.ThreadPoolExecutor(threads) as ex:
+            list(ex.map(work, range(threads)))
+    dt = time.perf_counter() - t0
+    steps_per_s = sample_rows / rows / dt
+    sample = (f"{sample_rows} of {rows} rows x {cols} cols ({threads} chunk(s) of {chunk} rows), "
+              f"oracle replay of the same tape (CpuBackend primitives), {threads} thread(s)")
+    return steps_per_s, sample, dt
+
+
+def run_reference_tape(args):
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return 0
+    rows, cols, label = TAPE_CONFIGS[args.config]
+    threads = os.cpu_count() or 1
+    total = args.steps + args.warmup
+    budget = max(0.2, min(5.0, 90.0 / max(total, 1)))
+    x, g = rms_inputs_host(rows, cols)
+    for _ in range(args.warmup):
+        cpu_tape_rate(rows, cols, threads, budget, x, g)
+    rates, times, sample = [], [], ""
+    for _ in range(args.steps):
+        r, sample, dt = cpu_tape_rate(rows, cols, threads, budget, x, g)
+        rates.append(r)
+        times.append(1.0 / r)
+    value = statistics.median(rates)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 5), "unit": "steps/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1e3 * statistics.median(times), 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": label, "rows": rows, "cols": cols},
+        "cpu_baseline": {"value": round(value, 5), "unit": "steps/s", "cores": threads,
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 5), "unit": "steps/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def run_reference(args):
+    if args.config in TAPE_CONFIGS:
+        return run_reference_tape(args)
     world, rank, _ = dist_env()
     if rank != 0:
         return 0
@@ -214,7 +304,179 @@ def run_reference(args):
 # engine arm
 # ------------------------------------------------------------------------------------------------
 
+def run_engine_tape(args):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    sys.path.insert(0, HERE)
+    from jax4j_b200 import jit as J, nn
+    from jax4j_b200 import _lib
+    from jax4j_b200.backend import B200Backend, TapeHandle, torch_stream
+    from jax4j_b200.prng import PrngKey
+
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    be = B200Backend(local)
+    rows, cols, label = TAPE_CONFIGS[args.config]
+    per_step = tape_alg_bytes(rows, cols)
+    dev = torch.device("cuda", local)
+
+    # ---- synthetic inputs on the device: x ~ N(0,1) [rows, cols] per rank, g = 1 + 0.1 N(0,1)
+    kx, kg = PrngKey.of(0).split(2)
+    x = be.random_normal(kx.seed, kx.counter + rank * rows * cols, (rows, cols))
+    g = be.scalar("ADD", be.scalar("MUL", be.random_normal(kg.seed, kg.counter, (cols,)), 0.1), 1.0)
+
+    # the tape: value and gradient of the mean of y^2 over the global batch (each rank's mean
+    # scaled by 1/world, so the all-reduced sums are the global loss and dg)
+    if world == 1:
+        fn = nn.rms_swiglu_value_and_grad
+    else:
+        inv = 1.0 / world
+
+        def fn(xt, gt):
+            from jax4j_b200 import transforms as T
+            loss, (dx, dg) = T.value_and_grad_tree(
+                lambda ps: nn.rms_swiglu_loss(ps[0], ps[1]).mul(inv), [xt, gt])
+            return [loss, dx, dg]
+    tape = J.trace(fn, [(rows, cols), (cols,)])
+    handle = TapeHandle(be, tape)
+    loss = torch.empty(1, dtype=torch.float32, device=dev)
+    dx = torch.empty(rows * cols, dtype=torch.float32, device=dev)
+    dg = torch.empty(cols, dtype=torch.float32, device=dev)
+    launches = handle.stats()["launches"]
+
+    def step(stream=None):
+        handle.launch([x.ptr, g.ptr], [loss.data_ptr(), dx.data_ptr(), dg.data_ptr()],
+                      torch_stream() if stream is None else stream)
+        if world > 1:
+            dist.all_reduce(dg)
+            dist.all_reduce(loss)
+
+    def capture(n):
+        gr = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            step()
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        with torch.cuda.graph(gr):
+            for _ in range(n):
+                step()
+        return gr
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(ms):
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    K, W = args.steps, max(3, args.warmup)
+    warm = capture(W)
+    main = capture(K)
+    warm.replay()
+    torch.cuda.synchronize()
+    soak_t0 = time.perf_counter()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        while time.perf_counter() - soak_t0 < 0.5:
+            warm.replay()
+            torch.cuda.synchronize()
+        barrier()
+        start.record()
+        main.replay()
+        end.record()
+        barrier()
+        tail = time.perf_counter()
+        while time.perf_counter() - tail < 0.3:
+            warm.replay()
+            torch.cuda.synchronize()
+    clk = clocks.summary()
+    ms = max_over_ranks(start.elapsed_time(end))
+    step_us = ms * 1e3 / K
+    value = world * K / (ms * 1e-3)
+    achieved = per_step / (step_us * 1e-6) / 1e9
+    peak, peak_kind = measured_peaks()
+
+    # ---- end to end through the public API: pinned host x, g -> device, tape, loss -> host
+    x_host = torch.from_numpy(np.ascontiguousarray(be.download(x))).pin_memory()
+    g_host = torch.from_numpy(np.ascontiguousarray(be.download(g))).pin_memory()
+    loss_host = torch.empty(1, dtype=torch.float32).pin_memory()
+    xin = be.full(0.0, (rows, cols))
+    gin = be.full(0.0, (cols,))
+    e2e_steps = max(3, min(K, 50))
+    stream = torch_stream()
+    barrier()
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_start.record()
+    for _ in range(e2e_steps):
+        _lib.call("j4b_h2d", xin.ptr, ctypes.c_void_p(x_host.data_ptr()), x_host.numel() * 4, stream)
+        _lib.call("j4b_h2d", gin.ptr, ctypes.c_void_p(g_host.data_ptr()), g_host.numel() * 4, stream)
+        handle.launch([xin.ptr, gin.ptr], [loss.data_ptr(), dx.data_ptr(), dg.data_ptr()], stream)
+        if world > 1:
+            dist.all_reduce(dg)
+            dist.all_reduce(loss)
+        _lib.call("j4b_d2h", ctypes.c_void_p(loss_host.data_ptr()), loss.data_ptr(), 4, stream)
+    e_end.record()
+    barrier()
+    e_ms = max_over_ranks(e_start.elapsed_time(e_end))
+    e2e_value = world * e2e_steps / (e_ms * 1e-3)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rate, sample, _ = cpu_tape_rate(rows, cols, 1, 10.0)
+        cpu = {"value": round(rate, 5), "unit": "steps/s", "cores": 1, "kind": "port",
+               "sample": sample + f" (host has {os.cpu_count()} cores)"}
+
+    if rank == 0:
+        st = handle.stats()
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "steps/s", "n_gpus": world,
+            "steps": K, "warmup": W, "ms_per_step": round(ms / K, 6), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {
+                "workload": label, "rows_per_gpu": rows, "cols": cols,
+                "bytes_per_step_per_gpu": per_step,
+                "tape": {"calls": st["calls"], "kernels": st["groups"], "folds": st["folds"],
+                         "eager_steps": st["eager_steps"]},
+                "l2": f"inputs larger than L2 (x {rows * cols * 4 / 1e6:.0f} MB, dx written {rows * cols * 4 / 1e6:.0f} MB)",
+                "parallelism": "replica" if world == 1 else f"data-parallel x{world}: rows per rank, NCCL all-reduce of dg and loss",
+                "timing": "CUDA graph of K tape replays, CUDA events, max over ranks",
+            },
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "traffic": profiled_traffic(args.config),
+                         "peak_source": f"{peak_kind} MEASURED_PEAKS.json hbm_gbs" if peak_kind == "measured" else "fallback 6.65 TB/s",
+                         "kernel": "j4b_group0 + j4b_group0_fold (the whole step)",
+                         "kernel_avg_us": round(step_us, 3)},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e_value, 3), "unit": "steps/s",
+                    "h2d_bytes_per_step": (rows * cols + cols) * 4, "d2h_bytes_per_step": 4},
+            "gpu_launches": K * launches,
+            "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"],
+                       "reasons": clk["reasons"], "samples": clk["samples"]},
+        }
+        print(json.dumps(line), flush=True)
+    del main, warm
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def run_engine(args):
+    if args.config in TAPE_CONFIGS:
+        return run_engine_tape(args)
     import numpy as np
     import torch
     import torch.distributed as dist
@@ -385,7 +647,7 @@ def main():
     p.add_argument("--steps", type=int, default=20000)
     p.add_argument("--warmup", type=int, default=200)
     p.add_argument("--impl", choices=["engine", "reference"], default="engine")
-    p.add_argument("--config", choices=sorted(CONFIGS), default="q8_0_b8")
+    p.add_argument("--config", choices=sorted(CONFIGS) + sorted(TAPE_CONFIGS), default="q8_0_b8")
     p.add_argument("--no-cpu-baseline", action="store_true")
     args = p.parse_args()
     if args.impl == "reference":

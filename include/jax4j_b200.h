@@ -190,6 +190,51 @@ int j4b_quant_gather_row(j4b_qweight_t w, int64_t row, j4b_buf out, j4b_stream s
 int j4b_quantize(int ggml_type, j4b_buf w, int64_t rows, int64_t cols, j4b_buf out_blocks,
                  j4b_stream s);
 
+/* ---- JIT tapes: ExecutionPlan.capture / execute (core/tensor/ExecutionPlan.java:49-132) ----
+ *
+ * A tape is the SPI call list a compiled function records once per input signature
+ * (Jit.compile / compileTree, core/tensor/Jit.java:67-114), serialised as int64 words:
+ *   header   MAGIC 0x314550415442344A, n_buffers, n_inputs, n_outputs, n_calls
+ *   buffers  per buffer: rank, dims...
+ *   inputs   buffer ids;  outputs  buffer ids
+ *   calls    per call: opcode, out id, n_in, in ids..., n_attr, attrs...
+ * Opcodes: 1 full, 2 fused, 3 transpose, 4 matmul, 5 batchedMatmul, 6 sliceAxis0, 7 stackAxis0,
+ * 8 reduceSum, 9 reduceMax, 10 sumAxis, 11 maxAxis, 12 argMaxAxis, 13 maxAxisBackward,
+ * 14 reshape, 15 broadcastTo, 16 reindex, 17 scatterAdd, 18 reluBackward, 19 randomUniform,
+ * 20 randomNormal, 21 binary, 22 scalar, 23 unary. Attributes: full [value as f64 bits];
+ * fused [postfix program: 0 idx | 1 op | 2 op | 3 op lo32 hi32]; sliceAxis0 [index];
+ * sumAxis/maxAxis [axis, keep]; argMaxAxis/maxAxisBackward [axis]; reindex/scatterAdd
+ * [1, offset, rank, strides...] (affine over the gather side's index) or [0, n, map...];
+ * random [seed, counter]; binary/unary [op]; scalar [op, value as f64 bits].
+ *
+ * j4b_tape_compile validates the tape (J4B_EINVAL with the reference's messages), groups its
+ * calls into fused sm_100a kernels (NVRTC) and allocates the tape's arena on `dev`.
+ * j4b_tape_launch replays it: inputs and outputs are caller buffers (16-byte aligned, dense
+ * f32, shapes as recorded; outputs must not alias inputs). Launches of one tape are serialised
+ * by the tape (its arena is reused), as Jit.Compiled.apply is synchronized (Jit.java:80). */
+typedef struct j4b_tape j4b_tape;
+typedef struct j4b_tape_stats {
+  int calls;          /* recorded SPI calls */
+  int groups;         /* fused kernels */
+  int folds;          /* cross-row reduction folds */
+  int eager_steps;    /* calls run by the eager SPI kernels (matmul, transpose, ...) */
+  int fills;
+  int copies;
+  int launches;       /* kernel launches per replay */
+  int64_t arena_bytes;
+} j4b_tape_stats;
+int j4b_tape_compile(int dev, const int64_t* words, size_t nwords, j4b_tape** out);
+int j4b_tape_launch(j4b_tape* tape, const j4b_buf* inputs, int n_inputs, const j4b_buf* outputs,
+                    int n_outputs, j4b_stream s);
+int j4b_tape_free(j4b_tape* tape);
+int j4b_tape_info(j4b_tape* tape, j4b_tape_stats* stats);
+/* Plans a tape and compiles its kernels without a device (NVRTC only): stats and the generated
+ * CUDA source of every group. For tests and tooling on machines without a GPU. */
+int j4b_tape_dryrun(const int64_t* words, size_t nwords, j4b_tape_stats* stats, char* buf,
+                    size_t cap, size_t* len);
+/* The generated CUDA source of fused kernel `group` (diagnostics). */
+int j4b_tape_source(j4b_tape* tape, int group, char* buf, size_t cap, size_t* len);
+
 #ifdef __cplusplus
 }
 #endif

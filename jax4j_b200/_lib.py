@@ -31,6 +31,12 @@ class Diagnostics(ctypes.Structure):
                 ("d2h_bytes", ctypes.c_uint64), ("compilations", ctypes.c_uint64)]
 
 
+class TapeStats(ctypes.Structure):
+    _fields_ = [("calls", ctypes.c_int), ("groups", ctypes.c_int), ("folds", ctypes.c_int),
+                ("eager_steps", ctypes.c_int), ("fills", ctypes.c_int), ("copies", ctypes.c_int),
+                ("launches", ctypes.c_int), ("arena_bytes", ctypes.c_int64)]
+
+
 _u64 = ctypes.c_uint64
 _i64 = ctypes.c_int64
 _int = ctypes.c_int
@@ -81,6 +87,14 @@ SIGNATURES = {
     "j4b_quant_matvec": [_vp, _u64, _u64, _u64, _i64, _vp],
     "j4b_quant_gather_row": [_vp, _i64, _u64, _vp],
     "j4b_quantize": [_int, _u64, _i64, _i64, _u64, _vp],
+    "j4b_tape_compile": [_int, _i64p, ctypes.c_size_t, ctypes.POINTER(_vp)],
+    "j4b_tape_launch": [_vp, ctypes.POINTER(_u64), _int, ctypes.POINTER(_u64), _int, _vp],
+    "j4b_tape_free": [_vp],
+    "j4b_tape_info": [_vp, ctypes.POINTER(TapeStats)],
+    "j4b_tape_dryrun": [_i64p, ctypes.c_size_t, ctypes.POINTER(TapeStats), ctypes.c_char_p,
+                        ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t)],
+    "j4b_tape_source": [_vp, _int, ctypes.c_char_p, ctypes.c_size_t,
+                        ctypes.POINTER(ctypes.c_size_t)],
 }
 
 _lib = None
@@ -137,3 +151,19 @@ def diagnostics() -> dict:
 
 def exported_symbols() -> list[str]:
     return list(SIGNATURES)
+
+
+def tape_dryrun(words) -> tuple[dict, str]:
+    """Plans a serialised tape and compiles its kernels with NVRTC, without a device: returns the
+    plan statistics and the generated CUDA source (j4b_tape_dryrun)."""
+    import numpy as np
+    w = np.ascontiguousarray(words, dtype=np.int64)
+    st = TapeStats()
+    n = ctypes.c_size_t(0)
+    call("j4b_tape_dryrun", w.ctypes.data_as(_i64p), w.size, ctypes.byref(st), None, 0,
+         ctypes.byref(n))
+    buf = ctypes.create_string_buffer(n.value + 1)
+    call("j4b_tape_dryrun", w.ctypes.data_as(_i64p), w.size, ctypes.byref(st), buf, n.value + 1,
+         ctypes.byref(n))
+    stats = {name: int(getattr(st, name)) for name, _ in TapeStats._fields_}
+    return stats, buf.value.decode()

@@ -80,8 +80,53 @@ class QuantBuffer:
             self.handle = 0
 
 
+class TapeHandle:
+    """A compiled tape on one device."""
+
+    def __init__(self, backend: "B200Backend", tape):
+        words = np.ascontiguousarray(tape.serialize(), dtype=np.int64)
+        h = ctypes.c_void_p()
+        call("j4b_tape_compile", backend.device, words.ctypes.data_as(_lib._i64p), words.size,
+             ctypes.byref(h))
+        self.handle = h
+        self.backend = backend
+        self.in_shapes = [tuple(tape.shapes[i]) for i in tape.inputs]
+        self.out_shapes = [tuple(tape.shapes[o]) for o in tape.outputs]
+
+    def stats(self) -> dict:
+        st = _lib.TapeStats()
+        call("j4b_tape_info", self.handle, ctypes.byref(st))
+        return {name: int(getattr(st, name)) for name, _ in _lib.TapeStats._fields_}
+
+    def source(self, group: int) -> str:
+        n = ctypes.c_size_t(0)
+        call("j4b_tape_source", self.handle, group, None, 0, ctypes.byref(n))
+        buf = ctypes.create_string_buffer(n.value + 1)
+        call("j4b_tape_source", self.handle, group, buf, n.value + 1, ctypes.byref(n))
+        return buf.value.decode()
+
+    def launch(self, in_ptrs: list, out_ptrs: list, stream: int) -> None:
+        ins = (ctypes.c_uint64 * max(len(in_ptrs), 1))(*in_ptrs)
+        outs = (ctypes.c_uint64 * max(len(out_ptrs), 1))(*out_ptrs)
+        call("j4b_tape_launch", self.handle, ins, len(in_ptrs), outs, len(out_ptrs), stream)
+
+    def run(self, buffers: list) -> list:
+        for b, s in zip(buffers, self.in_shapes):
+            if tuple(b.shape) != s:
+                raise ValueError(f"tape input shape {b.shape} does not match the recorded {s}")
+        outs = [self.backend._new(s) for s in self.out_shapes]
+        self.launch([b.ptr for b in buffers], [o.ptr for o in outs], self.backend.stream)
+        return outs
+
+    def __del__(self):
+        if getattr(self, "handle", None) and _lib._lib is not None:
+            _lib.load().j4b_tape_free(self.handle)
+            self.handle = None
+
+
 class B200Backend:
     """The sm_100a engine behind name() == "cuda" (BackendRegistry selects it by name)."""
+    executes_tapes = True
 
     def __init__(self, device: int = 0):
         if not torch.cuda.is_available():
@@ -333,6 +378,16 @@ class B200Backend:
         return out
 
     # ---- lifecycle ----
+    # ---- compiled tapes (ExecutionPlan.execute, ExecutionPlan.java:77-132) ----
+    def execute_tape(self, tape, plan: dict, buffers: list) -> list:
+        """Replays a recorded tape (jax4j_b200.jit.Tape) on the engine: compiled once per plan
+        (j4b_tape_compile), launched per call (j4b_tape_launch) into fresh output buffers."""
+        handle = plan.get("engine")
+        if handle is None:
+            handle = TapeHandle(self, tape)
+            plan["engine"] = handle
+        return handle.run(buffers)
+
     def sync(self) -> None:
         torch.cuda.current_stream(self._torch_device).synchronize()
         call("j4b_sync", self.device)

@@ -75,7 +75,10 @@ def build(force: bool = False, verbose: bool = False, extra: list[str] | None = 
         objs = list(ex.map(lambda s: _compile(s, verbose, extra or []), srcs))
     if force or _stale(LIB, objs):
         libdirs = sum((["-L", d] for d in cuda_lib_dirs()), [])
-        cmd = [nvcc(), *ARCH, "-shared", "-o", LIB, *objs, *libdirs, "-lcudart", "-lcuda", "-lnvrtc"]
+        # libcuda is not linked: driver entry points are resolved at run time through the runtime,
+        # so the library also loads (for planning and ABI checks) where no driver is installed
+        rpath = ["-Xlinker", "-rpath=" + cuda_lib_dirs()[0]]
+        cmd = [nvcc(), *ARCH, "-shared", "-o", LIB, *objs, *libdirs, *rpath, "-lcudart", "-lnvrtc"]
         subprocess.run(cmd, check=True)
     return LIB
 
