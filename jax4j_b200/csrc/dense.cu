@@ -305,6 +305,20 @@ __global__ void scatter_add_kernel(const float* __restrict__ a, int64_t n_src, c
   }
 }
 
+// scatterAdd with a static map, as a gather: destination k sums its sources in increasing
+// source order (offsets[k] .. offsets[k+1] of `sources`), the float order of the reference's
+// sequential loop (ComputeBackend.java:261-274), so the result is bit-exact and deterministic.
+__global__ void segment_sum_kernel(const float* __restrict__ a, const int64_t* __restrict__ offsets,
+                                   const int64_t* __restrict__ sources, int64_t n_dst,
+                                   float* __restrict__ out) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; k < n_dst; k += stride) {
+    float acc = 0.0f;
+    for (int64_t p = offsets[k]; p < offsets[k + 1]; ++p) acc = __fadd_rn(acc, a[sources[p]]);
+    out[k] = acc;
+  }
+}
+
 // PRNG: ComputeBackend.java:282-295 (splitmix64), bit-exact uniforms.
 __device__ __forceinline__ uint64_t mix64(uint64_t v) {
   v = (v ^ (v >> 30)) * 0xBF58476D1CE4E5B9ULL;
@@ -575,6 +589,17 @@ extern "C" int j4b_scatter_add(j4b_buf a, int64_t n_src, j4b_buf map, int64_t n_
   J4B_CHECK_LAUNCH("scatter_add_kernel");
   return J4B_OK;
 }
+
+namespace j4b {
+int launch_segment_sum(const float* a, const int64_t* offsets, const int64_t* sources, int64_t n_dst,
+                       float* out, j4b_stream s) {
+  if (n_dst == 0) return J4B_OK;
+  J4B_DEVICE_OF(out);
+  segment_sum_kernel<<<grid_for(n_dst, dev), kThreads, 0, stream>>>(a, offsets, sources, n_dst, out);
+  J4B_CHECK_LAUNCH("segment_sum_kernel");
+  return J4B_OK;
+}
+}  // namespace j4b
 
 extern "C" int j4b_random_uniform(int64_t seed, int64_t counter, j4b_buf out, int64_t n,
                                   j4b_stream s) {

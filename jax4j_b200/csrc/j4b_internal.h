@@ -54,6 +54,10 @@ struct DeviceGuard {
   }
 };
 
+// out[k] = sum of a[sources[p]] for p in [offsets[k], offsets[k+1]), in that order
+int launch_segment_sum(const float* a, const int64_t* offsets, const int64_t* sources, int64_t n_dst,
+                       float* out, j4b_stream s);
+
 }  // namespace j4b
 
 #define J4B_CHECK_LAUNCH(what)                                 \

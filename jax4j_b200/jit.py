@@ -269,18 +269,18 @@ class RecordingBackend(Backend):
 # ---------------------------------------------------------------------------------------------
 
 class ExprBuffer(Buffer):
-    __slots__ = ("expr", "leaves", "shape")
+    __slots__ = ("expr", "leaves", "shape", "materialized")
 
     def __init__(self, expr, leaves, shape):
         self.expr = expr
         self.leaves = list(leaves)
         self.shape = tuple(shape)
+        self.materialized = None  # the delegate's buffer once this chain hit a boundary
 
 
 class FusingBackend(Backend):
     def __init__(self, delegate: Backend):
         self.d = delegate
-        self.materialized: dict[int, Buffer] = {}
 
     @staticmethod
     def traced(b) -> ExprBuffer:
@@ -292,14 +292,12 @@ class FusingBackend(Backend):
         """FusingBackend.materialize (FusingBackend.java:273-286)."""
         if not isinstance(b, ExprBuffer):
             return b
-        got = self.materialized.get(id(b))
-        if got is not None:
-            return got
+        if b.materialized is not None:
+            return b.materialized
         if isinstance(b.expr, E.Input) and len(b.leaves) == 1:
             return b.leaves[0]
-        r = self.d.fused(b.expr, b.leaves)
-        self.materialized[id(b)] = r
-        return r
+        b.materialized = self.d.fused(b.expr, b.leaves)
+        return b.materialized
 
     @staticmethod
     def merge(left: ExprBuffer, right: ExprBuffer):

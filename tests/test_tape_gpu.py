@@ -43,12 +43,19 @@ def engine_vs_oracle(backend, fn, inputs, rel=REL, check_reuse=True):
     outs = backend.execute_tape(tape, plan, bufs)
     want = run_tape(tape, inputs)
     got = [backend.download(o) for o in outs]
-    for g, w in zip(got, want):
-        close(g, w, rel)
+    for k, (g, w) in enumerate(zip(got, want)):
+        try:
+            close(g, w, rel)
+        except AssertionError as e:
+            bad = np.flatnonzero(~np.isclose(g.reshape(-1), w.reshape(-1), rtol=rel, atol=1e-6, equal_nan=True))
+            raise AssertionError(f"output {k} (shape {w.shape}): {e}; first bad flat indices "
+                                 f"{bad[:8].tolist()} got {g.reshape(-1)[bad[:4]].tolist()} "
+                                 f"want {w.reshape(-1)[bad[:4]].tolist()}") from None
     if check_reuse:
         again = [backend.download(o) for o in backend.execute_tape(tape, plan, bufs)]
-        for a, g in zip(again, got):
-            assert np.array_equal(a.reshape(-1), g.reshape(-1)), "replay is not deterministic"
+        for k, (a, g) in enumerate(zip(again, got)):
+            same = np.array_equal(a.reshape(-1), g.reshape(-1), equal_nan=True)
+            assert same, f"replay is not deterministic: output {k}"
     return plan["engine"], got
 
 
