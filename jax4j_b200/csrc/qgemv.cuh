@@ -77,6 +77,17 @@ __device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// Same with a zero accumulator input: starts a chain without zeroing registers first.
+__device__ __forceinline__ void mma16816_z(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                           uint32_t a3, uint32_t b0, uint32_t b1) {
+  const float z = 0.0f;
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%10,%10,%10,%10};\n"
+      : "=f"(c[0]), "=f"(c[1]), "=f"(c[2]), "=f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(z));
+}
+
 __device__ __forceinline__ uint32_t rotr(uint32_t v, int s) { return __funnelshift_r(v, v, s); }
 __device__ __forceinline__ uint32_t lop_or(uint32_t v, uint32_t mask, uint32_t bias) {
   return (v & mask) | bias;
@@ -307,6 +318,116 @@ __device__ __forceinline__ void tile_compute(const uint8_t* __restrict__ sq,
   }
 }
 
+// Batch <= 4: the B fragment carries x's fp16 hi part of batch b in n-column 2b and its lo part
+// in column 2b+1, so one mma covers both halves and lane (g, t) reads batch t of rows g and
+// g + 8 as c0 + c1 and c2 + c3. acc[0] is row g, acc[1] row g + 8.
+template <int QT>
+__device__ __forceinline__ void tile_compute_pk(const uint8_t* __restrict__ sq,
+                                                const uint8_t* __restrict__ sm, int warp, int lane,
+                                                const uint32_t (&bp)[8][2],
+                                                const float (&xblk)[kXBlocks<QT>],
+                                                float (&acc)[2]) {
+  const int g = lane >> 2, t = lane & 3;
+  if constexpr (QT == J4B_Q8_0) {
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      const uint4 line = *reinterpret_cast<const uint4*>(sq + (warp * 4 + q) * 512 + lane * 16);
+      const uint32_t sc = *reinterpret_cast<const uint32_t*>(sm + (warp * 4 + q) * 32 + g * 4);
+      float c[4];
+      uint32_t a0, a1, a2, a3;
+      q8_pairs(line.x, a0, a1);
+      q8_pairs(line.y, a2, a3);
+      mma16816_z(c, a0, a1, a2, a3, bp[2 * q][0], bp[2 * q][1]);
+      q8_pairs(line.z, a0, a1);
+      q8_pairs(line.w, a2, a3);
+      mma16816(c, a0, a1, a2, a3, bp[2 * q + 1][0], bp[2 * q + 1][1]);
+      const float2 d = __half22float2(*reinterpret_cast<const __half2*>(&sc));
+      acc[0] = fmaf(d.x, c[0] + c[1], acc[0]);
+      acc[1] = fmaf(d.y, c[2] + c[3], acc[1]);
+    }
+  } else if constexpr (QT == J4B_Q4_0) {
+    const uint4 l0 = *reinterpret_cast<const uint4*>(sq + warp * 1024 + lane * 16);
+    const uint4 l1 = *reinterpret_cast<const uint4*>(sq + warp * 1024 + 512 + lane * 16);
+    const uint32_t wv[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      const uint32_t sc = *reinterpret_cast<const uint32_t*>(sm + (warp * 4 + q) * 32 + g * 4);
+      float c[4];
+      uint32_t av[4];
+      q4_pairs(wv[2 * q], av);
+      mma16816_z(c, av[0], av[1], av[2], av[3], bp[2 * q][0], bp[2 * q][1]);
+      q4_pairs(wv[2 * q + 1], av);
+      mma16816(c, av[0], av[1], av[2], av[3], bp[2 * q + 1][0], bp[2 * q + 1][1]);
+      const float2 d = __half22float2(*reinterpret_cast<const __half2*>(&sc));
+      acc[0] += d.x * fmaf(16.f, c[0] + c[1], -24.f * xblk[q]);
+      acc[1] += d.y * fmaf(16.f, c[2] + c[3], -24.f * xblk[q]);
+    }
+  } else if constexpr (QT == J4B_Q2_0) {
+    const uint4 line = *reinterpret_cast<const uint4*>(sq + warp * 512 + lane * 16);
+    const uint32_t sc = *reinterpret_cast<const uint32_t*>(sm + warp * 32 + g * 4);
+    const uint32_t wv[4] = {line.x, line.y, line.z, line.w};
+    float c[4];
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+#pragma unroll
+      for (int ks = 0; ks < 2; ks++) {
+        const uint32_t a0 = q2_pair(wv[q], 4 * ks), a1 = q2_pair(wv[q], 4 * ks + 1);
+        const uint32_t a2 = q2_pair(wv[q], 4 * ks + 2), a3 = q2_pair(wv[q], 4 * ks + 3);
+        const int j = 2 * q + ks;
+        if (j == 0) mma16816_z(c, a0, a1, a2, a3, bp[j][0], bp[j][1]);
+        else mma16816(c, a0, a1, a2, a3, bp[j][0], bp[j][1]);
+      }
+    }
+    const float2 d = __half22float2(*reinterpret_cast<const __half2*>(&sc));
+    acc[0] += d.x * fmaf(4.f, c[0] + c[1], -5.f * xblk[0]);
+    acc[1] += d.y * fmaf(4.f, c[2] + c[3], -5.f * xblk[0]);
+  } else {  // Q4_K, as in tile_compute
+    const int h = warp & 1;
+    const uint4 l0 = *reinterpret_cast<const uint4*>(sq + warp * 1024 + lane * 32);
+    const uint4 l1 = *reinterpret_cast<const uint4*>(sq + warp * 1024 + lane * 32 + 16);
+    const uint8_t* mp = sm + (warp >> 1) * 256 + g * 32;
+    const uint4 mm[2] = {*reinterpret_cast<const uint4*>(mp), *reinterpret_cast<const uint4*>(mp + 16)};
+    float cs[2], cx[2];
+#pragma unroll
+    for (int r = 0; r < 2; r++) {
+      const uint32_t w0 = mm[r].x, w1 = mm[r].y, w2 = mm[r].z, w3 = mm[r].w;
+      const float d = __half2float(__ushort_as_half((uint16_t)(w0 & 0xFFFF)));
+      const float dmin = __half2float(__ushort_as_half((uint16_t)(w0 >> 16)));
+      const int j = 4 * h + t;
+      int sc, mn;
+      if (j < 4) {
+        sc = (w1 >> (8 * j)) & 63;
+        mn = (w2 >> (8 * j)) & 63;
+      } else {
+        const int jj = j - 4;
+        const uint32_t qj4 = (w3 >> (8 * jj)) & 0xFF;
+        sc = (qj4 & 0xF) | (((w1 >> (8 * jj + 6)) & 3) << 4);
+        mn = (qj4 >> 4) | (((w2 >> (8 * jj + 6)) & 3) << 4);
+      }
+      const float ds = d * (float)sc;
+      cs[r] = 16.f * ds;
+      cx[r] = -fmaf(16.f, ds, dmin * (float)mn);
+    }
+    const uint32_t wv[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      float c[4];
+      uint32_t av[4];
+      q4_pairs(wv[2 * q], av);
+      mma16816_z(c, av[0], av[1], av[2], av[3], bp[2 * q][0], bp[2 * q][1]);
+      q4_pairs(wv[2 * q + 1], av);
+      mma16816(c, av[0], av[1], av[2], av[3], bp[2 * q + 1][0], bp[2 * q + 1][1]);
+      const int src = (lane & ~3) | q;
+      const float s0 = __shfl_sync(0xffffffffu, cs[0], src);
+      const float s1 = __shfl_sync(0xffffffffu, cs[1], src);
+      const float z0 = __shfl_sync(0xffffffffu, cx[0], src);
+      const float z1 = __shfl_sync(0xffffffffu, cx[1], src);
+      acc[0] += fmaf(s0, c[0] + c[1], z0 * xblk[q]);
+      acc[1] += fmaf(s1, c[2] + c[3], z1 * xblk[q]);
+    }
+  }
+}
+
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
@@ -330,12 +451,18 @@ __device__ __forceinline__ void out_coord(int v, int& row, int& bcol) {
   bcol = 8 * n + 2 * (ln & 3) + (c & 1);
 }
 
-template <int QT, int NT>
+// Output element v (0 .. 64) of a tile in the packed (batch <= 4) layout.
+__device__ __forceinline__ void out_coord_pk(int v, int& row, int& bcol) {
+  row = ((v & 31) >> 2) + 8 * (v >> 5);
+  bcol = v & 3;
+}
+
+template <int QT, int NT, bool PK>
 __global__ void __launch_bounds__(kGemvThreads, 1) qgemv_kernel(GemvArgs a) {
   using T = GemvTraits<QT>;
   constexpr int kStages = T::kStages, kM = kTilesPerCopy<QT, NT>;
   constexpr int kStageBytes = kM * T::kChunk;
-  constexpr int kVals = NT * 128;  // outputs of one tile
+  constexpr int kVals = PK ? 64 : NT * 128;  // outputs of one tile
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* stage_base = smem;
   float* red = reinterpret_cast<float*>(smem + kStages * kStageBytes);  // [kM][8 chunks][kVals]
@@ -406,11 +533,14 @@ __global__ void __launch_bounds__(kGemvThreads, 1) qgemv_kernel(GemvArgs a) {
   }
   __syncthreads();
   // ---- x fragments of this warp's 128-column chunk: hi/lo fp16, per n-tile and k-step ----
-  uint32_t bh[NT][8][2], bl[NT][8][2];
-  float xs[NT][8];
+  // (packed: lane group g holds batch g / 2, its hi part for even g and lo part for odd g)
+  constexpr int NTF = PK ? 1 : NT;
+  uint32_t bh[NTF][8][2], bl[PK ? 1 : NT][8][2];
+  float xs[NTF][8];
 #pragma unroll
-  for (int n = 0; n < NT; n++) {
-    const float* xr = xstage + (8 * n + g) * kXStride + chunk * 128 + 2 * t;
+  for (int n = 0; n < NTF; n++) {
+    const int xrow = PK ? (g >> 1) : 8 * n + g;
+    const float* xr = xstage + xrow * kXStride + chunk * 128 + 2 * t;
 #pragma unroll
     for (int j = 0; j < 8; j++) {
       const float2 p0 = *reinterpret_cast<const float2*>(xr + 16 * j);
@@ -421,20 +551,29 @@ __global__ void __launch_bounds__(kGemvThreads, 1) qgemv_kernel(GemvArgs a) {
       const float2 f0 = __half22float2(h0), f1 = __half22float2(h1);
       __half2 l0 = __floats2half2_rn(v[0] - f0.x, v[1] - f0.y);
       __half2 l1 = __floats2half2_rn(v[2] - f1.x, v[3] - f1.y);
-      bh[n][j][0] = *reinterpret_cast<uint32_t*>(&h0);
-      bh[n][j][1] = *reinterpret_cast<uint32_t*>(&h1);
-      bl[n][j][0] = *reinterpret_cast<uint32_t*>(&l0);
-      bl[n][j][1] = *reinterpret_cast<uint32_t*>(&l1);
       const float2 g0 = __half22float2(l0), g1 = __half22float2(l1);
-      xs[n][j] = (f0.x + g0.x) + (f0.y + g0.y) + (f1.x + g1.x) + (f1.y + g1.y);
+      if constexpr (PK) {
+        const bool lo = g & 1;
+        bh[n][j][0] = lo ? *reinterpret_cast<uint32_t*>(&l0) : *reinterpret_cast<uint32_t*>(&h0);
+        bh[n][j][1] = lo ? *reinterpret_cast<uint32_t*>(&l1) : *reinterpret_cast<uint32_t*>(&h1);
+        xs[n][j] = lo ? (g0.x + g0.y) + (g1.x + g1.y) : (f0.x + f0.y) + (f1.x + f1.y);
+      } else {
+        bh[n][j][0] = *reinterpret_cast<uint32_t*>(&h0);
+        bh[n][j][1] = *reinterpret_cast<uint32_t*>(&h1);
+        bl[n][j][0] = *reinterpret_cast<uint32_t*>(&l0);
+        bl[n][j][1] = *reinterpret_cast<uint32_t*>(&l1);
+        xs[n][j] = (f0.x + g0.x) + (f0.y + g0.y) + (f1.x + g1.x) + (f1.y + g1.y);
+      }
     }
   }
-  // Block sums of x for the output columns this lane holds (batch 2t, 2t+1 of each n-tile).
+  // Block sums of x for the output columns this lane holds (batch 2t, 2t+1 of each n-tile;
+  // packed: batch t, the sum of its hi and lo column sums).
   constexpr int kXB = kXBlocks<QT>;
   float xblk[NT][kXB][2] = {};
+  float xblkp[kXB] = {};
   if constexpr (QT != J4B_Q8_0) {
 #pragma unroll
-    for (int n = 0; n < NT; n++) {
+    for (int n = 0; n < NTF; n++) {
 #pragma unroll
       for (int q = 0; q < kXB; q++) {
         float s = 0.f;
@@ -443,8 +582,14 @@ __global__ void __launch_bounds__(kGemvThreads, 1) qgemv_kernel(GemvArgs a) {
         for (int j = 0; j < kSteps; j++) s += xs[n][q * kSteps + j];
         s += __shfl_xor_sync(0xffffffffu, s, 1);
         s += __shfl_xor_sync(0xffffffffu, s, 2);
-        xblk[n][q][0] = __shfl_sync(0xffffffffu, s, 4 * (2 * t));
-        xblk[n][q][1] = __shfl_sync(0xffffffffu, s, 4 * (2 * t + 1));
+        const float s0 = __shfl_sync(0xffffffffu, s, 4 * (2 * t));
+        const float s1 = __shfl_sync(0xffffffffu, s, 4 * (2 * t + 1));
+        if constexpr (PK) {
+          xblkp[q] = s0 + s1;
+        } else {
+          xblk[n][q][0] = s0;
+          xblk[n][q][1] = s1;
+        }
       }
     }
   }
@@ -456,23 +601,39 @@ __global__ void __launch_bounds__(kGemvThreads, 1) qgemv_kernel(GemvArgs a) {
     const int count = min(kM, ntiles - c * kM);
     if (!mbar_wait_bounded(&full[s], (uint32_t)((c / kStages) & 1))) failed = true;
     constexpr int kMine = kM / 2;  // tiles of the stage this warp computes: sub, sub + 2, ...
-    float acc[kMine][NT][4] = {};
-    if (active && !failed) {
-      const uint8_t* st = stage_base + s * kStageBytes;
-      // tiles past `count` read stale stage bytes and are discarded
+    if constexpr (PK) {
+      float acc[kMine][2] = {};
+      if (active && !failed) {
+        const uint8_t* st = stage_base + s * kStageBytes;
 #pragma unroll
-      for (int jj = 0; jj < kMine; jj++) {
-        const int j = sub + 2 * jj;
-        tile_compute<QT, NT>(st + j * chunk_bytes, st + j * chunk_bytes + meta_off, chunk, lane, bh, bl, xblk, acc[jj]);
+        for (int jj = 0; jj < kMine; jj++) {
+          const int j = sub + 2 * jj;
+          tile_compute_pk<QT>(st + j * chunk_bytes, st + j * chunk_bytes + meta_off, chunk, lane, bh[0], xblkp, acc[jj]);
+        }
       }
+#pragma unroll
+      for (int jj = 0; jj < kMine; jj++)
+#pragma unroll
+        for (int cc = 0; cc < 2; cc++) red[((sub + 2 * jj) * 8 + chunk) * kVals + cc * 32 + lane] = acc[jj][cc];
+    } else {
+      float acc[kMine][NT][4] = {};
+      if (active && !failed) {
+        const uint8_t* st = stage_base + s * kStageBytes;
+        // tiles past `count` read stale stage bytes and are discarded
+#pragma unroll
+        for (int jj = 0; jj < kMine; jj++) {
+          const int j = sub + 2 * jj;
+          tile_compute<QT, NT>(st + j * chunk_bytes, st + j * chunk_bytes + meta_off, chunk, lane, bh, bl, xblk, acc[jj]);
+        }
+      }
+#pragma unroll
+      for (int jj = 0; jj < kMine; jj++)
+#pragma unroll
+        for (int n = 0; n < NT; n++)
+#pragma unroll
+          for (int cc = 0; cc < 4; cc++)
+            red[((sub + 2 * jj) * 8 + chunk) * kVals + (n * 4 + cc) * 32 + lane] = acc[jj][n][cc];
     }
-#pragma unroll
-    for (int jj = 0; jj < kMine; jj++)
-#pragma unroll
-      for (int n = 0; n < NT; n++)
-#pragma unroll
-        for (int cc = 0; cc < 4; cc++)
-          red[((sub + 2 * jj) * 8 + chunk) * kVals + (n * 4 + cc) * 32 + lane] = acc[jj][n][cc];
     if (__syncthreads_or(failed)) {
       failed = true;
       break;
@@ -491,7 +652,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) qgemv_kernel(GemvArgs a) {
       const int64_t tile = tile0 + c * kM + j;
       if (a.ksplit == 1) {
         int row, bcol;
-        out_coord(v, row, bcol);
+        if (PK) out_coord_pk(v, row, bcol); else out_coord(v, row, bcol);
         const int64_t r = tile * 16 + row;
         if (r < a.rows && bcol < a.batch) {
           if (a.add) total += a.add[(int64_t)bcol * a.rows + r];
@@ -534,7 +695,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) qgemv_kernel(GemvArgs a) {
         float total = mine[i];
         for (int sp = 1; sp < a.ksplit; sp++) total += landing[(sp - 1) * nv + i];
         int row, bcol;
-        out_coord(i % kVals, row, bcol);
+        if (PK) out_coord_pk(i % kVals, row, bcol); else out_coord(i % kVals, row, bcol);
         const int64_t r = (tile0 + i / kVals) * 16 + row;
         if (r < a.rows && bcol < a.batch) {
           if (a.add) total += a.add[(int64_t)bcol * a.rows + r];
@@ -571,7 +732,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) qgemv_kernel(GemvArgs a) {
         if (idx >= nv) break;
         const int64_t tile = tile0 + idx / kVals;
         int row, bcol;
-        out_coord(idx % kVals, row, bcol);
+        if (PK) out_coord_pk(idx % kVals, row, bcol); else out_coord(idx % kVals, row, bcol);
         const int64_t r = tile * 16 + row;
         if (r < a.rows && bcol < a.batch) {
           float v = tot[u];
@@ -584,24 +745,24 @@ __global__ void __launch_bounds__(kGemvThreads, 1) qgemv_kernel(GemvArgs a) {
   }
 }
 
-template <int QT, int NT>
+template <int QT, int NT, bool PK>
 cudaError_t launch_gemv(const j4b_qweight* w, const float* x, const float* add, float* y,
                         int batch, int sms, cudaStream_t stream) {
   // Largest dynamic shared memory a CTA may request: the device's opt-in limit minus the
   // kernel's static shared memory (set once per instantiation).
   static int64_t kMaxSmem = -1;
   constexpr int base = gemv_smem_base<QT, NT>();
-  constexpr int kVals = NT * 128;
+  constexpr int kVals = PK ? 64 : NT * 128;
   if (kMaxSmem < 0) {
     int dev = 0, optin = 0;
     cudaGetDevice(&dev);
     cudaError_t e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     cudaFuncAttributes fa;
-    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, qgemv_kernel<QT, NT>);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, qgemv_kernel<QT, NT, PK>);
     if (e != cudaSuccess) return e;
     const int64_t lim = (int64_t)optin - (int64_t)fa.sharedSizeBytes;
     if (lim < base) return cudaErrorInvalidConfiguration;
-    e = cudaFuncSetAttribute(qgemv_kernel<QT, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)lim);
+    e = cudaFuncSetAttribute(qgemv_kernel<QT, NT, PK>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)lim);
     if (e != cudaSuccess) return e;
     kMaxSmem = lim;
   }
@@ -645,7 +806,7 @@ cudaError_t launch_gemv(const j4b_qweight* w, const float* x, const float* add, 
       occ.attrs = ca;
       occ.numAttrs = 1;
       int max_clusters = 0;
-      if (cudaOccupancyMaxActiveClusters(&max_clusters, qgemv_kernel<QT, NT>, &occ) == cudaSuccess &&
+      if (cudaOccupancyMaxActiveClusters(&max_clusters, qgemv_kernel<QT, NT, PK>, &occ) == cudaSuccess &&
           max_clusters >= 1) {
         if (groups > max_clusters) {  // keep one wave
           tiles = (w->rt + max_clusters - 1) / max_clusters;
@@ -676,12 +837,13 @@ cudaError_t launch_gemv(const j4b_qweight* w, const float* x, const float* add, 
   attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = a.cluster ? 2 : 1;
-  return cudaLaunchKernelEx(&cfg, qgemv_kernel<QT, NT>, a);
+  return cudaLaunchKernelEx(&cfg, qgemv_kernel<QT, NT, PK>, a);
 }
 
 template <int QT>
 cudaError_t gemv_dispatch(const j4b_qweight* w, const float* x, const float* add, float* y,
                           int batch, int sms, cudaStream_t stream) {
-  if (batch <= 8) return launch_gemv<QT, 1>(w, x, add, y, batch, sms, stream);
-  return launch_gemv<QT, 2>(w, x, add, y, batch, sms, stream);
+  if (batch <= 4) return launch_gemv<QT, 1, true>(w, x, add, y, batch, sms, stream);
+  if (batch <= 8) return launch_gemv<QT, 1, false>(w, x, add, y, batch, sms, stream);
+  return launch_gemv<QT, 2, false>(w, x, add, y, batch, sms, stream);
 }
