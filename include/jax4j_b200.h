@@ -159,7 +159,10 @@ int j4b_relu_backward(j4b_buf upstream, j4b_buf input, j4b_buf out, int64_t n, j
 int j4b_random_uniform(int64_t seed, int64_t counter, j4b_buf out, int64_t n, j4b_stream s);
 int j4b_random_normal(int64_t seed, int64_t counter, j4b_buf out, int64_t n, j4b_stream s);
 /* matmul / batchedMatmul: ComputeBackend.java:97-101. out[b] = a[b] (m x k) . b[b] (k x n),
- * row-major f32. precision 0 = fp32-accurate (rel 1e-4), 1 = bf16 tensor-core operands. */
+ * row-major f32. precision 0 = fp32-accurate (rel 1e-4): SIMT for small shapes, the tcgen05
+ * tensor cores with a 3-term bf16 split (hi.hi + hi.lo + lo.hi) when m n k >= 2^24;
+ * 1 = bf16 operands on the tensor cores (rel 1e-2); 2 = the 3-term split on the tensor cores
+ * at any size. */
 int j4b_matmul(j4b_buf a, j4b_buf b, j4b_buf out, int64_t batch, int64_t m, int64_t k,
                int64_t n, int precision, j4b_stream s);
 

@@ -622,8 +622,14 @@ extern "C" int j4b_random_normal(int64_t seed, int64_t counter, j4b_buf out, int
 extern "C" int j4b_matmul(j4b_buf a, j4b_buf b, j4b_buf out, int64_t batch, int64_t m, int64_t k,
                           int64_t n, int precision, j4b_stream s) {
   J4B_REQUIRE(batch >= 1 && m >= 1 && k >= 1 && n >= 1, "matmul dimensions must be positive");
-  J4B_REQUIRE(precision == 0 || precision == 1, "matmul precision must be 0 or 1");
+  J4B_REQUIRE(precision >= 0 && precision <= 2, "matmul precision must be 0, 1 or 2");
   J4B_DEVICE_OF(out);
+  // tensor cores (tcgen05): bf16 operands (1), or the 3-term bf16 split for fp32 accuracy (2, and
+  // 0 when the contraction is large enough to amortise the operand conversion)
+  const bool big = m * n * k >= (int64_t(1) << 24) && m >= 64 && n >= 64;
+  if (precision == 1 || precision == 2 || big)
+    return tc_matmul((const float*)(uintptr_t)a, (const float*)(uintptr_t)b, (float*)(uintptr_t)out, batch, m,
+                     k, n, precision == 1 ? 1 : 3, dev, stream);
   dim3 grid((unsigned)((n + 63) / 64), (unsigned)((m + 63) / 64), (unsigned)batch);
   sgemm_kernel<<<grid, 256, 0, stream>>>((const float*)(uintptr_t)a, (const float*)(uintptr_t)b,
                                          (float*)(uintptr_t)out, m, k, n);

@@ -1,0 +1,381 @@
+// Dense f32 matmul on the 5th-generation tensor cores (tcgen05 + TMEM + TMA), the engine's
+// ComputeBackend.matmul / batchedMatmul for shapes large enough to be real contractions
+// (core/tensor/spi/ComputeBackend.java:97-101; the reference's CUDA backend runs 16x16 SIMT
+// tiles, cuda/backend/cuda/CudaBackend.java:102-173, 572-623).
+//
+// C[M,N] = A[M,K] B[K,N], f32 row-major in and out. The operands are first rewritten as bf16,
+// K-major (A as is, B transposed), K padded to the 64-element tile with zeros; for the
+// fp32-accurate mode each operand is split into hi = bf16(x) and lo = bf16(x - hi) and the
+// product is hi.hi + hi.lo + lo.hi (about 16 mantissa bits, relative error ~1e-5), for the bf16
+// mode only hi.hi.
+//
+// One CTA computes one 128 x 128 tile of C with six warps:
+//   warp 0  one thread streams 64-wide K slices of the A and B tiles into a ring of
+//           shared-memory stages with 2-D TMA tile loads (128-byte swizzle), completion counted
+//           on the stage's `full` mbarrier;
+//   warp 1  allocates 128 TMEM columns (the fp32 accumulator, one lane per tile row) and one
+//           thread issues tcgen05.mma (M=128, N=128, K=16 per instruction) from shared-memory
+//           descriptors; tcgen05.commit releases each stage (`empty`) and finally signals the
+//           epilogue (`acc_full`);
+//   warps 2-5  read the accumulator with tcgen05.ld (32 lanes x 8 columns per load; warp w
+//           may access TMEM lanes 32 (w % 4) .. + 31) and store C.
+// Every mbarrier wait is bounded; a wait that gives up records an error in the status word.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_bf16.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "j4b_internal.h"
+
+namespace j4b {
+namespace {
+
+constexpr int kBM = 128, kBN = 128, kBK = 64;
+constexpr int kTcThreads = 192;
+constexpr uint32_t kTcWaitLimit = 1u << 26;
+constexpr int kTileBytes = kBM * kBK * 2;  // one 128 x 64 bf16 tile (A or B)
+
+__device__ __forceinline__ uint32_t saddr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void bar_init(uint64_t* b, uint32_t n) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(saddr(b)), "r"(n));
+}
+__device__ __forceinline__ void bar_expect_tx(uint64_t* b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(saddr(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool bar_try_wait(uint64_t* b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(saddr(b)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool bar_wait(uint64_t* b, uint32_t parity) {
+  for (uint32_t i = 0; i < kTcWaitLimit; ++i)
+    if (bar_try_wait(b, parity)) return true;
+  return false;
+}
+
+// 2-D TMA tile load into this CTA's shared memory (one destination CTA); x is the K coordinate
+// (a multiple of 64 elements = 128 bytes), y the row.
+__device__ __forceinline__ void tma_tile(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          saddr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(saddr(bar))
+      : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, rows of 128 bytes, 8-row
+// groups 1024 bytes apart (start >> 4 at [0,14), LBO at [16,30), SBO at [32,46), version 1 at
+// [46,48), layout SWIZZLE_128B = 2 at [61,64)).
+__device__ __forceinline__ uint64_t kmajor_sw128(uint32_t smem_byte_addr) {
+  return (uint64_t)((smem_byte_addr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// Instruction descriptor, kind::f16: fp32 accumulator, bf16 A and B, both K-major, M x N.
+constexpr uint32_t idesc_bf16(int m, int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc,
+                                          uint32_t accumulate) {
+  const uint32_t z = 0;
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n}\n" ::"r"(tmem_d),
+      "l"(da), "l"(db), "r"(idesc), "r"(accumulate), "r"(z));
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(saddr(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+struct TcArgs {
+  int M, N, Kp;   // Kp: K padded to a multiple of 64
+  int terms;      // 1: hi.hi (bf16 mode); 3: hi.hi + hi.lo + lo.hi (fp32-accurate mode)
+  float* C;
+  int64_t ldc;
+  int* status;
+};
+
+template <int TERMS>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_constant__ CUtensorMap a_lo,
+                   const __grid_constant__ CUtensorMap b_hi, const __grid_constant__ CUtensorMap b_lo, TcArgs p) {
+  constexpr int kPerStage = TERMS == 1 ? 2 : 4;          // tiles per stage: A hi, B hi (+ A lo, B lo)
+  constexpr int kStages = TERMS == 1 ? 6 : 3;
+  constexpr uint32_t kStageBytes = kPerStage * kTileBytes;
+  extern __shared__ uint8_t smem_raw[];
+  // 128-byte swizzled tiles need 1024-byte aligned bases
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+  uint64_t* empty = full + kStages;
+  uint64_t* acc_full = empty + kStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.y * kBM, n0 = blockIdx.x * kBN;
+  const int nk = p.Kp / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      bar_init(&full[s], 1);
+      bar_init(&empty[s], 1);
+    }
+    bar_init(acc_full, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(tmem_slot)),
+                 "r"(kBN));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  bool ok = true;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int kb = 0; kb < nk; ++kb) {
+        const int s = kb % kStages, use = kb / kStages;
+        if (use > 0 && !bar_wait(&empty[s], (uint32_t)((use - 1) & 1))) ok = false;
+        uint8_t* st = smem + s * kStageBytes;
+        bar_expect_tx(&full[s], kStageBytes);
+        tma_tile(st, &a_hi, kb * kBK, m0, &full[s]);
+        tma_tile(st + kTileBytes, &b_hi, kb * kBK, n0, &full[s]);
+        if (TERMS == 3) {
+          tma_tile(st + 2 * kTileBytes, &a_lo, kb * kBK, m0, &full[s]);
+          tma_tile(st + 3 * kTileBytes, &b_lo, kb * kBK, n0, &full[s]);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16(kBM, kBN);
+      for (int kb = 0; kb < nk; ++kb) {
+        const int s = kb % kStages;
+        if (!bar_wait(&full[s], (uint32_t)((kb / kStages) & 1))) ok = false;
+        tc_fence_after();
+        const uint32_t st = saddr(smem + s * kStageBytes);
+#pragma unroll
+        for (int k = 0; k < kBK / 16; ++k) {  // 16 bf16 = 32 bytes along the swizzled row
+          const uint64_t ah = kmajor_sw128(st + k * 32), bh = kmajor_sw128(st + kTileBytes + k * 32);
+          umma_bf16(tmem, ah, bh, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          if (TERMS == 3) {
+            const uint64_t al = kmajor_sw128(st + 2 * kTileBytes + k * 32);
+            const uint64_t bl = kmajor_sw128(st + 3 * kTileBytes + k * 32);
+            umma_bf16(tmem, ah, bl, idesc, 1u);
+            umma_bf16(tmem, al, bh, idesc, 1u);
+          }
+        }
+        umma_commit(&empty[s]);  // the stage is free once these MMAs have read it
+      }
+      umma_commit(acc_full);
+    }
+  } else {
+    // epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31 = tile rows
+    const int quarter = warp & 3;
+    const int row = m0 + quarter * 32 + lane;
+    if (!bar_wait(acc_full, 0)) ok = false;
+    tc_fence_after();
+    const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16);
+    float* crow = p.C + (int64_t)row * p.ldc;
+#pragma unroll 1
+    for (int c = 0; c < kBN; c += 8) {
+      uint32_t v[8];
+      asm volatile(
+          "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];\n"
+          : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+          : "r"(taddr + (uint32_t)c));
+      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+      const int col = n0 + c;
+      if (row < p.M) {
+        if (col + 8 <= p.N && (p.ldc & 3) == 0) {
+          float4* dst = reinterpret_cast<float4*>(crow + col);
+          dst[0] = make_float4(__uint_as_float(v[0]), __uint_as_float(v[1]), __uint_as_float(v[2]), __uint_as_float(v[3]));
+          dst[1] = make_float4(__uint_as_float(v[4]), __uint_as_float(v[5]), __uint_as_float(v[6]), __uint_as_float(v[7]));
+        } else {
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            if (col + u < p.N) crow[col + u] = __uint_as_float(v[u]);
+        }
+      }
+    }
+  }
+  if (!ok) atomicExch(p.status, 1);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kBN));
+  }
+}
+
+// f32 [rows, cols] (row stride ld) -> bf16 hi (and lo) [rows, kp], zero-padded columns.
+__global__ void split_rows_kernel(const float* __restrict__ src, int64_t rows, int64_t cols, int64_t ld,
+                                  int64_t kp, __nv_bfloat16* __restrict__ hi, __nv_bfloat16* __restrict__ lo) {
+  const int64_t total = rows * kp;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / kp, c = i % kp;
+    const float v = c < cols ? src[r * ld + c] : 0.0f;
+    const __nv_bfloat16 h = __float2bfloat16_rn(v);
+    hi[i] = h;
+    if (lo) lo[i] = __float2bfloat16_rn(v - __bfloat162float(h));
+  }
+}
+
+// f32 B [k, n] -> bf16 B^T hi (and lo) [n, kp] through 32 x 32 shared-memory tiles.
+__global__ void split_transpose_kernel(const float* __restrict__ b, int64_t k, int64_t n, int64_t kp,
+                                       __nv_bfloat16* __restrict__ hi, __nv_bfloat16* __restrict__ lo) {
+  __shared__ float tile[32][33];
+  const int64_t k0 = (int64_t)blockIdx.x * 32, n0 = (int64_t)blockIdx.y * 32;
+  for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+    const int64_t kk = k0 + r, nn = n0 + threadIdx.x;
+    tile[r][threadIdx.x] = (kk < k && nn < n) ? b[kk * n + nn] : 0.0f;
+  }
+  __syncthreads();
+  for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+    const int64_t nn = n0 + r, kk = k0 + threadIdx.x;
+    if (nn < n && kk < kp) {
+      const float v = tile[threadIdx.x][r];
+      const __nv_bfloat16 h = __float2bfloat16_rn(v);
+      hi[nn * kp + kk] = h;
+      if (lo) lo[nn * kp + kk] = __float2bfloat16_rn(v - __bfloat162float(h));
+    }
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// bf16 [rows, kp] K-major operand, 128 x 64 boxes, 128-byte swizzle
+bool make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t kp) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)kp, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(kp * 2)};
+  cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)kBM};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int* tc_status(int dev) {
+  static int* status[kMaxDevices] = {};
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lk(mu);
+  if (!status[dev]) {
+    if (cudaMalloc(&status[dev], sizeof(int)) != cudaSuccess) return nullptr;
+    cudaMemset(status[dev], 0, sizeof(int));
+  }
+  return status[dev];
+}
+
+template <int TERMS>
+cudaError_t launch_tc(const CUtensorMap& ah, const CUtensorMap& al, const CUtensorMap& bh, const CUtensorMap& bl,
+                      const TcArgs& a, cudaStream_t stream) {
+  constexpr int kPerStage = TERMS == 1 ? 2 : 4;
+  constexpr int kStages = TERMS == 1 ? 6 : 3;
+  const size_t smem = (size_t)kStages * kPerStage * kTileBytes + 1024 + 256;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<TERMS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  dim3 grid((unsigned)((a.N + kBN - 1) / kBN), (unsigned)((a.M + kBM - 1) / kBM));
+  tc_gemm_kernel<TERMS><<<grid, kTcThreads, smem, stream>>>(ah, al, bh, bl, a);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+// C[b] = A[b] (m x k) . B[b] (k x n) on tcgen05; terms 1 (bf16 operands) or 3 (fp32-accurate).
+int tc_matmul(const float* a, const float* b, float* out, int64_t batch, int64_t m, int64_t k, int64_t n,
+              int terms, int dev, cudaStream_t stream) {
+  if (m == 0 || n == 0) return J4B_OK;
+  if (k == 0) {
+    J4B_CUDA(cudaMemsetAsync(out, 0, (size_t)(batch * m * n) * 4, stream), "cudaMemsetAsync");
+    return J4B_OK;
+  }
+  if (m > INT32_MAX / 2 || n > INT32_MAX / 2 || k > INT32_MAX / 2)
+    return set_error(J4B_EINVAL, "matmul dimension too large for the tensor-core path");
+  int* status = tc_status(dev);
+  if (!status) return set_error(J4B_ENOMEM, "tensor-core status word allocation failed");
+  const int64_t kp = (k + kBK - 1) / kBK * kBK;
+  const bool split = terms == 3;
+  const size_t abytes = (size_t)(m * kp) * 2, bbytes = (size_t)(n * kp) * 2;
+  void* scratch = nullptr;
+  const size_t total = (abytes + bbytes) * (split ? 2 : 1) + 1024;
+  J4B_CUDA(cudaMallocAsync(&scratch, total, stream), "cudaMallocAsync(matmul operands)");
+  auto al256 = [](size_t v) { return (v + 255) & ~size_t(255); };
+  uint8_t* base = (uint8_t*)scratch;
+  __nv_bfloat16* ahi = (__nv_bfloat16*)base;
+  __nv_bfloat16* alo = split ? (__nv_bfloat16*)(base + al256(abytes)) : nullptr;
+  size_t off = al256(abytes) * (split ? 2 : 1);
+  __nv_bfloat16* bhi = (__nv_bfloat16*)(base + off);
+  __nv_bfloat16* blo = split ? (__nv_bfloat16*)(base + off + al256(bbytes)) : nullptr;
+  int rc = J4B_OK;
+  for (int64_t bi = 0; bi < batch && rc == J4B_OK; ++bi) {
+    const float* ab = a + bi * m * k;
+    const float* bb = b + bi * k * n;
+    float* cb = out + bi * m * n;
+    split_rows_kernel<<<(unsigned)std::min<int64_t>((m * kp + 255) / 256, 148 * 16), 256, 0, stream>>>(ab, m, k, k, kp, ahi, alo);
+    dim3 tg((unsigned)((kp + 31) / 32), (unsigned)((n + 31) / 32));
+    split_transpose_kernel<<<tg, dim3(32, 8), 0, stream>>>(bb, k, n, kp, bhi, blo);
+    CUtensorMap mah, mal, mbh, mbl;
+    if (!make_map(&mah, ahi, m, kp) || !make_map(&mbh, bhi, n, kp) ||
+        (split && (!make_map(&mal, alo, m, kp) || !make_map(&mbl, blo, n, kp)))) {
+      rc = set_error(J4B_ECUDA, "cuTensorMapEncodeTiled failed for the matmul operands");
+      break;
+    }
+    if (!split) {
+      mal = mah;
+      mbl = mbh;
+    }
+    TcArgs args;
+    args.M = (int)m;
+    args.N = (int)n;
+    args.Kp = (int)kp;
+    args.terms = terms;
+    args.C = cb;
+    args.ldc = n;
+    args.status = status;
+    cudaError_t e = split ? launch_tc<3>(mah, mal, mbh, mbl, args, stream) : launch_tc<1>(mah, mal, mbh, mbl, args, stream);
+    if (e != cudaSuccess) rc = cuda_error(e, "tc_gemm_kernel");
+    count_launch(3);
+  }
+  cudaFreeAsync(scratch, stream);
+  return rc;
+}
+
+int tc_status_read(int dev, int* value) {
+  int* st = tc_status(dev);
+  if (!st) return set_error(J4B_ENOMEM, "status");
+  J4B_CUDA(cudaMemcpy(value, st, sizeof(int), cudaMemcpyDeviceToHost), "cudaMemcpy(status)");
+  return J4B_OK;
+}
+
+}  // namespace j4b

@@ -54,6 +54,11 @@ struct DeviceGuard {
   }
 };
 
+// C[b] = A[b] . B[b] on the tcgen05 tensor cores; terms 1 = bf16 operands, 3 = fp32-accurate split
+int tc_matmul(const float* a, const float* b, float* out, int64_t batch, int64_t m, int64_t k, int64_t n,
+              int terms, int dev, cudaStream_t stream);
+int tc_status_read(int dev, int* value);
+
 // out[k] = sum of a[sources[p]] for p in [offsets[k], offsets[k+1]), in that order
 int launch_segment_sum(const float* a, const int64_t* offsets, const int64_t* sources, int64_t n_dst,
                        float* out, j4b_stream s);

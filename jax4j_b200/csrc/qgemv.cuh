@@ -36,7 +36,8 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
                "r"(bytes)
                : "memory");
 }
-// 1-D bulk copy global -> this CTA's shared memory (no multicast). 16-byte aligned, size % 16 == 0.
+// 1-D bulk copy global -> this CTA's own shared memory (one destination CTA). 16-byte aligned,
+// size % 16 == 0.
 __device__ __forceinline__ void tma_load_1d(void* dst, const void* src, uint32_t bytes,
                                             uint64_t* bar) {
   asm volatile(
