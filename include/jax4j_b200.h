@@ -185,6 +185,11 @@ int j4b_quant_shape(j4b_qweight_t w, int* ggml_type, int64_t* rows, int64_t* col
  * add [batch, rows] f32 or 0, y [batch, rows] f32. batch = 1 is the reference call. */
 int j4b_quant_matvec(j4b_qweight_t w, j4b_buf x, j4b_buf add, j4b_buf y, int64_t batch,
                      j4b_stream s);
+/* Prefill projection (no reference counterpart: the reference only has the rank-1 quantMatvec):
+ * y [m, rows] = x [m, cols] . W^T, f32 row-major, on the tcgen05 tensor cores. precision
+ * 1 = bf16 operands (rel 1e-2); 0 or 2 = 3-term bf16 split of both operands (rel 1e-4). The
+ * weight is decoded bit-exactly (as quantGatherRow) into stream-ordered scratch first. */
+int j4b_quant_gemm(j4b_qweight_t w, j4b_buf x, j4b_buf y, int64_t m, int precision, j4b_stream s);
 /* quantGatherRow (QuantizedOps.java:32-33): bit-exact dequantised row, out [cols] f32. */
 int j4b_quant_gather_row(j4b_qweight_t w, int64_t row, j4b_buf out, j4b_stream s);
 /* Encoder (no reference counterpart; producers of GGUF data): w [rows, cols] f32 on the device

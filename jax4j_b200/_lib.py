@@ -87,6 +87,7 @@ SIGNATURES = {
     "j4b_quant_matvec": [_vp, _u64, _u64, _u64, _i64, _vp],
     "j4b_quant_gather_row": [_vp, _i64, _u64, _vp],
     "j4b_quantize": [_int, _u64, _i64, _i64, _u64, _vp],
+    "j4b_quant_gemm": [_vp, _u64, _u64, _i64, _int, _vp],
     "j4b_tape_compile": [_int, _i64p, ctypes.c_size_t, ctypes.POINTER(_vp)],
     "j4b_tape_launch": [_vp, ctypes.POINTER(_u64), _int, ctypes.POINTER(_u64), _int, _vp],
     "j4b_tape_free": [_vp],

@@ -438,6 +438,16 @@ class B200Backend:
     def quant_matvec_add(self, w: QuantBuffer, x: DeviceBuffer, add: DeviceBuffer):
         return self.quant_matvec(w, x, add)
 
+    def quant_gemm(self, w: QuantBuffer, x: DeviceBuffer, precision: int = 1) -> DeviceBuffer:
+        """Prefill projection y [m, rows] = x [m, cols] . W^T on the tensor cores (j4b_quant_gemm)."""
+        rows, cols = w.shape
+        if len(x.shape) != 2 or x.shape[1] != cols:
+            raise ValueError(f"quant_gemm expects x [m, {cols}], got {x.shape}")
+        out = self._new((x.shape[0], rows))
+        call("j4b_quant_gemm", ctypes.c_void_p(w.handle), x.ptr, out.ptr, x.shape[0], precision,
+             self.stream)
+        return out
+
     def quant_gather_row(self, w: QuantBuffer, row: int) -> DeviceBuffer:
         if len(w.shape) != 2:
             raise ValueError(f"quantGatherRow requires a rank-2 quantized matrix, got {w.shape}")

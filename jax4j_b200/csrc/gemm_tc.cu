@@ -312,6 +312,47 @@ cudaError_t launch_tc(const CUtensorMap& ah, const CUtensorMap& al, const CUtens
 
 }  // namespace
 
+// C (m x n, row stride n) = A (m x k, f32 row-major) . Bt^T, with Bt given as bf16 hi (and lo)
+// [n, kp] K-major (kp = k rounded up to 64, zero-padded). A is converted here.
+int tc_gemm_bt(const float* a, int64_t m, int64_t k, const __nv_bfloat16* bt_hi, const __nv_bfloat16* bt_lo,
+               int64_t n, int terms, float* out, int dev, cudaStream_t stream) {
+  if (m == 0 || n == 0) return J4B_OK;
+  int* status = tc_status(dev);
+  if (!status) return set_error(J4B_ENOMEM, "tensor-core status word allocation failed");
+  const int64_t kp = (k + kBK - 1) / kBK * kBK;
+  const bool split = terms == 3;
+  const size_t abytes = (size_t)(m * kp) * 2;
+  void* scratch = nullptr;
+  J4B_CUDA(cudaMallocAsync(&scratch, 2 * abytes + 512, stream), "cudaMallocAsync(matmul operand)");
+  __nv_bfloat16* ahi = (__nv_bfloat16*)scratch;
+  __nv_bfloat16* alo = split ? (__nv_bfloat16*)((uint8_t*)scratch + ((abytes + 255) & ~size_t(255))) : nullptr;
+  split_rows_kernel<<<(unsigned)std::min<int64_t>((m * kp + 255) / 256, 148 * 16), 256, 0, stream>>>(a, m, k, k, kp, ahi, alo);
+  int rc = J4B_OK;
+  CUtensorMap mah, mal, mbh, mbl;
+  if (!make_map(&mah, ahi, m, kp) || !make_map(&mbh, bt_hi, n, kp) ||
+      (split && (!make_map(&mal, alo, m, kp) || !make_map(&mbl, bt_lo, n, kp)))) {
+    rc = set_error(J4B_ECUDA, "cuTensorMapEncodeTiled failed for the matmul operands");
+  } else {
+    if (!split) {
+      mal = mah;
+      mbl = mbh;
+    }
+    TcArgs args;
+    args.M = (int)m;
+    args.N = (int)n;
+    args.Kp = (int)kp;
+    args.terms = terms;
+    args.C = out;
+    args.ldc = n;
+    args.status = status;
+    cudaError_t e = split ? launch_tc<3>(mah, mal, mbh, mbl, args, stream) : launch_tc<1>(mah, mal, mbh, mbl, args, stream);
+    if (e != cudaSuccess) rc = cuda_error(e, "tc_gemm_kernel");
+    count_launch(2);
+  }
+  cudaFreeAsync(scratch, stream);
+  return rc;
+}
+
 // C[b] = A[b] (m x k) . B[b] (k x n) on tcgen05; terms 1 (bf16 operands) or 3 (fp32-accurate).
 int tc_matmul(const float* a, const float* b, float* out, int64_t batch, int64_t m, int64_t k, int64_t n,
               int terms, int dev, cudaStream_t stream) {
@@ -322,50 +363,19 @@ int tc_matmul(const float* a, const float* b, float* out, int64_t batch, int64_t
   }
   if (m > INT32_MAX / 2 || n > INT32_MAX / 2 || k > INT32_MAX / 2)
     return set_error(J4B_EINVAL, "matmul dimension too large for the tensor-core path");
-  int* status = tc_status(dev);
-  if (!status) return set_error(J4B_ENOMEM, "tensor-core status word allocation failed");
   const int64_t kp = (k + kBK - 1) / kBK * kBK;
   const bool split = terms == 3;
-  const size_t abytes = (size_t)(m * kp) * 2, bbytes = (size_t)(n * kp) * 2;
+  const size_t bbytes = (size_t)(n * kp) * 2;
   void* scratch = nullptr;
-  const size_t total = (abytes + bbytes) * (split ? 2 : 1) + 1024;
-  J4B_CUDA(cudaMallocAsync(&scratch, total, stream), "cudaMallocAsync(matmul operands)");
-  auto al256 = [](size_t v) { return (v + 255) & ~size_t(255); };
-  uint8_t* base = (uint8_t*)scratch;
-  __nv_bfloat16* ahi = (__nv_bfloat16*)base;
-  __nv_bfloat16* alo = split ? (__nv_bfloat16*)(base + al256(abytes)) : nullptr;
-  size_t off = al256(abytes) * (split ? 2 : 1);
-  __nv_bfloat16* bhi = (__nv_bfloat16*)(base + off);
-  __nv_bfloat16* blo = split ? (__nv_bfloat16*)(base + off + al256(bbytes)) : nullptr;
+  J4B_CUDA(cudaMallocAsync(&scratch, 2 * bbytes + 512, stream), "cudaMallocAsync(matmul operand)");
+  __nv_bfloat16* bhi = (__nv_bfloat16*)scratch;
+  __nv_bfloat16* blo = split ? (__nv_bfloat16*)((uint8_t*)scratch + ((bbytes + 255) & ~size_t(255))) : nullptr;
   int rc = J4B_OK;
   for (int64_t bi = 0; bi < batch && rc == J4B_OK; ++bi) {
-    const float* ab = a + bi * m * k;
-    const float* bb = b + bi * k * n;
-    float* cb = out + bi * m * n;
-    split_rows_kernel<<<(unsigned)std::min<int64_t>((m * kp + 255) / 256, 148 * 16), 256, 0, stream>>>(ab, m, k, k, kp, ahi, alo);
     dim3 tg((unsigned)((kp + 31) / 32), (unsigned)((n + 31) / 32));
-    split_transpose_kernel<<<tg, dim3(32, 8), 0, stream>>>(bb, k, n, kp, bhi, blo);
-    CUtensorMap mah, mal, mbh, mbl;
-    if (!make_map(&mah, ahi, m, kp) || !make_map(&mbh, bhi, n, kp) ||
-        (split && (!make_map(&mal, alo, m, kp) || !make_map(&mbl, blo, n, kp)))) {
-      rc = set_error(J4B_ECUDA, "cuTensorMapEncodeTiled failed for the matmul operands");
-      break;
-    }
-    if (!split) {
-      mal = mah;
-      mbl = mbh;
-    }
-    TcArgs args;
-    args.M = (int)m;
-    args.N = (int)n;
-    args.Kp = (int)kp;
-    args.terms = terms;
-    args.C = cb;
-    args.ldc = n;
-    args.status = status;
-    cudaError_t e = split ? launch_tc<3>(mah, mal, mbh, mbl, args, stream) : launch_tc<1>(mah, mal, mbh, mbl, args, stream);
-    if (e != cudaSuccess) rc = cuda_error(e, "tc_gemm_kernel");
-    count_launch(3);
+    split_transpose_kernel<<<tg, dim3(32, 8), 0, stream>>>(b + bi * k * n, k, n, kp, bhi, blo);
+    count_launch(1);
+    rc = tc_gemm_bt(a + bi * m * k, m, k, bhi, blo, n, terms, out + bi * m * n, dev, stream);
   }
   cudaFreeAsync(scratch, stream);
   return rc;

@@ -58,6 +58,13 @@ struct DeviceGuard {
 int tc_matmul(const float* a, const float* b, float* out, int64_t batch, int64_t m, int64_t k, int64_t n,
               int terms, int dev, cudaStream_t stream);
 int tc_status_read(int dev, int* value);
+}  // namespace j4b
+#include <cuda_bf16.h>
+namespace j4b {
+// C (m x n) = A (m x k f32) . Bt^T, Bt bf16 hi (and lo for terms 3) [n, kp] K-major, kp = k
+// rounded up to 64 with zero padding
+int tc_gemm_bt(const float* a, int64_t m, int64_t k, const __nv_bfloat16* bt_hi, const __nv_bfloat16* bt_lo,
+               int64_t n, int terms, float* out, int dev, cudaStream_t stream);
 
 // out[k] = sum of a[sources[p]] for p in [offsets[k], offsets[k+1]), in that order
 int launch_segment_sum(const float* a, const int64_t* offsets, const int64_t* sources, int64_t n_dst,

@@ -31,6 +31,8 @@
 #include <algorithm>
 #include <cstring>
 
+#include <cuda_bf16.h>
+
 #include "j4b_internal.h"
 
 struct j4b_qweight {
@@ -288,6 +290,37 @@ __global__ void gather_row_kernel(Layout L, const uint8_t* __restrict__ data, in
     v = __fmul_rn(d, (float)code);
   }
   out[k] = v;
+}
+
+// Whole matrix to bf16 hi (and lo) [rows, kp], the K-major operand of the tensor-core GEMM;
+// each value is first decoded bit-exactly as by gather_row_kernel. Columns past `cols` are zeros.
+__global__ void dequant_bf16_kernel(Layout L, const uint8_t* __restrict__ data, int64_t rows, int64_t cols,
+                                    int64_t kp, __nv_bfloat16* __restrict__ hi, __nv_bfloat16* __restrict__ lo) {
+  const int64_t total = rows * kp;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = i / kp, k = i % kp;
+    float v = 0.0f;
+    if (k < cols) {
+      const int64_t tile = row / 16;
+      const int rr = (int)(row % 16), g = rr & 7, which = rr >> 3;
+      const int q = repacked_code(L, data, row, k);
+      const uint8_t* m = data + L.meta_offset(tile, k / 32, g, which);
+      if (L.type == J4B_Q4_K) {
+        const float d = __half2float(__ushort_as_half(rd16(m)));
+        const float dmin = __half2float(__ushort_as_half(rd16(m + 2)));
+        int sc, mn;
+        q4k_scale_min((int)((k % 256) / 32), m + 4, &sc, &mn);
+        v = __fsub_rn(__fmul_rn(__fmul_rn(d, (float)sc), (float)q), __fmul_rn(dmin, (float)mn));
+      } else {
+        const float d = __half2float(__ushort_as_half(rd16(m)));
+        const int code = L.type == J4B_Q8_0 ? q : (L.type == J4B_Q4_0 ? q - 8 : q - 1);
+        v = __fmul_rn(d, (float)code);
+      }
+    }
+    const __nv_bfloat16 h = __float2bfloat16_rn(v);
+    hi[i] = h;
+    if (lo) lo[i] = __float2bfloat16_rn(v - __bfloat162float(h));
+  }
 }
 
 Layout layout_of(const j4b_qweight* w) {
@@ -599,6 +632,36 @@ extern "C" int j4b_quant_gather_row(j4b_qweight_t w, int64_t row, j4b_buf out, j
       layout_of(w), w->data, w->cols, row, (float*)(uintptr_t)out);
   J4B_CHECK_LAUNCH("gather_row_kernel");
   return J4B_OK;
+}
+
+// Prefill projection: y[m, rows] = x[m, cols] . W^T on the tcgen05 tensor cores. The weight is
+// decoded (bit-exact) to bf16 K-major operands in stream-ordered scratch, then multiplied.
+extern "C" int j4b_quant_gemm(j4b_qweight_t w, j4b_buf x, j4b_buf y, int64_t m, int precision,
+                              j4b_stream s) {
+  J4B_REQUIRE(w != nullptr, "null quantized matrix");
+  J4B_REQUIRE(m >= 0, "negative row count");
+  J4B_REQUIRE(precision >= 0 && precision <= 2, "precision must be 0, 1 or 2");
+  if (m == 0) return J4B_OK;
+  J4B_REQUIRE(x && y, "quant_gemm needs x and y");
+  DeviceGuard guard(w->dev);
+  cudaStream_t stream = resolve_stream(w->dev, s);
+  const int terms = precision == 1 ? 1 : 3;
+  const int64_t kp = (w->cols + 63) / 64 * 64;
+  const size_t bytes = (size_t)(w->rows * kp) * 2;
+  void* scratch = nullptr;
+  J4B_CUDA(cudaMallocAsync(&scratch, 2 * bytes + 512, stream), "cudaMallocAsync(dequantised weight)");
+  __nv_bfloat16* hi = (__nv_bfloat16*)scratch;
+  __nv_bfloat16* lo = terms == 3 ? (__nv_bfloat16*)((uint8_t*)scratch + ((bytes + 255) & ~size_t(255))) : nullptr;
+  const int64_t total = w->rows * kp;
+  dequant_bf16_kernel<<<(unsigned)std::min<int64_t>((total + 255) / 256, 148 * 32), 256, 0, stream>>>(
+      layout_of(w), w->data, w->rows, w->cols, kp, hi, lo);
+  cudaError_t e = cudaGetLastError();
+  int rc = e == cudaSuccess ? J4B_OK : cuda_error(e, "dequant_bf16_kernel");
+  count_launch();
+  if (rc == J4B_OK)
+    rc = tc_gemm_bt((const float*)(uintptr_t)x, m, w->cols, hi, lo, w->rows, terms, (float*)(uintptr_t)y, w->dev, stream);
+  cudaFreeAsync(scratch, stream);
+  return rc;
 }
 
 extern "C" int j4b_quantize(int type, j4b_buf w, int64_t rows, int64_t cols, j4b_buf out,

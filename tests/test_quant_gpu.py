@@ -128,3 +128,43 @@ def test_baseline_sizes(backend, oracle, qtype, rows, cols, batch):
     for r in (0, rows - 1):
         got = backend.download(backend.quant_gather_row(w, r))
         assert np.array_equal(got, oracle.gather_row(qtype, blob, rows, cols, r))
+
+
+# ---- prefill projection: y [m, rows] = x [m, cols] . W^T on the tensor cores ----
+# 3-term split: normwise 1e-4. bf16 operands: 1e-2 of the magnitude of the summed products
+# (|x| . |W|^T), the scale of a bf16 rounding-error bound -- a lone output of a short dot product
+# can cancel below its terms' magnitude, where a plain normwise ratio would measure cancellation.
+
+@pytest.mark.parametrize("qtype", TYPES)
+@pytest.mark.parametrize("precision,tol", [(1, 1e-2), (2, 1e-4)])
+def test_quant_gemm_prefill(backend, oracle, qtype, precision, tol):
+    for i, (rows, cols) in enumerate(SHAPES[qtype]):
+        _, blob = make(oracle, qtype, rows, cols, 300 + i)
+        w = backend.upload_quantized(blob, qtype, (rows, cols))
+        deq = oracle.dequantize(qtype, blob, rows, cols).astype(np.float64)
+        for m in (1, 77, 300):
+            x = np.random.default_rng(m + i).standard_normal((m, cols)).astype(np.float32)
+            y = backend.download(backend.quant_gemm(w, backend.upload(x, x.shape), precision)).reshape(m, rows)
+            want = x.astype(np.float64) @ deq.T
+            if precision == 1:
+                scale = (np.abs(x).astype(np.float64) @ np.abs(deq).T).max()
+                err = float(np.abs(y - want).max() / scale)
+            else:
+                err = normwise(y, want)
+            assert err <= tol, (rows, cols, m, err)
+
+
+def test_quant_gemm_config5_shape(backend, oracle):
+    """A Q4_0 FFN projection at prefill scale: x [2048, 4096] . W^T, W [14336 x 4096]."""
+    rows, cols, m = 14336, 4096, 2048
+    g = torch.Generator(device="cuda").manual_seed(5)
+    w32 = (torch.randn(rows, cols, device="cuda", generator=g) * 0.02).contiguous()
+    blob = backend.quantize(backend.wrap(w32), Q4_0)
+    w = backend.upload_quantized(blob, Q4_0, (rows, cols))
+    x = torch.randn(m, cols, device="cuda", generator=g)
+    y = backend.quant_gemm(w, backend.wrap(x), 1).tensor.reshape(m, rows)
+    deq = torch.stack([backend.quant_gather_row(w, r).tensor for r in range(0, rows, 512)])
+    want = x.double() @ deq.double().T
+    got = y[:, ::512].double()
+    err = (got - want).abs().max() / want.abs().max()
+    assert err.item() <= 1e-2
