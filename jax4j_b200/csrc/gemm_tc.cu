@@ -9,12 +9,13 @@
 // product is hi.hi + hi.lo + lo.hi (about 16 mantissa bits, relative error ~1e-5), for the bf16
 // mode only hi.hi.
 //
-// One CTA computes one 128 x 128 tile of C with six warps:
+// One CTA computes one 128 x 256 (bf16 mode) or 128 x 128 (3-term mode) tile of C with six
+// warps:
 //   warp 0  one thread streams 64-wide K slices of the A and B tiles into a ring of
 //           shared-memory stages with 2-D TMA tile loads (128-byte swizzle), completion counted
 //           on the stage's `full` mbarrier;
-//   warp 1  allocates 128 TMEM columns (the fp32 accumulator, one lane per tile row) and one
-//           thread issues tcgen05.mma (M=128, N=128, K=16 per instruction) from shared-memory
+//   warp 1  allocates 256 / 128 TMEM columns (the fp32 accumulator, one lane per tile row) and
+//           one thread issues tcgen05.mma (M=128, N=256 / 128, K=16 each) from shared-memory
 //           descriptors; tcgen05.commit releases each stage (`empty`) and finally signals the
 //           epilogue (`acc_full`);
 //   warps 2-5  read the accumulator with tcgen05.ld (32 lanes x 8 columns per load; warp w
@@ -32,10 +33,20 @@
 namespace j4b {
 namespace {
 
-constexpr int kBM = 128, kBN = 128, kBK = 64;
+constexpr int kBM = 128, kBK = 64;
 constexpr int kTcThreads = 192;
 constexpr uint32_t kTcWaitLimit = 1u << 26;
-constexpr int kTileBytes = kBM * kBK * 2;  // one 128 x 64 bf16 tile (A or B)
+constexpr int kTileBytes = kBM * kBK * 2;  // one 128 x 64 bf16 tile
+
+// bf16 mode: 128 x 256 output tiles (A 16 KB + B 32 KB per stage), a 2-stage ring (96 KB) so two
+// CTAs share an SM and one's prologue / epilogue overlaps the other's tensor work (TMEM: 2 x 256
+// columns). 3-term mode: 128 x 128 tiles, 3 stages of four 16 KB tiles, one CTA per SM.
+template <int TERMS>
+constexpr int tc_bn() { return TERMS == 1 ? 256 : 128; }
+template <int TERMS>
+constexpr int tc_stages() { return TERMS == 1 ? 2 : 3; }
+template <int TERMS>
+constexpr uint32_t tc_stage_bytes() { return TERMS == 1 ? kTileBytes * 3 : kTileBytes * 4; }
 
 __device__ __forceinline__ uint32_t saddr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -107,12 +118,13 @@ struct TcArgs {
 };
 
 template <int TERMS>
-__global__ void __launch_bounds__(kTcThreads, 1)
+__global__ void __launch_bounds__(kTcThreads, TERMS == 1 ? 2 : 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap a_hi, const __grid_constant__ CUtensorMap a_lo,
                    const __grid_constant__ CUtensorMap b_hi, const __grid_constant__ CUtensorMap b_lo, TcArgs p) {
-  constexpr int kPerStage = TERMS == 1 ? 2 : 4;          // tiles per stage: A hi, B hi (+ A lo, B lo)
-  constexpr int kStages = TERMS == 1 ? 6 : 3;
-  constexpr uint32_t kStageBytes = kPerStage * kTileBytes;
+  constexpr int kBN = tc_bn<TERMS>();
+  constexpr int kStages = tc_stages<TERMS>();
+  constexpr uint32_t kStageBytes = tc_stage_bytes<TERMS>();
+  constexpr uint32_t kBTile = (uint32_t)kBN * kBK * 2;  // B tile bytes
   extern __shared__ uint8_t smem_raw[];
   // 128-byte swizzled tiles need 1024-byte aligned bases
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -154,8 +166,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         tma_tile(st, &a_hi, kb * kBK, m0, &full[s]);
         tma_tile(st + kTileBytes, &b_hi, kb * kBK, n0, &full[s]);
         if (TERMS == 3) {
-          tma_tile(st + 2 * kTileBytes, &a_lo, kb * kBK, m0, &full[s]);
-          tma_tile(st + 3 * kTileBytes, &b_lo, kb * kBK, n0, &full[s]);
+          tma_tile(st + kTileBytes + kBTile, &a_lo, kb * kBK, m0, &full[s]);
+          tma_tile(st + 2 * kTileBytes + kBTile, &b_lo, kb * kBK, n0, &full[s]);
         }
       }
     }
@@ -172,8 +184,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           const uint64_t ah = kmajor_sw128(st + k * 32), bh = kmajor_sw128(st + kTileBytes + k * 32);
           umma_bf16(tmem, ah, bh, idesc, (kb > 0 || k > 0) ? 1u : 0u);
           if (TERMS == 3) {
-            const uint64_t al = kmajor_sw128(st + 2 * kTileBytes + k * 32);
-            const uint64_t bl = kmajor_sw128(st + 3 * kTileBytes + k * 32);
+            const uint64_t al = kmajor_sw128(st + kTileBytes + kBTile + k * 32);
+            const uint64_t bl = kmajor_sw128(st + 2 * kTileBytes + kBTile + k * 32);
             umma_bf16(tmem, ah, bl, idesc, 1u);
             umma_bf16(tmem, al, bh, idesc, 1u);
           }
@@ -222,16 +234,32 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
 }
 
-// f32 [rows, cols] (row stride ld) -> bf16 hi (and lo) [rows, kp], zero-padded columns.
+// f32 [rows, cols] (row stride ld) -> bf16 hi (and lo) [rows, kp], zero-padded columns. One
+// thread per 8 consecutive columns of a row (blockIdx.y strides the rows): one 16-byte store.
 __global__ void split_rows_kernel(const float* __restrict__ src, int64_t rows, int64_t cols, int64_t ld,
                                   int64_t kp, __nv_bfloat16* __restrict__ hi, __nv_bfloat16* __restrict__ lo) {
-  const int64_t total = rows * kp;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = i / kp, c = i % kp;
-    const float v = c < cols ? src[r * ld + c] : 0.0f;
-    const __nv_bfloat16 h = __float2bfloat16_rn(v);
-    hi[i] = h;
-    if (lo) lo[i] = __float2bfloat16_rn(v - __bfloat162float(h));
+  const int64_t c0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  if (c0 >= kp) return;
+  const bool vec = (ld % 4) == 0 && (reinterpret_cast<uintptr_t>(src) & 15) == 0 && c0 + 8 <= cols;
+  for (int64_t r = blockIdx.y; r < rows; r += gridDim.y) {
+    const float* s = src + r * ld + c0;
+    float v[8];
+    if (vec) {
+      const float4 a = __ldg(reinterpret_cast<const float4*>(s));
+      const float4 b = __ldg(reinterpret_cast<const float4*>(s) + 1);
+      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    } else {
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = c0 + u < cols ? s[u] : 0.0f;
+    }
+    alignas(16) __nv_bfloat16 h8[8], l8[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      h8[u] = __float2bfloat16_rn(v[u]);
+      l8[u] = __float2bfloat16_rn(v[u] - __bfloat162float(h8[u]));
+    }
+    *reinterpret_cast<uint4*>(hi + r * kp + c0) = *reinterpret_cast<const uint4*>(h8);
+    if (lo) *reinterpret_cast<uint4*>(lo + r * kp + c0) = *reinterpret_cast<const uint4*>(l8);
   }
 }
 
@@ -269,13 +297,13 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// bf16 [rows, kp] K-major operand, 128 x 64 boxes, 128-byte swizzle
-bool make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t kp) {
+// bf16 [rows, kp] K-major operand, box_rows x 64 boxes, 128-byte swizzle
+bool make_map(CUtensorMap* map, const void* base, int64_t rows, int64_t kp, int box_rows) {
   auto fn = encode_fn();
   if (!fn) return false;
   cuuint64_t dims[2] = {(cuuint64_t)kp, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)(kp * 2)};
-  cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)kBM};
+  cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
   return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -296,9 +324,9 @@ int* tc_status(int dev) {
 template <int TERMS>
 cudaError_t launch_tc(const CUtensorMap& ah, const CUtensorMap& al, const CUtensorMap& bh, const CUtensorMap& bl,
                       const TcArgs& a, cudaStream_t stream) {
-  constexpr int kPerStage = TERMS == 1 ? 2 : 4;
-  constexpr int kStages = TERMS == 1 ? 6 : 3;
-  const size_t smem = (size_t)kStages * kPerStage * kTileBytes + 1024 + 256;
+  constexpr int kStages = tc_stages<TERMS>();
+  constexpr int kBN = tc_bn<TERMS>();
+  const size_t smem = (size_t)kStages * tc_stage_bytes<TERMS>() + 1024 + 256;
   static bool configured = false;
   if (!configured) {
     cudaError_t e = cudaFuncSetAttribute(tc_gemm_kernel<TERMS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -326,11 +354,15 @@ int tc_gemm_bt(const float* a, int64_t m, int64_t k, const __nv_bfloat16* bt_hi,
   J4B_CUDA(cudaMallocAsync(&scratch, 2 * abytes + 512, stream), "cudaMallocAsync(matmul operand)");
   __nv_bfloat16* ahi = (__nv_bfloat16*)scratch;
   __nv_bfloat16* alo = split ? (__nv_bfloat16*)((uint8_t*)scratch + ((abytes + 255) & ~size_t(255))) : nullptr;
-  split_rows_kernel<<<(unsigned)std::min<int64_t>((m * kp + 255) / 256, 148 * 16), 256, 0, stream>>>(a, m, k, k, kp, ahi, alo);
+  {
+    dim3 grid((unsigned)((kp / 8 + 127) / 128), (unsigned)std::min<int64_t>(m, 65535));
+    split_rows_kernel<<<grid, 128, 0, stream>>>(a, m, k, k, kp, ahi, alo);
+  }
   int rc = J4B_OK;
   CUtensorMap mah, mal, mbh, mbl;
-  if (!make_map(&mah, ahi, m, kp) || !make_map(&mbh, bt_hi, n, kp) ||
-      (split && (!make_map(&mal, alo, m, kp) || !make_map(&mbl, bt_lo, n, kp)))) {
+  const int bn = split ? tc_bn<3>() : tc_bn<1>();
+  if (!make_map(&mah, ahi, m, kp, kBM) || !make_map(&mbh, bt_hi, n, kp, bn) ||
+      (split && (!make_map(&mal, alo, m, kp, kBM) || !make_map(&mbl, bt_lo, n, kp, bn)))) {
     rc = set_error(J4B_ECUDA, "cuTensorMapEncodeTiled failed for the matmul operands");
   } else {
     if (!split) {

@@ -293,33 +293,49 @@ __global__ void gather_row_kernel(Layout L, const uint8_t* __restrict__ data, in
 }
 
 // Whole matrix to bf16 hi (and lo) [rows, kp], the K-major operand of the tensor-core GEMM;
-// each value is first decoded bit-exactly as by gather_row_kernel. Columns past `cols` are zeros.
+// each value is first decoded bit-exactly as by gather_row_kernel. One thread per (row, 32-column
+// group): the group's scale once, 32 codes, four 16-byte stores. Columns past `cols` are zeros.
 __global__ void dequant_bf16_kernel(Layout L, const uint8_t* __restrict__ data, int64_t rows, int64_t cols,
                                     int64_t kp, __nv_bfloat16* __restrict__ hi, __nv_bfloat16* __restrict__ lo) {
-  const int64_t total = rows * kp;
+  const int64_t groups = kp / 32;
+  const int64_t total = rows * groups;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t row = i / kp, k = i % kp;
-    float v = 0.0f;
-    if (k < cols) {
-      const int64_t tile = row / 16;
-      const int rr = (int)(row % 16), g = rr & 7, which = rr >> 3;
-      const int q = repacked_code(L, data, row, k);
-      const uint8_t* m = data + L.meta_offset(tile, k / 32, g, which);
+    const int64_t row = i / groups, G = i % groups, k0 = G * 32;
+    const int64_t tile = row / 16;
+    const int rr = (int)(row % 16), g = rr & 7, which = rr >> 3;
+    float d1 = 0.f, m1 = 0.f, d = 0.f;
+    const bool live = k0 < cols;
+    if (live) {
+      const uint8_t* m = data + L.meta_offset(tile, G, g, which);
+      d = __half2float(__ushort_as_half(rd16(m)));
       if (L.type == J4B_Q4_K) {
-        const float d = __half2float(__ushort_as_half(rd16(m)));
         const float dmin = __half2float(__ushort_as_half(rd16(m + 2)));
         int sc, mn;
-        q4k_scale_min((int)((k % 256) / 32), m + 4, &sc, &mn);
-        v = __fsub_rn(__fmul_rn(__fmul_rn(d, (float)sc), (float)q), __fmul_rn(dmin, (float)mn));
-      } else {
-        const float d = __half2float(__ushort_as_half(rd16(m)));
-        const int code = L.type == J4B_Q8_0 ? q : (L.type == J4B_Q4_0 ? q - 8 : q - 1);
-        v = __fmul_rn(d, (float)code);
+        q4k_scale_min((int)((k0 % 256) / 32), m + 4, &sc, &mn);
+        d1 = __fmul_rn(d, (float)sc);
+        m1 = __fmul_rn(dmin, (float)mn);
       }
     }
-    const __nv_bfloat16 h = __float2bfloat16_rn(v);
-    hi[i] = h;
-    if (lo) lo[i] = __float2bfloat16_rn(v - __bfloat162float(h));
+    __nv_bfloat16* hrow = hi + row * kp + k0;
+    __nv_bfloat16* lrow = lo ? lo + row * kp + k0 : nullptr;
+#pragma unroll
+    for (int c = 0; c < 32; c += 8) {
+      alignas(16) __nv_bfloat16 h8[8], l8[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int64_t k = k0 + c + u;
+        float v = 0.0f;
+        if (live && k < cols) {
+          const int q = repacked_code(L, data, row, k);
+          if (L.type == J4B_Q4_K) v = __fsub_rn(__fmul_rn(d1, (float)q), m1);
+          else v = __fmul_rn(d, (float)(L.type == J4B_Q8_0 ? q : (L.type == J4B_Q4_0 ? q - 8 : q - 1)));
+        }
+        h8[u] = __float2bfloat16_rn(v);
+        l8[u] = __float2bfloat16_rn(v - __bfloat162float(h8[u]));
+      }
+      *reinterpret_cast<uint4*>(hrow + c) = *reinterpret_cast<const uint4*>(h8);
+      if (lrow) *reinterpret_cast<uint4*>(lrow + c) = *reinterpret_cast<const uint4*>(l8);
+    }
   }
 }
 
@@ -652,7 +668,7 @@ extern "C" int j4b_quant_gemm(j4b_qweight_t w, j4b_buf x, j4b_buf y, int64_t m, 
   J4B_CUDA(cudaMallocAsync(&scratch, 2 * bytes + 512, stream), "cudaMallocAsync(dequantised weight)");
   __nv_bfloat16* hi = (__nv_bfloat16*)scratch;
   __nv_bfloat16* lo = terms == 3 ? (__nv_bfloat16*)((uint8_t*)scratch + ((bytes + 255) & ~size_t(255))) : nullptr;
-  const int64_t total = w->rows * kp;
+  const int64_t total = w->rows * (kp / 32);
   dequant_bf16_kernel<<<(unsigned)std::min<int64_t>((total + 255) / 256, 148 * 32), 256, 0, stream>>>(
       layout_of(w), w->data, w->rows, w->cols, kp, hi, lo);
   cudaError_t e = cudaGetLastError();
