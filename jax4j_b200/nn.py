@@ -91,6 +91,20 @@ def mlp_value_and_grad(w1, b1, w2, b2, x, onehot):
     return [loss, *grads]
 
 
+def mlp_train_step(opt: "FunctionalAdam"):
+    """One compiled training step of the MLP workload: value and gradient of mlp_loss, then the
+    Adam update, as one function of (params, first moments, second moments, step, x, onehot) ->
+    [loss, params', m', v', step'] (the shape of the reference's compiled training step,
+    TransformsTest.java:455-490)."""
+
+    def step(w1, b1, w2, b2, m1, m2, m3, m4, v1, v2, v3, v4, t, x, onehot):
+        loss, grads = T.value_and_grad_tree(lambda ps: mlp_loss(ps, x, onehot), [w1, b1, w2, b2])
+        out = opt._step_flat(w1, b1, w2, b2, *grads, m1, m2, m3, m4, v1, v2, v3, v4, t)
+        return [loss, *out]
+
+    return step
+
+
 def rms_swiglu_rows(x: Tensor, g: Tensor, eps: float = 1e-5) -> Tensor:
     """vmap over the rows of x [R, C] of the per-row RMSNorm + SwiGLU body; y [R, C/2]."""
     c = x.shape[1]

@@ -180,3 +180,16 @@ def test_tape_rejects_bad_launch_arguments(backend):
         plan["engine"].launch([buf.ptr, buf.ptr], [buf.ptr], backend.stream)
     with pytest.raises(ValueError):
         plan["engine"].launch([buf.ptr + 4], [buf.ptr], backend.stream)
+
+
+@pytest.mark.parametrize("dims", [(16, 32, 24, 10), (256, 784, 512, 10)])
+def test_mlp_training_step_tape(backend, dims):
+    """valueAndGrad + Adam in one compiled step (the reference's compiled training step)."""
+    w1, b1, w2, b2, x, onehot = mlp_inputs(*dims)
+    ps = [w1, b1, w2, b2]
+    rng = np.random.default_rng(4)
+    ms = [0.01 * rng.standard_normal(p.shape).astype(np.float32) for p in ps]
+    vs = [np.abs(0.01 * rng.standard_normal(p.shape)).astype(np.float32) for p in ps]
+    step = np.array([2.0], np.float32)
+    fn = nn.mlp_train_step(nn.FunctionalAdam(1e-3))
+    engine_vs_oracle(backend, fn, ps + ms + vs + [step, x, onehot])
