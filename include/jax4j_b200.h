@@ -198,6 +198,31 @@ int j4b_quant_gather_row(j4b_qweight_t w, int64_t row, j4b_buf out, j4b_stream s
 int j4b_quantize(int ggml_type, j4b_buf w, int64_t rows, int64_t cols, j4b_buf out_blocks,
                  j4b_stream s);
 
+/* ---- Collectives over NVLink peer memory (no reference counterpart: the reference has no
+ * multi-GPU path). One process per GPU; each rank allocates one buffer, exchanges the 64-byte
+ * IPC handles out of band (e.g. torch.distributed), maps the others and builds a group. A
+ * `channel` (0..15) is an independent sequence of collective calls; every rank must make the
+ * same calls on a channel in the same order. Waits are bounded (about a second); a wait that
+ * gives up sets the group status (j4b_peer_status) instead of hanging. ---- */
+typedef struct j4b_peer_group j4b_peer_group;
+int j4b_peer_alloc(int dev, size_t bytes, j4b_buf* local, uint8_t* ipc_handle_64);
+int j4b_peer_open(int dev, const uint8_t* ipc_handle_64, j4b_buf* remote);
+int j4b_peer_close(j4b_buf remote);
+int j4b_peer_free(j4b_buf local);
+/* bases[r] = rank r's buffer as mapped in this process (the local one for r == rank). */
+int j4b_peer_group_create(int dev, int nranks, int rank, const j4b_buf* bases, size_t bytes,
+                          j4b_peer_group** out);
+int j4b_peer_group_free(j4b_peer_group* g);
+int j4b_peer_status(j4b_peer_group* g, int* status);
+/* Row-sharded quantMatvec fused with its all-gather: this rank's W holds rows
+ * [rank*rows, (rank+1)*rows) of the whole matrix; the GEMV stores its outputs straight into
+ * every rank's buffer and y_all [batch, rows * nranks] receives the gathered result. batch <= 16. */
+int j4b_quant_matvec_allgather(j4b_qweight_t w, j4b_buf x, j4b_buf add, j4b_buf y_all, int64_t batch,
+                               j4b_peer_group* g, int channel, j4b_stream s);
+/* out[i] = sum over ranks of src[i], summed in rank order (identical on every rank), n <= 131072. */
+int j4b_peer_allreduce(j4b_peer_group* g, int channel, j4b_buf src, int64_t n, j4b_buf out,
+                       j4b_stream s);
+
 /* ---- JIT tapes: ExecutionPlan.capture / execute (core/tensor/ExecutionPlan.java:49-132) ----
  *
  * A tape is the SPI call list a compiled function records once per input signature

@@ -88,6 +88,16 @@ SIGNATURES = {
     "j4b_quant_gather_row": [_vp, _i64, _u64, _vp],
     "j4b_quantize": [_int, _u64, _i64, _i64, _u64, _vp],
     "j4b_quant_gemm": [_vp, _u64, _u64, _i64, _int, _vp],
+    "j4b_peer_alloc": [_int, ctypes.c_size_t, ctypes.POINTER(_u64), ctypes.c_char_p],
+    "j4b_peer_open": [_int, ctypes.c_char_p, ctypes.POINTER(_u64)],
+    "j4b_peer_close": [_u64],
+    "j4b_peer_free": [_u64],
+    "j4b_peer_group_create": [_int, _int, _int, ctypes.POINTER(_u64), ctypes.c_size_t,
+                              ctypes.POINTER(_vp)],
+    "j4b_peer_group_free": [_vp],
+    "j4b_peer_status": [_vp, ctypes.POINTER(ctypes.c_int)],
+    "j4b_quant_matvec_allgather": [_vp, _u64, _u64, _u64, _i64, _vp, _int, _vp],
+    "j4b_peer_allreduce": [_vp, _int, _u64, _i64, _u64, _vp],
     "j4b_tape_compile": [_int, _i64p, ctypes.c_size_t, ctypes.POINTER(_vp)],
     "j4b_tape_launch": [_vp, ctypes.POINTER(_u64), _int, ctypes.POINTER(_u64), _int, _vp],
     "j4b_tape_free": [_vp],

@@ -66,6 +66,22 @@ namespace j4b {
 int tc_gemm_bt(const float* a, int64_t m, int64_t k, const __nv_bfloat16* bt_hi, const __nv_bfloat16* bt_lo,
                int64_t n, int terms, float* out, int dev, cudaStream_t stream);
 
+// ---- collectives over peer memory (peer.cu) ----
+constexpr int kMaxPeerRanks = 8;
+
+// Where a GEMV's y goes when it is all-gathered over peer memory.
+struct GemvPeers {
+  int nranks, rank;
+  float* y[kMaxPeerRanks];       // each rank's gathered buffer (the channel's data slice)
+  unsigned* ctr[kMaxPeerRanks];  // each rank's arrival counter for this rank as the source
+  const unsigned* step;          // this rank's step counter of the channel
+  int64_t half_floats;           // floats per parity half of the slice
+};
+int peer_group_ranks(const j4b_peer_group* g);
+int peer_gemv_targets(const j4b_peer_group* g, int channel, int64_t gathered_floats, GemvPeers* t);
+int peer_wait_copy(const j4b_peer_group* g, int channel, unsigned incr, float* out, int64_t n,
+                   cudaStream_t stream);
+
 // out[k] = sum of a[sources[p]] for p in [offsets[k], offsets[k+1]), in that order
 int launch_segment_sum(const float* a, const int64_t* offsets, const int64_t* sources, int64_t n_dst,
                        float* out, j4b_stream s);

@@ -144,7 +144,37 @@ struct GemvArgs {
   float* partials;     // [ksplit][rt][256] (global split-K fold only)
   unsigned* arrivals;  // one counter per tile group
   int* status;         // nonzero after a bounded wait gave up
+  // All-gather over peer memory (nranks > 1): this rank's rows of y go straight into every
+  // rank's gathered buffer, [batch][rows * nranks] in the parity half selected by the local step
+  // counter, and every CTA counts one arrival at every rank after its stores.
+  int nranks, rank;
+  float* peer_y[kMaxPeerRanks];
+  unsigned* peer_ctr[kMaxPeerRanks];  // at rank p: the counter of this rank as a source
+  const unsigned* step;
+  int64_t half_floats;
 };
+
+// Stores one output, locally or into every rank's gathered buffer.
+__device__ __forceinline__ void store_y(const GemvArgs& a, int64_t par_off, int bcol, int64_t r, float v) {
+  if (a.nranks <= 1) {
+    a.y[(int64_t)bcol * a.rows + r] = v;
+    return;
+  }
+  const int64_t idx = par_off + (int64_t)bcol * (a.rows * a.nranks) + (int64_t)a.rank * a.rows + r;
+  for (int p = 0; p < a.nranks; ++p) a.peer_y[p][idx] = v;
+}
+
+// After this CTA's last store: the CTA barrier orders every thread's stores before thread 0's
+// system-scope fence, which orders them before the arrival counted at every rank. Called by
+// every thread of the CTA on each exit path.
+__device__ __forceinline__ void signal_peers(const GemvArgs& a) {
+  if (a.nranks <= 1) return;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    for (int p = 0; p < a.nranks; ++p) atomicAdd_system(a.peer_ctr[p], 1u);
+  }
+}
 
 constexpr int kXStride = 1024 + 4;  // floats per staged x row (padding spreads the banks)
 
@@ -458,6 +488,14 @@ __device__ __forceinline__ void out_coord_pk(int v, int& row, int& bcol) {
   bcol = v & 3;
 }
 
+// Inverse maps: the element index v of (row in tile, batch column). The epilogues walk outputs
+// row-fastest with them, so a warp's stores to y are 128 contiguous bytes (over NVLink too).
+__device__ __forceinline__ int out_index(int row, int bcol) {
+  const int n = bcol >> 3, t = (bcol & 7) >> 1, c = 2 * (row >> 3) + (bcol & 1);
+  return 32 * (4 * n + c) + 4 * (row & 7) + t;
+}
+__device__ __forceinline__ int out_index_pk(int row, int bcol) { return 32 * (row >> 3) + 4 * (row & 7) + bcol; }
+
 template <int QT, int NT, bool PK>
 __global__ void __launch_bounds__(kGemvThreads, 1) qgemv_kernel(GemvArgs a) {
   using T = GemvTraits<QT>;
@@ -473,6 +511,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) qgemv_kernel(GemvArgs a) {
   __shared__ int last_flag;
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int64_t par_off = 0;  // parity half of the gathered buffer, read after the dependency wait
   // 16 warps: warp w works on the 128-column chunk w % 8 of the CTA's K range, for the tiles of
   // each stage whose index has the parity w / 8.
   const int chunk = warp & 7, sub = warp >> 3;
@@ -512,6 +551,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) qgemv_kernel(GemvArgs a) {
     for (; issued < kStages && issued < ncopies; issued++) issue(issued);
   pdl_launch_dependents();
   pdl_wait();
+  if (a.nranks > 1) par_off = (int64_t)(*a.step & 1u) * a.half_floats;
 
   // ---- x: the CTA's 1024-column slice of every batch row, staged once in shared memory with
   // coalesced 128-bit loads (columns past K and rows past the batch are zeros) ----
@@ -657,7 +697,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) qgemv_kernel(GemvArgs a) {
         const int64_t r = tile * 16 + row;
         if (r < a.rows && bcol < a.batch) {
           if (a.add) total += a.add[(int64_t)bcol * a.rows + r];
-          a.y[(int64_t)bcol * a.rows + r] = total;
+          store_y(a, par_off, bcol, r, total);
         }
       } else if (a.cluster) {
         mine[(c * kM + j) * kVals + v] = total;
@@ -676,7 +716,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) qgemv_kernel(GemvArgs a) {
         mbar_wait_bounded(&full[cc % kStages], (uint32_t)((cc / kStages) & 1));
     }
     __syncthreads();
-    if (!a.cluster) return;  // cluster members still take both cluster barriers below
+    if (!a.cluster) {
+      signal_peers(a);
+      return;  // cluster members still take both cluster barriers below
+    }
   }
 
   if (a.cluster) {
@@ -692,18 +735,20 @@ __global__ void __launch_bounds__(kGemvThreads, 1) qgemv_kernel(GemvArgs a) {
         st_cluster_f32(landing + (rank - 1) * nv + i, 0, mine[i]);
     cluster_sync();
     if (rank == 0 && !failed) {
-      for (int i = threadIdx.x; i < nv; i += kGemvThreads) {
+      const int nr = ntiles * 16;  // rows of this tile group, walked fastest
+      for (int j = threadIdx.x; j < a.batch * nr; j += kGemvThreads) {
+        const int bcol = j / nr, rr = j % nr;
+        const int i = (rr >> 4) * kVals + (PK ? out_index_pk(rr & 15, bcol) : out_index(rr & 15, bcol));
         float total = mine[i];
         for (int sp = 1; sp < a.ksplit; sp++) total += landing[(sp - 1) * nv + i];
-        int row, bcol;
-        if (PK) out_coord_pk(i % kVals, row, bcol); else out_coord(i % kVals, row, bcol);
-        const int64_t r = (tile0 + i / kVals) * 16 + row;
-        if (r < a.rows && bcol < a.batch) {
+        const int64_t r = tile0 * 16 + rr;
+        if (r < a.rows) {
           if (a.add) total += a.add[(int64_t)bcol * a.rows + r];
-          a.y[(int64_t)bcol * a.rows + r] = total;
+          store_y(a, par_off, bcol, r, total);
         }
       }
     }
+    signal_peers(a);
     return;
   }
 
@@ -712,43 +757,50 @@ __global__ void __launch_bounds__(kGemvThreads, 1) qgemv_kernel(GemvArgs a) {
     __syncthreads();
     if (threadIdx.x == 0) last_flag = atomicAdd(a.arrivals + group, 1u) == (unsigned)(a.ksplit - 1);
     __syncthreads();
-    if (!last_flag) return;
+    if (!last_flag) {
+      signal_peers(a);
+      return;
+    }
     __threadfence();
-    // The last CTA of the group folds the K splits in split order (deterministic); four outputs
-    // per thread per pass keep all their loads in flight together.
-    const int nv = ntiles * kVals;
-    for (int i0 = threadIdx.x; i0 < nv; i0 += 4 * kGemvThreads) {
+    // The last CTA of the group folds the K splits in split order (deterministic), walking the
+    // outputs row-fastest; four outputs per thread per pass keep their loads in flight together.
+    const int nr = ntiles * 16;
+    const int nout = a.batch * nr;
+    for (int j0 = threadIdx.x; j0 < nout; j0 += 4 * kGemvThreads) {
       float tot[4] = {0.f, 0.f, 0.f, 0.f};
+      int64_t off[4];
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        const int j = min(j0 + u * kGemvThreads, nout - 1);
+        const int bcol = j / nr, rr = j % nr;
+        off[u] = (tile0 + (rr >> 4)) * 256 + (PK ? out_index_pk(rr & 15, bcol) : out_index(rr & 15, bcol));
+      }
       for (int sp = 0; sp < a.ksplit; sp++) {
 #pragma unroll
-        for (int u = 0; u < 4; u++) {
-          const int idx = min(i0 + u * kGemvThreads, nv - 1);
-          const int64_t tile = tile0 + idx / kVals;
-          tot[u] += __ldcg(a.partials + ((int64_t)sp * a.rt + tile) * 256 + idx % kVals);
-        }
+        for (int u = 0; u < 4; u++) tot[u] += __ldcg(a.partials + (int64_t)sp * a.rt * 256 + off[u]);
       }
 #pragma unroll
       for (int u = 0; u < 4; u++) {
-        const int idx = i0 + u * kGemvThreads;
-        if (idx >= nv) break;
-        const int64_t tile = tile0 + idx / kVals;
-        int row, bcol;
-        if (PK) out_coord_pk(idx % kVals, row, bcol); else out_coord(idx % kVals, row, bcol);
-        const int64_t r = tile * 16 + row;
-        if (r < a.rows && bcol < a.batch) {
+        const int j = j0 + u * kGemvThreads;
+        if (j >= nout) break;
+        const int bcol = j / nr, rr = j % nr;
+        const int64_t r = tile0 * 16 + rr;
+        if (r < a.rows) {
           float v = tot[u];
           if (a.add) v += a.add[(int64_t)bcol * a.rows + r];
-          a.y[(int64_t)bcol * a.rows + r] = v;
+          store_y(a, par_off, bcol, r, v);
         }
       }
     }
     if (threadIdx.x == 0) a.arrivals[group] = 0u;
   }
+  signal_peers(a);
 }
 
 template <int QT, int NT, bool PK>
 cudaError_t launch_gemv(const j4b_qweight* w, const float* x, const float* add, float* y,
-                        int batch, int sms, cudaStream_t stream) {
+                        int batch, int sms, cudaStream_t stream, const GemvPeers* peers,
+                        unsigned* grid_out) {
   // Largest dynamic shared memory a CTA may request: the device's opt-in limit minus the
   // kernel's static shared memory (set once per instantiation).
   static int64_t kMaxSmem = -1;
@@ -782,6 +834,24 @@ cudaError_t launch_gemv(const j4b_qweight* w, const float* x, const float* add, 
   a.partials = w->partials;
   a.arrivals = w->arrivals;
   a.status = w->status;
+  a.nranks = 1;
+  a.rank = 0;
+  a.step = nullptr;
+  a.half_floats = 0;
+  for (int p = 0; p < kMaxPeerRanks; ++p) {
+    a.peer_y[p] = nullptr;
+    a.peer_ctr[p] = nullptr;
+  }
+  if (peers) {
+    a.nranks = peers->nranks;
+    a.rank = peers->rank;
+    a.step = peers->step;
+    a.half_floats = peers->half_floats;
+    for (int p = 0; p < peers->nranks; ++p) {
+      a.peer_y[p] = peers->y[p];
+      a.peer_ctr[p] = peers->ctr[p];
+    }
+  }
   // One 16-warp CTA per SM: as many tile groups as fit next to the K splits, tiles shared out
   // evenly.
   int64_t groups_fit = std::max<int64_t>(1, (int64_t)sms / w->ksplit);
@@ -838,13 +908,15 @@ cudaError_t launch_gemv(const j4b_qweight* w, const float* x, const float* add, 
   attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = a.cluster ? 2 : 1;
+  if (grid_out) *grid_out = cfg.gridDim.x;
   return cudaLaunchKernelEx(&cfg, qgemv_kernel<QT, NT, PK>, a);
 }
 
 template <int QT>
 cudaError_t gemv_dispatch(const j4b_qweight* w, const float* x, const float* add, float* y,
-                          int batch, int sms, cudaStream_t stream) {
-  if (batch <= 4) return launch_gemv<QT, 1, true>(w, x, add, y, batch, sms, stream);
-  if (batch <= 8) return launch_gemv<QT, 1, false>(w, x, add, y, batch, sms, stream);
-  return launch_gemv<QT, 2, false>(w, x, add, y, batch, sms, stream);
+                          int batch, int sms, cudaStream_t stream, const GemvPeers* peers = nullptr,
+                          unsigned* grid_out = nullptr) {
+  if (batch <= 4) return launch_gemv<QT, 1, true>(w, x, add, y, batch, sms, stream, peers, grid_out);
+  if (batch <= 8) return launch_gemv<QT, 1, false>(w, x, add, y, batch, sms, stream, peers, grid_out);
+  return launch_gemv<QT, 2, false>(w, x, add, y, batch, sms, stream, peers, grid_out);
 }

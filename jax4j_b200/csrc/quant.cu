@@ -637,6 +637,36 @@ extern "C" int j4b_quant_matvec(j4b_qweight_t w, j4b_buf x, j4b_buf add, j4b_buf
   return J4B_OK;
 }
 
+extern "C" int j4b_quant_matvec_allgather(j4b_qweight_t w, j4b_buf x, j4b_buf add, j4b_buf y_all,
+                                          int64_t batch, j4b_peer_group* g, int channel, j4b_stream s) {
+  if (!w) return set_error(J4B_EINVAL, "null quantized weight");
+  J4B_REQUIRE(g != nullptr, "null peer group");
+  J4B_REQUIRE(batch >= 1 && batch <= 16, "all-gathered quantMatvec takes batch 1..16, got %lld", (long long)batch);
+  J4B_REQUIRE(x && y_all, "quantMatvec needs x and y buffers");
+  J4B_REQUIRE((x & 15) == 0 && ((y_all | add) & 3) == 0, "quantMatvec needs x 16-byte aligned");
+  DeviceGuard guard(w->dev);
+  cudaStream_t stream = resolve_stream(w->dev, s);
+  const int nranks = peer_group_ranks(g);
+  const int64_t gathered = batch * w->rows * nranks;
+  GemvPeers t;
+  int st = peer_gemv_targets(g, channel, gathered, &t);
+  if (st) return st;
+  const float* xp = (const float*)(uintptr_t)x;
+  const float* ap = add ? (const float*)(uintptr_t)add : nullptr;
+  const int sms = device_ctx(w->dev)->sm_count;
+  unsigned grid = 0;
+  cudaError_t e = cudaErrorInvalidValue;
+  switch (w->type) {
+    case J4B_Q8_0: e = gemv_dispatch<J4B_Q8_0>(w, xp, ap, nullptr, (int)batch, sms, stream, &t, &grid); break;
+    case J4B_Q4_0: e = gemv_dispatch<J4B_Q4_0>(w, xp, ap, nullptr, (int)batch, sms, stream, &t, &grid); break;
+    case J4B_Q4_K: e = gemv_dispatch<J4B_Q4_K>(w, xp, ap, nullptr, (int)batch, sms, stream, &t, &grid); break;
+    case J4B_Q2_0: e = gemv_dispatch<J4B_Q2_0>(w, xp, ap, nullptr, (int)batch, sms, stream, &t, &grid); break;
+  }
+  if (e != cudaSuccess) return cuda_error(e, "qgemv_kernel");
+  count_launch();
+  return peer_wait_copy(g, channel, grid, (float*)(uintptr_t)y_all, gathered, stream);
+}
+
 extern "C" int j4b_quant_gather_row(j4b_qweight_t w, int64_t row, j4b_buf out, j4b_stream s) {
   if (!w) return set_error(J4B_EINVAL, "null quantized weight");
   J4B_REQUIRE(row >= 0 && row < w->rows, "quantGatherRow row %lld out of range [0, %lld)",
