@@ -1,20 +1,31 @@
-"""Benchmark of the jax4j B200 engine's hot path (one JSON line on rank 0).
+"""Benchmark of the jax4j B200 engine's hot paths (one JSON line on rank 0).
 
-Workload (the metric's "Q8_0 dequant-GEMV GB/s"): y[8, 4096] = W x with W a
-4096 x 4096 weight drawn 0.02*N(0,1) by the engine's own counter PRNG (PrngKey(0).split(2)[1])
-and quantised Q8_0 on the device, x [8, 4096] ~ N(0,1) (split(2)[0]). A step is one GEMV call;
-`value` is algorithmic bytes (GGUF weight bytes + x + y) per second over all GPUs.
+Default workload (the metric's "Q8_0 dequant-GEMV GB/s"): y[8, 4096] = W x
+with W a 4096 x 4096 weight drawn 0.02*N(0,1) by the engine's own counter PRNG
+(PrngKey(0).split(2)[1]) and quantised Q8_0 on the device, x [8, 4096] ~ N(0,1)
+(split(2)[0]). A step is one GEMV call; `value` is algorithmic bytes (GGUF weight bytes + x + y)
+per second over all GPUs. Other workloads (--config):
+  q4_k_b1, q4_k_b16   configs[2]: Q4_K decode GEMV, W [14336 x 4096], batch 1 / 16 (GB/s)
+  rms_swiglu          configs[3]: the vmap-batched RMSNorm + SwiGLU value-and-gradient tape,
+                      x [4096, 8192] per GPU (steps/s)
+  mlp_adam            configs[0]: the compiled MLP valueAndGrad + Adam training step (steps/s)
+  prefill_q4_0        configs[4] prefill projection x [16384, 4096] . W^T, W Q4_0 [14336 x 4096]
+                      on the tcgen05 tensor cores (TFLOP/s)
+  gemm_f32            the same shape as a dense f32 matmul, fp32-accurate 3-term mode (TFLOP/s)
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl engine|reference]
-                  [--config q8_0_b8|q4_k_b1|q4_k_b16]
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl engine|reference] [--config NAME]
 
-N > 1 (launched by torchrun, one rank per GPU): each rank owns a 4096-row slab of a (4096 N)-row
-weight (weak scaling), computes its y slab and all-gathers the slabs over NCCL each step.
+N > 1 (launched by torchrun, one rank per GPU), weak scaling: for the GEMV each rank owns a
+4096-row slab of a (4096 N)-row weight and the GEMV epilogue stores its y slab into every rank's
+buffer over NVLink (j4b_quant_matvec_allgather); for the tape each rank owns 4096 rows and
+[dg, loss] are summed over NVLink peer memory (j4b_peer_allreduce); the GEMM and MLP workloads
+run as independent replicas.
 
-Timing: W untimed warm-up steps, then exactly K steps replayed from a CUDA graph, bracketed by a
-barrier and device synchronisation, timed with CUDA events on the launching stream, max over
-ranks. The weights rotate over enough identical copies (>= 2x L2) that every step streams its
-weight from HBM. nvidia-smi samples clocks during the timed region.
+Timing: W untimed warm-up steps, then exactly K steps (replayed from a CUDA graph where the step
+is graph-capturable), bracketed by a barrier and device synchronisation, timed with CUDA events
+on the launching stream, max over ranks. The GEMV weights rotate over enough identical copies
+(>= 2x L2) that every step streams its weight from HBM; the tape and GEMM inputs are larger than
+L2. nvidia-smi samples clocks during the timed region.
 """
 from __future__ import annotations
 
@@ -76,6 +87,8 @@ def mlp_tape_fn():
     sys.path.insert(0, HERE)
     from jax4j_b200 import nn
     return nn.mlp_train_step(nn.FunctionalAdam(1e-3))
+
+
 GEMM_CONFIGS = {
     # name: (m, n, k, ggml type or None for dense f32, precision, label)
     "prefill_q4_0": (16384, 14336, 4096, 2, 1, "BASELINE configs[4] prefill projection: x[8*2048, 4096] . "
@@ -605,16 +618,7 @@ def run_engine_tape(args):
 
     # the tape: value and gradient of the mean of y^2 over the global batch (each rank's mean
     # scaled by 1/world, so the all-reduced sums are the global loss and dg)
-    if world == 1:
-        fn = nn.rms_swiglu_value_and_grad
-    else:
-        inv = 1.0 / world
-
-        def fn(xt, gt):
-            from jax4j_b200 import transforms as T
-            loss, (dx, dg) = T.value_and_grad_tree(
-                lambda ps: nn.rms_swiglu_loss(ps[0], ps[1]).mul(inv), [xt, gt])
-            return [loss, dx, dg]
+    fn = nn.rms_swiglu_value_and_grad_dp(world)
     tape = J.trace(fn, [(rows, cols), (cols,)])
     handle = TapeHandle(be, tape)
     # dg and the loss share one buffer (loss right after dg, 16-byte aligned) so one

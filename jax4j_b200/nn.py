@@ -129,3 +129,19 @@ def rms_swiglu_value_and_grad(x: Tensor, g: Tensor):
     """[loss, dx, dg] of rms_swiglu_loss."""
     loss, (dx, dg) = T.value_and_grad_tree(lambda ps: rms_swiglu_loss(ps[0], ps[1]), [x, g])
     return [loss, dx, dg]
+
+
+def rms_swiglu_value_and_grad_dp(world: int):
+    """Data-parallel shard of the same step: each of `world` ranks holds an equal share of the
+    rows; its loss carries the 1/world factor, so summing loss and dg over the ranks gives the
+    loss and dg of the whole batch, and each rank's dx is its rows of the whole batch's dx."""
+    if world == 1:
+        return rms_swiglu_value_and_grad
+    inv = 1.0 / world
+
+    def fn(x: Tensor, g: Tensor):
+        loss, (dx, dg) = T.value_and_grad_tree(
+            lambda ps: rms_swiglu_loss(ps[0], ps[1]).mul(inv), [x, g])
+        return [loss, dx, dg]
+
+    return fn

@@ -18,11 +18,14 @@ ALLREDUCE_CHANNEL = 1
 
 
 class PeerGroup:
-    def __init__(self, device: int, rank: int, world: int, nbytes: int = 80 << 20):
+    def __init__(self, device: int, rank: int, world: int, nbytes: int = 80 << 20, call=call):
+        """Collective over the ranks of the default process group. `call` is the C-ABI caller
+        (replaceable for tests of the exchange without a GPU)."""
         import torch.distributed as dist
         if world > 8:
             raise ValueError("peer groups hold at most 8 ranks")
         self.device, self.rank, self.world, self.nbytes = device, rank, world, nbytes
+        self.bases = []
         local = ctypes.c_uint64(0)
         handle = ctypes.create_string_buffer(64)
         call("j4b_peer_alloc", device, nbytes, ctypes.byref(local), handle)
@@ -42,6 +45,7 @@ class PeerGroup:
         g = ctypes.c_void_p()
         call("j4b_peer_group_create", device, world, rank, bases, nbytes, ctypes.byref(g))
         self.handle = g
+        self.bases = list(bases)
         dist.barrier()
 
     def allgather_matvec(self, w, x_ptr: int, y_all_ptr: int, batch: int, stream: int, add_ptr: int = 0):
