@@ -29,13 +29,13 @@
 #include <mutex>
 
 #include "j4b_internal.h"
+#include "j4b_wait.cuh"
 
 namespace j4b {
 namespace {
 
 constexpr int kBM = 128, kBK = 64;
 constexpr int kTcThreads = 192;
-constexpr uint32_t kTcWaitLimit = 1u << 26;
 constexpr int kTileBytes = kBM * kBK * 2;  // one 128 x 64 bf16 tile
 
 // bf16 mode: 128 x 256 output tiles (A 16 KB + B 32 KB per stage), a 2-stage ring (96 KB) so two
@@ -56,19 +56,8 @@ __device__ __forceinline__ void bar_init(uint64_t* b, uint32_t n) {
 __device__ __forceinline__ void bar_expect_tx(uint64_t* b, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(saddr(b)), "r"(bytes) : "memory");
 }
-__device__ __forceinline__ bool bar_try_wait(uint64_t* b, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(ok)
-      : "r"(saddr(b)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
 __device__ __forceinline__ bool bar_wait(uint64_t* b, uint32_t parity) {
-  for (uint32_t i = 0; i < kTcWaitLimit; ++i)
-    if (bar_try_wait(b, parity)) return true;
-  return false;
+  return mbar_wait_timed(saddr(b), parity);
 }
 
 // 2-D TMA tile load into this CTA's shared memory (one destination CTA); x is the K coordinate

@@ -13,11 +13,10 @@
 // Launches use programmatic dependent launch: the weight prefetch of one GEMV overlaps the tail
 // of the kernel before it (see the comment at the prefetch).
 //
-// Every mbarrier wait is bounded: on timeout the CTA records an error code in the weight's
+// Every mbarrier wait is bounded in time (0.2 s): on timeout the CTA records an error code in the weight's
 // status word, waits (bounded) for its copies in flight, and returns.
 
 constexpr int kGemvThreads = 512;
-constexpr uint32_t kWaitLimit = 1u << 26;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return (uint32_t)__cvta_generic_to_shared(p);
@@ -46,20 +45,8 @@ __device__ __forceinline__ void tma_load_1d(void* dst, const void* src, uint32_t
       "l"(src), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t phase) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, "
-      "0, p;\n}\n"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(phase)
-      : "memory");
-  return ok != 0;
-}
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t phase) {
-  for (uint32_t it = 0; it < kWaitLimit; ++it)
-    if (mbar_try_wait(bar, phase)) return true;
-  return false;
+  return mbar_wait_timed(smem_u32(bar), phase);
 }
 
 // Programmatic dependent launch: let the next kernel in the stream start its prologue early /

@@ -34,6 +34,7 @@
 #include <cuda_bf16.h>
 
 #include "j4b_internal.h"
+#include "j4b_wait.cuh"
 
 struct j4b_qweight {
   int dev;
