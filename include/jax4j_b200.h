@@ -223,6 +223,31 @@ int j4b_quant_matvec_allgather(j4b_qweight_t w, j4b_buf x, j4b_buf add, j4b_buf 
 int j4b_peer_allreduce(j4b_peer_group* g, int channel, j4b_buf src, int64_t n, j4b_buf out,
                        j4b_stream s);
 
+/* ---- Decoder block (the Llama-style block of the quantised workloads; no reference counterpart:
+ * the reference has no attention op, RoPE or KV cache, so a block written with its Tensor API
+ * composes matmul, elementwise ops and axis reductions, and these kernels compute the same
+ * functions). Activations are token-major f32 [tokens, width]. The fused QKV projection output
+ * is [tokens, 3 * heads * head_dim] (q | k | v). The KV cache is f16 [batch, heads, capacity,
+ * head_dim]; rotated queries are f32 [batch, heads, seq, head_dim]; attention output is token-
+ * major f32 [batch * seq, heads * head_dim]. head_dim must be 128. ---- */
+/* out[r, :] = x[r, :] / sqrt(mean(x[r, :]^2) + eps) * g; cols % 4 == 0, 16-byte aligned. */
+int j4b_rmsnorm(j4b_buf x, j4b_buf g, float eps, int64_t rows, int64_t cols, j4b_buf out, j4b_stream s);
+/* RoPE on q and k of tokens (b, t) at positions pos0 + t, t < seq: adjacent pairs (2i, 2i+1) of a
+ * head rotated by pos * theta^(-2i / head_dim). Writes q_out, and k (rotated) and v as f16 into
+ * the caches at slots pos0 .. pos0 + seq - 1. */
+int j4b_rope_kv(j4b_buf qkv, int64_t batch, int64_t seq, int64_t heads, int64_t head_dim, int64_t pos0,
+                double theta, j4b_buf q_out, j4b_buf k_cache, j4b_buf v_cache, int64_t capacity, j4b_stream s);
+/* Decode: one query per sequence (q_out of j4b_rope_kv with seq 1) against the first `length`
+ * cached tokens; out [batch, heads * head_dim]. f32 softmax and accumulation. */
+int j4b_attention_decode(j4b_buf q, j4b_buf k_cache, j4b_buf v_cache, int64_t batch, int64_t heads,
+                         int64_t head_dim, int64_t capacity, int64_t length, j4b_buf out, j4b_stream s);
+/* Causal prefill of seq tokens per sequence (seq % 64 == 0, cached at slots 0 .. seq - 1): f16
+ * tensor-core products with f32 softmax and accumulation (the rel 1e-2 tensor-core bar). */
+int j4b_attention_prefill(j4b_buf q, j4b_buf k_cache, j4b_buf v_cache, int64_t batch, int64_t heads,
+                          int64_t head_dim, int64_t capacity, int64_t seq, j4b_buf out, j4b_stream s);
+/* out [rows, width] = gate * sigmoid(gate) * up, gate_up [rows, 2 * width] = gate | up. */
+int j4b_swiglu(j4b_buf gate_up, int64_t rows, int64_t width, j4b_buf out, j4b_stream s);
+
 /* ---- JIT tapes: ExecutionPlan.capture / execute (core/tensor/ExecutionPlan.java:49-132) ----
  *
  * A tape is the SPI call list a compiled function records once per input signature

@@ -88,6 +88,11 @@ SIGNATURES = {
     "j4b_quant_gather_row": [_vp, _i64, _u64, _vp],
     "j4b_quantize": [_int, _u64, _i64, _i64, _u64, _vp],
     "j4b_quant_gemm": [_vp, _u64, _u64, _i64, _int, _vp],
+    "j4b_rmsnorm": [_u64, _u64, ctypes.c_float, _i64, _i64, _u64, _vp],
+    "j4b_rope_kv": [_u64, _i64, _i64, _i64, _i64, _i64, ctypes.c_double, _u64, _u64, _u64, _i64, _vp],
+    "j4b_attention_decode": [_u64, _u64, _u64, _i64, _i64, _i64, _i64, _i64, _u64, _vp],
+    "j4b_attention_prefill": [_u64, _u64, _u64, _i64, _i64, _i64, _i64, _i64, _u64, _vp],
+    "j4b_swiglu": [_u64, _i64, _i64, _u64, _vp],
     "j4b_peer_alloc": [_int, ctypes.c_size_t, ctypes.POINTER(_u64), ctypes.c_char_p],
     "j4b_peer_open": [_int, ctypes.c_char_p, ctypes.POINTER(_u64)],
     "j4b_peer_close": [_u64],
