@@ -89,6 +89,37 @@ def mlp_tape_fn():
     return nn.mlp_train_step(nn.FunctionalAdam(1e-3))
 
 
+DECODER_CONFIGS = {
+    # name: (batch, seq or cached tokens, label); d_model 4096, 32 heads x 128, FFN 14336, Q4_0
+    "decoder_decode": (64, 2048, "BASELINE configs[4] decode: Llama-style block, Q4_0 weights, batch 64, "
+                       "one new token per sequence against a 2048-token f16 KV cache"),
+    "decoder_prefill": (8, 2048, "BASELINE configs[4] prefill: Llama-style block, Q4_0 weights, batch 8 x "
+                        "seq 2048, causal attention, bf16 tensor-core projections"),
+}
+DEC_D, DEC_HEADS, DEC_FFN = 4096, 32, 14336
+# default timed steps and warm-up per workload family (a GEMV call is microseconds, a prefill
+# step tens of milliseconds)
+DEFAULT_STEPS = {"gemv": (20000, 200), "tape": (20000, 200), "gemm": (100, 5), "decoder_decode": (200, 5),
+                 "decoder_prefill": (10, 3)}
+
+
+def decoder_weight_bytes():
+    d, f = DEC_D, DEC_FFN
+    params = 3 * d * d + d * d + 2 * f * d + d * f
+    return params // 32 * 18
+
+
+def decoder_kv_bytes(batch, cached):
+    return 2 * batch * DEC_HEADS * cached * 128 * 2
+
+
+def decoder_prefill_flops(batch, seq):
+    d, f = DEC_D, DEC_FFN
+    proj = 2.0 * batch * seq * (3 * d * d + d * d + 2 * f * d + d * f)
+    attn = 2.0 * 2.0 * batch * DEC_HEADS * (seq * (seq + 1) / 2) * 128  # causal q.k^T and p.v
+    return proj + attn
+
+
 GEMM_CONFIGS = {
     # name: (m, n, k, ggml type or None for dense f32, precision, label)
     "prefill_q4_0": (16384, 14336, 4096, 2, 1, "BASELINE configs[4] prefill projection: x[8*2048, 4096] . "
@@ -407,6 +438,8 @@ def run_reference_gemm(args):
 
 
 def run_reference(args):
+    if args.config in DECODER_CONFIGS:
+        return run_reference_decoder(args)
     if args.config in TAPE_CONFIGS:
         return run_reference_tape(args)
     if args.config in GEMM_CONFIGS:
@@ -883,7 +916,278 @@ def run_engine_gemm(args):
     return 0
 
 
+# ------------------------------------------------------------------------------------------------
+# decoder block
+# ------------------------------------------------------------------------------------------------
+
+def cpu_decoder_rate(mode, blobs, g_attn, g_ffn, budget_s, threads):
+    """Times the float64 oracle block (oracle/decoder.py) on a bounded sample: decode of one of the
+    sequences against a 2048-token cache, or prefill of one 64-token sequence, with numpy's BLAS
+    limited to `threads`. Returns (rate in the workload's unit, sample text, seconds per step)."""
+    from threadpoolctl import threadpool_limits
+    with threadpool_limits(threads):
+        return _cpu_decoder_rate(mode, blobs, g_attn, g_ffn, budget_s)
+
+
+def _cpu_decoder_rate(mode, blobs, g_attn, g_ffn, budget_s):
+    import numpy as np
+    sys.path.insert(0, HERE)
+    from oracle.decoder import Block
+    ref = Block(blobs, DEC_D, DEC_HEADS, DEC_FFN, g_attn, g_ffn)
+    rng = np.random.default_rng(0)
+    if mode == "decoder_decode":
+        cached = 2048
+        k = rng.standard_normal((1, DEC_HEADS, cached, 128)).astype(np.float16)
+        v = rng.standard_normal((1, DEC_HEADS, cached, 128)).astype(np.float16)
+        x = rng.standard_normal((1, DEC_D)).astype(np.float32)
+        n, t0 = 0, time.perf_counter()
+        while True:
+            ref.decode(x, k, v, cached - 1)
+            n += 1
+            dt = time.perf_counter() - t0
+            if dt >= budget_s:
+                break
+        per = decoder_weight_bytes() + decoder_kv_bytes(1, cached)
+        return per * n / dt / 1e9, (f"{n} decode step(s) of 1 of 64 sequences (2048 cached tokens), float64 "
+                                    "numpy oracle block"), dt / n
+    seq = 64
+    x = rng.standard_normal((seq, DEC_D)).astype(np.float32)
+    n, t0 = 0, time.perf_counter()
+    while True:
+        ref.prefill(x, 1, seq)
+        n += 1
+        dt = time.perf_counter() - t0
+        if dt >= budget_s:
+            break
+    return (decoder_prefill_flops(1, seq) * n / dt / 1e12,
+            f"{n} prefill(s) of one 64-token sequence, float64 numpy oracle block", dt / n)
+
+
+def run_reference_decoder(args):
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return 0
+    import numpy as np
+    sys.path.insert(0, HERE)
+    from oracle import oracle as o
+    batch, seq, label = DECODER_CONFIGS[args.config]
+    # host-drawn weights with the oracle's encoder (no GPU on this arm)
+    rng = np.random.default_rng(1)
+    shapes = {"wqkv": (3 * DEC_D, DEC_D), "wo": (DEC_D, DEC_D), "wgu": (2 * DEC_FFN, DEC_D), "wd": (DEC_D, DEC_FFN)}
+    blobs = {name: o.quantize(2, (rng.standard_normal(shape, dtype=np.float32) * 0.02).astype(np.float32))
+             for name, shape in shapes.items()}
+    g_attn = (1 + 0.1 * rng.standard_normal(DEC_D)).astype(np.float32)
+    g_ffn = (1 + 0.1 * rng.standard_normal(DEC_D)).astype(np.float32)
+    threads = os.cpu_count() or 1
+    budget = max(0.5, min(10.0, 90.0 / max(args.steps + args.warmup, 1)))
+    for _ in range(min(args.warmup, 1)):
+        cpu_decoder_rate(args.config, blobs, g_attn, g_ffn, budget, threads)
+    rates, times, sample = [], [], ""
+    for _ in range(min(args.steps, 5)):
+        r, sample, dt = cpu_decoder_rate(args.config, blobs, g_attn, g_ffn, budget, threads)
+        rates.append(r)
+        times.append(dt)
+    value = statistics.median(rates)
+    unit = "GB/s" if args.config == "decoder_decode" else "TFLOP/s"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 6), "unit": unit, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * statistics.median(times), 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+        "config": {"workload": label, "batch": batch, "seq": seq, "d_model": DEC_D, "heads": DEC_HEADS,
+                   "ffn": DEC_FFN},
+        "cpu_baseline": {"value": round(value, 6), "unit": unit, "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 6), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_engine_decoder(args):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    sys.path.insert(0, HERE)
+    from jax4j_b200 import _lib
+    from jax4j_b200.backend import B200Backend, torch_stream
+    from jax4j_b200.decoder import HEAD_DIM, DecoderBlock, DecoderWeights, KVCache
+    from jax4j_b200.prng import PrngKey
+
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    be = B200Backend(local)
+    batch, seq, label = DECODER_CONFIGS[args.config]
+    decode = args.config == "decoder_decode"
+    dev = torch.device("cuda", local)
+    want_cpu = rank == 0 and world == 1 and not args.no_cpu_baseline
+    w = DecoderWeights.random(be, DEC_D, DEC_HEADS, DEC_FFN, PrngKey.of(1), keep_blobs=want_cpu)
+    block = DecoderBlock(be, w)
+    kx, kc = PrngKey.of(0).split(2)
+    cache = KVCache(be, batch, DEC_HEADS, seq)
+    if decode:
+        tokens = batch
+        # cached keys/values of slots 0 .. seq - 2 ~ N(0, 1), drawn per sequence by the engine's PRNG
+        per = DEC_HEADS * seq * HEAD_DIM
+        for b in range(batch):
+            for dst in (cache.k, cache.v):
+                r = be.random_normal(kc.seed, kc.counter + (2 * b + (dst is cache.v)) * per, (DEC_HEADS, seq, HEAD_DIM))
+                dst[b] = r.tensor.view(DEC_HEADS, seq, HEAD_DIM).half()
+        cache.k[:, :, seq - 1:] = 0
+        cache.v[:, :, seq - 1:] = 0
+        pos = seq - 1
+        step_bytes = decoder_weight_bytes() + decoder_kv_bytes(batch, seq) + 2 * batch * DEC_D * 4
+    else:
+        tokens = batch * seq
+        flops = decoder_prefill_flops(batch, seq)
+    x = be.random_normal(kx.seed, kx.counter, (tokens, DEC_D))
+    torch.cuda.synchronize()
+
+    def step():
+        return block.decode(x, cache, pos) if decode else block.prefill(x, cache, seq, 1)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    K, W = args.steps, max(3, args.warmup)
+    for _ in range(W):
+        step()
+    barrier()
+    graph = None
+    if decode:
+        # decode steps replay from a CUDA graph (no host work between the ~12 launches of a step)
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            step()
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(K):
+                step()
+        graph.replay()  # the first replay of a graph also uploads it: keep that out of the timed one
+        torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        barrier()
+        start.record()
+        if graph is not None:
+            graph.replay()
+        else:
+            for _ in range(K):
+                step()
+        end.record()
+        barrier()
+    clk = clocks.summary()
+    ms = start.elapsed_time(end)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    step_ms = ms / K
+    peaks_path = os.path.join(HERE, "MEASURED_PEAKS.json")
+    pk = json.load(open(peaks_path)) if os.path.exists(peaks_path) else {}
+
+    # dominant kernel alone
+    s = torch_stream()
+    if decode:
+        q = torch.randn(batch * DEC_HEADS * HEAD_DIM, device=dev)
+        att = torch.empty(batch * DEC_D, device=dev)
+        reps = 20
+        for _ in range(3):
+            _lib.call("j4b_attention_decode", q.data_ptr(), cache.k.data_ptr(), cache.v.data_ptr(), batch,
+                      DEC_HEADS, HEAD_DIM, seq, seq, att.data_ptr(), s)
+        torch.cuda.synchronize()
+        k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        k0.record()
+        for _ in range(reps):
+            _lib.call("j4b_attention_decode", q.data_ptr(), cache.k.data_ptr(), cache.v.data_ptr(), batch,
+                      DEC_HEADS, HEAD_DIM, seq, seq, att.data_ptr(), s)
+        k1.record()
+        torch.cuda.synchronize()
+        kern_us = k0.elapsed_time(k1) * 1e3 / reps
+        kv = decoder_kv_bytes(batch, seq) + 2 * batch * DEC_D * 4
+        peak = float(pk.get("hbm_gbs", 6650.0))
+        roof = {"bound": "hbm", "achieved": round(kv / (kern_us * 1e-6) / 1e9, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(kv / (kern_us * 1e-6) / 1e9 / peak, 4), "traffic": None,
+                "peak_source": "measured MEASURED_PEAKS.json hbm_gbs" if pk else "fallback",
+                "kernel": "attn_decode_kernel (KV cache read, 2,147,483,648 B + q/out per launch)",
+                "kernel_avg_us": round(kern_us, 1)}
+        value = world * step_bytes / (step_ms * 1e-3) / 1e9
+        unit = "GB/s"
+    else:
+        peak = float(pk.get("bf16_tflops_sustained", 1400.0))
+        achieved = flops / (step_ms * 1e-3) / 1e12
+        roof = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
+                "frac": round(achieved / peak, 4), "traffic": None,
+                "peak_source": "measured MEASURED_PEAKS.json bf16_tflops_sustained" if pk else "fallback 1.4 PFLOP/s",
+                "kernel": "the whole prefill step (tc_gemm_kernel projections hold ~97% of its flops)",
+                "kernel_avg_us": round(step_ms * 1e3, 1)}
+        value = world * flops / (step_ms * 1e-3) / 1e12
+        unit = "TFLOP/s"
+
+    # end to end through the public API: x from pinned host memory, the block output back
+    x_host = torch.from_numpy(np.ascontiguousarray(be.download(x))).pin_memory()
+    y_host = torch.empty(tokens * DEC_D, dtype=torch.float32).pin_memory()
+    e_steps = max(2, min(K, 20 if decode else 3))
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(e_steps):
+        _lib.call("j4b_h2d", x.ptr, ctypes.c_void_p(x_host.data_ptr()), x_host.numel() * 4, s)
+        y = step()
+        _lib.call("j4b_d2h", ctypes.c_void_p(y_host.data_ptr()), y.ptr, y_host.numel() * 4, s)
+    e1.record()
+    barrier()
+    e_s = e0.elapsed_time(e1) * 1e-3
+    e2e = world * (step_bytes / 1e9 if decode else flops / 1e12) * e_steps / e_s
+
+    cpu = None
+    if want_cpu:
+        blobs = {k2: v2.cpu().numpy() for k2, v2 in w.blobs.items()}
+        rate, sample, _ = cpu_decoder_rate(args.config, blobs, be.download(w.g_attn), be.download(w.g_ffn), 10.0, 1)
+        cpu = {"value": round(rate, 6), "unit": unit, "cores": 1, "kind": "port",
+               "sample": sample + f", 1 BLAS thread (host has {os.cpu_count()} cores)"}
+    if rank == 0:
+        cfg = {"workload": label, "batch": batch, "seq" if not decode else "cached_tokens": seq, "d_model": DEC_D,
+               "heads": DEC_HEADS, "head_dim": HEAD_DIM, "ffn": DEC_FFN, "quant": "Q4_0",
+               "parallelism": "replica" if world == 1 else f"{world} independent replicas",
+               "l2": "weights 137 MB and KV cache 2.1 GB exceed L2" if decode else "activations exceed L2"}
+        if decode:
+            cfg["tokens_per_s"] = round(world * batch / (step_ms * 1e-3), 1)
+            cfg["bytes_per_step"] = step_bytes
+            cfg["timing"] = "CUDA graph of K decode steps, CUDA events"
+        else:
+            cfg["flop_per_step"] = flops
+            cfg["timing"] = "K back-to-back prefill steps, CUDA events"
+        line = {
+            "metric": METRIC, "value": round(value, 3), "unit": unit, "n_gpus": world, "steps": K, "warmup": W,
+            "ms_per_step": round(step_ms, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32 (Q4_0 weights, f16 KV)" if decode else "bf16 (Q4_0 weights, f16 attention)",
+            "data": "synthetic", "config": cfg, "roofline": roof, "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e, 3), "unit": unit, "h2d_bytes_per_step": tokens * DEC_D * 4,
+                    "d2h_bytes_per_step": tokens * DEC_D * 4},
+            "gpu_launches": K * (21 if decode else 19),
+            "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"], "reasons": clk["reasons"],
+                       "samples": clk["samples"]},
+        }
+        print(json.dumps(line), flush=True)
+    if graph is not None:
+        del graph
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def run_engine(args):
+    if args.config in DECODER_CONFIGS:
+        return run_engine_decoder(args)
     if args.config in TAPE_CONFIGS:
         return run_engine_tape(args)
     if args.config in GEMM_CONFIGS:
@@ -1071,13 +1375,18 @@ def run_engine(args):
 def main():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=20000)
-    p.add_argument("--warmup", type=int, default=200)
+    p.add_argument("--steps", type=int, default=None, help="timed steps (default per workload)")
+    p.add_argument("--warmup", type=int, default=None, help="warm-up steps (default per workload)")
     p.add_argument("--impl", choices=["engine", "reference"], default="engine")
-    p.add_argument("--config", choices=sorted(CONFIGS) + sorted(TAPE_CONFIGS) + sorted(GEMM_CONFIGS),
-                   default="q8_0_b8")
+    p.add_argument("--config", choices=sorted(CONFIGS) + sorted(TAPE_CONFIGS) + sorted(GEMM_CONFIGS)
+                   + sorted(DECODER_CONFIGS), default="q8_0_b8")
     p.add_argument("--no-cpu-baseline", action="store_true")
     args = p.parse_args()
+    family = ("tape" if args.config in TAPE_CONFIGS else "gemm" if args.config in GEMM_CONFIGS
+              else args.config if args.config in DECODER_CONFIGS else "gemv")
+    steps, warmup = DEFAULT_STEPS[family]
+    args.steps = steps if args.steps is None else args.steps
+    args.warmup = warmup if args.warmup is None else args.warmup
     if args.impl == "reference":
         return run_reference(args)
     return run_engine(args)

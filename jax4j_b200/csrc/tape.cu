@@ -972,32 +972,36 @@ __device__ __forceinline__ void rmax_combine(float& v, long long& i, float v2, l
   if (v2 != v2) return;
   if (v2 > v || (v2 == v && i2 < i)) { v = v2; i = i2; }
 }
-// Block sum, identical in every thread: butterfly within warps, then each warp combines the
-// per-warp sums with a second butterfly (same order in every warp).
-template <int NT> __device__ __forceinline__ double block_sum(double v, double* red) {
+// Block reductions, identical in every thread: butterfly within warps, then each warp combines
+// the per-warp values (same order in every warp). Consecutive reductions alternate between the two
+// halves of `red` (rp counts the reductions a thread has made; every thread makes the same ones),
+// so one barrier per reduction suffices: a warp writes half h again only after the barrier of the
+// next reduction, which every warp reaches after its reads of half h.
+template <int NT> __device__ __forceinline__ double block_sum(double v, double* red, int& rp) {
+  double* r = red + (rp++ & 1) * (2 * (NT / 32));
   #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  if ((threadIdx.x & 31) == 0) r[threadIdx.x >> 5] = v;
   __syncthreads();
   const int lane = threadIdx.x & 31;
-  double tot = lane < NT / 32 ? red[lane] : 0.0;
+  double tot = lane < NT / 32 ? r[lane] : 0.0;
   #pragma unroll
   for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
-  __syncthreads();
   return tot;
 }
-template <int NT> __device__ __forceinline__ float block_jmax(float v, double* red) {
+template <int NT> __device__ __forceinline__ float block_jmax(float v, double* red, int& rp) {
+  double* r = red + (rp++ & 1) * (2 * (NT / 32));
   #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = jmax(v, __shfl_xor_sync(0xffffffffu, v, o));
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = (double)v;
+  if ((threadIdx.x & 31) == 0) r[threadIdx.x >> 5] = (double)v;
   __syncthreads();
   float tot = -J4B_INF;
   #pragma unroll
-  for (int w = 0; w < NT / 32; ++w) tot = jmax(tot, (float)red[w]);
-  __syncthreads();
+  for (int w = 0; w < NT / 32; ++w) tot = jmax(tot, (float)r[w]);
   return tot;
 }
-template <int NT, int MODE> __device__ __forceinline__ long long block_pair(float& v, long long i, double* red) {
+template <int NT, int MODE> __device__ __forceinline__ long long block_pair(float& v, long long i, double* red, int& rp) {
+  double* r = red + (rp++ & 1) * (2 * (NT / 32));
   #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     float v2 = __shfl_xor_sync(0xffffffffu, v, o);
@@ -1005,18 +1009,17 @@ template <int NT, int MODE> __device__ __forceinline__ long long block_pair(floa
     if (MODE == 0) amax_combine(v, i, v2, i2); else rmax_combine(v, i, v2, i2);
   }
   if ((threadIdx.x & 31) == 0) {
-    red[2 * (threadIdx.x >> 5)] = (double)v;
-    red[2 * (threadIdx.x >> 5) + 1] = (double)i;
+    r[2 * (threadIdx.x >> 5)] = (double)v;
+    r[2 * (threadIdx.x >> 5) + 1] = (double)i;
   }
   __syncthreads();
-  float bv = (float)red[0];
-  long long bi = (long long)red[1];
+  float bv = (float)r[0];
+  long long bi = (long long)r[1];
   #pragma unroll
   for (int w = 1; w < NT / 32; ++w) {
-    if (MODE == 0) amax_combine(bv, bi, (float)red[2 * w], (long long)red[2 * w + 1]);
-    else rmax_combine(bv, bi, (float)red[2 * w], (long long)red[2 * w + 1]);
+    if (MODE == 0) amax_combine(bv, bi, (float)r[2 * w], (long long)r[2 * w + 1]);
+    else rmax_combine(bv, bi, (float)r[2 * w], (long long)r[2 * w + 1]);
   }
-  __syncthreads();
   v = bv;
   return bi;
 }
@@ -1777,18 +1780,18 @@ struct Gen {
       if (c.op == T_SUMAX || c.op == T_RSUM) {
         // per-thread partial in float, combined across threads in double
         os << "  float " << vname(b) << ";\n  {\n  float acc = 0.0f;\n" << loop << "acc += " << val
-           << ";\n    }\n  }\n  " << vname(b) << " = (float)block_sum<" << NT << ">((double)acc, red);\n  }\n";
+           << ";\n    }\n  }\n  " << vname(b) << " = (float)block_sum<" << NT << ">((double)acc, red, rp);\n  }\n";
       } else if (c.op == T_MAXAX) {
         os << "  float " << vname(b) << ";\n  {\n  float acc = -J4B_INF;\n" << loop << "acc = jmax(acc, " << val
-           << ");\n    }\n  }\n  " << vname(b) << " = block_jmax<" << NT << ">(acc, red);\n  }\n";
+           << ");\n    }\n  }\n  " << vname(b) << " = block_jmax<" << NT << ">(acc, red, rp);\n  }\n";
       } else if (c.op == T_RMAX) {
         os << "  float " << vname(b) << ";\n  {\n  float bv = -J4B_INF; long long bi = 0x7fffffffffffffffLL;\n"
            << loop << "rmax_combine(bv, bi, " << val << ", j);\n    }\n  }\n"
-           << "  block_pair<" << NT << ", 1>(bv, bi, red);\n  " << vname(b) << " = bv;\n  }\n";
+           << "  block_pair<" << NT << ", 1>(bv, bi, red, rp);\n  " << vname(b) << " = bv;\n  }\n";
       } else {  // argmax
         os << "  float " << vname(b) << ";\n  {\n  float bv = -J4B_INF; long long bi = 0x7fffffffffffffffLL;\n"
            << loop << "amax_combine(bv, bi, " << val << ", j);\n    }\n  }\n"
-           << "  long long w = block_pair<" << NT << ", 0>(bv, bi, red);\n  " << vname(b)
+           << "  long long w = block_pair<" << NT << ", 0>(bv, bi, red, rp);\n  " << vname(b)
            << " = (float)(w == 0x7fffffffffffffffLL ? 0 : w);\n  }\n";
       }
       return;
@@ -1802,7 +1805,7 @@ struct Gen {
          << "    #pragma unroll\n    for (int q = 0; q < 4; ++q) {\n"
          << "      const long long j = ((long long)e * " << NT << " + t) * 4 + q;\n"
          << "      if (j < " << istr(Win) << ") amax_combine(bv, bi, " << val << ", j);\n    }\n  }\n"
-         << "  am" << b << " = block_pair<" << NT << ", 0>(bv, bi, red);\n"
+         << "  am" << b << " = block_pair<" << NT << ", 0>(bv, bi, red, rp);\n"
          << "  if (am" << b << " == 0x7fffffffffffffffLL) am" << b << " = 0;\n  }\n"
          << "  const float up" << b << " = " << up << ";\n"
          << "  float " << vname(b) << "[" << E(Win) * 4 << "];\n"
@@ -1944,8 +1947,9 @@ struct Gen {
         if (gc.ctx == X_SHARED) wmax = std::max(wmax, t.size[x]);
       }
     }
-    // about 16 elements of the widest row per thread (measured faster than 8 on the
-    // RMSNorm + SwiGLU gradient: fewer block-reduction partners, no register cap)
+    // about 16 elements of the widest row per thread. Measured on the RMSNorm + SwiGLU gradient
+    // (x [4096, 8192]): 16 per thread at 512 threads 76 us; 8 per thread at 1024 threads 87 us
+    // (64-register cap); two 512-thread CTAs per SM (64-register cap, spills) 116 us.
     NT = 32;
     while (NT < 1024 && (int64_t)NT * 16 < wmax) NT *= 2;
     row_loaded.assign(t.shape.size(), 0);
@@ -2035,11 +2039,11 @@ struct Gen {
       } else if (gc.kind == G_GLOBRED) {
         int slot = part_slot[b];
         if (c.op == T_RMAX)
-          fin << "  {\n    long long w = block_pair<" << NT << ", 1>(gm" << b << ", gi" << b << ", red);\n"
+          fin << "  {\n    long long w = block_pair<" << NT << ", 1>(gm" << b << ", gi" << b << ", red, rp);\n"
               << "    if (t == 0) { double* pp = (double*)A.p[" << slot << "]; pp[2 * blockIdx.x] = gm" << b
               << "; pp[2 * blockIdx.x + 1] = (double)w; }\n  }\n";
         else
-          fin << "  {\n    double s = block_sum<" << NT << ">(ga" << b << ", red);\n"
+          fin << "  {\n    double s = block_sum<" << NT << ">(ga" << b << ", red, rp);\n"
               << "    if (t == 0) ((double*)A.p[" << slot << "])[blockIdx.x] = s;\n  }\n";
       }
     }
@@ -2063,7 +2067,8 @@ struct Gen {
     src << "extern \"C\" __global__ void __launch_bounds__(" << NT << ") " << rn << "(const Args A) {\n"
         << "  extern __shared__ __align__(16) unsigned char smraw[];\n"
         << "  double* red = reinterpret_cast<double*>(smraw);\n"
-        << "  float* sm = reinterpret_cast<float*>(smraw + " << (2 * (NT / 32) * 8) << ");\n"
+        << "  int rp = 0;\n  (void)rp;\n"
+        << "  float* sm = reinterpret_cast<float*>(smraw + " << (4 * (NT / 32) * 8) << ");\n"
         << "  (void)red; (void)sm;\n"
         << "  const int t = threadIdx.x;\n"
         << "  const long long R = A.R;\n  (void)R;\n"
@@ -2090,7 +2095,7 @@ struct Gen {
     gcode.row_name = rn;
     gcode.fold_name = rn + "_fold";
     gcode.NT = NT;
-    gcode.smem = 2 * (NT / 32) * 8 + smem_floats * 4;
+    gcode.smem = 4 * (NT / 32) * 8 + smem_floats * 4;
     gcode.fold = has_fold;
     gcode.fold_len = flen;
     gcode.partials = partials;
