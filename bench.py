@@ -1020,6 +1020,8 @@ def run_engine_decoder(args):
                                 device_id=torch.device("cuda", local))
     be = B200Backend(local)
     batch, seq, label = DECODER_CONFIGS[args.config]
+    if args.batch:
+        batch, label = args.batch, label + f" (batch overridden to {args.batch})"
     decode = args.config == "decoder_decode"
     dev = torch.device("cuda", local)
     want_cpu = rank == 0 and world == 1 and not args.no_cpu_baseline
@@ -1381,6 +1383,8 @@ def main():
     p.add_argument("--config", choices=sorted(CONFIGS) + sorted(TAPE_CONFIGS) + sorted(GEMM_CONFIGS)
                    + sorted(DECODER_CONFIGS), default="q8_0_b8")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--batch", type=int, default=None,
+                   help="decoder workloads only: override the batch (e.g. a smaller case for profiling)")
     args = p.parse_args()
     family = ("tape" if args.config in TAPE_CONFIGS else "gemm" if args.config in GEMM_CONFIGS
               else args.config if args.config in DECODER_CONFIGS else "gemv")
