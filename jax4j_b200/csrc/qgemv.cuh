@@ -179,8 +179,9 @@ constexpr int kXBlocks = QT == J4B_Q2_0 ? 1 : 4;  // x block sums per warp chunk
 
 // One warp's contribution to one 16-row tile: its 128-column slice of the tile's chunk (quants at
 // sq, scales at sm) times the x fragments, accumulated into acc (C-fragment layout: rows g and
-// g+8, batch columns 2t and 2t+1 of each n-tile). hi and lo halves of x accumulate separately so
-// each dependent chain is two mma long.
+// g+8, batch columns 2t and 2t+1 of each n-tile). Per 32-column block, the hi and lo halves of x
+// run through one accumulator chain that starts with a zero-C mma (four mma deep, no zeroing and
+// no hi + lo add), and the block scale and the code-offset term are two fmas per output.
 template <int QT, int NT>
 __device__ __forceinline__ void tile_compute(const uint8_t* __restrict__ sq,
                                              const uint8_t* __restrict__ sm, int warp, int lane,  // warp = K chunk 0..7
@@ -189,32 +190,35 @@ __device__ __forceinline__ void tile_compute(const uint8_t* __restrict__ sq,
                                              const float (&xblk)[NT][kXBlocks<QT>][2],
                                              float (&acc)[NT][4]) {
   const int g = lane >> 2, t = lane & 3;
+  // c[n] = W_block . x over k-steps j0 and j0 + 1 (hi and lo), fresh chain per block
+  auto block_mma = [&](float (&c)[NT][4], const uint32_t (&a)[2][4], int j0) {
+#pragma unroll
+    for (int n = 0; n < NT; n++) {
+      mma16816_z(c[n], a[0][0], a[0][1], a[0][2], a[0][3], bh[n][j0][0], bh[n][j0][1]);
+      mma16816(c[n], a[0][0], a[0][1], a[0][2], a[0][3], bl[n][j0][0], bl[n][j0][1]);
+      mma16816(c[n], a[1][0], a[1][1], a[1][2], a[1][3], bh[n][j0 + 1][0], bh[n][j0 + 1][1]);
+      mma16816(c[n], a[1][0], a[1][1], a[1][2], a[1][3], bl[n][j0 + 1][0], bl[n][j0 + 1][1]);
+    }
+  };
   if constexpr (QT == J4B_Q8_0) {
 #pragma unroll
     for (int q = 0; q < 4; q++) {
       const uint4 line = *reinterpret_cast<const uint4*>(sq + (warp * 4 + q) * 512 + lane * 16);
       const uint32_t sc = *reinterpret_cast<const uint32_t*>(sm + (warp * 4 + q) * 32 + g * 4);
-      float th[NT][4] = {}, tl[NT][4] = {};
-      const uint32_t wv[4] = {line.x, line.y, line.z, line.w};
-#pragma unroll
-      for (int ks = 0; ks < 2; ks++) {
-        uint32_t a0, a1, a2, a3;
-        q8_pairs(wv[2 * ks], a0, a1);
-        q8_pairs(wv[2 * ks + 1], a2, a3);
-        const int j = 2 * q + ks;
-#pragma unroll
-        for (int n = 0; n < NT; n++) {
-          mma16816(th[n], a0, a1, a2, a3, bh[n][j][0], bh[n][j][1]);
-          mma16816(tl[n], a0, a1, a2, a3, bl[n][j][0], bl[n][j][1]);
-        }
-      }
+      uint32_t a[2][4];
+      q8_pairs(line.x, a[0][0], a[0][1]);
+      q8_pairs(line.y, a[0][2], a[0][3]);
+      q8_pairs(line.z, a[1][0], a[1][1]);
+      q8_pairs(line.w, a[1][2], a[1][3]);
+      float c[NT][4];
+      block_mma(c, a, 2 * q);
       const float2 d = __half22float2(*reinterpret_cast<const __half2*>(&sc));
 #pragma unroll
       for (int n = 0; n < NT; n++) {
-        acc[n][0] = fmaf(d.x, th[n][0] + tl[n][0], acc[n][0]);
-        acc[n][1] = fmaf(d.x, th[n][1] + tl[n][1], acc[n][1]);
-        acc[n][2] = fmaf(d.y, th[n][2] + tl[n][2], acc[n][2]);
-        acc[n][3] = fmaf(d.y, th[n][3] + tl[n][3], acc[n][3]);
+        acc[n][0] = fmaf(d.x, c[n][0], acc[n][0]);
+        acc[n][1] = fmaf(d.x, c[n][1], acc[n][1]);
+        acc[n][2] = fmaf(d.y, c[n][2], acc[n][2]);
+        acc[n][3] = fmaf(d.y, c[n][3], acc[n][3]);
       }
     }
   } else if constexpr (QT == J4B_Q4_0) {
@@ -224,46 +228,44 @@ __device__ __forceinline__ void tile_compute(const uint8_t* __restrict__ sq,
 #pragma unroll
     for (int q = 0; q < 4; q++) {
       const uint32_t sc = *reinterpret_cast<const uint32_t*>(sm + (warp * 4 + q) * 32 + g * 4);
-      float th[NT][4] = {}, tl[NT][4] = {};
-#pragma unroll
-      for (int ks = 0; ks < 2; ks++) {
-        uint32_t av[4];
-        q4_pairs(wv[2 * q + ks], av);
-        const int j = 2 * q + ks;
-#pragma unroll
-        for (int n = 0; n < NT; n++) {
-          mma16816(th[n], av[0], av[1], av[2], av[3], bh[n][j][0], bh[n][j][1]);
-          mma16816(tl[n], av[0], av[1], av[2], av[3], bl[n][j][0], bl[n][j][1]);
-        }
-      }
+      uint32_t a[2][4];
+      q4_pairs(wv[2 * q], a[0]);
+      q4_pairs(wv[2 * q + 1], a[1]);
+      float c[NT][4];
+      block_mma(c, a, 2 * q);
       // sum w x = d (16 C' - 24 X), C' = sum (1 + q/16) x
       const float2 d = __half22float2(*reinterpret_cast<const __half2*>(&sc));
       const float c0 = 16.f * d.x, c1 = 16.f * d.y, x0 = -24.f * d.x, x1 = -24.f * d.y;
 #pragma unroll
       for (int n = 0; n < NT; n++) {
-        acc[n][0] += fmaf(c0, th[n][0] + tl[n][0], x0 * xblk[n][q][0]);
-        acc[n][1] += fmaf(c0, th[n][1] + tl[n][1], x0 * xblk[n][q][1]);
-        acc[n][2] += fmaf(c1, th[n][2] + tl[n][2], x1 * xblk[n][q][0]);
-        acc[n][3] += fmaf(c1, th[n][3] + tl[n][3], x1 * xblk[n][q][1]);
+        acc[n][0] = fmaf(x0, xblk[n][q][0], fmaf(c0, c[n][0], acc[n][0]));
+        acc[n][1] = fmaf(x0, xblk[n][q][1], fmaf(c0, c[n][1], acc[n][1]));
+        acc[n][2] = fmaf(x1, xblk[n][q][0], fmaf(c1, c[n][2], acc[n][2]));
+        acc[n][3] = fmaf(x1, xblk[n][q][1], fmaf(c1, c[n][3], acc[n][3]));
       }
     }
   } else if constexpr (QT == J4B_Q2_0) {
     const uint4 line = *reinterpret_cast<const uint4*>(sq + warp * 512 + lane * 16);
     const uint32_t sc = *reinterpret_cast<const uint32_t*>(sm + warp * 32 + g * 4);
     const uint32_t wv[4] = {line.x, line.y, line.z, line.w};
-    float th[NT][4] = {}, tl[NT][4] = {};
+    float c[NT][4];
 #pragma unroll
     for (int q = 0; q < 4; q++) {
+      uint32_t a[2][4];
 #pragma unroll
-      for (int ks = 0; ks < 2; ks++) {
-        const uint32_t a0 = q2_pair(wv[q], 4 * ks), a1 = q2_pair(wv[q], 4 * ks + 1);
-        const uint32_t a2 = q2_pair(wv[q], 4 * ks + 2), a3 = q2_pair(wv[q], 4 * ks + 3);
-        const int j = 2 * q + ks;
+      for (int ks = 0; ks < 2; ks++)
 #pragma unroll
-        for (int n = 0; n < NT; n++) {
-          mma16816(th[n], a0, a1, a2, a3, bh[n][j][0], bh[n][j][1]);
-          mma16816(tl[n], a0, a1, a2, a3, bl[n][j][0], bl[n][j][1]);
-        }
+        for (int p = 0; p < 4; p++) a[ks][p] = q2_pair(wv[q], 4 * ks + p);
+      if (q == 0) {
+        block_mma(c, a, 0);
+      } else {
+#pragma unroll
+        for (int n = 0; n < NT; n++)
+#pragma unroll
+          for (int ks = 0; ks < 2; ks++) {
+            mma16816(c[n], a[ks][0], a[ks][1], a[ks][2], a[ks][3], bh[n][2 * q + ks][0], bh[n][2 * q + ks][1]);
+            mma16816(c[n], a[ks][0], a[ks][1], a[ks][2], a[ks][3], bl[n][2 * q + ks][0], bl[n][2 * q + ks][1]);
+          }
       }
     }
     // sum w x = d (4 C' - 5 X), C' = sum (1 + c/4) x
@@ -271,10 +273,10 @@ __device__ __forceinline__ void tile_compute(const uint8_t* __restrict__ sq,
     const float c0 = 4.f * d.x, c1 = 4.f * d.y, x0 = -5.f * d.x, x1 = -5.f * d.y;
 #pragma unroll
     for (int n = 0; n < NT; n++) {
-      acc[n][0] += fmaf(c0, th[n][0] + tl[n][0], x0 * xblk[n][0][0]);
-      acc[n][1] += fmaf(c0, th[n][1] + tl[n][1], x0 * xblk[n][0][1]);
-      acc[n][2] += fmaf(c1, th[n][2] + tl[n][2], x1 * xblk[n][0][0]);
-      acc[n][3] += fmaf(c1, th[n][3] + tl[n][3], x1 * xblk[n][0][1]);
+      acc[n][0] = fmaf(x0, xblk[n][0][0], fmaf(c0, c[n][0], acc[n][0]));
+      acc[n][1] = fmaf(x0, xblk[n][0][1], fmaf(c0, c[n][1], acc[n][1]));
+      acc[n][2] = fmaf(x1, xblk[n][0][0], fmaf(c1, c[n][2], acc[n][2]));
+      acc[n][3] = fmaf(x1, xblk[n][0][1], fmaf(c1, c[n][3], acc[n][3]));
     }
   } else {  // Q4_K: warp w holds half (w & 1) of super-block w / 2 of the CTA's K range
     const int h = warp & 1;
@@ -308,18 +310,11 @@ __device__ __forceinline__ void tile_compute(const uint8_t* __restrict__ sq,
     const uint32_t wv[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
 #pragma unroll
     for (int q = 0; q < 4; q++) {
-      float th[NT][4] = {}, tl[NT][4] = {};
-#pragma unroll
-      for (int ks = 0; ks < 2; ks++) {
-        uint32_t av[4];
-        q4_pairs(wv[2 * q + ks], av);
-        const int j = 2 * q + ks;
-#pragma unroll
-        for (int n = 0; n < NT; n++) {
-          mma16816(th[n], av[0], av[1], av[2], av[3], bh[n][j][0], bh[n][j][1]);
-          mma16816(tl[n], av[0], av[1], av[2], av[3], bl[n][j][0], bl[n][j][1]);
-        }
-      }
+      uint32_t a[2][4];
+      q4_pairs(wv[2 * q], a[0]);
+      q4_pairs(wv[2 * q + 1], a[1]);
+      float c[NT][4];
+      block_mma(c, a, 2 * q);
       const int src = (lane & ~3) | q;
       const float s0 = __shfl_sync(0xffffffffu, cs[0], src);
       const float s1 = __shfl_sync(0xffffffffu, cs[1], src);
@@ -327,10 +322,10 @@ __device__ __forceinline__ void tile_compute(const uint8_t* __restrict__ sq,
       const float z1 = __shfl_sync(0xffffffffu, cx[1], src);
 #pragma unroll
       for (int n = 0; n < NT; n++) {
-        acc[n][0] += fmaf(s0, th[n][0] + tl[n][0], z0 * xblk[n][q][0]);
-        acc[n][1] += fmaf(s0, th[n][1] + tl[n][1], z0 * xblk[n][q][1]);
-        acc[n][2] += fmaf(s1, th[n][2] + tl[n][2], z1 * xblk[n][q][0]);
-        acc[n][3] += fmaf(s1, th[n][3] + tl[n][3], z1 * xblk[n][q][1]);
+        acc[n][0] = fmaf(z0, xblk[n][q][0], fmaf(s0, c[n][0], acc[n][0]));
+        acc[n][1] = fmaf(z0, xblk[n][q][1], fmaf(s0, c[n][1], acc[n][1]));
+        acc[n][2] = fmaf(z1, xblk[n][q][0], fmaf(s1, c[n][2], acc[n][2]));
+        acc[n][3] = fmaf(z1, xblk[n][q][1], fmaf(s1, c[n][3], acc[n][3]));
       }
     }
   }
