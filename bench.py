@@ -1025,18 +1025,22 @@ def run_engine_decoder(args):
     decode = args.config == "decoder_decode"
     dev = torch.device("cuda", local)
     want_cpu = rank == 0 and world == 1 and not args.no_cpu_baseline
-    w = DecoderWeights.random(be, DEC_D, DEC_HEADS, DEC_FFN, PrngKey.of(1), keep_blobs=want_cpu)
+    # world > 1: tensor parallel, rank r holds heads and FFN rows [r/n, (r+1)/n) (strong scaling)
+    w = DecoderWeights.random(be, DEC_D, DEC_HEADS, DEC_FFN, PrngKey.of(1), keep_blobs=want_cpu,
+                              world=world, rank=rank)
     block = DecoderBlock(be, w)
     kx, kc = PrngKey.of(0).split(2)
-    cache = KVCache(be, batch, DEC_HEADS, seq)
+    hl = w.heads
+    cache = KVCache(be, batch, hl, seq)
     if decode:
         tokens = batch
-        # cached keys/values of slots 0 .. seq - 2 ~ N(0, 1), drawn per sequence by the engine's PRNG
+        # cached keys/values of slots 0 .. seq - 2 ~ N(0, 1), drawn per sequence by the engine's
+        # PRNG over all heads (so every world size sees the same cache), this rank's heads kept
         per = DEC_HEADS * seq * HEAD_DIM
         for b in range(batch):
             for dst in (cache.k, cache.v):
                 r = be.random_normal(kc.seed, kc.counter + (2 * b + (dst is cache.v)) * per, (DEC_HEADS, seq, HEAD_DIM))
-                dst[b] = r.tensor.view(DEC_HEADS, seq, HEAD_DIM).half()
+                dst[b] = r.tensor.view(DEC_HEADS, seq, HEAD_DIM)[rank * hl:(rank + 1) * hl].half()
         cache.k[:, :, seq - 1:] = 0
         cache.v[:, :, seq - 1:] = 0
         pos = seq - 1
@@ -1060,7 +1064,7 @@ def run_engine_decoder(args):
         step()
     barrier()
     graph = None
-    if decode:
+    if decode and world == 1:
         # decode steps replay from a CUDA graph (no host work between the ~12 launches of a step)
         side = torch.cuda.Stream()
         side.wait_stream(torch.cuda.current_stream())
@@ -1103,24 +1107,24 @@ def run_engine_decoder(args):
         reps = 20
         for _ in range(3):
             _lib.call("j4b_attention_decode", q.data_ptr(), cache.k.data_ptr(), cache.v.data_ptr(), batch,
-                      DEC_HEADS, HEAD_DIM, seq, seq, att.data_ptr(), s)
+                      hl, HEAD_DIM, seq, seq, att.data_ptr(), s)
         torch.cuda.synchronize()
         k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         k0.record()
         for _ in range(reps):
             _lib.call("j4b_attention_decode", q.data_ptr(), cache.k.data_ptr(), cache.v.data_ptr(), batch,
-                      DEC_HEADS, HEAD_DIM, seq, seq, att.data_ptr(), s)
+                      hl, HEAD_DIM, seq, seq, att.data_ptr(), s)
         k1.record()
         torch.cuda.synchronize()
         kern_us = k0.elapsed_time(k1) * 1e3 / reps
-        kv = decoder_kv_bytes(batch, seq) + 2 * batch * DEC_D * 4
+        kv = decoder_kv_bytes(batch, seq) // world + 2 * batch * hl * HEAD_DIM * 4
         peak = float(pk.get("hbm_gbs", 6650.0))
         roof = {"bound": "hbm", "achieved": round(kv / (kern_us * 1e-6) / 1e9, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(kv / (kern_us * 1e-6) / 1e9 / peak, 4), "traffic": None,
                 "peak_source": "measured MEASURED_PEAKS.json hbm_gbs" if pk else "fallback",
-                "kernel": "attn_decode_kernel (KV cache read, 2,147,483,648 B + q/out per launch)",
+                "kernel": f"attn_decode_kernel ({batch} x {hl} heads x {seq} cached tokens of f16 K and V per launch)",
                 "kernel_avg_us": round(kern_us, 1)}
-        value = world * step_bytes / (step_ms * 1e-3) / 1e9
+        value = step_bytes / (step_ms * 1e-3) / 1e9  # the whole block's bytes: strong scaling
         unit = "GB/s"
     else:
         peak = float(pk.get("bf16_tflops_sustained", 1400.0))
@@ -1130,7 +1134,7 @@ def run_engine_decoder(args):
                 "peak_source": "measured MEASURED_PEAKS.json bf16_tflops_sustained" if pk else "fallback 1.4 PFLOP/s",
                 "kernel": "the whole prefill step (tc_gemm_kernel projections hold ~97% of its flops)",
                 "kernel_avg_us": round(step_ms * 1e3, 1)}
-        value = world * flops / (step_ms * 1e-3) / 1e12
+        value = flops / (step_ms * 1e-3) / 1e12
         unit = "TFLOP/s"
 
     # end to end through the public API: x from pinned host memory, the block output back
@@ -1147,7 +1151,7 @@ def run_engine_decoder(args):
     e1.record()
     barrier()
     e_s = e0.elapsed_time(e1) * 1e-3
-    e2e = world * (step_bytes / 1e9 if decode else flops / 1e12) * e_steps / e_s
+    e2e = (step_bytes / 1e9 if decode else flops / 1e12) * e_steps / e_s
 
     cpu = None
     if want_cpu:
@@ -1158,18 +1162,20 @@ def run_engine_decoder(args):
     if rank == 0:
         cfg = {"workload": label, "batch": batch, "seq" if not decode else "cached_tokens": seq, "d_model": DEC_D,
                "heads": DEC_HEADS, "head_dim": HEAD_DIM, "ffn": DEC_FFN, "quant": "Q4_0",
-               "parallelism": "replica" if world == 1 else f"{world} independent replicas",
+               "parallelism": "single GPU" if world == 1 else
+               f"tensor parallel tp{world}: heads and FFN rows sharded, 2 NCCL all-reduces of [tokens, d] per step",
                "l2": "weights 137 MB and KV cache 2.1 GB exceed L2" if decode else "activations exceed L2"}
         if decode:
             cfg["tokens_per_s"] = round(world * batch / (step_ms * 1e-3), 1)
             cfg["bytes_per_step"] = step_bytes
-            cfg["timing"] = "CUDA graph of K decode steps, CUDA events"
+            cfg["timing"] = ("CUDA graph of K decode steps, CUDA events" if world == 1 else
+                             "K eager decode steps (NCCL all-reduces between), CUDA events, max over ranks")
         else:
             cfg["flop_per_step"] = flops
             cfg["timing"] = "K back-to-back prefill steps, CUDA events"
         line = {
             "metric": METRIC, "value": round(value, 3), "unit": unit, "n_gpus": world, "steps": K, "warmup": W,
-            "ms_per_step": round(step_ms, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "ms_per_step": round(step_ms, 4), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "f32 (Q4_0 weights, f16 KV)" if decode else "bf16 (Q4_0 weights, f16 attention)",
             "data": "synthetic", "config": cfg, "roofline": roof, "cpu_baseline": cpu,
             "e2e": {"value": round(e2e, 3), "unit": unit, "h2d_bytes_per_step": tokens * DEC_D * 4,

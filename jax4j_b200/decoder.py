@@ -9,6 +9,15 @@ Wqkv [3d, d] holds the q, k and v rows, Wgu [2F, d] the gate and up rows, Wo [d,
 all are GGUF Q4_0 blobs quantised along the input dimension, so q/k/v and gate/up each come out
 of one projection. Attention has `heads` heads of 128 dims and a per-sequence f16 KV cache.
 
+Tensor parallel over `world` GPUs (one process each): rank r holds heads [r H/n, (r+1) H/n) --
+their q, k, v rows of Wqkv, their KV cache and attention -- the matching input columns of Wo,
+FFN rows [r F/n, (r+1) F/n) of the gate and up halves of Wgu and the matching input columns of
+Wd. Each half-block then ends in one sum over ranks (torch.distributed all-reduce over NCCL)
+of a [tokens, d] partial; rank 0's partial carries the residual (the GEMV's `add`). The shards
+are slices of the unsharded matrices, quantised along K in 32-column blocks that never straddle
+a shard boundary, so the sharded weights are bit-identical to the corresponding parts of the
+single-GPU block.
+
 Decode (one new token per sequence) runs the projections as batched dequant-GEMVs
 (j4b_quant_matvec, with the residual fused as its `add`); prefill runs them as dequant-GEMMs on
 the tcgen05 tensor cores (j4b_quant_gemm) and attention as the causal flash kernel.
@@ -32,11 +41,29 @@ Q4_0 = 2
 HEAD_DIM = 128
 
 
+def shard_ranges(d_model: int, heads: int, ffn: int, world: int, rank: int) -> dict:
+    """Rows / columns of each unsharded matrix that rank `rank` of `world` holds (half-open
+    ranges). Requires heads and ffn / 32 divisible by world."""
+    if heads % world or ffn % (32 * world):
+        raise ValueError(f"heads {heads} and ffn {ffn} must split evenly in 32-column blocks over {world} ranks")
+    hd, fr = heads // world * HEAD_DIM, ffn // world
+    d = d_model
+    q = (rank * hd, (rank + 1) * hd)
+    return {
+        "wqkv_rows": [q, (d + q[0], d + q[1]), (2 * d + q[0], 2 * d + q[1])],
+        "wo_cols": q,
+        "wgu_rows": [(rank * fr, (rank + 1) * fr), (ffn + rank * fr, ffn + (rank + 1) * fr)],
+        "wd_cols": (rank * fr, (rank + 1) * fr),
+        "heads": heads // world,
+        "ffn": fr,
+    }
+
+
 @dataclass
 class DecoderWeights:
     d_model: int
-    heads: int
-    ffn: int
+    heads: int  # heads held here (all heads when world == 1)
+    ffn: int    # FFN width held here
     wqkv: QuantBuffer
     wo: QuantBuffer
     wgu: QuantBuffer
@@ -44,14 +71,19 @@ class DecoderWeights:
     g_attn: DeviceBuffer
     g_ffn: DeviceBuffer
     blobs: dict  # name -> CUDA uint8 GGUF blob (kept for parity checks)
+    world: int = 1
+    rank: int = 0
 
     @staticmethod
     def random(backend: B200Backend, d_model: int = 4096, heads: int = 32, ffn: int = 14336,
-               key: PrngKey | None = None, keep_blobs: bool = False) -> "DecoderWeights":
+               key: PrngKey | None = None, keep_blobs: bool = False, world: int = 1,
+               rank: int = 0) -> "DecoderWeights":
         """Weights drawn 0.02 N(0, 1) by the engine's counter PRNG and quantised Q4_0 on the
-        device; gains g = 1 + 0.1 N(0, 1). Key splits: 0 Wqkv, 1 Wo, 2 Wgu, 3 Wd, 4 g_attn, 5 g_ffn."""
+        device; gains g = 1 + 0.1 N(0, 1). Key splits: 0 Wqkv, 1 Wo, 2 Wgu, 3 Wd, 4 g_attn, 5 g_ffn.
+        With world > 1, every rank draws the same unsharded matrices and keeps its shard."""
         if d_model != heads * HEAD_DIM:
             raise ValueError(f"d_model {d_model} must equal heads * {HEAD_DIM}")
+        sh = shard_ranges(d_model, heads, ffn, world, rank)
         keys = (key or PrngKey.of(1)).split(6)
         shapes = {"wqkv": (3 * d_model, d_model), "wo": (d_model, d_model),
                   "wgu": (2 * ffn, d_model), "wd": (d_model, ffn)}
@@ -59,6 +91,16 @@ class DecoderWeights:
         for i, (name, (rows, cols)) in enumerate(shapes.items()):
             w = backend.random_normal(keys[i].seed, keys[i].counter, (rows, cols))
             w = backend.scalar("MUL", w, 0.02)
+            if world > 1:
+                full = w.tensor.view(rows, cols)
+                if name in ("wqkv", "wgu"):
+                    part = torch.cat([full[a:b] for a, b in sh[name + "_rows"]])
+                else:
+                    a, b = sh[name + "_cols"]
+                    part = full[:, a:b].contiguous()
+                del full
+                w = backend.wrap(part)
+                rows, cols = part.shape
             blob = backend.quantize(w, Q4_0)
             del w
             quant[name] = backend.upload_quantized(blob, Q4_0, (rows, cols))
@@ -68,8 +110,8 @@ class DecoderWeights:
         for k in keys[4:6]:
             g = backend.random_normal(k.seed, k.counter, (d_model,))
             gains.append(backend.scalar("ADD", backend.scalar("MUL", g, 0.1), 1.0))
-        return DecoderWeights(d_model, heads, ffn, quant["wqkv"], quant["wo"], quant["wgu"],
-                              quant["wd"], gains[0], gains[1], blobs)
+        return DecoderWeights(d_model, sh["heads"], sh["ffn"], quant["wqkv"], quant["wo"], quant["wgu"],
+                              quant["wd"], gains[0], gains[1], blobs, world, rank)
 
 
 class KVCache:
@@ -84,8 +126,23 @@ class KVCache:
 
 class DecoderBlock:
     def __init__(self, backend: B200Backend, weights: DecoderWeights, eps: float = 1e-5,
-                 theta: float = 10000.0):
-        self.be, self.w, self.eps, self.theta = backend, weights, eps, theta
+                 theta: float = 10000.0, group=None):
+        """`group`: the torch.distributed process group of the ranks sharing the block (default:
+        the world group) when the weights are sharded."""
+        self.be, self.w, self.eps, self.theta, self.group = backend, weights, eps, theta, group
+
+    def _sum_ranks(self, partial: DeviceBuffer) -> DeviceBuffer:
+        if self.w.world > 1:
+            import torch.distributed as dist
+            dist.all_reduce(partial.tensor, group=self.group)
+        return partial
+
+    def _residual(self, x: DeviceBuffer):
+        """Rank 0's partial carries the residual, so the sum over ranks adds it once."""
+        return x if self.w.rank == 0 else None
+
+    def _add_residual(self, partial: DeviceBuffer, x: DeviceBuffer) -> DeviceBuffer:
+        return self.be.binary("ADD", partial, x) if self.w.rank == 0 else partial
 
     def _buf(self, shape) -> DeviceBuffer:
         return self.be._new(shape)
@@ -117,12 +174,12 @@ class DecoderBlock:
             raise ValueError("KV cache does not match the batch or the head count")
         qkv = be.quant_matvec(w.wqkv, self.rmsnorm(x, w.g_attn))
         q = self.rope_kv(qkv, cache, batch, 1, pos)
-        attn = self._buf((batch, w.d_model))
+        attn = self._buf((batch, w.heads * HEAD_DIM))
         call("j4b_attention_decode", q.ptr, cache.k.data_ptr(), cache.v.data_ptr(), batch, w.heads,
              HEAD_DIM, cache.capacity, pos + 1, attn.ptr, be.stream)
-        h = be.quant_matvec_add(w.wo, attn, x)
+        h = self._sum_ranks(be.quant_matvec(w.wo, attn, self._residual(x)))
         gu = be.quant_matvec(w.wgu, self.rmsnorm(h, w.g_ffn))
-        return be.quant_matvec_add(w.wd, self.swiglu(gu), h)
+        return self._sum_ranks(be.quant_matvec(w.wd, self.swiglu(gu), self._residual(h)))
 
     def prefill(self, x: DeviceBuffer, cache: KVCache, seq: int, precision: int = 1) -> DeviceBuffer:
         """seq tokens per sequence at positions 0 .. seq - 1: x [batch * seq, d] -> same shape;
@@ -135,9 +192,9 @@ class DecoderBlock:
         qkv = be.quant_gemm(w.wqkv, self.rmsnorm(x, w.g_attn), precision)
         q = self.rope_kv(qkv, cache, batch, seq, 0)
         del qkv
-        attn = self._buf((tokens, w.d_model))
+        attn = self._buf((tokens, w.heads * HEAD_DIM))
         call("j4b_attention_prefill", q.ptr, cache.k.data_ptr(), cache.v.data_ptr(), batch, w.heads,
              HEAD_DIM, cache.capacity, seq, attn.ptr, be.stream)
-        h = be.binary("ADD", be.quant_gemm(w.wo, attn, precision), x)
+        h = self._sum_ranks(self._add_residual(be.quant_gemm(w.wo, attn, precision), x))
         gu = be.quant_gemm(w.wgu, self.rmsnorm(h, w.g_ffn), precision)
-        return be.binary("ADD", be.quant_gemm(w.wd, self.swiglu(gu), precision), h)
+        return self._sum_ranks(self._add_residual(be.quant_gemm(w.wd, self.swiglu(gu), precision), h))
