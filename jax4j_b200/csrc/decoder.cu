@@ -115,11 +115,17 @@ __device__ __forceinline__ void h8_to_f(const uint4& u, float (&f)[8]) {
   }
 }
 
+// With gridDim.y > 1 the token range is split: CTA (bh, s) covers tokens [s chunk, (s+1) chunk)
+// and writes its unnormalised state (max, sum, 128 output dims) to part[(bh * splits + s) * 130]
+// for attn_combine_kernel; with one split it writes the normalised output.
 __global__ void __launch_bounds__(kDecWarps * 32) attn_decode_kernel(const float* __restrict__ q, const __half* __restrict__ kc,
                                                                     const __half* __restrict__ vc, int heads,
-                                                                    int64_t capacity, int64_t len, float scale_log2,
-                                                                    float* __restrict__ out) {
+                                                                    int64_t capacity, int64_t len, int64_t chunk,
+                                                                    float scale_log2, float* __restrict__ out,
+                                                                    float* __restrict__ part) {
   const int bh = blockIdx.x;  // b * heads + h
+  const int64_t t_begin = (int64_t)blockIdx.y * chunk;
+  const int64_t t_end = min(len, t_begin + chunk);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int half = lane >> 4, sub = lane & 15;
   const float* qp = q + (int64_t)bh * kHeadDim + sub * 8;
@@ -129,18 +135,19 @@ __global__ void __launch_bounds__(kDecWarps * 32) attn_decode_kernel(const float
     qv[0] = a.x * scale_log2; qv[1] = a.y * scale_log2; qv[2] = a.z * scale_log2; qv[3] = a.w * scale_log2;
     qv[4] = b.x * scale_log2; qv[5] = b.y * scale_log2; qv[6] = b.z * scale_log2; qv[7] = b.w * scale_log2;
   }
-  const __half* kb = kc + (int64_t)bh * capacity * kHeadDim + sub * 8;
-  const __half* vb = vc + (int64_t)bh * capacity * kHeadDim + sub * 8;
+  const __half* kb = kc + ((int64_t)bh * capacity + t_begin) * kHeadDim + sub * 8;
+  const __half* vb = vc + ((int64_t)bh * capacity + t_begin) * kHeadDim + sub * 8;
+  const int64_t n_tok = t_end - t_begin;
   float m = -INFINITY, l = 0.f, acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   // token of (step, u) for this half-warp: ((step * kDecUnroll + u) * kDecWarps + warp) * 2 + half
   const int64_t per_step = (int64_t)kDecUnroll * kDecWarps * 2;
-  for (int64_t base = 0; base < len; base += per_step) {
+  for (int64_t base = 0; base < n_tok; base += per_step) {
     uint4 kr[kDecUnroll], vr[kDecUnroll];
     bool ok[kDecUnroll];
 #pragma unroll
     for (int u = 0; u < kDecUnroll; ++u) {
       const int64_t tk = base + ((int64_t)u * kDecWarps + warp) * 2 + half;
-      ok[u] = tk < len;
+      ok[u] = tk < n_tok;
       const int64_t off = (ok[u] ? tk : 0) * kHeadDim;
       kr[u] = __ldg(reinterpret_cast<const uint4*>(kb + off));
       vr[u] = __ldg(reinterpret_cast<const uint4*>(vb + off));
@@ -199,7 +206,33 @@ __global__ void __launch_bounds__(kDecWarps * 32) attn_decode_kernel(const float
     lt = fmaf(sm_l[w], f, lt);
     ot = fmaf(sm_acc[w][d], f, ot);
   }
-  // out is token-major [batch, heads * head_dim]: (b, h) maps to row b, column block h
+  if (gridDim.y == 1) {
+    // out is token-major [batch, heads * head_dim]: (b, h) maps to row b, column block h
+    out[(int64_t)bh * kHeadDim + d] = ot / lt;
+  } else {
+    float* p = part + ((int64_t)bh * gridDim.y + blockIdx.y) * (kHeadDim + 2);
+    p[2 + d] = ot;
+    if (d == 0) {
+      p[0] = mt;
+      p[1] = lt;
+    }
+  }
+}
+
+// Merges the split states of one (sequence, head) in split order.
+__global__ void __launch_bounds__(kHeadDim) attn_combine_kernel(const float* __restrict__ part, int splits,
+                                                              float* __restrict__ out) {
+  const int bh = blockIdx.x, d = threadIdx.x;
+  const float* p = part + (int64_t)bh * splits * (kHeadDim + 2);
+  float mt = -INFINITY;
+  for (int s = 0; s < splits; ++s) mt = fmaxf(mt, p[s * (kHeadDim + 2)]);
+  float lt = 0.f, ot = 0.f;
+  for (int s = 0; s < splits; ++s) {
+    const float* ps = p + s * (kHeadDim + 2);
+    const float f = exp2f(ps[0] - mt);
+    lt = fmaf(ps[1], f, lt);
+    ot = fmaf(ps[2 + d], f, ot);
+  }
   out[(int64_t)bh * kHeadDim + d] = ot / lt;
 }
 
@@ -481,10 +514,34 @@ extern "C" int j4b_attention_decode(j4b_buf q, j4b_buf k_cache, j4b_buf v_cache,
               "attention needs 16-byte aligned buffers");
   J4B_DEV_OF(out);
   const float scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)kHeadDim));
-  attn_decode_kernel<<<(unsigned)(batch * heads), kDecWarps * 32, 0, stream>>>(
+  // One CTA per (sequence, head) streams the cache at full bandwidth once there are enough of
+  // them (batch 64 x 32 heads: ~14 per SM); fewer are split along the tokens (at least 256 per
+  // split) to about 16 CTAs per SM, and their states merged by a second kernel.
+  const int64_t pairs = batch * heads;
+  const int sms = device_ctx(dev) ? device_ctx(dev)->sm_count : 148;
+  int64_t splits = 1;
+  if (pairs < 8LL * sms) {
+    splits = std::min<int64_t>((16LL * sms + pairs - 1) / pairs, (length + 255) / 256);
+    splits = std::max<int64_t>(1, std::min<int64_t>(splits, 64));
+  }
+  const int64_t chunk = (length + splits - 1) / splits;
+  splits = (length + chunk - 1) / chunk;  // every split holds at least one token
+  float* part = nullptr;
+  if (splits > 1)
+    J4B_CUDA(cudaMallocAsync((void**)&part, (size_t)(pairs * splits * (kHeadDim + 2)) * sizeof(float), stream),
+             "cudaMallocAsync(attention split state)");
+  attn_decode_kernel<<<dim3((unsigned)pairs, (unsigned)splits), kDecWarps * 32, 0, stream>>>(
       (const float*)(uintptr_t)q, (const __half*)(uintptr_t)k_cache, (const __half*)(uintptr_t)v_cache, (int)heads,
-      capacity, length, scale_log2, (float*)(uintptr_t)out);
-  J4B_CHECK_LAUNCH("attn_decode_kernel");
+      capacity, length, chunk, scale_log2, (float*)(uintptr_t)out, part);
+  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess && splits > 1) {
+    count_launch();
+    attn_combine_kernel<<<(unsigned)pairs, kHeadDim, 0, stream>>>(part, (int)splits, (float*)(uintptr_t)out);
+    e = cudaGetLastError();
+  }
+  if (part) cudaFreeAsync(part, stream);
+  if (e != cudaSuccess) return cuda_error(e, "attn_decode_kernel");
+  count_launch();
   return J4B_OK;
 }
 

@@ -67,11 +67,14 @@ def test_rope_writes_rotated_queries_and_f16_cache_slots():
     assert not kc[:, :, :pos0].any() and not kc[:, :, pos0 + seq:].any()
 
 
-@pytest.mark.parametrize("length", [1, 7, 33, 100, 128])
-def test_attention_decode_matches_float64(length):
+@pytest.mark.parametrize("length,cap", [(1, 128), (7, 128), (33, 128), (100, 128), (128, 128),
+                                        (300, 320), (1000, 1024), (2048, 2048)])
+def test_attention_decode_matches_float64(length, cap):
+    """Short ranges run one CTA per (sequence, head); long ones on few pairs are split along the
+    tokens and merged by the combine kernel (2 to 8 splits here)."""
     from oracle.decoder import attention
     rng = np.random.default_rng(length)
-    batch, heads, cap = 3, 2, 128
+    batch, heads = 3, 2
     q = rng.standard_normal((batch, heads, D)).astype(np.float32)
     k = rng.standard_normal((batch, heads, cap, D)).astype(np.float16)
     v = rng.standard_normal((batch, heads, cap, D)).astype(np.float16)
