@@ -35,6 +35,7 @@ namespace j4b {
 namespace {
 
 constexpr int kBM = 128, kBK = 64;
+constexpr int kGroupM = 16;  // row tiles per rasterisation group
 constexpr int kTcThreads = 192;
 constexpr int kTileBytes = kBM * kBK * 2;  // one 128 x 64 bf16 tile
 
@@ -123,7 +124,21 @@ __global__ void __launch_bounds__(kTcThreads, TERMS == 1 ? 2 : 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.y * kBM, n0 = blockIdx.x * kBN;
+  // Grouped rasterisation of the 1-D grid: tiles are taken in groups of kGroupM row tiles with the
+  // row index fastest, so the CTAs resident at one time share a few A row panels and about
+  // (resident / kGroupM) B column panels, which stay in L2 (row-major order would sweep all of
+  // B's panels at once).
+  int m_tile, n_tile;
+  {
+    const int mt = (p.M + kBM - 1) / kBM;
+    const int nt = (p.N + kBN - 1) / kBN;
+    const int per_group = kGroupM * nt;
+    const int grp = (int)blockIdx.x / per_group, idx = (int)blockIdx.x % per_group;
+    const int gm = min(kGroupM, mt - grp * kGroupM);
+    m_tile = grp * kGroupM + idx % gm;
+    n_tile = idx / gm;
+  }
+  const int m0 = m_tile * kBM, n0 = n_tile * kBN;
   const int nk = p.Kp / kBK;
 
   if (threadIdx.x == 0) {
@@ -322,8 +337,9 @@ cudaError_t launch_tc(const CUtensorMap& ah, const CUtensorMap& al, const CUtens
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  dim3 grid((unsigned)((a.N + kBN - 1) / kBN), (unsigned)((a.M + kBM - 1) / kBM));
-  tc_gemm_kernel<TERMS><<<grid, kTcThreads, smem, stream>>>(ah, al, bh, bl, a);
+  const int64_t tiles = (int64_t)((a.N + kBN - 1) / kBN) * ((a.M + kBM - 1) / kBM);
+  if (tiles > 0x7fffffffLL) return cudaErrorInvalidValue;
+  tc_gemm_kernel<TERMS><<<(unsigned)tiles, kTcThreads, smem, stream>>>(ah, al, bh, bl, a);
   return cudaGetLastError();
 }
 

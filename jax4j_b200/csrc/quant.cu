@@ -293,9 +293,50 @@ __global__ void gather_row_kernel(Layout L, const uint8_t* __restrict__ data, in
   out[k] = v;
 }
 
-// Whole matrix to bf16 hi (and lo) [rows, kp], the K-major operand of the tensor-core GEMM;
+// Prefill operands: W decoded to bf16 hi (and lo = residual, for the 3-term mode) K-major [rows, kp];
 // each value is first decoded bit-exactly as by gather_row_kernel. One thread per (row, 32-column
-// group): the group's scale once, 32 codes, four 16-byte stores. Columns past `cols` are zeros.
+// group): the group's scale once, its 32 codes from the fragment words of lanes 4g .. 4g+3 (row
+// rr of a tile lives in lanes 4 (rr & 7) + t, half rr >> 3 of their elements) at positions fixed at
+// compile time, four 16-byte stores. Columns past `cols` are zeros.
+template <int QT>
+__device__ __forceinline__ void group_codes(const Layout& L, const uint8_t* __restrict__ data, int64_t tile,
+                                            int64_t G, int g, int hi8, int (&q)[32]) {
+#pragma unroll
+  for (int t = 0; t < 4; ++t) {
+    const uint8_t* p = data + L.quant_offset(tile, G, 4 * g + t);
+    uint32_t w[4];
+    if constexpr (QT == J4B_Q8_0) {
+      const uint4 v = *reinterpret_cast<const uint4*>(p);
+      w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
+    } else if constexpr (QT == J4B_Q2_0) {
+      w[0] = *reinterpret_cast<const uint32_t*>(p);
+    } else {
+      const uint2 v = *reinterpret_cast<const uint2*>(p);
+      w[0] = v.x; w[1] = v.y;
+    }
+#pragma unroll
+    for (int ks = 0; ks < 2; ++ks)
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int b = 0; b < 2; ++b) {
+          const int e = b + 2 * hi8 + 4 * h;  // hi8 is 0 or 1: both cases unroll below
+          const int col = 16 * ks + 8 * h + 2 * t + b;
+          int code;
+          if constexpr (QT == J4B_Q8_0) {
+            const int byte = 8 * ks + e;
+            code = (int)(int8_t)(((w[byte >> 2] >> (8 * (byte & 3))) & 0xFF) ^ 0x80);
+          } else if constexpr (QT == J4B_Q2_0) {
+            code = (int)(rotr32(w[0], crumb_pos(4 * ks + (e >> 1), e & 1)) & 3);
+          } else {
+            code = (int)(rotr32(w[ks], nib_pos(e)) & 0xF);
+          }
+          q[col] = code;
+        }
+  }
+}
+
+template <int QT>
 __global__ void dequant_bf16_kernel(Layout L, const uint8_t* __restrict__ data, int64_t rows, int64_t cols,
                                     int64_t kp, __nv_bfloat16* __restrict__ hi, __nv_bfloat16* __restrict__ lo) {
   const int64_t groups = kp / 32;
@@ -306,16 +347,19 @@ __global__ void dequant_bf16_kernel(Layout L, const uint8_t* __restrict__ data, 
     const int rr = (int)(row % 16), g = rr & 7, which = rr >> 3;
     float d1 = 0.f, m1 = 0.f, d = 0.f;
     const bool live = k0 < cols;
+    int q[32];
     if (live) {
       const uint8_t* m = data + L.meta_offset(tile, G, g, which);
       d = __half2float(__ushort_as_half(rd16(m)));
-      if (L.type == J4B_Q4_K) {
+      if constexpr (QT == J4B_Q4_K) {
         const float dmin = __half2float(__ushort_as_half(rd16(m + 2)));
         int sc, mn;
         q4k_scale_min((int)((k0 % 256) / 32), m + 4, &sc, &mn);
         d1 = __fmul_rn(d, (float)sc);
         m1 = __fmul_rn(dmin, (float)mn);
       }
+      if (which) group_codes<QT>(L, data, tile, G, g, 1, q);
+      else group_codes<QT>(L, data, tile, G, g, 0, q);
     }
     __nv_bfloat16* hrow = hi + row * kp + k0;
     __nv_bfloat16* lrow = lo ? lo + row * kp + k0 : nullptr;
@@ -327,9 +371,8 @@ __global__ void dequant_bf16_kernel(Layout L, const uint8_t* __restrict__ data, 
         const int64_t k = k0 + c + u;
         float v = 0.0f;
         if (live && k < cols) {
-          const int q = repacked_code(L, data, row, k);
-          if (L.type == J4B_Q4_K) v = __fsub_rn(__fmul_rn(d1, (float)q), m1);
-          else v = __fmul_rn(d, (float)(L.type == J4B_Q8_0 ? q : (L.type == J4B_Q4_0 ? q - 8 : q - 1)));
+          if constexpr (QT == J4B_Q4_K) v = __fsub_rn(__fmul_rn(d1, (float)q[c + u]), m1);
+          else v = __fmul_rn(d, (float)(QT == J4B_Q8_0 ? q[c + u] : (QT == J4B_Q4_0 ? q[c + u] - 8 : q[c + u] - 1)));
         }
         h8[u] = __float2bfloat16_rn(v);
         l8[u] = __float2bfloat16_rn(v - __bfloat162float(h8[u]));
@@ -700,8 +743,14 @@ extern "C" int j4b_quant_gemm(j4b_qweight_t w, j4b_buf x, j4b_buf y, int64_t m, 
   __nv_bfloat16* hi = (__nv_bfloat16*)scratch;
   __nv_bfloat16* lo = terms == 3 ? (__nv_bfloat16*)((uint8_t*)scratch + ((bytes + 255) & ~size_t(255))) : nullptr;
   const int64_t total = w->rows * (kp / 32);
-  dequant_bf16_kernel<<<(unsigned)std::min<int64_t>((total + 255) / 256, 148 * 32), 256, 0, stream>>>(
-      layout_of(w), w->data, w->rows, w->cols, kp, hi, lo);
+  const unsigned grid = (unsigned)std::min<int64_t>((total + 255) / 256, 148 * 32);
+  const Layout L = layout_of(w);
+  switch (w->type) {
+    case J4B_Q8_0: dequant_bf16_kernel<J4B_Q8_0><<<grid, 256, 0, stream>>>(L, w->data, w->rows, w->cols, kp, hi, lo); break;
+    case J4B_Q4_0: dequant_bf16_kernel<J4B_Q4_0><<<grid, 256, 0, stream>>>(L, w->data, w->rows, w->cols, kp, hi, lo); break;
+    case J4B_Q4_K: dequant_bf16_kernel<J4B_Q4_K><<<grid, 256, 0, stream>>>(L, w->data, w->rows, w->cols, kp, hi, lo); break;
+    default: dequant_bf16_kernel<J4B_Q2_0><<<grid, 256, 0, stream>>>(L, w->data, w->rows, w->cols, kp, hi, lo); break;
+  }
   cudaError_t e = cudaGetLastError();
   int rc = e == cudaSuccess ? J4B_OK : cuda_error(e, "dequant_bf16_kernel");
   count_launch();
