@@ -66,25 +66,30 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const float* __restrict__ 
 }
 
 // ---------------------------------------------------------------------------------------------
-// RoPE + KV append: one thread per (token, head, pair). Token (b, t) sits at position pos0 + t.
-// The angle is formed in double (positions reach thousands of radians).
-__global__ void rope_kv_kernel(const float* __restrict__ qkv, int64_t stride, int64_t batch, int64_t seq,
-                               int heads, int64_t pos0, double theta, float* __restrict__ q_out,
-                               __half* __restrict__ k_cache, __half* __restrict__ v_cache, int64_t capacity) {
+// RoPE + KV append: one CTA per token (b, t) at position pos0 + t. The token's 64 rotation angles
+// are formed once, in double (positions reach thousands of radians), into shared memory; the
+// CTA's threads then rotate every head's (q, k) pairs and copy v.
+__global__ void __launch_bounds__(256) rope_kv_kernel(const float* __restrict__ qkv, int64_t stride, int64_t seq,
+                                                      int heads, int64_t pos0, double theta,
+                                                      float* __restrict__ q_out, __half* __restrict__ k_cache,
+                                                      __half* __restrict__ v_cache, int64_t capacity) {
   constexpr int kPairs = kHeadDim / 2;
-  const int64_t n = batch * seq * heads * kPairs;
-  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < n; idx += (int64_t)gridDim.x * blockDim.x) {
-    const int i = (int)(idx % kPairs);
-    const int h = (int)((idx / kPairs) % heads);
-    const int64_t tok = idx / kPairs / heads;
-    const int64_t b = tok / seq, t = tok % seq;
-    const int64_t pos = pos0 + t;
-    const double ang = (double)pos * pow(theta, -2.0 * i / kHeadDim);
-    double sn, cs;
-    sincos(ang, &sn, &cs);
-    const float c = (float)cs, s = (float)sn;
-    const float* row = qkv + tok * stride;
-    const int64_t width = (int64_t)heads * kHeadDim;
+  __shared__ float2 cs[kPairs];
+  const int64_t tok = blockIdx.x;
+  const int64_t b = tok / seq, t = tok % seq;
+  const int64_t pos = pos0 + t;
+  if (threadIdx.x < kPairs) {
+    const double ang = (double)pos * pow(theta, -2.0 * threadIdx.x / kHeadDim);
+    double sn, c;
+    sincos(ang, &sn, &c);
+    cs[threadIdx.x] = make_float2((float)c, (float)sn);
+  }
+  __syncthreads();
+  const float* row = qkv + tok * stride;
+  const int64_t width = (int64_t)heads * kHeadDim;
+  for (int idx = threadIdx.x; idx < heads * kPairs; idx += blockDim.x) {
+    const int h = idx / kPairs, i = idx % kPairs;
+    const float c = cs[i].x, s = cs[i].y;
     const int col = h * kHeadDim + 2 * i;
     const float2 q = *reinterpret_cast<const float2*>(row + col);
     const float2 k = *reinterpret_cast<const float2*>(row + width + col);
@@ -441,20 +446,26 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(const float* __restri
 }
 
 // ---------------------------------------------------------------------------------------------
-// SwiGLU over a fused [rows, 2 * width] gate|up buffer -> [rows, width]
-__global__ void swiglu_kernel(const float* __restrict__ gu, int64_t rows, int64_t width, float* __restrict__ out) {
-  const int64_t n = rows * width;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = i / width, c = i % width;
-    const float gv = gu[r * 2 * width + c], uv = gu[r * 2 * width + width + c];
-    out[i] = gv / (1.0f + expf(-gv)) * uv;
+// SwiGLU over a fused [rows, 2 * width] gate|up buffer -> [rows, width]: blockIdx.y strides the
+// rows, threads take float4s of a row (width % 4 == 0 and 16-byte aligned rows) or single floats.
+__global__ void swiglu_kernel(const float* __restrict__ gu, int64_t rows, int64_t width, bool vec,
+                              float* __restrict__ out) {
+  const int64_t n = vec ? width / 4 : width;
+  for (int64_t r = blockIdx.y; r < rows; r += gridDim.y) {
+    const float* g = gu + r * 2 * width;
+    const float* u = g + width;
+    float* o = out + r * width;
+    for (int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; c < n; c += (int64_t)gridDim.x * blockDim.x) {
+      if (vec) {
+        const float4 a = reinterpret_cast<const float4*>(g)[c], b = reinterpret_cast<const float4*>(u)[c];
+        reinterpret_cast<float4*>(o)[c] =
+            make_float4(a.x / (1.0f + expf(-a.x)) * b.x, a.y / (1.0f + expf(-a.y)) * b.y,
+                        a.z / (1.0f + expf(-a.z)) * b.z, a.w / (1.0f + expf(-a.w)) * b.w);
+      } else {
+        o[c] = g[c] / (1.0f + expf(-g[c])) * u[c];
+      }
+    }
   }
-}
-
-unsigned grid_of(int64_t n, int dev, int threads) {
-  const int sms = device_ctx(dev) ? device_ctx(dev)->sm_count : 148;
-  const int64_t want = (n + threads - 1) / threads;
-  return (unsigned)std::max<int64_t>(1, std::min<int64_t>(want, (int64_t)sms * 16));
 }
 
 }  // namespace
@@ -496,9 +507,9 @@ extern "C" int j4b_rope_kv(j4b_buf qkv, int64_t batch, int64_t seq, int64_t head
   J4B_REQUIRE(qkv && q_out && k_cache && v_cache && ((qkv | q_out) & 7) == 0 && ((k_cache | v_cache) & 3) == 0,
               "rope: misaligned buffers");
   J4B_DEV_OF(q_out);
-  const int64_t n = batch * seq * heads * (kHeadDim / 2);
-  rope_kv_kernel<<<grid_of(n, dev, 256), 256, 0, stream>>>(
-      (const float*)(uintptr_t)qkv, 3 * heads * kHeadDim, batch, seq, (int)heads, pos0, theta, (float*)(uintptr_t)q_out,
+  J4B_REQUIRE(batch * seq <= 0x7fffffffLL, "rope: too many tokens");
+  rope_kv_kernel<<<(unsigned)(batch * seq), 256, 0, stream>>>(
+      (const float*)(uintptr_t)qkv, 3 * heads * kHeadDim, seq, (int)heads, pos0, theta, (float*)(uintptr_t)q_out,
       (__half*)(uintptr_t)k_cache, (__half*)(uintptr_t)v_cache, capacity);
   J4B_CHECK_LAUNCH("rope_kv_kernel");
   return J4B_OK;
@@ -573,8 +584,12 @@ extern "C" int j4b_swiglu(j4b_buf gate_up, int64_t rows, int64_t width, j4b_buf 
   J4B_REQUIRE(gate_up && out && ((gate_up | out) & 3) == 0, "swiglu: misaligned buffers");
   if (rows == 0) return J4B_OK;
   J4B_DEV_OF(out);
-  swiglu_kernel<<<grid_of(rows * width, dev, 256), 256, 0, stream>>>((const float*)(uintptr_t)gate_up, rows, width,
-                                                                      (float*)(uintptr_t)out);
+  const bool vec = width % 4 == 0 && ((gate_up | out) & 15) == 0;
+  const int64_t per_row = vec ? width / 4 : width;
+  const unsigned gx = (unsigned)std::min<int64_t>((per_row + 255) / 256, 64);
+  const unsigned gy = (unsigned)std::min<int64_t>(rows, 65535);
+  swiglu_kernel<<<dim3(gx, gy), 256, 0, stream>>>((const float*)(uintptr_t)gate_up, rows, width, vec,
+                                                  (float*)(uintptr_t)out);
   J4B_CHECK_LAUNCH("swiglu_kernel");
   return J4B_OK;
 }
