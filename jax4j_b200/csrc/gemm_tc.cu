@@ -35,7 +35,9 @@ namespace j4b {
 namespace {
 
 constexpr int kBM = 128, kBK = 64;
-constexpr int kGroupM = 16;  // row tiles per rasterisation group
+// row tiles per rasterisation group (measured on the 16384 x 14336 x 4096 prefill projection:
+// 16, 32 and 64 within 2% of each other; 32 and 64 slower on the fp32-accurate 128-wide tiles)
+constexpr int kGroupM = 16;
 constexpr int kTcThreads = 192;
 constexpr int kTileBytes = kBM * kBK * 2;  // one 128 x 64 bf16 tile
 
