@@ -49,6 +49,8 @@ CONFIGS = {
     "q8_0_b8": (8, 4096, 4096, 8, "BASELINE configs[1]: GGUF Q8_0 matmul x[8,4096] . W[4096x4096]"),
     "q4_k_b1": (12, 14336, 4096, 1, "BASELINE configs[2]: Q4_K decode GEMV B=1, W[14336x4096]"),
     "q4_k_b16": (12, 14336, 4096, 16, "BASELINE configs[2]: Q4_K decode GEMV B=16, W[14336x4096]"),
+    "q6_k_b1": (14, 4096, 14336, 1, "Q6_K decode GEMV B=1, W[4096x14336] (ffn_down of GGUF Q4_K_M files)"),
+    "q6_k_b16": (14, 4096, 14336, 16, "Q6_K decode GEMV B=16, W[4096x14336] (ffn_down of GGUF Q4_K_M files)"),
 }
 TAPE_CONFIGS = {
     # name: (rows per rank, cols, label)
@@ -127,8 +129,8 @@ GEMM_CONFIGS = {
     "gemm_f32": (16384, 14336, 4096, None, 2, "dense f32 matmul [16384, 4096] . [4096, 14336], "
                  "fp32-accurate 3-term bf16 split on tcgen05"),
 }
-TYPE_NAME = {8: "Q8_0", 12: "Q4_K", 2: "Q4_0", 42: "Q2_0"}
-BLOCK = {8: (32, 34), 12: (256, 144), 2: (32, 18), 42: (128, 34)}
+TYPE_NAME = {8: "Q8_0", 12: "Q4_K", 14: "Q6_K", 2: "Q4_0", 42: "Q2_0"}
+BLOCK = {8: (32, 34), 12: (256, 144), 14: (256, 210), 2: (32, 18), 42: (128, 34)}
 METRIC = "Q4_K/Q8_0 dequant-GEMV GB/s vs HBM peak; fused-JIT tape steps/s at 1/2/4/8 B200"
 
 
@@ -1350,7 +1352,7 @@ def run_engine(args):
             "config": {
                 "workload": label, "quant": TYPE_NAME[qtype], "batch": batch,
                 "rows_per_gpu": rows, "cols": cols, "bytes_per_step_per_gpu": per_call,
-                "compute": "Q8/Q4 codes -> fp16 mma.sync, x split fp16 hi+lo, fp32 accumulate",
+                "compute": "quant codes -> exact fp16 mma.sync operands, x split fp16 hi+lo, fp32 accumulate",
                 "l2": f"weights rotate over {copies} copies ({copies * per_call / 1e6:.0f} MB > 2x L2)",
                 "parallelism": "replica" if world == 1 else f"row-shard x{world}, all-gather fused into the GEMV epilogue (NVLink peer stores)",
                 "timing": "CUDA graph of K GEMV calls, CUDA events, max over ranks",

@@ -47,6 +47,7 @@ typedef struct j4b_qweight* j4b_qweight_t; /* opaque quantized matrix (Quantized
 #define J4B_Q4_0 2
 #define J4B_Q8_0 8
 #define J4B_Q4_K 12
+#define J4B_Q6_K 14
 #define J4B_Q2_0 42
 
 /* Op codes: the ordinal order of core/tensor/Op.java:19-23 (the reference's CUDA kernels

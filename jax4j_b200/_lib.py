@@ -16,9 +16,9 @@ LIB_PATH = os.environ.get("JAX4J_B200_LIB", os.path.join(HERE, "libjax4j_b200.so
 
 OK, EINVAL, ENOMEM, ECUDA, EUNSUPPORTED, ENOTINIT, ETIMEOUT = range(7)
 
-Q4_0, Q8_0, Q4_K, Q2_0 = 2, 8, 12, 42
-QUANT_NAMES = {Q4_0: "Q4_0", Q8_0: "Q8_0", Q4_K: "Q4_K", Q2_0: "Q2_0"}
-QUANT_BLOCK = {Q4_0: (32, 18), Q8_0: (32, 34), Q4_K: (256, 144), Q2_0: (128, 34)}
+Q4_0, Q8_0, Q4_K, Q6_K, Q2_0 = 2, 8, 12, 14, 42
+QUANT_NAMES = {Q4_0: "Q4_0", Q8_0: "Q8_0", Q4_K: "Q4_K", Q6_K: "Q6_K", Q2_0: "Q2_0"}
+QUANT_BLOCK = {Q4_0: (32, 18), Q8_0: (32, 34), Q4_K: (256, 144), Q6_K: (256, 210), Q2_0: (128, 34)}
 
 OPS = ["ADD", "SUB", "MUL", "DIV", "MAX", "MIN", "NEG", "EXP", "LOG", "SQRT", "RSQRT", "TANH",
        "SIGMOID", "RELU", "ABS", "SIGN"]

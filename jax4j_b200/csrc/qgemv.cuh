@@ -102,6 +102,21 @@ __device__ __forceinline__ void q4_pairs(uint32_t w, uint32_t (&a)[4]) {
 __device__ __forceinline__ uint32_t q2_pair(uint32_t w, int p) {
   return lop_or(rotr(w, 2 * p), 0x03000300u, 0x3C003C00u);
 }
+// 6-bit (Q6_K): the low-nibble word of k-step ks and the group's high-crumb word -> four half2
+// holding the exact integers q - 32: pair p's nibbles go to bits 0..3 / 16..19 and its crumbs to
+// bits 4..5 / 20..21 of half2(1024, 1024), then 1056 = 1024 + 32 is subtracted.
+__device__ __forceinline__ void q6_pairs(uint32_t nw, uint32_t cw, int ks, uint32_t (&a)[4]) {
+  const uint32_t kBias = 0x64206420u;  // half2(1056, 1056)
+#pragma unroll
+  for (int p = 0; p < 4; p++) {
+    const uint32_t v = (rotr(nw, 6 + 4 * p) & 0x000F000Fu) | (rotr(cw, 4 + 2 * (4 * ks + p)) & 0x00300030u);
+    a[p] = h2sub(v | 0x64006400u, kBias);
+  }
+}
+// Q6_K sub-block scale j (0..7) of the half super-block held in two words, as a float.
+__device__ __forceinline__ float q6_scale(uint2 s, int j) {
+  return (float)(int8_t)(((j < 4 ? s.x : s.y) >> (8 * (j & 3))) & 0xFF);
+}
 
 // Bytes of one tile chunk, and the tiles per bulk copy: as many as two stages, the staged x and
 // the warp-partial buffer leave room for in shared memory (a copy of 35-147 KB; bulk-copy
@@ -109,13 +124,16 @@ __device__ __forceinline__ uint32_t q2_pair(uint32_t w, int p) {
 // independent mma chains per warp).
 template <int QT>
 struct GemvTraits {
-  static constexpr int kQ = QT == J4B_Q8_0 ? 512 : (QT == J4B_Q2_0 ? 128 : 256);
-  static constexpr int kM = QT == J4B_Q2_0 ? 8 : 32;
+  static constexpr int kQ = QT == J4B_Q8_0 ? 512 : (QT == J4B_Q2_0 ? 128 : (QT == J4B_Q6_K ? 384 : 256));
+  static constexpr int kM = QT == J4B_Q2_0 ? 8 : (QT == J4B_Q6_K ? 36 : 32);
   static constexpr int kChunk = 32 * (kQ + kM);  // bytes of one full tile chunk
   static constexpr int kStages = 2;
 };
 template <int QT, int NT>
-constexpr int kTilesPerCopy = QT == J4B_Q8_0 ? (NT == 1 ? 4 : 2) : (QT == J4B_Q2_0 ? 8 : (NT == 1 ? 8 : 4));
+constexpr int kTilesPerCopy = QT == J4B_Q8_0   ? (NT == 1 ? 4 : 2)
+                              : QT == J4B_Q2_0 ? 8
+                              : QT == J4B_Q6_K ? (NT == 1 ? 6 : 2)
+                                               : (NT == 1 ? 8 : 4);
 
 struct GemvArgs {
   const uint8_t* data;
@@ -174,8 +192,9 @@ __host__ __device__ constexpr int gemv_smem_base() {
          GemvTraits<QT>::kStages * 8 + 16;
 }
 
+// x block sums per warp chunk (Q8_0 and Q6_K multiply exact signed codes and need none)
 template <int QT>
-constexpr int kXBlocks = QT == J4B_Q2_0 ? 1 : 4;  // x block sums per warp chunk
+constexpr int kXBlocks = (QT == J4B_Q2_0 || QT == J4B_Q6_K) ? 1 : 4;
 
 // One warp's contribution to one 16-row tile: its 128-column slice of the tile's chunk (quants at
 // sq, scales at sm) times the x fragments, accumulated into acc (C-fragment layout: rows g and
@@ -277,6 +296,36 @@ __device__ __forceinline__ void tile_compute(const uint8_t* __restrict__ sq,
       acc[n][1] = fmaf(x0, xblk[n][0][1], fmaf(c0, c[n][1], acc[n][1]));
       acc[n][2] = fmaf(x1, xblk[n][0][0], fmaf(c1, c[n][2], acc[n][2]));
       acc[n][3] = fmaf(x1, xblk[n][0][1], fmaf(c1, c[n][3], acc[n][3]));
+    }
+  } else if constexpr (QT == J4B_Q6_K) {
+    // warp w holds half (w & 1) of super-block w / 2 of the CTA's K range; one scale d * sc per
+    // 16-column k-step, so each k-step is its own hi + lo chain of exact signed codes
+    const int h = warp & 1;
+    const uint8_t* lp = sq + warp * 1536 + lane * 48;
+    const uint4 n0 = *reinterpret_cast<const uint4*>(lp);
+    const uint4 n1 = *reinterpret_cast<const uint4*>(lp + 16);
+    const uint4 cr = *reinterpret_cast<const uint4*>(lp + 32);
+    const uint8_t* mp = sm + (warp >> 1) * 288;
+    const uint2 s0 = *reinterpret_cast<const uint2*>(mp + (2 * g) * 16 + 8 * h);
+    const uint2 s1 = *reinterpret_cast<const uint2*>(mp + (2 * g + 1) * 16 + 8 * h);
+    const float2 d = __half22float2(*reinterpret_cast<const __half2*>(mp + 256 + 4 * g));
+    const uint32_t wv[8] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
+    const uint32_t cv[4] = {cr.x, cr.y, cr.z, cr.w};
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      uint32_t a[4];
+      q6_pairs(wv[j], cv[j >> 1], j & 1, a);
+      const float f0 = d.x * q6_scale(s0, j), f1 = d.y * q6_scale(s1, j);
+#pragma unroll
+      for (int n = 0; n < NT; n++) {
+        float c[4];
+        mma16816_z(c, a[0], a[1], a[2], a[3], bh[n][j][0], bh[n][j][1]);
+        mma16816(c, a[0], a[1], a[2], a[3], bl[n][j][0], bl[n][j][1]);
+        acc[n][0] = fmaf(f0, c[0], acc[n][0]);
+        acc[n][1] = fmaf(f0, c[1], acc[n][1]);
+        acc[n][2] = fmaf(f1, c[2], acc[n][2]);
+        acc[n][3] = fmaf(f1, c[3], acc[n][3]);
+      }
     }
   } else {  // Q4_K: warp w holds half (w & 1) of super-block w / 2 of the CTA's K range
     const int h = warp & 1;
@@ -394,6 +443,27 @@ __device__ __forceinline__ void tile_compute_pk(const uint8_t* __restrict__ sq,
     const float2 d = __half22float2(*reinterpret_cast<const __half2*>(&sc));
     acc[0] += d.x * fmaf(4.f, c[0] + c[1], -5.f * xblk[0]);
     acc[1] += d.y * fmaf(4.f, c[2] + c[3], -5.f * xblk[0]);
+  } else if constexpr (QT == J4B_Q6_K) {  // as in tile_compute
+    const int h = warp & 1;
+    const uint8_t* lp = sq + warp * 1536 + lane * 48;
+    const uint4 n0 = *reinterpret_cast<const uint4*>(lp);
+    const uint4 n1 = *reinterpret_cast<const uint4*>(lp + 16);
+    const uint4 cr = *reinterpret_cast<const uint4*>(lp + 32);
+    const uint8_t* mp = sm + (warp >> 1) * 288;
+    const uint2 s0 = *reinterpret_cast<const uint2*>(mp + (2 * g) * 16 + 8 * h);
+    const uint2 s1 = *reinterpret_cast<const uint2*>(mp + (2 * g + 1) * 16 + 8 * h);
+    const float2 d = __half22float2(*reinterpret_cast<const __half2*>(mp + 256 + 4 * g));
+    const uint32_t wv[8] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
+    const uint32_t cv[4] = {cr.x, cr.y, cr.z, cr.w};
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      uint32_t a[4];
+      q6_pairs(wv[j], cv[j >> 1], j & 1, a);
+      float c[4];
+      mma16816_z(c, a[0], a[1], a[2], a[3], bp[j][0], bp[j][1]);
+      acc[0] = fmaf(d.x * q6_scale(s0, j), c[0] + c[1], acc[0]);
+      acc[1] = fmaf(d.y * q6_scale(s1, j), c[2] + c[3], acc[1]);
+    }
   } else {  // Q4_K, as in tile_compute
     const int h = warp & 1;
     const uint4 l0 = *reinterpret_cast<const uint4*>(sq + warp * 1024 + lane * 32);
@@ -594,7 +664,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) qgemv_kernel(GemvArgs a) {
   constexpr int kXB = kXBlocks<QT>;
   float xblk[NT][kXB][2] = {};
   float xblkp[kXB] = {};
-  if constexpr (QT != J4B_Q8_0) {
+  if constexpr (QT != J4B_Q8_0 && QT != J4B_Q6_K) {
 #pragma unroll
     for (int n = 0; n < NTF; n++) {
 #pragma unroll

@@ -3,12 +3,13 @@
 //
 // Reference interface: core/tensor/spi/QuantizedOps.java:19-34, CPU semantics in
 // core/backend/cpu/CpuBackend.java:690-755, CpuQ4Gemm.java:17-77, CpuQ2Gemm.java:17-83. The
-// reference has no GPU quantised path; Q8_0 and Q4_K have no implementation at all there
-// (core/tensor/QuantType.java:8-9 only) and follow the public GGUF block layouts.
+// reference has no GPU quantised path; Q8_0, Q4_K and Q6_K have no implementation at all there
+// (core/tensor/QuantType.java:8-10 only) and follow the public GGUF block layouts.
 //
 // Device layout ("fragment-major repack", same byte count as the GGUF blob):
 //   A weight of R rows x K columns is cut into row tiles of 16 rows. Inside a row tile, every
-//   group of 32 columns (one Q8_0/Q4_0 block, one Q4_K sub-block, a quarter Q2_0 block) holds
+//   group of 32 columns (one Q8_0/Q4_0 block, one Q4_K sub-block, an eighth of a Q6_K
+//   super-block, a quarter Q2_0 block) holds
 //   exactly the bytes lane l of a warp needs to build its mma.m16n8k16 A fragments for those 32
 //   columns, stored contiguously in lane order, so a warp streams its tile with fully coalesced
 //   128-bit loads. Per-row scales live in a separate plane in the same tile order. Padding rows
@@ -61,6 +62,7 @@ __host__ __device__ inline int block_elems(int t) {
   switch (t) {
     case J4B_Q4_0: case J4B_Q8_0: return 32;
     case J4B_Q4_K: return 256;
+    case J4B_Q6_K: return 256;
     case J4B_Q2_0: return 128;
   }
   return -1;
@@ -70,6 +72,7 @@ __host__ __device__ inline int block_bytes(int t) {
     case J4B_Q4_0: return 18;
     case J4B_Q8_0: return 34;
     case J4B_Q4_K: return 144;
+    case J4B_Q6_K: return 210;
     case J4B_Q2_0: return 34;
   }
   return -1;
@@ -123,6 +126,12 @@ __device__ inline int raw_code(int type, const uint8_t* blob, int64_t rows, int6
       int b = blk[16 + 32 * c + l];
       return h ? (b >> 4) : (b & 0xF);
     }
+    case J4B_Q6_K: {  // 6-bit code 0..63: ql nibble | qh crumb << 4
+      const int n = w / 128, s = (w % 128) / 32, l = w % 32;
+      const int b = blk[64 * n + l + 32 * (s & 1)];
+      const int nib = s >= 2 ? (b >> 4) : (b & 0xF);
+      return nib | (((blk[128 + 32 * n + l] >> (2 * s)) & 3) << 4);
+    }
   }
   return 0;
 }
@@ -140,11 +149,15 @@ __device__ inline int raw_code(int type, const uint8_t* blob, int64_t rows, int6
 //         row's 16 GGUF bytes (d, dmin, 12 packed 6-bit scales/mins) per super-block
 //   Q2_0: quants (gl/4)*512 + lane*16 + (gl%4)*4 (one word, crumbs at crumb_pos);
 //         scales (gl/4)*32 + g*4 + which*2
+//   Q6_K: quants (gl/4)*1536 + lane*48: the lane's low-nibble words at + (gl%4)*8 (two words,
+//         k-steps 0/1, nibbles at nib_pos) and its high-crumb word at + 32 + (gl%4)*4 (bits 4-5
+//         of each code at crumb_pos); scales (gl/8)*288: the row's 16 int8 sub-block scales at
+//         + (g*2+which)*16, its f16 d at + 256 + (g*2+which)*2
 // ---------------------------------------------------------------------------------------------
 __host__ __device__ inline int group_quant_bytes(int t) {
-  return t == J4B_Q8_0 ? 512 : (t == J4B_Q2_0 ? 128 : 256);
+  return t == J4B_Q8_0 ? 512 : (t == J4B_Q2_0 ? 128 : (t == J4B_Q6_K ? 384 : 256));
 }
-__host__ __device__ inline int group_meta_bytes(int t) { return t == J4B_Q2_0 ? 8 : 32; }
+__host__ __device__ inline int group_meta_bytes(int t) { return t == J4B_Q2_0 ? 8 : (t == J4B_Q6_K ? 36 : 32); }
 
 struct Layout {
   int type;
@@ -172,8 +185,14 @@ struct Layout {
       case J4B_Q8_0: return base + gl * 512 + lane * 16;
       case J4B_Q4_0: return base + (gl / 2) * 512 + lane * 16 + (gl % 2) * 8;
       case J4B_Q4_K: return base + (gl / 4) * 1024 + lane * 32 + (gl % 4) * 8;
+      case J4B_Q6_K: return base + (gl / 4) * 1536 + lane * 48 + (gl % 4) * 8;
       default: return base + (gl / 4) * 512 + lane * 16 + (gl % 4) * 4;
     }
+  }
+  // Q6_K: byte offset of lane `lane`'s high-crumb word for global group G of `tile`
+  __host__ __device__ int64_t crumb_offset(int64_t tile, int64_t G, int lane) const {
+    const int gl = (int)(G % 32);
+    return chunk_offset(G / 32, tile) + (gl / 4) * 1536 + lane * 48 + 32 + (gl % 4) * 4;
   }
   // byte offset of the scale data of row (g, which) of `tile` for global group G
   __host__ __device__ int64_t meta_offset(int64_t tile, int64_t G, int g, int which) const {
@@ -182,9 +201,17 @@ struct Layout {
     const int64_t base = chunk_offset(s, tile) + (int64_t)groups_in_split(s) * group_quant_bytes(type);
     switch (type) {
       case J4B_Q4_K: return base + (gl / 8) * 256 + (g * 2 + which) * 16;
+      case J4B_Q6_K: return base + (gl / 8) * 288 + (g * 2 + which) * 16;
       case J4B_Q2_0: return base + (gl / 4) * 32 + g * 4 + which * 2;
       default: return base + gl * 32 + g * 4 + which * 2;
     }
+  }
+  // Q6_K: byte offset of the f16 d of row (g, which) of `tile` for global group G
+  __host__ __device__ int64_t d_offset(int64_t tile, int64_t G, int g, int which) const {
+    const int64_t s = G / 32;
+    const int gl = (int)(G % 32);
+    return chunk_offset(s, tile) + (int64_t)groups_in_split(s) * group_quant_bytes(type) + (gl / 8) * 288 + 256 +
+           (g * 2 + which) * 2;
   }
 };
 
@@ -225,6 +252,17 @@ __global__ void repack_quants_kernel(Layout L, const uint8_t* __restrict__ blob,
         word |= rotl32((uint32_t)(c & 3), crumb_pos(4 * ks + (e >> 1), e & 1));
       }
     reinterpret_cast<uint32_t*>(dst)[0] = word;
+  } else if (type == J4B_Q6_K) {
+    uint32_t words[2] = {0, 0}, crumbs = 0;
+    for (int ks = 0; ks < 2; ks++)
+      for (int e = 0; e < 8; e++) {
+        const int q = raw_code(type, blob, rows, cols, r0 + frag_row(lane, e), k0 + 16 * ks + frag_col(lane, e), &in);
+        words[ks] |= rotl32((uint32_t)(q & 0xF), nib_pos(e));
+        crumbs |= rotl32((uint32_t)((q >> 4) & 3), crumb_pos(4 * ks + (e >> 1), e & 1));
+      }
+    reinterpret_cast<uint32_t*>(dst)[0] = words[0];
+    reinterpret_cast<uint32_t*>(dst)[1] = words[1];
+    *reinterpret_cast<uint32_t*>(out + L.crumb_offset(tile, grp, lane)) = crumbs;
   }
 }
 
@@ -245,6 +283,13 @@ __global__ void repack_meta_kernel(Layout L, const uint8_t* __restrict__ blob, i
   const int g = rr & 7, which = rr >> 3;
   const int64_t G = blk * be / 32;  // first 32-column group of the block
   uint8_t* dst = out + L.meta_offset(tile, G, g, which);
+  if (type == J4B_Q6_K) {  // 16 scales from byte 192, d from byte 208
+    for (int i = 0; i < 16; i++) dst[i] = in ? src[192 + i] : 0;
+    uint8_t* dd = out + L.d_offset(tile, G, g, which);
+    dd[0] = in ? src[208] : 0;
+    dd[1] = in ? src[209] : 0;
+    return;
+  }
   const int n = type == J4B_Q4_K ? 16 : 2;
   for (int i = 0; i < n; i++) dst[i] = in ? src[i] : 0;
 }
@@ -265,6 +310,11 @@ __device__ inline int repacked_code(const Layout& L, const uint8_t* data, int64_
   if (L.type == J4B_Q8_0) return (int)(int8_t)(p[8 * ks + e] ^ 0x80);
   if (L.type == J4B_Q4_0 || L.type == J4B_Q4_K)
     return rotr32(reinterpret_cast<const uint32_t*>(p)[ks], nib_pos(e)) & 0xF;
+  if (L.type == J4B_Q6_K) {
+    const uint32_t cw = *reinterpret_cast<const uint32_t*>(data + L.crumb_offset(tile, grp, lane));
+    return (int)((rotr32(reinterpret_cast<const uint32_t*>(p)[ks], nib_pos(e)) & 0xF) |
+                 ((rotr32(cw, crumb_pos(4 * ks + (e >> 1), e & 1)) & 3) << 4));
+  }
   return rotr32(reinterpret_cast<const uint32_t*>(p)[0], crumb_pos(4 * ks + (e >> 1), e & 1)) & 3;
 }
 
@@ -285,6 +335,10 @@ __global__ void gather_row_kernel(Layout L, const uint8_t* __restrict__ data, in
     q4k_scale_min(j, m + 4, &sc, &mn);
     const float d1 = __fmul_rn(d, (float)sc), m1 = __fmul_rn(dmin, (float)mn);
     v = __fsub_rn(__fmul_rn(d1, (float)q), m1);  // d1*q is exact; one rounding, as the oracle
+  } else if (L.type == J4B_Q6_K) {
+    const float d = __half2float(__ushort_as_half(rd16(data + L.d_offset(tile, k / 32, g, which))));
+    const int sc = (int)(int8_t)m[(k % 256) / 16];
+    v = __fmul_rn(__fmul_rn(d, (float)sc), (float)(q - 32));  // (d * sc) * (q - 32), as the oracle
   } else {
     const float d = __half2float(__ushort_as_half(rd16(m)));
     const int code = L.type == J4B_Q8_0 ? q : (L.type == J4B_Q4_0 ? q - 8 : q - 1);
@@ -313,6 +367,7 @@ __device__ __forceinline__ void group_codes(const Layout& L, const uint8_t* __re
     } else {
       const uint2 v = *reinterpret_cast<const uint2*>(p);
       w[0] = v.x; w[1] = v.y;
+      if constexpr (QT == J4B_Q6_K) w[2] = *reinterpret_cast<const uint32_t*>(data + L.crumb_offset(tile, G, 4 * g + t));
     }
 #pragma unroll
     for (int ks = 0; ks < 2; ++ks)
@@ -328,6 +383,8 @@ __device__ __forceinline__ void group_codes(const Layout& L, const uint8_t* __re
             code = (int)(int8_t)(((w[byte >> 2] >> (8 * (byte & 3))) & 0xFF) ^ 0x80);
           } else if constexpr (QT == J4B_Q2_0) {
             code = (int)(rotr32(w[0], crumb_pos(4 * ks + (e >> 1), e & 1)) & 3);
+          } else if constexpr (QT == J4B_Q6_K) {
+            code = (int)((rotr32(w[ks], nib_pos(e)) & 0xF) | ((rotr32(w[2], crumb_pos(4 * ks + (e >> 1), e & 1)) & 3) << 4));
           } else {
             code = (int)(rotr32(w[ks], nib_pos(e)) & 0xF);
           }
@@ -345,7 +402,7 @@ __global__ void dequant_bf16_kernel(Layout L, const uint8_t* __restrict__ data, 
     const int64_t row = i / groups, G = i % groups, k0 = G * 32;
     const int64_t tile = row / 16;
     const int rr = (int)(row % 16), g = rr & 7, which = rr >> 3;
-    float d1 = 0.f, m1 = 0.f, d = 0.f;
+    float d1 = 0.f, m1 = 0.f, d = 0.f;  // Q6_K: d1, m1 = d * sc of the group's two sub-blocks
     const bool live = k0 < cols;
     int q[32];
     if (live) {
@@ -357,6 +414,11 @@ __global__ void dequant_bf16_kernel(Layout L, const uint8_t* __restrict__ data, 
         q4k_scale_min((int)((k0 % 256) / 32), m + 4, &sc, &mn);
         d1 = __fmul_rn(d, (float)sc);
         m1 = __fmul_rn(dmin, (float)mn);
+      } else if constexpr (QT == J4B_Q6_K) {
+        d = __half2float(__ushort_as_half(rd16(data + L.d_offset(tile, G, g, which))));
+        const int j = (int)((k0 % 256) / 16);
+        d1 = __fmul_rn(d, (float)(int8_t)m[j]);
+        m1 = __fmul_rn(d, (float)(int8_t)m[j + 1]);
       }
       if (which) group_codes<QT>(L, data, tile, G, g, 1, q);
       else group_codes<QT>(L, data, tile, G, g, 0, q);
@@ -372,6 +434,7 @@ __global__ void dequant_bf16_kernel(Layout L, const uint8_t* __restrict__ data, 
         float v = 0.0f;
         if (live && k < cols) {
           if constexpr (QT == J4B_Q4_K) v = __fsub_rn(__fmul_rn(d1, (float)q[c + u]), m1);
+          else if constexpr (QT == J4B_Q6_K) v = __fmul_rn(c < 16 ? d1 : m1, (float)(q[c + u] - 32));
           else v = __fmul_rn(d, (float)(QT == J4B_Q8_0 ? q[c + u] : (QT == J4B_Q4_0 ? q[c + u] - 8 : q[c + u] - 1)));
         }
         h8[u] = __float2bfloat16_rn(v);
@@ -400,7 +463,7 @@ __device__ inline uint16_t f2h(float f) { return __half_as_ushort(__float2half_r
 
 // A block is assembled in a register array of 32-bit words, then written out byte by byte.
 struct BlockBytes {
-  uint32_t w[36] = {};
+  uint32_t w[53] = {};
   __device__ void put(int i, uint32_t v) { w[i >> 2] |= (v & 0xffu) << (8 * (i & 3)); }
   __device__ void put16(int i, uint16_t v) {
     put(i, v & 0xffu);
@@ -502,6 +565,34 @@ __global__ void quantize_kernel(int type, const float* __restrict__ w, int64_t r
         }
         blk.put(16 + 32 * c + l, (uint32_t)(q[0] | (q[1] << 4)));
       }
+  } else if (type == J4B_Q6_K) {
+    // per 16 elements s_j = (the largest-magnitude value) / 31; d = max |s_j| / 127 (f16);
+    // sc_j = round(s_j / d) in [-127, 127]; codes round(w / (d sc_j)) in [-32, 31], stored + 32
+    float sub[16], max_abs = 0.f;
+    for (int j = 0; j < 16; j++) {
+      float best = 0.f;
+      for (int i = 0; i < 16; i++)
+        if (fabsf(src[16 * j + i]) > fabsf(best)) best = src[16 * j + i];
+      sub[j] = __fdiv_rn(best, 31.0f);
+      if (fabsf(sub[j]) > max_abs) max_abs = fabsf(sub[j]);
+    }
+    const uint16_t dh = f2h(__fdiv_rn(max_abs, 127.0f));
+    const float d = __half2float(__ushort_as_half(dh));
+    int sc[16];
+    for (int j = 0; j < 16; j++) {
+      const int v = d > 0.f ? (int)roundf(__fdiv_rn(sub[j], d)) : 0;
+      sc[j] = max(-127, min(127, v));
+      blk.put(192 + j, (uint32_t)(sc[j] & 0xff));
+    }
+    blk.put16(208, dh);
+    for (int e = 0; e < 256; e++) {
+      const int n = e / 128, s = (e % 128) / 32, l = e % 32;
+      const float ds = __fmul_rn(d, (float)sc[e / 16]);
+      int q = ds != 0.f ? (int)roundf(__fdiv_rn(src[e], ds)) : 0;
+      q = max(-32, min(31, q)) + 32;
+      blk.put(64 * n + l + 32 * (s & 1), (uint32_t)((q & 0xF) << (s >= 2 ? 4 : 0)));
+      blk.put(128 + 32 * n + l, (uint32_t)(((q >> 4) & 3) << (2 * s)));
+    }
   }
   uint8_t* dst = out + idx * bb;
   for (int i = 0; i < bb; i++) dst[i] = blk.get(i);
@@ -519,7 +610,7 @@ int upload_common(int dev, const uint8_t* dblob, int type, int64_t rows, int64_t
   w->cols = cols;
   w->rt = (rows + 15) / 16;
   w->kpad = (cols + kWarpCols - 1) / kWarpCols * kWarpCols;
-  if (type == J4B_Q4_K) w->kpad = (cols + 255) / 256 * 256;
+  if (type == J4B_Q4_K || type == J4B_Q6_K) w->kpad = (cols + 255) / 256 * 256;
   w->ksplit = (int)((w->kpad + kCtaCols - 1) / kCtaCols);
   const Layout L = layout_of(w);
   w->data_bytes = (size_t)L.total_bytes();
@@ -580,10 +671,10 @@ int check_geometry(int type, int64_t rows, int64_t cols, size_t bytes) {
 using namespace j4b;
 
 extern "C" int j4b_quant_supported(int* ids, int cap, int* n) {
-  static const int kIds[] = {J4B_Q4_0, J4B_Q8_0, J4B_Q4_K, J4B_Q2_0};
+  static const int kIds[] = {J4B_Q4_0, J4B_Q8_0, J4B_Q4_K, J4B_Q6_K, J4B_Q2_0};
   if (!n) return set_error(J4B_EINVAL, "n is null");
-  *n = 4;
-  for (int i = 0; i < 4 && i < cap && ids; i++) ids[i] = kIds[i];
+  *n = 5;
+  for (int i = 0; i < 5 && i < cap && ids; i++) ids[i] = kIds[i];
   return J4B_OK;
 }
 
@@ -673,6 +764,7 @@ extern "C" int j4b_quant_matvec(j4b_qweight_t w, j4b_buf x, j4b_buf add, j4b_buf
       case J4B_Q8_0: e = gemv_dispatch<J4B_Q8_0>(w, xp, ap, yp, nb, sms, stream); break;
       case J4B_Q4_0: e = gemv_dispatch<J4B_Q4_0>(w, xp, ap, yp, nb, sms, stream); break;
       case J4B_Q4_K: e = gemv_dispatch<J4B_Q4_K>(w, xp, ap, yp, nb, sms, stream); break;
+      case J4B_Q6_K: e = gemv_dispatch<J4B_Q6_K>(w, xp, ap, yp, nb, sms, stream); break;
       case J4B_Q2_0: e = gemv_dispatch<J4B_Q2_0>(w, xp, ap, yp, nb, sms, stream); break;
     }
     if (e != cudaSuccess) return cuda_error(e, "qgemv_kernel");
@@ -704,6 +796,7 @@ extern "C" int j4b_quant_matvec_allgather(j4b_qweight_t w, j4b_buf x, j4b_buf ad
     case J4B_Q8_0: e = gemv_dispatch<J4B_Q8_0>(w, xp, ap, nullptr, (int)batch, sms, stream, &t, &grid); break;
     case J4B_Q4_0: e = gemv_dispatch<J4B_Q4_0>(w, xp, ap, nullptr, (int)batch, sms, stream, &t, &grid); break;
     case J4B_Q4_K: e = gemv_dispatch<J4B_Q4_K>(w, xp, ap, nullptr, (int)batch, sms, stream, &t, &grid); break;
+    case J4B_Q6_K: e = gemv_dispatch<J4B_Q6_K>(w, xp, ap, nullptr, (int)batch, sms, stream, &t, &grid); break;
     case J4B_Q2_0: e = gemv_dispatch<J4B_Q2_0>(w, xp, ap, nullptr, (int)batch, sms, stream, &t, &grid); break;
   }
   if (e != cudaSuccess) return cuda_error(e, "qgemv_kernel");
@@ -749,6 +842,7 @@ extern "C" int j4b_quant_gemm(j4b_qweight_t w, j4b_buf x, j4b_buf y, int64_t m, 
     case J4B_Q8_0: dequant_bf16_kernel<J4B_Q8_0><<<grid, 256, 0, stream>>>(L, w->data, w->rows, w->cols, kp, hi, lo); break;
     case J4B_Q4_0: dequant_bf16_kernel<J4B_Q4_0><<<grid, 256, 0, stream>>>(L, w->data, w->rows, w->cols, kp, hi, lo); break;
     case J4B_Q4_K: dequant_bf16_kernel<J4B_Q4_K><<<grid, 256, 0, stream>>>(L, w->data, w->rows, w->cols, kp, hi, lo); break;
+    case J4B_Q6_K: dequant_bf16_kernel<J4B_Q6_K><<<grid, 256, 0, stream>>>(L, w->data, w->rows, w->cols, kp, hi, lo); break;
     default: dequant_bf16_kernel<J4B_Q2_0><<<grid, 256, 0, stream>>>(L, w->data, w->rows, w->cols, kp, hi, lo); break;
   }
   cudaError_t e = cudaGetLastError();

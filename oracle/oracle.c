@@ -130,6 +130,7 @@ static int block_elems(int type) {
     case J4O_Q4_0: return 32;
     case J4O_Q8_0: return 32;
     case J4O_Q4_K: return 256;
+    case J4O_Q6_K: return 256;
     case J4O_Q2_0: return 128;
     default: return -1;
   }
@@ -140,6 +141,7 @@ static int block_bytes(int type) {
     case J4O_Q4_0: return 18;
     case J4O_Q8_0: return 34;
     case J4O_Q4_K: return 144;
+    case J4O_Q6_K: return 210;
     case J4O_Q2_0: return 34;
     default: return -1;
   }
@@ -332,6 +334,60 @@ static float dec_q4_k(const uint8_t* blk, int within) {
   return d1 * (float)q - m1;
 }
 
+/* Q6_K (GGUF type 14, QuantType.java:10 geometry only): 256-element super-block = ql[128] low
+ * nibbles, qh[64] high 2-bit pairs, scales[16] int8 (one per 16 elements), f16 d (public GGUF
+ * layout). Element l + 32 s of half n (l < 32, s < 4): ql byte 64 n + l + 32 (s & 1), low
+ * nibble for s < 2 and high for s >= 2; qh byte 32 n + l, bits 2 s .. 2 s + 1; scale 8 n + l/16
+ * + 2 s; code q = nibble | high << 4 in [0, 63]; w = (d * sc) * (q - 32), in that order.
+ * Encoding (ours, single pass): per 16 elements s_j = max|w| / 31 (signed by the largest
+ * magnitude); d = max |s_j| / 127 (f16); sc_j = round(s_j / d) in [-127, 127];
+ * q = clamp(round(w / (d sc_j)), -32, 31) + 32. All arithmetic in float. */
+static void enc_q6_k(const float* w, uint8_t* blk) {
+  float sub[16], max_abs = 0.0f;
+  for (int j = 0; j < 16; j++) {
+    float best = 0.0f;
+    for (int i = 0; i < 16; i++) {
+      float v = w[16 * j + i];
+      if (fabsf(v) > fabsf(best)) best = v;
+    }
+    sub[j] = best / 31.0f;
+    if (fabsf(sub[j]) > max_abs) max_abs = fabsf(sub[j]);
+  }
+  uint16_t dh = j4o_float_to_half(max_abs / 127.0f);
+  float d = j4o_half_to_float(dh);
+  int8_t sc[16];
+  for (int j = 0; j < 16; j++) {
+    int v = d > 0.0f ? round_away(sub[j] / d) : 0;
+    sc[j] = (int8_t)(v < -127 ? -127 : (v > 127 ? 127 : v));
+  }
+  uint8_t* ql = blk;
+  uint8_t* qh = blk + 128;
+  int8_t* scales = (int8_t*)(blk + 192);
+  memset(blk, 0, 192);
+  for (int j = 0; j < 16; j++) scales[j] = sc[j];
+  wr16(blk + 208, dh);
+  for (int e = 0; e < 256; e++) {
+    int n = e / 128, r = e % 128, s = r / 32, l = r % 32;
+    float ds = d * (float)sc[16 * 0 + (e / 16)];
+    int q = ds != 0.0f ? round_away(w[e] / ds) : 0;
+    q = (q < -32 ? -32 : (q > 31 ? 31 : q)) + 32;
+    int qlb = 64 * n + l + 32 * (s & 1);
+    ql[qlb] |= (uint8_t)((q & 0xF) << (s >= 2 ? 4 : 0));
+    qh[32 * n + l] |= (uint8_t)(((q >> 4) & 3) << (2 * s));
+  }
+}
+
+static float dec_q6_k(const uint8_t* blk, int within) {
+  float d = j4o_half_to_float(rd16(blk + 208));
+  int n = within / 128, r = within % 128, s = r / 32, l = r % 32;
+  int qlb = blk[64 * n + l + 32 * (s & 1)];
+  int nib = s >= 2 ? (qlb >> 4) : (qlb & 0xF);
+  int hi = (blk[128 + 32 * n + l] >> (2 * s)) & 3;
+  int q = (nib | (hi << 4)) - 32;
+  int sc = (int)((const int8_t*)(blk + 192))[8 * n + l / 16 + 2 * s];
+  return (d * (float)sc) * (float)q;
+}
+
 int j4o_quantize(int type, const float* w, int64_t rows, int64_t cols, uint8_t* out) {
   int64_t rb = j4o_quant_row_bytes(type, cols);
   if (rb < 0 || rows <= 0) return -1;
@@ -344,6 +400,7 @@ int j4o_quantize(int type, const float* w, int64_t rows, int64_t cols, uint8_t* 
         case J4O_Q8_0: enc_q8_0(src, dst); break;
         case J4O_Q4_0: enc_q4_0(src, dst); break;
         case J4O_Q4_K: enc_q4_k(src, dst); break;
+        case J4O_Q6_K: enc_q6_k(src, dst); break;
         case J4O_Q2_0: enc_q2_0(src, dst); break;
         default: return -1;
       }
@@ -360,6 +417,7 @@ static float dec_elem(int type, const uint8_t* row, int64_t idx) {
     case J4O_Q8_0: return dec_q8_0(blk, within);
     case J4O_Q4_0: return dec_q4_0(blk, within);
     case J4O_Q4_K: return dec_q4_k(blk, within);
+    case J4O_Q6_K: return dec_q6_k(blk, within);
     case J4O_Q2_0: return dec_q2_0(blk, within);
   }
   return NAN;
@@ -420,7 +478,7 @@ static void mv_q2_0(const uint8_t* w, const float* x, int64_t rows, int64_t cols
   }
 }
 
-/* Q8_0 / Q4_K multiply: no reference implementation exists. Same style as CpuQ4Gemm: one float
+/* Q8_0 / Q4_K / Q6_K multiply: no reference implementation exists. Same style as CpuQ4Gemm: one float
  * accumulator per row, elements in index order, sum += w_dequant * x. */
 static void mv_generic(int type, const uint8_t* w, const float* x, int64_t rows, int64_t cols,
                        float* y) {
@@ -443,7 +501,8 @@ int j4o_quant_matvec(int type, const uint8_t* blob, int64_t rows, int64_t cols,
       case J4O_Q4_0: mv_q4_0(blob, xb, rows, cols, yb); break;
       case J4O_Q2_0: mv_q2_0(blob, xb, rows, cols, yb); break;
       case J4O_Q8_0:
-      case J4O_Q4_K: mv_generic(type, blob, xb, rows, cols, yb); break;
+      case J4O_Q4_K:
+      case J4O_Q6_K: mv_generic(type, blob, xb, rows, cols, yb); break;
       default: return -1;
     }
   }

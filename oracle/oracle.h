@@ -39,7 +39,7 @@ float j4o_half_to_float(uint32_t bits);
 uint16_t j4o_float_to_half(float f);
 
 /* ---- GGUF block codecs. type ids follow QuantType.java:4-13 ---- */
-enum { J4O_Q4_0 = 2, J4O_Q8_0 = 8, J4O_Q4_K = 12, J4O_Q2_0 = 42 };
+enum { J4O_Q4_0 = 2, J4O_Q8_0 = 8, J4O_Q4_K = 12, J4O_Q6_K = 14, J4O_Q2_0 = 42 };
 int64_t j4o_quant_row_bytes(int type, int64_t cols);
 /* Encode rows x cols f32 (row-major) into GGUF blocks. Returns 0 or -1 on bad geometry. */
 int j4o_quantize(int type, const float* w, int64_t rows, int64_t cols, uint8_t* out);

@@ -53,11 +53,12 @@ def test_quant_geometry_checks(lib):
     assert lib.j4b_quant_bytes(2, 10, 64, ctypes.byref(b)) == 0 and b.value == 10 * 2 * 18
     assert lib.j4b_quant_bytes(8, 4, 33, ctypes.byref(b)) == _lib.EINVAL
     assert "block-aligned" in _lib.last_error()
-    assert lib.j4b_quant_bytes(14, 4, 256, ctypes.byref(b)) == _lib.EUNSUPPORTED
+    assert lib.j4b_quant_bytes(14, 4, 512, ctypes.byref(b)) == 0 and b.value == 4 * 2 * 210
+    assert lib.j4b_quant_bytes(41, 4, 256, ctypes.byref(b)) == _lib.EUNSUPPORTED
     ids = (ctypes.c_int * 8)()
     n = ctypes.c_int(0)
     assert lib.j4b_quant_supported(ids, 8, ctypes.byref(n)) == 0
-    assert sorted(ids[i] for i in range(n.value)) == [2, 8, 12, 42]
+    assert sorted(ids[i] for i in range(n.value)) == [2, 8, 12, 14, 42]
 
 
 def test_invalid_arguments_fail_before_launch(lib):

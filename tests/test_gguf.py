@@ -14,10 +14,12 @@ def _blobs(oracle):
     w4 = (rng.standard_normal((48, 256)) * 0.02).astype(np.float32)
     w8 = (rng.standard_normal((16, 128)) * 0.02).astype(np.float32)
     wk = (rng.standard_normal((8, 512)) * 0.02).astype(np.float32)
+    w6 = (rng.standard_normal((24, 256)) * 0.02).astype(np.float32)
     f = rng.standard_normal((3, 5)).astype(np.float32)
     return [("blk.0.attn_q.weight", (48, 256), 2, oracle.quantize(2, w4)),
             ("blk.0.ffn_up.weight", (16, 128), 8, oracle.quantize(8, w8)),
             ("blk.0.ffn_down.weight", (8, 512), 12, oracle.quantize(12, wk)),
+            ("output.weight", (24, 256), 14, oracle.quantize(14, w6)),
             ("token_norm", (3, 5), 0, f.view(np.uint8)),
             ("scale", (7,), 1, np.arange(7, dtype=np.float16).view(np.uint8))]
 
@@ -77,7 +79,7 @@ def test_load_quantized_matrices_match_the_oracle(tmp_path, oracle, backend):
     for name, shape, tid, raw in tensors:
         buf = loaded[name]
         if tid in (0, 1):
-            want = np.asarray(raw).view(np.float32 if tid == 0 else np.float16).astype(np.float32)
+            want = np.asarray(raw).reshape(-1).view(np.float32 if tid == 0 else np.float16).astype(np.float32)
             assert np.array_equal(backend.download(buf).reshape(-1), want)
             continue
         assert buf.shape == shape

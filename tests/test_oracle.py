@@ -81,7 +81,7 @@ def test_q2_0_hand_built_block(oracle):
     assert np.array_equal(row, np.array([2.0 * (c - 1) for c in codes], np.float32))
 
 
-@pytest.mark.parametrize("qtype", [8, 2, 12, 42])
+@pytest.mark.parametrize("qtype", [8, 2, 12, 14, 42])
 def test_codec_geometry_and_roundtrip(oracle, qtype):
     rng = np.random.default_rng(qtype)
     be, bb = oracle.BLOCK[qtype]
@@ -91,7 +91,7 @@ def test_codec_geometry_and_roundtrip(oracle, qtype):
     assert blob.size == rows * cols // be * bb == oracle.quant_row_bytes(qtype, cols) * rows
     deq = oracle.dequantize(qtype, blob, rows, cols)
     err = np.sqrt(np.mean((deq - w) ** 2)) / np.sqrt(np.mean(w ** 2))
-    assert err < {8: 0.01, 2: 0.15, 12: 0.15, 42: 1.0}[qtype]
+    assert err < {8: 0.01, 2: 0.15, 12: 0.15, 14: 0.05, 42: 1.0}[qtype]
     # re-encoding a decoded matrix is stable for the byte-exact types
     if qtype == 8:
         assert np.array_equal(oracle.quantize(qtype, deq), blob)
@@ -120,6 +120,43 @@ def test_q4_k_scale_packing(oracle):
     q = blob[4:16]
     sc = [(q[j] & 63) if j < 4 else ((q[j + 4] & 0xF) | ((q[j - 4] >> 6) << 4)) for j in range(8)]
     assert max(sc) <= 63 and max(sc) >= 60  # the largest scale uses the full 6-bit range
+
+
+def _q6_k_block_published(blk):
+    """Public GGUF Q6_K decode, written per 128-element half: for l < 32 the four codes of
+    elements l, l+32, l+64, l+96 come from ql[l] / ql[l+32] (low, low, high, high nibble) and
+    qh[l] (bit pairs 0, 2, 4, 6); scales is + 0, 2, 4, 6 with is = l // 16; y = (d * sc) * (q - 32)."""
+    d = np.float32(np.frombuffer(bytes(blk[208:210]), np.float16)[0])
+    sc = np.frombuffer(bytes(blk[192:208]), np.int8)
+    y = np.empty(256, np.float32)
+    for n in range(2):
+        ql, qh, s = blk[64 * n:64 * n + 64], blk[128 + 32 * n:160 + 32 * n], sc[8 * n:8 * n + 8]
+        for l in range(32):
+            is_ = l // 16
+            codes = [(ql[l] & 15) | ((qh[l] & 3) << 4), (ql[l + 32] & 15) | (((qh[l] >> 2) & 3) << 4),
+                     (ql[l] >> 4) | (((qh[l] >> 4) & 3) << 4), (ql[l + 32] >> 4) | (((qh[l] >> 6) & 3) << 4)]
+            for k in range(4):
+                y[128 * n + l + 32 * k] = (d * np.float32(s[is_ + 2 * k])) * np.float32(int(codes[k]) - 32)
+    return y
+
+
+def test_q6_k_random_blocks_decode_as_published(oracle):
+    # Arbitrary bytes (any f16 d that is finite, any int8 scales, every code) decode bit-exactly.
+    rng = np.random.default_rng(14)
+    blk = rng.integers(0, 256, (4, 210), dtype=np.uint8)
+    blk[:, 208:210] = np.frombuffer(np.float16([0.01, -0.5, 3e-5, 7.0]).tobytes(), np.uint8).reshape(4, 2)
+    for b in range(4):
+        got = oracle.gather_row(oracle.Q6_K, blk[b].copy(), 1, 256, 0)
+        assert np.array_equal(got.view(np.uint32), _q6_k_block_published(blk[b]).view(np.uint32))
+
+
+def test_q6_k_encoder_uses_the_code_range(oracle):
+    rng = np.random.default_rng(3)
+    w = (rng.standard_normal((1, 256)) * 0.05).astype(np.float32)
+    blob = oracle.quantize(oracle.Q6_K, w)
+    assert np.abs(oracle.dequantize(oracle.Q6_K, blob, 1, 256) - w).max() < 0.01
+    sc = blob[192:208].view(np.int8)
+    assert np.abs(sc).max() == 127
 
 
 def test_kat_elementwise_sum_matmul(oracle):

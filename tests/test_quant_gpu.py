@@ -8,8 +8,8 @@ import numpy as np
 import pytest
 import torch
 
-Q4_0, Q8_0, Q4_K, Q2_0 = 2, 8, 12, 42
-TYPES = [Q8_0, Q4_0, Q4_K, Q2_0]
+Q4_0, Q8_0, Q4_K, Q6_K, Q2_0 = 2, 8, 12, 14, 42
+TYPES = [Q8_0, Q4_0, Q4_K, Q6_K, Q2_0]
 REL = 1e-4
 
 pytestmark = pytest.mark.gpu
@@ -31,6 +31,7 @@ SHAPES = {
     Q8_0: [(37, 96), (1, 32), (64, 1056), (130, 2080)],
     Q4_0: [(37, 96), (1, 32), (64, 1056), (130, 2080)],
     Q4_K: [(21, 256), (1, 512), (48, 1280), (130, 2304)],
+    Q6_K: [(21, 256), (1, 512), (48, 1280), (130, 2304)],
     Q2_0: [(37, 128), (1, 384), (64, 1152), (130, 2176)],
 }
 
@@ -104,7 +105,7 @@ def test_invalid_geometry_rejected(backend, oracle):
     with pytest.raises(ValueError, match="bytes"):
         backend.upload_quantized(np.zeros(30, np.uint8), Q8_0, (1, 32))
     with pytest.raises(NotImplementedError):
-        backend.upload_quantized(np.zeros(210, np.uint8), 14, (1, 256))
+        backend.upload_quantized(np.zeros(34, np.uint8), 41, (1, 256))
 
 
 @pytest.mark.parametrize("qtype,rows,cols,batch", [
@@ -112,6 +113,7 @@ def test_invalid_geometry_rejected(backend, oracle):
     (Q4_K, 14336, 4096, 1),    # BASELINE config 3, decode
     (Q4_K, 14336, 4096, 16),   # BASELINE config 3, batch 16
     (Q4_0, 4096, 14336, 4),    # config 5 down-projection shape
+    (Q6_K, 4096, 14336, 8),    # Q6_K output/down projections of GGUF Q4_K_M files
 ])
 def test_baseline_sizes(backend, oracle, qtype, rows, cols, batch):
     """Full BASELINE shapes: device-encoded weights, checked against the float64 oracle."""
