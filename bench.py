@@ -102,7 +102,7 @@ DEC_D, DEC_HEADS, DEC_FFN = 4096, 32, 14336
 # default timed steps and warm-up per workload family (a GEMV call is microseconds, a prefill
 # step tens of milliseconds)
 DEFAULT_STEPS = {"gemv": (20000, 200), "tape": (20000, 200), "gemm": (100, 5), "decoder_decode": (200, 5),
-                 "decoder_prefill": (10, 3)}
+                 "decoder_prefill": (10, 3), "aad": (20, 3), "aad_eager": (5, 3)}
 
 
 def decoder_weight_bytes():
@@ -440,6 +440,8 @@ def run_reference_gemm(args):
 
 
 def run_reference(args):
+    if args.config in AAD_CONFIGS:
+        return run_reference_aad(args)
     if args.config in DECODER_CONFIGS:
         return run_reference_decoder(args)
     if args.config in TAPE_CONFIGS:
@@ -919,6 +921,208 @@ def run_engine_gemm(args):
 
 
 # ------------------------------------------------------------------------------------------------
+# scalar-AAD Monte-Carlo replay (the AadEngine SPI's CUDA engines)
+# ------------------------------------------------------------------------------------------------
+
+AAD_CONFIGS = {
+    # name: (engine, paths per step, label)
+    "aad_asian": ("cuda", 1 << 24, "scalar-AAD replay, engine cuda (generated kernel), FLOAT32: 64-step "
+                  "arithmetic Asian call under GBM (408 nodes, 64 normal draws), value + 5 adjoints"),
+    "aad_asian_interp": ("cuda-interp", 1 << 24, "scalar-AAD replay, engine cuda-interp (fixed interpreter), "
+                         "FLOAT32: 64-step arithmetic Asian call under GBM, value + 5 adjoints"),
+    "aad_asian_eager": ("cuda-eager", 1 << 21, "scalar-AAD replay, engine cuda-eager (one launch per node), "
+                        "FLOAT32: 64-step arithmetic Asian call under GBM, value + 5 adjoints"),
+}
+AAD_STEPS = 64
+
+
+def asian_tape(steps=AAD_STEPS):
+    """Arithmetic-average Asian call under geometric Brownian motion (log-Euler steps):
+    exp(-r T) max(mean_t S_t - K, 0); inputs S0, K, sigma, r, T."""
+    from jax4j_b200.aad import AadRecorder
+
+    def body(rec):
+        s0, k, sig, r, t = (rec.input(n, v) for n, v in
+                            (("S0", 100.0), ("K", 100.0), ("sigma", 0.2), ("r", 0.05), ("T", 1.0)))
+        dt = t / steps
+        drift = (r - sig * sig * 0.5) * dt
+        vol = sig * dt.sqrt()
+        s, total = s0, rec.constant(0.0)
+        for _ in range(steps):
+            s = s * (drift + vol * rec.randn()).exp()
+            total = total + s
+        rec.output(((total / steps - k).max(0.0)) * (r.neg() * t).exp())
+    return AadRecorder.record(body)
+
+
+def cpu_aad_rate(tape, budget_s, threads):
+    """The CPU engine's replay (oracle restatement of ScalarReplay, double precision) on
+    `threads` host threads over a sample sized to ~budget_s: paths/s."""
+    sys.path.insert(0, HERE)
+    from oracle import oracle
+    args = (tape.ops, tape.arg_a, tape.arg_b, tape.constants, tape.recorded_inputs(), tape.input_nodes,
+            tape.output_nodes, tape.rand_stream_count())
+    n = 2000 * threads
+    t0 = time.perf_counter()
+    oracle.aad_replay(*args, n, 0, 42, True, threads)
+    probe = time.perf_counter() - t0
+    n = max(n, int(n * budget_s / max(probe, 1e-6)))
+    t0 = time.perf_counter()
+    oracle.aad_replay(*args, n, 0, 42, True, threads)
+    return n / (time.perf_counter() - t0), n
+
+
+def aad_inst_per_path(cfg):
+    """Warp instructions per path of the engine's kernel from the committed ncu summary."""
+    path = os.path.join(HERE, "profiles", f"{cfg}.md")
+    if not os.path.exists(path):
+        return None
+    m = re.search(r"warp_instructions_per_path:\s*([0-9.]+)", open(path).read())
+    return float(m.group(1)) if m else None
+
+
+def run_reference_aad(args):
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return 0
+    engine, _, label = AAD_CONFIGS[args.config]
+    tape = asian_tape()
+    threads = os.cpu_count() or 1
+    K, W = args.steps, max(3, args.warmup)
+    rate, n = cpu_aad_rate(tape, 2.0, threads)  # warm-up + sizing
+    times = []
+    for _ in range(K):
+        t0 = time.perf_counter()
+        sys.path.insert(0, HERE)
+        from oracle import oracle
+        oracle.aad_replay(tape.ops, tape.arg_a, tape.arg_b, tape.constants, tape.recorded_inputs(),
+                          tape.input_nodes, tape.output_nodes, 1, n, 0, 42, True, threads)
+        times.append(time.perf_counter() - t0)
+    sec = sum(times) / len(times)
+    v = n / sec
+    line = {"metric": AAD_METRIC, "value": round(v, 1), "unit": "paths/s", "n_gpus": world, "steps": K,
+            "warmup": W, "ms_per_step": round(sec * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f64", "data": "synthetic", "impl": "reference",
+            "config": {"workload": label.replace("FLOAT32", "FLOAT64 CPU"), "paths_per_step": n},
+            "cpu_baseline": {"value": round(v, 1), "unit": "paths/s", "cores": threads, "kind": "port",
+                             "sample": f"{n} paths per step, oracle restatement of ScalarReplay on {threads} threads"},
+            "e2e": {"value": round(v, 1), "unit": "paths/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+AAD_METRIC = "scalar-AAD Monte-Carlo replay paths/s (value + adjoints of every input)"
+
+
+def run_engine_aad(args):
+    import torch
+    import torch.distributed as dist
+    sys.path.insert(0, HERE)
+    from jax4j_b200.aad import AadEngines, AadOptions, Precision
+    from jax4j_b200.backend import torch_stream
+
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    engine, P, label = AAD_CONFIGS[args.config]
+    tape = asian_tape()
+    exe = AadEngines.require(engine, AadOptions(Precision.FLOAT32), local).compile(tape, AadOptions(Precision.FLOAT32))
+    dev = torch.device("cuda", local)
+    ins = torch.tensor(exe.inputs, dtype=torch.float64, device=dev)
+    sums = torch.zeros(exe.channels, dtype=torch.float64, device=dev)
+    s = torch_stream()
+    K, W = args.steps, max(3, args.warmup)
+    base = rank * (K + W + 8) * P  # disjoint scenario ranges per rank
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for i in range(W):
+        exe.launch(ins.data_ptr(), P, base + i * P, 42, sums.data_ptr(), s)
+    barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        barrier()
+        start.record()
+        for i in range(K):
+            exe.launch(ins.data_ptr(), P, base + (W + i) * P, 42, sums.data_ptr(), s)
+        end.record()
+        barrier()
+    clk = clocks.summary()
+    ms = start.elapsed_time(end)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    step_ms = ms / K
+    value = world * P * K / (ms * 1e-3)
+
+    # end to end through the public call: host inputs up, host sums back, every step
+    e_steps = max(2, min(K, 5))
+    barrier()
+    t0 = time.perf_counter()
+    for i in range(e_steps):
+        r = exe.replay(P, base + i * P, 43)
+    e_sec = time.perf_counter() - t0
+    e2e = world * P * e_steps / e_sec
+    launches_per_step = 1 if engine != "cuda-eager" else None
+    if engine == "cuda-eager":
+        active = int(tape.active.sum())
+        n_rev = sum(1 for i in range(tape.size()) if tape.active[i] and tape.op(i) > 3)
+        chunks = -(-P // exe.threads_or_slot)
+        launches_per_step = chunks * (tape.size() + 2 + 1 + n_rev + tape.input_count())
+        del active
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        rate, n = cpu_aad_rate(tape, 10.0, threads)
+        cpu = {"value": round(rate, 1), "unit": "paths/s", "cores": threads, "kind": "port",
+               "sample": f"{n} paths of the same tape, oracle restatement of ScalarReplay (double) on "
+                         f"{threads} threads"}
+    ipp = aad_inst_per_path(args.config)
+    if rank == 0:
+        clock_hz = (clk["sm_mhz"] or 1965.0) * 1e6
+        sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        peak_issue = sms * 4 * clock_hz / 1e9  # warp instructions per second, 4 schedulers per SM
+        achieved = ipp * P / (step_ms * 1e-3) / 1e9 if ipp else None
+        line = {
+            "metric": AAD_METRIC, "value": round(value, 1), "unit": "paths/s", "n_gpus": world,
+            "steps": K, "warmup": W, "ms_per_step": round(step_ms, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32 (f64 accumulation)", "data": "synthetic",
+            "config": {"workload": label, "engine": engine, "paths_per_step": P, "nodes": tape.size(),
+                       "value_check": round(r.value(), 6), "delta_S0": round(r.gradient("S0"), 6),
+                       "l2": "no memory-resident inputs: draws are generated in-kernel from (path, seed)",
+                       "parallelism": "replica" if world == 1 else f"{world} ranks, disjoint scenario ranges",
+                       "timing": "K back-to-back launches on device buffers, CUDA events, max over ranks"},
+            "roofline": {"bound": "issue", "achieved": round(achieved, 1) if achieved else None,
+                         "peak": round(peak_issue, 1), "unit": "G warp-instructions/s",
+                         "frac": round(achieved / peak_issue, 4) if achieved else None, "traffic": None,
+                         "peak_source": f"{sms} SMs x 4 schedulers x measured median SM clock",
+                         "kernel": {"cuda": "aad_replay (generated)", "cuda-interp": "aad_interp_kernel",
+                                    "cuda-eager": "aad_eager_forward/reverse/reduce"}[engine],
+                         "kernel_avg_us": round(step_ms * 1e3, 1)},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e, 1), "unit": "paths/s", "h2d_bytes_per_step": 8 * tape.input_count(),
+                    "d2h_bytes_per_step": 8 * exe.channels},
+            "gpu_launches": K * launches_per_step,
+            "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"],
+                       "reasons": clk["reasons"], "samples": clk["samples"]},
+        }
+        print(json.dumps(line), flush=True)
+    exe.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+# ------------------------------------------------------------------------------------------------
 # decoder block (BASELINE configs[4])
 # ------------------------------------------------------------------------------------------------
 
@@ -1196,6 +1400,8 @@ def run_engine_decoder(args):
 
 
 def run_engine(args):
+    if args.config in AAD_CONFIGS:
+        return run_engine_aad(args)
     if args.config in DECODER_CONFIGS:
         return run_engine_decoder(args)
     if args.config in TAPE_CONFIGS:
@@ -1389,13 +1595,15 @@ def main():
     p.add_argument("--warmup", type=int, default=None, help="warm-up steps (default per workload)")
     p.add_argument("--impl", choices=["engine", "reference"], default="engine")
     p.add_argument("--config", choices=sorted(CONFIGS) + sorted(TAPE_CONFIGS) + sorted(GEMM_CONFIGS)
-                   + sorted(DECODER_CONFIGS), default="q8_0_b8")
+                   + sorted(DECODER_CONFIGS) + sorted(AAD_CONFIGS), default="q8_0_b8")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--batch", type=int, default=None,
                    help="decoder workloads only: override the batch (e.g. a smaller case for profiling)")
     args = p.parse_args()
     family = ("tape" if args.config in TAPE_CONFIGS else "gemm" if args.config in GEMM_CONFIGS
-              else args.config if args.config in DECODER_CONFIGS else "gemv")
+              else args.config if args.config in DECODER_CONFIGS
+              else ("aad_eager" if args.config == "aad_asian_eager" else "aad") if args.config in AAD_CONFIGS
+              else "gemv")
     steps, warmup = DEFAULT_STEPS[family]
     args.steps = steps if args.steps is None else args.steps
     args.warmup = warmup if args.warmup is None else args.warmup

@@ -294,6 +294,51 @@ int j4b_tape_dryrun(const int64_t* words, size_t nwords, j4b_tape_stats* stats, 
 /* The generated CUDA source of fused kernel `group` (diagnostics). */
 int j4b_tape_source(j4b_tape* tape, int group, char* buf, size_t cap, size_t* len);
 
+/* ---- Scalar-AAD Monte-Carlo replay engines: AadEngine / AadExecutable
+ * (core/engine/AadEngine.java:29-75, AadExecutable.java:34-75; the CUDA engines of
+ * engine/CudaAadEngine.java, CudaInterpEngine.java, CudaEagerEngine.java).
+ *
+ * A tape is n_nodes records (ops[i], arg_a[i], arg_b[i], constants[i]) with op codes the AadOp
+ * ordinals: 0 CONST, 1 INPUT (arg_a = input index), 2 RANDN (arg_a = draw ordinal, arg_b =
+ * stream), 3 RANDU, 4 ADD, 5 SUB, 6 MUL, 7 DIV, 8 NEG, 9 EXP, 10 LOG, 11 SQRT, 12 MAX, 13 MIN,
+ * 14 ABS; arguments name earlier nodes. input_nodes[j] is the INPUT node of input j and
+ * output_node the single output. RANDU and named streams return J4B_EUNSUPPORTED, as the
+ * reference's CUDA engines decline them (AadEngine.requireBasicRandom).
+ *
+ * engine: J4B_AAD_ENGINE_GENERATED ("cuda": per-tape generated kernel, NVRTC), _INTERP
+ * ("cuda-interp": fixed interpreter kernel; at most 32 inputs), _EAGER ("cuda-eager": one launch
+ * per node). precision: 4 = FLOAT32, 8 = FLOAT64 working precision; accumulation is always f64.
+ * scratch_option: 0 = default; interpreter: threads; eager: scratch budget in bytes.
+ *
+ * A replay of `paths` scenarios starting at `path_offset` (scenario p draws from Philox keyed on
+ * (p, seed), core/engine/cpu/Philox.java) produces sums[0] = sum of the output, sums[1] = sum of
+ * its square and, with adjoints, sums[2 + j] = sum of d output / d input j. j4b_aad_replay takes
+ * host inputs and returns host sums (blocking); j4b_aad_launch takes device inputs and sums and
+ * is stream-ordered. A handle is not safe for concurrent use. */
+#define J4B_AAD_ENGINE_GENERATED 0
+#define J4B_AAD_ENGINE_INTERP 1
+#define J4B_AAD_ENGINE_EAGER 2
+typedef struct j4b_aad* j4b_aad_t;
+int j4b_aad_compile(int dev, int engine, int n_nodes, const int32_t* ops, const int32_t* arg_a,
+                    const int32_t* arg_b, const double* constants, int n_inputs,
+                    const int32_t* input_nodes, int output_node, int precision, int adjoints,
+                    int64_t scratch_option, j4b_aad_t* out);
+int j4b_aad_replay(j4b_aad_t h, const double* inputs, uint64_t paths, uint64_t path_offset,
+                   uint64_t seed, double* sums, j4b_stream s);
+int j4b_aad_launch(j4b_aad_t h, j4b_buf inputs, uint64_t paths, uint64_t path_offset, uint64_t seed,
+                   j4b_buf sums, j4b_stream s);
+/* channels = 2 + inputs (with adjoints) or 2; compile_seconds of the generated kernel (0 for a
+ * cached source and the fixed kernels); threads_or_slot: resident threads (generated),
+ * interpreter threads, or eager scenarios per chunk. */
+int j4b_aad_info(j4b_aad_t h, int* channels, double* compile_seconds, int64_t* threads_or_slot);
+/* The generated kernel's CUDA source (empty for the interpreter and eager engines). */
+int j4b_aad_source(j4b_aad_t h, char* buf, size_t cap, size_t* len);
+int j4b_aad_free(j4b_aad_t h);
+/* Validates a tape, generates its kernel source and compiles it with NVRTC, without a device. */
+int j4b_aad_dryrun(int n_nodes, const int32_t* ops, const int32_t* arg_a, const int32_t* arg_b,
+                   const double* constants, int n_inputs, const int32_t* input_nodes, int output_node,
+                   int precision, int adjoints, char* buf, size_t cap, size_t* len);
+
 #ifdef __cplusplus
 }
 #endif

@@ -42,6 +42,8 @@ _i64 = ctypes.c_int64
 _int = ctypes.c_int
 _vp = ctypes.c_void_p
 _i64p = ctypes.POINTER(ctypes.c_int64)
+_i32p = ctypes.POINTER(ctypes.c_int32)
+_f64p = ctypes.POINTER(ctypes.c_double)
 
 # name -> argtypes (every function returns int status)
 SIGNATURES = {
@@ -111,6 +113,15 @@ SIGNATURES = {
                         ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t)],
     "j4b_tape_source": [_vp, _int, ctypes.c_char_p, ctypes.c_size_t,
                         ctypes.POINTER(ctypes.c_size_t)],
+    "j4b_aad_compile": [_int, _int, _int, _i32p, _i32p, _i32p, _f64p, _int, _i32p, _int, _int, _int,
+                        _i64, ctypes.POINTER(_vp)],
+    "j4b_aad_replay": [_vp, _f64p, _u64, _u64, _u64, _f64p, _vp],
+    "j4b_aad_launch": [_vp, _u64, _u64, _u64, _u64, _u64, _vp],
+    "j4b_aad_info": [_vp, ctypes.POINTER(ctypes.c_int), _f64p, _i64p],
+    "j4b_aad_source": [_vp, ctypes.c_char_p, ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t)],
+    "j4b_aad_free": [_vp],
+    "j4b_aad_dryrun": [_int, _i32p, _i32p, _i32p, _f64p, _int, _i32p, _int, _int, _int,
+                       ctypes.c_char_p, ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t)],
 }
 
 _lib = None

@@ -22,7 +22,10 @@ INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
-              "-I", INCLUDE]
+              "-I", INCLUDE, "-I", BUILD]
+# Device headers that are also compiled at run time (NVRTC) are embedded as string literals:
+# csrc/<name>.cuh -> _build/<name>.inc
+EMBEDDED = ["aad_device.cuh"]
 
 
 def nvcc() -> str:
@@ -65,11 +68,23 @@ def _compile(src: str, verbose: bool, extra: list[str]) -> str:
     return obj
 
 
+def _embed() -> None:
+    for name in EMBEDDED:
+        text = open(os.path.join(CSRC, name)).read()
+        assert ')J4B"' not in text
+        body = 'R"J4B(' + text + ')J4B"\n'
+        target = os.path.join(BUILD, name.rsplit(".", 1)[0] + ".inc")
+        if not os.path.exists(target) or open(target).read() != body:
+            with open(target, "w") as f:
+                f.write(body)
+
+
 def build(force: bool = False, verbose: bool = False, extra: list[str] | None = None) -> str:
     os.makedirs(BUILD, exist_ok=True)
     if force:
         for f in os.listdir(BUILD):
             os.remove(os.path.join(BUILD, f))
+    _embed()
     srcs = sources()
     with concurrent.futures.ThreadPoolExecutor(max_workers=min(8, len(srcs))) as ex:
         objs = list(ex.map(lambda s: _compile(s, verbose, extra or []), srcs))

@@ -35,6 +35,7 @@
 #include <vector>
 
 #include "j4b_internal.h"
+#include "j4b_rtc.h"
 
 namespace j4b {
 namespace {
@@ -1024,85 +1025,6 @@ template <int NT, int MODE> __device__ __forceinline__ long long block_pair(floa
   return bi;
 }
 )PRELUDE";
-
-// Driver entry points, resolved through the runtime so the library loads on machines without
-// a driver (CPU build and planning checks).
-struct Driver {
-  PFN_cuModuleLoadData_v2000 ModuleLoadData = nullptr;
-  PFN_cuModuleGetFunction_v2000 ModuleGetFunction = nullptr;
-  PFN_cuModuleUnload_v2000 ModuleUnload = nullptr;
-  PFN_cuFuncSetAttribute_v9000 FuncSetAttribute = nullptr;
-  PFN_cuOccupancyMaxActiveBlocksPerMultiprocessor_v6050 Occupancy = nullptr;
-  PFN_cuLaunchKernel_v4000 LaunchKernel = nullptr;
-  PFN_cuGetErrorName_v6000 GetErrorName = nullptr;
-  bool ok = false;
-};
-
-const Driver& driver() {
-  static Driver d;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    auto get = [](const char* name, void** fn) {
-      cudaDriverEntryPointQueryResult q;
-      return cudaGetDriverEntryPointByVersion(name, fn, 12000, cudaEnableDefault, &q) == cudaSuccess &&
-             q == cudaDriverEntryPointSuccess && *fn != nullptr;
-    };
-    d.ok = get("cuModuleLoadData", (void**)&d.ModuleLoadData) &&
-           get("cuModuleGetFunction", (void**)&d.ModuleGetFunction) &&
-           get("cuModuleUnload", (void**)&d.ModuleUnload) &&
-           get("cuFuncSetAttribute", (void**)&d.FuncSetAttribute) &&
-           get("cuOccupancyMaxActiveBlocksPerMultiprocessor", (void**)&d.Occupancy) &&
-           get("cuLaunchKernel", (void**)&d.LaunchKernel) &&
-           get("cuGetErrorName", (void**)&d.GetErrorName);
-  });
-  return d;
-}
-
-std::mutex g_nvrtc_mu;
-std::unordered_map<std::string, std::vector<char>>& cubin_cache() {
-  static std::unordered_map<std::string, std::vector<char>> c;
-  return c;
-}
-
-int compile_source(const std::string& src, std::vector<char>& cubin) {
-  {
-    std::lock_guard<std::mutex> lk(g_nvrtc_mu);
-    auto it = cubin_cache().find(src);
-    if (it != cubin_cache().end()) {
-      cubin = it->second;
-      return J4B_OK;
-    }
-  }
-  nvrtcProgram prog;
-  if (nvrtcCreateProgram(&prog, src.c_str(), "j4b_tape.cu", 0, nullptr, nullptr) != NVRTC_SUCCESS)
-    return set_error(J4B_ECUDA, "nvrtcCreateProgram failed");
-  const char* opts[] = {"--gpu-architecture=sm_100a", "-std=c++17", "--fmad=false",
-                        "-default-device", "-lineinfo"};
-  nvrtcResult r = nvrtcCompileProgram(prog, 5, opts);
-  if (r != NVRTC_SUCCESS) {
-    size_t ls = 0;
-    nvrtcGetProgramLogSize(prog, &ls);
-    std::string log(ls, '\0');
-    nvrtcGetProgramLog(prog, &log[0]);
-    nvrtcDestroyProgram(&prog);
-    return set_error(J4B_ECUDA, "tape kernel compilation failed: %s", log.substr(0, 900).c_str());
-  }
-  size_t n = 0;
-  nvrtcGetCUBINSize(prog, &n);
-  cubin.resize(n);
-  nvrtcGetCUBIN(prog, cubin.data());
-  nvrtcDestroyProgram(&prog);
-  counters().compilations++;
-  std::lock_guard<std::mutex> lk(g_nvrtc_mu);
-  cubin_cache()[src] = cubin;
-  return J4B_OK;
-}
-
-int cu_error(CUresult r, const char* what) {
-  const char* name = nullptr;
-  if (driver().GetErrorName) driver().GetErrorName(r, &name);
-  return set_error(J4B_ECUDA, "%s failed: %s (code %d)", what, name ? name : "?", (int)r);
-}
 
 // ---------------------------------------------------------------------------------------------
 // code generation for one group
@@ -2206,7 +2128,7 @@ extern "C" int j4b_tape_dryrun(const int64_t* words, size_t nwords, j4b_tape_sta
   std::string all;
   for (size_t g = 0; g < codes.size(); ++g) {
     std::vector<char> cubin;
-    st = compile_source(codes[g].src, cubin);
+    st = compile_source(codes[g].src, "j4b_tape.cu", cubin);
     if (st) return st;
     all += "// ---- group " + std::to_string(g) + " ----\n" + codes[g].src;
   }
@@ -2257,7 +2179,7 @@ extern "C" int j4b_tape_compile(int dev, const int64_t* words, size_t nwords, j4
   for (size_t g = 0; g < tp->groups.size(); ++g) {
     j4b_tape::GroupRun& run = tp->runs[g];
     std::vector<char> cubin;
-    st = compile_source(codes[g].src, cubin);
+    st = compile_source(codes[g].src, "j4b_tape.cu", cubin);
     if (st) return st;
     CUresult r = driver().ModuleLoadData(&run.mod, cubin.data());
     if (r != CUDA_SUCCESS) return cu_error(r, "cuModuleLoadData");

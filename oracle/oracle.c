@@ -790,3 +790,176 @@ int j4o_fused(const int32_t* prog, int prog_len, const float* const* inputs, int
   }
   return 0;
 }
+
+/* ------------------------------------------------------------------------------------------
+ * Scalar-AAD replay (test infrastructure): the CPU engine's Monte-Carlo replay of a recorded
+ * scalar tape, one scenario at a time, forward then reverse, in double precision.
+ *
+ * Philox2x32-10 keyed on the scenario: core/engine/cpu/Philox.java:30-94. lo = (int) path ^
+ * (int) seed, hi = (int) (path >>> 32) ^ (int) (seed >>> 32), stream s != 0 folds s *
+ * 0x9E3779B1 into hi. normal(): Philox of (lo, hi ^ counter++) -> Box-Muller pair, cosine leg
+ * returned first and the sine leg on the next call; uniform(): counter (ucounter++ | 0x40000000).
+ * Replay: core/engine/cpu/ScalarReplay.java:145-232 (forward switch, adjoint switch with the
+ * active-node skip, per-output value / value^2 / gradient sums); active flags as
+ * core/engine/AadTape.java:61-74. Op codes are AadOp ordinals (core/engine/AadOp.java:22-37).
+ * ------------------------------------------------------------------------------------------ */
+enum { AAD_CONST, AAD_INPUT, AAD_RANDN, AAD_RANDU, AAD_ADD, AAD_SUB, AAD_MUL, AAD_DIV, AAD_NEG,
+       AAD_EXP, AAD_LOG, AAD_SQRT, AAD_MAX, AAD_MIN, AAD_ABS };
+
+typedef struct {
+  uint32_t lo, hi, counter, ucounter;
+  double spare;
+  int has;
+} philox_t;
+
+static void philox_rounds_key(uint32_t* c0, uint32_t* c1, uint32_t key) {
+  for (int i = 0; i < 10; i++) {
+    uint64_t product = (uint64_t)0xD256D193u * (uint64_t)*c0;
+    uint32_t high = (uint32_t)(product >> 32), low = (uint32_t)product;
+    *c0 = high ^ key ^ *c1;
+    *c1 = low;
+    key += 0x9E3779B9u;
+  }
+}
+/* The replay's generator always starts from key 0x1BD11BDA (Philox.java:56). */
+static void philox_rounds(uint32_t* c0, uint32_t* c1) { philox_rounds_key(c0, c1, 0x1BD11BDAu); }
+
+static void philox_init(philox_t* g, int64_t path, int64_t seed, int stream) {
+  g->lo = (uint32_t)path ^ (uint32_t)seed;
+  g->hi = (uint32_t)((uint64_t)path >> 32) ^ (uint32_t)((uint64_t)seed >> 32);
+  if (stream != 0) g->hi ^= (uint32_t)stream * 0x9E3779B1u;
+  g->counter = g->ucounter = 0;
+  g->has = 0;
+  g->spare = 0.0;
+}
+
+static const double kUintScale = 2.3283064365386963e-10;
+
+static double philox_normal(philox_t* g) {
+  if (g->has) {
+    g->has = 0;
+    return g->spare;
+  }
+  uint32_t c0 = g->lo, c1 = g->hi ^ g->counter++;
+  philox_rounds(&c0, &c1);
+  double u1 = ((double)c0 + 0.5) * kUintScale;
+  double u2 = ((double)c1 + 0.5) * kUintScale;
+  double radius = sqrt(-2.0 * log(u1));
+  double angle = 6.283185307179586 * u2;
+  g->spare = radius * sin(angle);
+  g->has = 1;
+  return radius * cos(angle);
+}
+
+static double philox_uniform(philox_t* g) {
+  uint32_t c0 = g->lo, c1 = g->hi ^ (g->ucounter++ | 0x40000000u);
+  philox_rounds(&c0, &c1);
+  return ((double)c0 + 0.5) * kUintScale;
+}
+
+/* java.lang.Math.max / min on doubles: NaN if either is NaN; +0.0 above -0.0. */
+static double java_max_d(double a, double b) {
+  if (a != a) return a;
+  if (b != b) return b;
+  if (a == 0.0 && b == 0.0) return signbit(a) ? b : a;
+  return a >= b ? a : b;
+}
+static double java_min_d(double a, double b) {
+  if (a != a) return a;
+  if (b != b) return b;
+  if (a == 0.0 && b == 0.0) return signbit(a) ? a : b;
+  return a <= b ? a : b;
+}
+
+int j4o_aad_replay(int n, const int32_t* op, const int32_t* arg_a, const int32_t* arg_b,
+                   const double* constant, const double* inputs, int n_in, const int32_t* in_nodes,
+                   int n_out, const int32_t* out_nodes, int n_streams, int adjoints, int64_t path_from,
+                   int64_t count, int64_t seed, double* value, double* sumsq, double* grad) {
+  if (n <= 0 || n_out <= 0 || n_streams <= 0) return -1;
+  double* v = (double*)calloc((size_t)n, sizeof(double));
+  double* d = (double*)calloc((size_t)n, sizeof(double));
+  unsigned char* active = (unsigned char*)calloc((size_t)n, 1);
+  philox_t* rng = (philox_t*)calloc((size_t)n_streams, sizeof(philox_t));
+  if (!v || !d || !active || !rng) {
+    free(v); free(d); free(active); free(rng);
+    return -2;
+  }
+  for (int i = 0; i < n; i++) {
+    switch (op[i]) {
+      case AAD_INPUT: active[i] = 1; break;
+      case AAD_CONST: case AAD_RANDN: case AAD_RANDU: active[i] = 0; break;
+      case AAD_NEG: case AAD_EXP: case AAD_LOG: case AAD_SQRT: case AAD_ABS: active[i] = active[arg_a[i]]; break;
+      default: active[i] = active[arg_a[i]] || active[arg_b[i]];
+    }
+  }
+  for (int o = 0; o < n_out; o++) {
+    value[o] = 0.0;
+    sumsq[o] = 0.0;
+    for (int j = 0; j < n_in; j++) grad[o * n_in + j] = 0.0;
+  }
+  for (int64_t path = path_from; path < path_from + count; path++) {
+    for (int s = 0; s < n_streams; s++) philox_init(&rng[s], path, seed, s);
+    for (int i = 0; i < n; i++) {
+      const int a = arg_a[i], b = arg_b[i];
+      double r = 0.0;
+      switch (op[i]) {
+        case AAD_CONST: r = constant[i]; break;
+        case AAD_INPUT: r = inputs[a]; break;
+        case AAD_RANDN: r = philox_normal(&rng[b]); break;
+        case AAD_RANDU: r = philox_uniform(&rng[b]); break;
+        case AAD_ADD: r = v[a] + v[b]; break;
+        case AAD_SUB: r = v[a] - v[b]; break;
+        case AAD_MUL: r = v[a] * v[b]; break;
+        case AAD_DIV: r = v[a] / v[b]; break;
+        case AAD_NEG: r = -v[a]; break;
+        case AAD_EXP: r = exp(v[a]); break;
+        case AAD_LOG: r = log(v[a]); break;
+        case AAD_SQRT: r = sqrt(v[a]); break;
+        case AAD_ABS: r = fabs(v[a]); break;
+        case AAD_MAX: r = java_max_d(v[a], v[b]); break;
+        case AAD_MIN: r = java_min_d(v[a], v[b]); break;
+      }
+      v[i] = r;
+    }
+    for (int o = 0; o < n_out; o++) {
+      const double y = v[out_nodes[o]];
+      value[o] += y;
+      sumsq[o] += y * y;
+    }
+    if (!adjoints) continue;
+    for (int o = 0; o < n_out; o++) {
+      memset(d, 0, (size_t)n * sizeof(double));
+      d[out_nodes[o]] = 1.0;
+      for (int i = n - 1; i >= 0; i--) {
+        const double adj = d[i];
+        if (adj == 0.0 || !active[i]) continue;
+        const int a = arg_a[i], b = arg_b[i];
+        switch (op[i]) {
+          case AAD_ADD: d[a] += adj; d[b] += adj; break;
+          case AAD_SUB: d[a] += adj; d[b] -= adj; break;
+          case AAD_MUL: d[a] += adj * v[b]; d[b] += adj * v[a]; break;
+          case AAD_DIV: d[a] += adj / v[b]; d[b] -= adj * v[i] / v[b]; break;
+          case AAD_NEG: d[a] -= adj; break;
+          case AAD_EXP: d[a] += adj * v[i]; break;
+          case AAD_LOG: d[a] += adj / v[a]; break;
+          case AAD_SQRT: d[a] += adj * 0.5 / v[i]; break;
+          case AAD_ABS: d[a] += v[a] < 0.0 ? -adj : adj; break;
+          case AAD_MAX: if (v[a] >= v[b]) d[a] += adj; else d[b] += adj; break;
+          case AAD_MIN: if (v[a] <= v[b]) d[a] += adj; else d[b] += adj; break;
+          default: break;
+        }
+      }
+      for (int j = 0; j < n_in; j++) grad[o * n_in + j] += d[in_nodes[j]];
+    }
+  }
+  free(v); free(d); free(active); free(rng);
+  return 0;
+}
+
+/* One Philox2x32-10 block (10 rounds on counter (c0, c1) from `key`), exposed for known-answer
+ * checks against the published Random123 vectors. */
+void j4o_philox2x32_10(uint32_t c0, uint32_t c1, uint32_t key, uint32_t* out0, uint32_t* out1) {
+  philox_rounds_key(&c0, &c1, key);
+  *out0 = c0;
+  *out1 = c1;
+}

@@ -94,6 +94,16 @@ void j4o_relu_backward(const float* up, const float* in, int64_t n, float* out);
 int j4o_fused(const int32_t* prog, int prog_len, const float* const* inputs, int n_inputs,
               int64_t n, float* out);
 
+/* Scalar-AAD Monte-Carlo replay (core/engine/cpu/ScalarReplay.java:145-232, Philox.java:30-94):
+ * paths [path_from, path_from + count) of a tape of n nodes (op codes = AadOp ordinals; RANDN /
+ * RANDU: arg_a = ordinal, arg_b = stream). Fills per output o: value[o] = sum of y, sumsq[o] =
+ * sum of y^2, grad[o * n_in + j] = sum of dy/d input j (when adjoints). Returns 0 on success. */
+int j4o_aad_replay(int n, const int32_t* op, const int32_t* arg_a, const int32_t* arg_b,
+                   const double* constant, const double* inputs, int n_in, const int32_t* in_nodes,
+                   int n_out, const int32_t* out_nodes, int n_streams, int adjoints, int64_t path_from,
+                   int64_t count, int64_t seed, double* value, double* sumsq, double* grad);
+void j4o_philox2x32_10(uint32_t c0, uint32_t c1, uint32_t key, uint32_t* out0, uint32_t* out1);
+
 #ifdef __cplusplus
 }
 #endif

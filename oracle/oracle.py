@@ -90,6 +90,11 @@ def _declare(L):
     L.j4o_relu_backward.argtypes = [_f32p, _f32p, _i64, _f32p]
     L.j4o_fused.argtypes = [_i32p, ctypes.c_int, ctypes.POINTER(_f32p), ctypes.c_int, _i64,
                             _f32p]
+    L.j4o_aad_replay.argtypes = [ctypes.c_int, _i32p, _i32p, _i32p, _f64p, _f64p, ctypes.c_int, _i32p,
+                                 ctypes.c_int, _i32p, ctypes.c_int, ctypes.c_int, _i64, _i64, _i64,
+                                 _f64p, _f64p, _f64p]
+    L.j4o_philox2x32_10.argtypes = [ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32,
+                                    ctypes.POINTER(ctypes.c_uint32), ctypes.POINTER(ctypes.c_uint32)]
 
 
 def _p(a, t=_f32p):
@@ -336,3 +341,51 @@ def scalar_words(value: float) -> list[int]:
     """Splits a double into the two int32 words a scalar op carries in a postfix program."""
     lo, hi = struct.unpack("<ii", struct.pack("<d", value))
     return [lo, hi]
+
+
+# ---- scalar-AAD Monte-Carlo replay (the CPU engine, ScalarReplay) ----
+
+def philox2x32_10(c0: int, c1: int, key: int = 0x1BD11BDA) -> tuple[int, int]:
+    o0, o1 = ctypes.c_uint32(), ctypes.c_uint32()
+    lib().j4o_philox2x32_10(c0 & 0xFFFFFFFF, c1 & 0xFFFFFFFF, key & 0xFFFFFFFF, ctypes.byref(o0),
+                            ctypes.byref(o1))
+    return o0.value, o1.value
+
+
+def aad_replay(ops, arg_a, arg_b, constants, inputs, input_nodes, output_nodes, n_streams, paths,
+               path_offset, seed, adjoints=True, threads=1):
+    """Sums over scenarios [path_offset, path_offset + paths): per output the value sum and the
+    value^2 sum, and [output][input] the adjoint sums. With threads > 1 the range is split into
+    contiguous runs as ScalarReplay.runParallel does (ctypes releases the GIL during each run)."""
+    ops, a, b = (np.ascontiguousarray(v, np.int32) for v in (ops, arg_a, arg_b))
+    cst = np.ascontiguousarray(constants, np.float64)
+    ins = np.ascontiguousarray(inputs if len(inputs) else [0.0], np.float64)
+    inn = np.ascontiguousarray(input_nodes if len(input_nodes) else [0], np.int32)
+    outn = np.ascontiguousarray(output_nodes, np.int32)
+    n_in, n_out = len(input_nodes), len(outn)
+
+    def run(frm, count):
+        v, sq = np.zeros(n_out), np.zeros(n_out)
+        g = np.zeros(max(1, n_out * n_in))
+        rc = lib().j4o_aad_replay(len(ops), _p(ops, _i32p), _p(a, _i32p), _p(b, _i32p), _p(cst, _f64p),
+                                  _p(ins, _f64p), n_in, _p(inn, _i32p), n_out, _p(outn, _i32p),
+                                  n_streams, int(bool(adjoints)), frm, count, seed & 0xFFFFFFFFFFFFFFFF
+                                  if seed < 2 ** 63 else seed - 2 ** 64, _p(v, _f64p), _p(sq, _f64p),
+                                  _p(g, _f64p))
+        if rc:
+            raise ValueError("invalid tape")
+        return v, sq, g[:n_out * n_in].reshape(n_out, n_in)
+
+    threads = max(1, min(threads, paths))
+    if threads == 1:
+        return run(path_offset, paths)
+    from concurrent.futures import ThreadPoolExecutor
+    each, extra = divmod(paths, threads)
+    runs, cur = [], path_offset
+    for t in range(threads):
+        c = each + (1 if t < extra else 0)
+        runs.append((cur, c))
+        cur += c
+    with ThreadPoolExecutor(threads) as ex:
+        parts = list(ex.map(lambda r: run(*r), runs))
+    return tuple(sum(p[i] for p in parts) for i in range(3))
