@@ -24,6 +24,7 @@
 
 #include <algorithm>
 #include <chrono>
+#include <queue>
 #include <cmath>
 #include <cstring>
 #include <sstream>
@@ -55,8 +56,16 @@ __host__ __device__ inline bool is_binary(int op) {
 }
 
 // ---------------------------------------------------------------------------------------------
-// interpreter: node record {op, a, b, flags}; flags bit 0 = node active, bit 1 = a active,
-// bit 2 = b active (only active rows are cleared and written in the reverse sweep)
+// interpreter. The tape is planned on the host into slots: a value occupies a slot from its
+// definition to its last use (forward operand, reverse-sweep operand, or the output read), an
+// adjoint from its first contribution (an assignment, so no slot is ever cleared) to the node's
+// own reverse step; slots are reused by linear scan. Per-thread state is (value + adjoint slots)
+// x element size, which for most tapes fits shared memory ([slot][thread], conflict-free);
+// larger tapes use the same layout in global memory. Two int4 per node:
+//   r0 = {op | flags << 8, value slot (-1: never read), slot of a (leaf: aux), slot of b}
+//   r1 = {adjoint slot of the node, adjoint slot of a (-1: none), of b, unused}
+// flags: 1 = swept in the reverse pass, 2 = first contribution to a, 4 = first to b;
+// aux: CONST constant index, INPUT input index, RANDN draw ordinal.
 // ---------------------------------------------------------------------------------------------
 template <typename real>
 __device__ __forceinline__ real unary_fwd(int op, real x);
@@ -92,7 +101,7 @@ __device__ __forceinline__ real binary_fwd(int op, real x, real y) {
   }
 }
 
-// Adjoint contributions of node i (value vi, adjoint adj) to its arguments.
+// Adjoint contributions of node i (value vi, adjoint adj) to its arguments (eager engine).
 template <typename real>
 __device__ __forceinline__ void node_adjoint(int op, real va, real vb, real vi, real adj, real& ga, real& gb) {
   ga = 0;
@@ -113,13 +122,41 @@ __device__ __forceinline__ void node_adjoint(int op, real va, real vb, real vi, 
   }
 }
 
-template <typename real>
+constexpr int kSwept = 0x100, kFirstA = 0x200, kFirstB = 0x400;
+constexpr unsigned kNoSlot = 0xFFFFu;
+constexpr int kInterpMaxNodes = 0xFFFE;  // node indices and slots are 16-bit in the records
+
+// One interpreter step per node, packed in 16 bytes (16-bit slots, kNoSlot = none):
+//   x = op | flags << 8 | value slot << 16       y = slot of a (leaf: aux) | slot of b << 16
+//   z = adjoint slot of the node | of a << 16     w = adjoint slot of b
+// flags: kSwept (reverse step), kFirstA / kFirstB (first contribution: assign, not add);
+// aux: CONST constant index, INPUT input index, RANDN draw ordinal.
+// SMEM: slots and records live in dynamic shared memory ([slot][thread], 32-bit addressing);
+// otherwise slots are [slot][thread] in global scratch with T threads and records are read
+// through the read-only cache.
+template <typename real, bool SMEM>
 __global__ void __launch_bounds__(J4B_AAD_BLOCK) aad_interp_kernel(
-    const int4* __restrict__ nodes, const double* __restrict__ consts, const double* __restrict__ inputs,
-    const int* __restrict__ in_nodes, int n, int n_in, int out, int adjoints, unsigned long long n_paths,
-    unsigned long long offset, unsigned long long seed, real* __restrict__ vs, real* __restrict__ ds,
+    const int4* __restrict__ rec, const double* __restrict__ consts, const double* __restrict__ inputs,
+    const int* __restrict__ in_dslot, int n, int n_in, int out_vslot, int out_dslot, int nv, int nd, int adjoints,
+    unsigned long long n_paths, unsigned long long offset, unsigned long long seed, real* __restrict__ gscratch,
     unsigned long long T, double* partials, unsigned int* ticket, double* sums) {
+  extern __shared__ __align__(16) unsigned char j4b_interp_smem[];
   const unsigned long long tid = (unsigned long long)blockIdx.x * blockDim.x + threadIdx.x;
+  real* sv = reinterpret_cast<real*>(j4b_interp_smem);
+  const unsigned bd = blockDim.x, tx = threadIdx.x;
+  const int4* R = rec;
+  if constexpr (SMEM) {
+    int4* srec = reinterpret_cast<int4*>(sv + (size_t)(nv + nd) * bd);
+    for (int i = tx; i < n; i += bd) srec[i] = rec[i];
+    __syncthreads();
+    R = srec;
+  }
+  real* gv = gscratch + tid;
+  auto VAL = [&](unsigned s) -> real& {
+    if constexpr (SMEM) return sv[s * bd + tx];
+    else return gv[(unsigned long long)s * T];
+  };
+  auto ADJ = [&](unsigned s) -> real& { return VAL((unsigned)nv + s); };
   double acc[kInterpChannels];
 #pragma unroll
   for (int c = 0; c < kInterpChannels; ++c) acc[c] = 0.0;
@@ -129,47 +166,89 @@ __global__ void __launch_bounds__(J4B_AAD_BLOCK) aad_interp_kernel(
     int pair = -1;
     real zc = 0, zs = 0;
     for (int i = 0; i < n; ++i) {
-      const int4 nd = __ldg(nodes + i);
-      real r;
-      if (nd.x == J4B_AAD_CONST) {
-        r = (real)__ldg(consts + i);
-      } else if (nd.x == J4B_AAD_INPUT) {
-        r = (real)__ldg(inputs + nd.y);
-      } else if (nd.x == J4B_AAD_RANDN) {
-        const int m = nd.y >> 1;
-        if (m != pair) {
-          j4b_normal_pair<real>(lo, hi, (unsigned int)m, zc, zs);
-          pair = m;
+      const int4 r = SMEM ? R[i] : __ldg(R + i);
+      const int op = r.x & 0xff;
+      const unsigned a = (unsigned)r.y & 0xFFFFu, b = (unsigned)r.y >> 16, vs = (unsigned)r.x >> 16;
+      real v;
+      switch (op) {  // dense: one indirect branch
+        case J4B_AAD_CONST: v = (real)__ldg(consts + a); break;
+        case J4B_AAD_INPUT: v = (real)__ldg(inputs + a); break;
+        case J4B_AAD_RANDN: {
+          const int m = (int)(a >> 1);
+          if (m != pair) {
+            j4b_normal_pair<real>(lo, hi, (unsigned int)m, zc, zs);
+            pair = m;
+          }
+          v = (a & 1) ? zs : zc;
+          break;
         }
-        r = (nd.y & 1) ? zs : zc;
-      } else if (is_binary(nd.x)) {
-        r = binary_fwd<real>(nd.x, vs[(unsigned long long)nd.y * T + tid], vs[(unsigned long long)nd.z * T + tid]);
-      } else {
-        r = unary_fwd<real>(nd.x, vs[(unsigned long long)nd.y * T + tid]);
+        case J4B_AAD_ADD: v = VAL(a) + VAL(b); break;
+        case J4B_AAD_SUB: v = VAL(a) - VAL(b); break;
+        case J4B_AAD_MUL: v = VAL(a) * VAL(b); break;
+        case J4B_AAD_DIV: v = VAL(a) / VAL(b); break;
+        case J4B_AAD_NEG: v = -VAL(a); break;
+        case J4B_AAD_EXP: v = unary_fwd<real>(J4B_AAD_EXP, VAL(a)); break;
+        case J4B_AAD_LOG: v = unary_fwd<real>(J4B_AAD_LOG, VAL(a)); break;
+        case J4B_AAD_SQRT: v = unary_fwd<real>(J4B_AAD_SQRT, VAL(a)); break;
+        case J4B_AAD_MAX: v = fmax(VAL(a), VAL(b)); break;
+        case J4B_AAD_MIN: v = fmin(VAL(a), VAL(b)); break;
+        default: v = unary_fwd<real>(J4B_AAD_ABS, VAL(a)); break;
       }
-      vs[(unsigned long long)i * T + tid] = r;
+      if (vs != kNoSlot) VAL(vs) = v;
     }
-    const double y = (double)vs[(unsigned long long)out * T + tid];
+    const double y = (double)VAL((unsigned)out_vslot);
     acc[0] += y;
     acc[1] += y * y;
     if (!adjoints) continue;
-    for (int i = 0; i < n; ++i)
-      if (__ldg(nodes + i).w & 1) ds[(unsigned long long)i * T + tid] = (real)0;
-    if (__ldg(nodes + out).w & 1) ds[(unsigned long long)out * T + tid] = (real)1;
+    if (out_dslot >= 0) ADJ((unsigned)out_dslot) = (real)1;
     for (int i = n - 1; i >= 0; --i) {
-      const int4 nd = __ldg(nodes + i);
-      if (!(nd.w & 1) || nd.x <= J4B_AAD_RANDU) continue;
-      const real adj = ds[(unsigned long long)i * T + tid];
-      const real va = vs[(unsigned long long)nd.y * T + tid];
-      const real vb = is_binary(nd.x) ? vs[(unsigned long long)nd.z * T + tid] : (real)0;
-      real ga, gb;
-      node_adjoint<real>(nd.x, va, vb, vs[(unsigned long long)i * T + tid], adj, ga, gb);
-      if (nd.w & 2) ds[(unsigned long long)nd.y * T + tid] += ga;
-      if (nd.w & 4) ds[(unsigned long long)nd.z * T + tid] += gb;
+      const int4 r = SMEM ? R[i] : __ldg(R + i);
+      if (!(r.x & kSwept)) continue;
+      const int op = r.x & 0xff;
+      const unsigned a = (unsigned)r.y & 0xFFFFu, b = (unsigned)r.y >> 16, vs = (unsigned)r.x >> 16;
+      const unsigned di = (unsigned)r.z & 0xFFFFu, da = (unsigned)r.z >> 16, db = (unsigned)r.w;
+      const real adj = ADJ(di);
+      real ga = 0, gb = 0;
+      switch (op) {
+        case J4B_AAD_ADD: ga = adj; gb = adj; break;
+        case J4B_AAD_SUB: ga = adj; gb = -adj; break;
+        case J4B_AAD_MUL: ga = adj * VAL(b); gb = adj * VAL(a); break;
+        case J4B_AAD_DIV: {
+          const real vb = VAL(b);
+          ga = adj / vb;
+          if (db != kNoSlot) gb = -(adj * VAL(vs) / vb);
+          break;
+        }
+        case J4B_AAD_NEG: ga = -adj; break;
+        case J4B_AAD_EXP: ga = adj * VAL(vs); break;
+        case J4B_AAD_LOG: ga = adj / VAL(a); break;
+        case J4B_AAD_SQRT: ga = adj * (real)0.5 / VAL(vs); break;
+        case J4B_AAD_ABS: ga = VAL(a) < (real)0 ? -adj : adj; break;
+        case J4B_AAD_MAX:
+        case J4B_AAD_MIN: {
+          const real va = VAL(a), vb = VAL(b);
+          const bool take_a = op == J4B_AAD_MAX ? va >= vb : va <= vb;
+          ga = take_a ? adj : (real)0;
+          gb = take_a ? (real)0 : adj;
+          break;
+        }
+        default: break;
+      }
+      if (da != kNoSlot) {
+        real& p = ADJ(da);
+        p = (r.x & kFirstA) ? ga : p + ga;
+      }
+      if (db != kNoSlot) {
+        real& p = ADJ(db);
+        p = (r.x & kFirstB) ? gb : p + gb;
+      }
     }
 #pragma unroll
     for (int j = 0; j < kInterpMaxInputs; ++j)
-      if (j < n_in) acc[2 + j] += (double)ds[(unsigned long long)__ldg(in_nodes + j) * T + tid];
+      if (j < n_in) {
+        const int sl = __ldg(in_dslot + j);
+        if (sl >= 0) acc[2 + j] += (double)ADJ((unsigned)sl);
+      }
   }
   j4b_aad_finish<kInterpChannels>(acc, 2 + (adjoints ? n_in : 0), partials, ticket, sums, false);
 }
@@ -263,14 +342,18 @@ struct j4b_aad {
   CUfunction fn = nullptr;
   int gen_blocks_per_sm = 1;
   double compile_seconds = 0.0;
-  // interpreter
+  // interpreter: slot-planned records, per-input adjoint slots, launch shape
   int4* d_nodes = nullptr;
   double* d_consts = nullptr;
-  int* d_in_nodes = nullptr;
+  int* d_in_nodes = nullptr;  // adjoint slot per input (-1: gradient identically 0)
+  int nv = 0, nd = 0, out_vslot = 0, out_dslot = -1;
+  int interp_block = J4B_AAD_BLOCK;
+  size_t interp_smem = 0;  // dynamic shared memory per CTA; 0 = slots in global scratch
   int64_t interp_threads = 0;
   // eager
   int64_t slot = 0;
-  // scratch: interpreter [node][thread] values + adjoints; eager [node][slot] values + adjoints
+  // scratch: interpreter [slot][thread] values then adjoints (global mode, in vs); eager
+  // [node][scenario] values (vs) and adjoints (ds)
   void* vs = nullptr;
   void* ds = nullptr;
   // common
@@ -315,16 +398,29 @@ std::string generate(const j4b_aad& h) {
        "       path += stride) {\n"
        "    unsigned int lo, hi;\n"
        "    j4b_scenario_key(path + path_offset, seed, lo, hi);\n";
-  std::vector<char> pair_done;
+  // Box-Muller pairs in use; pairs 2g and 2g + 1 are drawn together (interleaved Philox) at the
+  // first use of either.
+  std::vector<char> pair_used, group_done;
+  for (int i = 0; i < h.n; ++i)
+    if (h.op[i] == J4B_AAD_RANDN) {
+      const int m = h.a[i] >> 1;
+      if ((int)pair_used.size() <= m) pair_used.resize(m + 1, 0);
+      pair_used[m] = 1;
+    }
+  pair_used.push_back(0);
+  group_done.assign(pair_used.size() / 2 + 1, 0);
   for (int i = 0; i < h.n; ++i) {
     const int o = h.op[i], a = h.a[i], b = h.b[i];
-    if (o == J4B_AAD_RANDN) {
-      const int m = a >> 1;
-      if ((int)pair_done.size() <= m) pair_done.resize(m + 1, 0);
-      if (!pair_done[m]) {
+    if (o == J4B_AAD_RANDN && !group_done[(a >> 1) / 2]) {
+      const int g = (a >> 1) / 2, m0 = 2 * g, m1 = 2 * g + 1;
+      group_done[g] = 1;
+      if (pair_used[m0] && pair_used[m1]) {
+        s << "    real zc" << m0 << ", zs" << m0 << ", zc" << m1 << ", zs" << m1 << ";\n    j4b_normal_pair2<real>(lo, hi, "
+          << m0 << "u, zc" << m0 << ", zs" << m0 << ", zc" << m1 << ", zs" << m1 << ");\n";
+      } else {
+        const int m = pair_used[m0] ? m0 : m1;
         s << "    real zc" << m << ", zs" << m << ";\n    j4b_normal_pair<real>(lo, hi, " << m << "u, zc" << m << ", zs" << m
           << ");\n";
-        pair_done[m] = 1;
       }
     }
     s << "    const real v" << i << " = ";
@@ -407,6 +503,139 @@ std::string generate(const j4b_aad& h) {
   return s.str();
 }
 
+// Linear-scan slot assignment: interval k = [start, end] gets slot_of[k]; a slot whose interval
+// ends at t may be taken by one that starts at t (a node reads its operands before it writes).
+int assign_slots(const std::vector<std::pair<int64_t, int64_t>>& iv, std::vector<int>& slot_of) {
+  std::vector<int> order(iv.size());
+  for (size_t k = 0; k < iv.size(); ++k) order[k] = (int)k;
+  std::sort(order.begin(), order.end(), [&](int x, int y) { return iv[x].first < iv[y].first; });
+  using EndSlot = std::pair<int64_t, int>;
+  std::priority_queue<EndSlot, std::vector<EndSlot>, std::greater<EndSlot>> busy;
+  std::priority_queue<int, std::vector<int>, std::greater<int>> free_slots;
+  int slots = 0;
+  slot_of.assign(iv.size(), -1);
+  for (int k : order) {
+    while (!busy.empty() && busy.top().first <= iv[k].first) {
+      free_slots.push(busy.top().second);
+      busy.pop();
+    }
+    int sl;
+    if (!free_slots.empty()) {
+      sl = free_slots.top();
+      free_slots.pop();
+    } else {
+      sl = slots++;
+    }
+    slot_of[k] = sl;
+    busy.push({iv[k].second, sl});
+  }
+  return slots;
+}
+
+// Plans the interpreter's slots and records (see the kernel). Times: forward node i at i, the
+// output read at n, reverse step of node j at n + (n - 1 - j), the input gradients read at 2n.
+void plan_interp(j4b_aad& h, std::vector<int4>& rec, std::vector<int>& in_dslot) {
+  const int n = h.n, out = h.out;
+  auto R = [&](int j) { return (int64_t)n + (n - 1 - j); };
+  auto args = [&](int j) { return is_unary(h.op[j]) || is_binary(h.op[j]); };
+  // adjoint needed: the output, and every active operand of a swept node
+  std::vector<char> need(n, 0), swept(n, 0);
+  need[out] = 1;
+  for (int j = n - 1; j >= 0; --j) {
+    if (!(need[j] && h.active[j] && args(j) && h.adjoints)) continue;
+    swept[j] = 1;
+    if (h.active[h.a[j]]) need[h.a[j]] = 1;
+    if (is_binary(h.op[j]) && h.active[h.b[j]]) need[h.b[j]] = 1;
+  }
+  // value intervals
+  std::vector<int64_t> vend(n, -1);
+  auto use = [&](int x, int64_t t) { vend[x] = std::max(vend[x], t); };
+  for (int k = 0; k < n; ++k) {
+    if (args(k)) use(h.a[k], k);
+    if (is_binary(h.op[k])) use(h.b[k], k);
+  }
+  use(out, n);
+  for (int j = 0; j < n; ++j) {
+    if (!swept[j]) continue;
+    const int o = h.op[j], a = h.a[j], b = h.b[j];
+    const bool la = h.active[a], lb = is_binary(o) && h.active[b];
+    switch (o) {
+      case J4B_AAD_MUL: if (la) use(b, R(j)); if (lb) use(a, R(j)); break;
+      case J4B_AAD_DIV: use(b, R(j)); if (lb) use(j, R(j)); break;
+      case J4B_AAD_EXP: case J4B_AAD_SQRT: use(j, R(j)); break;
+      case J4B_AAD_LOG: case J4B_AAD_ABS: use(a, R(j)); break;
+      case J4B_AAD_MAX: case J4B_AAD_MIN: use(a, R(j)); use(b, R(j)); break;
+      default: break;
+    }
+  }
+  std::vector<std::pair<int64_t, int64_t>> iv;
+  std::vector<int> owner;
+  for (int i = 0; i < n; ++i)
+    if (vend[i] >= 0) {
+      iv.push_back({i, vend[i]});
+      owner.push_back(i);
+    }
+  std::vector<int> sl;
+  h.nv = assign_slots(iv, sl);
+  std::vector<int> vslot(n, -1);
+  for (size_t k = 0; k < owner.size(); ++k) vslot[owner[k]] = sl[k];
+  // adjoint intervals and first-contribution flags
+  std::vector<int64_t> dstart(n, -1);
+  std::vector<int> flags(n, 0);
+  if (h.adjoints) dstart[out] = n;
+  for (int j = n - 1; j >= 0; --j) {
+    if (!swept[j]) continue;
+    const int o = h.op[j], a = h.a[j], b = h.b[j];
+    if (h.active[a]) {
+      if (dstart[a] < 0) {
+        dstart[a] = R(j);
+        flags[j] |= kFirstA;
+      }
+    }
+    if (is_binary(o) && h.active[b]) {
+      if (dstart[b] < 0) {
+        dstart[b] = R(j);
+        flags[j] |= kFirstB;
+      }
+    }
+  }
+  iv.clear();
+  owner.clear();
+  for (int x = 0; x < n; ++x)
+    if (dstart[x] >= 0) {
+      iv.push_back({dstart[x], h.op[x] == J4B_AAD_INPUT ? 2 * (int64_t)n : R(x)});
+      owner.push_back(x);
+    }
+  h.nd = assign_slots(iv, sl);
+  std::vector<int> dslot(n, -1);
+  for (size_t k = 0; k < owner.size(); ++k) dslot[owner[k]] = sl[k];
+  auto u16 = [](int v) { return (unsigned)(v < 0 ? kNoSlot : v); };
+  rec.assign((size_t)n, make_int4(0, 0, 0, 0));
+  for (int i = 0; i < n; ++i) {
+    const int o = h.op[i];
+    const int fl = (swept[i] ? kSwept : 0) | flags[i];
+    unsigned a = 0, b = 0;
+    if (o == J4B_AAD_CONST) a = (unsigned)i;
+    else if (o == J4B_AAD_INPUT || o == J4B_AAD_RANDN) a = (unsigned)h.a[i];
+    else {
+      a = u16(vslot[h.a[i]]);
+      b = is_binary(o) ? u16(vslot[h.b[i]]) : 0u;
+    }
+    unsigned di = kNoSlot, da = kNoSlot, db = kNoSlot;
+    if (swept[i]) {
+      di = u16(dslot[i]);
+      if (h.active[h.a[i]]) da = u16(dslot[h.a[i]]);
+      if (is_binary(o) && h.active[h.b[i]]) db = u16(dslot[h.b[i]]);
+    }
+    rec[i] = make_int4((int)((unsigned)o | (unsigned)fl | (u16(vslot[i]) << 16)), (int)(a | (b << 16)),
+                       (int)(di | (da << 16)), (int)db);
+  }
+  in_dslot.assign(std::max(1, h.n_in), -1);
+  for (int j = 0; j < h.n_in; ++j) in_dslot[j] = dslot[h.in_nodes[j]];
+  h.out_vslot = vslot[out];
+  h.out_dslot = h.adjoints ? dslot[out] : -1;
+}
+
 int ensure_partials(j4b_aad* h, int64_t slots) {
   if (slots <= h->partial_slots) return J4B_OK;
   if (h->d_partials) cudaFree(h->d_partials);
@@ -471,6 +700,20 @@ int eager_replay(j4b_aad* h, uint64_t paths, uint64_t offset, uint64_t seed, cud
   return J4B_OK;
 }
 
+template <typename real, bool SMEM>
+void launch_interp(j4b_aad* h, unsigned grid, const double* d_inputs, uint64_t paths, uint64_t offset, uint64_t seed,
+                   cudaStream_t st) {
+  aad_interp_kernel<real, SMEM><<<grid, h->interp_block, h->interp_smem, st>>>(
+      h->d_nodes, h->d_consts, d_inputs, h->d_in_nodes, h->n, h->n_in, h->out_vslot, h->out_dslot, h->nv, h->nd,
+      h->adjoints, paths, offset, seed, (real*)h->vs, (unsigned long long)h->interp_threads, h->d_partials, h->d_ticket,
+      h->d_sums);
+}
+
+const void* interp_fn(bool f32, bool smem) {
+  if (f32) return smem ? (const void*)aad_interp_kernel<float, true> : (const void*)aad_interp_kernel<float, false>;
+  return smem ? (const void*)aad_interp_kernel<double, true> : (const void*)aad_interp_kernel<double, false>;
+}
+
 int launch_replay(j4b_aad* h, const double* d_inputs, uint64_t paths, uint64_t offset, uint64_t seed,
                   cudaStream_t st) {
   const int sms = device_ctx(h->dev)->sm_count;
@@ -487,17 +730,17 @@ int launch_replay(j4b_aad* h, const double* d_inputs, uint64_t paths, uint64_t o
     return J4B_OK;
   }
   if (h->engine == J4B_AAD_ENGINE_INTERP) {
-    const unsigned grid = (unsigned)(h->interp_threads / J4B_AAD_BLOCK);
+    const unsigned grid = (unsigned)(h->interp_threads / h->interp_block);
     int rc = ensure_partials(h, (int64_t)grid * h->channels);
     if (rc) return rc;
-    if (h->f32)
-      aad_interp_kernel<float><<<grid, J4B_AAD_BLOCK, 0, st>>>(
-          h->d_nodes, h->d_consts, d_inputs, h->d_in_nodes, h->n, h->n_in, h->out, h->adjoints, paths, offset, seed,
-          (float*)h->vs, (float*)h->ds, (unsigned long long)h->interp_threads, h->d_partials, h->d_ticket, h->d_sums);
-    else
-      aad_interp_kernel<double><<<grid, J4B_AAD_BLOCK, 0, st>>>(
-          h->d_nodes, h->d_consts, d_inputs, h->d_in_nodes, h->n, h->n_in, h->out, h->adjoints, paths, offset, seed,
-          (double*)h->vs, (double*)h->ds, (unsigned long long)h->interp_threads, h->d_partials, h->d_ticket, h->d_sums);
+    const bool sm = h->interp_smem > 0;
+    if (h->f32) {
+      if (sm) launch_interp<float, true>(h, grid, d_inputs, paths, offset, seed, st);
+      else launch_interp<float, false>(h, grid, d_inputs, paths, offset, seed, st);
+    } else {
+      if (sm) launch_interp<double, true>(h, grid, d_inputs, paths, offset, seed, st);
+      else launch_interp<double, false>(h, grid, d_inputs, paths, offset, seed, st);
+    }
     J4B_CHECK_LAUNCH("aad_interp_kernel");
     return J4B_OK;
   }
@@ -543,8 +786,10 @@ int load_tape(j4b_aad* h, int engine, int n_nodes, const int32_t* ops, const int
     J4B_REQUIRE(v >= 0 && v < n_nodes && ops[v] == J4B_AAD_INPUT && arg_a[v] == j, "input %d does not name its INPUT node",
                 j);
   }
-  if (engine == J4B_AAD_ENGINE_INTERP)
+  if (engine == J4B_AAD_ENGINE_INTERP) {
     J4B_REQUIRE(n_inputs <= kInterpMaxInputs, "the interpreting engine supports at most %d inputs", kInterpMaxInputs);
+    J4B_REQUIRE(n_nodes <= kInterpMaxNodes, "the interpreting engine supports at most %d nodes", kInterpMaxNodes);
+  }
   h->engine = engine;
   h->f32 = precision == 4;
   h->adjoints = adjoints ? 1 : 0;
@@ -642,39 +887,53 @@ extern "C" int j4b_aad_compile(int dev, int engine, int n_nodes, const int32_t* 
     if (r != CUDA_SUCCESS) return fail(cu_error(r, "cuOccupancyMaxActiveBlocksPerMultiprocessor(aad)"));
     h->gen_blocks_per_sm = std::max(1, per_sm);
   } else if (engine == J4B_AAD_ENGINE_INTERP) {
-    std::vector<int4> nodes(n_nodes);
-    for (int i = 0; i < n_nodes; ++i) {
-      const int o = ops[i];
-      const bool args = is_unary(o) || is_binary(o);
-      const int fa = args && h->active[arg_a[i]] ? 2 : 0;
-      const int fb = is_binary(o) && h->active[arg_b[i]] ? 4 : 0;
-      nodes[i] = make_int4(o, arg_a[i], arg_b[i], (h->active[i] ? 1 : 0) | fa | fb);
-    }
-    if ((e = cudaMalloc(&h->d_nodes, nodes.size() * sizeof(int4))) != cudaSuccess) return cuda_fail(e, "cudaMalloc(aad nodes)");
+    std::vector<int4> rec;
+    std::vector<int> in_dslot;
+    plan_interp(*h, rec, in_dslot);
+    if ((e = cudaMalloc(&h->d_nodes, rec.size() * sizeof(int4))) != cudaSuccess) return cuda_fail(e, "cudaMalloc(aad nodes)");
     if ((e = cudaMalloc(&h->d_consts, (size_t)n_nodes * sizeof(double))) != cudaSuccess)
       return cuda_fail(e, "cudaMalloc(aad constants)");
-    if ((e = cudaMalloc(&h->d_in_nodes, (size_t)std::max(1, n_inputs) * sizeof(int))) != cudaSuccess)
-      return cuda_fail(e, "cudaMalloc(aad input nodes)");
+    if ((e = cudaMalloc(&h->d_in_nodes, in_dslot.size() * sizeof(int))) != cudaSuccess)
+      return cuda_fail(e, "cudaMalloc(aad input slots)");
     counters().allocations += 3;
-    cudaMemcpy(h->d_nodes, nodes.data(), nodes.size() * sizeof(int4), cudaMemcpyHostToDevice);
+    cudaMemcpy(h->d_nodes, rec.data(), rec.size() * sizeof(int4), cudaMemcpyHostToDevice);
     cudaMemcpy(h->d_consts, constants, (size_t)n_nodes * sizeof(double), cudaMemcpyHostToDevice);
-    if (n_inputs) cudaMemcpy(h->d_in_nodes, input_nodes, (size_t)n_inputs * sizeof(int), cudaMemcpyHostToDevice);
-    // Threads: every SM's resident blocks, fewer when the [node][thread] scratch would not stay in L2,
-    // at least one block per SM; `scratch_option` > 0 sets the thread count (rounded to blocks).
-    int per_sm = 1;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-        &per_sm, h->f32 ? (const void*)aad_interp_kernel<float> : (const void*)aad_interp_kernel<double>, J4B_AAD_BLOCK, 0);
-    const int64_t per_thread = (int64_t)n_nodes * (int64_t)elt * (h->adjoints ? 2 : 1);
-    int64_t threads = (int64_t)sms * std::max(1, per_sm) * J4B_AAD_BLOCK;
-    threads = std::min(threads, std::max<int64_t>((int64_t)sms * J4B_AAD_BLOCK, kInterpL2Budget / per_thread));
-    if (scratch_option > 0) threads = scratch_option;
-    threads = std::max<int64_t>(J4B_AAD_BLOCK, threads / J4B_AAD_BLOCK * J4B_AAD_BLOCK);
-    h->interp_threads = threads;
-    if ((e = cudaMalloc(&h->vs, (size_t)n_nodes * threads * elt)) != cudaSuccess)
-      return cuda_fail(e, "cudaMalloc(aad interpreter values)");
-    if (h->adjoints && (e = cudaMalloc(&h->ds, (size_t)n_nodes * threads * elt)) != cudaSuccess)
-      return cuda_fail(e, "cudaMalloc(aad interpreter adjoints)");
-    counters().allocations += h->adjoints ? 2 : 1;
+    cudaMemcpy(h->d_in_nodes, in_dslot.data(), in_dslot.size() * sizeof(int), cudaMemcpyHostToDevice);
+    // Shared-memory slots (and records) when at least one warp's state fits a CTA (up to 256
+    // threads per CTA, as many CTAs per SM as fit); otherwise [slot][thread] in global memory with
+    // one CTA per SM, more while the scratch stays within L2. `scratch_option` > 0 forces the
+    // global layout with that many threads.
+    const int64_t per_thread = (int64_t)(h->nv + (h->adjoints ? h->nd : 0)) * (int64_t)elt;
+    const int64_t rec_bytes = (int64_t)rec.size() * (int64_t)sizeof(int4);
+    int optin = 0;
+    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    cudaFuncAttributes fa;
+    cudaFuncGetAttributes(&fa, interp_fn(h->f32, true));
+    const int64_t smem_cap = (int64_t)optin - (int64_t)fa.sharedSizeBytes;
+    const int64_t fit = smem_cap > rec_bytes ? (smem_cap - rec_bytes) / std::max<int64_t>(1, per_thread) / 32 * 32 : 0;
+    if (scratch_option == 0 && fit >= 32) {
+      const void* kfn = interp_fn(h->f32, true);
+      h->interp_block = (int)std::min<int64_t>(J4B_AAD_BLOCK, fit);
+      h->interp_smem = (size_t)(h->interp_block * per_thread + rec_bytes);
+      if ((e = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_cap)) != cudaSuccess)
+        return cuda_fail(e, "cudaFuncSetAttribute(aad interpreter)");
+      int per_sm = 1;
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kfn, h->interp_block, h->interp_smem);
+      h->interp_threads = (int64_t)sms * std::max(1, per_sm) * h->interp_block;
+    } else {
+      const void* kfn = interp_fn(h->f32, false);
+      h->interp_block = J4B_AAD_BLOCK;
+      h->interp_smem = 0;
+      int per_sm = 1;
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kfn, J4B_AAD_BLOCK, 0);
+      int64_t threads = (int64_t)sms * std::max(1, per_sm) * J4B_AAD_BLOCK;
+      threads = std::min(threads, std::max<int64_t>((int64_t)sms * J4B_AAD_BLOCK, kInterpL2Budget / std::max<int64_t>(1, per_thread)));
+      if (scratch_option > 0) threads = scratch_option;
+      h->interp_threads = std::max<int64_t>(J4B_AAD_BLOCK, threads / J4B_AAD_BLOCK * J4B_AAD_BLOCK);
+      if ((e = cudaMalloc(&h->vs, (size_t)std::max<int64_t>(1, per_thread) * h->interp_threads)) != cudaSuccess)
+        return cuda_fail(e, "cudaMalloc(aad interpreter slots)");
+      counters().allocations++;
+    }
   } else {
     // Scenarios per chunk bounded by the scratch budget (CudaEagerExecutable.java:81-85).
     const int64_t budget = scratch_option > 0 ? scratch_option : kEagerDefaultBytes;

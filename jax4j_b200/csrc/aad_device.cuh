@@ -38,6 +38,23 @@ __device__ __forceinline__ void j4b_philox10(unsigned int& c0, unsigned int& c1)
   }
 }
 
+// Two independent Philox blocks with their rounds interleaved (two dependency chains in flight
+// per thread).
+__device__ __forceinline__ void j4b_philox10x2(unsigned int& a0, unsigned int& a1, unsigned int& b0,
+                                               unsigned int& b1) {
+  unsigned int key = 0x1BD11BDAu;
+#pragma unroll
+  for (int i = 0; i < 10; i++) {
+    const unsigned int ha = __umulhi(0xD256D193u, a0), la = 0xD256D193u * a0;
+    const unsigned int hb = __umulhi(0xD256D193u, b0), lb = 0xD256D193u * b0;
+    a0 = ha ^ key ^ a1;
+    a1 = la;
+    b0 = hb ^ key ^ b1;
+    b1 = lb;
+    key += 0x9E3779B9u;
+  }
+}
+
 // Scenario key: lo = low word of path ^ low word of seed, hi = the high words
 // (Philox.java:36-38).
 __device__ __forceinline__ void j4b_scenario_key(unsigned long long path, unsigned long long seed,
@@ -49,19 +66,15 @@ __device__ __forceinline__ void j4b_scenario_key(unsigned long long path, unsign
 // Standard-normal draws 2m (cosine leg) and 2m + 1 (sine leg) of a scenario: Box-Muller on the
 // Philox block of counter (lo, hi ^ m), u = (c + 1/2) 2^-32, r = sqrt(-2 ln u1), angle 2 pi u2
 // (Philox.java:47-63).
-template <typename real>
-__device__ __forceinline__ void j4b_normal_pair(unsigned int lo, unsigned int hi, unsigned int m,
-                                                real& zc, real& zs);
-
 // FLOAT32: u1 keeps full relative precision (one rounding of c0 to 24 bits), so the radius is
 // accurate however close u1 is to 0 or 1; the angle is taken as 2 pi t + pi with t = u2 - 1/2
 // to 2^-24 (the top 23 bits of c1, centred), so sin and cos are evaluated on [-pi, pi], where
 // the hardware approximations are accurate to 2^-21.4 absolute.
+template <typename real>
+__device__ __forceinline__ void j4b_box_muller(unsigned int c0, unsigned int c1, real& zc, real& zs);
+
 template <>
-__device__ __forceinline__ void j4b_normal_pair<float>(unsigned int lo, unsigned int hi,
-                                                       unsigned int m, float& zc, float& zs) {
-  unsigned int c0 = lo, c1 = hi ^ m;
-  j4b_philox10(c0, c1);
+__device__ __forceinline__ void j4b_box_muller<float>(unsigned int c0, unsigned int c1, float& zc, float& zs) {
   const float u1 = fmaf(__uint2float_rn(c0), 2.3283064365386963e-10f, 1.16415321826934814e-10f);
   const float t = (__uint_as_float(0x3F800000u | (c1 >> 9)) - 1.5f) + 5.9604644775390625e-8f;
   const float r = sqrtf(-2.0f * logf(u1));
@@ -71,11 +84,9 @@ __device__ __forceinline__ void j4b_normal_pair<float>(unsigned int lo, unsigned
   zs = -r * s;
 }
 
+// FLOAT64: exactly the CPU engine's formulation.
 template <>
-__device__ __forceinline__ void j4b_normal_pair<double>(unsigned int lo, unsigned int hi,
-                                                        unsigned int m, double& zc, double& zs) {
-  unsigned int c0 = lo, c1 = hi ^ m;
-  j4b_philox10(c0, c1);
+__device__ __forceinline__ void j4b_box_muller<double>(unsigned int c0, unsigned int c1, double& zc, double& zs) {
   const double u1 = ((double)c0 + 0.5) * 2.3283064365386963e-10;
   const double u2 = ((double)c1 + 0.5) * 2.3283064365386963e-10;
   const double r = sqrt(-2.0 * log(u1));
@@ -83,6 +94,23 @@ __device__ __forceinline__ void j4b_normal_pair<double>(unsigned int lo, unsigne
   sincos(6.283185307179586 * u2, &s, &c);
   zc = r * c;
   zs = r * s;
+}
+
+template <typename real>
+__device__ __forceinline__ void j4b_normal_pair(unsigned int lo, unsigned int hi, unsigned int m, real& zc, real& zs) {
+  unsigned int c0 = lo, c1 = hi ^ m;
+  j4b_philox10(c0, c1);
+  j4b_box_muller<real>(c0, c1, zc, zs);
+}
+
+// Pairs m and m + 1 (draws 2m .. 2m + 3) from interleaved Philox blocks.
+template <typename real>
+__device__ __forceinline__ void j4b_normal_pair2(unsigned int lo, unsigned int hi, unsigned int m, real& zc0,
+                                                 real& zs0, real& zc1, real& zs1) {
+  unsigned int a0 = lo, a1 = hi ^ m, b0 = lo, b1 = hi ^ (m + 1u);
+  j4b_philox10x2(a0, a1, b0, b1);
+  j4b_box_muller<real>(a0, a1, zc0, zs0);
+  j4b_box_muller<real>(b0, b1, zc1, zs1);
 }
 
 // Sums C per-thread double accumulators over the grid: warp shuffles, then the block's warps in
@@ -104,10 +132,10 @@ __device__ __forceinline__ void j4b_aad_finish(const double (&acc)[C], int live,
     if (lane == 0) red[c][warp] = v;
   }
   __syncthreads();
+  const int warps = (int)(blockDim.x >> 5);  // blockDim.x is a multiple of 32, at most J4B_AAD_BLOCK
   for (int c = threadIdx.x; c < live; c += blockDim.x) {
     double s = 0.0;
-#pragma unroll
-    for (int w = 0; w < J4B_AAD_WARPS; ++w) s += red[c][w];
+    for (int w = 0; w < warps; ++w) s += red[c][w];
     partials[(unsigned long long)blockIdx.x * live + c] = s;
   }
   __threadfence();

@@ -200,6 +200,7 @@ def test_generated_kernel_compiles(precision, adjoints):
 
 
 def test_generated_kernel_shares_box_muller_pairs():
+    """Each Philox block serves two draws, and pairs of blocks are computed together."""
     def body(rec):
         x = rec.input("x", 1.0)
         acc = x
@@ -207,7 +208,8 @@ def test_generated_kernel_shares_box_muller_pairs():
             acc = acc * rec.randn()
         rec.output(acc)
     src = dryrun(AadRecorder.record(body))
-    assert src.count("j4b_normal_pair<real>(lo, hi,") == 4  # draws 0..6 -> pairs 0..3
+    # draws 0..6 -> Box-Muller pairs 0..3 -> two interleaved Philox calls covering two pairs each
+    assert src.count("j4b_normal_pair2<real>(lo, hi,") == 2 and "j4b_normal_pair<real>(lo" not in src
 
 
 def test_tape_validation_in_the_abi():

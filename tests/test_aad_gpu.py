@@ -224,3 +224,41 @@ def test_device_launch_is_stream_ordered():
         s = sums.cpu().numpy() / 4096
         assert s[0] == pytest.approx(12 + math.exp(2) + math.exp(3), rel=1e-14)
         assert s[2] == pytest.approx(12 + math.exp(2), rel=1e-14) and s[3] == pytest.approx(4 + math.exp(3), rel=1e-14)
+
+
+def edge_tape():
+    """Repeated operands (x * x, a first contribution that is also accumulated), MAX/MIN between
+    active and inactive sides, an unused input, nodes recorded after the output."""
+    def body(rec):
+        x, y, unused = rec.input("x", 0.3), rec.input("y", 2.0), rec.input("unused", 5.0)
+        z = rec.randn()
+        w = (x * x + y.exp() * z).max(x * 0.5).min(y) / y + (x - y).abs().sqrt().log()
+        rec.output(w)
+        w * 3.0 + unused  # after the output: never swept
+    return AadRecorder.record(body)
+
+
+@pytest.mark.parametrize("layout", ["shared", "global"])
+def test_interpreter_slot_plan(oracle, layout):
+    """The interpreter's liveness-planned slots, in shared memory and in global scratch, against
+    the oracle (FLOAT64, 1e-12) on tapes that stress the plan; an unused input's gradient is 0."""
+    opts = AadOptions(Precision.FLOAT64)
+    if layout == "global":
+        opts = opts.with_engine_option("cuda-interp", "threads", 8192)
+    for tape in (edge_tape(), conformance_tape(), asian_tape(16)):
+        v, _, g = oracle_means(oracle, tape, 50_000, 77, 5)
+        with CudaInterpEngine().compile(tape, opts) as exe:
+            assert (exe.threads_or_slot == 8192) == (layout == "global")
+            r = exe.replay(50_000, 77, 5)
+        assert r.value() == pytest.approx(v, rel=1e-12)
+        np.testing.assert_allclose(r.gradients(), g, rtol=1e-12, atol=1e-12)
+    with CudaInterpEngine().compile(edge_tape(), opts) as exe:
+        assert exe.replay(1000, 0, 1).gradient("unused") == 0.0
+
+
+@pytest.mark.parametrize("engine_cls", ENGINES)
+def test_output_is_an_input(engine_cls):
+    tape = AadRecorder.record(lambda rec: rec.output(rec.input("x", 1.5)))
+    with engine_cls().compile(tape, AadOptions(Precision.FLOAT64)) as exe:
+        r = exe.replay(999, 0, 1)
+        assert r.value() == 1.5 and r.gradients() == [1.0] and r.standard_error() == 0.0
