@@ -96,3 +96,30 @@ def remap(expr: Expr, mapping: dict[int, int], memo: dict | None = None) -> Expr
         r = Scalar(expr.op, remap(expr.a, mapping, memo), expr.value)
     memo[id(expr)] = r
     return r
+
+
+def from_postfix(prog: list[int]) -> Expr:
+    """The expression a postfix program encodes (inverse of `postfix`)."""
+    stack: list[Expr] = []
+    i = 0
+    while i < len(prog):
+        kind = prog[i]
+        if kind == 0:
+            stack.append(Input(prog[i + 1]))
+            i += 2
+        elif kind == 1:
+            stack.append(Unary(OPS[prog[i + 1]], stack.pop()))
+            i += 2
+        elif kind == 2:
+            b, a = stack.pop(), stack.pop()
+            stack.append(Binary(OPS[prog[i + 1]], a, b))
+            i += 2
+        elif kind == 3:
+            value = struct.unpack("<d", struct.pack("<ii", prog[i + 2], prog[i + 3]))[0]
+            stack.append(Scalar(OPS[prog[i + 1]], stack.pop(), value))
+            i += 4
+        else:
+            raise ValueError(f"bad postfix word {kind} at {i}")
+    if len(stack) != 1:
+        raise ValueError("postfix program does not reduce to one expression")
+    return stack[0]

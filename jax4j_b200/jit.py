@@ -35,12 +35,13 @@ TAPE_MAGIC = 0x31455041_5442344A  # "J4BTAPE1" little-endian words
 
 
 class Sym(Buffer):
-    """A symbolic buffer of the tape (shape only)."""
-    __slots__ = ("id", "shape")
+    """A symbolic buffer of one recorder's tape (shape only)."""
+    __slots__ = ("id", "shape", "owner")
 
-    def __init__(self, bid: int, shape: tuple):
+    def __init__(self, bid: int, shape: tuple, owner=None):
         self.id = bid
         self.shape = tuple(int(d) for d in shape)
+        self.owner = owner
 
 
 @dataclass
@@ -54,9 +55,10 @@ class Call:
 @dataclass
 class Tape:
     shapes: list            # buffer id -> shape
-    inputs: list            # buffer ids
+    inputs: list            # buffer ids: the explicit inputs, then one per captured buffer
     outputs: list           # buffer ids
     calls: list             # Call
+    captured: list = field(default_factory=list)  # buffers closed over by the traced function
 
     def serialize(self) -> np.ndarray:
         """int64 words: header, buffer shapes, inputs, outputs, calls (see the engine parser)."""
@@ -141,15 +143,30 @@ class RecordingBackend(Backend):
     def __init__(self):
         self.shapes: list = []
         self.calls: list = []
+        self.captured: list = []   # (buffer, Sym) for buffers from outside the traced function
+        self._capture_ids: dict = {}
 
     def new(self, shape) -> Sym:
-        s = Sym(len(self.shapes), shape)
+        s = Sym(len(self.shapes), shape, self)
         self.shapes.append(s.shape)
         return s
 
+    def sym(self, b) -> Sym:
+        """This recorder's symbol for b: b itself, or the input that captures a buffer the traced
+        function closed over (a constant tensor, or a value of an enclosing trace)."""
+        if isinstance(b, Sym) and b.owner is self:
+            return b
+        got = self._capture_ids.get(id(b))
+        if got is None:
+            got = self.new(b.shape)
+            self._capture_ids[id(b)] = got
+            self.captured.append((b, got))
+        return got
+
     def rec(self, op: str, shape, ins=(), **attrs) -> Sym:
+        ids = [self.sym(b).id for b in ins]
         out = self.new(shape)
-        self.calls.append(Call(op, out.id, [b.id for b in ins], attrs))
+        self.calls.append(Call(op, out.id, ids, attrs))
         return out
 
     def download(self, b):
@@ -269,29 +286,35 @@ class RecordingBackend(Backend):
 # ---------------------------------------------------------------------------------------------
 
 class ExprBuffer(Buffer):
-    __slots__ = ("expr", "leaves", "shape", "materialized")
+    __slots__ = ("expr", "leaves", "shape", "materialized", "owner")
 
-    def __init__(self, expr, leaves, shape):
+    def __init__(self, expr, leaves, shape, owner=None):
         self.expr = expr
         self.leaves = list(leaves)
         self.shape = tuple(shape)
         self.materialized = None  # the delegate's buffer once this chain hit a boundary
+        self.owner = owner        # the FusingBackend that built the chain
 
 
 class FusingBackend(Backend):
     def __init__(self, delegate: Backend):
         self.d = delegate
 
-    @staticmethod
-    def traced(b) -> ExprBuffer:
+    def traced(self, b) -> ExprBuffer:
+        """b as an expression of this backend; a chain built by another fusing backend (an
+        enclosing trace) is a leaf here, materialised by its owner."""
         if isinstance(b, ExprBuffer):
-            return b
-        return ExprBuffer(E.Input(0), [b], b.shape)
+            if b.owner is self or b.owner is None:
+                return b
+            b = b.owner.materialize(b)
+        return ExprBuffer(E.Input(0), [b], b.shape, self)
 
     def materialize(self, b):
         """FusingBackend.materialize (FusingBackend.java:273-286)."""
         if not isinstance(b, ExprBuffer):
             return b
+        if b.owner is not None and b.owner is not self:
+            return b.owner.materialize(b)
         if b.materialized is not None:
             return b.materialized
         if isinstance(b.expr, E.Input) and len(b.leaves) == 1:
@@ -322,15 +345,15 @@ class FusingBackend(Backend):
     def binary(self, op, a, b):
         la, rb = self.traced(a), self.traced(b)
         le, re_, leaves = self.merge(la, rb)
-        return ExprBuffer(E.Binary(op, le, re_), leaves, la.shape)
+        return ExprBuffer(E.Binary(op, le, re_), leaves, la.shape, self)
 
     def scalar(self, op, a, value):
         t = self.traced(a)
-        return ExprBuffer(E.Scalar(op, t.expr, float(value)), t.leaves, t.shape)
+        return ExprBuffer(E.Scalar(op, t.expr, float(value)), t.leaves, t.shape, self)
 
     def unary(self, op, a):
         t = self.traced(a)
-        return ExprBuffer(E.Unary(op, t.expr), t.leaves, t.shape)
+        return ExprBuffer(E.Unary(op, t.expr), t.leaves, t.shape, self)
 
     # everything else is a boundary
     def full(self, value, shape):
@@ -374,8 +397,9 @@ def trace(fn: Callable, input_shapes: list) -> Tape:
     fusing = FusingBackend(rec)
     out = fn(*[Tensor(fusing, b) for b in inputs])
     outs = list(out) if isinstance(out, (list, tuple)) else [out]
-    out_ids = [fusing.materialize(t.buffer).id for t in outs]
-    return Tape(rec.shapes, [b.id for b in inputs], out_ids, rec.calls)
+    out_ids = [rec.sym(fusing.materialize(t.buffer)).id for t in outs]
+    return Tape(rec.shapes, [b.id for b in inputs] + [s.id for _, s in rec.captured], out_ids, rec.calls,
+                [b for b, _ in rec.captured])
 
 
 class Compiled:
@@ -388,6 +412,8 @@ class Compiled:
 
     def tape_for(self, shapes: list) -> Tape:
         key = tuple(tuple(s) for s in shapes)
+        if self.plans.get(key, {}).get("eager"):
+            return None
         if key not in self.plans:
             self.traces += 1
             self.plans[key] = {"tape": trace(self.fn, list(key))}
@@ -405,8 +431,16 @@ class Compiled:
             return self.fn(*tensors)
         shapes = [t.shape for t in tensors]
         key = tuple(tuple(s) for s in shapes)
-        tape = self.tape_for(shapes)
-        outs = backend.execute_tape(tape, self.plans[key], [t.buffer for t in tensors])
+        from .control_flow import Untraceable
+        try:
+            tape = self.tape_for(shapes)
+        except Untraceable:
+            # data-dependent control flow (a while loop): this signature runs eagerly
+            self.plans[key] = {"eager": True}
+            tape = None
+        if tape is None or self.plans[key].get("eager"):
+            return self.fn(*tensors)
+        outs = backend.execute_tape(tape, self.plans[key], [t.buffer for t in tensors] + tape.captured)
         results = [Tensor(backend, b) for b in outs]
         return results if len(results) > 1 else results[0]
 

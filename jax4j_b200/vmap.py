@@ -112,6 +112,21 @@ class BatchingBackend(Backend):
         idx = (i // size) * n + ix * size + i % size
         return Batched(self, self.real.reindex(a.physical, self.batch_shape(sample), idx), sample)
 
+    def stack_axis0(self, xs):
+        """Stack of samples: the physical [B, ...] buffers stacked to [n, B, ...], gathered to
+        [B, n, ...]."""
+        if not any(self._mapped(x) for x in xs):
+            return self.real.stack_axis0(xs)
+        n, bsz = len(xs), self.batch
+        sample = tuple(xs[0].shape)
+        m = prod(sample)
+        st = self.real.stack_axis0([self.phys(x) for x in xs])
+        idx = np.arange(bsz * n * m, dtype=np.int64)
+        b, rest = np.divmod(idx, n * m)
+        j, k = np.divmod(rest, m)
+        out = self.real.reindex(st, (bsz, n) + sample, ((j * bsz + b) * m + k).tolist())
+        return Batched(self, out, (n,) + sample)
+
     def _batched_map(self, name, a, target, indices):
         target = tuple(target)
         base = np.asarray(indices, dtype=np.int64)
