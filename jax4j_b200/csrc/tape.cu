@@ -1306,7 +1306,7 @@ struct Gen {
     if (a.local) {
       if (bv.W == 1 && (a.k == TB_ID || a.k == TB_CONST)) return vname(a.base);
       if (a.k == TB_ID && a.Wb == W) return vname(a.base) + "[e * 4 + q]";
-      if (a.k == TB_SHIFT && a.param % (4LL * NT) == 0) {
+      if (a.k == TB_SHIFT && a.param % (4LL * NT) == 0 && bv.W > 1) {  // width-1 bases are scalars
         int64_t se = a.param / (4LL * NT);
         std::string es = "(e + " + std::to_string(se) + ")";
         std::string eb = std::to_string(E(a.Wb));

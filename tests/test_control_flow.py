@@ -25,7 +25,8 @@ def be(request, oracle):
 
 def arr(be, x, *shape):
     a = np.asarray(x, np.float32)
-    return Tensor(be, be.upload(a.reshape(shape) if shape else a))
+    a = a.reshape(shape) if shape else a
+    return Tensor(be, be.upload(a, a.shape))
 
 
 def get(t):
@@ -162,3 +163,35 @@ def test_jit_with_while_runs_eagerly_and_closures_are_captured(be):
     closure = J.compile(lambda t: t.mul(w).add(1))
     assert get(closure(arr(be, [1, 2], 2))).tolist() == [11, 41]
     assert get(closure(arr(be, [3, 3], 2))).tolist() == [31, 61]
+
+
+def test_packed_tree_regions_compile_for_the_engine(oracle):
+    """The tree forms' pack / unpack regions (reindex views with padding over width-1 values)
+    plan and compile with the engine's tape compiler (j4b_tape_dryrun: NVRTC, no device)."""
+    import ctypes
+    from jax4j_b200 import _lib
+    from oracle.backend import OracleBackend
+    be = OracleBackend()
+    tapes = []
+    init = CF._Region.__init__
+
+    def spy(self, fn, shapes):
+        init(self, fn, shapes)
+        tapes.append(self.tape)
+    CF._Region.__init__ = spy
+    try:
+        x, y, xs = arr(be, [1], 1), arr(be, [2], 1), arr(be, [1, 2, 3], 3, 1)
+        CF.while_tree(lambda s: s["a"].neg().add(3).sign().maximum(0),
+                      lambda s: {"a": s["a"].add(1), "b": s["b"].mul(2)}, {"a": x, "b": y})
+        CF.scan_tree(lambda c, v: CF.ScanStep({"a": c["a"].add(v["x"]), "b": c["b"].mul(2)}, {"y": c["a"]}),
+                     {"a": x, "b": y}, {"x": xs})
+    finally:
+        CF._Region.__init__ = init
+    assert len(tapes) == 3
+    for t in tapes:
+        w = t.serialize()
+        st = _lib.TapeStats()
+        n = ctypes.c_size_t()
+        _lib.call("j4b_tape_dryrun", w.ctypes.data_as(ctypes.POINTER(ctypes.c_int64)), w.size, ctypes.byref(st),
+                  None, 0, ctypes.byref(n))
+        assert st.groups >= 1
