@@ -167,6 +167,21 @@ int j4b_random_normal(int64_t seed, int64_t counter, j4b_buf out, int64_t n, j4b
 int j4b_matmul(j4b_buf a, j4b_buf b, j4b_buf out, int64_t batch, int64_t m, int64_t k,
                int64_t n, int precision, j4b_stream s);
 
+/* ---- conv2d / conv2dGradInput / conv2dGradWeight: ComputeBackend.java:191-200 (CPU semantics
+ * CpuBackend.java:479-609). ConvSpec (core/tensor/ConvSpec.java) as plain ints: images NCHW
+ * flattened per row, x [batch, in_c*in_h*in_w], w [out_c, in_c*kernel*kernel], output
+ * [batch, out_c*out_h*out_w] with out_h = (in_h + 2 pad - kernel) / stride + 1 (likewise out_w).
+ * precision as j4b_matmul (0 = fp32-accurate). Invalid specs: J4B_EINVAL with ConvSpec's
+ * messages. */
+int j4b_conv2d(j4b_buf x, j4b_buf w, j4b_buf out, int64_t batch, int in_c, int in_h, int in_w,
+               int out_c, int kernel, int stride, int pad, int precision, j4b_stream s);
+int j4b_conv2d_grad_input(j4b_buf upstream, j4b_buf w, j4b_buf out, int64_t batch, int in_c,
+                          int in_h, int in_w, int out_c, int kernel, int stride, int pad,
+                          int precision, j4b_stream s);
+int j4b_conv2d_grad_weight(j4b_buf x, j4b_buf upstream, j4b_buf out, int64_t batch, int in_c,
+                           int in_h, int in_w, int out_c, int kernel, int stride, int pad,
+                           int precision, j4b_stream s);
+
 /* ---- QuantizedOps: core/tensor/spi/QuantizedOps.java:19-34 ---- */
 
 /* supportedQuantTypes (QuantizedOps.java:21): writes up to cap ids, returns the count in *n. */

@@ -79,6 +79,9 @@ SIGNATURES = {
     "j4b_random_uniform": [_i64, _i64, _u64, _i64, _vp],
     "j4b_random_normal": [_i64, _i64, _u64, _i64, _vp],
     "j4b_matmul": [_u64, _u64, _u64, _i64, _i64, _i64, _i64, _int, _vp],
+    "j4b_conv2d": [_u64, _u64, _u64, _i64, _int, _int, _int, _int, _int, _int, _int, _int, _vp],
+    "j4b_conv2d_grad_input": [_u64, _u64, _u64, _i64, _int, _int, _int, _int, _int, _int, _int, _int, _vp],
+    "j4b_conv2d_grad_weight": [_u64, _u64, _u64, _i64, _int, _int, _int, _int, _int, _int, _int, _int, _vp],
     "j4b_quant_supported": [ctypes.POINTER(ctypes.c_int), _int, ctypes.POINTER(ctypes.c_int)],
     "j4b_quant_bytes": [_int, _i64, _i64, _i64p],
     "j4b_quant_upload": [_int, _vp, ctypes.c_size_t, _int, _i64, _i64, ctypes.POINTER(_vp)],

@@ -238,6 +238,30 @@ class B200Backend:
         call("j4b_transpose", a.ptr, out.ptr, r, c, self.stream)
         return out
 
+    # ---- conv2d (ComputeBackend.java:191-200) ----
+    def _conv(self, entry, a, b, spec, out_shape, precision):
+        out = self._new(out_shape)
+        call(entry, a.ptr, b.ptr, out.ptr, a.shape[0], *spec.ints(), precision, self.stream)
+        return out
+
+    def conv2d(self, x: DeviceBuffer, w: DeviceBuffer, spec, precision: int = 0) -> DeviceBuffer:
+        batch = spec.batch_of(x.shape, "conv2d input")
+        if x.shape[1] != spec.input_size or tuple(w.shape) != spec.weight_shape():
+            raise ValueError(f"conv2d shapes {x.shape} x {w.shape} do not match {spec}")
+        return self._conv("j4b_conv2d", x, w, spec, spec.output_shape(batch), precision)
+
+    def conv2d_grad_input(self, up: DeviceBuffer, w: DeviceBuffer, spec, precision: int = 0) -> DeviceBuffer:
+        batch = spec.batch_of(up.shape, "conv2dGradInput upstream")
+        if up.shape[1] != spec.output_size or tuple(w.shape) != spec.weight_shape():
+            raise ValueError(f"conv2dGradInput shapes {up.shape} x {w.shape} do not match {spec}")
+        return self._conv("j4b_conv2d_grad_input", up, w, spec, spec.input_shape(batch), precision)
+
+    def conv2d_grad_weight(self, x: DeviceBuffer, up: DeviceBuffer, spec, precision: int = 0) -> DeviceBuffer:
+        batch = spec.batch_of(x.shape, "conv2dGradWeight input")
+        if x.shape[1] != spec.input_size or tuple(up.shape) != spec.output_shape(batch):
+            raise ValueError(f"conv2dGradWeight shapes {x.shape} x {up.shape} do not match {spec}")
+        return self._conv("j4b_conv2d_grad_weight", x, up, spec, spec.weight_shape(), precision)
+
     def matmul(self, a: DeviceBuffer, b: DeviceBuffer, precision: int = 0) -> DeviceBuffer:
         if len(a.shape) != 2 or len(b.shape) != 2 or a.shape[1] != b.shape[0]:
             raise ValueError(f"incompatible matmul shapes: {a.shape} x {b.shape}")

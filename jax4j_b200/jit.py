@@ -280,6 +280,12 @@ class RecordingBackend(Backend):
     def relu_backward(self, up, inp):
         return self.rec("relu_backward", up.shape, (up, inp))
 
+    def _untraceable(self, *args):
+        from .control_flow import Untraceable
+        raise Untraceable("the tape format has no convolution call")
+
+    conv2d = conv2d_grad_input = conv2d_grad_weight = _untraceable
+
 
 # ---------------------------------------------------------------------------------------------
 # FusingBackend (FusingBackend.java:31-371)

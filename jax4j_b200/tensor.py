@@ -8,6 +8,8 @@ ExecutionPlan records.
 """
 from __future__ import annotations
 
+from dataclasses import dataclass
+
 import math
 from typing import Sequence
 
@@ -48,6 +50,68 @@ def reshape_target(shape: tuple, dims: Sequence[int]) -> tuple:
     if prod(dims) != total:
         raise ValueError(f"cannot reshape {shape} to {tuple(dims)}")
     return tuple(int(d) for d in dims)
+
+
+@dataclass(frozen=True)
+class ConvSpec:
+    """2-D convolution geometry (core/tensor/ConvSpec.java): NCHW images flattened per row."""
+    in_channels: int
+    in_height: int
+    in_width: int
+    out_channels: int
+    kernel: int
+    stride: int = 1
+    pad: int = 0
+
+    def __post_init__(self):
+        if min(self.in_channels, self.in_height, self.in_width, self.out_channels) < 1:
+            raise ValueError("channels and spatial dims must be positive")
+        if self.kernel < 1 or self.stride < 1 or self.pad < 0:
+            raise ValueError("kernel/stride must be positive, pad non-negative")
+        if self.in_height + 2 * self.pad < self.kernel or self.in_width + 2 * self.pad < self.kernel:
+            raise ValueError(f"kernel {self.kernel} does not fit {self.in_height}x{self.in_width} with pad {self.pad}")
+
+    @property
+    def out_height(self) -> int:
+        return (self.in_height + 2 * self.pad - self.kernel) // self.stride + 1
+
+    @property
+    def out_width(self) -> int:
+        return (self.in_width + 2 * self.pad - self.kernel) // self.stride + 1
+
+    @property
+    def input_size(self) -> int:
+        return self.in_channels * self.in_height * self.in_width
+
+    @property
+    def output_size(self) -> int:
+        return self.out_channels * self.out_height * self.out_width
+
+    @property
+    def weight_size(self) -> int:
+        return self.in_channels * self.kernel * self.kernel
+
+    def weight_shape(self) -> tuple:
+        return (self.out_channels, self.weight_size)
+
+    def input_shape(self, batch: int) -> tuple:
+        return (batch, self.input_size)
+
+    def output_shape(self, batch: int) -> tuple:
+        return (batch, self.output_size)
+
+    def next(self, out_channels: int, kernel: int, stride: int, pad: int) -> "ConvSpec":
+        """The spec of a layer that consumes this layer's output."""
+        return ConvSpec(self.out_channels, self.out_height, self.out_width, out_channels, kernel, stride, pad)
+
+    def ints(self) -> tuple:
+        return (self.in_channels, self.in_height, self.in_width, self.out_channels, self.kernel, self.stride,
+                self.pad)
+
+    def batch_of(self, shape: tuple, what: str) -> int:
+        if len(shape) != 2:
+            raise ValueError(f"{what} must be rank-2, got {shape}")
+        return shape[0]
 
 
 class Buffer:
@@ -240,6 +304,21 @@ class Tensor:
     def scatter_add(self, target, indices) -> "Tensor":
         return self.wrap(self.backend.scatter_add(self.buffer, tuple(target),
                                                   np.asarray(indices, dtype=np.int64)))
+
+    # ---- convolution (Tensor.java:400-420) ----
+    def conv2d(self, weights: "Tensor", spec: ConvSpec) -> "Tensor":
+        be = pick_backend(self.backend, weights.backend)
+        return Tensor(be, be.conv2d(self.buffer, weights.buffer, spec))
+
+    def conv2d_grad_input(self, weights: "Tensor", spec: ConvSpec) -> "Tensor":
+        """Gradient of conv2d with respect to its input; this is the upstream gradient."""
+        be = pick_backend(self.backend, weights.backend)
+        return Tensor(be, be.conv2d_grad_input(self.buffer, weights.buffer, spec))
+
+    def conv2d_grad_weight(self, upstream: "Tensor", spec: ConvSpec) -> "Tensor":
+        """Gradient of conv2d with respect to its weights; this is the input."""
+        be = pick_backend(self.backend, upstream.backend)
+        return Tensor(be, be.conv2d_grad_weight(self.buffer, upstream.buffer, spec))
 
     def relu_backward(self, inp: "Tensor") -> "Tensor":
         be = pick_backend(self.backend, inp.backend)

@@ -210,6 +210,24 @@ class ADBackend(Backend):
                            lambda p: self.inner.relu_backward(p[0], p[1]), rule)
 
     # ---- contractions ----
+    # conv2d family (Transforms.java:614-629): each op is bilinear; its two pullbacks are the
+    # other two ops of the family
+    def conv2d(self, x, w, spec):
+        def rule(a, b, out, ps):
+            return lambda g: [g.conv2d_grad_input(b, spec), a.conv2d_grad_weight(g, spec)]
+        return self._apply("conv2d", [x, w], lambda p: self.inner.conv2d(p[0], p[1], spec), rule)
+
+    def conv2d_grad_input(self, up, w, spec):
+        def rule(a, b, out, ps):
+            return lambda g: [g.conv2d(b, spec), g.conv2d_grad_weight(a, spec)]
+        return self._apply("conv2dGradInput", [up, w], lambda p: self.inner.conv2d_grad_input(p[0], p[1], spec), rule)
+
+    def conv2d_grad_weight(self, x, up, spec):
+        def rule(a, b, out, ps):
+            return lambda g: [b.conv2d_grad_input(g, spec), a.conv2d(g, spec)]
+        return self._apply("conv2dGradWeight", [x, up], lambda p: self.inner.conv2d_grad_weight(p[0], p[1], spec),
+                           rule)
+
     def matmul(self, x, y):
         def rule(a, b, out, ps):
             return lambda g: [_reduce_to(g.matmul(b.transpose()), a.shape),

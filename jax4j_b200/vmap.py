@@ -112,6 +112,34 @@ class BatchingBackend(Backend):
         idx = (i // size) * n + ix * size + i % size
         return Batched(self, self.real.reindex(a.physical, self.batch_shape(sample), idx), sample)
 
+    # conv2d family: the image batch of a mapped first operand folds into the convolution's own
+    # batch when the second operand is shared; otherwise each sample is convolved on its own
+    def _conv(self, name, a, b, spec):
+        real = self.real
+        fn = getattr(real, name)
+        if not (self._mapped(a) or self._mapped(b)):
+            return fn(a, b, spec)
+        if self._mapped(a) and not self._mapped(b) and name != "conv2d_grad_weight":
+            n, width = a.shape[0], a.shape[1]
+            flat = real.reshape(a.physical, (self.batch * n, width))
+            out = fn(flat, b, spec)
+            return Batched(self, real.reshape(out, (self.batch, n) + tuple(out.shape[1:])), (n,) + tuple(out.shape[1:]))
+        outs = []
+        for i in range(self.batch):
+            ai = real.slice_axis0(a.physical, i) if self._mapped(a) else a
+            bi = real.slice_axis0(b.physical, i) if self._mapped(b) else b
+            outs.append(fn(ai, bi, spec))
+        return Batched(self, real.stack_axis0(outs), tuple(outs[0].shape))
+
+    def conv2d(self, x, w, spec):
+        return self._conv("conv2d", x, w, spec)
+
+    def conv2d_grad_input(self, up, w, spec):
+        return self._conv("conv2d_grad_input", up, w, spec)
+
+    def conv2d_grad_weight(self, x, up, spec):
+        return self._conv("conv2d_grad_weight", x, up, spec)
+
     def stack_axis0(self, xs):
         """Stack of samples: the physical [B, ...] buffers stacked to [n, B, ...], gathered to
         [B, n, ...]."""

@@ -50,6 +50,15 @@ class OracleBackend(Backend):
         n = int(np.prod(shape, dtype=np.int64))
         return _w(O.random_normal(seed, counter, n).reshape(shape))
 
+    def conv2d(self, x, w, spec):
+        return _w(O.conv2d(x.a.reshape(x.shape[0], -1), w.a, spec.ints()))
+
+    def conv2d_grad_input(self, up, w, spec):
+        return _w(O.conv2d_grad_input(up.a.reshape(up.shape[0], -1), w.a, spec.ints()))
+
+    def conv2d_grad_weight(self, x, up, spec):
+        return _w(O.conv2d_grad_weight(x.a.reshape(x.shape[0], -1), up.a.reshape(up.shape[0], -1), spec.ints()))
+
     def binary(self, op, a, b):
         return _w(O.binary(op, a.a, b.a).reshape(a.shape))
 

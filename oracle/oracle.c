@@ -963,3 +963,96 @@ void j4o_philox2x32_10(uint32_t c0, uint32_t c1, uint32_t key, uint32_t* out0, u
   *out0 = c0;
   *out1 = c1;
 }
+
+/* ------------------------------------------------------------------------------------------
+ * conv2d, conv2dGradInput, conv2dGradWeight: CpuBackend.java:479-609, float accumulation in the
+ * same loop order (image, out channel, output row, output column, in channel, kernel row, kernel
+ * column), taps in the zero padding skipped, zero upstream elements skipped in the gradients.
+ * ------------------------------------------------------------------------------------------ */
+typedef struct { int C, H, W, O, k, s, pad, OH, OW; } conv_geom;
+
+static int conv_geometry(int in_c, int in_h, int in_w, int out_c, int kernel, int stride, int pad, conv_geom* g) {
+  if (in_c < 1 || in_h < 1 || in_w < 1 || out_c < 1 || kernel < 1 || stride < 1 || pad < 0) return -1;
+  if (in_h + 2 * pad < kernel || in_w + 2 * pad < kernel) return -1;
+  g->C = in_c; g->H = in_h; g->W = in_w; g->O = out_c; g->k = kernel; g->s = stride; g->pad = pad;
+  g->OH = (in_h + 2 * pad - kernel) / stride + 1;
+  g->OW = (in_w + 2 * pad - kernel) / stride + 1;
+  return 0;
+}
+
+int j4o_conv2d(const float* x, const float* w, int64_t batch, int in_c, int in_h, int in_w, int out_c, int kernel,
+               int stride, int pad, float* out) {
+  conv_geom g;
+  if (conv_geometry(in_c, in_h, in_w, out_c, kernel, stride, pad, &g)) return -1;
+  const int64_t isz = (int64_t)g.C * g.H * g.W, osz = (int64_t)g.O * g.OH * g.OW, wsz = (int64_t)g.C * g.k * g.k;
+  for (int64_t b = 0; b < batch; b++)
+    for (int oc = 0; oc < g.O; oc++)
+      for (int oh = 0; oh < g.OH; oh++)
+        for (int ow = 0; ow < g.OW; ow++) {
+          float acc = 0.0f;
+          for (int ic = 0; ic < g.C; ic++)
+            for (int kh = 0; kh < g.k; kh++) {
+              const int ih = oh * g.s - g.pad + kh;
+              if (ih < 0 || ih >= g.H) continue;
+              for (int kw = 0; kw < g.k; kw++) {
+                const int iw = ow * g.s - g.pad + kw;
+                if (iw < 0 || iw >= g.W) continue;
+                acc += x[b * isz + ((int64_t)ic * g.H + ih) * g.W + iw] * w[oc * wsz + ((int64_t)ic * g.k + kh) * g.k + kw];
+              }
+            }
+          out[b * osz + ((int64_t)oc * g.OH + oh) * g.OW + ow] = acc;
+        }
+  return 0;
+}
+
+int j4o_conv2d_grad_input(const float* up, const float* w, int64_t batch, int in_c, int in_h, int in_w, int out_c,
+                          int kernel, int stride, int pad, float* dx) {
+  conv_geom g;
+  if (conv_geometry(in_c, in_h, in_w, out_c, kernel, stride, pad, &g)) return -1;
+  const int64_t isz = (int64_t)g.C * g.H * g.W, osz = (int64_t)g.O * g.OH * g.OW, wsz = (int64_t)g.C * g.k * g.k;
+  memset(dx, 0, (size_t)(batch * isz) * sizeof(float));
+  for (int64_t b = 0; b < batch; b++)
+    for (int oc = 0; oc < g.O; oc++)
+      for (int oh = 0; oh < g.OH; oh++)
+        for (int ow = 0; ow < g.OW; ow++) {
+          const float gv = up[b * osz + ((int64_t)oc * g.OH + oh) * g.OW + ow];
+          if (gv == 0.0f) continue;
+          for (int ic = 0; ic < g.C; ic++)
+            for (int kh = 0; kh < g.k; kh++) {
+              const int ih = oh * g.s - g.pad + kh;
+              if (ih < 0 || ih >= g.H) continue;
+              for (int kw = 0; kw < g.k; kw++) {
+                const int iw = ow * g.s - g.pad + kw;
+                if (iw < 0 || iw >= g.W) continue;
+                dx[b * isz + ((int64_t)ic * g.H + ih) * g.W + iw] += gv * w[oc * wsz + ((int64_t)ic * g.k + kh) * g.k + kw];
+              }
+            }
+        }
+  return 0;
+}
+
+int j4o_conv2d_grad_weight(const float* x, const float* up, int64_t batch, int in_c, int in_h, int in_w, int out_c,
+                           int kernel, int stride, int pad, float* dw) {
+  conv_geom g;
+  if (conv_geometry(in_c, in_h, in_w, out_c, kernel, stride, pad, &g)) return -1;
+  const int64_t isz = (int64_t)g.C * g.H * g.W, osz = (int64_t)g.O * g.OH * g.OW, wsz = (int64_t)g.C * g.k * g.k;
+  memset(dw, 0, (size_t)(g.O * wsz) * sizeof(float));
+  for (int64_t b = 0; b < batch; b++)
+    for (int oc = 0; oc < g.O; oc++)
+      for (int oh = 0; oh < g.OH; oh++)
+        for (int ow = 0; ow < g.OW; ow++) {
+          const float gv = up[b * osz + ((int64_t)oc * g.OH + oh) * g.OW + ow];
+          if (gv == 0.0f) continue;
+          for (int ic = 0; ic < g.C; ic++)
+            for (int kh = 0; kh < g.k; kh++) {
+              const int ih = oh * g.s - g.pad + kh;
+              if (ih < 0 || ih >= g.H) continue;
+              for (int kw = 0; kw < g.k; kw++) {
+                const int iw = ow * g.s - g.pad + kw;
+                if (iw < 0 || iw >= g.W) continue;
+                dw[oc * wsz + ((int64_t)ic * g.k + kh) * g.k + kw] += gv * x[b * isz + ((int64_t)ic * g.H + ih) * g.W + iw];
+              }
+            }
+        }
+  return 0;
+}

@@ -104,6 +104,15 @@ int j4o_aad_replay(int n, const int32_t* op, const int32_t* arg_a, const int32_t
                    int64_t count, int64_t seed, double* value, double* sumsq, double* grad);
 void j4o_philox2x32_10(uint32_t c0, uint32_t c1, uint32_t key, uint32_t* out0, uint32_t* out1);
 
+/* conv2d / conv2dGradInput / conv2dGradWeight (CpuBackend.java:479-609); ConvSpec as ints.
+ * Return -1 for a spec ConvSpec rejects. */
+int j4o_conv2d(const float* x, const float* w, int64_t batch, int in_c, int in_h, int in_w, int out_c, int kernel,
+               int stride, int pad, float* out);
+int j4o_conv2d_grad_input(const float* up, const float* w, int64_t batch, int in_c, int in_h, int in_w, int out_c,
+                          int kernel, int stride, int pad, float* dx);
+int j4o_conv2d_grad_weight(const float* x, const float* up, int64_t batch, int in_c, int in_h, int in_w, int out_c,
+                           int kernel, int stride, int pad, float* dw);
+
 #ifdef __cplusplus
 }
 #endif

@@ -90,6 +90,8 @@ def _declare(L):
     L.j4o_relu_backward.argtypes = [_f32p, _f32p, _i64, _f32p]
     L.j4o_fused.argtypes = [_i32p, ctypes.c_int, ctypes.POINTER(_f32p), ctypes.c_int, _i64,
                             _f32p]
+    for name in ("j4o_conv2d", "j4o_conv2d_grad_input", "j4o_conv2d_grad_weight"):
+        getattr(L, name).argtypes = [_f32p, _f32p, _i64] + [ctypes.c_int] * 7 + [_f32p]
     L.j4o_aad_replay.argtypes = [ctypes.c_int, _i32p, _i32p, _i32p, _f64p, _f64p, ctypes.c_int, _i32p,
                                  ctypes.c_int, _i32p, ctypes.c_int, ctypes.c_int, _i64, _i64, _i64,
                                  _f64p, _f64p, _f64p]
@@ -389,3 +391,36 @@ def aad_replay(ops, arg_a, arg_b, constants, inputs, input_nodes, output_nodes, 
     with ThreadPoolExecutor(threads) as ex:
         parts = list(ex.map(lambda r: run(*r), runs))
     return tuple(sum(p[i] for p in parts) for i in range(3))
+
+
+# ---- conv2d (CpuBackend.conv2d / conv2dGradInput / conv2dGradWeight) ----
+
+def _conv_out(spec):
+    c, h, w, o, k, s, p = spec
+    return o * ((h + 2 * p - k) // s + 1) * ((w + 2 * p - k) // s + 1)
+
+
+def conv2d(x, w, spec):
+    """spec = (in_c, in_h, in_w, out_c, kernel, stride, pad); x [batch, in_c*in_h*in_w]."""
+    x, w = _f32(x), _f32(w)
+    out = np.empty((x.shape[0], _conv_out(spec)), np.float32)
+    if lib().j4o_conv2d(_p(x), _p(w), x.shape[0], *spec, _p(out)):
+        raise ValueError("invalid conv spec")
+    return out
+
+
+def conv2d_grad_input(up, w, spec):
+    up, w = _f32(up), _f32(w)
+    c, h, wd = spec[0], spec[1], spec[2]
+    out = np.empty((up.shape[0], c * h * wd), np.float32)
+    if lib().j4o_conv2d_grad_input(_p(up), _p(w), up.shape[0], *spec, _p(out)):
+        raise ValueError("invalid conv spec")
+    return out
+
+
+def conv2d_grad_weight(x, up, spec):
+    x, up = _f32(x), _f32(up)
+    out = np.empty((spec[3], spec[0] * spec[4] * spec[4]), np.float32)
+    if lib().j4o_conv2d_grad_weight(_p(x), _p(up), x.shape[0], *spec, _p(out)):
+        raise ValueError("invalid conv spec")
+    return out
