@@ -440,6 +440,8 @@ def run_reference_gemm(args):
 
 
 def run_reference(args):
+    if args.config in CONV_CONFIGS:
+        return run_reference_conv(args)
     if args.config in AAD_CONFIGS:
         return run_reference_aad(args)
     if args.config in DECODER_CONFIGS:
@@ -910,6 +912,162 @@ def run_engine_gemm(args):
             "e2e": {"value": round(e2e, 3), "unit": "TFLOP/s", "h2d_bytes_per_step": m * k * 4,
                     "d2h_bytes_per_step": m * n * 4},
             "gpu_launches": K * 3,
+            "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"],
+                       "reasons": clk["reasons"], "samples": clk["samples"]},
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+# ------------------------------------------------------------------------------------------------
+# convolution (ComputeBackend.conv2d)
+# ------------------------------------------------------------------------------------------------
+
+CONV_CONFIGS = {
+    # name: (batch, ConvSpec ints (in_c, in_h, in_w, out_c, kernel, stride, pad), precision, label)
+    "conv_resnet": (64, (64, 56, 56, 64, 3, 1, 1), 0, "conv2d forward, ResNet-style 3x3 layer: x [64, 64x56x56], "
+                    "W [64, 64x3x3], stride 1, pad 1, fp32-accurate (3-term bf16 split on tcgen05)"),
+}
+CONV_METRIC = "conv2d TFLOP/s (2 x batch x outC x outH x outW x inC x k x k)"
+
+
+def run_reference_conv(args):
+    """The CPU conv2d (oracle restatement of CpuBackend.conv2d) on all host threads, one image per
+    task, over a sample of the batch per step."""
+    import numpy as np
+    from concurrent.futures import ThreadPoolExecutor
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return 0
+    sys.path.insert(0, HERE)
+    from oracle import oracle as O
+    batch, ints, prec, label = CONV_CONFIGS[args.config]
+    c, h, w_, o, k, st, pd = ints
+    oh, ow = (h + 2 * pd - k) // st + 1, (w_ + 2 * pd - k) // st + 1
+    flops_img = 2.0 * o * oh * ow * c * k * k
+    threads = os.cpu_count() or 1
+    rng = np.random.default_rng(0)
+    sample = min(batch, threads)
+    x = rng.standard_normal((sample, c * h * w_)).astype(np.float32)
+    wt = (rng.standard_normal((o, c * k * k)) * 0.05).astype(np.float32)
+    K, W = args.steps, max(3, args.warmup)
+    times = []
+    with ThreadPoolExecutor(threads) as ex:
+        for i in range(K + 1):
+            t0 = time.perf_counter()
+            list(ex.map(lambda j: O.conv2d(x[j:j + 1], wt, ints), range(sample)))
+            if i:
+                times.append(time.perf_counter() - t0)
+    sec = sum(times) / len(times)
+    v = flops_img * sample / sec / 1e12
+    print(json.dumps({"metric": CONV_METRIC, "value": round(v, 6), "unit": "TFLOP/s", "n_gpus": world, "steps": K,
+                      "warmup": W, "ms_per_step": round(sec * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+                      "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+                      "config": {"workload": label, "images_per_step": sample},
+                      "cpu_baseline": {"value": round(v, 6), "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                                       "sample": f"{sample} images per step, one per thread"},
+                      "e2e": {"value": round(v, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                              "d2h_bytes_per_step": 0}}), flush=True)
+    return 0
+
+
+def run_engine_conv(args):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    sys.path.insert(0, HERE)
+    from jax4j_b200.backend import B200Backend
+    from jax4j_b200.prng import PrngKey
+    from jax4j_b200.tensor import ConvSpec
+
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    be = B200Backend(local)
+    batch, ints, prec, label = CONV_CONFIGS[args.config]
+    spec = ConvSpec(*ints)
+    flops = 2.0 * batch * spec.out_channels * spec.out_height * spec.out_width * spec.weight_size
+    kx, kw = PrngKey.of(0).split(2)
+    x = be.random_normal(kx.seed, kx.counter + rank * batch * spec.input_size, spec.input_shape(batch))
+    w = be.scalar("MUL", be.random_normal(kw.seed, kw.counter, spec.weight_shape()), 0.05)
+    dev = torch.device("cuda", local)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    K, W = args.steps, max(3, args.warmup)
+    for _ in range(W):
+        y = be.conv2d(x, w, spec, prec)
+        del y
+    barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        barrier()
+        start.record()
+        for _ in range(K):
+            y = be.conv2d(x, w, spec, prec)
+        end.record()
+        barrier()
+    clk = clocks.summary()
+    ms = start.elapsed_time(end)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    step_ms = ms / K
+    value = world * flops * K / (ms * 1e-3) / 1e12
+    peaks_path = os.path.join(HERE, "MEASURED_PEAKS.json")
+    pk = json.load(open(peaks_path)) if os.path.exists(peaks_path) else {}
+    peak = float(pk.get("bf16_tflops_sustained", 1400.0))
+    # end to end through the public call: x from pinned host memory, y back to the host, every step
+    x_host = torch.from_numpy(np.ascontiguousarray(be.download(x))).pin_memory()
+    y_host = torch.empty(tuple(y.shape), dtype=torch.float32).pin_memory()
+    e_steps = max(2, min(K, 5))
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(e_steps):
+        x.tensor.view(-1).copy_(x_host.view(-1), non_blocking=True)
+        yy = be.conv2d(x, w, spec, prec)
+        y_host.view(-1).copy_(yy.tensor.view(-1), non_blocking=True)
+    e1.record()
+    barrier()
+    e2e = world * flops * e_steps / (e0.elapsed_time(e1) * 1e-3) / 1e12
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import oracle as O
+        xs = be.download(x)[:2]
+        t0 = time.perf_counter()
+        O.conv2d(xs, be.download(w), ints)
+        sec = time.perf_counter() - t0
+        cpu = {"value": round(flops / batch * 2 / sec / 1e12, 6), "unit": "TFLOP/s", "cores": 1, "kind": "port",
+               "sample": f"2 of {batch} images, oracle restatement of CpuBackend.conv2d, 1 thread"}
+    if rank == 0:
+        achieved = flops / (step_ms * 1e-3) / 1e12
+        line = {
+            "metric": CONV_METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": K,
+            "warmup": W, "ms_per_step": round(step_ms, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32 (3-term bf16)" if prec != 1 else "bf16", "data": "synthetic",
+            "config": {"workload": label, "batch": batch, "spec": list(ints),
+                       "l2": "patch matrix 462 MB > L2 per call",
+                       "parallelism": "replica" if world == 1 else f"{world} independent replicas",
+                       "timing": "K back-to-back calls (patch gather, tcgen05 GEMM, permute), CUDA events"},
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
+                         "frac": round(achieved / peak, 4), "traffic": None,
+                         "peak_source": "measured MEASURED_PEAKS.json bf16_tflops_sustained",
+                         "kernel": "conv2d call (im2col + tc_gemm + permute)", "kernel_avg_us": round(step_ms * 1e3, 1)},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e, 3), "unit": "TFLOP/s", "h2d_bytes_per_step": batch * spec.input_size * 4,
+                    "d2h_bytes_per_step": batch * spec.output_size * 4},
+            "gpu_launches": None,
             "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"],
                        "reasons": clk["reasons"], "samples": clk["samples"]},
         }
@@ -1400,6 +1558,8 @@ def run_engine_decoder(args):
 
 
 def run_engine(args):
+    if args.config in CONV_CONFIGS:
+        return run_engine_conv(args)
     if args.config in AAD_CONFIGS:
         return run_engine_aad(args)
     if args.config in DECODER_CONFIGS:
@@ -1595,7 +1755,7 @@ def main():
     p.add_argument("--warmup", type=int, default=None, help="warm-up steps (default per workload)")
     p.add_argument("--impl", choices=["engine", "reference"], default="engine")
     p.add_argument("--config", choices=sorted(CONFIGS) + sorted(TAPE_CONFIGS) + sorted(GEMM_CONFIGS)
-                   + sorted(DECODER_CONFIGS) + sorted(AAD_CONFIGS), default="q8_0_b8")
+                   + sorted(DECODER_CONFIGS) + sorted(AAD_CONFIGS) + sorted(CONV_CONFIGS), default="q8_0_b8")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--batch", type=int, default=None,
                    help="decoder workloads only: override the batch (e.g. a smaller case for profiling)")
@@ -1603,6 +1763,7 @@ def main():
     family = ("tape" if args.config in TAPE_CONFIGS else "gemm" if args.config in GEMM_CONFIGS
               else args.config if args.config in DECODER_CONFIGS
               else ("aad_eager" if args.config == "aad_asian_eager" else "aad") if args.config in AAD_CONFIGS
+              else "gemm" if args.config in CONV_CONFIGS
               else "gemv")
     steps, warmup = DEFAULT_STEPS[family]
     args.steps = steps if args.steps is None else args.steps

@@ -89,6 +89,10 @@ __global__ void col2im_kernel(const float* __restrict__ dcol, ConvGeom g, float*
   }
 }
 
+// Sub-buffers of one scratch allocation start on 256-byte boundaries (the GEMM stores its output
+// with 16-byte vector stores).
+int64_t aligned(int64_t floats) { return (floats + 63) / 64 * 64; }
+
 unsigned grid_for(int64_t n, int dev) {
   const int sms = device_ctx(dev)->sm_count;
   return (unsigned)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, (int64_t)sms * 16));
@@ -146,9 +150,10 @@ extern "C" int j4b_conv2d(j4b_buf x, j4b_buf w, j4b_buf out, J4B_CONV_ARGS, int 
   cudaStream_t stream = resolve_stream(dev, s);
   const int64_t col_n = g.K * g.B * g.P, y_n = g.O * g.B * g.P;
   Scratch sc(stream);
-  J4B_CUDA(cudaMallocAsync(&sc.p, (size_t)(col_n + y_n) * sizeof(float), stream), "cudaMallocAsync(conv2d patches)");
+  J4B_CUDA(cudaMallocAsync(&sc.p, (size_t)(aligned(col_n) + y_n) * sizeof(float), stream),
+           "cudaMallocAsync(conv2d patches)");
   float* col = (float*)sc.p;
-  float* y = col + col_n;
+  float* y = col + aligned(col_n);
   im2col_kernel<<<grid_for(col_n, dev), 256, 0, stream>>>((const float*)(uintptr_t)x, g, false, col);
   J4B_CHECK_LAUNCH("im2col_kernel");
   st = j4b_matmul(w, (j4b_buf)(uintptr_t)col, (j4b_buf)(uintptr_t)y, 1, g.O, g.K, g.B * g.P, precision, stream);
@@ -172,11 +177,11 @@ extern "C" int j4b_conv2d_grad_input(j4b_buf upstream, j4b_buf w, j4b_buf out, J
   cudaStream_t stream = resolve_stream(dev, s);
   const int64_t dy_n = g.O * g.B * g.P, wt_n = g.K * g.O, col_n = g.K * g.B * g.P;
   Scratch sc(stream);
-  J4B_CUDA(cudaMallocAsync(&sc.p, (size_t)(dy_n + wt_n + col_n) * sizeof(float), stream),
+  J4B_CUDA(cudaMallocAsync(&sc.p, (size_t)(aligned(dy_n) + aligned(wt_n) + col_n) * sizeof(float), stream),
            "cudaMallocAsync(conv2dGradInput scratch)");
   float* dy = (float*)sc.p;
-  float* wt = dy + dy_n;
-  float* dcol = wt + wt_n;
+  float* wt = dy + aligned(dy_n);
+  float* dcol = wt + aligned(wt_n);
   swap_outer_kernel<<<grid_for(dy_n, dev), 256, 0, stream>>>((const float*)(uintptr_t)upstream, g.O, g.B, g.P, false,
                                                                dy);
   J4B_CHECK_LAUNCH("swap_outer_kernel");
@@ -204,10 +209,10 @@ extern "C" int j4b_conv2d_grad_weight(j4b_buf x, j4b_buf upstream, j4b_buf out, 
   cudaStream_t stream = resolve_stream(dev, s);
   const int64_t dy_n = g.O * g.B * g.P, col_n = g.B * g.P * g.K;
   Scratch sc(stream);
-  J4B_CUDA(cudaMallocAsync(&sc.p, (size_t)(dy_n + col_n) * sizeof(float), stream),
+  J4B_CUDA(cudaMallocAsync(&sc.p, (size_t)(aligned(dy_n) + col_n) * sizeof(float), stream),
            "cudaMallocAsync(conv2dGradWeight scratch)");
   float* dy = (float*)sc.p;
-  float* colt = dy + dy_n;
+  float* colt = dy + aligned(dy_n);
   swap_outer_kernel<<<grid_for(dy_n, dev), 256, 0, stream>>>((const float*)(uintptr_t)upstream, g.O, g.B, g.P, false,
                                                                dy);
   J4B_CHECK_LAUNCH("swap_outer_kernel");

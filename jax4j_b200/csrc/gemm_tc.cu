@@ -218,7 +218,7 @@ __global__ void __launch_bounds__(kTcThreads, TERMS == 1 ? 2 : 1)
       asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
       const int col = n0 + c;
       if (row < p.M) {
-        if (col + 8 <= p.N && (p.ldc & 3) == 0) {
+        if (col + 8 <= p.N && (p.ldc & 3) == 0 && (reinterpret_cast<uintptr_t>(p.C) & 15) == 0) {
           float4* dst = reinterpret_cast<float4*>(crow + col);
           dst[0] = make_float4(__uint_as_float(v[0]), __uint_as_float(v[1]), __uint_as_float(v[2]), __uint_as_float(v[3]));
           dst[1] = make_float4(__uint_as_float(v[4]), __uint_as_float(v[5]), __uint_as_float(v[6]), __uint_as_float(v[7]));

@@ -132,3 +132,18 @@ def test_engine_rejects_bad_shapes(backend):
     w = backend.upload(np.zeros(spec.weight_shape(), np.float32), spec.weight_shape())
     with pytest.raises(ValueError, match="do not match"):
         backend.conv2d(x, w, spec)
+
+
+@pytest.mark.gpu
+def test_tensor_core_matmul_into_an_unaligned_output(backend):
+    """The tensor-core GEMM stores C with 16-byte vector stores only where C is 16-byte aligned;
+    an output that starts one float into a buffer (a conv scratch sub-buffer, a caller's slice)
+    takes the scalar store path."""
+    from jax4j_b200 import _lib
+    m, k, n = 9, 27, 40
+    a, b = rand((m, k), 31), rand((k, n), 32)
+    da, db = backend.upload(a, a.shape), backend.upload(b, b.shape)
+    out = backend.upload(np.zeros(m * n + 1, np.float32), (m * n + 1,))
+    _lib.call("j4b_matmul", da.ptr, db.ptr, out.ptr + 4, 1, m, k, n, 1, backend.stream)
+    got = backend.download(out)[1:].reshape(m, n)
+    assert normwise(got, a.astype(np.float64) @ b) <= 1e-2
