@@ -10,7 +10,11 @@
 //   conv2dGradInput  dXcol [K, B*P]  = W^T [K, outC] . dY' [outC, B*P], then a gather over the
 //                    taps that touch each input pixel (no atomics, deterministic)
 //   conv2dGradWeight dW [outC, K]    = dY' [outC, B*P] . XcolT [B*P, K]
+// On the tensor cores the forward runs the other way round: the patches are written straight
+// into the GEMM's bf16 operand (hi and lo halves for the fp32-accurate split), K-major
+// [B*P, Kp], the weights are the second operand, and C' [B*P, outC] is transposed per image.
 // Scratch (patches, transposes) is stream-ordered (cudaMallocAsync) and freed after the call.
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -44,6 +48,120 @@ __global__ void im2col_kernel(const float* __restrict__ x, ConvGeom g, bool tran
     float v = 0.0f;
     if (ih >= 0 && ih < g.H && iw >= 0 && iw < g.W) v = __ldg(x + ((b * g.C + ic) * g.H + ih) * g.W + iw);
     col[idx] = v;
+  }
+}
+
+// Patches as the bf16 GEMM operand: row = output position (b, oh, ow), 8 taps per thread, columns
+// past K zero; hi = bf16(v), lo = bf16(v - hi) when lo is given.
+__global__ void im2col_bf16_kernel(const float* __restrict__ x, ConvGeom g, int64_t kp, __nv_bfloat16* __restrict__ hi,
+                                   __nv_bfloat16* __restrict__ lo) {
+  // 32-bit index arithmetic (the host keeps B*P and K below 2^30); one division per coordinate
+  // per thread, then the tap (ic, kh, kw) steps along
+  const int groups = (int)(kp / 8), P = (int)g.P, OW = (int)g.OW, k = (int)g.k, kk = k * k, K = (int)g.K;
+  const int H = (int)g.H, W = (int)g.W, s = (int)g.s, pad = (int)g.pad;
+  const int64_t total = g.B * g.P * groups;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += stride) {
+    const int pos = (int)(idx / groups), c0 = (int)(idx - (int64_t)pos * groups) * 8;
+    const int b = pos / P, p = pos - b * P, oh = p / OW, ow = p - oh * OW;
+    const float* img = x + (int64_t)b * g.C * H * W;
+    int ic = c0 / kk, r = c0 - ic * kk, kh = r / k, kw = r - kh * k;
+    alignas(16) __nv_bfloat16 h8[8], l8[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      float v = 0.0f;
+      const int ih = oh * s - pad + kh, iw = ow * s - pad + kw;
+      if (c0 + u < K && ih >= 0 && ih < H && iw >= 0 && iw < W) v = __ldg(img + ((int64_t)ic * H + ih) * W + iw);
+      h8[u] = __float2bfloat16_rn(v);
+      l8[u] = __float2bfloat16_rn(v - __bfloat162float(h8[u]));
+      if (++kw == k) {
+        kw = 0;
+        if (++kh == k) {
+          kh = 0;
+          ++ic;
+        }
+      }
+    }
+    *reinterpret_cast<uint4*>(hi + (int64_t)pos * kp + c0) = *reinterpret_cast<const uint4*>(h8);
+    if (lo) *reinterpret_cast<uint4*>(lo + (int64_t)pos * kp + c0) = *reinterpret_cast<const uint4*>(l8);
+  }
+}
+
+// The same operand, one CTA per output row (b, oh). The k input rows of every channel that the
+// row's windows cover are staged in shared memory with coalesced loads (zeros in the padding),
+// with a table of each tap's offset into the stage (taps past K point at a zero slot); then each
+// warp takes an output position and its lanes consecutive 8-tap groups, so a warp writes 512
+// contiguous bytes per pass (no integer division in either phase). Shared
+// memory: (C * k * Wn + 1) floats + kp ints, Wn = (OW - 1) * stride + k.
+__global__ void im2col_rows_bf16_kernel(const float* __restrict__ x, ConvGeom g, int64_t kp,
+                                        __nv_bfloat16* __restrict__ hi, __nv_bfloat16* __restrict__ lo) {
+  extern __shared__ __align__(16) float rows[];
+  const int C = (int)g.C, H = (int)g.H, W = (int)g.W, k = (int)g.k, s = (int)g.s, pad = (int)g.pad;
+  const int OW = (int)g.OW, OH = (int)g.OH, K = (int)g.K, kk = k * k, kpi = (int)kp;
+  const int Wn = (OW - 1) * s + k, zero = C * k * Wn;
+  int* tapoff = reinterpret_cast<int*>(rows + (zero + 4) / 4 * 4);  // 16-byte aligned (int4 reads)
+  const int b = blockIdx.x / OH, oh = blockIdx.x - b * OH;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  const float* img = x + (int64_t)b * C * H * W;
+  for (int c = warp; c < C; c += nwarps)
+    for (int kh = 0; kh < k; ++kh) {
+      const int ih = oh * s - pad + kh;
+      const bool row_in = ih >= 0 && ih < H;
+      const float* src = img + ((int64_t)c * H + ih) * W;
+      float* dst = rows + (c * k + kh) * Wn;
+      for (int j = lane; j < Wn; j += 32) {
+        const int iw = j - pad;
+        dst[j] = (row_in && iw >= 0 && iw < W) ? __ldg(src + iw) : 0.0f;
+      }
+    }
+  for (int t = threadIdx.x; t < kpi; t += blockDim.x) {
+    int off = zero;
+    if (t < K) {
+      const int ic = t / kk, r = t - ic * kk, kh = r / k, kw = r - kh * k;
+      off = (ic * k + kh) * Wn + kw;
+    }
+    tapoff[t] = off;
+  }
+  if (threadIdx.x == 0) rows[zero] = 0.0f;
+  __syncthreads();
+  const int groups = kpi / 8;
+  const int64_t row0 = ((int64_t)b * OH + oh) * OW;
+  for (int ow = warp; ow < OW; ow += nwarps) {
+    const int base = ow * s;
+    __nv_bfloat16* hrow = hi + (row0 + ow) * kp;
+    __nv_bfloat16* lrow = lo ? lo + (row0 + ow) * kp : nullptr;
+    for (int gi = lane; gi < groups; gi += 32) {
+      const int c0 = gi * 8;
+      const int4 o0 = *reinterpret_cast<const int4*>(tapoff + c0);
+      const int4 o1 = *reinterpret_cast<const int4*>(tapoff + c0 + 4);
+      const int off[8] = {o0.x, o0.y, o0.z, o0.w, o1.x, o1.y, o1.z, o1.w};
+      alignas(16) __nv_bfloat162 h4[4], l4[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float v0 = rows[off[2 * u] + (off[2 * u] == zero ? 0 : base)];
+        const float v1 = rows[off[2 * u + 1] + (off[2 * u + 1] == zero ? 0 : base)];
+        h4[u] = __float22bfloat162_rn(make_float2(v0, v1));
+        const float2 hf = __bfloat1622float2(h4[u]);
+        l4[u] = __float22bfloat162_rn(make_float2(v0 - hf.x, v1 - hf.y));
+      }
+      *reinterpret_cast<uint4*>(hrow + c0) = *reinterpret_cast<const uint4*>(h4);
+      if (lrow) *reinterpret_cast<uint4*>(lrow + c0) = *reinterpret_cast<const uint4*>(l4);
+    }
+  }
+}
+
+// out[b][o][p] = c[b*P + p][o]: 32 x 32 tiles through shared memory, one image per blockIdx.z.
+__global__ void positions_to_channels_kernel(const float* __restrict__ c, int64_t P, int64_t O, float* __restrict__ out) {
+  __shared__ float tile[32][33];
+  const int64_t b = blockIdx.z, p0 = (int64_t)blockIdx.x * 32, o0 = (int64_t)blockIdx.y * 32;
+  for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+    const int64_t p = p0 + r, o = o0 + threadIdx.x;
+    if (p < P && o < O) tile[r][threadIdx.x] = __ldg(c + (b * P + p) * O + o);
+  }
+  __syncthreads();
+  for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+    const int64_t o = o0 + r, p = p0 + threadIdx.x;
+    if (p < P && o < O) out[(b * O + o) * P + p] = tile[threadIdx.x][r];
   }
 }
 
@@ -88,6 +206,9 @@ __global__ void col2im_kernel(const float* __restrict__ dcol, ConvGeom g, float*
     dx[idx] = acc;
   }
 }
+
+// Largest per-row input stage for the shared-memory im2col (two CTAs per SM fit).
+constexpr int64_t kRowStageBytes = 96 * 1024;
 
 // Sub-buffers of one scratch allocation start on 256-byte boundaries (the GEMM stores its output
 // with 16-byte vector stores).
@@ -148,6 +269,43 @@ extern "C" int j4b_conv2d(j4b_buf x, j4b_buf w, j4b_buf out, J4B_CONV_ARGS, int 
   if (st) return st;
   DeviceGuard guard(dev);
   cudaStream_t stream = resolve_stream(dev, s);
+  const int64_t M = g.B * g.P;
+  if ((precision != 0 || M * g.O * g.K >= (int64_t(1) << 24)) && M >= 128 && M < (int64_t(1) << 30) &&
+      g.K < (int64_t(1) << 30)) {
+    // tensor cores: bf16 patches [M, Kp] . W^T -> C' [M, O] -> out [B, O, P]
+    const int terms = precision == 1 ? 1 : 3;
+    const int64_t kp = (g.K + 63) / 64 * 64;
+    const int64_t a_n = aligned(M * kp / 2), b_n = aligned(g.O * kp / 2);  // in floats (2 bf16 each)
+    Scratch sc(stream);
+    J4B_CUDA(cudaMallocAsync(&sc.p, (size_t)(2 * a_n + 2 * b_n + M * g.O) * sizeof(float), stream),
+             "cudaMallocAsync(conv2d operands)");
+    float* base = (float*)sc.p;
+    __nv_bfloat16* ahi = (__nv_bfloat16*)base;
+    __nv_bfloat16* alo = terms == 3 ? (__nv_bfloat16*)(base + a_n) : nullptr;
+    __nv_bfloat16* bhi = (__nv_bfloat16*)(base + 2 * a_n);
+    __nv_bfloat16* blo = terms == 3 ? (__nv_bfloat16*)(base + 2 * a_n + b_n) : nullptr;
+    float* cbuf = base + 2 * a_n + 2 * b_n;
+    const int64_t row_smem = (g.C * g.k * ((g.OW - 1) * g.s + g.k) + 1) * (int64_t)sizeof(float) + 16 + kp * 4;
+    if (row_smem <= kRowStageBytes && g.B * g.OH <= INT32_MAX) {
+      J4B_CUDA(cudaFuncSetAttribute(im2col_rows_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)kRowStageBytes),
+               "cudaFuncSetAttribute(im2col_rows_bf16_kernel)");
+      im2col_rows_bf16_kernel<<<(unsigned)(g.B * g.OH), 256, (size_t)row_smem, stream>>>((const float*)(uintptr_t)x, g,
+                                                                                          kp, ahi, alo);
+      J4B_CHECK_LAUNCH("im2col_rows_bf16_kernel");
+    } else {
+      im2col_bf16_kernel<<<grid_for(M * (kp / 8), dev), 256, 0, stream>>>((const float*)(uintptr_t)x, g, kp, ahi, alo);
+      J4B_CHECK_LAUNCH("im2col_bf16_kernel");
+    }
+    st = tc_split_rows((const float*)(uintptr_t)w, g.O, g.K, g.K, kp, bhi, blo, stream);
+    if (st) return st;
+    st = tc_gemm_bf16(ahi, alo, M, kp, bhi, blo, g.O, terms, cbuf, dev, stream);
+    if (st) return st;
+    dim3 tg((unsigned)((g.P + 31) / 32), (unsigned)((g.O + 31) / 32), (unsigned)g.B);
+    positions_to_channels_kernel<<<tg, dim3(32, 8), 0, stream>>>(cbuf, g.P, g.O, (float*)(uintptr_t)out);
+    J4B_CHECK_LAUNCH("positions_to_channels_kernel");
+    return J4B_OK;
+  }
   const int64_t col_n = g.K * g.B * g.P, y_n = g.O * g.B * g.P;
   Scratch sc(stream);
   J4B_CUDA(cudaMallocAsync(&sc.p, (size_t)(aligned(col_n) + y_n) * sizeof(float), stream),

@@ -347,13 +347,55 @@ cudaError_t launch_tc(const CUtensorMap& ah, const CUtensorMap& al, const CUtens
 
 }  // namespace
 
+// C (m x n, row stride n) = A . Bt^T with both operands already bf16 hi (and lo, terms 3),
+// K-major [m, kp] and [n, kp], kp a multiple of 64 with zero padding.
+int tc_gemm_bf16(const __nv_bfloat16* a_hi, const __nv_bfloat16* a_lo, int64_t m, int64_t kp,
+                 const __nv_bfloat16* bt_hi, const __nv_bfloat16* bt_lo, int64_t n, int terms, float* out, int dev,
+                 cudaStream_t stream) {
+  if (m == 0 || n == 0) return J4B_OK;
+  if (kp % kBK) return set_error(J4B_EINVAL, "tensor-core operand width %lld is not a multiple of %d", (long long)kp, kBK);
+  int* status = tc_status(dev);
+  if (!status) return set_error(J4B_ENOMEM, "tensor-core status word allocation failed");
+  const bool split = terms == 3;
+  CUtensorMap mah, mal, mbh, mbl;
+  const int bn = split ? tc_bn<3>() : tc_bn<1>();
+  if (!make_map(&mah, a_hi, m, kp, kBM) || !make_map(&mbh, bt_hi, n, kp, bn) ||
+      (split && (!make_map(&mal, a_lo, m, kp, kBM) || !make_map(&mbl, bt_lo, n, kp, bn))))
+    return set_error(J4B_ECUDA, "cuTensorMapEncodeTiled failed for the matmul operands");
+  if (!split) {
+    mal = mah;
+    mbl = mbh;
+  }
+  TcArgs args;
+  args.M = (int)m;
+  args.N = (int)n;
+  args.Kp = (int)kp;
+  args.terms = terms;
+  args.C = out;
+  args.ldc = n;
+  args.status = status;
+  cudaError_t e = split ? launch_tc<3>(mah, mal, mbh, mbl, args, stream) : launch_tc<1>(mah, mal, mbh, mbl, args, stream);
+  if (e != cudaSuccess) return cuda_error(e, "tc_gemm_kernel");
+  count_launch(1);
+  return J4B_OK;
+}
+
+// f32 [rows, cols] (row stride ld) -> bf16 hi (and lo) [rows, kp] with zero-padded columns.
+int tc_split_rows(const float* src, int64_t rows, int64_t cols, int64_t ld, int64_t kp, __nv_bfloat16* hi,
+                  __nv_bfloat16* lo, cudaStream_t stream) {
+  dim3 grid((unsigned)((kp / 8 + 127) / 128), (unsigned)std::min<int64_t>(rows, 65535));
+  split_rows_kernel<<<grid, 128, 0, stream>>>(src, rows, cols, ld, kp, hi, lo);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_error(e, "split_rows_kernel");
+  count_launch(1);
+  return J4B_OK;
+}
+
 // C (m x n, row stride n) = A (m x k, f32 row-major) . Bt^T, with Bt given as bf16 hi (and lo)
 // [n, kp] K-major (kp = k rounded up to 64, zero-padded). A is converted here.
 int tc_gemm_bt(const float* a, int64_t m, int64_t k, const __nv_bfloat16* bt_hi, const __nv_bfloat16* bt_lo,
                int64_t n, int terms, float* out, int dev, cudaStream_t stream) {
   if (m == 0 || n == 0) return J4B_OK;
-  int* status = tc_status(dev);
-  if (!status) return set_error(J4B_ENOMEM, "tensor-core status word allocation failed");
   const int64_t kp = (k + kBK - 1) / kBK * kBK;
   const bool split = terms == 3;
   const size_t abytes = (size_t)(m * kp) * 2;
@@ -361,33 +403,8 @@ int tc_gemm_bt(const float* a, int64_t m, int64_t k, const __nv_bfloat16* bt_hi,
   J4B_CUDA(cudaMallocAsync(&scratch, 2 * abytes + 512, stream), "cudaMallocAsync(matmul operand)");
   __nv_bfloat16* ahi = (__nv_bfloat16*)scratch;
   __nv_bfloat16* alo = split ? (__nv_bfloat16*)((uint8_t*)scratch + ((abytes + 255) & ~size_t(255))) : nullptr;
-  {
-    dim3 grid((unsigned)((kp / 8 + 127) / 128), (unsigned)std::min<int64_t>(m, 65535));
-    split_rows_kernel<<<grid, 128, 0, stream>>>(a, m, k, k, kp, ahi, alo);
-  }
-  int rc = J4B_OK;
-  CUtensorMap mah, mal, mbh, mbl;
-  const int bn = split ? tc_bn<3>() : tc_bn<1>();
-  if (!make_map(&mah, ahi, m, kp, kBM) || !make_map(&mbh, bt_hi, n, kp, bn) ||
-      (split && (!make_map(&mal, alo, m, kp, kBM) || !make_map(&mbl, bt_lo, n, kp, bn)))) {
-    rc = set_error(J4B_ECUDA, "cuTensorMapEncodeTiled failed for the matmul operands");
-  } else {
-    if (!split) {
-      mal = mah;
-      mbl = mbh;
-    }
-    TcArgs args;
-    args.M = (int)m;
-    args.N = (int)n;
-    args.Kp = (int)kp;
-    args.terms = terms;
-    args.C = out;
-    args.ldc = n;
-    args.status = status;
-    cudaError_t e = split ? launch_tc<3>(mah, mal, mbh, mbl, args, stream) : launch_tc<1>(mah, mal, mbh, mbl, args, stream);
-    if (e != cudaSuccess) rc = cuda_error(e, "tc_gemm_kernel");
-    count_launch(2);
-  }
+  int rc = tc_split_rows(a, m, k, k, kp, ahi, alo, stream);
+  if (rc == J4B_OK) rc = tc_gemm_bf16(ahi, alo, m, kp, bt_hi, bt_lo, n, terms, out, dev, stream);
   cudaFreeAsync(scratch, stream);
   return rc;
 }

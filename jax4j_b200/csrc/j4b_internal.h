@@ -65,6 +65,14 @@ namespace j4b {
 // rounded up to 64 with zero padding
 int tc_gemm_bt(const float* a, int64_t m, int64_t k, const __nv_bfloat16* bt_hi, const __nv_bfloat16* bt_lo,
                int64_t n, int terms, float* out, int dev, cudaStream_t stream);
+// C (m x n) = A . Bt^T with both operands bf16 hi (and lo for terms 3) K-major [m, kp] / [n, kp],
+// kp a multiple of 64, zero-padded
+int tc_gemm_bf16(const __nv_bfloat16* a_hi, const __nv_bfloat16* a_lo, int64_t m, int64_t kp,
+                 const __nv_bfloat16* bt_hi, const __nv_bfloat16* bt_lo, int64_t n, int terms, float* out, int dev,
+                 cudaStream_t stream);
+// f32 [rows, cols] (row stride ld) -> bf16 hi (and lo) [rows, kp], zero-padded columns
+int tc_split_rows(const float* src, int64_t rows, int64_t cols, int64_t ld, int64_t kp, __nv_bfloat16* hi,
+                  __nv_bfloat16* lo, cudaStream_t stream);
 
 // ---- collectives over peer memory (peer.cu) ----
 constexpr int kMaxPeerRanks = 8;

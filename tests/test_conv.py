@@ -18,6 +18,7 @@ SPECS = [  # (batch, spec)
     (2, ConvSpec(4, 9, 9, 6, 3, 2, 0)),
     (1, ConvSpec(2, 6, 5, 3, 5, 1, 2)),
     (4, ConvSpec(8, 16, 16, 16, 3, 2, 1)),
+    (8, ConvSpec(32, 32, 32, 64, 3, 1, 1)),  # large enough for the tensor-core forward at fp32 accuracy
 ]
 
 
