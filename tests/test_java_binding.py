@@ -1,0 +1,143 @@
+"""The Java FFM binding module (jax4j_b200/java/jax4j-engine-b200) against the C ABI it binds.
+
+No JDK is installed on the build machine, so the Java sources are checked here structurally:
+every downcall names a function that include/jax4j_b200.h declares and libjax4j_b200.so exports,
+with an argument layout list whose length and kinds (int, int64/size_t/j4b_buf, float, double,
+pointer) match the C parameter list; the service files name classes that exist; the Op and
+AadOp ordinals the binding passes are the engine's op codes."""
+import ctypes
+import pathlib
+import re
+
+import pytest
+
+ROOT = pathlib.Path(__file__).resolve().parents[1]
+MODULE = ROOT / "jax4j_b200" / "java" / "jax4j-engine-b200"
+SOURCES = sorted((MODULE / "src" / "main" / "java").rglob("*.java"))
+LETTER = {"JAVA_INT": "I", "JAVA_LONG": "L", "JAVA_FLOAT": "F", "JAVA_DOUBLE": "D", "ADDRESS": "P",
+          "I": "I", "L": "L", "F": "F", "D": "D", "P": "P"}
+
+
+def c_signatures() -> dict:
+    text = (ROOT / "include" / "jax4j_b200.h").read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    out = {}
+    for name, params in re.findall(r"\bint\s+(j4b_\w+)\s*\(([^)]*)\)\s*;", text):
+        kinds = []
+        for p in (x.strip() for x in params.split(",")):
+            if not p or p == "void":
+                continue
+            if "*" in p or p.split()[0] in ("j4b_stream", "j4b_qweight_t", "j4b_aad_t"):
+                kinds.append("P")
+            elif p.split()[0] in ("j4b_buf", "int64_t", "uint64_t", "size_t"):
+                kinds.append("L")
+            elif p.split()[0] == "int":
+                kinds.append("I")
+            elif p.split()[0] == "float":
+                kinds.append("F")
+            elif p.split()[0] == "double":
+                kinds.append("D")
+            else:
+                raise AssertionError(f"unmapped C parameter type in {name}: {p}")
+        out[name] = "".join(kinds)
+    return out
+
+
+def java_downcalls() -> list:
+    """(file, function, layout letters) for every call(...) and fn(...) in the module."""
+    found = []
+    for src in SOURCES:
+        text = src.read_text()
+        arrays = {n: "".join(LETTER[x.strip()] for x in body.split(",") if x.strip())
+                  for n, body in re.findall(r"MemoryLayout\[\]\s+(\w+)\s*=\s*sig\(([^)]*)\)", text)}
+        for name, arg in re.findall(r'\bcall\(\s*(?:entry|"(j4b_\w+)")\s*,\s*(sig\([^)]*\)|\w+)', text):
+            if not name:
+                continue
+            if arg.startswith("sig("):
+                letters = "".join(LETTER[x.strip()] for x in arg[4:-1].split(",") if x.strip())
+            else:
+                letters = arrays[arg]
+            found.append((src.name, name, letters))
+        for name, rest in re.findall(r'\bfn\(\s*"(j4b_\w+)"((?:\s*,\s*\w+)*)\s*\)', text):
+            found.append((src.name, name, "".join(LETTER[x.strip()] for x in rest.split(",") if x.strip())))
+        # call(entry, ...) forwards a name chosen at the call site: resolve those names too
+        for helper, layout in (("axisReduce", "AXIS"), ("conv", "CONV")):
+            for name in re.findall(helper + r'\(\s*"(j4b_\w+)"', text):
+                found.append((src.name, name, arrays[layout]))
+    return found
+
+
+def test_every_downcall_matches_the_c_declaration():
+    sigs = c_signatures()
+    calls = java_downcalls()
+    assert len({c[1] for c in calls}) >= 40
+    for src, name, letters in calls:
+        assert name in sigs, f"{src}: {name} is not declared in include/jax4j_b200.h"
+        assert letters == sigs[name], f"{src}: {name} binds ({letters}), the header declares ({sigs[name]})"
+
+
+def test_every_bound_function_is_exported(oracle):
+    from jax4j_b200 import _lib
+    lib = ctypes.CDLL(_lib.LIB_PATH)
+    for _, name, _ in java_downcalls():
+        assert hasattr(lib, name), f"{name} is not exported by {_lib.LIB_PATH}"
+
+
+def test_service_files_name_existing_provider_classes():
+    services = MODULE / "src" / "main" / "resources" / "META-INF" / "services"
+    wanted = {"com.nablatensor.jax4j.tensor.spi.ComputeBackend": "implements ComputeBackend, QuantizedOps",
+              "com.nablatensor.jax4j.engine.AadEngine": "extends B200AadEngines.Base"}
+    for service, marker in wanted.items():
+        names = [n.strip() for n in (services / service).read_text().splitlines() if n.strip()]
+        assert names
+        for cls in names:
+            path = MODULE / "src" / "main" / "java" / (cls.replace(".", "/") + ".java")
+            text = path.read_text()
+            simple = cls.rsplit(".", 1)[1]
+            assert f"public final class {simple}" in text and marker in text
+            assert re.search(rf"public {simple}\(\)", text) or "public B200Backend" not in text
+
+
+def test_op_codes_are_the_reference_ordinals():
+    """Op (tensor/Op.java) and AadOp ordinals are what the binding passes as op codes."""
+    from jax4j_b200 import aad, expr
+    ops = ["ADD", "SUB", "MUL", "DIV", "MAX", "MIN", "NEG", "EXP", "LOG", "SQRT", "RSQRT", "TANH",
+           "SIGMOID", "RELU", "ABS", "SIGN"]
+    assert [expr.OP[o] for o in ops] == list(range(16))
+    assert [m.name for m in aad.AadOp] == ["CONST", "INPUT", "RANDN", "RANDU", "ADD", "SUB", "MUL", "DIV",
+                                          "NEG", "EXP", "LOG", "SQRT", "MAX", "MIN", "ABS"]
+
+
+@pytest.mark.parametrize("path", SOURCES, ids=lambda p: p.name)
+def test_sources_are_balanced_and_packaged(path):
+    text = path.read_text()
+    stripped = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    stripped = re.sub(r'"(?:\\.|[^"\\])*"', '""', re.sub(r"//[^\n]*", "", stripped))
+    for a, b in ("()", "{}", "[]"):
+        assert stripped.count(a) == stripped.count(b), f"{path.name}: unbalanced {a}{b}"
+    assert text.startswith("package com.nablatensor.jax4j.backend.b200;")
+
+
+def test_one_call_fused_tape_layout_plans(oracle):
+    """B200Backend.fused serialises an expression as a one-call tape: header, n input shapes and
+    the output shape (input 0's), inputs 0..n-1, output n, then the call (opcode 2, out n, n ins,
+    postfix program with scalars as signed lo32/hi32). The engine's planner accepts that layout
+    (j4b_tape_dryrun: NVRTC, no device) for x * y + 3 over two [4, 5] inputs."""
+    import numpy as np
+    import struct
+    from jax4j_b200 import _lib
+    from jax4j_b200.jit import TAPE_MAGIC
+    lo, hi = struct.unpack("<ii", struct.pack("<d", 3.0))
+    program = [0, 0, 0, 1, 2, _lib.OP["MUL"], 3, _lib.OP["ADD"], lo, hi]
+    n, dims = 2, [4, 5]
+    words = [TAPE_MAGIC, n + 1, n, 1, 1]
+    for _ in range(n + 1):
+        words += [len(dims)] + dims
+    words += list(range(n)) + [n]
+    words += [2, n, n] + list(range(n)) + [len(program)] + program
+    w = np.asarray(words, np.int64)
+    st = _lib.TapeStats()
+    size = ctypes.c_size_t()
+    _lib.call("j4b_tape_dryrun", w.ctypes.data_as(ctypes.POINTER(ctypes.c_int64)), w.size, ctypes.byref(st),
+              None, 0, ctypes.byref(size))
+    assert (st.calls, st.groups) == (1, 1)
