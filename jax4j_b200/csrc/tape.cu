@@ -48,6 +48,8 @@ enum : int {
 
 constexpr int64_t kTapeMagic = 0x314550415442344ALL;  // "J4BTAPE1"
 constexpr int64_t kSharedMax = 16384;  // largest row-invariant vector kept per CTA
+// fold kernel: 8 warps per 32-column slice (32 warps measured 2% slower per tape step)
+constexpr int kFoldThreads = 256;
 constexpr int64_t kRowMax = 16384;     // widest row a CTA keeps in registers
 constexpr int kMaxPtrs = 96;
 
@@ -956,7 +958,9 @@ __device__ __forceinline__ float jmin(float a, float b) {
 }
 __device__ __forceinline__ float jsign(float x) { return x > 0.0f ? 1.0f : (x < 0.0f ? -1.0f : 0.0f); }
 // exp and sigmoid use the fast exponential (ex2.approx: a few ulp, far inside the engine's
-// fp32 tolerance against the reference's double-evaluated transcendentals)
+// fp32 tolerance against the reference's double-evaluated transcendentals). rsqrt stays the
+// correctly rounded reciprocal of the correctly rounded root: rsqrtf measured 40% slower on the
+// RMSNorm gradient tape (62 -> 88 us), although it executes fewer instructions.
 __device__ __forceinline__ float jexp(float x) { return __expf(x); }
 __device__ __forceinline__ float jsigmoid(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
 __device__ __forceinline__ float jrsqrt(float x) { return __frcp_rn(__fsqrt_rn(x)); }
@@ -988,6 +992,30 @@ template <int NT> __device__ __forceinline__ double block_sum(double v, double* 
   double tot = lane < NT / 32 ? r[lane] : 0.0;
   #pragma unroll
   for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
+  return tot;
+}
+// Row sums: the same in float, and the per-warp values summed by every thread straight from
+// shared memory in warp order (broadcast vector loads instead of a second shuffle butterfly: a
+// short dependent chain, since every row waits on its reductions). The partials are per-thread
+// float sums of at most a few dozen elements, so float here stays far inside the fp32 tolerance
+// of the reference's double accumulator.
+template <int NT> __device__ __forceinline__ float block_sumf(float v, double* red, int& rp) {
+  float* r = reinterpret_cast<float*>(red + (rp++ & 1) * (2 * (NT / 32)));
+  #pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  if ((threadIdx.x & 31) == 0) r[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float tot = 0.0f;
+  if constexpr (NT / 32 >= 4) {
+    #pragma unroll
+    for (int w = 0; w < NT / 32; w += 4) {
+      const float4 p = *reinterpret_cast<const float4*>(r + w);
+      tot += (p.x + p.y) + (p.z + p.w);
+    }
+  } else {
+    #pragma unroll
+    for (int w = 0; w < NT / 32; ++w) tot += r[w];
+  }
   return tot;
 }
 template <int NT> __device__ __forceinline__ float block_jmax(float v, double* red, int& rp) {
@@ -1127,6 +1155,15 @@ struct Gen {
       : T(tp), t(tp.ir), V(tp.V), G(tp.groups[g]), gi(g), ptrs(p), tables(tb) {}
 
   int E(int64_t W) const { return (int)((W + 4LL * NT - 1) / (4LL * NT)); }
+
+  // Bounds test `var + off < lim` of the slot j = (e * NT + t) * 4 + q of a row loop (c4 * 4
+  // for the float4 form), with a leading term that is a compile-time constant once e is
+  // unrolled: when even thread NT - 1's slots of step e are in range, (e + 1) * 4 NT + off <=
+  // lim, the whole test folds to true and no per-element compare is executed.
+  std::string jlt(int64_t off, int64_t lim, const char* var = "j") const {
+    const std::string o = off ? " + " + istr(off) : "";
+    return "((e + 1) * " + istr(4LL * NT) + o + " <= " + istr(lim) + " || " + var + o + " < " + istr(lim) + ")";
+  }
 
   // pointer slot for a materialised value (its storage root + element offset) -> "P<k>" symbol
   int canon(int b) const {
@@ -1310,7 +1347,7 @@ struct Gen {
         int64_t se = a.param / (4LL * NT);
         std::string es = "(e + " + std::to_string(se) + ")";
         std::string eb = std::to_string(E(a.Wb));
-        return "((" + es + " >= 0 && " + es + " < " + eb + " && j + " + istr(a.param) + " < " + istr(a.Wb) +
+        return "((" + es + " >= 0 && " + es + " < " + eb + " && " + jlt(a.param, a.Wb) +
                ") ? " + vname(a.base) + "[(" + es + " < 0 ? 0 : (" + es + " >= " + eb + " ? 0 : " + es +
                ")) * 4 + q] : 0.0f)";
       }
@@ -1341,7 +1378,7 @@ struct Gen {
       os << "  #pragma unroll\n  for (int e = 0; e < " << E(W) << "; ++e) {\n"
          << "    const long long c4 = (long long)e * " << NT << " + t;\n"
          << "    float4 x4 = make_float4(0.f, 0.f, 0.f, 0.f);\n"
-         << "    if (c4 * 4 < " << istr(W) << ") x4 = __ldg(reinterpret_cast<const float4*>(" << p << rowoff
+         << "    if (" << jlt(0, W, "c4 * 4") << ") x4 = __ldg(reinterpret_cast<const float4*>(" << p << rowoff
          << ") + c4);\n"
          << "    " << nm << "[e * 4] = x4.x; " << nm << "[e * 4 + 1] = x4.y; " << nm << "[e * 4 + 2] = x4.z; "
          << nm << "[e * 4 + 3] = x4.w;\n  }\n";
@@ -1349,7 +1386,7 @@ struct Gen {
       os << "  #pragma unroll\n  for (int e = 0; e < " << E(W) << "; ++e) {\n"
          << "    #pragma unroll\n    for (int q = 0; q < 4; ++q) {\n"
          << "      const long long j = ((long long)e * " << NT << " + t) * 4 + q;\n"
-         << "      " << nm << "[e * 4 + q] = j < " << istr(W) << " ? __ldg(" << p << rowoff
+         << "      " << nm << "[e * 4 + q] = " << jlt(0, W) << " ? __ldg(" << p << rowoff
          << " + j) : 0.0f;\n    }\n  }\n";
     }
   }
@@ -1360,7 +1397,7 @@ struct Gen {
     os << "  #pragma unroll\n  for (int e = 0; e < " << E(V[b].W) << "; ++e) {\n"
        << "    #pragma unroll\n    for (int q = 0; q < 4; ++q) {\n"
        << "      const long long j = ((long long)e * " << NT << " + t) * 4 + q;\n"
-       << "      if (j < " << istr(V[b].W) << ") sm[" << off << " + j] = " << vname(b) << "[e * 4 + q];\n"
+       << "      if (" << jlt(0, V[b].W) << ") sm[" << off << " + j] = " << vname(b) << "[e * 4 + q];\n"
        << "    }\n  }\n  __syncthreads();\n";
   }
 
@@ -1401,14 +1438,17 @@ struct Gen {
         return "*" + fstr(1.0f / fv);
       return fstr(fv);
     };
+    // + - * are plain IEEE operations that the compiler may contract into fused multiply-adds
+    // (one rounding instead of two: within the fp32 tolerance of the reference's separately
+    // rounded float ops, and ~a quarter fewer instructions in gradient tapes)
     auto bin = [](int op, const std::string& a, const std::string& b) -> std::string {
-      if (!b.empty() && b[0] == '*') return "__fmul_rn(" + a + ", " + b.substr(1) + ")";
+      if (!b.empty() && b[0] == '*') return "(" + a + " * " + b.substr(1) + ")";
       // 1 / x is the correctly rounded reciprocal: identical to the IEEE division
       if (op == J4B_DIV && a == fstr(1.0f)) return "__frcp_rn(" + b + ")";
       switch (op) {
-        case J4B_ADD: return "__fadd_rn(" + a + ", " + b + ")";
-        case J4B_SUB: return "__fsub_rn(" + a + ", " + b + ")";
-        case J4B_MUL: return "__fmul_rn(" + a + ", " + b + ")";
+        case J4B_ADD: return "(" + a + " + " + b + ")";
+        case J4B_SUB: return "(" + a + " - " + b + ")";
+        case J4B_MUL: return "(" + a + " * " + b + ")";
         case J4B_DIV: return "__fdiv_rn(" + a + ", " + b + ")";
         case J4B_MAX: return "jmax(" + a + ", " + b + ")";
         case J4B_MIN: return "jmin(" + a + ", " + b + ")";
@@ -1473,7 +1513,7 @@ struct Gen {
     if (vec) {
       os << "  #pragma unroll\n  for (int e = 0; e < " << E(W) << "; ++e) {\n"
          << "    const long long c4 = (long long)e * " << NT << " + t;\n"
-         << "    if (c4 * 4 < " << istr(W) << ") reinterpret_cast<float4*>(" << p << " + r * " << istr(W)
+         << "    if (" << jlt(0, W, "c4 * 4") << ") reinterpret_cast<float4*>(" << p << " + r * " << istr(W)
          << ")[c4] = make_float4(" << vname(b) << "[e * 4], " << vname(b) << "[e * 4 + 1], " << vname(b)
          << "[e * 4 + 2], " << vname(b) << "[e * 4 + 3]);\n  }\n";
       return;
@@ -1481,7 +1521,7 @@ struct Gen {
     os << "  #pragma unroll\n  for (int e = 0; e < " << E(W) << "; ++e) {\n"
        << "    #pragma unroll\n    for (int q = 0; q < 4; ++q) {\n"
        << "      const long long j = ((long long)e * " << NT << " + t) * 4 + q;\n"
-       << "      if (j < " << istr(W) << ") " << p << "[r * " << istr(W) << " + j] = " << val << ";\n"
+       << "      if (" << jlt(0, W) << ") " << p << "[r * " << istr(W) << " + j] = " << val << ";\n"
        << "    }\n  }\n";
   }
 
@@ -1498,7 +1538,7 @@ struct Gen {
     os << "  if (blockIdx.x == 0) {\n  #pragma unroll\n  for (int e = 0; e < " << E(v.W) << "; ++e) {\n"
        << "    #pragma unroll\n    for (int q = 0; q < 4; ++q) {\n"
        << "      const long long j = ((long long)e * " << NT << " + t) * 4 + q;\n"
-       << "      if (j < " << istr(v.W) << ") " << p << "[j] = " << val << ";\n"
+       << "      if (" << jlt(0, v.W) << ") " << p << "[j] = " << val << ";\n"
        << "    }\n  }\n  }\n";
   }
 
@@ -1571,7 +1611,7 @@ struct Gen {
     if (full) {
       os << body.str();
     } else {
-      os << "      if (j < " << istr(W) << ") {\n" << body.str() << "      } else {\n";
+      os << "      if (" << jlt(0, W) << ") {\n" << body.str() << "      } else {\n";
       for (const GCall& m : batch)
         if (m.kind == G_EXPR) os << "        " << vname(t.calls[(size_t)m.call].out) << "[e * 4 + q] = 0.0f;\n";
       os << "      }\n";
@@ -1634,7 +1674,7 @@ struct Gen {
            << "    #pragma unroll\n    for (int q = 0; q < 4; ++q) {\n"
            << "      const long long j = ((long long)e * " << NT << " + t) * 4 + q;\n"
            << "      float res = 0.0f;\n"
-           << "      if (j < " << istr(v.W) << ") {\n" << body.str() << "      res = " << r << ";\n      }\n"
+           << "      if (" << jlt(0, v.W) << ") {\n" << body.str() << "      res = " << r << ";\n      }\n"
            << "      " << vname(b) << "[e * 4 + q] = res;\n    }\n  }\n";
       }
       if (v.need_store) (row ? store_row(os, b) : store_shared(os, b));
@@ -1654,7 +1694,7 @@ struct Gen {
       os << "  #pragma unroll\n  for (int e = 0; e < " << E(W) << "; ++e) {\n"
          << "    #pragma unroll\n    for (int q = 0; q < 4; ++q) {\n"
          << "      const long long j = ((long long)e * " << NT << " + t) * 4 + q;\n"
-         << "      if (j < " << istr(W) << ") ";
+         << "      if (" << jlt(0, W) << ") ";
       if (mx) os << "cm" << b << "[e * 4 + q] = jmax(cm" << b << "[e * 4 + q], " << val << ");\n";
       else os << "ca" << b << "[e * 4 + q] += " << val << ";\n";
       os << "    }\n  }\n";
@@ -1669,7 +1709,7 @@ struct Gen {
       os << "  #pragma unroll\n  for (int e = 0; e < " << E(W) << "; ++e) {\n"
          << "    #pragma unroll\n    for (int q = 0; q < 4; ++q) {\n"
          << "      const long long j = ((long long)e * " << NT << " + t) * 4 + q;\n"
-         << "      if (j < " << istr(W) << ") ";
+         << "      if (" << jlt(0, W) << ") ";
       if (mx) os << "rmax_combine(gm" << b << ", gi" << b << ", " << val << ", r * " << istr(W) << " + j);\n";
       else os << "ga" << b << " += (double)" << val << ";\n";
       os << "    }\n  }\n";
@@ -1698,11 +1738,11 @@ struct Gen {
       std::string loop = "  #pragma unroll\n  for (int e = 0; e < " + std::to_string(E(Win)) +
                          "; ++e) {\n    #pragma unroll\n    for (int q = 0; q < 4; ++q) {\n"
                          "      const long long j = ((long long)e * " + std::to_string(NT) +
-                         " + t) * 4 + q;\n      if (j < " + istr(Win) + ") ";
+                         " + t) * 4 + q;\n      if (" + jlt(0, Win) + ") ";
       if (c.op == T_SUMAX || c.op == T_RSUM) {
-        // per-thread partial in float, combined across threads in double
+        // per-thread partial in float, combined across threads in float (block_sumf)
         os << "  float " << vname(b) << ";\n  {\n  float acc = 0.0f;\n" << loop << "acc += " << val
-           << ";\n    }\n  }\n  " << vname(b) << " = (float)block_sum<" << NT << ">((double)acc, red, rp);\n  }\n";
+           << ";\n    }\n  }\n  " << vname(b) << " = block_sumf<" << NT << ">(acc, red, rp);\n  }\n";
       } else if (c.op == T_MAXAX) {
         os << "  float " << vname(b) << ";\n  {\n  float acc = -J4B_INF;\n" << loop << "acc = jmax(acc, " << val
            << ");\n    }\n  }\n  " << vname(b) << " = block_jmax<" << NT << ">(acc, red, rp);\n  }\n";
@@ -1726,7 +1766,7 @@ struct Gen {
          << "  #pragma unroll\n  for (int e = 0; e < " << E(Win) << "; ++e) {\n"
          << "    #pragma unroll\n    for (int q = 0; q < 4; ++q) {\n"
          << "      const long long j = ((long long)e * " << NT << " + t) * 4 + q;\n"
-         << "      if (j < " << istr(Win) << ") amax_combine(bv, bi, " << val << ", j);\n    }\n  }\n"
+         << "      if (" << jlt(0, Win) << ") amax_combine(bv, bi, " << val << ", j);\n    }\n  }\n"
          << "  am" << b << " = block_pair<" << NT << ", 0>(bv, bi, red, rp);\n"
          << "  if (am" << b << " == 0x7fffffffffffffffLL) am" << b << " = 0;\n  }\n"
          << "  const float up" << b << " = " << up << ";\n"
@@ -1747,7 +1787,7 @@ struct Gen {
        << "  #pragma unroll\n  for (int e = 0; e < " << E(Wo) << "; ++e) {\n"
        << "    #pragma unroll\n    for (int q = 0; q < 4; ++q) {\n"
        << "      const long long j = ((long long)e * " << NT << " + t) * 4 + q;\n"
-       << "      float res = 0.0f;\n      if (j < " << istr(Wo) << ") {\n";
+       << "      float res = 0.0f;\n      if (" << jlt(0, Wo) << ") {\n";
     if (c.op == T_MAXBWD) {
       // j indexes the input; find its group's first maximum
       os << "        const long long o = j / " << istr(nn * inner) << ", in_ = j % " << istr(inner)
@@ -1806,17 +1846,17 @@ struct Gen {
     if (gc.kind == G_VIEW) {
       // identity / scalar-broadcast view: nothing to compute
     } else if (gc.kind == G_COLRED) {
-      // 32 columns per CTA; warp w folds CTAs w, w+8, ...; the eight partials are combined
-      // in warp order, so the sum is deterministic
+      // 32 columns per CTA; warp w folds CTAs w, w + kFoldWarps, ...; the warp partials are
+      // combined in warp order, so the sum is deterministic
       int slot = part_slot[b];
       bool mx = c.op == T_MAXAX;
       os << "  float p" << b << ";\n  {\n    const double* pp = (const double*)A.p[" << slot << "];\n";
-      if (mx) os << "    float acc = -J4B_INF;\n    if (i < " << istr(v.W) << ") for (long long cta = warp; cta < A.G; cta += 8) acc = jmax(acc, (float)pp[cta * " << istr(v.W) << " + i]);\n"
+      if (mx) os << "    float acc = -J4B_INF;\n    if (i < " << istr(v.W) << ") for (long long cta = warp; cta < A.G; cta += kFoldWarps) acc = jmax(acc, (float)pp[cta * " << istr(v.W) << " + i]);\n"
                  << "    fred[warp * 32 + lane] = (double)acc;\n    __syncthreads();\n"
-                 << "    float tot = -J4B_INF;\n    for (int w = 0; w < 8; ++w) tot = jmax(tot, (float)fred[w * 32 + lane]);\n";
-      else os << "    double acc = 0.0;\n    if (i < " << istr(v.W) << ") for (long long cta = warp; cta < A.G; cta += 8) acc += pp[cta * " << istr(v.W) << " + i];\n"
+                 << "    float tot = -J4B_INF;\n    for (int w = 0; w < kFoldWarps; ++w) tot = jmax(tot, (float)fred[w * 32 + lane]);\n";
+      else os << "    double acc = 0.0;\n    if (i < " << istr(v.W) << ") for (long long cta = warp; cta < A.G; cta += kFoldWarps) acc += pp[cta * " << istr(v.W) << " + i];\n"
               << "    fred[warp * 32 + lane] = acc;\n    __syncthreads();\n"
-              << "    double tot = 0.0;\n    for (int w = 0; w < 8; ++w) tot += fred[w * 32 + lane];\n";
+              << "    double tot = 0.0;\n    for (int w = 0; w < kFoldWarps; ++w) tot += fred[w * 32 + lane];\n";
       os << "    __syncthreads();\n    p" << b << " = (float)tot;\n  }\n";
     } else if (gc.kind == G_GLOBRED) {
       // every warp folds all CTA partials (lane-strided, then a butterfly): same value in all
@@ -1880,7 +1920,7 @@ struct Gen {
     shared_loaded.assign(t.shape.size(), 0);
 
     // accumulators of cross-row reductions
-    std::ostringstream acc, colflush;
+    std::ostringstream acc, colflush, colstore;
     for (const GCall& gc : G.calls) {
       const TCall& c = t.calls[(size_t)gc.call];
       int b = c.out;
@@ -1890,14 +1930,16 @@ struct Gen {
         else acc << "  float ca" << b << "[" << E(W) * 4 << "];\n  #pragma unroll\n  for (int s = 0; s < " << E(W) * 4 << "; ++s) ca" << b << "[s] = 0.0f;\n";
         int slot = add_partial(b, W);
         if (c.op != T_MAXAX) {
-          // column sums: float per thread for up to 32 rows, then added into this CTA's double
-          // partial (each thread owns its columns of it)
+          // column sums: float per thread for up to 32 rows, then stored (first flush) or added
+          // (later flushes) into this CTA's double partial; each thread owns its columns of it,
+          // so the partial needs no zeroing pass
           std::string loop = "  #pragma unroll\n  for (int e = 0; e < " + std::to_string(E(W)) +
                              "; ++e) {\n    #pragma unroll\n    for (int q = 0; q < 4; ++q) {\n"
                              "      const long long j = ((long long)e * " + std::to_string(NT) + " + t) * 4 + q;\n"
-                             "      if (j < " + istr(W) + ") ";
+                             "      if (" + jlt(0, W) + ") ";
           std::string pp = "((double*)A.p[" + std::to_string(slot) + "])[(long long)blockIdx.x * " + istr(W) + " + j]";
-          acc << loop << pp << " = 0.0;\n    }\n  }\n";
+          colstore << loop << pp << " = (double)ca" << b << "[e * 4 + q];\n      ca" << b
+                   << "[e * 4 + q] = 0.0f;\n    }\n  }\n";
           colflush << loop << pp << " += (double)ca" << b << "[e * 4 + q];\n      ca" << b
                    << "[e * 4 + q] = 0.0f;\n    }\n  }\n";
         }
@@ -1956,7 +1998,7 @@ struct Gen {
             << "    #pragma unroll\n    for (int e = 0; e < " << E(W) << "; ++e) {\n"
             << "      #pragma unroll\n      for (int q = 0; q < 4; ++q) {\n"
             << "        const long long j = ((long long)e * " << NT << " + t) * 4 + q;\n"
-            << "        if (j < " << istr(W) << ") pp[j] = "
+            << "        if (" << jlt(0, W) << ") pp[j] = "
             << (c.op == T_MAXAX ? "(double)cm" : "ca") << b << "[e * 4 + q];\n      }\n    }\n  }\n";
       } else if (gc.kind == G_GLOBRED) {
         int slot = part_slot[b];
@@ -1995,7 +2037,11 @@ struct Gen {
         << "  const int t = threadIdx.x;\n"
         << "  const long long R = A.R;\n  (void)R;\n"
         << pro.str() << acc.str();
-    const std::string cf = colflush.str();
+    std::string cf;
+    if (!colflush.str().empty()) {
+      src << "  bool col_first = true;\n";
+      cf = "  if (col_first) {\n" + colstore.str() + "  } else {\n" + colflush.str() + "  }\n  col_first = false;\n";
+    }
     if (G.has_rows) {
       for (int b : row_loads) src << "  float N" << b << "[" << E(t.size[b] / G.R) * 4 << "];\n";
       if (!row_loads.empty()) src << "  if ((long long)blockIdx.x < R) {\n" << prefetch << "  }\n";
@@ -2008,8 +2054,9 @@ struct Gen {
     }
     src << cf << fin.str() << "}\n";
     if (has_fold) {
-      src << "extern \"C\" __global__ void __launch_bounds__(256) " << rn << "_fold(const Args A) {\n"
-          << "  __shared__ double fred[256];\n  (void)fred;\n"
+      src << "constexpr int kFoldWarps = " << kFoldThreads / 32 << ";\n"
+          << "extern \"C\" __global__ void __launch_bounds__(" << kFoldThreads << ") " << rn << "_fold(const Args A) {\n"
+          << "  __shared__ double fred[" << kFoldThreads << "];\n  (void)fred;\n"
           << "  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;\n  (void)warp;\n"
           << "  const long long i = (long long)blockIdx.x * 32 + lane;\n" << fold.str() << "}\n";
     }
@@ -2128,7 +2175,7 @@ extern "C" int j4b_tape_dryrun(const int64_t* words, size_t nwords, j4b_tape_sta
   std::string all;
   for (size_t g = 0; g < codes.size(); ++g) {
     std::vector<char> cubin;
-    st = compile_source(codes[g].src, "j4b_tape.cu", cubin);
+    st = compile_source(codes[g].src, "j4b_tape.cu", cubin, true);
     if (st) return st;
     all += "// ---- group " + std::to_string(g) + " ----\n" + codes[g].src;
   }
@@ -2179,7 +2226,7 @@ extern "C" int j4b_tape_compile(int dev, const int64_t* words, size_t nwords, j4
   for (size_t g = 0; g < tp->groups.size(); ++g) {
     j4b_tape::GroupRun& run = tp->runs[g];
     std::vector<char> cubin;
-    st = compile_source(codes[g].src, "j4b_tape.cu", cubin);
+    st = compile_source(codes[g].src, "j4b_tape.cu", cubin, true);
     if (st) return st;
     CUresult r = driver().ModuleLoadData(&run.mod, cubin.data());
     if (r != CUDA_SUCCESS) return cu_error(r, "cuModuleLoadData");
@@ -2425,7 +2472,7 @@ extern "C" int j4b_tape_launch(j4b_tape* tp, const j4b_buf* inputs, int nin, con
       if (r != CUDA_SUCCESS) return cu_error(r, "cuLaunchKernel(tape group)");
       count_launch();
       if (run.fold) {
-        r = driver().LaunchKernel(run.fold, (unsigned)run.fold_grid, 1, 1, 256, 1, 1, 0, (CUstream)stream, params, nullptr);
+        r = driver().LaunchKernel(run.fold, (unsigned)run.fold_grid, 1, 1, kFoldThreads, 1, 1, 0, (CUstream)stream, params, nullptr);
         if (r != CUDA_SUCCESS) return cu_error(r, "cuLaunchKernel(tape fold)");
         count_launch();
       }
