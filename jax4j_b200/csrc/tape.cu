@@ -1150,6 +1150,8 @@ struct Gen {
   std::vector<char> row_loaded;           // stored tensors hoisted as row tiles (per value id)
   std::vector<char> staged_now;
   int tmp = 0;
+  std::map<std::string, std::string> scalar_cse;  // per-row scalar subexpressions -> temporaries
+  const std::ostringstream* scalar_os = nullptr;   // the stream (scope) scalar_cse belongs to
 
   Gen(j4b_tape& tp, int g, std::vector<PtrRef>& p, std::vector<std::vector<int64_t>>& tb)
       : T(tp), t(tp.ir), V(tp.V), G(tp.groups[g]), gi(g), ptrs(p), tables(tb) {}
@@ -1660,9 +1662,16 @@ struct Gen {
         std::vector<std::string> in;
         for (int x : c.ins) in.push_back(slot_uniform(x, need));
         ensure_staged(os, need);
+        // per-row scalars share subexpressions across calls (a gradient recomputes its forward's
+        // scalars, e.g. the rsqrt of a mean square): temporaries live at the scope of the stream
+        // they are emitted into (kernel prologue or row body), so the table is reset per stream
+        if (&os != scalar_os) {
+          scalar_cse.clear();
+          scalar_os = &os;
+        }
         std::ostringstream body;
-        std::string r = expr_code(c, in, body, "  ");
-        os << "  float " << vname(b) << ";\n  {\n" << body.str() << "  " << vname(b) << " = " << r << ";\n  }\n";
+        std::string r = expr_code(c, in, body, "  ", &scalar_cse);
+        os << body.str() << "  float " << vname(b) << " = " << r << ";\n";
       } else {
         std::vector<std::string> in;
         for (int x : c.ins) in.push_back(slot(x, v.W, need));

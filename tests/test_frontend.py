@@ -153,6 +153,13 @@ def test_tape_plan_rms_swiglu_is_one_fused_kernel():
     # forward + backward of the vmapped body: one row program plus one cross-row fold
     assert stats["groups"] == 1 and stats["folds"] == 1 and stats["eager_steps"] == 0
     assert "block_sum<512>" in src and "__ldg(reinterpret_cast<const float4*>" in src
+    # the two row sums (mean square forward, its cotangent backward) reduce in float; the loss
+    # keeps the double block sum
+    assert src.count("block_sumf<512>(") == 2
+    # the backward reuses the forward's per-row rsqrt (one call besides the helper's definition)
+    assert src.count("jrsqrt(") == 2
+    # dg's per-CTA partial is stored on its first flush: no zeroing pass, no read-back
+    assert "col_first" in src and "+ j] = 0.0;" not in src
 
 
 def test_tape_plan_mlp_and_adam():
