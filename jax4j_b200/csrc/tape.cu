@@ -1919,8 +1919,9 @@ struct Gen {
       }
     }
     // about 16 elements of the widest row per thread. Measured on the RMSNorm + SwiGLU gradient
-    // (x [4096, 8192]): 16 per thread at 512 threads 76 us; 8 per thread at 1024 threads 87 us
-    // (64-register cap); two 512-thread CTAs per SM (64-register cap, spills) 116 us.
+    // (x [4096, 8192]): 16 per thread at 512 threads 62.3 us per step; 8 per thread at 1024
+    // threads 74.4 us (64-register cap); two 512-thread CTAs per SM (64-register cap, spills)
+    // 116 us.
     NT = 32;
     while (NT < 1024 && (int64_t)NT * 16 < wmax) NT *= 2;
     row_loaded.assign(t.shape.size(), 0);
