@@ -141,3 +141,26 @@ def test_one_call_fused_tape_layout_plans(oracle):
     _lib.call("j4b_tape_dryrun", w.ctypes.data_as(ctypes.POINTER(ctypes.c_int64)), w.size, ctypes.byref(st),
               None, 0, ctypes.byref(size))
     assert (st.calls, st.groups) == (1, 1)
+
+
+def test_backend_overrides_every_spi_method_with_its_signature():
+    """B200Backend declares every ComputeBackend and QuantizedOps method with the reference's
+    parameter and return types (tests/golden/spi_signatures.json, generated from the SPI sources
+    by tests/golden/make_spi_signatures.py). Only `program` and `custom` keep the SPI defaults:
+    those evaluate through the backend's own calls, which are all device-local here."""
+    import json
+    spi = json.loads((ROOT / "tests" / "golden" / "spi_signatures.json").read_text())
+    src = (MODULE / "src" / "main" / "java" / "com" / "nablatensor" / "jax4j" / "backend" / "b200" /
+           "B200Backend.java").read_text()
+    declared = {}
+    for ret, name, params in re.findall(r"public\s+([\w.<>\[\], ]+?)\s+(\w+)\(([^)]*)\)", src):
+        types = [" ".join(p.split()).rsplit(" ", 1)[0] for p in params.split(",") if p.strip()]
+        declared.setdefault(name, []).append((ret.strip(), types))
+    assert len(spi["ComputeBackend"]) == 37 and len(spi["QuantizedOps"]) == 5
+    for iface, methods in spi.items():
+        for m in methods:
+            if m["name"] in ("program", "custom"):
+                continue
+            assert m["name"] in declared, f"{iface}.{m['name']} is not implemented"
+            assert (m["returns"], m["params"]) in declared[m["name"]], \
+                f"{iface}.{m['name']}: {declared[m['name']]} vs ({m['returns']}, {m['params']})"
