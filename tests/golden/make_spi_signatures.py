@@ -4,9 +4,11 @@ Java binding module implements.
 
   ComputeBackend  <- jax4j-core/src/main/java/com/nablatensor/jax4j/tensor/spi/ComputeBackend.java
   QuantizedOps    <- jax4j-core/src/main/java/com/nablatensor/jax4j/tensor/spi/QuantizedOps.java
+  AadEngine       <- jax4j-core/src/main/java/com/nablatensor/jax4j/engine/AadEngine.java
+  AadExecutable   <- jax4j-core/src/main/java/com/nablatensor/jax4j/engine/AadExecutable.java
 
 Each entry is {name, returns, params (simple type names), default (has a default body)};
-private helpers are skipped.
+private and static helpers are skipped.
 
 Usage: python tests/golden/make_spi_signatures.py /path/to/jax4j
 """
@@ -16,7 +18,10 @@ import re
 import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-SPI = "jax4j-core/src/main/java/com/nablatensor/jax4j/tensor/spi"
+SOURCES = {"ComputeBackend": "jax4j-core/src/main/java/com/nablatensor/jax4j/tensor/spi",
+           "QuantizedOps": "jax4j-core/src/main/java/com/nablatensor/jax4j/tensor/spi",
+           "AadEngine": "jax4j-core/src/main/java/com/nablatensor/jax4j/engine",
+           "AadExecutable": "jax4j-core/src/main/java/com/nablatensor/jax4j/engine"}
 DECL = re.compile(r"^\s*(default\s+)?([A-Za-z_][\w.<>\[\], ]*?)\s+(\w+)\(([^)]*)\)\s*(;|\{)", re.M)
 
 
@@ -32,7 +37,7 @@ def parse(path: str) -> list:
     out = []
     for m in DECL.finditer(text):
         ret, name = m.group(2).strip(), m.group(3)
-        if ret.startswith(("private", "return", "new", "throw", "else")) or name in ("if", "for", "while", "switch"):
+        if ret.startswith(("private", "static", "return", "new", "throw", "else")) or name in ("if", "for", "while", "switch"):
             continue
         params = [simple(p.rsplit(" ", 1)[0]) for p in (x.strip() for x in m.group(4).split(",")) if p]
         out.append({"name": name, "returns": simple(ret), "params": params, "default": bool(m.group(1))})
@@ -40,8 +45,7 @@ def parse(path: str) -> list:
 
 
 def main(ref_root: str) -> None:
-    fixture = {iface: parse(os.path.join(ref_root, SPI, iface + ".java"))
-               for iface in ("ComputeBackend", "QuantizedOps")}
+    fixture = {iface: parse(os.path.join(ref_root, d, iface + ".java")) for iface, d in SOURCES.items()}
     with open(os.path.join(HERE, "spi_signatures.json"), "w") as f:
         json.dump(fixture, f, indent=1)
 

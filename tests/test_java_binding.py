@@ -157,10 +157,34 @@ def test_backend_overrides_every_spi_method_with_its_signature():
         types = [" ".join(p.split()).rsplit(" ", 1)[0] for p in params.split(",") if p.strip()]
         declared.setdefault(name, []).append((ret.strip(), types))
     assert len(spi["ComputeBackend"]) == 37 and len(spi["QuantizedOps"]) == 5
-    for iface, methods in spi.items():
-        for m in methods:
+    for iface in ("ComputeBackend", "QuantizedOps"):
+        for m in spi[iface]:
             if m["name"] in ("program", "custom"):
                 continue
             assert m["name"] in declared, f"{iface}.{m['name']} is not implemented"
             assert (m["returns"], m["params"]) in declared[m["name"]], \
                 f"{iface}.{m['name']}: {declared[m['name']]} vs ({m['returns']}, {m['params']})"
+
+
+def test_aad_providers_implement_the_engine_interfaces():
+    """The AadEngine methods are declared by the providers' shared base, and B200AadExecutable
+    declares the AadExecutable methods AbstractAadExecutable leaves open (engineName, replay)
+    plus its close and compileSeconds, all with the reference's types."""
+    import json
+    spi = json.loads((ROOT / "tests" / "golden" / "spi_signatures.json").read_text())
+    pkg = MODULE / "src" / "main" / "java" / "com" / "nablatensor" / "jax4j" / "backend" / "b200"
+
+    def declared(path):
+        out = {}
+        for ret, name, params in re.findall(r"public\s+(?:synchronized\s+)?([\w.<>\[\], ]+?)\s+(\w+)\(([^)]*)\)",
+                                            path.read_text()):
+            types = [" ".join(p.split()).rsplit(" ", 1)[0] for p in params.split(",") if p.strip()]
+            out.setdefault(name, []).append((ret.strip(), types))
+        return out
+
+    engines, exe = declared(pkg / "B200AadEngines.java"), declared(pkg / "B200AadExecutable.java")
+    for m in spi["AadEngine"]:
+        assert (m["returns"], m["params"]) in engines.get(m["name"], []), f"AadEngine.{m['name']}"
+    want = {m["name"]: m for m in spi["AadExecutable"]}
+    for name in ("engineName", "replay", "close", "compileSeconds"):
+        assert (want[name]["returns"], want[name]["params"]) in exe.get(name, []), f"AadExecutable.{name}"
