@@ -188,3 +188,36 @@ def test_aad_providers_implement_the_engine_interfaces():
     want = {m["name"]: m for m in spi["AadExecutable"]}
     for name in ("engineName", "replay", "close", "compileSeconds"):
         assert (want[name]["returns"], want[name]["params"]) in exe.get(name, []), f"AadExecutable.{name}"
+
+
+# JDK and JUnit members the module calls (java.lang.foreign, java.lang.invoke, java.util,
+# java.util.stream, java.lang.ref, Math/Long/Double/Integer/System, enum values/ordinal/name,
+# JUnit's DynamicTest)
+JDK_NAMES = {
+    "of", "add", "get", "ofConfined", "allocate", "allocateFrom", "size", "equals", "toArray", "stream",
+    "toString", "flatMap", "map", "byteSize", "append", "addAll", "values", "register", "nanoTime",
+    "multiplyExact", "libraryLookup", "global", "getString", "dynamicTest", "create", "contains",
+    "computeIfAbsent", "compareAndSet", "clean", "asLongStream", "trim", "sqrt", "sin", "cos", "exp",
+    "remove", "parseLong", "orElseThrow", "ofArray", "noneOf", "newKeySet", "nativeLinker", "mapToLong",
+    "isNative", "isEmpty", "invokeWithArguments", "invokeExact", "getProperty", "getInteger", "getAtIndex",
+    "find", "downcallHandle", "doubleToRawLongBits", "copyOfRange", "copy", "clone", "asSlice", "arraycopy",
+    "max", "ordinal", "name", "longValue", "valueOf",
+}
+
+
+def test_every_called_member_exists_in_the_reference_or_the_jdk():
+    """Each `.name(` call in the module names a member of an imported reference class (from the
+    reference sources, tests/golden/spi_signatures.json), of the module itself, or of the JDK /
+    JUnit APIs listed above: a mistyped reference accessor fails here rather than at a
+    maintainer's first compile."""
+    import json
+    ref = json.loads((ROOT / "tests" / "golden" / "spi_signatures.json").read_text())["reference_names"]
+    known = set().union(*ref.values()) | JDK_NAMES
+    sources = sorted((MODULE / "src").rglob("*.java"))
+    own = set()
+    for src in sources:
+        own |= set(re.findall(r"\b(\w+)\s*\([^;{]*\)\s*(?:throws [\w, ]+)?\{", src.read_text()))
+    for src in sources:
+        text = re.sub(r'"(?:\\.|[^"\\])*"', '""', re.sub(r"//[^\n]*|/\*.*?\*/", "", src.read_text(), flags=re.S))
+        for name in set(re.findall(r"\.(\w+)\(", text)):
+            assert name in known or name in own, f"{src.name}: .{name}( is not a known member"
