@@ -194,3 +194,35 @@ def test_tape_validation_rejects_malformed_tapes():
     bad_shape.shapes[bad_shape.inputs[1]] = (5, 4)
     with pytest.raises(ValueError, match="incompatible matmul shapes"):
         L.tape_dryrun(bad_shape.serialize())
+
+
+@pytest.mark.parametrize("cols", [8, 12, 40, 70, 256, 1000, 8192])
+def test_static_bounds_terms_never_skip_a_needed_check(cols):
+    """Every bounds test the row compiler emits has the form ((e + 1) * 4NT + off <= lim ||
+    var + off < lim); its compile-time left term may replace the runtime test only if every
+    slot of step e is in range. Checked by evaluation over all threads t < NT and q < 4 of the
+    RMSNorm + SwiGLU gradient tape (row loads, shifted views, reductions, stores) at ragged and
+    full widths."""
+    import re as _re
+    L = _lib()
+    tape = J.trace(nn.rms_swiglu_value_and_grad, [(3, cols), (cols,)])
+    _, src = L.tape_dryrun(tape.serialize())
+    term = _re.compile(r"\(\(e \+ 1\) \* (\d+)LL(?: \+ (-?\d+)LL)? <= (-?\d+)LL \|\| (j|c4 \* 4)(?: \+ (-?\d+)LL)? < (-?\d+)LL\)")
+    found = checked = 0
+    for kernel in src.split('extern "C"')[1:]:
+        nts = set(_re.findall(r"\(\(long long\)e \* (\d+) \+ t\)", kernel)) | set(_re.findall(r"\(long long\)e \* (\d+) \+ t;", kernel))
+        assert len(nts) <= 1
+        for span, off1, lim1, var, off2, lim2 in term.findall(kernel):
+            found += 1
+            nt = int(next(iter(nts)))
+            span, lim = int(span), int(lim1)
+            off = int(off1 or 0)
+            assert span == 4 * nt and lim == int(lim2) and off == int(off2 or 0)
+            for e in range(lim // span + 2):
+                if (e + 1) * span + off > lim:
+                    continue
+                worst = 4 * (e * nt + nt - 1) + (3 if var == "j" else 0)
+                assert worst + off < lim, (cols, span, off, lim, e)
+                checked += 1
+    # every test was recognised; at widths of whole slot steps the static term decides some
+    assert found > 0 and (checked > 0 or cols % 128)
