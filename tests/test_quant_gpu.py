@@ -165,7 +165,10 @@ def test_quant_gemm_config5_shape(backend, oracle):
     w = backend.upload_quantized(blob, Q4_0, (rows, cols))
     x = torch.randn(m, cols, device="cuda", generator=g)
     y = backend.quant_gemm(w, backend.wrap(x), 1).tensor.reshape(m, rows)
-    deq = torch.stack([backend.quant_gather_row(w, r).tensor for r in range(0, rows, 512)])
+    # expected weights from the C oracle's decode of the encoded blocks (not the engine's own gather)
+    host_blob = blob.cpu().numpy()
+    deq = torch.from_numpy(np.stack([oracle.gather_row(Q4_0, host_blob, rows, cols, r)
+                                     for r in range(0, rows, 512)])).to(x.device)
     want = x.double() @ deq.double().T
     got = y[:, ::512].double()
     err = (got - want).abs().max() / want.abs().max()
