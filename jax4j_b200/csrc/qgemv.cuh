@@ -964,10 +964,15 @@ cudaError_t launch_gemv(const j4b_qweight* w, const float* x, const float* add, 
   return cudaLaunchKernelEx(&cfg, qgemv_kernel<QT, NT, PK>, a);
 }
 
+#include "qgemv_stream.cuh"
+
 template <int QT>
 cudaError_t gemv_dispatch(const j4b_qweight* w, const float* x, const float* add, float* y,
                           int batch, int sms, cudaStream_t stream, const GemvPeers* peers = nullptr,
                           unsigned* grid_out = nullptr) {
+  static const bool legacy = getenv("J4B_QGEMV_LEGACY") != nullptr;  // development A/B only
+  if (!legacy && batch <= 4) return launch_gemv_stream<QT, true>(w, x, add, y, batch, sms, stream, peers, grid_out);
+  if (!legacy && batch <= 8) return launch_gemv_stream<QT, false>(w, x, add, y, batch, sms, stream, peers, grid_out);
   if (batch <= 4) return launch_gemv<QT, 1, true>(w, x, add, y, batch, sms, stream, peers, grid_out);
   if (batch <= 8) return launch_gemv<QT, 1, false>(w, x, add, y, batch, sms, stream, peers, grid_out);
   return launch_gemv<QT, 2, false>(w, x, add, y, batch, sms, stream, peers, grid_out);

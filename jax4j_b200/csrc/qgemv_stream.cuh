@@ -1,0 +1,419 @@
+// Streaming dequant-GEMV for batch <= 8 (included by qgemv.cuh, inside namespace
+// j4b::<anonymous>; it reuses that file's fragment decoders tile_compute / tile_compute_pk and
+// its bulk-copy and mbarrier helpers).
+//
+// Shape of one launch: one CTA per SM, sized to at most half of an SM (<= 112 KB of shared
+// memory, 288 threads, <= 112 registers per thread), so that under programmatic dependent launch
+// the next GEMV's CTAs are resident and already streaming their weights while this launch's CTAs
+// finish their last tiles and their split-K folds. A CTA owns one 1024-column K range ("split")
+// of a contiguous run of 16-row tiles:
+//   - warp 8 is the producer: one elected lane streams the run's tile chunks (contiguous in the
+//     split-major layout) into a ring of shared-memory stages with 1-D bulk copies, each stage
+//     completing on its `full` mbarrier; it refills a stage once the warps that read it have
+//     arrived on its `empty` mbarrier. The first ring's worth is issued before the dependency
+//     wait (weights are immutable once uploaded).
+//   - warps 0..7 first turn x's 1024-column slice into fp16 hi/lo mma fragments in shared memory
+//     (warp w converts 128-column chunk w), then each warp takes whole tiles round-robin and
+//     walks the tile's 8 chunks itself, so a tile's partial sum over the split never leaves the
+//     warp's registers: no block barrier and no cross-warp reduction in the main loop.
+//   - split-K: a warp stores its tile's partial into the weight's scratch, and the warp whose
+//     arrival completes the tile's counter adds the splits in split order (deterministic) and
+//     writes y (+ add); with one split the warp writes y directly.
+// Every mbarrier wait is bounded (j4b_wait.cuh); on a timeout the CTA records an error in the
+// weight's status word, lets every copy still in flight land, and returns.
+
+constexpr int kStreamWarps = 8;                         // compute warps
+constexpr int kStreamThreads = (kStreamWarps + 1) * 32;  // + the producer warp
+constexpr int kStreamSmem = 112 * 1024;                  // two CTAs per SM
+
+template <int QT>
+constexpr bool stream_needs_xblk() {
+  return QT != J4B_Q8_0 && QT != J4B_Q6_K;
+}
+// Tile chunks per ring stage: copies of ~9-18 KB.
+template <int QT>
+constexpr int stream_tiles_per_stage() {
+  return GemvTraits<QT>::kChunk <= 5000 ? 4 : (GemvTraits<QT>::kChunk <= 10000 ? 2 : 1);
+}
+// Shared-memory bytes of one 128-column chunk's x fragments: packed (batch <= 4) 4 x 16 bytes
+// per lane of B fragments (+ 16 bytes of x block sums), unpacked 8 x 16 bytes (hi, lo of each
+// k-step) (+ 32 bytes of block sums).
+template <int QT, bool PK>
+constexpr int stream_frag_chunk() {
+  return PK ? 2048 + (stream_needs_xblk<QT>() ? 512 : 0) : 4096 + (stream_needs_xblk<QT>() ? 1024 : 0);
+}
+template <int QT, bool PK>
+constexpr int stream_stages() {
+  constexpr int stage = stream_tiles_per_stage<QT>() * GemvTraits<QT>::kChunk;
+  constexpr int r = (kStreamSmem - 8 * stream_frag_chunk<QT, PK>() - 256) / stage;
+  return r > 8 ? 8 : r;
+}
+template <int QT, bool PK>
+constexpr int stream_smem_bytes() {
+  return stream_stages<QT, PK>() * stream_tiles_per_stage<QT>() * GemvTraits<QT>::kChunk +
+         8 * stream_frag_chunk<QT, PK>() + 2 * 8 * stream_stages<QT, PK>();
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+// Barrier 1 over the eight compute warps only (the producer warp never takes it).
+__device__ __forceinline__ void compute_warps_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kStreamWarps * 32) : "memory");
+}
+
+// Warp `c` converts x's columns [kc0 + 128c, kc0 + 128c + 128) of every batch row into the
+// chunk's fragment block (columns past K and rows past the batch are zeros).
+template <int QT, bool PK>
+__device__ __forceinline__ void stream_prep_x(const GemvArgs& a, int64_t kc0, int c, int lane, uint8_t* frag) {
+  const int g = lane >> 2, t = lane & 3;
+  constexpr int kXB = kXBlocks<QT>;
+  uint8_t* dst = frag + c * stream_frag_chunk<QT, PK>();
+  const int xrow = PK ? (g >> 1) : g;
+  const bool row_ok = xrow < a.batch;
+  const float* xr = a.x + (int64_t)xrow * a.cols;
+  const int64_t kb = kc0 + c * 128 + 2 * t;
+  float2 p0[8], p1[8];
+#pragma unroll
+  for (int j = 0; j < 8; j++) {  // all loads first (cols is a multiple of 32, so k < cols covers k + 9)
+    const int64_t k = kb + 16 * j;
+    const bool ok = row_ok && k < a.cols;
+    p0[j] = ok ? __ldg(reinterpret_cast<const float2*>(xr + k)) : make_float2(0.f, 0.f);
+    p1[j] = ok ? __ldg(reinterpret_cast<const float2*>(xr + k + 8)) : make_float2(0.f, 0.f);
+  }
+  uint32_t hi[8][2], lo[8][2];
+  float xs_hi[8], xs_lo[8];
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    __half2 h0 = __floats2half2_rn(p0[j].x, p0[j].y);
+    __half2 h1 = __floats2half2_rn(p1[j].x, p1[j].y);
+    const float2 f0 = __half22float2(h0), f1 = __half22float2(h1);
+    __half2 l0 = __floats2half2_rn(p0[j].x - f0.x, p0[j].y - f0.y);
+    __half2 l1 = __floats2half2_rn(p1[j].x - f1.x, p1[j].y - f1.y);
+    const float2 g0 = __half22float2(l0), g1 = __half22float2(l1);
+    hi[j][0] = *reinterpret_cast<uint32_t*>(&h0);
+    hi[j][1] = *reinterpret_cast<uint32_t*>(&h1);
+    lo[j][0] = *reinterpret_cast<uint32_t*>(&l0);
+    lo[j][1] = *reinterpret_cast<uint32_t*>(&l1);
+    xs_hi[j] = (f0.x + f0.y) + (f1.x + f1.y);
+    xs_lo[j] = (g0.x + g0.y) + (g1.x + g1.y);
+  }
+  if constexpr (PK) {
+    // lane group g carries batch g / 2: its hi part for even g, its lo part for odd g
+    const bool odd = g & 1;
+#pragma unroll
+    for (int jj = 0; jj < 4; jj++) {
+      const uint4 v = odd ? make_uint4(lo[2 * jj][0], lo[2 * jj][1], lo[2 * jj + 1][0], lo[2 * jj + 1][1])
+                          : make_uint4(hi[2 * jj][0], hi[2 * jj][1], hi[2 * jj + 1][0], hi[2 * jj + 1][1]);
+      *reinterpret_cast<uint4*>(dst + (jj * 32 + lane) * 16) = v;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; j++)
+      *reinterpret_cast<uint4*>(dst + (j * 32 + lane) * 16) = make_uint4(hi[j][0], hi[j][1], lo[j][0], lo[j][1]);
+  }
+  if constexpr (stream_needs_xblk<QT>()) {
+    // block sums of the represented x (hi + lo) for the output columns this lane holds
+    float sums[kXB][2];
+#pragma unroll
+    for (int q = 0; q < kXB; q++) {
+      constexpr int kSteps = 8 / kXB;
+      float s = 0.f;
+#pragma unroll
+      for (int j = 0; j < kSteps; j++) {
+        const int jj = q * kSteps + j;
+        s += PK ? ((g & 1) ? xs_lo[jj] : xs_hi[jj]) : xs_hi[jj] + xs_lo[jj];
+      }
+      s += __shfl_xor_sync(0xffffffffu, s, 1);
+      s += __shfl_xor_sync(0xffffffffu, s, 2);
+      sums[q][0] = __shfl_sync(0xffffffffu, s, 4 * (2 * t));
+      sums[q][1] = __shfl_sync(0xffffffffu, s, 4 * (2 * t + 1));
+    }
+    if constexpr (PK) {
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      float* vp = reinterpret_cast<float*>(&v);
+#pragma unroll
+      for (int q = 0; q < kXB; q++) vp[q] = sums[q][0] + sums[q][1];  // batch t: hi + lo sums
+      *reinterpret_cast<float4*>(dst + 2048 + lane * 16) = v;
+    } else {
+      float4 v[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
+      float* vp = reinterpret_cast<float*>(v);
+#pragma unroll
+      for (int q = 0; q < kXB; q++) {
+        vp[2 * q] = sums[q][0];      // batch 2t
+        vp[2 * q + 1] = sums[q][1];  // batch 2t + 1
+      }
+      *reinterpret_cast<float4*>(dst + 4096 + lane * 16) = v[0];
+      *reinterpret_cast<float4*>(dst + 4096 + 512 + lane * 16) = v[1];
+    }
+  }
+}
+
+// Output element cc of lane (g, t)'s accumulator -> (row in tile, batch column).
+template <bool PK>
+__device__ __forceinline__ void stream_coord(int lane, int cc, int& row, int& bcol) {
+  const int g = lane >> 2, t = lane & 3;
+  if (PK) {
+    row = g + 8 * cc;
+    bcol = t;
+  } else {
+    row = g + 8 * (cc >> 1);
+    bcol = 2 * t + (cc & 1);
+  }
+}
+
+template <int QT, bool PK>
+__global__ void __launch_bounds__(kStreamThreads, 2) qgemv_stream_kernel(GemvArgs a) {
+  using T = GemvTraits<QT>;
+  constexpr int R = stream_stages<QT, PK>();
+  constexpr int kU = stream_tiles_per_stage<QT>();
+  constexpr int kStage = kU * T::kChunk;
+  constexpr int kFrag = stream_frag_chunk<QT, PK>();
+  constexpr int kNV = PK ? 2 : 4;  // accumulator floats per lane per tile
+  constexpr int kXB = kXBlocks<QT>;
+  static_assert(R >= 2, "ring too small");
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t* ring = smem;
+  uint8_t* frag = smem + R * kStage;
+  uint64_t* full = reinterpret_cast<uint64_t*>(frag + 8 * kFrag);
+  uint64_t* empty = full + R;
+
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int split = blockIdx.x % a.ksplit;
+  const int ngroups = gridDim.x / a.ksplit;
+  const int group = blockIdx.x / a.ksplit;
+  const int64_t tile0 = (int64_t)group * a.rt / ngroups;
+  const int ntiles = (int)((int64_t)(group + 1) * a.rt / ngroups - tile0);
+  const int nstages = (ntiles + kU - 1) / kU;
+  const int64_t kc0 = (int64_t)split * 1024;
+  const uint32_t chunk_bytes = (uint32_t)a.L.chunk_bytes(split);
+  const uint32_t meta_off = (uint32_t)(a.L.groups_in_split(split) * T::kQ);
+  const int nchunks = (int)(a.kpad - kc0 >= 1024 ? 8 : (a.kpad - kc0) / 128);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < R; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kU);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  bool failed = false;
+  int issued = 0;  // stages issued (producer lane 0 only)
+  if (warp == kStreamWarps) {
+    // ---------------- producer ----------------
+    auto issue = [&](int st) {
+      const int first = st * kU, count = min(kU, ntiles - first);
+      const uint32_t bytes = (uint32_t)count * chunk_bytes;
+      uint64_t* bar = &full[st % R];
+      mbar_expect_tx(bar, bytes);
+      tma_load_1d(ring + (st % R) * kStage, a.data + a.L.chunk_offset(split, tile0 + first), bytes, bar);
+    };
+    if (lane == 0)
+      for (; issued < R && issued < nstages; issued++) issue(issued);
+    pdl_launch_dependents();
+    pdl_wait();
+    if (lane == 0) {
+      for (; issued < nstages; issued++) {
+        const int slot = issued % R;
+        if (!mbar_wait_bounded(&empty[slot], (uint32_t)(((issued / R) - 1) & 1))) {
+          failed = true;
+          break;
+        }
+        fence_proxy_async();  // the readers' generic-proxy reads of the slot precede the refill
+        issue(issued);
+      }
+    }
+  } else {
+    // ---------------- compute warps ----------------
+    pdl_launch_dependents();
+    pdl_wait();
+    int64_t par_off = 0;  // parity half of the gathered buffer (peer all-gather only)
+    if (a.nranks > 1) par_off = (int64_t)(*a.step & 1u) * a.half_floats;
+    if (warp < nchunks) stream_prep_x<QT, PK>(a, kc0, warp, lane, frag);
+    compute_warps_sync();
+
+    for (int u = warp; u < ntiles; u += kStreamWarps) {
+      const int st = u / kU, slot = st % R;
+      if (!failed && !mbar_wait_bounded(&full[slot], (uint32_t)((st / R) & 1))) failed = true;
+      float acc[kNV];
+#pragma unroll
+      for (int i = 0; i < kNV; i++) acc[i] = 0.f;
+      if (!failed) {
+        const uint8_t* base = ring + slot * kStage + (u % kU) * chunk_bytes;
+#pragma unroll 1
+        for (int c = 0; c < nchunks; c++) {
+          const uint8_t* fc = frag + c * kFrag;
+          if constexpr (PK) {
+            uint32_t bp[8][2];
+#pragma unroll
+            for (int jj = 0; jj < 4; jj++) {
+              const uint4 v = *reinterpret_cast<const uint4*>(fc + (jj * 32 + lane) * 16);
+              bp[2 * jj][0] = v.x;
+              bp[2 * jj][1] = v.y;
+              bp[2 * jj + 1][0] = v.z;
+              bp[2 * jj + 1][1] = v.w;
+            }
+            float xb[kXB];
+            if constexpr (stream_needs_xblk<QT>()) {
+              const float4 v = *reinterpret_cast<const float4*>(fc + 2048 + lane * 16);
+              const float vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+              for (int q = 0; q < kXB; q++) xb[q] = vv[q];
+            } else {
+#pragma unroll
+              for (int q = 0; q < kXB; q++) xb[q] = 0.f;
+            }
+            float r2[2] = {acc[0], acc[1]};
+            tile_compute_pk<QT>(base, base + meta_off, c, lane, bp, xb, r2);
+            acc[0] = r2[0];
+            acc[1] = r2[1];
+          } else {
+            uint32_t bh[1][8][2], bl[1][8][2];
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+              const uint4 v = *reinterpret_cast<const uint4*>(fc + (j * 32 + lane) * 16);
+              bh[0][j][0] = v.x;
+              bh[0][j][1] = v.y;
+              bl[0][j][0] = v.z;
+              bl[0][j][1] = v.w;
+            }
+            float xb[1][kXB][2];
+            if constexpr (stream_needs_xblk<QT>()) {
+              const float4 v0 = *reinterpret_cast<const float4*>(fc + 4096 + lane * 16);
+              const float4 v1 = *reinterpret_cast<const float4*>(fc + 4096 + 512 + lane * 16);
+              const float vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+#pragma unroll
+              for (int q = 0; q < kXB; q++) {
+                xb[0][q][0] = vv[2 * q];
+                xb[0][q][1] = vv[2 * q + 1];
+              }
+            } else {
+#pragma unroll
+              for (int q = 0; q < kXB; q++) xb[0][q][0] = xb[0][q][1] = 0.f;
+            }
+            float r4[1][4] = {{acc[0], acc[1], acc[2], acc[3]}};
+            tile_compute<QT, 1>(base, base + meta_off, c, lane, bh, bl, xb, r4);
+#pragma unroll
+            for (int i = 0; i < 4; i++) acc[i] = r4[0][i];
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);  // this warp is done reading the stage
+      if (failed) continue;
+
+      const int64_t tile = tile0 + u;
+      if (a.ksplit > 1) {
+        float* part = a.partials + ((int64_t)split * a.rt + tile) * 256;
+#pragma unroll
+        for (int i = 0; i < kNV; i++) __stcg(part + i * 32 + lane, acc[i]);
+        __threadfence();
+        __syncwarp();
+        unsigned last = 0;
+        if (lane == 0) last = atomicAdd(a.arrivals + tile, 1u) == (unsigned)(a.ksplit - 1);
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (!last) continue;
+        __threadfence();
+        // the last arrival adds the splits in split order, four splits' loads in flight at once
+        const float* p0 = a.partials + tile * 256 + lane;
+        const int64_t sstride = a.rt * 256;
+#pragma unroll
+        for (int i = 0; i < kNV; i++) acc[i] = 0.f;
+        for (int sp0 = 0; sp0 < a.ksplit; sp0 += 4) {
+          float v[4][kNV];
+#pragma unroll
+          for (int s = 0; s < 4; s++)
+#pragma unroll
+            for (int i = 0; i < kNV; i++)
+              v[s][i] = sp0 + s < a.ksplit ? __ldcg(p0 + (sp0 + s) * sstride + i * 32) : 0.f;
+#pragma unroll
+          for (int s = 0; s < 4; s++)
+#pragma unroll
+            for (int i = 0; i < kNV; i++)
+              if (sp0 + s < a.ksplit) acc[i] += v[s][i];
+        }
+        if (lane == 0) a.arrivals[tile] = 0u;  // ready for the next launch
+      }
+#pragma unroll
+      for (int i = 0; i < kNV; i++) {
+        int row, bcol;
+        stream_coord<PK>(lane, i, row, bcol);
+        const int64_t r = tile * 16 + row;
+        if (r < a.rows && bcol < a.batch) {
+          float v = acc[i];
+          if (a.add) v += a.add[(int64_t)bcol * a.rows + r];
+          store_y(a, par_off, bcol, r, v);
+        }
+      }
+    }
+  }
+
+  if (__syncthreads_or(failed)) {
+    // Let every copy still in flight land before the CTA's shared memory is released.
+    if (warp == kStreamWarps && lane == 0) {
+      atomicExch(a.status, 1);
+      for (int s = 0; s < R && s < issued; s++) {
+        const int last = s + ((issued - 1 - s) / R) * R;  // the last stage issued into slot s
+        mbar_wait_bounded(&full[s], (uint32_t)((last / R) & 1));
+      }
+    }
+    __syncthreads();
+  }
+  signal_peers(a);
+}
+
+template <int QT, bool PK>
+cudaError_t launch_gemv_stream(const j4b_qweight* w, const float* x, const float* add, float* y, int batch,
+                               int sms, cudaStream_t stream, const GemvPeers* peers, unsigned* grid_out) {
+  constexpr int smem = stream_smem_bytes<QT, PK>();
+  static bool attr_set[kMaxDevices] = {};  // function attributes are per device context
+  if (w->dev < 0 || w->dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  if (!attr_set[w->dev]) {
+    cudaError_t e = cudaFuncSetAttribute(qgemv_stream_kernel<QT, PK>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    attr_set[w->dev] = true;
+  }
+  GemvArgs a;
+  memset(&a, 0, sizeof(a));
+  a.data = w->data;
+  a.L = layout_of(w);
+  a.rows = w->rows;
+  a.cols = w->cols;
+  a.kpad = w->kpad;
+  a.rt = w->rt;
+  a.x = x;
+  a.add = add;
+  a.y = y;
+  a.batch = batch;
+  a.ksplit = w->ksplit;
+  a.partials = w->partials;
+  a.arrivals = w->arrivals;
+  a.status = w->status;
+  a.nranks = 1;
+  if (peers) {
+    a.nranks = peers->nranks;
+    a.rank = peers->rank;
+    a.step = peers->step;
+    a.half_floats = peers->half_floats;
+    for (int p = 0; p < peers->nranks; ++p) {
+      a.peer_y[p] = peers->y[p];
+      a.peer_ctr[p] = peers->ctr[p];
+    }
+  }
+  // one CTA per SM: as many tile groups as fit next to the K splits
+  const int64_t groups = std::max<int64_t>(1, std::min<int64_t>(w->rt, (int64_t)sms / w->ksplit));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(groups * w->ksplit));
+  cfg.blockDim = dim3(kStreamThreads);
+  cfg.dynamicSmemBytes = (size_t)smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (grid_out) *grid_out = cfg.gridDim.x;
+  return cudaLaunchKernelEx(&cfg, qgemv_stream_kernel<QT, PK>, a);
+}
