@@ -146,9 +146,10 @@ int j4b_reindex(j4b_buf a, int64_t n_src, j4b_buf map, int64_t n_dst, j4b_buf ou
 int j4b_scatter_add(j4b_buf a, int64_t n_src, j4b_buf map, int64_t n_dst, j4b_buf out,
                     j4b_stream s);
 /* Full sum that allocates nothing (no counterpart in the reference). For callers that cannot
- * allocate device memory while they run -- code inside CUDA stream capture in global capture
- * mode, or a host that fixes its device-memory budget up front -- where j4b_reduce_sum would
- * allocate its block partials. Same result as j4b_reduce_sum (double accumulation, one float
+ * allocate device memory while they run -- a host that fixes its device-memory budget up front
+ * (a JVM handing the engine a pre-sized arena), a serving loop that must not take the
+ * allocator's locks or fail for lack of memory mid-request -- where j4b_reduce_sum would
+ * allocate its block partials. The input must be on the output's device (J4B_EINVAL otherwise). Same result as j4b_reduce_sum (double accumulation, one float
  * out) within the sums' rounding. Its scratch is a static device array of 512 KiB per GPU that
  * loads the library, held until exit, so n is limited to 134,217,728 elements (J4B_EINVAL
  * above that). The first call on a device looks the array up and zeroes its counter, so make

@@ -445,8 +445,11 @@ class B200Backend:
                  qtype, rows, cols, ctypes.byref(handle))
         return QuantBuffer(handle.value, qtype, (rows, cols))
 
-    def quant_matvec(self, w: QuantBuffer, x: DeviceBuffer, add: DeviceBuffer | None = None):
-        """y = W x (+ add). x of shape (cols,) is the reference call; (batch, cols) is batched."""
+    def quant_matvec(self, w: QuantBuffer, x: DeviceBuffer, add: DeviceBuffer | None = None,
+                     out: DeviceBuffer | None = None):
+        """y = W x (+ add). x of shape (cols,) is the reference call; (batch, cols) is batched.
+        `out`, when given, is a preallocated buffer of batch * rows floats that receives y
+        (a decode loop reuses it instead of allocating an output per call)."""
         rows, cols = w.shape
         if x.shape[-1] != cols or len(x.shape) > 2:
             raise ValueError(f"quantMatvec shape mismatch: {w.shape} x {x.shape}")
@@ -454,7 +457,10 @@ class B200Backend:
         out_shape = (rows,) if len(x.shape) == 1 else (batch, rows)
         if add is not None and add.size != batch * rows:
             raise ValueError(f"quantMatvecAdd addend shape {add.shape} does not match {out_shape}")
-        out = self._new(out_shape)
+        if out is None:
+            out = self._new(out_shape)
+        elif out.size != batch * rows:
+            raise ValueError(f"quantMatvec output holds {out.size} floats, the product needs {batch * rows}")
         call("j4b_quant_matvec", ctypes.c_void_p(w.handle), x.ptr, add.ptr if add else 0, out.ptr,
              batch, self.stream)
         return out

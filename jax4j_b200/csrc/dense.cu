@@ -410,6 +410,18 @@ using namespace j4b;
   DeviceGuard guard_(dev);                                          \
   cudaStream_t stream = resolve_stream(dev, s)
 
+// After J4B_DEVICE_OF(out): an input must live on out's device (a kernel launched on out's
+// device must not be handed another GPU's memory, or host memory).
+#define J4B_SAME_DEVICE(ptr, what)                                                           \
+  do {                                                                                       \
+    int in_dev_ = -1;                                                                        \
+    int st_ = device_of((const void*)(uintptr_t)(ptr), &in_dev_);                            \
+    if (st_) return st_;                                                                     \
+    if (in_dev_ != dev)                                                                      \
+      return set_error(J4B_EINVAL, "%s is on device %d but the output is on device %d", what, \
+                       in_dev_, dev);                                                        \
+  } while (0)
+
 extern "C" int j4b_fill(j4b_buf out, int64_t n, float value, j4b_stream s) {
   J4B_REQUIRE(n >= 0, "negative element count");
   if (n == 0) return J4B_OK;
@@ -473,6 +485,7 @@ extern "C" int j4b_transpose(j4b_buf a, j4b_buf out, int64_t rows, int64_t cols,
 static int reduce_all(bool is_max, j4b_buf a, int64_t n, j4b_buf out, j4b_stream s) {
   J4B_REQUIRE(n >= 0, "negative element count");
   J4B_DEVICE_OF(out);
+  if (n > 0) J4B_SAME_DEVICE(a, "the input");
   const unsigned grid = grid_for(n, dev, 8);
   void* ws = nullptr;
   J4B_CUDA(cudaMallocAsync(&ws, grid * sizeof(double) + 16, stream), "cudaMallocAsync(reduce)");
@@ -640,10 +653,10 @@ extern "C" int j4b_matmul(j4b_buf a, j4b_buf b, j4b_buf out, int64_t batch, int6
 // ---------------------------------------------------------------------------------------------
 // Full sum without any allocation.
 //
-// Some callers cannot allocate device memory when they reduce: code that runs inside CUDA stream
-// capture in global capture mode (where allocation calls are errors), and hosts that reserve a
-// fixed device-memory budget up front and forbid growth afterwards (a JVM that hands the engine
-// a pre-sized arena, a serving loop that must not take allocator locks). j4b_reduce_sum above
+// Some callers cannot allocate device memory when they reduce: hosts that reserve a fixed
+// device-memory budget up front and forbid growth afterwards (a JVM that hands the engine a
+// pre-sized arena and accounts for every byte of it), and serving loops that must not take the
+// allocator's locks or risk an out-of-memory failure in the middle of a request. j4b_reduce_sum above
 // allocates its block partials on every call; this variant keeps them in the static array below,
 // which every GPU that loads the library holds until the process exits (512 KiB + 256 bytes).
 //
@@ -730,6 +743,7 @@ extern "C" int j4b_reduce_sum_noalloc(j4b_buf a, int64_t n, j4b_buf out, j4b_str
               (long long)(kNoallocChunk * kNoallocMaxChunks), (long long)kNoallocMaxChunks,
               (long long)kNoallocChunk, (long long)n);
   J4B_DEVICE_OF(out);
+  if (n > 0) J4B_SAME_DEVICE(a, "the input");
   double* scratch = nullptr;
   int st = noalloc_scratch(dev, stream, &scratch);
   if (st) return st;
