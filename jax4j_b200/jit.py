@@ -163,10 +163,11 @@ class RecordingBackend(Backend):
             self.captured.append((b, got))
         return got
 
-    def rec(self, op: str, shape, ins=(), **attrs) -> Sym:
+    def rec(self, call_op: str, shape, ins=(), /, **attrs) -> Sym:
+        # positional-only: elementwise calls carry their operator as the attribute `op`
         ids = [self.sym(b).id for b in ins]
         out = self.new(shape)
-        self.calls.append(Call(op, out.id, ids, attrs))
+        self.calls.append(Call(call_op, out.id, ids, attrs))
         return out
 
     def download(self, b):

@@ -153,6 +153,9 @@ class Backend:
     def release(self, buf) -> None:
         pass
 
+    def sync(self) -> None:
+        pass
+
     def unwrap(self):
         """The backend this one wraps (tracers), or None for an executing backend."""
         for name in ("inner", "real", "d"):
@@ -176,9 +179,6 @@ def pick_backend(a, b):
     if a is b or not isinstance(b, Backend) or not b.wraps(a):
         return a
     return b
-
-    def sync(self) -> None:
-        pass
 
 
 class Tensor:

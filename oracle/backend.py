@@ -140,13 +140,11 @@ def _tensor_map(c):
     return np.asarray(c.attrs["map"], dtype=np.int64)
 
 
-def run_tape(tape, inputs: list[np.ndarray]) -> list[np.ndarray]:
-    """Interprets a tape (jax4j_b200.jit.Tape) call by call on the oracle: ExecutionPlan.execute
-    (ExecutionPlan.java:77-132) with the CPU backend."""
-    be = OracleBackend()
-    env: dict[int, NpBuf] = {}
-    for bid, x in zip(tape.inputs, inputs):
-        env[bid] = _w(np.asarray(x, np.float32).reshape(tape.shapes[bid]))
+def replay_tape(be, tape, buffers: list) -> list:
+    """ExecutionPlan.execute (ExecutionPlan.java:96-132): the tape's calls replayed one SPI call
+    at a time on the backend `be` (any SPI backend with a `fused_program` call); returns the
+    output buffers."""
+    env: dict = dict(zip(tape.inputs, buffers))
     for c in tape.calls:
         ins = [env[i] for i in c.ins]
         a = c.attrs
@@ -181,7 +179,15 @@ def run_tape(tape, inputs: list[np.ndarray]) -> list[np.ndarray]:
             r = getattr(be, op)(ins[0], tape.shapes[c.out], _tensor_map(c))
         else:
             r = getattr(be, op)(*ins)
-        if r.shape != tuple(tape.shapes[c.out]):
+        if tuple(r.shape) != tuple(tape.shapes[c.out]):
             raise RuntimeError(f"tape shape mismatch at {op}: {r.shape} vs {tape.shapes[c.out]}")
         env[c.out] = r
-    return [env[o].a.copy() for o in tape.outputs]
+    return [env[o] for o in tape.outputs]
+
+
+def run_tape(tape, inputs: list[np.ndarray]) -> list[np.ndarray]:
+    """Interprets a tape (jax4j_b200.jit.Tape) call by call on the oracle: ExecutionPlan.execute
+    (ExecutionPlan.java:77-132) with the CPU backend."""
+    be = OracleBackend()
+    bufs = [_w(np.asarray(x, np.float32).reshape(tape.shapes[bid])) for bid, x in zip(tape.inputs, inputs)]
+    return [b.a.copy() for b in replay_tape(be, tape, bufs)]
