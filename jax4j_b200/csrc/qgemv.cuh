@@ -852,7 +852,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) qgemv_kernel(GemvArgs a) {
 template <int QT, int NT, bool PK>
 cudaError_t launch_gemv(const j4b_qweight* w, const float* x, const float* add, float* y,
                         int batch, int sms, cudaStream_t stream, const GemvPeers* peers,
-                        unsigned* grid_out) {
+                        unsigned* grid_out, bool pdl) {
   // Largest dynamic shared memory a CTA may request: the device's opt-in limit minus the
   // kernel's static shared memory (set once per instantiation).
   static int64_t kMaxSmem = -1;
@@ -953,7 +953,7 @@ cudaError_t launch_gemv(const j4b_qweight* w, const float* x, const float* add, 
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   attr[1].id = cudaLaunchAttributeClusterDimension;
   attr[1].val.clusterDim.x = a.cluster ? (unsigned)w->ksplit : 1u;
   attr[1].val.clusterDim.y = 1;
@@ -970,10 +970,18 @@ template <int QT>
 cudaError_t gemv_dispatch(const j4b_qweight* w, const float* x, const float* add, float* y,
                           int batch, int sms, cudaStream_t stream, const GemvPeers* peers = nullptr,
                           unsigned* grid_out = nullptr) {
-  static const bool legacy = getenv("J4B_QGEMV_LEGACY") != nullptr;  // development A/B only
-  if (!legacy && batch <= 4) return launch_gemv_stream<QT, true>(w, x, add, y, batch, sms, stream, peers, grid_out);
-  if (!legacy && batch <= 8) return launch_gemv_stream<QT, false>(w, x, add, y, batch, sms, stream, peers, grid_out);
-  if (batch <= 4) return launch_gemv<QT, 1, true>(w, x, add, y, batch, sms, stream, peers, grid_out);
-  if (batch <= 8) return launch_gemv<QT, 1, false>(w, x, add, y, batch, sms, stream, peers, grid_out);
-  return launch_gemv<QT, 2, false>(w, x, add, y, batch, sms, stream, peers, grid_out);
+  static const char* variant = getenv("J4B_QGEMV_VARIANT");  // development A/B only
+  static const bool legacy = variant && variant[0] == 'l';
+  static const bool wide = variant && variant[0] == 'w';
+  const bool pdl = !w->fresh;
+  const_cast<j4b_qweight*>(w)->fresh = false;
+  if (!legacy && batch <= 4)
+    return wide ? launch_gemv_stream<QT, true, 16>(w, x, add, y, batch, sms, stream, peers, grid_out, pdl)
+                : launch_gemv_stream<QT, true, 8>(w, x, add, y, batch, sms, stream, peers, grid_out, pdl);
+  if (!legacy && batch <= 8)
+    return wide ? launch_gemv_stream<QT, false, 16>(w, x, add, y, batch, sms, stream, peers, grid_out, pdl)
+                : launch_gemv_stream<QT, false, 8>(w, x, add, y, batch, sms, stream, peers, grid_out, pdl);
+  if (batch <= 4) return launch_gemv<QT, 1, true>(w, x, add, y, batch, sms, stream, peers, grid_out, pdl);
+  if (batch <= 8) return launch_gemv<QT, 1, false>(w, x, add, y, batch, sms, stream, peers, grid_out, pdl);
+  return launch_gemv<QT, 2, false>(w, x, add, y, batch, sms, stream, peers, grid_out, pdl);
 }

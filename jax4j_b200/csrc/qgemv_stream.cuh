@@ -2,17 +2,18 @@
 // j4b::<anonymous>; it reuses that file's fragment decoders tile_compute / tile_compute_pk and
 // its bulk-copy and mbarrier helpers).
 //
-// Shape of one launch: one CTA per SM, sized to at most half of an SM (<= 112 KB of shared
-// memory, 288 threads, <= 112 registers per thread), so that under programmatic dependent launch
-// the next GEMV's CTAs are resident and already streaming their weights while this launch's CTAs
-// finish their last tiles and their split-K folds. A CTA owns one 1024-column K range ("split")
+// Shape of one launch: one CTA per SM. With 8 compute warps the CTA takes at most half of an SM
+// (<= 112 KB of shared memory, 288 threads, <= 112 registers per thread), so that under
+// programmatic dependent launch the next GEMV's CTAs are resident and already streaming their
+// weights while this launch's CTAs finish their last tiles and their split-K folds; with 16 it
+// holds the whole SM with a deeper ring. A CTA owns one 1024-column K range ("split")
 // of a contiguous run of 16-row tiles:
-//   - warp 8 is the producer: one elected lane streams the run's tile chunks (contiguous in the
+//   - the last warp is the producer: one elected lane streams the run's tile chunks (contiguous in the
 //     split-major layout) into a ring of shared-memory stages with 1-D bulk copies, each stage
 //     completing on its `full` mbarrier; it refills a stage once the warps that read it have
 //     arrived on its `empty` mbarrier. The first ring's worth is issued before the dependency
 //     wait (weights are immutable once uploaded).
-//   - warps 0..7 first turn x's 1024-column slice into fp16 hi/lo mma fragments in shared memory
+//   - the compute warps first turn x's 1024-column slice into fp16 hi/lo mma fragments in shared memory
 //     (warp w converts 128-column chunk w), then each warp takes whole tiles round-robin and
 //     walks the tile's 8 chunks itself, so a tile's partial sum over the split never leaves the
 //     warp's registers: no block barrier and no cross-warp reduction in the main loop.
@@ -22,9 +23,12 @@
 // Every mbarrier wait is bounded (j4b_wait.cuh); on a timeout the CTA records an error in the
 // weight's status word, lets every copy still in flight land, and returns.
 
-constexpr int kStreamWarps = 8;                         // compute warps
-constexpr int kStreamThreads = (kStreamWarps + 1) * 32;  // + the producer warp
-constexpr int kStreamSmem = 112 * 1024;                  // two CTAs per SM
+// NW compute warps + 1 producer warp. NW = 8: at most half an SM (112 KB of shared memory), so
+// two launches' CTAs co-reside; NW = 16: one CTA per SM with a deeper ring.
+template <int NW>
+constexpr int stream_threads() { return (NW + 1) * 32; }
+template <int NW>
+constexpr int stream_smem_budget() { return NW == 8 ? 112 * 1024 : 220 * 1024; }
 
 template <int QT>
 constexpr bool stream_needs_xblk() {
@@ -42,24 +46,37 @@ template <int QT, bool PK>
 constexpr int stream_frag_chunk() {
   return PK ? 2048 + (stream_needs_xblk<QT>() ? 512 : 0) : 4096 + (stream_needs_xblk<QT>() ? 1024 : 0);
 }
-template <int QT, bool PK>
+template <int QT, bool PK, int NW>
 constexpr int stream_stages() {
   constexpr int stage = stream_tiles_per_stage<QT>() * GemvTraits<QT>::kChunk;
-  constexpr int r = (kStreamSmem - 8 * stream_frag_chunk<QT, PK>() - 256) / stage;
-  return r > 8 ? 8 : r;
+  constexpr int r = (stream_smem_budget<NW>() - 8 * stream_frag_chunk<QT, PK>() - 512) / stage;
+  return r > 16 ? 16 : r;
 }
-template <int QT, bool PK>
+// ring | x fragments | full[R] | empty[R] mbarriers | seq[R] stage numbers
+template <int QT, bool PK, int NW>
 constexpr int stream_smem_bytes() {
-  return stream_stages<QT, PK>() * stream_tiles_per_stage<QT>() * GemvTraits<QT>::kChunk +
-         8 * stream_frag_chunk<QT, PK>() + 2 * 8 * stream_stages<QT, PK>();
+  return stream_stages<QT, PK, NW>() * stream_tiles_per_stage<QT>() * GemvTraits<QT>::kChunk +
+         8 * stream_frag_chunk<QT, PK>() + 2 * 8 * stream_stages<QT, PK, NW>() + 4 * stream_stages<QT, PK, NW>();
 }
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
-// Barrier 1 over the eight compute warps only (the producer warp never takes it).
+// Barrier 1 over the compute warps only (the producer warp never takes it).
+template <int NW>
 __device__ __forceinline__ void compute_warps_sync() {
-  asm volatile("bar.sync 1, %0;" ::"n"(kStreamWarps * 32) : "memory");
+  asm volatile("bar.sync 1, %0;" ::"n"(NW * 32) : "memory");
+}
+// Waits (bounded) until the producer has issued stage `st` into its slot: only then is the slot's
+// `full` barrier on the phase of that stage, so its parity identifies the stage. (A warp can reach
+// a slot while the slot's previous stage is still in flight; the parity of that earlier phase
+// would otherwise read as complete.)
+__device__ __forceinline__ bool wait_issued(const volatile int* seq, int st) {
+  if (*seq == st) return true;
+  const uint64_t t0 = global_ns();
+  while (*seq != st)
+    if (global_ns() - t0 > kWaitNs) return false;
+  return true;
 }
 
 // Warp `c` converts x's columns [kc0 + 128c, kc0 + 128c + 128) of every batch row into the
@@ -162,10 +179,10 @@ __device__ __forceinline__ void stream_coord(int lane, int cc, int& row, int& bc
   }
 }
 
-template <int QT, bool PK>
-__global__ void __launch_bounds__(kStreamThreads, 2) qgemv_stream_kernel(GemvArgs a) {
+template <int QT, bool PK, int NW>
+__global__ void __launch_bounds__(stream_threads<NW>(), NW == 8 ? 2 : 1) qgemv_stream_kernel(GemvArgs a) {
   using T = GemvTraits<QT>;
-  constexpr int R = stream_stages<QT, PK>();
+  constexpr int R = stream_stages<QT, PK, NW>();
   constexpr int kU = stream_tiles_per_stage<QT>();
   constexpr int kStage = kU * T::kChunk;
   constexpr int kFrag = stream_frag_chunk<QT, PK>();
@@ -177,6 +194,7 @@ __global__ void __launch_bounds__(kStreamThreads, 2) qgemv_stream_kernel(GemvArg
   uint8_t* frag = smem + R * kStage;
   uint64_t* full = reinterpret_cast<uint64_t*>(frag + 8 * kFrag);
   uint64_t* empty = full + R;
+  volatile int* seq = reinterpret_cast<volatile int*>(empty + R);  // stage last issued per slot
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int split = blockIdx.x % a.ksplit;
@@ -194,6 +212,7 @@ __global__ void __launch_bounds__(kStreamThreads, 2) qgemv_stream_kernel(GemvArg
     for (int s = 0; s < R; s++) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kU);
+      seq[s] = -1;
     }
     fence_mbar_init();
   }
@@ -201,12 +220,13 @@ __global__ void __launch_bounds__(kStreamThreads, 2) qgemv_stream_kernel(GemvArg
 
   bool failed = false;
   int issued = 0;  // stages issued (producer lane 0 only)
-  if (warp == kStreamWarps) {
+  if (warp == NW) {
     // ---------------- producer ----------------
     auto issue = [&](int st) {
       const int first = st * kU, count = min(kU, ntiles - first);
       const uint32_t bytes = (uint32_t)count * chunk_bytes;
       uint64_t* bar = &full[st % R];
+      seq[st % R] = st;
       mbar_expect_tx(bar, bytes);
       tma_load_1d(ring + (st % R) * kStage, a.data + a.L.chunk_offset(split, tile0 + first), bytes, bar);
     };
@@ -232,11 +252,13 @@ __global__ void __launch_bounds__(kStreamThreads, 2) qgemv_stream_kernel(GemvArg
     int64_t par_off = 0;  // parity half of the gathered buffer (peer all-gather only)
     if (a.nranks > 1) par_off = (int64_t)(*a.step & 1u) * a.half_floats;
     if (warp < nchunks) stream_prep_x<QT, PK>(a, kc0, warp, lane, frag);
-    compute_warps_sync();
+    compute_warps_sync<NW>();
 
-    for (int u = warp; u < ntiles; u += kStreamWarps) {
+    for (int u = warp; u < ntiles; u += NW) {
       const int st = u / kU, slot = st % R;
-      if (!failed && !mbar_wait_bounded(&full[slot], (uint32_t)((st / R) & 1))) failed = true;
+      if (!failed && !(wait_issued(seq + slot, st) && mbar_wait_bounded(&full[slot], (uint32_t)((st / R) & 1))))
+        failed = true;
+      failed = __any_sync(0xffffffffu, failed);  // keep the warp's lanes together
       float acc[kNV];
 #pragma unroll
       for (int i = 0; i < kNV; i++) acc[i] = 0.f;
@@ -352,7 +374,7 @@ __global__ void __launch_bounds__(kStreamThreads, 2) qgemv_stream_kernel(GemvArg
 
   if (__syncthreads_or(failed)) {
     // Let every copy still in flight land before the CTA's shared memory is released.
-    if (warp == kStreamWarps && lane == 0) {
+    if (warp == NW && lane == 0) {
       atomicExch(a.status, 1);
       for (int s = 0; s < R && s < issued; s++) {
         const int last = s + ((issued - 1 - s) / R) * R;  // the last stage issued into slot s
@@ -364,14 +386,15 @@ __global__ void __launch_bounds__(kStreamThreads, 2) qgemv_stream_kernel(GemvArg
   signal_peers(a);
 }
 
-template <int QT, bool PK>
+template <int QT, bool PK, int NW>
 cudaError_t launch_gemv_stream(const j4b_qweight* w, const float* x, const float* add, float* y, int batch,
-                               int sms, cudaStream_t stream, const GemvPeers* peers, unsigned* grid_out) {
-  constexpr int smem = stream_smem_bytes<QT, PK>();
+                               int sms, cudaStream_t stream, const GemvPeers* peers, unsigned* grid_out,
+                               bool pdl) {
+  constexpr int smem = stream_smem_bytes<QT, PK, NW>();
   static bool attr_set[kMaxDevices] = {};  // function attributes are per device context
   if (w->dev < 0 || w->dev >= kMaxDevices) return cudaErrorInvalidDevice;
   if (!attr_set[w->dev]) {
-    cudaError_t e = cudaFuncSetAttribute(qgemv_stream_kernel<QT, PK>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaError_t e = cudaFuncSetAttribute(qgemv_stream_kernel<QT, PK, NW>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     attr_set[w->dev] = true;
   }
@@ -406,14 +429,14 @@ cudaError_t launch_gemv_stream(const j4b_qweight* w, const float* x, const float
   const int64_t groups = std::max<int64_t>(1, std::min<int64_t>(w->rt, (int64_t)sms / w->ksplit));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(groups * w->ksplit));
-  cfg.blockDim = dim3(kStreamThreads);
+  cfg.blockDim = dim3(stream_threads<NW>());
   cfg.dynamicSmemBytes = (size_t)smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl ? 1 : 0;
   if (grid_out) *grid_out = cfg.gridDim.x;
-  return cudaLaunchKernelEx(&cfg, qgemv_stream_kernel<QT, PK>, a);
+  return cudaLaunchKernelEx(&cfg, qgemv_stream_kernel<QT, PK, NW>, a);
 }

@@ -50,6 +50,11 @@ struct j4b_qweight {
   float* partials;     // [ksplit][rt][256] split-K scratch
   unsigned* arrivals;  // [rt] arrival counters (one per tile group), zero between launches
   int* status;         // set to nonzero by a kernel whose bounded wait gave up
+  // Set by the upload: the repack kernels that wrote `data` may be the kernels right before the
+  // next GEMV in the stream, and a GEMV launched with programmatic dependent launch reads its
+  // weights before it waits on the kernel before it; the first GEMV after an upload therefore
+  // launches without it (host-side flag, cleared at that launch).
+  bool fresh;
 };
 
 namespace j4b {
@@ -650,6 +655,7 @@ int upload_common(int dev, const uint8_t* dblob, int type, int64_t rows, int64_t
     }
     count_launch();
   }
+  w->fresh = true;
   *out = w;
   return J4B_OK;
 }
