@@ -4,20 +4,25 @@ Default workload (the metric's "Q8_0 dequant-GEMV GB/s"): y
 with W a 4096 x 4096 weight drawn 0.02*N(0,1) by the engine's own counter PRNG
 (PrngKey(0).split(2)[1]) and quantised Q8_0 on the device, x [8, 4096] ~ N(0,1)
 (split(2)[0]). A step is one GEMV call; `value` is algorithmic bytes (GGUF weight bytes + x + y)
-per second over all GPUs. Other workloads (--config):
+per second over all GPUs. The same run measures the metric's other workloads and reports each as
+an entry of `secondary` (value, roofline, clocks, CPU baseline and end-to-end figure of its own):
+q4_k_b1 and q4_k_b16 and rms_swiglu; --primary-only skips them.
+Workloads selectable with --config:
   q4_k_b1, q4_k_b16   configs[2]: Q4_K decode GEMV, W [14336 x 4096], batch 1 / 16 (GB/s)
+  q6_k_b1, q6_k_b16   Q6_K decode GEMV, W [4096 x 14336] (GB/s)
   rms_swiglu          configs[3]: the vmap-batched RMSNorm + SwiGLU value-and-gradient tape,
                       x [4096, 8192] per GPU (steps/s)
   mlp_adam            configs[0]: the compiled MLP valueAndGrad + Adam training step (steps/s)
   prefill_q4_0        configs[4] prefill projection x [16384, 4096] . W^T, W Q4_0 [14336 x 4096]
                       on the tcgen05 tensor cores (TFLOP/s)
   gemm_f32            the same shape as a dense f32 matmul, fp32-accurate 3-term mode (TFLOP/s)
+  decoder_decode, decoder_prefill, conv*, aad*   see their tables below
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl engine|reference] [--config NAME]
 
 N > 1 (launched by torchrun, one rank per GPU), weak scaling: for the GEMV each rank owns a
-4096-row slab of a (4096 N)-row weight and the GEMV epilogue stores its y slab into every rank's
-buffer over NVLink (j4b_quant_matvec_allgather); for the tape each rank owns 4096 rows and
+rows-per-GPU slab of a (rows N)-row weight and the GEMV epilogue stores its y slab into every
+rank's buffer over NVLink (j4b_quant_matvec_allgather); for the tape each rank owns 4096 rows and
 [dg, loss] are summed over NVLink peer memory (j4b_peer_allreduce); the GEMM and MLP workloads
 run as independent replicas.
 
@@ -26,6 +31,10 @@ is graph-capturable), bracketed by a barrier and device synchronisation, timed w
 on the launching stream, max over ranks. The GEMV weights rotate over enough identical copies
 (>= 2x L2) that every step streams its weight from HBM; the tape and GEMM inputs are larger than
 L2. nvidia-smi samples clocks during the timed region.
+
+--impl reference runs the oracle's restatement of the reference's CPU path (the reference is Java;
+no JVM exists on the GPU box) on all host cores, with the same config dicts, metric and seeded
+inputs (the oracle restates the engine's counter PRNG), rank 0 only.
 """
 from __future__ import annotations
 
@@ -148,16 +157,6 @@ def measured_peaks():
     return 6650.0, "fallback"
 
 
-def profiled_traffic(cfg):
-    """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary, if any."""
-    name = f"tape_{cfg}.md" if cfg in TAPE_CONFIGS else f"qgemv_{cfg}.md"
-    path = os.path.join(HERE, "profiles", name)
-    if not os.path.exists(path):
-        return None
-    m = re.search(r"traffic_bytes_per_launch:\s*([0-9]+)", open(path).read())
-    return int(m.group(1)) if m else None
-
-
 class ClockSampler:
     """nvidia-smi sampling of SM clocks and throttle reasons while the GPU is busy."""
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
@@ -225,23 +224,97 @@ def dist_env():
 # CPU side: the oracle restatement of the reference's CPU path (baseline and --impl reference)
 # ------------------------------------------------------------------------------------------------
 
-def cpu_matvec_rate(qtype, rows, cols, batch, threads, budget_s, blob=None, x=None):
-    """Times the oracle's float-sequential quantMatvec (reference loop style) on a bounded row
-    sample split over `threads` host threads. Returns (GB/s of algorithmic bytes, sample text)."""
+DEFAULT_CONFIG = "q8_0_b8"
+# measured beside the default workload in the same run, each with its own roofline, clocks,
+# CPU baseline and end-to-end figure
+SECONDARY = ("q4_k_b1", "q4_k_b16", "rms_swiglu")
+
+# Per-launch DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of each workload's
+# dominant kernel from one ncu capture of the same command, with the capture it comes from. A
+# constant of this file, not a run-time measurement: the bench itself never runs under ncu.
+TRAFFIC = {
+    "q8_0_b8": (17994496, "ncu capture of one qgemv_kernel launch (profiles/qgemv_q8_0_b8.md)"),
+    "q4_k_b1": (33096192, "ncu capture of one qgemv_kernel launch (profiles/qgemv_q4_k_b1.md)"),
+    "q6_k_b1": (48293632, "ncu capture of one qgemv_kernel launch (profiles/qgemv_q6_k_b1.md)"),
+    "rms_swiglu": (229038848, "ncu capture of one j4b_group0 launch (profiles/tape_rms_swiglu.md)"),
+}
+
+
+def gemv_config(name, world):
+    """The workload's config dict, identical in the engine and the reference arm."""
+    qtype, rows, cols, batch, label = CONFIGS[name]
+    return {"workload": label, "quant": TYPE_NAME[qtype], "batch": batch, "rows_per_gpu": rows,
+            "cols": cols, "bytes_per_step_per_gpu": alg_bytes(qtype, rows, cols, batch),
+            "inputs": "PrngKey(0).split(2) -> (kx, kw): x = normal(kx) [batch, cols]; "
+                      "W = 0.02 * normal(kw, counter + rank * rows * cols) [rows, cols], "
+                      "quantised by the GGUF block encoder",
+            "parallelism": "replica" if world == 1 else
+            f"row-shard x{world}: each rank a {rows}-row slab, y all-gathered over NVLink peer stores "
+            "fused into the GEMV epilogue (no NCCL call)"}
+
+
+def tape_config(name, world):
+    rows, cols, label = TAPE_CONFIGS[name]
+    return {"workload": label, "rows_per_gpu": rows, "cols": cols,
+            "bytes_per_step_per_gpu": tape_alg_bytes(rows, cols),
+            "inputs": "PrngKey(0).split(2) -> (kx, kg): x = normal(kx, counter + rank * rows * cols) "
+                      "[rows, cols]; g = 1 + 0.1 * normal(kg) [cols]",
+            "parallelism": "replica" if world == 1 else
+            f"data-parallel x{world}: rows per rank, [dg, loss] summed over NVLink peer memory "
+            "(rank-ordered, no NCCL call)"}
+
+
+def _keys():
+    sys.path.insert(0, HERE)
+    from jax4j_b200.prng import PrngKey
+    return PrngKey.of(0).split(2)
+
+
+def gemv_inputs_host(qtype, cols, batch, row0, nrows, rank=0, rows_per_rank=0):
+    """Rows [row0, row0 + nrows) of the bench's weight and its x, drawn on the host by the
+    oracle's restatement of the same counter PRNG the engine draws them with on the device."""
     import numpy as np
+    from oracle import oracle as o
+    kx, kw = _keys()
+    x = o.random_normal(kx.seed, kx.counter, batch * cols).reshape(batch, cols)
+    w = o.random_normal(kw.seed, kw.counter + (rank * rows_per_rank + row0) * cols, nrows * cols)
+    w = (w * np.float32(0.02)).astype(np.float32).reshape(nrows, cols)
+    return o.quantize(qtype, w), x
+
+
+def tape_inputs_host(rows, cols, row0, nrows, rank=0):
+    import numpy as np
+    from oracle import oracle as o
+    kx, kg = _keys()
+    x = o.random_normal(kx.seed, kx.counter + (rank * rows + row0) * cols, nrows * cols).reshape(nrows, cols)
+    g = (o.random_normal(kg.seed, kg.counter, cols) * np.float32(0.1) + np.float32(1.0)).astype(np.float32)
+    return x, g
+
+
+_CPU_INPUTS = {}  # the current sample's host inputs
+_CALIBRATION = {}  # seconds per row of one thread, per workload shape
+
+
+def cpu_matvec_rate(qtype, rows, cols, batch, threads, budget_s):
+    """Times the oracle's float-sequential quantMatvec (reference loop style) on a bounded row
+    sample of the bench's own weight (same PRNG keys), split over `threads` host threads.
+    Returns (GB/s of algorithmic bytes, sample text, seconds)."""
     sys.path.insert(0, HERE)
     from oracle import oracle as o
-    if blob is None:
-        rng = np.random.default_rng(0)
-        w = (rng.standard_normal((rows, cols)) * 0.02).astype(np.float32)
-        blob = o.quantize(qtype, w)
-        x = rng.standard_normal((batch, cols)).astype(np.float32)
     rb = o.quant_row_bytes(qtype, cols)
-    # calibrate: one row-block of 16 rows single-threaded
-    t0 = time.perf_counter()
-    o.quant_matvec(qtype, blob[:16 * rb], 16, cols, x)
-    per_row = (time.perf_counter() - t0) / 16
+    ckey = ("gemv-row-s", qtype, cols, batch)
+    if ckey not in _CALIBRATION:  # one thread, 16 rows
+        blob16, x = gemv_inputs_host(qtype, cols, batch, 0, 16)
+        t0 = time.perf_counter()
+        o.quant_matvec(qtype, blob16, 16, cols, x)
+        _CALIBRATION[ckey] = (time.perf_counter() - t0) / 16
+    per_row = _CALIBRATION[ckey]
     sample_rows = max(threads, min(rows, int(budget_s * threads / max(per_row, 1e-9))))
+    key = ("gemv", qtype, rows, cols, batch, sample_rows)
+    if key not in _CPU_INPUTS:
+        _CPU_INPUTS.clear()
+        _CPU_INPUTS[key] = gemv_inputs_host(qtype, cols, batch, 0, sample_rows)
+    blob, x = _CPU_INPUTS[key]
     chunks = [(i * sample_rows // threads, (i + 1) * sample_rows // threads) for i in range(threads)]
 
     def work(c):
@@ -267,37 +340,34 @@ def tape_alg_bytes(rows, cols):
     return 4 * (2 * rows * cols + 2 * cols + 1)
 
 
-def rms_inputs_host(rows, cols, seed=0):
-    import numpy as np
-    rng = np.random.default_rng(seed)
-    x = rng.standard_normal((rows, cols)).astype(np.float32)
-    g = (1 + 0.1 * rng.standard_normal(cols)).astype(np.float32)
-    return x, g
-
-
-def cpu_tape_rate(rows, cols, threads, budget_s, x=None, g=None):
+def cpu_tape_rate(rows, cols, threads, budget_s):
     """Times the oracle's call-by-call replay of the tape (the reference CPU backend's
-    primitives, single-threaded each) on a bounded row sample, split over `threads` host
-    threads (row chunks; their column sums and losses combine). Returns (steps/s of the full
-    workload, sample text, seconds)."""
+    primitives, single-threaded each) on a bounded row sample of the bench's own x (same PRNG
+    keys), split over `threads` host threads (row chunks; their column sums and losses combine).
+    Returns (steps/s of the full workload, sample text, seconds)."""
     sys.path.insert(0, HERE)
     from jax4j_b200 import jit as J, nn
     from oracle.backend import run_tape
-    if x is None:
-        x, g = rms_inputs_host(rows, cols)
-    # calibrate on 8 rows
-    t8 = J.trace(nn.rms_swiglu_value_and_grad, [(8, cols), (cols,)])
-    t0 = time.perf_counter()
-    run_tape(t8, [x[:8], g])
-    per_row = (time.perf_counter() - t0) / 8
+    ckey = ("tape-row-s", cols)
+    if ckey not in _CALIBRATION:  # one thread, 8 rows
+        x8, g = tape_inputs_host(rows, cols, 0, 8)
+        t8 = J.trace(nn.rms_swiglu_value_and_grad, [(8, cols), (cols,)])
+        t0 = time.perf_counter()
+        run_tape(t8, [x8, g])
+        _CALIBRATION[ckey] = (time.perf_counter() - t0) / 8
+    per_row = _CALIBRATION[ckey]
     sample_rows = max(threads, min(rows, int(budget_s * threads / max(per_row, 1e-9))))
     chunk = -(-sample_rows // threads)
     sample_rows = chunk * threads
+    key = ("tape", rows, cols, sample_rows)
+    if key not in _CPU_INPUTS:
+        _CPU_INPUTS.clear()
+        _CPU_INPUTS[key] = tape_inputs_host(rows, cols, 0, sample_rows)
+    x, g = _CPU_INPUTS[key]
     tape = J.trace(nn.rms_swiglu_value_and_grad, [(chunk, cols), (cols,)])
 
     def work(i):
-        r0 = (i * chunk) % max(rows - chunk + 1, 1)
-        return run_tape(tape, [x[r0:r0 + chunk], g])
+        return run_tape(tape, [x[i * chunk:(i + 1) * chunk], g])
 
     t0 = time.perf_counter()
     if threads == 1:
@@ -310,6 +380,10 @@ def cpu_tape_rate(rows, cols, threads, budget_s, x=None, g=None):
     sample = (f"{sample_rows} of {rows} rows x {cols} cols ({threads} chunk(s) of {chunk} rows), "
               f"oracle replay of the same tape (CpuBackend primitives), {threads} thread(s)")
     return steps_per_s, sample, dt
+
+
+def gemv_kernel_name(batch):
+    return "qgemv_stream_kernel" if batch <= 8 else "qgemv_kernel"
 
 
 def cpu_mlp_rate(batch, d_in, budget_s):
@@ -355,29 +429,57 @@ def run_reference_tape(args):
             "e2e": {"value": round(value, 5), "unit": "steps/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}), flush=True)
         return 0
-    threads = os.cpu_count() or 1
-    total = args.steps + args.warmup
-    budget = max(0.2, min(5.0, 90.0 / max(total, 1)))
-    x, g = rms_inputs_host(rows, cols)
-    for _ in range(args.warmup):
-        cpu_tape_rate(rows, cols, threads, budget, x, g)
+    return run_reference_workloads(args)
+
+
+def reference_entry(name, K, W, threads, budget, world):
+    """The reference arm's result for one GEMV / tape workload: the oracle port of the
+    reference's CPU path on `threads` host threads, K bounded samples after W warm-up ones."""
+    is_tape = name in TAPE_CONFIGS
+    if is_tape:
+        rows, cols, _ = TAPE_CONFIGS[name]
+        rate = lambda: cpu_tape_rate(rows, cols, threads, budget)  # noqa: E731
+        unit, cfg = "steps/s", tape_config(name, world)
+    else:
+        qtype, rows, cols, batch, _ = CONFIGS[name]
+        rate = lambda: cpu_matvec_rate(qtype, rows, cols, batch, threads, budget)  # noqa: E731
+        unit, cfg = "GB/s", gemv_config(name, world)
+    for _ in range(W):
+        rate()
     rates, times, sample = [], [], ""
-    for _ in range(args.steps):
-        r, sample, dt = cpu_tape_rate(rows, cols, threads, budget, x, g)
+    for _ in range(K):
+        r, sample, dt = rate()
         rates.append(r)
-        times.append(1.0 / r)
+        times.append((1.0 / r) if is_tape else dt)
     value = statistics.median(rates)
-    line = {
-        "impl": "reference", "metric": METRIC, "value": round(value, 5), "unit": "steps/s",
-        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(1e3 * statistics.median(times), 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": label, "rows": rows, "cols": cols},
-        "cpu_baseline": {"value": round(value, 5), "unit": "steps/s", "cores": threads,
-                         "kind": "port", "sample": sample},
-        "e2e": {"value": round(value, 5), "unit": "steps/s", "h2d_bytes_per_step": 0,
-                "d2h_bytes_per_step": 0},
-    }
+    digits = 5 if is_tape else 3
+    return {"name": name, "value": round(value, digits), "unit": unit, "steps": K, "warmup": W,
+            "ms_per_step": round(1e3 * statistics.median(times), 3), "higher_is_better": True,
+            "config": cfg,
+            "cpu_baseline": {"value": round(value, digits), "unit": unit, "cores": threads,
+                             "kind": "port", "sample": sample},
+            "e2e": {"value": round(value, digits), "unit": unit, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+
+
+def run_reference_workloads(args):
+    """Reference arm of the GEMV / tape workloads: rank 0 alone; the same config dicts and the
+    same seeded inputs as the engine arm, the default run with the same secondary workloads."""
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return 0
+    threads = os.cpu_count() or 1
+    names = [args.config] + (list(SECONDARY) if args.config == DEFAULT_CONFIG and not args.primary_only else [])
+    total = (args.steps + args.warmup) * len(names)
+    budget = max(0.002, min(2.0, 60.0 / max(total, 1)))  # whole run within a few minutes
+    entries = [reference_entry(n, args.steps, args.warmup, threads, budget, world) for n in names]
+    e = entries[0]
+    line = {"impl": "reference", "metric": METRIC, "value": e["value"], "unit": e["unit"],
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": e["ms_per_step"],
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": e["config"], "cpu_baseline": e["cpu_baseline"], "e2e": e["e2e"]}
+    if len(entries) > 1:
+        line["secondary"] = entries[1:]
     print(json.dumps(line), flush=True)
     return 0
 
@@ -450,42 +552,7 @@ def run_reference(args):
         return run_reference_tape(args)
     if args.config in GEMM_CONFIGS:
         return run_reference_gemm(args)
-    world, rank, _ = dist_env()
-    if rank != 0:
-        return 0
-    qtype, rows, cols, batch, label = CONFIGS[args.config]
-    threads = os.cpu_count() or 1
-    total_steps = args.steps + args.warmup
-    budget = max(0.05, min(2.0, 90.0 / max(total_steps, 1)))  # whole run within ~1.5 minutes
-    import numpy as np
-    sys.path.insert(0, HERE)
-    from oracle import oracle as o
-    rng = np.random.default_rng(0)
-    w = (rng.standard_normal((rows, cols)) * 0.02).astype(np.float32)
-    blob = o.quantize(qtype, w)
-    x = rng.standard_normal((batch, cols)).astype(np.float32)
-    for _ in range(args.warmup):
-        cpu_matvec_rate(qtype, rows, cols, batch, threads, budget, blob, x)
-    rates, times, sample = [], [], ""
-    for _ in range(args.steps):
-        r, sample, dt = cpu_matvec_rate(qtype, rows, cols, batch, threads, budget, blob, x)
-        rates.append(r)
-        times.append(dt)
-    value = statistics.median(rates)
-    line = {
-        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s",
-        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(1e3 * statistics.median(times), 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": label, "batch": batch, "rows": rows, "cols": cols,
-                   "quant": TYPE_NAME[qtype]},
-        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads,
-                         "kind": "port", "sample": sample},
-        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
-                "d2h_bytes_per_step": 0},
-    }
-    print(json.dumps(line), flush=True)
-    return 0
+    return run_reference_workloads(args)
 
 
 # ------------------------------------------------------------------------------------------------
@@ -631,25 +698,220 @@ def run_engine_mlp(args):
 def run_engine_tape(args):
     if args.config == "mlp_adam":
         return run_engine_mlp(args)
+    return run_engine_workloads(args)
+
+
+class EngineCtx:
+    """Per-process engine state shared by the workloads one bench run measures: the device,
+    the process group (N > 1), the backend and, created on first use, the peer-memory group."""
+
+    def __init__(self):
+        import torch
+        import torch.distributed as dist
+        sys.path.insert(0, HERE)
+        from jax4j_b200.backend import B200Backend
+        self.world, self.rank, self.local = dist_env()
+        torch.cuda.set_device(self.local)
+        if self.world > 1:
+            import datetime
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", self.local))
+        self.be = B200Backend(self.local)
+        self.dev = torch.device("cuda", self.local)
+        self._peers = None
+
+    def peers(self):
+        if self._peers is None:
+            from jax4j_b200.peers import PeerGroup
+            self._peers = PeerGroup(self.local, self.rank, self.world)
+        return self._peers
+
+    def barrier(self):
+        import torch
+        import torch.distributed as dist
+        if self.world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(self, ms):
+        import torch
+        import torch.distributed as dist
+        if self.world > 1:
+            t = torch.tensor([ms], device=self.dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    def close(self):
+        import torch.distributed as dist
+        if self.world > 1:
+            if self._peers is not None:
+                status = self._peers.status()
+                self._peers.close()
+                if status and self.rank == 0:
+                    print("peer collective wait gave up", file=sys.stderr)
+            dist.barrier()
+            dist.destroy_process_group()
+
+
+def timed_graph(ctx, step, K, W):
+    """Captures W warm-up and K timed steps in CUDA graphs, soaks ~0.5 s so clocks reach their
+    loaded state, then times the K-step graph with CUDA events on the launching stream between
+    barriers (max over ranks) while nvidia-smi samples the clocks. Returns (ms, clocks)."""
+    import torch
+
+    def capture(n):
+        g = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            step(0)  # warm the path on the capture stream
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        with torch.cuda.graph(g):
+            for i in range(n):
+                step(i)
+        return g
+
+    warm, main = capture(W), capture(K)
+    main.replay()  # the first replay of a graph also uploads it: keep that out of the timed one
+    warm.replay()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    soak_t0 = time.perf_counter()
+    with ClockSampler(ctx.local) as clocks:
+        while time.perf_counter() - soak_t0 < 0.5:
+            warm.replay()
+            torch.cuda.synchronize()
+        ctx.barrier()
+        start.record()
+        main.replay()
+        end.record()
+        ctx.barrier()
+        tail = time.perf_counter()  # keep sampling briefly so short timed regions get samples
+        while time.perf_counter() - tail < 0.3:
+            warm.replay()
+            torch.cuda.synchronize()
+    ms = ctx.max_over_ranks(start.elapsed_time(end))
+    del main, warm
+    return ms, clocks.summary()
+
+
+def roofline_entry(achieved, kernel, kernel_avg_us, traffic_key):
+    peak, peak_kind = measured_peaks()
+    traffic, traffic_src = TRAFFIC.get(traffic_key, (None, "no ncu capture"))
+    return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+            "frac": round(achieved / peak, 4), "traffic": traffic, "traffic_source": traffic_src,
+            "peak_source": f"{peak_kind} MEASURED_PEAKS.json hbm_gbs" if peak_kind == "measured" else "fallback 6.65 TB/s",
+            "kernel": kernel, "kernel_avg_us": round(kernel_avg_us, 3)}
+
+
+def clocks_entry(clk):
+    return {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"], "reasons": clk["reasons"],
+            "samples": clk["samples"]}
+
+
+def measure_gemv(ctx, name, K, W, cpu_budget):
+    """One GEMV workload (CONFIGS[name]); returns its result entry (rank 0) or None."""
     import numpy as np
     import torch
-    import torch.distributed as dist
-    sys.path.insert(0, HERE)
+    from jax4j_b200 import _lib
+    from jax4j_b200.backend import torch_stream
+    from jax4j_b200.prng import PrngKey
+    be, world, rank = ctx.be, ctx.world, ctx.rank
+    qtype, rows, cols, batch, label = CONFIGS[name]
+    per_call = alg_bytes(qtype, rows, cols, batch)
+
+    # ---- synthetic inputs, generated on the device by the engine (the keys of gemv_inputs_host) ----
+    kx, kw = PrngKey.of(0).split(2)
+    x = be.random_normal(kx.seed, kx.counter, (batch, cols))
+    w32 = be.scalar("MUL", be.random_normal(kw.seed, kw.counter + rank * rows * cols, (rows, cols)), 0.02)
+    blob = be.quantize(w32, qtype)
+    l2 = torch.cuda.get_device_properties(ctx.dev).L2_cache_size
+    copies = max(2, math.ceil(2 * l2 / blob.numel()))
+    weights = [be.upload_quantized(blob, qtype, (rows, cols)) for _ in range(copies)]
+    del w32, blob
+    y = torch.empty(batch * rows, dtype=torch.float32, device=ctx.dev)
+    y_all = torch.empty(world * batch * rows, dtype=torch.float32, device=ctx.dev) if world > 1 else None
+    peers = ctx.peers() if world > 1 else None
+    torch.cuda.synchronize()
+
+    def gemv(i):
+        _lib.call("j4b_quant_matvec", ctypes.c_void_p(weights[i % copies].handle), x.ptr, 0,
+                  y.data_ptr(), batch, torch_stream())
+
+    def step(i):
+        if world > 1:  # the GEMV's epilogue stores into every rank's buffer over NVLink
+            peers.allgather_matvec(weights[i % copies], x.ptr, y_all.data_ptr(), batch, torch_stream())
+        else:
+            gemv(i)
+
+    ms, clk = timed_graph(ctx, step, K, W)
+    kernel_ms = timed_graph(ctx, gemv, K, W)[0] if world > 1 else ms
+    value = world * per_call * K / (ms * 1e-3) / 1e9
+    kernel_avg_us = kernel_ms * 1e3 / K
+
+    # ---- end to end through the public API: pinned host x in, y out, every step ----
+    x_host = torch.from_numpy(np.ascontiguousarray(be.download(x))).pin_memory()
+    y_host = torch.empty(batch * rows, dtype=torch.float32).pin_memory()
+    out = be.full(0.0, (batch, rows))
+    xin = be.full(0.0, (batch, cols))
+    e2e_steps = max(K, 200)
+    stream = torch_stream()
+    for i in range(3):  # warm the path
+        be.quant_matvec(weights[i % copies], xin, out=out)
+    ctx.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
+    e0.record()
+    for i in range(e2e_steps):
+        _lib.call("j4b_h2d", xin.ptr, ctypes.c_void_p(x_host.data_ptr()), x_host.numel() * 4, stream)
+        be.quant_matvec(weights[i % copies], xin, out=out)
+        _lib.call("j4b_d2h", ctypes.c_void_p(y_host.data_ptr()), out.ptr, y_host.numel() * 4, stream)
+    e1.record()
+    host_issue_s = time.perf_counter() - t0
+    ctx.barrier()
+    e_ms = ctx.max_over_ranks(e0.elapsed_time(e1))
+    e2e_value = world * per_call * e2e_steps / (e_ms * 1e-3) / 1e9
+
+    cpu = None
+    if rank == 0 and world == 1 and cpu_budget > 0:
+        rate, sample, _ = cpu_matvec_rate(qtype, rows, cols, batch, 1, cpu_budget)
+        cpu = {"value": round(rate, 4), "unit": "GB/s", "cores": 1, "kind": "port",
+               "sample": sample + f" (host has {os.cpu_count()} cores)"}
+    del weights
+    if rank != 0:
+        return None
+    return {
+        "name": name, "value": round(value, 2), "unit": "GB/s", "steps": K, "warmup": W,
+        "ms_per_step": round(ms / K, 6), "higher_is_better": True,
+        "config": gemv_config(name, world),
+        "method": {"compute": "quant codes -> exact fp16 mma.sync operands, x split fp16 hi+lo, fp32 accumulate",
+                   "l2": f"weights rotate over {copies} copies ({copies * per_call / 1e6:.0f} MB > 2x L2)",
+                   "timing": "CUDA graph of K GEMV calls, CUDA events, max over ranks"},
+        "roofline": roofline_entry(per_call / (kernel_avg_us * 1e-6) / 1e9, gemv_kernel_name(batch),
+                                   kernel_avg_us, name),
+        "cpu_baseline": cpu,
+        "e2e": {"value": round(e2e_value, 3), "unit": "GB/s",
+                "h2d_bytes_per_step": batch * cols * 4, "d2h_bytes_per_step": batch * rows * 4,
+                "host_issue_us_per_step": round(host_issue_s * 1e6 / e2e_steps, 2),
+                "device_us_per_step": round(e_ms * 1e3 / e2e_steps, 2)},
+        "gpu_launches": K,
+        "clocks": clocks_entry(clk),
+    }
+
+
+def measure_tape(ctx, name, K, W, cpu_budget):
+    """The vmap-batched RMSNorm + SwiGLU value-and-gradient tape (TAPE_CONFIGS[name])."""
+    import numpy as np
+    import torch
     from jax4j_b200 import jit as J, nn
     from jax4j_b200 import _lib
-    from jax4j_b200.backend import B200Backend, TapeHandle, torch_stream
+    from jax4j_b200.backend import TapeHandle, torch_stream
     from jax4j_b200.prng import PrngKey
-
-    world, rank, local = dist_env()
-    torch.cuda.set_device(local)
-    if world > 1:
-        import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
-    be = B200Backend(local)
-    rows, cols, label = TAPE_CONFIGS[args.config]
+    be, world, rank = ctx.be, ctx.world, ctx.rank
+    rows, cols, label = TAPE_CONFIGS[name]
     per_step = tape_alg_bytes(rows, cols)
-    dev = torch.device("cuda", local)
 
     # ---- synthetic inputs on the device: x ~ N(0,1) [rows, cols] per rank, g = 1 + 0.1 N(0,1)
     kx, kg = PrngKey.of(0).split(2)
@@ -658,149 +920,102 @@ def run_engine_tape(args):
 
     # the tape: value and gradient of the mean of y^2 over the global batch (each rank's mean
     # scaled by 1/world, so the all-reduced sums are the global loss and dg)
-    fn = nn.rms_swiglu_value_and_grad_dp(world)
-    tape = J.trace(fn, [(rows, cols), (cols,)])
+    tape = J.trace(nn.rms_swiglu_value_and_grad_dp(world), [(rows, cols), (cols,)])
     handle = TapeHandle(be, tape)
-    # dg and the loss share one buffer (loss right after dg, 16-byte aligned) so one
-    # all-reduce carries both
+    # dg and the loss share one buffer (loss right after dg, 16-byte aligned): one all-reduce
     red_len = cols + 4
-    reduced = torch.empty(red_len, dtype=torch.float32, device=dev)
-    dg = reduced[:cols]
-    loss = reduced[cols:cols + 1]
-    dx = torch.empty(rows * cols, dtype=torch.float32, device=dev)
+    reduced = torch.empty(red_len, dtype=torch.float32, device=ctx.dev)
+    dg, loss = reduced[:cols], reduced[cols:cols + 1]
+    dx = torch.empty(rows * cols, dtype=torch.float32, device=ctx.dev)
     launches = handle.stats()["launches"]
-    peers = None
-    if world > 1:
-        from jax4j_b200.peers import PeerGroup
-        peers = PeerGroup(local, rank, world)
+    peers = ctx.peers() if world > 1 else None
 
-    def step(stream=None):
-        s = torch_stream() if stream is None else stream
-        handle.launch([x.ptr, g.ptr], [loss.data_ptr(), dx.data_ptr(), dg.data_ptr()], s)
-        if world > 1:
-            # rank-ordered sum over NVLink peer memory, in place (no NCCL call)
+    def step(i, xp=None, gp=None, s=None):
+        s = torch_stream() if s is None else s
+        handle.launch([x.ptr if xp is None else xp, g.ptr if gp is None else gp],
+                      [loss.data_ptr(), dx.data_ptr(), dg.data_ptr()], s)
+        if world > 1:  # rank-ordered sum over NVLink peer memory, in place (no NCCL call)
             peers.allreduce(reduced.data_ptr(), red_len, reduced.data_ptr(), s)
 
-    def capture(n):
-        gr = torch.cuda.CUDAGraph()
-        side = torch.cuda.Stream()
-        side.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(side):
-            step()
-        torch.cuda.current_stream().wait_stream(side)
-        torch.cuda.synchronize()
-        with torch.cuda.graph(gr):
-            for _ in range(n):
-                step()
-        return gr
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-
-    def max_over_ranks(ms):
-        if world > 1:
-            t = torch.tensor([ms], device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms = float(t.item())
-        return ms
-
-    K, W = args.steps, max(3, args.warmup)
-    warm = capture(W)
-    main = capture(K)
-    warm.replay()
-    main.replay()  # the first replay of a graph also uploads it: keep that out of the timed one
-    torch.cuda.synchronize()
-    soak_t0 = time.perf_counter()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
-        while time.perf_counter() - soak_t0 < 0.5:
-            warm.replay()
-            torch.cuda.synchronize()
-        barrier()
-        start.record()
-        main.replay()
-        end.record()
-        barrier()
-        tail = time.perf_counter()
-        while time.perf_counter() - tail < 0.3:
-            warm.replay()
-            torch.cuda.synchronize()
-    clk = clocks.summary()
-    ms = max_over_ranks(start.elapsed_time(end))
+    ms, clk = timed_graph(ctx, step, K, W)
     step_us = ms * 1e3 / K
     value = world * K / (ms * 1e-3)
-    achieved = per_step / (step_us * 1e-6) / 1e9
-    peak, peak_kind = measured_peaks()
 
     # ---- end to end through the public API: pinned host x, g -> device, tape, loss -> host
     x_host = torch.from_numpy(np.ascontiguousarray(be.download(x))).pin_memory()
     g_host = torch.from_numpy(np.ascontiguousarray(be.download(g))).pin_memory()
     loss_host = torch.empty(1, dtype=torch.float32).pin_memory()
-    xin = be.full(0.0, (rows, cols))
-    gin = be.full(0.0, (cols,))
+    xin, gin = be.full(0.0, (rows, cols)), be.full(0.0, (cols,))
     e2e_steps = max(3, min(K, 50))
     stream = torch_stream()
-    barrier()
-    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e_start.record()
-    for _ in range(e2e_steps):
+    ctx.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(e2e_steps):
         _lib.call("j4b_h2d", xin.ptr, ctypes.c_void_p(x_host.data_ptr()), x_host.numel() * 4, stream)
         _lib.call("j4b_h2d", gin.ptr, ctypes.c_void_p(g_host.data_ptr()), g_host.numel() * 4, stream)
-        handle.launch([xin.ptr, gin.ptr], [loss.data_ptr(), dx.data_ptr(), dg.data_ptr()], stream)
-        if world > 1:
-            peers.allreduce(reduced.data_ptr(), red_len, reduced.data_ptr(), stream)
+        step(i, xin.ptr, gin.ptr, stream)
         _lib.call("j4b_d2h", ctypes.c_void_p(loss_host.data_ptr()), loss.data_ptr(), 4, stream)
-    e_end.record()
-    barrier()
-    e_ms = max_over_ranks(e_start.elapsed_time(e_end))
+    e1.record()
+    ctx.barrier()
+    e_ms = ctx.max_over_ranks(e0.elapsed_time(e1))
     e2e_value = world * e2e_steps / (e_ms * 1e-3)
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        rate, sample, _ = cpu_tape_rate(rows, cols, 1, 10.0)
+    if rank == 0 and world == 1 and cpu_budget > 0:
+        rate, sample, _ = cpu_tape_rate(rows, cols, 1, cpu_budget)
         cpu = {"value": round(rate, 5), "unit": "steps/s", "cores": 1, "kind": "port",
                "sample": sample + f" (host has {os.cpu_count()} cores)"}
+    if rank != 0:
+        return None
+    st = handle.stats()
+    return {
+        "name": name, "value": round(value, 2), "unit": "steps/s", "steps": K, "warmup": W,
+        "ms_per_step": round(ms / K, 6), "higher_is_better": True,
+        "config": tape_config(name, world),
+        "method": {"tape": {"calls": st["calls"], "kernels": st["groups"], "folds": st["folds"],
+                            "eager_steps": st["eager_steps"]},
+                   "l2": f"inputs larger than L2 (x {rows * cols * 4 / 1e6:.0f} MB read, dx {rows * cols * 4 / 1e6:.0f} MB written per step)",
+                   "timing": "CUDA graph of K tape replays, CUDA events, max over ranks"},
+        "roofline": roofline_entry(per_step / (step_us * 1e-6) / 1e9,
+                                   "j4b_group0 + j4b_group0_fold (the whole step)", step_us, name),
+        "cpu_baseline": cpu,
+        "e2e": {"value": round(e2e_value, 3), "unit": "steps/s",
+                "h2d_bytes_per_step": (rows * cols + cols) * 4, "d2h_bytes_per_step": 4},
+        "gpu_launches": K * launches,
+        "clocks": clocks_entry(clk),
+    }
 
-    if rank == 0:
-        st = handle.stats()
-        line = {
-            "metric": METRIC, "value": round(value, 2), "unit": "steps/s", "n_gpus": world,
-            "steps": K, "warmup": W, "ms_per_step": round(ms / K, 6), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {
-                "workload": label, "rows_per_gpu": rows, "cols": cols,
-                "bytes_per_step_per_gpu": per_step,
-                "tape": {"calls": st["calls"], "kernels": st["groups"], "folds": st["folds"],
-                         "eager_steps": st["eager_steps"]},
-                "l2": f"inputs larger than L2 (x {rows * cols * 4 / 1e6:.0f} MB, dx written {rows * cols * 4 / 1e6:.0f} MB)",
-                "parallelism": "replica" if world == 1 else f"data-parallel x{world}: rows per rank, [dg, loss] all-reduced over NVLink peer memory (rank-ordered sum)",
-                "timing": "CUDA graph of K tape replays, CUDA events, max over ranks",
-            },
-            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
-                         "unit": "GB/s", "frac": round(achieved / peak, 4),
-                         "traffic": profiled_traffic(args.config),
-                         "peak_source": f"{peak_kind} MEASURED_PEAKS.json hbm_gbs" if peak_kind == "measured" else "fallback 6.65 TB/s",
-                         "kernel": "j4b_group0 + j4b_group0_fold (the whole step)",
-                         "kernel_avg_us": round(step_us, 3)},
-            "cpu_baseline": cpu,
-            "e2e": {"value": round(e2e_value, 3), "unit": "steps/s",
-                    "h2d_bytes_per_step": (rows * cols + cols) * 4, "d2h_bytes_per_step": 4},
-            "gpu_launches": K * launches,
-            "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"],
-                       "reasons": clk["reasons"], "samples": clk["samples"]},
-        }
-        print(json.dumps(line), flush=True)
-    del main, warm
-    if world > 1:
-        if peers is not None:
-            status = peers.status()
-            peers.close()
-            if status and rank == 0:
-                print("peer collective wait gave up", file=sys.stderr)
-        dist.barrier()
-        dist.destroy_process_group()
+
+def engine_line(entry, world, secondary=None):
+    """The contract's JSON line from a primary result entry (+ the secondary workloads)."""
+    line = {"metric": METRIC, "value": entry["value"], "unit": entry["unit"], "n_gpus": world,
+            "steps": entry["steps"], "warmup": entry["warmup"], "ms_per_step": entry["ms_per_step"],
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": entry["config"], "method": entry["method"],
+            "roofline": entry["roofline"], "cpu_baseline": entry["cpu_baseline"], "e2e": entry["e2e"],
+            "gpu_launches": entry["gpu_launches"] + sum(s["gpu_launches"] for s in secondary or []),
+            "clocks": entry["clocks"]}
+    if secondary is not None:
+        line["secondary"] = secondary
+    return line
+
+
+def run_engine_workloads(args):
+    """GEMV and RMSNorm+SwiGLU tape workloads. The default run measures BASELINE configs[1]
+    (q8_0_b8) as the line's value and the other headline workloads as `secondary` entries."""
+    ctx = EngineCtx()
+    names = [args.config] + (list(SECONDARY) if args.config == DEFAULT_CONFIG and not args.primary_only else [])
+    entries = []
+    for i, name in enumerate(names):
+        budget = 0.0 if args.no_cpu_baseline else (10.0 if i == 0 else 6.0)
+        if name in TAPE_CONFIGS:
+            entries.append(measure_tape(ctx, name, args.steps, max(3, args.warmup), budget))
+        else:
+            entries.append(measure_gemv(ctx, name, args.steps, max(3, args.warmup), budget))
+    if ctx.rank == 0:
+        print(json.dumps(engine_line(entries[0], ctx.world, entries[1:] if len(entries) > 1 else None)), flush=True)
+    ctx.close()
     return 0
 
 
@@ -1568,184 +1783,7 @@ def run_engine(args):
         return run_engine_tape(args)
     if args.config in GEMM_CONFIGS:
         return run_engine_gemm(args)
-    import numpy as np
-    import torch
-    import torch.distributed as dist
-    sys.path.insert(0, HERE)
-    from jax4j_b200 import _lib
-    from jax4j_b200.backend import B200Backend, torch_stream
-    from jax4j_b200.prng import PrngKey
-
-    world, rank, local = dist_env()
-    torch.cuda.set_device(local)
-    if world > 1:
-        import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
-    be = B200Backend(local)
-    qtype, rows, cols, batch, label = CONFIGS[args.config]
-    per_call = alg_bytes(qtype, rows, cols, batch)
-    dev = torch.device("cuda", local)
-
-    # ---- synthetic inputs, generated on the device by the engine ----
-    kx, kw = PrngKey.of(0).split(2)
-    x = be.random_normal(kx.seed, kx.counter, (batch, cols))
-    w32 = be.random_normal(kw.seed, kw.counter + rank * rows * cols, (rows, cols))
-    w32 = be.scalar("MUL", w32, 0.02)
-    blob = be.quantize(w32, qtype)
-    l2 = torch.cuda.get_device_properties(dev).L2_cache_size
-    copies = max(2, math.ceil(2 * l2 / blob.numel()))
-    weights = [be.upload_quantized(blob, qtype, (rows, cols)) for _ in range(copies)]
-    del w32, blob
-    y = torch.empty(batch * rows, dtype=torch.float32, device=dev)
-    y_all = torch.empty(world * batch * rows, dtype=torch.float32, device=dev) if world > 1 else None
-    peers = None
-    if world > 1:
-        from jax4j_b200.peers import PeerGroup
-        peers = PeerGroup(local, rank, world)
-    torch.cuda.synchronize()
-
-    def gemv(i, stream):
-        _lib.call("j4b_quant_matvec", ctypes.c_void_p(weights[i % copies].handle), x.ptr, 0,
-                  y.data_ptr(), batch, stream)
-
-    def step(i, with_collective=True):
-        s = torch_stream()
-        if world > 1 and with_collective:
-            # the GEMV's epilogue stores into every rank's buffer over NVLink (no NCCL call)
-            peers.allgather_matvec(weights[i % copies], x.ptr, y_all.data_ptr(), batch, s)
-        else:
-            gemv(i, s)
-
-    def capture(n, with_collective=True):
-        g = torch.cuda.CUDAGraph()
-        side = torch.cuda.Stream()
-        side.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(side):
-            step(0, with_collective)  # warm the path on the capture stream
-        torch.cuda.current_stream().wait_stream(side)
-        torch.cuda.synchronize()
-        with torch.cuda.graph(g):
-            for i in range(n):
-                step(i, with_collective)
-        return g
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-
-    def timed(g, n_rep=1):
-        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        barrier()
-        start.record()
-        for _ in range(n_rep):
-            g.replay()
-        end.record()
-        barrier()
-        ms = start.elapsed_time(end)
-        if world > 1:
-            t = torch.tensor([ms], device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms = float(t.item())
-        return ms
-
-    K, W = args.steps, max(3, args.warmup)
-    warm = capture(W)
-    main = capture(K)
-    kernel_only = capture(K, with_collective=False) if world > 1 else main
-    # the first replay of a graph also uploads it: keep that out of the timed one
-    main.replay()
-    if world > 1:
-        kernel_only.replay()
-    torch.cuda.synchronize()
-    # soak ~0.5 s so clocks are at their loaded state, then time K steps while sampling clocks
-    warm.replay()
-    torch.cuda.synchronize()
-    soak_t0 = time.perf_counter()
-    with ClockSampler(local) as clocks:
-        while time.perf_counter() - soak_t0 < 0.5:
-            warm.replay()
-            torch.cuda.synchronize()
-        ms = timed(main)
-        kernel_ms = timed(kernel_only) if world > 1 else ms
-        # keep sampling for a short tail so short timed regions still get samples
-        tail = time.perf_counter()
-        while time.perf_counter() - tail < 0.3:
-            main.replay()
-            torch.cuda.synchronize()
-    clk = clocks.summary()
-
-    value = world * per_call * K / (ms * 1e-3) / 1e9
-    kernel_avg_us = kernel_ms * 1e3 / K
-    achieved = per_call / (kernel_avg_us * 1e-6) / 1e9
-    peak, peak_kind = measured_peaks()
-
-    # ---- end to end through the public API, host buffers, copies inside the timed region ----
-    x_host = torch.from_numpy(np.ascontiguousarray(be.download(x))).pin_memory()
-    y_host = torch.empty(batch * rows, dtype=torch.float32).pin_memory()
-    e2e_steps = min(K, 2000)
-    xin = be.full(0.0, (batch, cols))
-    stream = torch_stream()
-    barrier()
-    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e_start.record()
-    for i in range(e2e_steps):
-        _lib.call("j4b_h2d", xin.ptr, ctypes.c_void_p(x_host.data_ptr()), x_host.numel() * 4, stream)
-        out = be.quant_matvec(weights[i % copies], xin)
-        _lib.call("j4b_d2h", ctypes.c_void_p(y_host.data_ptr()), out.ptr, y_host.numel() * 4, stream)
-    e_end.record()
-    barrier()
-    e_ms = e_start.elapsed_time(e_end)
-    if world > 1:
-        t = torch.tensor([e_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e_ms = float(t.item())
-    e2e_value = world * per_call * e2e_steps / (e_ms * 1e-3) / 1e9
-
-    # ---- CPU baseline (rank 0, N = 1 only) ----
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        rate, sample, _ = cpu_matvec_rate(qtype, rows, cols, batch, 1, 10.0)
-        cpu = {"value": round(rate, 4), "unit": "GB/s", "cores": 1, "kind": "port",
-               "sample": sample + f" (host has {os.cpu_count()} cores)"}
-
-    if rank == 0:
-        line = {
-            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
-            "steps": K, "warmup": W, "ms_per_step": round(ms / K, 6), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {
-                "workload": label, "quant": TYPE_NAME[qtype], "batch": batch,
-                "rows_per_gpu": rows, "cols": cols, "bytes_per_step_per_gpu": per_call,
-                "compute": "quant codes -> exact fp16 mma.sync operands, x split fp16 hi+lo, fp32 accumulate",
-                "l2": f"weights rotate over {copies} copies ({copies * per_call / 1e6:.0f} MB > 2x L2)",
-                "parallelism": "replica" if world == 1 else f"row-shard x{world}, all-gather fused into the GEMV epilogue (NVLink peer stores)",
-                "timing": "CUDA graph of K GEMV calls, CUDA events, max over ranks",
-            },
-            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
-                         "unit": "GB/s", "frac": round(achieved / peak, 4),
-                         "traffic": profiled_traffic(args.config),
-                         "peak_source": f"{peak_kind} MEASURED_PEAKS.json hbm_gbs" if peak_kind == "measured" else "fallback 6.65 TB/s",
-                         "kernel": "qgemv_kernel", "kernel_avg_us": round(kernel_avg_us, 3)},
-            "cpu_baseline": cpu,
-            "e2e": {"value": round(e2e_value, 3), "unit": "GB/s",
-                    "h2d_bytes_per_step": batch * cols * 4, "d2h_bytes_per_step": batch * rows * 4},
-            "gpu_launches": K,
-            "clocks": {"sm_mhz": clk["sm_mhz"], "sm_max_mhz": clk["sm_max_mhz"],
-                       "reasons": clk["reasons"], "samples": clk["samples"]},
-        }
-        print(json.dumps(line), flush=True)
-    del main, warm, kernel_only
-    if world > 1:
-        if peers is not None:
-            status = peers.status()
-            peers.close()
-            if status and rank == 0:
-                print("peer collective wait gave up", file=sys.stderr)
-        dist.barrier()
-        dist.destroy_process_group()
-    return 0
+    return run_engine_workloads(args)
 
 
 def main():
@@ -1755,8 +1793,10 @@ def main():
     p.add_argument("--warmup", type=int, default=None, help="warm-up steps (default per workload)")
     p.add_argument("--impl", choices=["engine", "reference"], default="engine")
     p.add_argument("--config", choices=sorted(CONFIGS) + sorted(TAPE_CONFIGS) + sorted(GEMM_CONFIGS)
-                   + sorted(DECODER_CONFIGS) + sorted(AAD_CONFIGS) + sorted(CONV_CONFIGS), default="q8_0_b8")
+                   + sorted(DECODER_CONFIGS) + sorted(AAD_CONFIGS) + sorted(CONV_CONFIGS), default=DEFAULT_CONFIG)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--primary-only", action="store_true",
+                   help="default config: measure q8_0_b8 alone, without the secondary workloads")
     p.add_argument("--batch", type=int, default=None,
                    help="decoder workloads only: override the batch (e.g. a smaller case for profiling)")
     args = p.parse_args()
