@@ -972,7 +972,7 @@ cudaError_t gemv_dispatch(const j4b_qweight* w, const float* x, const float* add
                           unsigned* grid_out = nullptr) {
   static const char* variant = getenv("J4B_QGEMV_VARIANT");  // development A/B only
   static const bool legacy = variant && variant[0] == 'l';
-  static const bool wide = variant && variant[0] == 'w';
+  static const bool wide = !(variant && variant[0] == 's');
   const bool pdl = !w->fresh;
   const_cast<j4b_qweight*>(w)->fresh = false;
   if (!legacy && batch <= 4)

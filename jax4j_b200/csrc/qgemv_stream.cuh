@@ -79,6 +79,15 @@ __device__ __forceinline__ bool wait_issued(const volatile int* seq, int st) {
   return true;
 }
 
+// Counts one arrival at a split-K counter with acquire-release semantics at GPU scope: the
+// arriving warp's partial stores (ordered before it by __syncwarp) are released with it, and the
+// last arrival acquires every other split's partials; one atomic in place of fence + atomic.
+__device__ __forceinline__ unsigned arrive_acq_rel(unsigned* ctr) {
+  unsigned old;
+  asm volatile("atom.add.acq_rel.gpu.u32 %0, [%1], 1;" : "=r"(old) : "l"(ctr) : "memory");
+  return old;
+}
+
 // Warp `c` converts x's columns [kc0 + 128c, kc0 + 128c + 128) of every batch row into the
 // chunk's fragment block (columns past K and rows past the batch are zeros).
 template <int QT, bool PK>
@@ -331,13 +340,12 @@ __global__ void __launch_bounds__(stream_threads<NW>(), NW == 8 ? 2 : 1) qgemv_s
         float* part = a.partials + ((int64_t)split * a.rt + tile) * 256;
 #pragma unroll
         for (int i = 0; i < kNV; i++) __stcg(part + i * 32 + lane, acc[i]);
-        __threadfence();
-        __syncwarp();
+        __syncwarp();  // every lane's partial store precedes lane 0's release
         unsigned last = 0;
-        if (lane == 0) last = atomicAdd(a.arrivals + tile, 1u) == (unsigned)(a.ksplit - 1);
+        if (lane == 0) last = arrive_acq_rel(a.arrivals + tile) == (unsigned)(a.ksplit - 1);
         last = __shfl_sync(0xffffffffu, last, 0);
         if (!last) continue;
-        __threadfence();
+        __syncwarp();  // lane 0's acquire precedes every lane's loads of the other partials
         // the last arrival adds the splits in split order, four splits' loads in flight at once
         const float* p0 = a.partials + tile * 256 + lane;
         const int64_t sstride = a.rt * 256;
