@@ -1,0 +1,329 @@
+// Prefill projection y [m, rows] = x [m, cols] . W^T with W's block dequantisation fused into the
+// tcgen05 pipeline (included by quant.cu inside namespace j4b::<anonymous>, after Layout).
+//
+// The quantised weight never exists as a bf16 matrix in HBM: decode warps turn its repacked
+// fragment-layout bytes (plus the per-row block scales) into the 128-byte-swizzled bf16 operand
+// tile in shared memory, k-block by k-block, right before the tensor cores read it. W is the
+// MMA's M = 128 operand and the activations its N operand (256 tokens in bf16 mode), so every
+// decoded weight element feeds 2 x 256 FLOPs; the tile's accumulator D[w row][token] lives in
+// TMEM and the epilogue writes it transposed, y[token][w row], with warp-coalesced stores.
+//
+// Warps of one CTA (one 128 x BN output tile):
+//   warp 0     one thread streams the x tile's 64-wide K slices with 2-D TMA loads;
+//   warp 1     allocates the TMEM accumulator; one thread issues tcgen05.mma per 16-wide K step and
+//              releases each stage with tcgen05.commit;
+//   warps 2-5  epilogue: tcgen05.ld of TMEM lanes 32 (w % 4) .. + 31 (= W rows), 8 tokens at a
+//              time, stores to y;
+//   warps 6-9  decoders: warp d decodes row tiles 2d, 2d + 1 (16 W rows each) of every k-block,
+//              loading the next k-block's bytes before writing the current one; each writes its
+//              part of the stage, fences the generic-proxy writes for the async proxy the tensor
+//              core reads through, and arrives on the stage's `full_a` barrier.
+// Values are those of the bit-exact gather (__fmul_rn(d, code) and the Q4_K d*sc*q - dmin*m in
+// float), rounded to bf16 (mode 1) or split into bf16 hi + lo (fp32-accurate mode: the product is
+// hi.hi + hi.lo + lo.hi, with x split the same way). Every mbarrier wait is bounded; a wait that
+// gives up records an error in the weight's status word.
+
+constexpr int kQgBM = 128, kQgBK = 64;
+constexpr int kQgThreads = 10 * 32;
+
+template <int TERMS>
+constexpr int qg_bn() { return TERMS == 1 ? 256 : 128; }
+template <int TERMS>
+constexpr int qg_stages() { return TERMS == 1 ? 2 : 3; }
+constexpr uint32_t kQgABytes = kQgBM * kQgBK * 2;  // one 128 x 64 bf16 tile
+template <int TERMS>
+constexpr uint32_t qg_b_bytes() { return (uint32_t)qg_bn<TERMS>() * kQgBK * 2; }
+// stage: A hi | B hi | (A lo | B lo)
+template <int TERMS>
+constexpr uint32_t qg_stage_bytes() { return (TERMS == 3 ? 2u : 1u) * (kQgABytes + qg_b_bytes<TERMS>()); }
+
+struct QgArgs {
+  const uint8_t* data;
+  Layout L;
+  int64_t rows, cols;
+  int m, kp;
+  float* y;
+  int* status;
+};
+
+// One lane's bytes of one 16-row tile for one 64-column k-block (two 32-column groups).
+struct QgBytes {
+  uint4 q0, q1;  // quants: Q8_0 one line per group; 4-bit formats q0 only (words: g0 ks0, g0 ks1, g1 ks0, g1 ks1)
+  uint4 s0, s1;  // scales: Q8_0/Q4_0 s0.x / s0.y = (d row g | d row g+8) of the two groups; Q4_K the
+                 // 16 GGUF header bytes of rows g (s0) and g + 8 (s1)
+};
+
+template <int QT>
+__device__ __forceinline__ void qg_load(const QgArgs& a, int64_t tile, int kb, int lane, QgBytes& b) {
+  const int g = lane >> 2;
+  const int64_t G = 2 * (int64_t)kb;
+  const int64_t s = G / 32;
+  const int gl = (int)(G % 32);
+  if (tile >= a.L.rt) {
+    b.q0 = b.q1 = b.s0 = b.s1 = make_uint4(0, 0, 0, 0);
+    return;
+  }
+  const uint8_t* base = a.data + a.L.chunk_offset(s, tile);
+  const int64_t meta = (int64_t)a.L.groups_in_split(s) * GemvTraits<QT>::kQ;
+  if constexpr (QT == J4B_Q8_0) {
+    b.q0 = __ldg(reinterpret_cast<const uint4*>(base + gl * 512 + lane * 16));
+    b.q1 = __ldg(reinterpret_cast<const uint4*>(base + (gl + 1) * 512 + lane * 16));
+    b.s0.x = __ldg(reinterpret_cast<const uint32_t*>(base + meta + gl * 32 + g * 4));
+    b.s0.y = __ldg(reinterpret_cast<const uint32_t*>(base + meta + (gl + 1) * 32 + g * 4));
+  } else if constexpr (QT == J4B_Q4_0) {
+    b.q0 = __ldg(reinterpret_cast<const uint4*>(base + (gl / 2) * 512 + lane * 16));
+    b.s0.x = __ldg(reinterpret_cast<const uint32_t*>(base + meta + gl * 32 + g * 4));
+    b.s0.y = __ldg(reinterpret_cast<const uint32_t*>(base + meta + (gl + 1) * 32 + g * 4));
+  } else {  // Q4_K
+    b.q0 = __ldg(reinterpret_cast<const uint4*>(base + (gl / 4) * 1024 + lane * 32 + (gl % 4) * 8));
+    const uint8_t* mp = base + meta + (gl / 8) * 256 + (g * 2) * 16;
+    b.s0 = __ldg(reinterpret_cast<const uint4*>(mp));
+    b.s1 = __ldg(reinterpret_cast<const uint4*>(mp + 16));
+  }
+}
+
+// Q4_K: d * sc_j and dmin * m_j of sub-block j from a row's 16 header bytes (the GGUF 6-bit pairs).
+__device__ __forceinline__ void q4k_row_scales(const uint4& h, int j, float& d1, float& m1) {
+  const float d = __half2float(__ushort_as_half((uint16_t)(h.x & 0xFFFF)));
+  const float dmin = __half2float(__ushort_as_half((uint16_t)(h.x >> 16)));
+  int sc, mn;
+  if (j < 4) {
+    sc = (h.y >> (8 * j)) & 63;
+    mn = (h.z >> (8 * j)) & 63;
+  } else {
+    const int jj = j - 4;
+    const uint32_t qj4 = (h.w >> (8 * jj)) & 0xFF;
+    sc = (qj4 & 0xF) | (((h.y >> (8 * jj + 6)) & 3) << 4);
+    mn = (qj4 >> 4) | (((h.z >> (8 * jj + 6)) & 3) << 4);
+  }
+  d1 = __fmul_rn(d, (float)sc);
+  m1 = __fmul_rn(dmin, (float)mn);
+}
+
+__device__ __forceinline__ uint32_t bf16x2_bits(__nv_bfloat162 v) { return *reinterpret_cast<uint32_t*>(&v); }
+
+// Writes one lane's 32 decoded elements of one 16-row tile (tile rows from r0 in the A operand).
+template <int QT, int TERMS>
+__device__ __forceinline__ void qg_store(const QgBytes& b, int kb, int lane, uint8_t* a_hi, uint8_t* a_lo, int r0) {
+  const int g = lane >> 2, t = lane & 3;
+  float d[2][2], m[2][2];  // [group][row g / g + 8]
+  if constexpr (QT == J4B_Q4_K) {
+    const int j0 = (2 * kb) % 8;
+#pragma unroll
+    for (int gg = 0; gg < 2; gg++) {
+      q4k_row_scales(b.s0, j0 + gg, d[gg][0], m[gg][0]);
+      q4k_row_scales(b.s1, j0 + gg, d[gg][1], m[gg][1]);
+    }
+  } else {
+#pragma unroll
+    for (int gg = 0; gg < 2; gg++) {
+      const uint32_t w = gg ? b.s0.y : b.s0.x;
+      d[gg][0] = __half2float(__ushort_as_half((uint16_t)(w & 0xFFFF)));
+      d[gg][1] = __half2float(__ushort_as_half((uint16_t)(w >> 16)));
+      m[gg][0] = m[gg][1] = 0.f;
+    }
+  }
+  const uint32_t q4[4] = {b.q0.x, b.q0.y, b.q0.z, b.q0.w};
+  const uint32_t q8[2][4] = {{b.q0.x, b.q0.y, b.q0.z, b.q0.w}, {b.q1.x, b.q1.y, b.q1.z, b.q1.w}};
+#pragma unroll
+  for (int gg = 0; gg < 2; gg++)
+#pragma unroll
+    for (int ks = 0; ks < 2; ks++)
+#pragma unroll
+      for (int i = 0; i < 4; i++) {  // element pair (2i, 2i + 1) of the k-step's A fragment
+        const int which = i & 1;
+        int c0, c1;
+        if constexpr (QT == J4B_Q8_0) {
+          const uint32_t w = q8[gg][2 * ks + (i >> 1)];
+          const int sh = 16 * (i & 1);
+          c0 = (int)(int8_t)(((w >> sh) & 0xFF) ^ 0x80);
+          c1 = (int)(int8_t)(((w >> (sh + 8)) & 0xFF) ^ 0x80);
+        } else {
+          const uint32_t w = rotr(q4[2 * gg + ks], 4 * i);
+          c0 = (int)((w >> 6) & 15);
+          c1 = (int)((w >> 22) & 15);
+        }
+        float v0, v1;
+        if constexpr (QT == J4B_Q4_K) {
+          v0 = __fsub_rn(__fmul_rn(d[gg][which], (float)c0), m[gg][which]);
+          v1 = __fsub_rn(__fmul_rn(d[gg][which], (float)c1), m[gg][which]);
+        } else if constexpr (QT == J4B_Q4_0) {
+          v0 = __fmul_rn(d[gg][which], (float)(c0 - 8));
+          v1 = __fmul_rn(d[gg][which], (float)(c1 - 8));
+        } else {
+          v0 = __fmul_rn(d[gg][which], (float)c0);
+          v1 = __fmul_rn(d[gg][which], (float)c1);
+        }
+        const int row = r0 + g + 8 * which;
+        const int col = 32 * gg + 16 * ks + 2 * t + 8 * (i >> 1);
+        const uint32_t off = sw128_offset(row, col);
+        const __nv_bfloat162 h = __floats2bfloat162_rn(v0, v1);
+        *reinterpret_cast<uint32_t*>(a_hi + off) = bf16x2_bits(h);
+        if constexpr (TERMS == 3) {
+          const float2 hf = __bfloat1622float2(h);
+          *reinterpret_cast<uint32_t*>(a_lo + off) = bf16x2_bits(__floats2bfloat162_rn(v0 - hf.x, v1 - hf.y));
+        }
+      }
+}
+
+template <int QT, int TERMS>
+__global__ void __launch_bounds__(kQgThreads, TERMS == 1 ? 2 : 1)
+    qgemm_fused_kernel(const __grid_constant__ CUtensorMap x_hi, const __grid_constant__ CUtensorMap x_lo, QgArgs p) {
+  constexpr int kBN = qg_bn<TERMS>();
+  constexpr int kStages = qg_stages<TERMS>();
+  constexpr uint32_t kStage = qg_stage_bytes<TERMS>();
+  constexpr uint32_t kB = qg_b_bytes<TERMS>();
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full_a = reinterpret_cast<uint64_t*>(smem + kStages * kStage);
+  uint64_t* full_b = full_a + kStages;
+  uint64_t* empty = full_b + kStages;
+  uint64_t* acc_full = empty + kStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_tiles = (int)((p.rows + kQgBM - 1) / kQgBM);
+  const int n_tile = (int)(blockIdx.x % n_tiles), t_tile = (int)(blockIdx.x / n_tiles);
+  const int64_t w0 = (int64_t)n_tile * kQgBM;
+  const int tok0 = t_tile * kBN;
+  const int nk = p.kp / kQgBK;
+  auto stage_a = [&](int s, int lo) { return smem + s * kStage + (lo ? kQgABytes + kB : 0); };
+  auto stage_b = [&](int s, int lo) { return smem + s * kStage + kQgABytes + (lo ? kQgABytes + kB : 0); };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      bar_init(&full_a[s], 4);
+      bar_init(&full_b[s], 1);
+      bar_init(&empty[s], 1);
+    }
+    bar_init(acc_full, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(tmem_slot)),
+                 "r"(kBN));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  bool ok = true;
+
+  if (warp == 0) {
+    if (lane == 0) {  // x tiles
+      for (int kb = 0; kb < nk; ++kb) {
+        const int s = kb % kStages, use = kb / kStages;
+        if (use > 0 && !bar_wait(&empty[s], (uint32_t)((use - 1) & 1))) ok = false;
+        bar_expect_tx(&full_b[s], (TERMS == 3 ? 2u : 1u) * kB);
+        tma_tile(stage_b(s, 0), &x_hi, kb * kQgBK, tok0, &full_b[s]);
+        if (TERMS == 3) tma_tile(stage_b(s, 1), &x_lo, kb * kQgBK, tok0, &full_b[s]);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // MMA issue
+      constexpr uint32_t idesc = idesc_bf16(kQgBM, kBN);
+      for (int kb = 0; kb < nk; ++kb) {
+        const int s = kb % kStages, par = (kb / kStages) & 1;
+        if (!bar_wait(&full_a[s], (uint32_t)par)) ok = false;
+        if (!bar_wait(&full_b[s], (uint32_t)par)) ok = false;
+        tc_fence_after();
+        const uint32_t ah = saddr(stage_a(s, 0)), bh = saddr(stage_b(s, 0));
+        const uint32_t al = saddr(stage_a(s, 1)), bl = saddr(stage_b(s, 1));
+#pragma unroll
+        for (int k = 0; k < kQgBK / 16; ++k) {  // 16 bf16 = 32 bytes along the swizzled row
+          const uint64_t dah = kmajor_sw128(ah + k * 32), dbh = kmajor_sw128(bh + k * 32);
+          umma_bf16(tmem, dah, dbh, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          if (TERMS == 3) {
+            umma_bf16(tmem, dah, kmajor_sw128(bl + k * 32), idesc, 1u);
+            umma_bf16(tmem, kmajor_sw128(al + k * 32), dbh, idesc, 1u);
+          }
+        }
+        umma_commit(&empty[s]);  // the stage is free once these MMAs have read it
+      }
+      umma_commit(acc_full);
+    }
+  } else if (warp < 6) {
+    // epilogue: TMEM lane = W row (warp w reads lanes 32 (w % 4) .. + 31), column = token
+    const int quarter = warp & 3;
+    const int64_t row = w0 + quarter * 32 + lane;
+    if (!bar_wait(acc_full, 0)) ok = false;
+    tc_fence_after();
+    const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16);
+#pragma unroll 1
+    for (int c = 0; c < kBN; c += 8) {
+      uint32_t v[8];
+      asm volatile(
+          "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];\n"
+          : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+          : "r"(taddr + (uint32_t)c));
+      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+      if (row < p.rows) {
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int tok = tok0 + c + u;
+          if (tok < p.m) p.y[(int64_t)tok * p.rows + row] = __uint_as_float(v[u]);
+        }
+      }
+    }
+  } else {
+    // decoders: warp d owns row tiles 2d, 2d + 1 of the 128-row A tile
+    const int d = warp - 6;
+    const int64_t tile0 = w0 / 16 + 2 * d;
+    QgBytes cur[2], nxt[2];
+    qg_load<QT>(p, tile0, 0, lane, cur[0]);
+    qg_load<QT>(p, tile0 + 1, 0, lane, cur[1]);
+    for (int kb = 0; kb < nk; ++kb) {
+      const int s = kb % kStages, use = kb / kStages;
+      if (kb + 1 < nk) {
+        qg_load<QT>(p, tile0, kb + 1, lane, nxt[0]);
+        qg_load<QT>(p, tile0 + 1, kb + 1, lane, nxt[1]);
+      }
+      if (use > 0 && !bar_wait(&empty[s], (uint32_t)((use - 1) & 1))) ok = false;
+      uint8_t* ahi = stage_a(s, 0);
+      uint8_t* alo = stage_a(s, 1);
+      qg_store<QT, TERMS>(cur[0], kb, lane, ahi, alo, 32 * d);
+      qg_store<QT, TERMS>(cur[1], kb, lane, ahi, alo, 32 * d + 16);
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor-core reads
+      __syncwarp();
+      if (lane == 0) bar_arrive(&full_a[s]);
+      cur[0] = nxt[0];
+      cur[1] = nxt[1];
+    }
+  }
+  if (!ok) atomicExch(p.status, 1);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kBN));
+  }
+}
+
+template <int QT, int TERMS>
+cudaError_t launch_qgemm_fused(const j4b_qweight* w, const CUtensorMap& xh, const CUtensorMap& xl, int m, int kp,
+                               float* y, cudaStream_t stream) {
+  constexpr int kBN = qg_bn<TERMS>();
+  const size_t smem = (size_t)qg_stages<TERMS>() * qg_stage_bytes<TERMS>() + 1024 + 256;
+  static bool attr_set[kMaxDevices] = {};
+  if (w->dev < 0 || w->dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  if (!attr_set[w->dev]) {
+    cudaError_t e = cudaFuncSetAttribute(qgemm_fused_kernel<QT, TERMS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    attr_set[w->dev] = true;
+  }
+  QgArgs p;
+  p.data = w->data;
+  p.L = layout_of(w);
+  p.rows = w->rows;
+  p.cols = w->cols;
+  p.m = m;
+  p.kp = kp;
+  p.y = y;
+  p.status = w->status;
+  const int64_t tiles = ((w->rows + kQgBM - 1) / kQgBM) * (((int64_t)m + kBN - 1) / kBN);
+  if (tiles > 0x7fffffffLL) return cudaErrorInvalidValue;
+  qgemm_fused_kernel<QT, TERMS><<<(unsigned)tiles, kQgThreads, smem, stream>>>(xh, xl, p);
+  return cudaGetLastError();
+}

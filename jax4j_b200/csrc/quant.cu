@@ -37,6 +37,7 @@
 
 #include "j4b_internal.h"
 #include "j4b_wait.cuh"
+#include "tc_common.cuh"
 
 struct j4b_qweight {
   int dev;
@@ -461,6 +462,7 @@ Layout layout_of(const j4b_qweight* w) {
 }
 
 #include "qgemv.cuh"
+#include "qgemm_fused.cuh"
 
 // ---------------------------------------------------------------------------------------------
 // device encoder: byte-identical to the published block encoders the oracle restates
@@ -826,6 +828,44 @@ extern "C" int j4b_quant_gather_row(j4b_qweight_t w, int64_t row, j4b_buf out, j
 
 // Prefill projection: y[m, rows] = x[m, cols] . W^T on the tcgen05 tensor cores. The weight is
 // decoded (bit-exact) to bf16 K-major operands in stream-ordered scratch, then multiplied.
+namespace j4b {
+namespace {
+// x -> bf16 hi (and lo) [m, kp] in stream-ordered scratch, then the fused dequant-GEMM.
+int quant_gemm_fused(const j4b_qweight* w, const float* x, float* y, int64_t m, int64_t kp, int terms,
+                     cudaStream_t stream) {
+  const size_t xbytes = (size_t)(m * kp) * 2;
+  void* scratch = nullptr;
+  J4B_CUDA(cudaMallocAsync(&scratch, 2 * xbytes + 512, stream), "cudaMallocAsync(x operand)");
+  __nv_bfloat16* xh = (__nv_bfloat16*)scratch;
+  __nv_bfloat16* xl = terms == 3 ? (__nv_bfloat16*)((uint8_t*)scratch + ((xbytes + 255) & ~size_t(255))) : nullptr;
+  int rc = tc_split_rows(x, m, w->cols, w->cols, kp, xh, xl, stream);
+  CUtensorMap mh, ml;
+  if (rc == J4B_OK) {
+    const int bn = terms == 3 ? qg_bn<3>() : qg_bn<1>();
+    if (!make_map(&mh, xh, m, kp, bn) || (terms == 3 && !make_map(&ml, xl, m, kp, bn)))
+      rc = set_error(J4B_ECUDA, "cuTensorMapEncodeTiled failed for the prefill activations");
+    if (terms != 3) ml = mh;
+  }
+  if (rc == J4B_OK) {
+    cudaError_t e = cudaErrorInvalidValue;
+    const int mi = (int)m, kpi = (int)kp;
+    switch (w->type * 4 + terms) {
+      case J4B_Q8_0 * 4 + 1: e = launch_qgemm_fused<J4B_Q8_0, 1>(w, mh, ml, mi, kpi, y, stream); break;
+      case J4B_Q8_0 * 4 + 3: e = launch_qgemm_fused<J4B_Q8_0, 3>(w, mh, ml, mi, kpi, y, stream); break;
+      case J4B_Q4_0 * 4 + 1: e = launch_qgemm_fused<J4B_Q4_0, 1>(w, mh, ml, mi, kpi, y, stream); break;
+      case J4B_Q4_0 * 4 + 3: e = launch_qgemm_fused<J4B_Q4_0, 3>(w, mh, ml, mi, kpi, y, stream); break;
+      case J4B_Q4_K * 4 + 1: e = launch_qgemm_fused<J4B_Q4_K, 1>(w, mh, ml, mi, kpi, y, stream); break;
+      case J4B_Q4_K * 4 + 3: e = launch_qgemm_fused<J4B_Q4_K, 3>(w, mh, ml, mi, kpi, y, stream); break;
+    }
+    if (e != cudaSuccess) rc = cuda_error(e, "qgemm_fused_kernel");
+    else count_launch();
+  }
+  cudaFreeAsync(scratch, stream);
+  return rc;
+}
+}  // namespace
+}  // namespace j4b
+
 extern "C" int j4b_quant_gemm(j4b_qweight_t w, j4b_buf x, j4b_buf y, int64_t m, int precision,
                               j4b_stream s) {
   J4B_REQUIRE(w != nullptr, "null quantized matrix");
@@ -837,6 +877,10 @@ extern "C" int j4b_quant_gemm(j4b_qweight_t w, j4b_buf x, j4b_buf y, int64_t m, 
   cudaStream_t stream = resolve_stream(w->dev, s);
   const int terms = precision == 1 ? 1 : 3;
   const int64_t kp = (w->cols + 63) / 64 * 64;
+  static const bool two_pass = getenv("J4B_QGEMM_TWO_PASS") != nullptr;  // development A/B only
+  if (!two_pass && (w->type == J4B_Q8_0 || w->type == J4B_Q4_0 || w->type == J4B_Q4_K) && m <= INT32_MAX &&
+      w->rows <= INT32_MAX)
+    return quant_gemm_fused(w, (const float*)(uintptr_t)x, (float*)(uintptr_t)y, m, kp, terms, stream);
   const size_t bytes = (size_t)(w->rows * kp) * 2;
   void* scratch = nullptr;
   J4B_CUDA(cudaMallocAsync(&scratch, 2 * bytes + 512, stream), "cudaMallocAsync(dequantised weight)");
