@@ -157,6 +157,9 @@ struct GemvArgs {
   unsigned* peer_ctr[kMaxPeerRanks];  // at rank p: the counter of this rank as a source
   const unsigned* step;
   int64_t half_floats;
+  // streaming kernel only: with K splits, store the split partials and leave their sum to
+  // qgemv_fold_kernel (launched right after), so the CTAs exit as soon as their tiles are done
+  int defer_fold;
 };
 
 // Stores one output, locally or into every rank's gathered buffer.
@@ -886,6 +889,7 @@ cudaError_t launch_gemv(const j4b_qweight* w, const float* x, const float* add, 
   a.partials = w->partials;
   a.arrivals = w->arrivals;
   a.status = w->status;
+  a.defer_fold = 0;
   a.nranks = 1;
   a.rank = 0;
   a.step = nullptr;

@@ -340,6 +340,7 @@ __global__ void __launch_bounds__(stream_threads<NW>(), NW == 8 ? 2 : 1) qgemv_s
         float* part = a.partials + ((int64_t)split * a.rt + tile) * 256;
 #pragma unroll
         for (int i = 0; i < kNV; i++) __stcg(part + i * 32 + lane, acc[i]);
+        if (a.defer_fold) continue;
         __syncwarp();  // every lane's partial store precedes lane 0's release
         unsigned last = 0;
         if (lane == 0) last = arrive_acq_rel(a.arrivals + tile) == (unsigned)(a.ksplit - 1);
@@ -394,6 +395,39 @@ __global__ void __launch_bounds__(stream_threads<NW>(), NW == 8 ? 2 : 1) qgemv_s
   signal_peers(a);
 }
 
+// y[b, r] = sum over splits of the streaming kernel's partials, in split order (+ add). One thread
+// per output, rows fastest. Launched right behind the streaming kernel with programmatic
+// dependent launch: its CTAs (small, no shared memory) sit next to the GEMV's while it runs, and
+// it lets the next kernel in the stream launch at once, so the next GEMV's CTAs take each SM as
+// soon as this GEMV's CTA there exits and start streaming their weights during this fold.
+template <bool PK>
+__global__ void __launch_bounds__(256) qgemv_fold_kernel(const float* __restrict__ partials, const float* __restrict__ add,
+                                                         float* __restrict__ y, int64_t rows, int64_t rt, int ksplit,
+                                                         int batch) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)batch * rows) return;
+  const int bcol = (int)(i / rows);
+  const int64_t r = i % rows;
+  const int row = (int)(r & 15);
+  const float* p = partials + (r >> 4) * 256 + (PK ? out_index_pk(row, bcol) : out_index(row, bcol));
+  const int64_t stride = rt * 256;
+  float tot = 0.f;
+  int sp = 0;
+  for (; sp + 4 <= ksplit; sp += 4) {
+    const float v0 = __ldcg(p + sp * stride), v1 = __ldcg(p + (sp + 1) * stride);
+    const float v2 = __ldcg(p + (sp + 2) * stride), v3 = __ldcg(p + (sp + 3) * stride);
+    tot += v0;
+    tot += v1;
+    tot += v2;
+    tot += v3;
+  }
+  for (; sp < ksplit; sp++) tot += __ldcg(p + sp * stride);
+  if (add) tot += add[i];
+  y[i] = tot;
+}
+
 template <int QT, bool PK, int NW>
 cudaError_t launch_gemv_stream(const j4b_qweight* w, const float* x, const float* add, float* y, int batch,
                                int sms, cudaStream_t stream, const GemvPeers* peers, unsigned* grid_out,
@@ -446,5 +480,23 @@ cudaError_t launch_gemv_stream(const j4b_qweight* w, const float* x, const float
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
   if (grid_out) *grid_out = cfg.gridDim.x;
-  return cudaLaunchKernelEx(&cfg, qgemv_stream_kernel<QT, PK, NW>, a);
+  // the separate fold applies to the local GEMV (the all-gather path folds in the kernel, where
+  // its epilogue stores into the peers' buffers)
+  a.defer_fold = (w->ksplit > 1 && !peers) ? 1 : 0;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, qgemv_stream_kernel<QT, PK, NW>, a);
+  if (e != cudaSuccess || !a.defer_fold) return e;
+  count_launch();
+  const int64_t n = (int64_t)batch * w->rows;
+  cudaLaunchConfig_t fc = {};
+  fc.gridDim = dim3((unsigned)((n + 255) / 256));
+  fc.blockDim = dim3(256);
+  fc.dynamicSmemBytes = 0;
+  fc.stream = stream;
+  cudaLaunchAttribute fa[1];
+  fa[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  fa[0].val.programmaticStreamSerializationAllowed = 1;
+  fc.attrs = fa;
+  fc.numAttrs = 1;
+  return cudaLaunchKernelEx(&fc, qgemv_fold_kernel<PK>, (const float*)w->partials, add, y, (int64_t)w->rows,
+                            (int64_t)w->rt, (int)w->ksplit, batch);
 }
