@@ -846,6 +846,10 @@ def measure_gemv(ctx, name, K, W, cpu_budget):
         else:
             gemv(i)
 
+    from jax4j_b200 import diagnostics
+    before = diagnostics()["dispatches"]
+    step(0)  # one eager call: the engine's kernel launches per step
+    launches = diagnostics()["dispatches"] - before
     ms, clk = timed_graph(ctx, step, K, W)
     kernel_ms = timed_graph(ctx, gemv, K, W)[0] if world > 1 else ms
     value = world * per_call * K / (ms * 1e-3) / 1e9
@@ -896,7 +900,7 @@ def measure_gemv(ctx, name, K, W, cpu_budget):
                 "h2d_bytes_per_step": batch * cols * 4, "d2h_bytes_per_step": batch * rows * 4,
                 "host_issue_us_per_step": round(host_issue_s * 1e6 / e2e_steps, 2),
                 "device_us_per_step": round(e_ms * 1e3 / e2e_steps, 2)},
-        "gpu_launches": K,
+        "gpu_launches": K * launches,
         "clocks": clocks_entry(clk),
     }
 

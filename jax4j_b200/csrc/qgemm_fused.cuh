@@ -4,9 +4,10 @@
 // The quantised weight never exists as a bf16 matrix in HBM: decode warps turn its repacked
 // fragment-layout bytes (plus the per-row block scales) into the 128-byte-swizzled bf16 operand
 // tile in shared memory, k-block by k-block, right before the tensor cores read it. W is the
-// MMA's M = 128 operand and the activations its N operand (256 tokens in bf16 mode), so every
-// decoded weight element feeds 2 x 256 FLOPs; the tile's accumulator D[w row][token] lives in
-// TMEM and the epilogue writes it transposed, y[token][w row], with warp-coalesced stores.
+// MMA's M = 128 operand and the activations its N operand: for long inputs a CTA holds two
+// accumulators of 256 tokens (the whole TMEM), so every decoded weight element feeds 2 x 512
+// FLOPs; the tile's accumulator D[w row][token] lives in TMEM and the epilogue writes it
+// transposed, y[token][w row], with warp-coalesced stores.
 //
 // Warps of one CTA (one 128 x BN output tile):
 //   warp 0     one thread streams the x tile's 64-wide K slices with 2-D TMA loads;
@@ -18,24 +19,26 @@
 //              loading the next k-block's bytes before writing the current one; each writes its
 //              part of the stage, fences the generic-proxy writes for the async proxy the tensor
 //              core reads through, and arrives on the stage's `full_a` barrier.
-// Values are those of the bit-exact gather (__fmul_rn(d, code) and the Q4_K d*sc*q - dmin*m in
-// float), rounded to bf16 (mode 1) or split into bf16 hi + lo (fp32-accurate mode: the product is
+// Values are those of the bit-exact gather (d * code in float; the Q4_K d*sc*q - dmin*m with one
+// rounding instead of two), rounded to bf16 (mode 1) or split into bf16 hi + lo (fp32-accurate mode: the product is
 // hi.hi + hi.lo + lo.hi, with x split the same way). Every mbarrier wait is bounded; a wait that
 // gives up records an error in the weight's status word.
 
 constexpr int kQgBM = 128, kQgBK = 64;
 constexpr int kQgThreads = 10 * 32;
 
+// Tokens per MMA (N); NH accumulators of N columns each per CTA (NH = 2: 512 tokens in bf16 mode,
+// the whole TMEM, one CTA per SM; NH = 1: two CTAs per SM, for short token counts).
 template <int TERMS>
 constexpr int qg_bn() { return TERMS == 1 ? 256 : 128; }
-template <int TERMS>
-constexpr int qg_stages() { return TERMS == 1 ? 2 : 3; }
+template <int TERMS, int NH>
+constexpr int qg_stages() { return TERMS == 1 ? 2 : (NH == 1 ? 3 : 2); }
 constexpr uint32_t kQgABytes = kQgBM * kQgBK * 2;  // one 128 x 64 bf16 tile
-template <int TERMS>
-constexpr uint32_t qg_b_bytes() { return (uint32_t)qg_bn<TERMS>() * kQgBK * 2; }
-// stage: A hi | B hi | (A lo | B lo)
-template <int TERMS>
-constexpr uint32_t qg_stage_bytes() { return (TERMS == 3 ? 2u : 1u) * (kQgABytes + qg_b_bytes<TERMS>()); }
+template <int TERMS, int NH>
+constexpr uint32_t qg_b_bytes() { return (uint32_t)(NH * qg_bn<TERMS>()) * kQgBK * 2; }
+// stage: A hi | B hi | (A lo | B lo); a B part holds the NH token boxes one after the other
+template <int TERMS, int NH>
+constexpr uint32_t qg_stage_bytes() { return (TERMS == 3 ? 2u : 1u) * (kQgABytes + qg_b_bytes<TERMS, NH>()); }
 
 struct QgArgs {
   const uint8_t* data;
@@ -102,29 +105,48 @@ __device__ __forceinline__ void q4k_row_scales(const uint4& h, int j, float& d1,
 
 __device__ __forceinline__ uint32_t bf16x2_bits(__nv_bfloat162 v) { return *reinterpret_cast<uint32_t*>(&v); }
 
-// Writes one lane's 32 decoded elements of one 16-row tile (tile rows from r0 in the A operand).
+// Writes one lane's 32 decoded elements of one 16-row tile (tile rows from r0, a multiple of 16,
+// in the A operand). Codes become floats without conversions: a 4-bit code masked into the
+// mantissa of 2^23 (bits 6..9) is 2^23 + 64 q, so one subtraction gives 64 q exactly and one fma
+// with d / 64 (exact: a power-of-two scale) gives d q - offset rounded once; a Q8_0 byte placed
+// under 2^23's exponent gives 2^23 + (code + 128).
 template <int QT, int TERMS>
 __device__ __forceinline__ void qg_store(const QgBytes& b, int kb, int lane, uint8_t* a_hi, uint8_t* a_lo, int r0) {
   const int g = lane >> 2, t = lane & 3;
-  float d[2][2], m[2][2];  // [group][row g / g + 8]
-  if constexpr (QT == J4B_Q4_K) {
-    const int j0 = (2 * kb) % 8;
+  float mul[2][2], off[2][2];  // value = fma(code_term, mul, off) per [group][row g / g + 8]
 #pragma unroll
-    for (int gg = 0; gg < 2; gg++) {
-      q4k_row_scales(b.s0, j0 + gg, d[gg][0], m[gg][0]);
-      q4k_row_scales(b.s1, j0 + gg, d[gg][1], m[gg][1]);
-    }
-  } else {
-#pragma unroll
-    for (int gg = 0; gg < 2; gg++) {
+  for (int gg = 0; gg < 2; gg++) {
+    if constexpr (QT == J4B_Q4_K) {
+      const int j = (2 * kb) % 8 + gg;
+      float d1, m1;
+      q4k_row_scales(b.s0, j, d1, m1);
+      mul[gg][0] = d1 * (1.f / 64.f);
+      off[gg][0] = -m1;
+      q4k_row_scales(b.s1, j, d1, m1);
+      mul[gg][1] = d1 * (1.f / 64.f);
+      off[gg][1] = -m1;
+    } else {
       const uint32_t w = gg ? b.s0.y : b.s0.x;
-      d[gg][0] = __half2float(__ushort_as_half((uint16_t)(w & 0xFFFF)));
-      d[gg][1] = __half2float(__ushort_as_half((uint16_t)(w >> 16)));
-      m[gg][0] = m[gg][1] = 0.f;
+      const float d0 = __half2float(__ushort_as_half((uint16_t)(w & 0xFFFF)));
+      const float d8 = __half2float(__ushort_as_half((uint16_t)(w >> 16)));
+      if constexpr (QT == J4B_Q4_0) {
+        mul[gg][0] = d0 * (1.f / 64.f);
+        off[gg][0] = -8.f * d0;
+        mul[gg][1] = d8 * (1.f / 64.f);
+        off[gg][1] = -8.f * d8;
+      } else {
+        mul[gg][0] = d0;
+        mul[gg][1] = d8;
+        off[gg][0] = off[gg][1] = 0.f;
+      }
     }
   }
   const uint32_t q4[4] = {b.q0.x, b.q0.y, b.q0.z, b.q0.w};
   const uint32_t q8[2][4] = {{b.q0.x, b.q0.y, b.q0.z, b.q0.w}, {b.q1.x, b.q1.y, b.q1.z, b.q1.w}};
+  const float kMagic = 8388608.f;  // 2^23
+  // row r0 + g + 8 which: 1024-byte row group (r0 >> 3) + which, row g inside it; the 16-byte
+  // chunk index of column col is col >> 3, XORed with the row's g (the 128-byte swizzle)
+  const uint32_t row_base = (uint32_t)((r0 >> 3) * 1024 + g * 128 + 4 * t);
 #pragma unroll
   for (int gg = 0; gg < 2; gg++)
 #pragma unroll
@@ -132,47 +154,41 @@ __device__ __forceinline__ void qg_store(const QgBytes& b, int kb, int lane, uin
 #pragma unroll
       for (int i = 0; i < 4; i++) {  // element pair (2i, 2i + 1) of the k-step's A fragment
         const int which = i & 1;
-        int c0, c1;
+        float v0, v1;
         if constexpr (QT == J4B_Q8_0) {
           const uint32_t w = q8[gg][2 * ks + (i >> 1)];
-          const int sh = 16 * (i & 1);
-          c0 = (int)(int8_t)(((w >> sh) & 0xFF) ^ 0x80);
-          c1 = (int)(int8_t)(((w >> (sh + 8)) & 0xFF) ^ 0x80);
+          const int sh = 2 * (i & 1);  // byte index of the pair's first code
+          const float c0 = __int_as_float((int)__byte_perm(w, 0x4B000000u, 0x7650 + sh)) - (kMagic + 128.f);
+          const float c1 = __int_as_float((int)__byte_perm(w, 0x4B000000u, 0x7651 + sh)) - (kMagic + 128.f);
+          v0 = c0 * mul[gg][which];
+          v1 = c1 * mul[gg][which];
         } else {
-          const uint32_t w = rotr(q4[2 * gg + ks], 4 * i);
-          c0 = (int)((w >> 6) & 15);
-          c1 = (int)((w >> 22) & 15);
+          const uint32_t w = q4[2 * gg + ks];
+          const float c0 = __int_as_float((int)((rotr(w, 4 * i) & 0x3C0u) | 0x4B000000u)) - kMagic;        // 64 q
+          const float c1 = __int_as_float((int)((rotr(w, 4 * i + 16) & 0x3C0u) | 0x4B000000u)) - kMagic;   // 64 q
+          v0 = fmaf(c0, mul[gg][which], off[gg][which]);
+          v1 = fmaf(c1, mul[gg][which], off[gg][which]);
         }
-        float v0, v1;
-        if constexpr (QT == J4B_Q4_K) {
-          v0 = __fsub_rn(__fmul_rn(d[gg][which], (float)c0), m[gg][which]);
-          v1 = __fsub_rn(__fmul_rn(d[gg][which], (float)c1), m[gg][which]);
-        } else if constexpr (QT == J4B_Q4_0) {
-          v0 = __fmul_rn(d[gg][which], (float)(c0 - 8));
-          v1 = __fmul_rn(d[gg][which], (float)(c1 - 8));
-        } else {
-          v0 = __fmul_rn(d[gg][which], (float)c0);
-          v1 = __fmul_rn(d[gg][which], (float)c1);
-        }
-        const int row = r0 + g + 8 * which;
-        const int col = 32 * gg + 16 * ks + 2 * t + 8 * (i >> 1);
-        const uint32_t off = sw128_offset(row, col);
+        const int chunk = ((4 * gg + 2 * ks + (i >> 1)) ^ g) & 7;
+        const uint32_t o = row_base + which * 1024 + (chunk << 4);
         const __nv_bfloat162 h = __floats2bfloat162_rn(v0, v1);
-        *reinterpret_cast<uint32_t*>(a_hi + off) = bf16x2_bits(h);
+        *reinterpret_cast<uint32_t*>(a_hi + o) = bf16x2_bits(h);
         if constexpr (TERMS == 3) {
           const float2 hf = __bfloat1622float2(h);
-          *reinterpret_cast<uint32_t*>(a_lo + off) = bf16x2_bits(__floats2bfloat162_rn(v0 - hf.x, v1 - hf.y));
+          *reinterpret_cast<uint32_t*>(a_lo + o) = bf16x2_bits(__floats2bfloat162_rn(v0 - hf.x, v1 - hf.y));
         }
       }
 }
 
-template <int QT, int TERMS>
-__global__ void __launch_bounds__(kQgThreads, TERMS == 1 ? 2 : 1)
+template <int QT, int TERMS, int NH>
+__global__ void __launch_bounds__(kQgThreads, TERMS == 1 && NH == 1 ? 2 : 1)
     qgemm_fused_kernel(const __grid_constant__ CUtensorMap x_hi, const __grid_constant__ CUtensorMap x_lo, QgArgs p) {
-  constexpr int kBN = qg_bn<TERMS>();
-  constexpr int kStages = qg_stages<TERMS>();
-  constexpr uint32_t kStage = qg_stage_bytes<TERMS>();
-  constexpr uint32_t kB = qg_b_bytes<TERMS>();
+  constexpr int kN = qg_bn<TERMS>();   // tokens per MMA
+  constexpr int kBN = NH * kN;         // tokens per tile (TMEM columns)
+  constexpr int kStages = qg_stages<TERMS, NH>();
+  constexpr uint32_t kStage = qg_stage_bytes<TERMS, NH>();
+  constexpr uint32_t kB = qg_b_bytes<TERMS, NH>();
+  constexpr uint32_t kBox = (uint32_t)kN * kQgBK * 2;  // one token box
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full_a = reinterpret_cast<uint64_t*>(smem + kStages * kStage);
@@ -216,13 +232,16 @@ __global__ void __launch_bounds__(kQgThreads, TERMS == 1 ? 2 : 1)
         const int s = kb % kStages, use = kb / kStages;
         if (use > 0 && !bar_wait(&empty[s], (uint32_t)((use - 1) & 1))) ok = false;
         bar_expect_tx(&full_b[s], (TERMS == 3 ? 2u : 1u) * kB);
-        tma_tile(stage_b(s, 0), &x_hi, kb * kQgBK, tok0, &full_b[s]);
-        if (TERMS == 3) tma_tile(stage_b(s, 1), &x_lo, kb * kQgBK, tok0, &full_b[s]);
+#pragma unroll
+        for (int h = 0; h < NH; ++h) {
+          tma_tile(stage_b(s, 0) + h * kBox, &x_hi, kb * kQgBK, tok0 + h * kN, &full_b[s]);
+          if (TERMS == 3) tma_tile(stage_b(s, 1) + h * kBox, &x_lo, kb * kQgBK, tok0 + h * kN, &full_b[s]);
+        }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {  // MMA issue
-      constexpr uint32_t idesc = idesc_bf16(kQgBM, kBN);
+      constexpr uint32_t idesc = idesc_bf16(kQgBM, kN);
       for (int kb = 0; kb < nk; ++kb) {
         const int s = kb % kStages, par = (kb / kStages) & 1;
         if (!bar_wait(&full_a[s], (uint32_t)par)) ok = false;
@@ -232,11 +251,16 @@ __global__ void __launch_bounds__(kQgThreads, TERMS == 1 ? 2 : 1)
         const uint32_t al = saddr(stage_a(s, 1)), bl = saddr(stage_b(s, 1));
 #pragma unroll
         for (int k = 0; k < kQgBK / 16; ++k) {  // 16 bf16 = 32 bytes along the swizzled row
-          const uint64_t dah = kmajor_sw128(ah + k * 32), dbh = kmajor_sw128(bh + k * 32);
-          umma_bf16(tmem, dah, dbh, idesc, (kb > 0 || k > 0) ? 1u : 0u);
-          if (TERMS == 3) {
-            umma_bf16(tmem, dah, kmajor_sw128(bl + k * 32), idesc, 1u);
-            umma_bf16(tmem, kmajor_sw128(al + k * 32), dbh, idesc, 1u);
+          const uint64_t dah = kmajor_sw128(ah + k * 32);
+#pragma unroll
+          for (int h = 0; h < NH; ++h) {  // accumulator h: TMEM columns [h N, (h + 1) N)
+            const uint32_t acc = tmem + (uint32_t)(h * kN);
+            const uint64_t dbh = kmajor_sw128(bh + h * kBox + k * 32);
+            umma_bf16(acc, dah, dbh, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            if (TERMS == 3) {
+              umma_bf16(acc, dah, kmajor_sw128(bl + h * kBox + k * 32), idesc, 1u);
+              umma_bf16(acc, kmajor_sw128(al + k * 32), dbh, idesc, 1u);
+            }
           }
         }
         umma_commit(&empty[s]);  // the stage is free once these MMAs have read it
@@ -301,15 +325,15 @@ __global__ void __launch_bounds__(kQgThreads, TERMS == 1 ? 2 : 1)
   }
 }
 
-template <int QT, int TERMS>
+template <int QT, int TERMS, int NH>
 cudaError_t launch_qgemm_fused(const j4b_qweight* w, const CUtensorMap& xh, const CUtensorMap& xl, int m, int kp,
                                float* y, cudaStream_t stream) {
-  constexpr int kBN = qg_bn<TERMS>();
-  const size_t smem = (size_t)qg_stages<TERMS>() * qg_stage_bytes<TERMS>() + 1024 + 256;
+  constexpr int kBN = NH * qg_bn<TERMS>();
+  const size_t smem = (size_t)qg_stages<TERMS, NH>() * qg_stage_bytes<TERMS, NH>() + 1024 + 256;
   static bool attr_set[kMaxDevices] = {};
   if (w->dev < 0 || w->dev >= kMaxDevices) return cudaErrorInvalidDevice;
   if (!attr_set[w->dev]) {
-    cudaError_t e = cudaFuncSetAttribute(qgemm_fused_kernel<QT, TERMS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e = cudaFuncSetAttribute(qgemm_fused_kernel<QT, TERMS, NH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     attr_set[w->dev] = true;
   }
@@ -324,6 +348,6 @@ cudaError_t launch_qgemm_fused(const j4b_qweight* w, const CUtensorMap& xh, cons
   p.status = w->status;
   const int64_t tiles = ((w->rows + kQgBM - 1) / kQgBM) * (((int64_t)m + kBN - 1) / kBN);
   if (tiles > 0x7fffffffLL) return cudaErrorInvalidValue;
-  qgemm_fused_kernel<QT, TERMS><<<(unsigned)tiles, kQgThreads, smem, stream>>>(xh, xl, p);
+  qgemm_fused_kernel<QT, TERMS, NH><<<(unsigned)tiles, kQgThreads, smem, stream>>>(xh, xl, p);
   return cudaGetLastError();
 }

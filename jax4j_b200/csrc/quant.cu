@@ -849,13 +849,18 @@ int quant_gemm_fused(const j4b_qweight* w, const float* x, float* y, int64_t m, 
   if (rc == J4B_OK) {
     cudaError_t e = cudaErrorInvalidValue;
     const int mi = (int)m, kpi = (int)kp;
-    switch (w->type * 4 + terms) {
-      case J4B_Q8_0 * 4 + 1: e = launch_qgemm_fused<J4B_Q8_0, 1>(w, mh, ml, mi, kpi, y, stream); break;
-      case J4B_Q8_0 * 4 + 3: e = launch_qgemm_fused<J4B_Q8_0, 3>(w, mh, ml, mi, kpi, y, stream); break;
-      case J4B_Q4_0 * 4 + 1: e = launch_qgemm_fused<J4B_Q4_0, 1>(w, mh, ml, mi, kpi, y, stream); break;
-      case J4B_Q4_0 * 4 + 3: e = launch_qgemm_fused<J4B_Q4_0, 3>(w, mh, ml, mi, kpi, y, stream); break;
-      case J4B_Q4_K * 4 + 1: e = launch_qgemm_fused<J4B_Q4_K, 1>(w, mh, ml, mi, kpi, y, stream); break;
-      case J4B_Q4_K * 4 + 3: e = launch_qgemm_fused<J4B_Q4_K, 3>(w, mh, ml, mi, kpi, y, stream); break;
+    const bool wide = m > 256;  // two 256-token accumulators per CTA
+    switch (w->type * 8 + terms * 2 + (wide ? 1 : 0)) {
+#define J4B_QG_CASE(QT, T)                                                                                     \
+  case QT * 8 + T * 2: e = launch_qgemm_fused<QT, T, 1>(w, mh, ml, mi, kpi, y, stream); break;              \
+  case QT * 8 + T * 2 + 1: e = launch_qgemm_fused<QT, T, 2>(w, mh, ml, mi, kpi, y, stream); break;
+      J4B_QG_CASE(J4B_Q8_0, 1)
+      J4B_QG_CASE(J4B_Q8_0, 3)
+      J4B_QG_CASE(J4B_Q4_0, 1)
+      J4B_QG_CASE(J4B_Q4_0, 3)
+      J4B_QG_CASE(J4B_Q4_K, 1)
+      J4B_QG_CASE(J4B_Q4_K, 3)
+#undef J4B_QG_CASE
     }
     if (e != cudaSuccess) rc = cuda_error(e, "qgemm_fused_kernel");
     else count_launch();
