@@ -976,15 +976,15 @@ cudaError_t gemv_dispatch(const j4b_qweight* w, const float* x, const float* add
                           unsigned* grid_out = nullptr) {
   static const char* variant = getenv("J4B_QGEMV_VARIANT");  // development A/B only
   static const bool legacy = variant && variant[0] == 'l';
-  static const bool wide = !(variant && variant[0] == 's');
+  static const bool pair = variant && variant[0] == 'p';
   const bool pdl = !w->fresh;
   const_cast<j4b_qweight*>(w)->fresh = false;
   if (!legacy && batch <= 4)
-    return wide ? launch_gemv_stream<QT, true, 16>(w, x, add, y, batch, sms, stream, peers, grid_out, pdl)
-                : launch_gemv_stream<QT, true, 8>(w, x, add, y, batch, sms, stream, peers, grid_out, pdl);
+    return pair ? launch_gemv_stream<QT, true, 16, true>(w, x, add, y, batch, sms, stream, peers, grid_out, pdl)
+                : launch_gemv_stream<QT, true, 16>(w, x, add, y, batch, sms, stream, peers, grid_out, pdl);
   if (!legacy && batch <= 8)
-    return wide ? launch_gemv_stream<QT, false, 16>(w, x, add, y, batch, sms, stream, peers, grid_out, pdl)
-                : launch_gemv_stream<QT, false, 8>(w, x, add, y, batch, sms, stream, peers, grid_out, pdl);
+    return pair ? launch_gemv_stream<QT, false, 16, true>(w, x, add, y, batch, sms, stream, peers, grid_out, pdl)
+                : launch_gemv_stream<QT, false, 16>(w, x, add, y, batch, sms, stream, peers, grid_out, pdl);
   if (batch <= 4) return launch_gemv<QT, 1, true>(w, x, add, y, batch, sms, stream, peers, grid_out, pdl);
   if (batch <= 8) return launch_gemv<QT, 1, false>(w, x, add, y, batch, sms, stream, peers, grid_out, pdl);
   return launch_gemv<QT, 2, false>(w, x, add, y, batch, sms, stream, peers, grid_out, pdl);
