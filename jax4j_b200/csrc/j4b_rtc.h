@@ -20,6 +20,7 @@ struct Driver {
   PFN_cuFuncSetAttribute_v9000 FuncSetAttribute = nullptr;
   PFN_cuOccupancyMaxActiveBlocksPerMultiprocessor_v6050 Occupancy = nullptr;
   PFN_cuLaunchKernel_v4000 LaunchKernel = nullptr;
+  PFN_cuLaunchKernelEx_v11060 LaunchKernelEx = nullptr;  // optional: programmatic dependent launch
   PFN_cuGetErrorName_v6000 GetErrorName = nullptr;
   bool ok = false;
 };

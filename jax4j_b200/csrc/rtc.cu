@@ -27,6 +27,7 @@ const Driver& driver() {
            get("cuOccupancyMaxActiveBlocksPerMultiprocessor", (void**)&d.Occupancy) &&
            get("cuLaunchKernel", (void**)&d.LaunchKernel) &&
            get("cuGetErrorName", (void**)&d.GetErrorName);
+    if (!get("cuLaunchKernelEx", (void**)&d.LaunchKernelEx)) d.LaunchKernelEx = nullptr;
   });
   return d;
 }

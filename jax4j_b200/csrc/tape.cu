@@ -47,6 +47,13 @@ enum : int {
 };
 
 constexpr int64_t kTapeMagic = 0x314550415442344ALL;  // "J4BTAPE1"
+// Row and fold kernels are launched with programmatic dependent launch: each waits for the kernel
+// before it (and its memory) before touching memory, and at once lets the next kernel in the
+// stream be scheduled, so a launch's set-up overlaps the tail of the previous one (a fold kernel
+// is resident before its row kernel ends).
+constexpr const char* kPdlPrologue =
+    "  asm volatile(\"griddepcontrol.wait;\" ::: \"memory\");\n"
+    "  asm volatile(\"griddepcontrol.launch_dependents;\" ::: \"memory\");\n";
 constexpr int64_t kSharedMax = 16384;  // largest row-invariant vector kept per CTA
 // fold kernel: 8 warps per 32-column slice (32 warps measured 2% slower per tape step)
 constexpr int kFoldThreads = 256;
@@ -2046,7 +2053,7 @@ struct Gen {
         << "  (void)red; (void)sm;\n"
         << "  const int t = threadIdx.x;\n"
         << "  const long long R = A.R;\n  (void)R;\n"
-        << pro.str() << acc.str();
+        << kPdlPrologue << pro.str() << acc.str();
     std::string cf;
     if (!colflush.str().empty()) {
       src << "  bool col_first = true;\n";
@@ -2068,7 +2075,7 @@ struct Gen {
           << "extern \"C\" __global__ void __launch_bounds__(" << kFoldThreads << ") " << rn << "_fold(const Args A) {\n"
           << "  __shared__ double fred[" << kFoldThreads << "];\n  (void)fred;\n"
           << "  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;\n  (void)warp;\n"
-          << "  const long long i = (long long)blockIdx.x * 32 + lane;\n" << fold.str() << "}\n";
+          << "  const long long i = (long long)blockIdx.x * 32 + lane;\n" << kPdlPrologue << fold.str() << "}\n";
     }
     gcode.src = src.str();
     gcode.row_name = rn;
@@ -2383,6 +2390,26 @@ uint64_t addr_of(const LaunchCtx& L, int b) {
   return resolve(L, L.tp->loc[(size_t)root]) + (uint64_t)off * 4;
 }
 
+// A generated kernel launch with programmatic stream serialization (cuLaunchKernelEx); plain
+// cuLaunchKernel where the driver lacks it (the kernels' griddepcontrol then return at once).
+CUresult launch_pdl(CUfunction f, unsigned grid, unsigned threads, unsigned smem, cudaStream_t stream, void** params) {
+  if (!driver().LaunchKernelEx)
+    return driver().LaunchKernel(f, grid, 1, 1, threads, 1, 1, smem, (CUstream)stream, params, nullptr);
+  CUlaunchConfig cfg = {};
+  cfg.gridDimX = grid;
+  cfg.gridDimY = cfg.gridDimZ = 1;
+  cfg.blockDimX = threads;
+  cfg.blockDimY = cfg.blockDimZ = 1;
+  cfg.sharedMemBytes = smem;
+  cfg.hStream = (CUstream)stream;
+  CUlaunchAttribute attr[1];
+  attr[0].id = CU_LAUNCH_ATTRIBUTE_PROGRAMMATIC_STREAM_SERIALIZATION;
+  attr[0].value.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return driver().LaunchKernelEx(&cfg, f, params, nullptr);
+}
+
 int run_eager(const LaunchCtx& L, int ci, cudaStream_t stream) {
   const TapeIR& t = L.tp->ir;
   const TCall& c = t.calls[(size_t)ci];
@@ -2477,12 +2504,11 @@ extern "C" int j4b_tape_launch(j4b_tape* tp, const j4b_buf* inputs, int nin, con
       args[np] = (uint64_t)run.R;
       args[np + 1] = (uint64_t)run.grid;
       void* params[] = {args.data()};
-      CUresult r = driver().LaunchKernel(run.row, (unsigned)run.grid, 1, 1, (unsigned)run.NT, 1, 1,
-                                  (unsigned)run.smem, (CUstream)stream, params, nullptr);
+      CUresult r = launch_pdl(run.row, (unsigned)run.grid, (unsigned)run.NT, (unsigned)run.smem, stream, params);
       if (r != CUDA_SUCCESS) return cu_error(r, "cuLaunchKernel(tape group)");
       count_launch();
       if (run.fold) {
-        r = driver().LaunchKernel(run.fold, (unsigned)run.fold_grid, 1, 1, kFoldThreads, 1, 1, 0, (CUstream)stream, params, nullptr);
+        r = launch_pdl(run.fold, (unsigned)run.fold_grid, kFoldThreads, 0, stream, params);
         if (r != CUDA_SUCCESS) return cu_error(r, "cuLaunchKernel(tape fold)");
         count_launch();
       }
