@@ -24,23 +24,25 @@ from jax4j_b200 import _lib
 be = B200Backend(rank)
 pg = PeerGroup(rank, rank, world)
 s = torch_stream()
-rows, cols, batch = 96, 512, 3
-rng = np.random.default_rng(100 + rank)
-w = (rng.standard_normal((rows, cols)) * 0.02).astype(np.float32)
-blob = be.quantize(be.upload(w, w.shape), 8)
-wq = be.upload_quantized(blob, 8, (rows, cols))
-x = np.random.default_rng(7).standard_normal((batch, cols)).astype(np.float32)
-xb = be.upload(x, x.shape)
-mine = be.download(be.quant_matvec(wq, xb)).reshape(batch, rows)
-y_all = torch.empty(batch * rows * world, device="cuda")
-for it in range(3):
-    pg.allgather_matvec(wq, xb.ptr, y_all.data_ptr(), batch, s)
-torch.cuda.synchronize()
-got = y_all.cpu().numpy().reshape(batch, world * rows)
-parts = [torch.empty(batch * rows, device="cuda") for _ in range(world)]
-dist.all_gather(parts, torch.from_numpy(mine.reshape(-1)).cuda())
-want = np.concatenate([p.cpu().numpy().reshape(batch, rows) for p in parts], axis=1)
-assert np.array_equal(got, want), "all-gather mismatch"
+# one K split (the epilogue stores y into every rank), and four K splits at batch 8 (the split-K
+# fold inside the all-gathering kernel, where the local GEMV folds in a separate kernel)
+for rows, cols, batch, qtype in ((96, 512, 3, 8), (256, 4096, 8, 8), (160, 2048, 1, 12)):
+    rng = np.random.default_rng(100 + rank)
+    w = (rng.standard_normal((rows, cols)) * 0.02).astype(np.float32)
+    blob = be.quantize(be.upload(w, w.shape), qtype)
+    wq = be.upload_quantized(blob, qtype, (rows, cols))
+    x = np.random.default_rng(7).standard_normal((batch, cols)).astype(np.float32)
+    xb = be.upload(x, x.shape)
+    mine = be.download(be.quant_matvec(wq, xb)).reshape(batch, rows)
+    y_all = torch.empty(batch * rows * world, device="cuda")
+    for it in range(3):
+        pg.allgather_matvec(wq, xb.ptr, y_all.data_ptr(), batch, s)
+    torch.cuda.synchronize()
+    got = y_all.cpu().numpy().reshape(batch, world * rows)
+    parts = [torch.empty(batch * rows, device="cuda") for _ in range(world)]
+    dist.all_gather(parts, torch.from_numpy(mine.reshape(-1)).cuda())
+    want = np.concatenate([p.cpu().numpy().reshape(batch, rows) for p in parts], axis=1)
+    assert np.array_equal(got, want), ("all-gather mismatch", rows, cols, batch)
 n = 5000
 for it in range(3):
     v = torch.from_numpy(np.random.default_rng(it * 10 + rank).standard_normal(n).astype(np.float32)).cuda()
