@@ -27,25 +27,27 @@
 constexpr int kQgBM = 128, kQgBK = 64;
 constexpr int kQgThreads = 10 * 32;
 
-// Tokens per MMA (N); NH accumulators of N columns each per CTA (NH = 2: 512 tokens in bf16 mode,
-// the whole TMEM, one CTA per SM; NH = 1: two CTAs per SM, for short token counts).
-template <int TERMS>
-constexpr int qg_bn() { return TERMS == 1 ? 256 : 128; }
-template <int TERMS, int NH>
-constexpr int qg_stages() { return TERMS == 1 ? 2 : (NH == 1 ? 3 : 2); }
+// N tokens per MMA, NH accumulators of N columns each per CTA (NH = 2, N = 256: 512 tokens in bf16
+// mode, the whole TMEM, one CTA per SM; N = 64: decode-time batches).
+template <int TERMS, int N, int NH>
+constexpr int qg_stages() { return (TERMS == 1 && N * NH <= 256) ? 2 : (TERMS == 3 && N * NH <= 128 ? 3 : 2); }
 constexpr uint32_t kQgABytes = kQgBM * kQgBK * 2;  // one 128 x 64 bf16 tile
-template <int TERMS, int NH>
-constexpr uint32_t qg_b_bytes() { return (uint32_t)(NH * qg_bn<TERMS>()) * kQgBK * 2; }
+template <int N, int NH>
+constexpr uint32_t qg_b_bytes() { return (uint32_t)(NH * N) * kQgBK * 2; }
 // stage: A hi | B hi | (A lo | B lo); a B part holds the NH token boxes one after the other
-template <int TERMS, int NH>
-constexpr uint32_t qg_stage_bytes() { return (TERMS == 3 ? 2u : 1u) * (kQgABytes + qg_b_bytes<TERMS, NH>()); }
+template <int TERMS, int N, int NH>
+constexpr uint32_t qg_stage_bytes() { return (TERMS == 3 ? 2u : 1u) * (kQgABytes + qg_b_bytes<N, NH>()); }
+template <int TERMS, int N, int NH>
+constexpr int qg_min_blocks() { return (TERMS == 1 && N * NH <= 256) ? 2 : 1; }
 
 struct QgArgs {
   const uint8_t* data;
   Layout L;
   int64_t rows, cols;
   int m, kp;
-  float* y;
+  int splits, kb_per;  // K splits and 64-column k-blocks per split
+  float* y;            // [m, rows]; with splits > 1 the partials [splits][m][rows]
+  const float* add;    // added to y (splits == 1 only; else the fold adds it)
   int* status;
 };
 
@@ -180,14 +182,14 @@ __device__ __forceinline__ void qg_store(const QgBytes& b, int kb, int lane, uin
       }
 }
 
-template <int QT, int TERMS, int NH>
-__global__ void __launch_bounds__(kQgThreads, TERMS == 1 && NH == 1 ? 2 : 1)
+template <int QT, int TERMS, int N, int NH>
+__global__ void __launch_bounds__(kQgThreads, qg_min_blocks<TERMS, N, NH>())
     qgemm_fused_kernel(const __grid_constant__ CUtensorMap x_hi, const __grid_constant__ CUtensorMap x_lo, QgArgs p) {
-  constexpr int kN = qg_bn<TERMS>();   // tokens per MMA
+  constexpr int kN = N;                // tokens per MMA
   constexpr int kBN = NH * kN;         // tokens per tile (TMEM columns)
-  constexpr int kStages = qg_stages<TERMS, NH>();
-  constexpr uint32_t kStage = qg_stage_bytes<TERMS, NH>();
-  constexpr uint32_t kB = qg_b_bytes<TERMS, NH>();
+  constexpr int kStages = qg_stages<TERMS, N, NH>();
+  constexpr uint32_t kStage = qg_stage_bytes<TERMS, N, NH>();
+  constexpr uint32_t kB = qg_b_bytes<N, NH>();
   constexpr uint32_t kBox = (uint32_t)kN * kQgBK * 2;  // one token box
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -198,11 +200,16 @@ __global__ void __launch_bounds__(kQgThreads, TERMS == 1 && NH == 1 ? 2 : 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // tile order: W-row tiles fastest, then K splits, then token tiles
   const int n_tiles = (int)((p.rows + kQgBM - 1) / kQgBM);
-  const int n_tile = (int)(blockIdx.x % n_tiles), t_tile = (int)(blockIdx.x / n_tiles);
+  const int n_tile = (int)(blockIdx.x % n_tiles);
+  const int split = (int)((blockIdx.x / n_tiles) % p.splits);
+  const int t_tile = (int)(blockIdx.x / n_tiles / p.splits);
   const int64_t w0 = (int64_t)n_tile * kQgBM;
   const int tok0 = t_tile * kBN;
-  const int nk = p.kp / kQgBK;
+  const int kb0 = split * p.kb_per;
+  const int nk = min(p.kp / kQgBK - kb0, p.kb_per);  // k-blocks of this CTA, from kb0
+  float* out = p.y + (int64_t)split * p.m * p.rows;
   auto stage_a = [&](int s, int lo) { return smem + s * kStage + (lo ? kQgABytes + kB : 0); };
   auto stage_b = [&](int s, int lo) { return smem + s * kStage + kQgABytes + (lo ? kQgABytes + kB : 0); };
 
@@ -232,10 +239,11 @@ __global__ void __launch_bounds__(kQgThreads, TERMS == 1 && NH == 1 ? 2 : 1)
         const int s = kb % kStages, use = kb / kStages;
         if (use > 0 && !bar_wait(&empty[s], (uint32_t)((use - 1) & 1))) ok = false;
         bar_expect_tx(&full_b[s], (TERMS == 3 ? 2u : 1u) * kB);
+        const int kx = (kb0 + kb) * kQgBK;
 #pragma unroll
         for (int h = 0; h < NH; ++h) {
-          tma_tile(stage_b(s, 0) + h * kBox, &x_hi, kb * kQgBK, tok0 + h * kN, &full_b[s]);
-          if (TERMS == 3) tma_tile(stage_b(s, 1) + h * kBox, &x_lo, kb * kQgBK, tok0 + h * kN, &full_b[s]);
+          tma_tile(stage_b(s, 0) + h * kBox, &x_hi, kx, tok0 + h * kN, &full_b[s]);
+          if (TERMS == 3) tma_tile(stage_b(s, 1) + h * kBox, &x_lo, kx, tok0 + h * kN, &full_b[s]);
         }
       }
     }
@@ -286,7 +294,10 @@ __global__ void __launch_bounds__(kQgThreads, TERMS == 1 && NH == 1 ? 2 : 1)
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
           const int tok = tok0 + c + u;
-          if (tok < p.m) p.y[(int64_t)tok * p.rows + row] = __uint_as_float(v[u]);
+          if (tok < p.m) {
+            const int64_t o = (int64_t)tok * p.rows + row;
+            out[o] = p.add ? __uint_as_float(v[u]) + p.add[o] : __uint_as_float(v[u]);
+          }
         }
       }
     }
@@ -295,19 +306,19 @@ __global__ void __launch_bounds__(kQgThreads, TERMS == 1 && NH == 1 ? 2 : 1)
     const int d = warp - 6;
     const int64_t tile0 = w0 / 16 + 2 * d;
     QgBytes cur[2], nxt[2];
-    qg_load<QT>(p, tile0, 0, lane, cur[0]);
-    qg_load<QT>(p, tile0 + 1, 0, lane, cur[1]);
+    qg_load<QT>(p, tile0, kb0, lane, cur[0]);
+    qg_load<QT>(p, tile0 + 1, kb0, lane, cur[1]);
     for (int kb = 0; kb < nk; ++kb) {
       const int s = kb % kStages, use = kb / kStages;
       if (kb + 1 < nk) {
-        qg_load<QT>(p, tile0, kb + 1, lane, nxt[0]);
-        qg_load<QT>(p, tile0 + 1, kb + 1, lane, nxt[1]);
+        qg_load<QT>(p, tile0, kb0 + kb + 1, lane, nxt[0]);
+        qg_load<QT>(p, tile0 + 1, kb0 + kb + 1, lane, nxt[1]);
       }
       if (use > 0 && !bar_wait(&empty[s], (uint32_t)((use - 1) & 1))) ok = false;
       uint8_t* ahi = stage_a(s, 0);
       uint8_t* alo = stage_a(s, 1);
-      qg_store<QT, TERMS>(cur[0], kb, lane, ahi, alo, 32 * d);
-      qg_store<QT, TERMS>(cur[1], kb, lane, ahi, alo, 32 * d + 16);
+      qg_store<QT, TERMS>(cur[0], kb0 + kb, lane, ahi, alo, 32 * d);
+      qg_store<QT, TERMS>(cur[1], kb0 + kb, lane, ahi, alo, 32 * d + 16);
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor-core reads
       __syncwarp();
       if (lane == 0) bar_arrive(&full_a[s]);
@@ -325,18 +336,30 @@ __global__ void __launch_bounds__(kQgThreads, TERMS == 1 && NH == 1 ? 2 : 1)
   }
 }
 
-template <int QT, int TERMS, int NH>
+// y[i] = sum over splits of part[sp][i], in split order (+ add[i]).
+__global__ void qgemm_fold_kernel(const float* __restrict__ part, int splits, int64_t n, const float* __restrict__ add,
+                                  float* __restrict__ y) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    float v = 0.f;
+    for (int sp = 0; sp < splits; ++sp) v += __ldcg(part + sp * n + i);
+    if (add) v += add[i];
+    y[i] = v;
+  }
+}
+
+template <int QT, int TERMS, int N, int NH>
 cudaError_t launch_qgemm_fused(const j4b_qweight* w, const CUtensorMap& xh, const CUtensorMap& xl, int m, int kp,
-                               float* y, cudaStream_t stream) {
-  constexpr int kBN = NH * qg_bn<TERMS>();
-  const size_t smem = (size_t)qg_stages<TERMS, NH>() * qg_stage_bytes<TERMS, NH>() + 1024 + 256;
+                               int splits, int kb_per, float* out, const float* add, cudaStream_t stream) {
+  constexpr int kBN = NH * N;
+  const size_t smem = (size_t)qg_stages<TERMS, N, NH>() * qg_stage_bytes<TERMS, N, NH>() + 1024 + 256;
   static bool attr_set[kMaxDevices] = {};
   if (w->dev < 0 || w->dev >= kMaxDevices) return cudaErrorInvalidDevice;
   if (!attr_set[w->dev]) {
-    cudaError_t e = cudaFuncSetAttribute(qgemm_fused_kernel<QT, TERMS, NH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e = cudaFuncSetAttribute(qgemm_fused_kernel<QT, TERMS, N, NH>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     attr_set[w->dev] = true;
   }
+  const int nk = kp / kQgBK;
   QgArgs p;
   p.data = w->data;
   p.L = layout_of(w);
@@ -344,10 +367,14 @@ cudaError_t launch_qgemm_fused(const j4b_qweight* w, const CUtensorMap& xh, cons
   p.cols = w->cols;
   p.m = m;
   p.kp = kp;
-  p.y = y;
+  p.kb_per = kb_per;
+  p.splits = splits;
+  if (splits < 1 || kb_per < 1 || (int64_t)(splits - 1) * kb_per >= nk) return cudaErrorInvalidValue;
+  p.y = out;
+  p.add = p.splits == 1 ? add : nullptr;
   p.status = w->status;
-  const int64_t tiles = ((w->rows + kQgBM - 1) / kQgBM) * (((int64_t)m + kBN - 1) / kBN);
+  const int64_t tiles = ((w->rows + kQgBM - 1) / kQgBM) * p.splits * (((int64_t)m + kBN - 1) / kBN);
   if (tiles > 0x7fffffffLL) return cudaErrorInvalidValue;
-  qgemm_fused_kernel<QT, TERMS, NH><<<(unsigned)tiles, kQgThreads, smem, stream>>>(xh, xl, p);
+  qgemm_fused_kernel<QT, TERMS, N, NH><<<(unsigned)tiles, kQgThreads, smem, stream>>>(xh, xl, p);
   return cudaGetLastError();
 }

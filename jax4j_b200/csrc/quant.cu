@@ -753,6 +753,13 @@ extern "C" int j4b_quant_shape(j4b_qweight_t w, int* type, int64_t* rows, int64_
   return J4B_OK;
 }
 
+namespace j4b {
+namespace {
+int quant_gemm_fused(const j4b_qweight* w, const float* x, float* y, const float* add, int64_t m, int64_t kp, int terms,
+                     int sms, cudaStream_t stream);
+}  // namespace
+}  // namespace j4b
+
 extern "C" int j4b_quant_matvec(j4b_qweight_t w, j4b_buf x, j4b_buf add, j4b_buf y,
                                 int64_t batch, j4b_stream s) {
   if (!w) return set_error(J4B_EINVAL, "null quantized weight");
@@ -763,6 +770,16 @@ extern "C" int j4b_quant_matvec(j4b_qweight_t w, j4b_buf x, j4b_buf add, j4b_buf
   DeviceGuard guard(w->dev);
   cudaStream_t stream = resolve_stream(w->dev, s);
   const int sms = device_ctx(w->dev)->sm_count;
+  // more than 16 rows of x: one pass over the weight on the tensor cores (the fused dequant-GEMM
+  // in its fp32-accurate 3-term mode) instead of a GEMV pass per 16 rows
+  static const bool passes = getenv("J4B_QGEMV_PASSES") != nullptr;  // development A/B only
+  if (batch > 16 && !passes && (w->type == J4B_Q8_0 || w->type == J4B_Q4_0 || w->type == J4B_Q4_K) &&
+      batch <= INT32_MAX) {
+    w->fresh = false;
+    return quant_gemm_fused(w, (const float*)(uintptr_t)x, (float*)(uintptr_t)y,
+                            add ? (const float*)(uintptr_t)add : nullptr, batch, (w->cols + 63) / 64 * 64, 3, sms,
+                            stream);
+  }
   for (int64_t b0 = 0; b0 < batch; b0 += 16) {
     const int nb = (int)std::min<int64_t>(16, batch - b0);
     const float* xp = (const float*)(uintptr_t)x + b0 * w->cols;
@@ -830,40 +847,65 @@ extern "C" int j4b_quant_gather_row(j4b_qweight_t w, int64_t row, j4b_buf out, j
 // decoded (bit-exact) to bf16 K-major operands in stream-ordered scratch, then multiplied.
 namespace j4b {
 namespace {
-// x -> bf16 hi (and lo) [m, kp] in stream-ordered scratch, then the fused dequant-GEMM.
-int quant_gemm_fused(const j4b_qweight* w, const float* x, float* y, int64_t m, int64_t kp, int terms,
-                     cudaStream_t stream) {
+// x -> bf16 hi (and lo) [m, kp] in stream-ordered scratch, then the fused dequant-GEMM (+ add).
+// Tile shape by token count: two 256-token accumulators per CTA for long inputs (prefill), one
+// for up to 256 tokens, 64-token tiles for decode-time batches; the K range is split over CTAs
+// (partials in stream-ordered scratch, summed in split order by qgemm_fold_kernel) when the
+// output tiles alone would leave SMs idle.
+int quant_gemm_fused(const j4b_qweight* w, const float* x, float* y, const float* add, int64_t m, int64_t kp, int terms,
+                     int sms, cudaStream_t stream) {
+  const int nk = (int)(kp / 64);
+  const int n_tiles = (int)((w->rows + kQgBM - 1) / kQgBM);
+  const int N = m <= 64 ? 64 : (terms == 1 ? 256 : 128);
+  const int NH = m > 256 ? 2 : 1;
+  const int64_t t_tiles = (m + (int64_t)N * NH - 1) / ((int64_t)N * NH);
+  int splits = 1;
+  if ((int64_t)n_tiles * t_tiles < sms) splits = (int)std::min<int64_t>((sms + n_tiles * t_tiles - 1) / (n_tiles * t_tiles), std::max(1, nk / 8));
+  const int kb_per = (nk + splits - 1) / splits;
+  splits = (nk + kb_per - 1) / kb_per;
   const size_t xbytes = (size_t)(m * kp) * 2;
+  const size_t xspan = (xbytes + 255) & ~size_t(255);
+  const size_t pbytes = splits > 1 ? (size_t)splits * (size_t)(m * w->rows) * 4 : 0;
   void* scratch = nullptr;
-  J4B_CUDA(cudaMallocAsync(&scratch, 2 * xbytes + 512, stream), "cudaMallocAsync(x operand)");
+  J4B_CUDA(cudaMallocAsync(&scratch, 2 * xspan + pbytes + 256, stream), "cudaMallocAsync(x operand)");
   __nv_bfloat16* xh = (__nv_bfloat16*)scratch;
-  __nv_bfloat16* xl = terms == 3 ? (__nv_bfloat16*)((uint8_t*)scratch + ((xbytes + 255) & ~size_t(255))) : nullptr;
+  __nv_bfloat16* xl = terms == 3 ? (__nv_bfloat16*)((uint8_t*)scratch + xspan) : nullptr;
+  float* part = splits > 1 ? (float*)((uint8_t*)scratch + 2 * xspan) : nullptr;
   int rc = tc_split_rows(x, m, w->cols, w->cols, kp, xh, xl, stream);
   CUtensorMap mh, ml;
   if (rc == J4B_OK) {
-    const int bn = terms == 3 ? qg_bn<3>() : qg_bn<1>();
-    if (!make_map(&mh, xh, m, kp, bn) || (terms == 3 && !make_map(&ml, xl, m, kp, bn)))
-      rc = set_error(J4B_ECUDA, "cuTensorMapEncodeTiled failed for the prefill activations");
+    if (!make_map(&mh, xh, m, kp, N) || (terms == 3 && !make_map(&ml, xl, m, kp, N)))
+      rc = set_error(J4B_ECUDA, "cuTensorMapEncodeTiled failed for the activations");
     if (terms != 3) ml = mh;
   }
   if (rc == J4B_OK) {
     cudaError_t e = cudaErrorInvalidValue;
     const int mi = (int)m, kpi = (int)kp;
-    const bool wide = m > 256;  // two 256-token accumulators per CTA
-    switch (w->type * 8 + terms * 2 + (wide ? 1 : 0)) {
-#define J4B_QG_CASE(QT, T)                                                                                     \
-  case QT * 8 + T * 2: e = launch_qgemm_fused<QT, T, 1>(w, mh, ml, mi, kpi, y, stream); break;              \
-  case QT * 8 + T * 2 + 1: e = launch_qgemm_fused<QT, T, 2>(w, mh, ml, mi, kpi, y, stream); break;
-      J4B_QG_CASE(J4B_Q8_0, 1)
-      J4B_QG_CASE(J4B_Q8_0, 3)
-      J4B_QG_CASE(J4B_Q4_0, 1)
-      J4B_QG_CASE(J4B_Q4_0, 3)
-      J4B_QG_CASE(J4B_Q4_K, 1)
-      J4B_QG_CASE(J4B_Q4_K, 3)
+    float* out = splits > 1 ? part : y;
+    const int shape = N == 64 ? 0 : (NH == 1 ? 1 : 2);
+    switch ((w->type * 4 + terms) * 3 + shape) {
+#define J4B_QG_CASE(QT, T, NW)                                                                                     \
+  case (QT * 4 + T) * 3 + 0: e = launch_qgemm_fused<QT, T, 64, 1>(w, mh, ml, mi, kpi, splits, kb_per, out, add, stream); break; \
+  case (QT * 4 + T) * 3 + 1: e = launch_qgemm_fused<QT, T, NW, 1>(w, mh, ml, mi, kpi, splits, kb_per, out, add, stream); break; \
+  case (QT * 4 + T) * 3 + 2: e = launch_qgemm_fused<QT, T, NW, 2>(w, mh, ml, mi, kpi, splits, kb_per, out, add, stream); break;
+      J4B_QG_CASE(J4B_Q8_0, 1, 256)
+      J4B_QG_CASE(J4B_Q8_0, 3, 128)
+      J4B_QG_CASE(J4B_Q4_0, 1, 256)
+      J4B_QG_CASE(J4B_Q4_0, 3, 128)
+      J4B_QG_CASE(J4B_Q4_K, 1, 256)
+      J4B_QG_CASE(J4B_Q4_K, 3, 128)
 #undef J4B_QG_CASE
     }
     if (e != cudaSuccess) rc = cuda_error(e, "qgemm_fused_kernel");
     else count_launch();
+    if (rc == J4B_OK && splits > 1) {
+      const int64_t n = m * w->rows;
+      qgemm_fold_kernel<<<(unsigned)std::min<int64_t>((n + 255) / 256, (int64_t)sms * 8), 256, 0, stream>>>(
+          part, splits, n, add, y);
+      cudaError_t fe = cudaGetLastError();
+      if (fe != cudaSuccess) rc = cuda_error(fe, "qgemm_fold_kernel");
+      else count_launch();
+    }
   }
   cudaFreeAsync(scratch, stream);
   return rc;
@@ -885,7 +927,8 @@ extern "C" int j4b_quant_gemm(j4b_qweight_t w, j4b_buf x, j4b_buf y, int64_t m, 
   static const bool two_pass = getenv("J4B_QGEMM_TWO_PASS") != nullptr;  // development A/B only
   if (!two_pass && (w->type == J4B_Q8_0 || w->type == J4B_Q4_0 || w->type == J4B_Q4_K) && m <= INT32_MAX &&
       w->rows <= INT32_MAX)
-    return quant_gemm_fused(w, (const float*)(uintptr_t)x, (float*)(uintptr_t)y, m, kp, terms, stream);
+    return quant_gemm_fused(w, (const float*)(uintptr_t)x, (float*)(uintptr_t)y, nullptr, m, kp, terms,
+                            device_ctx(w->dev)->sm_count, stream);
   const size_t bytes = (size_t)(w->rows * kp) * 2;
   void* scratch = nullptr;
   J4B_CUDA(cudaMallocAsync(&scratch, 2 * bytes + 512, stream), "cudaMallocAsync(dequantised weight)");
