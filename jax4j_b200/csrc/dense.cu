@@ -346,6 +346,55 @@ __global__ void random_kernel(int normal, int64_t seed, int64_t counter, float* 
   }
 }
 
+// Skinny fp32 matmuls, where a 64 x 64 output tile would leave most of the GPU idle (a logits
+// layer's n = 10, or its gradient's k = 10): fp32 FMA accumulation in ascending p, batch in
+// grid.y.
+// k <= 32: one thread per output element, the k products summed in order.
+__global__ void __launch_bounds__(256) gemm_short_k_kernel(const float* __restrict__ A, const float* __restrict__ B,
+                                                           float* __restrict__ C, int64_t M, int64_t K, int64_t N) {
+  const int64_t bz = blockIdx.y;
+  const int64_t idx = (int64_t)blockIdx.x * 256 + threadIdx.x;
+  if (idx >= M * N) return;
+  const int64_t i = idx / N, j = idx % N;
+  const float* a = A + bz * M * K + i * K;
+  const float* b = B + bz * K * N + j;
+  float acc = 0.f;
+  for (int64_t p = 0; p < K; p++) acc = fmaf(__ldg(a + p), __ldg(b + p * N), acc);
+  C[bz * M * N + idx] = acc;
+}
+
+// n <= 32: one warp per row of C; lane l takes p = l, l + 32, ... and keeps n partial sums, which
+// the warp adds lane-wise (butterfly), so the sum order is fixed.
+__global__ void __launch_bounds__(256) gemm_narrow_n_kernel(const float* __restrict__ A, const float* __restrict__ B,
+                                                            float* __restrict__ C, int64_t M, int64_t K, int N) {
+  const int64_t bz = blockIdx.y;
+  const int lane = threadIdx.x & 31;
+  const int64_t i = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (i >= M) return;
+  const float* a = A + bz * M * K + i * K;
+  const float* b = B + bz * K * N;
+  float acc[32];
+#pragma unroll
+  for (int j = 0; j < 32; j++) acc[j] = 0.f;
+  for (int64_t p = lane; p < K; p += 32) {
+    const float av = __ldg(a + p);
+    const float* br = b + p * N;
+#pragma unroll
+    for (int j = 0; j < 32; j++)
+      if (j < N) acc[j] = fmaf(av, __ldg(br + j), acc[j]);
+  }
+  float mine = 0.f;
+#pragma unroll
+  for (int j = 0; j < 32; j++) {
+    if (j >= N) break;
+    float v = acc[j];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == j) mine = v;
+  }
+  if (lane < N) C[bz * M * N + i * N + lane] = mine;
+}
+
 // fp32 SIMT matmul (precision 0): 64x64 output tile per 256-thread block, 4x4 per thread,
 // fp32 FMA accumulation; batch in grid.z.
 __global__ void __launch_bounds__(256) sgemm_kernel(const float* __restrict__ A,
@@ -643,9 +692,21 @@ extern "C" int j4b_matmul(j4b_buf a, j4b_buf b, j4b_buf out, int64_t batch, int6
   if (precision == 1 || precision == 2 || big)
     return tc_matmul((const float*)(uintptr_t)a, (const float*)(uintptr_t)b, (float*)(uintptr_t)out, batch, m,
                      k, n, precision == 1 ? 1 : 3, dev, stream);
+  const float* pa = (const float*)(uintptr_t)a;
+  const float* pb = (const float*)(uintptr_t)b;
+  float* pc = (float*)(uintptr_t)out;
+  if (k <= 32 && batch <= 65535 && (m * n + 255) / 256 <= INT32_MAX) {
+    gemm_short_k_kernel<<<dim3((unsigned)((m * n + 255) / 256), (unsigned)batch), 256, 0, stream>>>(pa, pb, pc, m, k, n);
+    J4B_CHECK_LAUNCH("gemm_short_k_kernel");
+    return J4B_OK;
+  }
+  if (n <= 32 && batch <= 65535 && (m + 7) / 8 <= INT32_MAX) {
+    gemm_narrow_n_kernel<<<dim3((unsigned)((m + 7) / 8), (unsigned)batch), 256, 0, stream>>>(pa, pb, pc, m, k, (int)n);
+    J4B_CHECK_LAUNCH("gemm_narrow_n_kernel");
+    return J4B_OK;
+  }
   dim3 grid((unsigned)((n + 63) / 64), (unsigned)((m + 63) / 64), (unsigned)batch);
-  sgemm_kernel<<<grid, 256, 0, stream>>>((const float*)(uintptr_t)a, (const float*)(uintptr_t)b,
-                                         (float*)(uintptr_t)out, m, k, n);
+  sgemm_kernel<<<grid, 256, 0, stream>>>(pa, pb, pc, m, k, n);
   J4B_CHECK_LAUNCH("sgemm_kernel");
   return J4B_OK;
 }

@@ -157,9 +157,6 @@ struct GemvArgs {
   unsigned* peer_ctr[kMaxPeerRanks];  // at rank p: the counter of this rank as a source
   const unsigned* step;
   int64_t half_floats;
-  // streaming kernel only: with K splits, store the split partials and leave their sum to
-  // qgemv_fold_kernel (launched right after), so the CTAs exit as soon as their tiles are done
-  int defer_fold;
 };
 
 // Stores one output, locally or into every rank's gathered buffer.
@@ -889,7 +886,6 @@ cudaError_t launch_gemv(const j4b_qweight* w, const float* x, const float* add, 
   a.partials = w->partials;
   a.arrivals = w->arrivals;
   a.status = w->status;
-  a.defer_fold = 0;
   a.nranks = 1;
   a.rank = 0;
   a.step = nullptr;
@@ -976,15 +972,10 @@ cudaError_t gemv_dispatch(const j4b_qweight* w, const float* x, const float* add
                           unsigned* grid_out = nullptr) {
   static const char* variant = getenv("J4B_QGEMV_VARIANT");  // development A/B only
   static const bool legacy = variant && variant[0] == 'l';
-  static const bool pair = variant && variant[0] == 'p';
   const bool pdl = !w->fresh;
   const_cast<j4b_qweight*>(w)->fresh = false;
-  if (!legacy && batch <= 4)
-    return pair ? launch_gemv_stream<QT, true, 16, true>(w, x, add, y, batch, sms, stream, peers, grid_out, pdl)
-                : launch_gemv_stream<QT, true, 16>(w, x, add, y, batch, sms, stream, peers, grid_out, pdl);
-  if (!legacy && batch <= 8)
-    return pair ? launch_gemv_stream<QT, false, 16, true>(w, x, add, y, batch, sms, stream, peers, grid_out, pdl)
-                : launch_gemv_stream<QT, false, 16>(w, x, add, y, batch, sms, stream, peers, grid_out, pdl);
+  if (!legacy && batch <= 4) return launch_gemv_stream<QT, true, 16>(w, x, add, y, batch, sms, stream, peers, grid_out, pdl);
+  if (!legacy && batch <= 8) return launch_gemv_stream<QT, false, 16>(w, x, add, y, batch, sms, stream, peers, grid_out, pdl);
   if (batch <= 4) return launch_gemv<QT, 1, true>(w, x, add, y, batch, sms, stream, peers, grid_out, pdl);
   if (batch <= 8) return launch_gemv<QT, 1, false>(w, x, add, y, batch, sms, stream, peers, grid_out, pdl);
   return launch_gemv<QT, 2, false>(w, x, add, y, batch, sms, stream, peers, grid_out, pdl);

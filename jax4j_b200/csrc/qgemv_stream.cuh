@@ -46,21 +46,17 @@ template <int QT, bool PK>
 constexpr int stream_frag_chunk() {
   return PK ? 2048 + (stream_needs_xblk<QT>() ? 512 : 0) : 4096 + (stream_needs_xblk<QT>() ? 1024 : 0);
 }
-// warp pairs (PAIR): per pair two parity slots of one warp's accumulators (kNV floats x 32 lanes)
-template <bool PK, int NW, bool PAIR>
-constexpr int stream_pair_bytes() { return PAIR ? (NW / 2) * 2 * (PK ? 2 : 4) * 32 * 4 : 0; }
 template <int QT, bool PK, int NW>
 constexpr int stream_stages() {
   constexpr int stage = stream_tiles_per_stage<QT>() * GemvTraits<QT>::kChunk;
-  constexpr int r = (stream_smem_budget<NW>() - 8 * stream_frag_chunk<QT, PK>() - stream_pair_bytes<PK, NW, true>() - 512) / stage;
+  constexpr int r = (stream_smem_budget<NW>() - 8 * stream_frag_chunk<QT, PK>() - 512) / stage;
   return r > 16 ? 16 : r;
 }
-// ring | x fragments | pair slots | full[R] | empty[R] mbarriers | seq[R] stage numbers
-template <int QT, bool PK, int NW, bool PAIR = false>
+// ring | x fragments | full[R] | empty[R] mbarriers | seq[R] stage numbers
+template <int QT, bool PK, int NW>
 constexpr int stream_smem_bytes() {
   return stream_stages<QT, PK, NW>() * stream_tiles_per_stage<QT>() * GemvTraits<QT>::kChunk +
-         8 * stream_frag_chunk<QT, PK>() + stream_pair_bytes<PK, NW, PAIR>() + 2 * 8 * stream_stages<QT, PK, NW>() +
-         4 * stream_stages<QT, PK, NW>();
+         8 * stream_frag_chunk<QT, PK>() + 2 * 8 * stream_stages<QT, PK, NW>() + 4 * stream_stages<QT, PK, NW>();
 }
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
@@ -192,10 +188,7 @@ __device__ __forceinline__ void stream_coord(int lane, int cc, int& row, int& bc
   }
 }
 
-// PAIR: the two warps of a pair share each tile (chunks 0-3 and 4-7); the second warp hands its
-// partial to the first through a parity slot in shared memory and one named barrier per tile
-// (barrier 2 + pair), so the first adds the halves in a fixed order.
-template <int QT, bool PK, int NW, bool PAIR>
+template <int QT, bool PK, int NW>
 __global__ void __launch_bounds__(stream_threads<NW>(), NW == 8 ? 2 : 1) qgemv_stream_kernel(GemvArgs a) {
   using T = GemvTraits<QT>;
   constexpr int R = stream_stages<QT, PK, NW>();
@@ -208,8 +201,7 @@ __global__ void __launch_bounds__(stream_threads<NW>(), NW == 8 ? 2 : 1) qgemv_s
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* ring = smem;
   uint8_t* frag = smem + R * kStage;
-  float* pair_slots = reinterpret_cast<float*>(frag + 8 * kFrag);
-  uint64_t* full = reinterpret_cast<uint64_t*>(frag + 8 * kFrag + stream_pair_bytes<PK, NW, PAIR>());
+  uint64_t* full = reinterpret_cast<uint64_t*>(frag + 8 * kFrag);
   uint64_t* empty = full + R;
   volatile int* seq = reinterpret_cast<volatile int*>(empty + R);  // stage last issued per slot
 
@@ -228,7 +220,7 @@ __global__ void __launch_bounds__(stream_threads<NW>(), NW == 8 ? 2 : 1) qgemv_s
   if (threadIdx.x == 0) {
     for (int s = 0; s < R; s++) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], PAIR ? 2 * kU : kU);
+      mbar_init(&empty[s], kU);
       seq[s] = -1;
     }
     fence_mbar_init();
@@ -271,12 +263,7 @@ __global__ void __launch_bounds__(stream_threads<NW>(), NW == 8 ? 2 : 1) qgemv_s
     if (warp < nchunks) stream_prep_x<QT, PK>(a, kc0, warp, lane, frag);
     compute_warps_sync<NW>();
 
-    constexpr int kUnits = PAIR ? NW / 2 : NW;  // tile owners: pairs or warps
-    const int owner = PAIR ? warp >> 1 : warp, half = PAIR ? warp & 1 : 0;
-    const int c_begin = PAIR ? 4 * half : 0;
-    const int c_end = PAIR ? min(nchunks, 4 * half + 4) : nchunks;
-    int parity = 0;
-    for (int u = owner; u < ntiles; u += kUnits) {
+    for (int u = warp; u < ntiles; u += NW) {
       const int st = u / kU, slot = st % R;
       if (!failed && !(wait_issued(seq + slot, st) && mbar_wait_bounded(&full[slot], (uint32_t)((st / R) & 1))))
         failed = true;
@@ -287,7 +274,7 @@ __global__ void __launch_bounds__(stream_threads<NW>(), NW == 8 ? 2 : 1) qgemv_s
       if (!failed) {
         const uint8_t* base = ring + slot * kStage + (u % kU) * chunk_bytes;
 #pragma unroll 1
-        for (int c = c_begin; c < c_end; c++) {
+        for (int c = 0; c < nchunks; c++) {
           const uint8_t* fc = frag + c * kFrag;
           if constexpr (PK) {
             uint32_t bp[8][2];
@@ -346,18 +333,6 @@ __global__ void __launch_bounds__(stream_threads<NW>(), NW == 8 ? 2 : 1) qgemv_s
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[slot]);  // this warp is done reading the stage
-      if constexpr (PAIR) {
-        float* ps = pair_slots + ((owner * 2 + parity) * kNV) * 32;
-        if (half) {
-#pragma unroll
-          for (int i = 0; i < kNV; i++) ps[i * 32 + lane] = acc[i];
-        }
-        asm volatile("bar.sync %0, 64;" ::"r"(2 + owner) : "memory");
-        parity ^= 1;
-        if (half) continue;
-#pragma unroll
-        for (int i = 0; i < kNV; i++) acc[i] += ps[i * 32 + lane];
-      }
       if (failed) continue;
 
       const int64_t tile = tile0 + u;
@@ -365,7 +340,6 @@ __global__ void __launch_bounds__(stream_threads<NW>(), NW == 8 ? 2 : 1) qgemv_s
         float* part = a.partials + ((int64_t)split * a.rt + tile) * 256;
 #pragma unroll
         for (int i = 0; i < kNV; i++) __stcg(part + i * 32 + lane, acc[i]);
-        if (a.defer_fold) continue;
         __syncwarp();  // every lane's partial store precedes lane 0's release
         unsigned last = 0;
         if (lane == 0) last = arrive_acq_rel(a.arrivals + tile) == (unsigned)(a.ksplit - 1);
@@ -420,48 +394,15 @@ __global__ void __launch_bounds__(stream_threads<NW>(), NW == 8 ? 2 : 1) qgemv_s
   signal_peers(a);
 }
 
-// y[b, r] = sum over splits of the streaming kernel's partials, in split order (+ add). One thread
-// per output, rows fastest. Launched right behind the streaming kernel with programmatic
-// dependent launch: its CTAs (small, no shared memory) sit next to the GEMV's while it runs, and
-// it lets the next kernel in the stream launch at once, so the next GEMV's CTAs take each SM as
-// soon as this GEMV's CTA there exits and start streaming their weights during this fold.
-template <bool PK>
-__global__ void __launch_bounds__(256) qgemv_fold_kernel(const float* __restrict__ partials, const float* __restrict__ add,
-                                                         float* __restrict__ y, int64_t rows, int64_t rt, int ksplit,
-                                                         int batch) {
-  pdl_launch_dependents();
-  pdl_wait();
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= (int64_t)batch * rows) return;
-  const int bcol = (int)(i / rows);
-  const int64_t r = i % rows;
-  const int row = (int)(r & 15);
-  const float* p = partials + (r >> 4) * 256 + (PK ? out_index_pk(row, bcol) : out_index(row, bcol));
-  const int64_t stride = rt * 256;
-  float tot = 0.f;
-  int sp = 0;
-  for (; sp + 4 <= ksplit; sp += 4) {
-    const float v0 = __ldcg(p + sp * stride), v1 = __ldcg(p + (sp + 1) * stride);
-    const float v2 = __ldcg(p + (sp + 2) * stride), v3 = __ldcg(p + (sp + 3) * stride);
-    tot += v0;
-    tot += v1;
-    tot += v2;
-    tot += v3;
-  }
-  for (; sp < ksplit; sp++) tot += __ldcg(p + sp * stride);
-  if (add) tot += add[i];
-  y[i] = tot;
-}
-
-template <int QT, bool PK, int NW, bool PAIR = false>
+template <int QT, bool PK, int NW>
 cudaError_t launch_gemv_stream(const j4b_qweight* w, const float* x, const float* add, float* y, int batch,
                                int sms, cudaStream_t stream, const GemvPeers* peers, unsigned* grid_out,
                                bool pdl) {
-  constexpr int smem = stream_smem_bytes<QT, PK, NW, PAIR>();
+  constexpr int smem = stream_smem_bytes<QT, PK, NW>();
   static bool attr_set[kMaxDevices] = {};  // function attributes are per device context
   if (w->dev < 0 || w->dev >= kMaxDevices) return cudaErrorInvalidDevice;
   if (!attr_set[w->dev]) {
-    cudaError_t e = cudaFuncSetAttribute(qgemv_stream_kernel<QT, PK, NW, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaError_t e = cudaFuncSetAttribute(qgemv_stream_kernel<QT, PK, NW>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     attr_set[w->dev] = true;
   }
@@ -505,23 +446,5 @@ cudaError_t launch_gemv_stream(const j4b_qweight* w, const float* x, const float
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
   if (grid_out) *grid_out = cfg.gridDim.x;
-  // the separate fold applies to the local GEMV (the all-gather path folds in the kernel, where
-  // its epilogue stores into the peers' buffers)
-  a.defer_fold = (w->ksplit > 1 && !peers) ? 1 : 0;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, qgemv_stream_kernel<QT, PK, NW, PAIR>, a);
-  if (e != cudaSuccess || !a.defer_fold) return e;
-  count_launch();
-  const int64_t n = (int64_t)batch * w->rows;
-  cudaLaunchConfig_t fc = {};
-  fc.gridDim = dim3((unsigned)((n + 255) / 256));
-  fc.blockDim = dim3(256);
-  fc.dynamicSmemBytes = 0;
-  fc.stream = stream;
-  cudaLaunchAttribute fa[1];
-  fa[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  fa[0].val.programmaticStreamSerializationAllowed = 1;
-  fc.attrs = fa;
-  fc.numAttrs = 1;
-  return cudaLaunchKernelEx(&fc, qgemv_fold_kernel<PK>, (const float*)w->partials, add, y, (int64_t)w->rows,
-                            (int64_t)w->rt, (int)w->ksplit, batch);
+  return cudaLaunchKernelEx(&cfg, qgemv_stream_kernel<QT, PK, NW>, a);
 }

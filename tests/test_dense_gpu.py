@@ -81,12 +81,20 @@ def test_matmul_kat_and_random(backend, oracle):
     b = np.float32([[7, 8], [9, 10], [11, 12]])
     c = backend.download(backend.matmul(backend.upload(a, a.shape), backend.upload(b, b.shape)))
     assert np.array_equal(c, np.float32([[58, 64], [139, 154]]))  # CudaTensorTest.java:27-33
-    for (m, k, n) in [(256, 784, 512), (256, 512, 10), (784, 256, 512), (5, 7, 3)]:
+    # the MLP's shapes, including the skinny ones (n = 10: the logits layer and its weight
+    # gradient; k = 10: the gradient into the hidden layer), and ragged small ones
+    for (m, k, n) in [(256, 784, 512), (256, 512, 10), (512, 256, 10), (256, 10, 512), (784, 256, 512),
+                      (5, 7, 3), (33, 100, 32), (1, 1000, 1), (70, 33, 65)]:
         a = rng(m).standard_normal((m, k)).astype(np.float32)
         b = rng(n).standard_normal((k, n)).astype(np.float32)
         got = backend.download(backend.matmul(backend.upload(a, a.shape), backend.upload(b, b.shape)))
         want = a.astype(np.float64) @ b.astype(np.float64)
         assert np.abs(got - want).max() / np.abs(want).max() <= 1e-4
+    for (bt, m, k, n) in [(3, 4, 5, 6), (2, 40, 300, 7)]:
+        a = rng(m).standard_normal((bt, m, k)).astype(np.float32)
+        b = rng(n).standard_normal((bt, k, n)).astype(np.float32)
+        got = backend.download(backend.batched_matmul(backend.upload(a, a.shape), backend.upload(b, b.shape)))
+        np.testing.assert_allclose(got, oracle.batched_matmul(a, b), rtol=1e-4, atol=1e-4)
     a = rng(9).standard_normal((3, 4, 5)).astype(np.float32)
     b = rng(8).standard_normal((3, 5, 6)).astype(np.float32)
     got = backend.download(backend.batched_matmul(backend.upload(a, a.shape),
