@@ -199,13 +199,18 @@ int j4b_quant_upload_device(int dev, j4b_buf blocks, size_t bytes, int ggml_type
 int j4b_quant_free(j4b_qweight_t w);
 int j4b_quant_shape(j4b_qweight_t w, int* ggml_type, int64_t* rows, int64_t* cols);
 /* quantMatvec / quantMatvecAdd (QuantizedOps.java:26-30), batched: x [batch, cols] f32,
- * add [batch, rows] f32 or 0, y [batch, rows] f32. batch = 1 is the reference call. */
+ * add [batch, rows] f32 or 0, y [batch, rows] f32. batch = 1 is the reference call. Up to 16
+ * rows of x: the dequant-GEMV (fp16 fragments of the codes, x split into fp16 hi + lo, fp32
+ * accumulation); more rows (Q8_0, Q4_0, Q4_K): one pass of the fused dequant-GEMM below in its
+ * fp32-accurate mode. Either way relative error ~1e-5 (bar 1e-4). */
 int j4b_quant_matvec(j4b_qweight_t w, j4b_buf x, j4b_buf add, j4b_buf y, int64_t batch,
                      j4b_stream s);
 /* Prefill projection (no reference counterpart: the reference only has the rank-1 quantMatvec):
  * y [m, rows] = x [m, cols] . W^T, f32 row-major, on the tcgen05 tensor cores. precision
- * 1 = bf16 operands (rel 1e-2); 0 or 2 = 3-term bf16 split of both operands (rel 1e-4). The
- * weight is decoded bit-exactly (as quantGatherRow) into stream-ordered scratch first. */
+ * 1 = bf16 operands (rel 1e-2); 0 or 2 = 3-term bf16 split of both operands (rel 1e-4). Q8_0,
+ * Q4_0, Q4_K: the weight's blocks are decoded inside the GEMM, into the tensor cores' shared-
+ * memory operand tiles (no dequantised copy); Q6_K, Q2_0: decoded into stream-ordered scratch
+ * first. x is converted to bf16 in stream-ordered scratch. */
 int j4b_quant_gemm(j4b_qweight_t w, j4b_buf x, j4b_buf y, int64_t m, int precision, j4b_stream s);
 /* quantGatherRow (QuantizedOps.java:32-33): bit-exact dequantised row, out [cols] f32. */
 int j4b_quant_gather_row(j4b_qweight_t w, int64_t row, j4b_buf out, j4b_stream s);
