@@ -1870,7 +1870,14 @@ struct Gen {
       if (mx) os << "    float acc = -J4B_INF;\n    if (i < " << istr(v.W) << ") for (long long cta = warp; cta < A.G; cta += kFoldWarps) acc = jmax(acc, (float)pp[cta * " << istr(v.W) << " + i]);\n"
                  << "    fred[warp * 32 + lane] = (double)acc;\n    __syncthreads();\n"
                  << "    float tot = -J4B_INF;\n    for (int w = 0; w < kFoldWarps; ++w) tot = jmax(tot, (float)fred[w * 32 + lane]);\n";
-      else os << "    double acc = 0.0;\n    if (i < " << istr(v.W) << ") for (long long cta = warp; cta < A.G; cta += kFoldWarps) acc += pp[cta * " << istr(v.W) << " + i];\n"
+      else os << "    double acc = 0.0;\n    if (i < " << istr(v.W) << ") {\n"
+              << "      const double* q = pp + i;\n      long long cta = warp;\n"
+              << "      // four loads in flight, the additions in the same (ascending CTA) order\n"
+              << "      for (; cta + 3 * kFoldWarps < A.G; cta += 4 * kFoldWarps) {\n"
+              << "        const double v0 = q[cta * " << istr(v.W) << "], v1 = q[(cta + kFoldWarps) * " << istr(v.W) << "];\n"
+              << "        const double v2 = q[(cta + 2 * kFoldWarps) * " << istr(v.W) << "], v3 = q[(cta + 3 * kFoldWarps) * " << istr(v.W) << "];\n"
+              << "        acc += v0; acc += v1; acc += v2; acc += v3;\n      }\n"
+              << "      for (; cta < A.G; cta += kFoldWarps) acc += q[cta * " << istr(v.W) << "];\n    }\n"
               << "    fred[warp * 32 + lane] = acc;\n    __syncthreads();\n"
               << "    double tot = 0.0;\n    for (int w = 0; w < kFoldWarps; ++w) tot += fred[w * 32 + lane];\n";
       os << "    __syncthreads();\n    p" << b << " = (float)tot;\n  }\n";
@@ -1884,7 +1891,11 @@ struct Gen {
            << "    for (int o = 16; o > 0; o >>= 1) { float v2 = __shfl_xor_sync(0xffffffffu, bv, o); long long i2 = __shfl_xor_sync(0xffffffffu, bi, o); rmax_combine(bv, bi, v2, i2); }\n"
            << "    p" << b << " = bv;\n  }\n";
       else
-        os << "    double acc = 0.0;\n    for (long long cta = lane; cta < A.G; cta += 32) acc += pp[cta];\n"
+        os << "    double acc = 0.0;\n    long long cta = lane;\n"
+           << "    for (; cta + 96 < A.G; cta += 128) {\n"
+           << "      const double v0 = pp[cta], v1 = pp[cta + 32], v2 = pp[cta + 64], v3 = pp[cta + 96];\n"
+           << "      acc += v0; acc += v1; acc += v2; acc += v3;\n    }\n"
+           << "    for (; cta < A.G; cta += 32) acc += pp[cta];\n"
            << "    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);\n"
            << "    p" << b << " = (float)acc;\n  }\n";
     } else if (gc.kind == G_EXPR) {
