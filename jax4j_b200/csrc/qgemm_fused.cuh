@@ -15,7 +15,7 @@
 //              releases each stage with tcgen05.commit;
 //   warps 2-5  epilogue: tcgen05.ld of TMEM lanes 32 (w % 4) .. + 31 (= W rows), 8 tokens at a
 //              time, stores to y;
-//   warps 6-9  decoders: warp d decodes row tiles 2d, 2d + 1 (16 W rows each) of every k-block,
+//   warps 6..  decoders (4 when two CTAs share an SM, else 8): each decodes one or two 16-row tiles of every k-block,
 //              loading the next k-block's bytes before writing the current one; each writes its
 //              part of the stage, fences the generic-proxy writes for the async proxy the tensor
 //              core reads through, and arrives on the stage's `full_a` barrier.
@@ -25,7 +25,12 @@
 // gives up records an error in the weight's status word.
 
 constexpr int kQgBM = 128, kQgBK = 64;
-constexpr int kQgThreads = 10 * 32;
+// decode warps: 4 (two 16-row tiles each) when two CTAs share an SM, 8 (one tile each) when a CTA
+// holds the SM alone, so an SM always runs eight decoders
+template <int TERMS, int N, int NH>
+constexpr int qg_decode_warps();
+template <int TERMS, int N, int NH>
+constexpr int qg_threads() { return (6 + qg_decode_warps<TERMS, N, NH>()) * 32; }
 
 // N tokens per MMA, NH accumulators of N columns each per CTA (NH = 2, N = 256: 512 tokens in bf16
 // mode, the whole TMEM, one CTA per SM; N = 64: decode-time batches).
@@ -39,6 +44,8 @@ template <int TERMS, int N, int NH>
 constexpr uint32_t qg_stage_bytes() { return (TERMS == 3 ? 2u : 1u) * (kQgABytes + qg_b_bytes<N, NH>()); }
 template <int TERMS, int N, int NH>
 constexpr int qg_min_blocks() { return (TERMS == 1 && N * NH <= 256) ? 2 : 1; }
+template <int TERMS, int N, int NH>
+constexpr int qg_decode_warps() { return qg_min_blocks<TERMS, N, NH>() == 2 ? 4 : 8; }
 
 struct QgArgs {
   const uint8_t* data;
@@ -183,7 +190,7 @@ __device__ __forceinline__ void qg_store(const QgBytes& b, int kb, int lane, uin
 }
 
 template <int QT, int TERMS, int N, int NH>
-__global__ void __launch_bounds__(kQgThreads, qg_min_blocks<TERMS, N, NH>())
+__global__ void __launch_bounds__(qg_threads<TERMS, N, NH>(), qg_min_blocks<TERMS, N, NH>())
     qgemm_fused_kernel(const __grid_constant__ CUtensorMap x_hi, const __grid_constant__ CUtensorMap x_lo, QgArgs p) {
   constexpr int kN = N;                // tokens per MMA
   constexpr int kBN = NH * kN;         // tokens per tile (TMEM columns)
@@ -215,7 +222,7 @@ __global__ void __launch_bounds__(kQgThreads, qg_min_blocks<TERMS, N, NH>())
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      bar_init(&full_a[s], 4);
+      bar_init(&full_a[s], qg_decode_warps<TERMS, N, NH>());
       bar_init(&full_b[s], 1);
       bar_init(&empty[s], 1);
     }
@@ -302,28 +309,29 @@ __global__ void __launch_bounds__(kQgThreads, qg_min_blocks<TERMS, N, NH>())
       }
     }
   } else {
-    // decoders: warp d owns row tiles 2d, 2d + 1 of the 128-row A tile
+    // decoders: warp d owns row tiles [kT d, kT (d + 1)) of the 128-row A tile
+    constexpr int kT = 8 / qg_decode_warps<TERMS, N, NH>();
     const int d = warp - 6;
-    const int64_t tile0 = w0 / 16 + 2 * d;
-    QgBytes cur[2], nxt[2];
-    qg_load<QT>(p, tile0, kb0, lane, cur[0]);
-    qg_load<QT>(p, tile0 + 1, kb0, lane, cur[1]);
+    const int64_t tile0 = w0 / 16 + kT * d;
+    QgBytes cur[kT], nxt[kT];
+#pragma unroll
+    for (int i = 0; i < kT; ++i) qg_load<QT>(p, tile0 + i, kb0, lane, cur[i]);
     for (int kb = 0; kb < nk; ++kb) {
       const int s = kb % kStages, use = kb / kStages;
       if (kb + 1 < nk) {
-        qg_load<QT>(p, tile0, kb0 + kb + 1, lane, nxt[0]);
-        qg_load<QT>(p, tile0 + 1, kb0 + kb + 1, lane, nxt[1]);
+#pragma unroll
+        for (int i = 0; i < kT; ++i) qg_load<QT>(p, tile0 + i, kb0 + kb + 1, lane, nxt[i]);
       }
       if (use > 0 && !bar_wait(&empty[s], (uint32_t)((use - 1) & 1))) ok = false;
       uint8_t* ahi = stage_a(s, 0);
       uint8_t* alo = stage_a(s, 1);
-      qg_store<QT, TERMS>(cur[0], kb0 + kb, lane, ahi, alo, 32 * d);
-      qg_store<QT, TERMS>(cur[1], kb0 + kb, lane, ahi, alo, 32 * d + 16);
+#pragma unroll
+      for (int i = 0; i < kT; ++i) qg_store<QT, TERMS>(cur[i], kb0 + kb, lane, ahi, alo, 16 * (kT * d + i));
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor-core reads
       __syncwarp();
       if (lane == 0) bar_arrive(&full_a[s]);
-      cur[0] = nxt[0];
-      cur[1] = nxt[1];
+#pragma unroll
+      for (int i = 0; i < kT; ++i) cur[i] = nxt[i];
     }
   }
   if (!ok) atomicExch(p.status, 1);
@@ -375,6 +383,6 @@ cudaError_t launch_qgemm_fused(const j4b_qweight* w, const CUtensorMap& xh, cons
   p.status = w->status;
   const int64_t tiles = ((w->rows + kQgBM - 1) / kQgBM) * p.splits * (((int64_t)m + kBN - 1) / kBN);
   if (tiles > 0x7fffffffLL) return cudaErrorInvalidValue;
-  qgemm_fused_kernel<QT, TERMS, N, NH><<<(unsigned)tiles, kQgThreads, smem, stream>>>(xh, xl, p);
+  qgemm_fused_kernel<QT, TERMS, N, NH><<<(unsigned)tiles, qg_threads<TERMS, N, NH>(), smem, stream>>>(xh, xl, p);
   return cudaGetLastError();
 }

@@ -857,7 +857,8 @@ int quant_gemm_fused(const j4b_qweight* w, const float* x, float* y, const float
   const int nk = (int)(kp / 64);
   const int n_tiles = (int)((w->rows + kQgBM - 1) / kQgBM);
   const int N = m <= 64 ? 64 : (terms == 1 ? 256 : 128);
-  const int NH = m > 256 ? 2 : 1;
+  static const bool one_acc = getenv("J4B_QGEMM_NH1") != nullptr;  // development A/B only
+  const int NH = (m > 256 && !one_acc) ? 2 : 1;
   const int64_t t_tiles = (m + (int64_t)N * NH - 1) / ((int64_t)N * NH);
   int splits = 1;
   if ((int64_t)n_tiles * t_tiles < sms) splits = (int)std::min<int64_t>((sms + n_tiles * t_tiles - 1) / (n_tiles * t_tiles), std::max(1, nk / 8));
