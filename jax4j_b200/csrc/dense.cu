@@ -376,7 +376,24 @@ __global__ void __launch_bounds__(256) gemm_narrow_n_kernel(const float* __restr
   float acc[32];
 #pragma unroll
   for (int j = 0; j < 32; j++) acc[j] = 0.f;
-  for (int64_t p = lane; p < K; p += 32) {
+  int64_t p = lane;
+  for (; p + 96 < K; p += 128) {  // four rows of B in flight, products added in ascending p
+    float av[4];
+#pragma unroll
+    for (int u = 0; u < 4; u++) av[u] = __ldg(a + p + 32 * u);
+#pragma unroll
+    for (int j = 0; j < 32; j++) {
+      if (j < N) {
+        const float b0 = __ldg(b + (p) * N + j), b1 = __ldg(b + (p + 32) * N + j);
+        const float b2 = __ldg(b + (p + 64) * N + j), b3 = __ldg(b + (p + 96) * N + j);
+        acc[j] = fmaf(av[0], b0, acc[j]);
+        acc[j] = fmaf(av[1], b1, acc[j]);
+        acc[j] = fmaf(av[2], b2, acc[j]);
+        acc[j] = fmaf(av[3], b3, acc[j]);
+      }
+    }
+  }
+  for (; p < K; p += 32) {
     const float av = __ldg(a + p);
     const float* br = b + p * N;
 #pragma unroll

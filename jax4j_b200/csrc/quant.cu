@@ -860,8 +860,19 @@ int quant_gemm_fused(const j4b_qweight* w, const float* x, float* y, const float
   static const bool one_acc = getenv("J4B_QGEMM_NH1") != nullptr;  // development A/B only
   const int NH = (m > 256 && !one_acc) ? 2 : 1;
   const int64_t t_tiles = (m + (int64_t)N * NH - 1) / ((int64_t)N * NH);
+  // K splits: the count (at most 9, each split at least 8 k-blocks) whose CTAs fill the SMs' slots
+  // best over whole waves, the fewest among near-equals (fewer partials to fold)
+  const int64_t slots = (int64_t)sms * ((terms == 1 && N * NH <= 256) ? 2 : 1);
   int splits = 1;
-  if ((int64_t)n_tiles * t_tiles < sms) splits = (int)std::min<int64_t>((sms + n_tiles * t_tiles - 1) / (n_tiles * t_tiles), std::max(1, nk / 8));
+  double best = 0.0;
+  for (int sp = 1; sp <= std::min(9, std::max(1, nk / 8)); ++sp) {
+    const int64_t ctas = (int64_t)n_tiles * t_tiles * sp;
+    const double eff = (double)ctas / (double)(((ctas + slots - 1) / slots) * slots);
+    if (eff > best + 0.02) {
+      best = eff;
+      splits = sp;
+    }
+  }
   const int kb_per = (nk + splits - 1) / splits;
   splits = (nk + kb_per - 1) / kb_per;
   const size_t xbytes = (size_t)(m * kp) * 2;
