@@ -860,12 +860,13 @@ int quant_gemm_fused(const j4b_qweight* w, const float* x, float* y, const float
   static const bool one_acc = getenv("J4B_QGEMM_NH1") != nullptr;  // development A/B only
   const int NH = (m > 256 && !one_acc) ? 2 : 1;
   const int64_t t_tiles = (m + (int64_t)N * NH - 1) / ((int64_t)N * NH);
-  // K splits: the count (at most 9, each split at least 8 k-blocks) whose CTAs fill the SMs' slots
-  // best over whole waves, the fewest among near-equals (fewer partials to fold)
+  // K splits: the count (at most 9, each split at least 8 k-blocks, partials at most 24 MB) whose
+  // CTAs fill the SMs' slots best over whole waves, the fewest among near-equals
   const int64_t slots = (int64_t)sms * ((terms == 1 && N * NH <= 256) ? 2 : 1);
   int splits = 1;
   double best = 0.0;
   for (int sp = 1; sp <= std::min(9, std::max(1, nk / 8)); ++sp) {
+    if (sp > 1 && m * w->rows * 4 * sp > ((int64_t)24 << 20)) break;  // partials stay small next to W
     const int64_t ctas = (int64_t)n_tiles * t_tiles * sp;
     const double eff = (double)ctas / (double)(((ctas + slots - 1) / slots) * slots);
     if (eff > best + 0.02) {
