@@ -2,32 +2,33 @@
 // j4b::<anonymous>; it reuses that file's fragment decoders tile_compute / tile_compute_pk and
 // its bulk-copy and mbarrier helpers).
 //
-// Shape of one launch: one CTA per SM (16 compute warps + 1 producer warp). A CTA owns one
-// 1024-column K range ("split") of a contiguous run of 16-row tiles:
-//   - the producer warp: one elected lane streams the run's tile chunks (contiguous in the
-//     split-major layout) into a ring of shared-memory slots with 1-D bulk copies, each slot's
-//     copy completing on its `full` mbarrier, and refills a slot once the tile(s) in it are done
-//     (`empty`). The first ring's worth is issued before the dependency wait (weights are
-//     immutable once uploaded; the first GEMV after an upload is launched without programmatic
-//     dependent launch, so that one waits).
-//   - compute warp w takes 128-column chunk c = w % 8 of the split and builds that chunk's x
-//     fragments (fp16 hi / lo) in its registers straight from global memory, once; the warps
-//     w / 8 = 0 and 1 take alternate tiles. For each tile the eight warps of its stream multiply
-//     their chunk in parallel and hand their partial sums over in shared memory; the eighth to
-//     arrive (a per-tile counter) adds the eight chunks in chunk order, releases the slot, and
-//     finishes the tile. No block barrier in the main loop.
-//   - split-K: the finishing warp stores the tile's split partial into the weight's scratch, and
-//     the warp whose arrival completes the tile's counter (one acquire-release atomic) adds the
-//     splits in split order (deterministic) and writes y (+ add); with one split the finishing
-//     warp writes y directly.
+// Shape of one launch: one CTA per SM. With 8 compute warps the CTA takes at most half of an SM
+// (<= 112 KB of shared memory, 288 threads, <= 112 registers per thread), so that under
+// programmatic dependent launch the next GEMV's CTAs are resident and already streaming their
+// weights while this launch's CTAs finish their last tiles and their split-K folds; with 16 it
+// holds the whole SM with a deeper ring. A CTA owns one 1024-column K range ("split")
+// of a contiguous run of 16-row tiles:
+//   - the last warp is the producer: one elected lane streams the run's tile chunks (contiguous in the
+//     split-major layout) into a ring of shared-memory stages with 1-D bulk copies, each stage
+//     completing on its `full` mbarrier; it refills a stage once the warps that read it have
+//     arrived on its `empty` mbarrier. The first ring's worth is issued before the dependency
+//     wait (weights are immutable once uploaded).
+//   - the compute warps first turn x's 1024-column slice into fp16 hi/lo mma fragments in shared memory
+//     (warp w converts 128-column chunk w), then each warp takes whole tiles round-robin and
+//     walks the tile's 8 chunks itself, so a tile's partial sum over the split never leaves the
+//     warp's registers: no block barrier and no cross-warp reduction in the main loop.
+//   - split-K: a warp stores its tile's partial into the weight's scratch, and the warp whose
+//     arrival completes the tile's counter adds the splits in split order (deterministic) and
+//     writes y (+ add); with one split the warp writes y directly.
 // Every mbarrier wait is bounded (j4b_wait.cuh); on a timeout the CTA records an error in the
 // weight's status word, lets every copy still in flight land, and returns.
 
-// NW compute warps (a multiple of 8: one warp per 128-column chunk per tile stream) + 1 producer.
+// NW compute warps + 1 producer warp. NW = 8: at most half an SM (112 KB of shared memory), so
+// two launches' CTAs co-reside; NW = 16: one CTA per SM with a deeper ring.
 template <int NW>
 constexpr int stream_threads() { return (NW + 1) * 32; }
 template <int NW>
-constexpr int stream_smem_budget() { return 220 * 1024; }
+constexpr int stream_smem_budget() { return NW == 8 ? 112 * 1024 : 220 * 1024; }
 
 template <int QT>
 constexpr bool stream_needs_xblk() {
@@ -38,27 +39,33 @@ template <int QT>
 constexpr int stream_tiles_per_stage() {
   return GemvTraits<QT>::kChunk <= 5000 ? 4 : (GemvTraits<QT>::kChunk <= 10000 ? 2 : 1);
 }
-// Shared-memory bytes of one ring slot: its tile chunks, plus for each of them the eight chunk
-// partials (kNV floats x 32 lanes each) the tile's warps hand to the warp that adds them.
+// Shared-memory bytes of one 128-column chunk's x fragments: packed (batch <= 4) 4 x 16 bytes
+// per lane of B fragments (+ 16 bytes of x block sums), unpacked 8 x 16 bytes (hi, lo of each
+// k-step) (+ 32 bytes of block sums).
 template <int QT, bool PK>
-constexpr int stream_slot_bytes() {
-  return stream_tiles_per_stage<QT>() * (GemvTraits<QT>::kChunk + 8 * (PK ? 2 : 4) * 32 * 4);
+constexpr int stream_frag_chunk() {
+  return PK ? 2048 + (stream_needs_xblk<QT>() ? 512 : 0) : 4096 + (stream_needs_xblk<QT>() ? 1024 : 0);
 }
 template <int QT, bool PK, int NW>
 constexpr int stream_stages() {
-  constexpr int r = (stream_smem_budget<NW>() - 1024) / stream_slot_bytes<QT, PK>();
+  constexpr int stage = stream_tiles_per_stage<QT>() * GemvTraits<QT>::kChunk;
+  constexpr int r = (stream_smem_budget<NW>() - 8 * stream_frag_chunk<QT, PK>() - 512) / stage;
   return r > 16 ? 16 : r;
 }
-// ring of tile chunks | chunk partials | full[R] | empty[R] mbarriers | seq[R] stage numbers |
-// cnt[R * tiles per stage] chunk arrivals
+// ring | x fragments | full[R] | empty[R] mbarriers | seq[R] stage numbers
 template <int QT, bool PK, int NW>
 constexpr int stream_smem_bytes() {
-  return stream_stages<QT, PK, NW>() * stream_slot_bytes<QT, PK>() + 2 * 8 * stream_stages<QT, PK, NW>() +
-         4 * stream_stages<QT, PK, NW>() + 4 * stream_stages<QT, PK, NW>() * stream_tiles_per_stage<QT>();
+  return stream_stages<QT, PK, NW>() * stream_tiles_per_stage<QT>() * GemvTraits<QT>::kChunk +
+         8 * stream_frag_chunk<QT, PK>() + 2 * 8 * stream_stages<QT, PK, NW>() + 4 * stream_stages<QT, PK, NW>();
 }
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+// Barrier 1 over the compute warps only (the producer warp never takes it).
+template <int NW>
+__device__ __forceinline__ void compute_warps_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(NW * 32) : "memory");
 }
 // Waits (bounded) until the producer has issued stage `st` into its slot: only then is the slot's
 // `full` barrier on the phase of that stage, so its parity identifies the stage. (A warp can reach
@@ -81,22 +88,13 @@ __device__ __forceinline__ unsigned arrive_acq_rel(unsigned* ctr) {
   return old;
 }
 
-// x fragments of one 128-column chunk (columns [kc0 + 128c, kc0 + 128c + 128) of every batch row,
-// zeros past K and past the batch), built in this warp's registers straight from global memory:
-// fp16 hi / lo B fragments per k-step and, for the formats whose codes carry an offset, the block
-// sums of the represented x (hi + lo) for the output columns this lane holds.
+// Warp `c` converts x's columns [kc0 + 128c, kc0 + 128c + 128) of every batch row into the
+// chunk's fragment block (columns past K and rows past the batch are zeros).
 template <int QT, bool PK>
-struct StreamX {
-  static constexpr int kXB = kXBlocks<QT>;
-  uint32_t hi[PK ? 1 : 1][8][2];  // packed: lane group g holds batch g / 2, hi for even g, lo for odd g
-  uint32_t lo[PK ? 1 : 1][8][2];  // unpacked only
-  float blk[kXB][2];              // unpacked: batch 2t, 2t + 1; packed: [q][0] = batch t
-};
-
-template <int QT, bool PK>
-__device__ __forceinline__ void stream_x_regs(const GemvArgs& a, int64_t kc0, int c, int lane, StreamX<QT, PK>& X) {
+__device__ __forceinline__ void stream_prep_x(const GemvArgs& a, int64_t kc0, int c, int lane, uint8_t* frag) {
   const int g = lane >> 2, t = lane & 3;
   constexpr int kXB = kXBlocks<QT>;
+  uint8_t* dst = frag + c * stream_frag_chunk<QT, PK>();
   const int xrow = PK ? (g >> 1) : g;
   const bool row_ok = xrow < a.batch;
   const float* xr = a.x + (int64_t)xrow * a.cols;
@@ -109,8 +107,8 @@ __device__ __forceinline__ void stream_x_regs(const GemvArgs& a, int64_t kc0, in
     p0[j] = ok ? __ldg(reinterpret_cast<const float2*>(xr + k)) : make_float2(0.f, 0.f);
     p1[j] = ok ? __ldg(reinterpret_cast<const float2*>(xr + k + 8)) : make_float2(0.f, 0.f);
   }
+  uint32_t hi[8][2], lo[8][2];
   float xs_hi[8], xs_lo[8];
-  const bool odd = g & 1;
 #pragma unroll
   for (int j = 0; j < 8; j++) {
     __half2 h0 = __floats2half2_rn(p0[j].x, p0[j].y);
@@ -119,42 +117,60 @@ __device__ __forceinline__ void stream_x_regs(const GemvArgs& a, int64_t kc0, in
     __half2 l0 = __floats2half2_rn(p0[j].x - f0.x, p0[j].y - f0.y);
     __half2 l1 = __floats2half2_rn(p1[j].x - f1.x, p1[j].y - f1.y);
     const float2 g0 = __half22float2(l0), g1 = __half22float2(l1);
-    const uint32_t hw0 = *reinterpret_cast<uint32_t*>(&h0), hw1 = *reinterpret_cast<uint32_t*>(&h1);
-    const uint32_t lw0 = *reinterpret_cast<uint32_t*>(&l0), lw1 = *reinterpret_cast<uint32_t*>(&l1);
-    if constexpr (PK) {
-      X.hi[0][j][0] = odd ? lw0 : hw0;
-      X.hi[0][j][1] = odd ? lw1 : hw1;
-    } else {
-      X.hi[0][j][0] = hw0;
-      X.hi[0][j][1] = hw1;
-      X.lo[0][j][0] = lw0;
-      X.lo[0][j][1] = lw1;
-    }
+    hi[j][0] = *reinterpret_cast<uint32_t*>(&h0);
+    hi[j][1] = *reinterpret_cast<uint32_t*>(&h1);
+    lo[j][0] = *reinterpret_cast<uint32_t*>(&l0);
+    lo[j][1] = *reinterpret_cast<uint32_t*>(&l1);
     xs_hi[j] = (f0.x + f0.y) + (f1.x + f1.y);
     xs_lo[j] = (g0.x + g0.y) + (g1.x + g1.y);
   }
+  if constexpr (PK) {
+    // lane group g carries batch g / 2: its hi part for even g, its lo part for odd g
+    const bool odd = g & 1;
 #pragma unroll
-  for (int q = 0; q < kXB; q++) X.blk[q][0] = X.blk[q][1] = 0.f;
+    for (int jj = 0; jj < 4; jj++) {
+      const uint4 v = odd ? make_uint4(lo[2 * jj][0], lo[2 * jj][1], lo[2 * jj + 1][0], lo[2 * jj + 1][1])
+                          : make_uint4(hi[2 * jj][0], hi[2 * jj][1], hi[2 * jj + 1][0], hi[2 * jj + 1][1]);
+      *reinterpret_cast<uint4*>(dst + (jj * 32 + lane) * 16) = v;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; j++)
+      *reinterpret_cast<uint4*>(dst + (j * 32 + lane) * 16) = make_uint4(hi[j][0], hi[j][1], lo[j][0], lo[j][1]);
+  }
   if constexpr (stream_needs_xblk<QT>()) {
+    // block sums of the represented x (hi + lo) for the output columns this lane holds
+    float sums[kXB][2];
 #pragma unroll
     for (int q = 0; q < kXB; q++) {
       constexpr int kSteps = 8 / kXB;
-      float sum = 0.f;
+      float s = 0.f;
 #pragma unroll
       for (int j = 0; j < kSteps; j++) {
         const int jj = q * kSteps + j;
-        sum += PK ? (odd ? xs_lo[jj] : xs_hi[jj]) : xs_hi[jj] + xs_lo[jj];
+        s += PK ? ((g & 1) ? xs_lo[jj] : xs_hi[jj]) : xs_hi[jj] + xs_lo[jj];
       }
-      sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-      sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-      const float s0 = __shfl_sync(0xffffffffu, sum, 4 * (2 * t));
-      const float s1 = __shfl_sync(0xffffffffu, sum, 4 * (2 * t + 1));
-      if constexpr (PK) {
-        X.blk[q][0] = s0 + s1;  // batch t: hi + lo sums
-      } else {
-        X.blk[q][0] = s0;  // batch 2t
-        X.blk[q][1] = s1;  // batch 2t + 1
+      s += __shfl_xor_sync(0xffffffffu, s, 1);
+      s += __shfl_xor_sync(0xffffffffu, s, 2);
+      sums[q][0] = __shfl_sync(0xffffffffu, s, 4 * (2 * t));
+      sums[q][1] = __shfl_sync(0xffffffffu, s, 4 * (2 * t + 1));
+    }
+    if constexpr (PK) {
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      float* vp = reinterpret_cast<float*>(&v);
+#pragma unroll
+      for (int q = 0; q < kXB; q++) vp[q] = sums[q][0] + sums[q][1];  // batch t: hi + lo sums
+      *reinterpret_cast<float4*>(dst + 2048 + lane * 16) = v;
+    } else {
+      float4 v[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
+      float* vp = reinterpret_cast<float*>(v);
+#pragma unroll
+      for (int q = 0; q < kXB; q++) {
+        vp[2 * q] = sums[q][0];      // batch 2t
+        vp[2 * q + 1] = sums[q][1];  // batch 2t + 1
       }
+      *reinterpret_cast<float4*>(dst + 4096 + lane * 16) = v[0];
+      *reinterpret_cast<float4*>(dst + 4096 + 512 + lane * 16) = v[1];
     }
   }
 }
@@ -173,21 +189,21 @@ __device__ __forceinline__ void stream_coord(int lane, int cc, int& row, int& bc
 }
 
 template <int QT, bool PK, int NW>
-__global__ void __launch_bounds__(stream_threads<NW>(), 1) qgemv_stream_kernel(GemvArgs a) {
+__global__ void __launch_bounds__(stream_threads<NW>(), NW == 8 ? 2 : 1) qgemv_stream_kernel(GemvArgs a) {
   using T = GemvTraits<QT>;
   constexpr int R = stream_stages<QT, PK, NW>();
   constexpr int kU = stream_tiles_per_stage<QT>();
   constexpr int kStage = kU * T::kChunk;
+  constexpr int kFrag = stream_frag_chunk<QT, PK>();
   constexpr int kNV = PK ? 2 : 4;  // accumulator floats per lane per tile
-  constexpr int kStreams = NW / 8;  // tile streams: warp w computes chunk w % 8 of stream w / 8's tiles
-  static_assert(R >= 2 && NW % 8 == 0, "ring too small");
+  constexpr int kXB = kXBlocks<QT>;
+  static_assert(R >= 2, "ring too small");
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* ring = smem;
-  float* part = reinterpret_cast<float*>(smem + R * kStage);  // [R * kU][8 chunks][kNV * 32]
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + R * stream_slot_bytes<QT, PK>());
+  uint8_t* frag = smem + R * kStage;
+  uint64_t* full = reinterpret_cast<uint64_t*>(frag + 8 * kFrag);
   uint64_t* empty = full + R;
   volatile int* seq = reinterpret_cast<volatile int*>(empty + R);  // stage last issued per slot
-  unsigned* cnt = reinterpret_cast<unsigned*>(empty + R) + R;       // chunk arrivals per tile slot
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int split = blockIdx.x % a.ksplit;
@@ -204,10 +220,9 @@ __global__ void __launch_bounds__(stream_threads<NW>(), 1) qgemv_stream_kernel(G
   if (threadIdx.x == 0) {
     for (int s = 0; s < R; s++) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kU);  // one arrival per tile: the warp that adds its chunk partials
+      mbar_init(&empty[s], kU);
       seq[s] = -1;
     }
-    for (int s = 0; s < R * kU; s++) cnt[s] = 0u;
     fence_mbar_init();
   }
   __syncthreads();
@@ -241,83 +256,95 @@ __global__ void __launch_bounds__(stream_threads<NW>(), 1) qgemv_stream_kernel(G
     }
   } else {
     // ---------------- compute warps ----------------
-    const int c = warp & 7, h = warp >> 3;
-    const bool active = c < nchunks;
     pdl_launch_dependents();
     pdl_wait();
     int64_t par_off = 0;  // parity half of the gathered buffer (peer all-gather only)
     if (a.nranks > 1) par_off = (int64_t)(*a.step & 1u) * a.half_floats;
-    StreamX<QT, PK> X;
-    if (active) stream_x_regs<QT, PK>(a, kc0, c, lane, X);
+    if (warp < nchunks) stream_prep_x<QT, PK>(a, kc0, warp, lane, frag);
+    compute_warps_sync<NW>();
 
-    for (int u = h; u < ntiles; u += kStreams) {
-      const int st = u / kU, slot = st % R, ts = slot * kU + u % kU;
+    for (int u = warp; u < ntiles; u += NW) {
+      const int st = u / kU, slot = st % R;
       if (!failed && !(wait_issued(seq + slot, st) && mbar_wait_bounded(&full[slot], (uint32_t)((st / R) & 1))))
         failed = true;
       failed = __any_sync(0xffffffffu, failed);  // keep the warp's lanes together
       float acc[kNV];
 #pragma unroll
       for (int i = 0; i < kNV; i++) acc[i] = 0.f;
-      if (!failed && active) {
+      if (!failed) {
         const uint8_t* base = ring + slot * kStage + (u % kU) * chunk_bytes;
-        if constexpr (PK) {
-          float xb[kXBlocks<QT>];
+#pragma unroll 2
+        for (int c = 0; c < nchunks; c++) {
+          const uint8_t* fc = frag + c * kFrag;
+          if constexpr (PK) {
+            uint32_t bp[8][2];
 #pragma unroll
-          for (int q = 0; q < kXBlocks<QT>; q++) xb[q] = X.blk[q][0];
-          float r2[2] = {0.f, 0.f};
-          tile_compute_pk<QT>(base, base + meta_off, c, lane, X.hi[0], xb, r2);
-          acc[0] = r2[0];
-          acc[1] = r2[1];
-        } else {
-          float r4[1][4] = {{0.f, 0.f, 0.f, 0.f}};
-          float xb[1][kXBlocks<QT>][2];
+            for (int jj = 0; jj < 4; jj++) {
+              const uint4 v = *reinterpret_cast<const uint4*>(fc + (jj * 32 + lane) * 16);
+              bp[2 * jj][0] = v.x;
+              bp[2 * jj][1] = v.y;
+              bp[2 * jj + 1][0] = v.z;
+              bp[2 * jj + 1][1] = v.w;
+            }
+            float xb[kXB];
+            if constexpr (stream_needs_xblk<QT>()) {
+              const float4 v = *reinterpret_cast<const float4*>(fc + 2048 + lane * 16);
+              const float vv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-          for (int q = 0; q < kXBlocks<QT>; q++) {
-            xb[0][q][0] = X.blk[q][0];
-            xb[0][q][1] = X.blk[q][1];
+              for (int q = 0; q < kXB; q++) xb[q] = vv[q];
+            } else {
+#pragma unroll
+              for (int q = 0; q < kXB; q++) xb[q] = 0.f;
+            }
+            float r2[2] = {acc[0], acc[1]};
+            tile_compute_pk<QT>(base, base + meta_off, c, lane, bp, xb, r2);
+            acc[0] = r2[0];
+            acc[1] = r2[1];
+          } else {
+            uint32_t bh[1][8][2], bl[1][8][2];
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+              const uint4 v = *reinterpret_cast<const uint4*>(fc + (j * 32 + lane) * 16);
+              bh[0][j][0] = v.x;
+              bh[0][j][1] = v.y;
+              bl[0][j][0] = v.z;
+              bl[0][j][1] = v.w;
+            }
+            float xb[1][kXB][2];
+            if constexpr (stream_needs_xblk<QT>()) {
+              const float4 v0 = *reinterpret_cast<const float4*>(fc + 4096 + lane * 16);
+              const float4 v1 = *reinterpret_cast<const float4*>(fc + 4096 + 512 + lane * 16);
+              const float vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+#pragma unroll
+              for (int q = 0; q < kXB; q++) {
+                xb[0][q][0] = vv[2 * q];
+                xb[0][q][1] = vv[2 * q + 1];
+              }
+            } else {
+#pragma unroll
+              for (int q = 0; q < kXB; q++) xb[0][q][0] = xb[0][q][1] = 0.f;
+            }
+            float r4[1][4] = {{acc[0], acc[1], acc[2], acc[3]}};
+            tile_compute<QT, 1>(base, base + meta_off, c, lane, bh, bl, xb, r4);
+#pragma unroll
+            for (int i = 0; i < 4; i++) acc[i] = r4[0][i];
           }
-          tile_compute<QT, 1>(base, base + meta_off, c, lane, X.hi, X.lo, xb, r4);
-#pragma unroll
-          for (int i = 0; i < 4; i++) acc[i] = r4[0][i];
         }
       }
-      // hand this chunk's partial over; the eighth warp to arrive adds the chunks in order
-      float* pt = part + (int64_t)ts * 8 * kNV * 32;
-#pragma unroll
-      for (int i = 0; i < kNV; i++) pt[(c * kNV + i) * 32 + lane] = acc[i];
       __syncwarp();
-      unsigned last = 0;
-      if (lane == 0) {
-        __threadfence_block();
-        last = atomicAdd(cnt + ts, 1u) == 7u;
-      }
-      last = __shfl_sync(0xffffffffu, last, 0);
-      if (!last) continue;
-      __threadfence_block();
-#pragma unroll
-      for (int i = 0; i < kNV; i++) {
-        float v = 0.f;
-#pragma unroll
-        for (int cc = 0; cc < 8; cc++) v += pt[(cc * kNV + i) * 32 + lane];
-        acc[i] = v;
-      }
-      __syncwarp();
-      if (lane == 0) {
-        cnt[ts] = 0u;
-        mbar_arrive(&empty[slot]);  // the tile is done with its slot (chunks and partials)
-      }
+      if (lane == 0) mbar_arrive(&empty[slot]);  // this warp is done reading the stage
       if (failed) continue;
 
       const int64_t tile = tile0 + u;
       if (a.ksplit > 1) {
-        float* gpart = a.partials + ((int64_t)split * a.rt + tile) * 256;
+        float* part = a.partials + ((int64_t)split * a.rt + tile) * 256;
 #pragma unroll
-        for (int i = 0; i < kNV; i++) __stcg(gpart + i * 32 + lane, acc[i]);
+        for (int i = 0; i < kNV; i++) __stcg(part + i * 32 + lane, acc[i]);
         __syncwarp();  // every lane's partial store precedes lane 0's release
-        unsigned lastk = 0;
-        if (lane == 0) lastk = arrive_acq_rel(a.arrivals + tile) == (unsigned)(a.ksplit - 1);
-        lastk = __shfl_sync(0xffffffffu, lastk, 0);
-        if (!lastk) continue;
+        unsigned last = 0;
+        if (lane == 0) last = arrive_acq_rel(a.arrivals + tile) == (unsigned)(a.ksplit - 1);
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (!last) continue;
         __syncwarp();  // lane 0's acquire precedes every lane's loads of the other partials
         // the last arrival adds the splits in split order, four splits' loads in flight at once
         const float* p0 = a.partials + tile * 256 + lane;
@@ -327,15 +354,15 @@ __global__ void __launch_bounds__(stream_threads<NW>(), 1) qgemv_stream_kernel(G
         for (int sp0 = 0; sp0 < a.ksplit; sp0 += 4) {
           float v[4][kNV];
 #pragma unroll
-          for (int s4 = 0; s4 < 4; s4++)
+          for (int s = 0; s < 4; s++)
 #pragma unroll
             for (int i = 0; i < kNV; i++)
-              v[s4][i] = sp0 + s4 < a.ksplit ? __ldcg(p0 + (sp0 + s4) * sstride + i * 32) : 0.f;
+              v[s][i] = sp0 + s < a.ksplit ? __ldcg(p0 + (sp0 + s) * sstride + i * 32) : 0.f;
 #pragma unroll
-          for (int s4 = 0; s4 < 4; s4++)
+          for (int s = 0; s < 4; s++)
 #pragma unroll
             for (int i = 0; i < kNV; i++)
-              if (sp0 + s4 < a.ksplit) acc[i] += v[s4][i];
+              if (sp0 + s < a.ksplit) acc[i] += v[s][i];
         }
         if (lane == 0) a.arrivals[tile] = 0u;  // ready for the next launch
       }
