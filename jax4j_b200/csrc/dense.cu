@@ -350,28 +350,32 @@ __global__ void random_kernel(int normal, int64_t seed, int64_t counter, float* 
 // layer's n = 10, or its gradient's k = 10): fp32 FMA accumulation in ascending p, batch in
 // grid.y.
 // k <= 32: one thread per output element, the k products summed in order.
+// Operand strides: A(i, p) = A[i * sai + p * sap], B(p, j) = B[p * sbp + j * sbj] (a transposed
+// operand is read in place).
 __global__ void __launch_bounds__(256) gemm_short_k_kernel(const float* __restrict__ A, const float* __restrict__ B,
-                                                           float* __restrict__ C, int64_t M, int64_t K, int64_t N) {
+                                                           float* __restrict__ C, int64_t M, int64_t K, int64_t N,
+                                                           int64_t sai, int64_t sap, int64_t sbp, int64_t sbj) {
   const int64_t bz = blockIdx.y;
   const int64_t idx = (int64_t)blockIdx.x * 256 + threadIdx.x;
   if (idx >= M * N) return;
   const int64_t i = idx / N, j = idx % N;
-  const float* a = A + bz * M * K + i * K;
-  const float* b = B + bz * K * N + j;
+  const float* a = A + bz * M * K + i * sai;
+  const float* b = B + bz * K * N + j * sbj;
   float acc = 0.f;
-  for (int64_t p = 0; p < K; p++) acc = fmaf(__ldg(a + p), __ldg(b + p * N), acc);
+  for (int64_t p = 0; p < K; p++) acc = fmaf(__ldg(a + p * sap), __ldg(b + p * sbp), acc);
   C[bz * M * N + idx] = acc;
 }
 
 // n <= 32: one warp per row of C; lane l takes p = l, l + 32, ... and keeps n partial sums, which
 // the warp adds lane-wise (butterfly), so the sum order is fixed.
 __global__ void __launch_bounds__(256) gemm_narrow_n_kernel(const float* __restrict__ A, const float* __restrict__ B,
-                                                            float* __restrict__ C, int64_t M, int64_t K, int N) {
+                                                            float* __restrict__ C, int64_t M, int64_t K, int N,
+                                                            int64_t sai, int64_t sap, int64_t sbp, int64_t sbj) {
   const int64_t bz = blockIdx.y;
   const int lane = threadIdx.x & 31;
   const int64_t i = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
   if (i >= M) return;
-  const float* a = A + bz * M * K + i * K;
+  const float* a = A + bz * M * K + i * sai;
   const float* b = B + bz * K * N;
   float acc[32];
 #pragma unroll
@@ -380,12 +384,12 @@ __global__ void __launch_bounds__(256) gemm_narrow_n_kernel(const float* __restr
   for (; p + 96 < K; p += 128) {  // four rows of B in flight, products added in ascending p
     float av[4];
 #pragma unroll
-    for (int u = 0; u < 4; u++) av[u] = __ldg(a + p + 32 * u);
+    for (int u = 0; u < 4; u++) av[u] = __ldg(a + (p + 32 * u) * sap);
 #pragma unroll
     for (int j = 0; j < 32; j++) {
       if (j < N) {
-        const float b0 = __ldg(b + (p) * N + j), b1 = __ldg(b + (p + 32) * N + j);
-        const float b2 = __ldg(b + (p + 64) * N + j), b3 = __ldg(b + (p + 96) * N + j);
+        const float b0 = __ldg(b + (p)*sbp + j * sbj), b1 = __ldg(b + (p + 32) * sbp + j * sbj);
+        const float b2 = __ldg(b + (p + 64) * sbp + j * sbj), b3 = __ldg(b + (p + 96) * sbp + j * sbj);
         acc[j] = fmaf(av[0], b0, acc[j]);
         acc[j] = fmaf(av[1], b1, acc[j]);
         acc[j] = fmaf(av[2], b2, acc[j]);
@@ -394,11 +398,11 @@ __global__ void __launch_bounds__(256) gemm_narrow_n_kernel(const float* __restr
     }
   }
   for (; p < K; p += 32) {
-    const float av = __ldg(a + p);
-    const float* br = b + p * N;
+    const float av = __ldg(a + p * sap);
+    const float* br = b + p * sbp;
 #pragma unroll
     for (int j = 0; j < 32; j++)
-      if (j < N) acc[j] = fmaf(av, __ldg(br + j), acc[j]);
+      if (j < N) acc[j] = fmaf(av, __ldg(br + j * sbj), acc[j]);
   }
   float mine = 0.f;
 #pragma unroll
@@ -416,7 +420,8 @@ __global__ void __launch_bounds__(256) gemm_narrow_n_kernel(const float* __restr
 // fp32 FMA accumulation; batch in grid.z.
 __global__ void __launch_bounds__(256) sgemm_kernel(const float* __restrict__ A,
                                                     const float* __restrict__ B, float* __restrict__ C,
-                                                    int64_t M, int64_t K, int64_t N) {
+                                                    int64_t M, int64_t K, int64_t N, int64_t sai, int64_t sap,
+                                                    int64_t sbp, int64_t sbj) {
   __shared__ float As[16][64 + 4];
   __shared__ float Bs[16][64 + 4];
   const int64_t bz = blockIdx.z;
@@ -430,10 +435,10 @@ __global__ void __launch_bounds__(256) sgemm_kernel(const float* __restrict__ A,
     for (int i = threadIdx.x; i < 64 * 16; i += 256) {
       const int r = i / 16, kk = i % 16;
       const int64_t gr = row0 + r, gk = k0 + kk;
-      As[kk][r] = (gr < M && gk < K) ? A[gr * K + gk] : 0.f;
+      As[kk][r] = (gr < M && gk < K) ? A[gr * sai + gk * sap] : 0.f;
       const int kb = i / 64, c = i % 64;
       const int64_t gk2 = k0 + kb, gc = col0 + c;
-      Bs[kb][c] = (gk2 < K && gc < N) ? B[gk2 * N + gc] : 0.f;
+      Bs[kb][c] = (gk2 < K && gc < N) ? B[gk2 * sbp + gc * sbj] : 0.f;
     }
     __syncthreads();
 #pragma unroll
@@ -698,34 +703,45 @@ extern "C" int j4b_random_normal(int64_t seed, int64_t counter, j4b_buf out, int
   return J4B_OK;
 }
 
+namespace j4b {
+// C (m x n) = A . B with A, B optionally transposed in place (ta: A given as [k, m]; tb: B given
+// as [n, k]); batch >= 1 only for untransposed operands. precision as j4b_matmul.
+int matmul_strided(const float* pa, const float* pb, float* pc, int64_t batch, int64_t m, int64_t k, int64_t n,
+                   bool ta, bool tb, int precision, int dev, cudaStream_t stream) {
+  // tensor cores (tcgen05): bf16 operands (1), or the 3-term bf16 split for fp32 accuracy (2, and
+  // 0 when the contraction is large enough to amortise the operand conversion)
+  const bool big = m * n * k >= (int64_t(1) << 24) && m >= 64 && n >= 64;
+  if (precision == 1 || precision == 2 || big) {
+    if (ta || tb) return tc_matmul_t(pa, pb, pc, m, k, n, ta, tb, precision == 1 ? 1 : 3, dev, stream);
+    return tc_matmul(pa, pb, pc, batch, m, k, n, precision == 1 ? 1 : 3, dev, stream);
+  }
+  const int64_t sai = ta ? 1 : k, sap = ta ? m : 1, sbp = tb ? 1 : n, sbj = tb ? k : 1;
+  if (k <= 32 && batch <= 65535 && (m * n + 255) / 256 <= INT32_MAX) {
+    gemm_short_k_kernel<<<dim3((unsigned)((m * n + 255) / 256), (unsigned)batch), 256, 0, stream>>>(pa, pb, pc, m, k, n,
+                                                                                                 sai, sap, sbp, sbj);
+    J4B_CHECK_LAUNCH("gemm_short_k_kernel");
+    return J4B_OK;
+  }
+  if (n <= 32 && batch <= 65535 && (m + 7) / 8 <= INT32_MAX) {
+    gemm_narrow_n_kernel<<<dim3((unsigned)((m + 7) / 8), (unsigned)batch), 256, 0, stream>>>(pa, pb, pc, m, k, (int)n,
+                                                                                          sai, sap, sbp, sbj);
+    J4B_CHECK_LAUNCH("gemm_narrow_n_kernel");
+    return J4B_OK;
+  }
+  dim3 grid((unsigned)((n + 63) / 64), (unsigned)((m + 63) / 64), (unsigned)batch);
+  sgemm_kernel<<<grid, 256, 0, stream>>>(pa, pb, pc, m, k, n, sai, sap, sbp, sbj);
+  J4B_CHECK_LAUNCH("sgemm_kernel");
+  return J4B_OK;
+}
+}  // namespace j4b
+
 extern "C" int j4b_matmul(j4b_buf a, j4b_buf b, j4b_buf out, int64_t batch, int64_t m, int64_t k,
                           int64_t n, int precision, j4b_stream s) {
   J4B_REQUIRE(batch >= 1 && m >= 1 && k >= 1 && n >= 1, "matmul dimensions must be positive");
   J4B_REQUIRE(precision >= 0 && precision <= 2, "matmul precision must be 0, 1 or 2");
   J4B_DEVICE_OF(out);
-  // tensor cores (tcgen05): bf16 operands (1), or the 3-term bf16 split for fp32 accuracy (2, and
-  // 0 when the contraction is large enough to amortise the operand conversion)
-  const bool big = m * n * k >= (int64_t(1) << 24) && m >= 64 && n >= 64;
-  if (precision == 1 || precision == 2 || big)
-    return tc_matmul((const float*)(uintptr_t)a, (const float*)(uintptr_t)b, (float*)(uintptr_t)out, batch, m,
-                     k, n, precision == 1 ? 1 : 3, dev, stream);
-  const float* pa = (const float*)(uintptr_t)a;
-  const float* pb = (const float*)(uintptr_t)b;
-  float* pc = (float*)(uintptr_t)out;
-  if (k <= 32 && batch <= 65535 && (m * n + 255) / 256 <= INT32_MAX) {
-    gemm_short_k_kernel<<<dim3((unsigned)((m * n + 255) / 256), (unsigned)batch), 256, 0, stream>>>(pa, pb, pc, m, k, n);
-    J4B_CHECK_LAUNCH("gemm_short_k_kernel");
-    return J4B_OK;
-  }
-  if (n <= 32 && batch <= 65535 && (m + 7) / 8 <= INT32_MAX) {
-    gemm_narrow_n_kernel<<<dim3((unsigned)((m + 7) / 8), (unsigned)batch), 256, 0, stream>>>(pa, pb, pc, m, k, (int)n);
-    J4B_CHECK_LAUNCH("gemm_narrow_n_kernel");
-    return J4B_OK;
-  }
-  dim3 grid((unsigned)((n + 63) / 64), (unsigned)((m + 63) / 64), (unsigned)batch);
-  sgemm_kernel<<<grid, 256, 0, stream>>>(pa, pb, pc, m, k, n);
-  J4B_CHECK_LAUNCH("sgemm_kernel");
-  return J4B_OK;
+  return matmul_strided((const float*)(uintptr_t)a, (const float*)(uintptr_t)b, (float*)(uintptr_t)out, batch, m, k,
+                        n, false, false, precision, dev, stream);
 }
 
 // ---------------------------------------------------------------------------------------------

@@ -362,6 +362,50 @@ int tc_matmul(const float* a, const float* b, float* out, int64_t batch, int64_t
   return rc;
 }
 
+// op(A) . op(B): each operand converted to its bf16 K-major form straight from its stored layout
+// (A [m, k] rows or A^T stored [k, m] through the transposing split; B likewise), so a transpose
+// feeding a matmul is never materialised.
+int tc_matmul_t(const float* a, const float* b, float* out, int64_t m, int64_t k, int64_t n, bool ta, bool tb,
+                int terms, int dev, cudaStream_t stream) {
+  if (m == 0 || n == 0) return J4B_OK;
+  if (k == 0) {
+    J4B_CUDA(cudaMemsetAsync(out, 0, (size_t)(m * n) * 4, stream), "cudaMemsetAsync");
+    return J4B_OK;
+  }
+  if (m > INT32_MAX / 2 || n > INT32_MAX / 2 || k > INT32_MAX / 2)
+    return set_error(J4B_EINVAL, "matmul dimension too large for the tensor-core path");
+  const int64_t kp = (k + kBK - 1) / kBK * kBK;
+  const bool split = terms == 3;
+  const size_t abytes = (size_t)(m * kp) * 2, bbytes = (size_t)(n * kp) * 2;
+  const size_t aspan = (abytes + 255) & ~size_t(255), bspan = (bbytes + 255) & ~size_t(255);
+  void* scratch = nullptr;
+  J4B_CUDA(cudaMallocAsync(&scratch, 2 * aspan + 2 * bspan + 256, stream), "cudaMallocAsync(matmul operands)");
+  __nv_bfloat16* ahi = (__nv_bfloat16*)scratch;
+  __nv_bfloat16* alo = split ? (__nv_bfloat16*)((uint8_t*)scratch + aspan) : nullptr;
+  __nv_bfloat16* bhi = (__nv_bfloat16*)((uint8_t*)scratch + 2 * aspan);
+  __nv_bfloat16* blo = split ? (__nv_bfloat16*)((uint8_t*)scratch + 2 * aspan + bspan) : nullptr;
+  int rc = J4B_OK;
+  if (ta) {  // stored [k, m] -> [m, kp]
+    split_transpose_kernel<<<dim3((unsigned)((kp + 31) / 32), (unsigned)((m + 31) / 32)), dim3(32, 8), 0, stream>>>(
+        a, k, m, kp, ahi, alo);
+    count_launch(1);
+  } else {
+    rc = tc_split_rows(a, m, k, k, kp, ahi, alo, stream);
+  }
+  if (rc == J4B_OK) {
+    if (tb) {  // stored [n, k] -> [n, kp]
+      rc = tc_split_rows(b, n, k, k, kp, bhi, blo, stream);
+    } else {  // stored [k, n] -> [n, kp]
+      split_transpose_kernel<<<dim3((unsigned)((kp + 31) / 32), (unsigned)((n + 31) / 32)), dim3(32, 8), 0, stream>>>(
+          b, k, n, kp, bhi, blo);
+      count_launch(1);
+    }
+  }
+  if (rc == J4B_OK) rc = tc_gemm_bf16(ahi, alo, m, kp, bhi, blo, n, terms, out, dev, stream);
+  cudaFreeAsync(scratch, stream);
+  return rc;
+}
+
 int tc_status_read(int dev, int* value) {
   int* st = tc_status(dev);
   if (!st) return set_error(J4B_ENOMEM, "status");

@@ -58,6 +58,13 @@ struct DeviceGuard {
 int tc_matmul(const float* a, const float* b, float* out, int64_t batch, int64_t m, int64_t k, int64_t n,
               int terms, int dev, cudaStream_t stream);
 int tc_status_read(int dev, int* value);
+// C (m x n) = op(A) . op(B) on tcgen05 with op = transpose where ta / tb (A stored [k, m], B [n, k])
+int tc_matmul_t(const float* a, const float* b, float* out, int64_t m, int64_t k, int64_t n, bool ta, bool tb,
+                int terms, int dev, cudaStream_t stream);
+// C (m x n) = op(A) . op(B), precision as j4b_matmul (SIMT, skinny or tensor-core kernels); batch > 1
+// only without transposes
+int matmul_strided(const float* a, const float* b, float* out, int64_t batch, int64_t m, int64_t k, int64_t n,
+                   bool ta, bool tb, int precision, int dev, cudaStream_t stream);
 }  // namespace j4b
 #include <cuda_bf16.h>
 namespace j4b {

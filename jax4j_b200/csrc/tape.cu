@@ -473,10 +473,13 @@ struct Planner {
   std::vector<Group> groups;
   std::vector<Step> steps;
   std::vector<int> fills;
+  // tsrc[b] = the source of transpose output b when every consumer of b is a matmul, which then
+  // reads the source transposed in place (b is never materialised); else -1
+  std::vector<int> tsrc;
   int cur = -1;
   std::string err;
 
-  explicit Planner(TapeIR& tape) : t(tape), V(tape.shape.size()) {}
+  explicit Planner(TapeIR& tape) : t(tape), V(tape.shape.size()), tsrc(tape.shape.size(), -1) {}
 
   // ---- helpers ----
   int64_t choose_R(const Shape& s) const {
@@ -848,7 +851,7 @@ struct Planner {
 
   void eager(int ci) {
     const TCall& c = t.calls[ci];
-    for (int b : c.ins) ensure_global(b);
+    for (int b : c.ins) ensure_global(tsrc[(size_t)b] >= 0 ? tsrc[(size_t)b] : b);
     cur = -1;
     Step s;
     s.kind = S_EAGER;
@@ -875,9 +878,27 @@ struct Planner {
       if (!live[(size_t)c.out]) continue;
       for (int b : c.ins) live[(size_t)b] = 1;
     }
+    // transposes read only by matmuls (as either operand) and not outputs are absorbed
+    {
+      std::vector<int> uses(t.shape.size(), 0), mm_uses(t.shape.size(), 0);
+      for (const TCall& c : t.calls) {
+        if (!live[(size_t)c.out]) continue;
+        for (int b : c.ins) {
+          uses[(size_t)b]++;
+          if (c.op == T_MATMUL) mm_uses[(size_t)b]++;
+        }
+      }
+      std::vector<char> is_out(t.shape.size(), 0);
+      for (int b : t.outputs) is_out[(size_t)b] = 1;
+      for (const TCall& c : t.calls)
+        if (c.op == T_TRANSPOSE && live[(size_t)c.out] && !is_out[(size_t)c.out] && uses[(size_t)c.out] > 0 &&
+            uses[(size_t)c.out] == mm_uses[(size_t)c.out])
+          tsrc[(size_t)c.out] = c.ins[0];
+    }
     for (int ci = 0; ci < (int)t.calls.size(); ++ci) {
       const TCall& c = t.calls[ci];
       if (!live[(size_t)c.out]) continue;
+      if (tsrc[(size_t)c.out] >= 0) continue;  // absorbed transpose: its matmul reads the source
       if (c.op == T_RESHAPE) {
         V[c.out] = V[c.ins[0]];
         // a reshape of a stored value shares its storage; of a kernel value, its slots
@@ -1108,6 +1129,7 @@ struct j4b_tape {
   std::vector<j4b::Group> groups;
   std::vector<j4b::Step> steps;
   std::vector<int> fills;
+  std::vector<int> tsrc;  // absorbed transposes: output id -> source id (else -1)
   struct GroupRun {
     CUmodule mod = nullptr;
     CUfunction row = nullptr, fold = nullptr;
@@ -2177,6 +2199,7 @@ int build_tape(j4b_tape* tp, const int64_t* words, size_t nwords, std::vector<Gr
   tp->groups = pl.groups;
   tp->steps = pl.steps;
   tp->fills = pl.fills;
+  tp->tsrc = pl.tsrc;
   codes.assign(tp->groups.size(), GroupCode());
   tp->runs.assign(tp->groups.size(), j4b_tape::GroupRun());
   for (size_t g = 0; g < tp->groups.size(); ++g) {
@@ -2430,8 +2453,15 @@ int run_eager(const LaunchCtx& L, int ci, cudaStream_t stream) {
   const Shape& os = t.shape[(size_t)c.out];
   auto ishape = [&](int i) -> const Shape& { return t.shape[(size_t)c.ins[(size_t)i]]; };
   switch (c.op) {
-    case T_MATMUL:
-      return j4b_matmul(A(0), A(1), o, 1, ishape(0)[0], ishape(0)[1], ishape(1)[1], 0, s);
+    case T_MATMUL: {
+      // an absorbed transpose operand is read from its source, transposed in place
+      const int b0 = c.ins[0], b1 = c.ins[1];
+      const int s0 = L.tp->tsrc[(size_t)b0], s1 = L.tp->tsrc[(size_t)b1];
+      const float* pa = (const float*)addr_of(L, s0 >= 0 ? s0 : b0);
+      const float* pb = (const float*)addr_of(L, s1 >= 0 ? s1 : b1);
+      return matmul_strided(pa, pb, (float*)o, 1, ishape(0)[0], ishape(0)[1], ishape(1)[1], s0 >= 0, s1 >= 0, 0,
+                            L.tp->dev, stream);
+    }
     case T_BMM:
       return j4b_matmul(A(0), A(1), o, ishape(0)[0], ishape(0)[1], ishape(0)[2], ishape(1)[2], 0, s);
     case T_TRANSPOSE: return j4b_transpose(A(0), o, ishape(0)[0], ishape(0)[1], s);
