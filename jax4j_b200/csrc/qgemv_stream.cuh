@@ -46,22 +46,17 @@ template <int QT, bool PK>
 constexpr int stream_frag_chunk() {
   return PK ? 2048 + (stream_needs_xblk<QT>() ? 512 : 0) : 4096 + (stream_needs_xblk<QT>() ? 1024 : 0);
 }
-// Tile pairs (a CTA with at most NW / 2 tiles gives each tile two warps): per pair two parity
-// slots of one warp's accumulators (kNV floats x 32 lanes).
-template <bool PK, int NW>
-constexpr int stream_pair_bytes() { return (NW / 2) * 2 * (PK ? 2 : 4) * 32 * 4; }
 template <int QT, bool PK, int NW>
 constexpr int stream_stages() {
   constexpr int stage = stream_tiles_per_stage<QT>() * GemvTraits<QT>::kChunk;
-  constexpr int r = (stream_smem_budget<NW>() - 8 * stream_frag_chunk<QT, PK>() - stream_pair_bytes<PK, NW>() - 512) / stage;
+  constexpr int r = (stream_smem_budget<NW>() - 8 * stream_frag_chunk<QT, PK>() - 512) / stage;
   return r > 16 ? 16 : r;
 }
-// ring | x fragments | pair slots | full[R] | empty[R] mbarriers | seq[R] stage numbers
+// ring | x fragments | full[R] | empty[R] mbarriers | seq[R] stage numbers
 template <int QT, bool PK, int NW>
 constexpr int stream_smem_bytes() {
   return stream_stages<QT, PK, NW>() * stream_tiles_per_stage<QT>() * GemvTraits<QT>::kChunk +
-         8 * stream_frag_chunk<QT, PK>() + stream_pair_bytes<PK, NW>() + 2 * 8 * stream_stages<QT, PK, NW>() +
-         4 * stream_stages<QT, PK, NW>();
+         8 * stream_frag_chunk<QT, PK>() + 2 * 8 * stream_stages<QT, PK, NW>() + 4 * stream_stages<QT, PK, NW>();
 }
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
@@ -206,8 +201,7 @@ __global__ void __launch_bounds__(stream_threads<NW>(), NW == 8 ? 2 : 1) qgemv_s
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* ring = smem;
   uint8_t* frag = smem + R * kStage;
-  float* pair_slots = reinterpret_cast<float*>(frag + 8 * kFrag);
-  uint64_t* full = reinterpret_cast<uint64_t*>(frag + 8 * kFrag + stream_pair_bytes<PK, NW>());
+  uint64_t* full = reinterpret_cast<uint64_t*>(frag + 8 * kFrag);
   uint64_t* empty = full + R;
   volatile int* seq = reinterpret_cast<volatile int*>(empty + R);  // stage last issued per slot
 
@@ -222,14 +216,11 @@ __global__ void __launch_bounds__(stream_threads<NW>(), NW == 8 ? 2 : 1) qgemv_s
   const uint32_t chunk_bytes = (uint32_t)a.L.chunk_bytes(split);
   const uint32_t meta_off = (uint32_t)(a.L.groups_in_split(split) * T::kQ);
   const int nchunks = (int)(a.kpad - kc0 >= 1024 ? 8 : (a.kpad - kc0) / 128);
-  // few tiles: two warps per tile (chunks 0-3 and 4-7), the second handing its partial to the
-  // first through a parity slot in shared memory and one named barrier (2 + pair) per tile
-  const bool pair = 2 * ntiles <= NW;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < R; s++) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], pair ? 2 * kU : kU);
+      mbar_init(&empty[s], kU);
       seq[s] = -1;
     }
     fence_mbar_init();
@@ -272,11 +263,7 @@ __global__ void __launch_bounds__(stream_threads<NW>(), NW == 8 ? 2 : 1) qgemv_s
     if (warp < nchunks) stream_prep_x<QT, PK>(a, kc0, warp, lane, frag);
     compute_warps_sync<NW>();
 
-    const int owner = pair ? warp >> 1 : warp, half = pair ? warp & 1 : 0;
-    const int c_begin = pair ? 4 * half : 0;
-    const int c_end = pair ? min(nchunks, 4 * half + 4) : nchunks;
-    int parity = 0;
-    for (int u = owner; u < ntiles; u += (pair ? NW / 2 : NW)) {
+    for (int u = warp; u < ntiles; u += NW) {
       const int st = u / kU, slot = st % R;
       if (!failed && !(wait_issued(seq + slot, st) && mbar_wait_bounded(&full[slot], (uint32_t)((st / R) & 1))))
         failed = true;
@@ -287,7 +274,7 @@ __global__ void __launch_bounds__(stream_threads<NW>(), NW == 8 ? 2 : 1) qgemv_s
       if (!failed) {
         const uint8_t* base = ring + slot * kStage + (u % kU) * chunk_bytes;
 #pragma unroll 2
-        for (int c = c_begin; c < c_end; c++) {
+        for (int c = 0; c < nchunks; c++) {
           const uint8_t* fc = frag + c * kFrag;
           if constexpr (PK) {
             uint32_t bp[8][2];
@@ -346,18 +333,6 @@ __global__ void __launch_bounds__(stream_threads<NW>(), NW == 8 ? 2 : 1) qgemv_s
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[slot]);  // this warp is done reading the stage
-      if (pair) {
-        float* ps = pair_slots + ((owner * 2 + parity) * kNV) * 32;
-        if (half) {
-#pragma unroll
-          for (int i = 0; i < kNV; i++) ps[i * 32 + lane] = acc[i];
-        }
-        asm volatile("bar.sync %0, 64;" ::"r"(2 + owner) : "memory");
-        parity ^= 1;
-        if (half) continue;
-#pragma unroll
-        for (int i = 0; i < kNV; i++) acc[i] += ps[i * 32 + lane];
-      }
       if (failed) continue;
 
       const int64_t tile = tile0 + u;
