@@ -84,6 +84,12 @@ int tc_split_rows(const float* src, int64_t rows, int64_t cols, int64_t ld, int6
 // ---- collectives over peer memory (peer.cu) ----
 constexpr int kMaxPeerRanks = 8;
 
+// Every all-gathering GEMV call adds exactly kPeerCallUnits to each rank's arrival counter of
+// its source (CTA 0 adds kPeerCallUnits - (grid - 1), every other CTA 1), whatever its grid, so
+// calls of different shapes can share a channel: source s has finished step k once its counter
+// reaches (k + 1) x kPeerCallUnits (compared modulo 2^32). A launch needs grid <= kPeerCallUnits.
+constexpr unsigned kPeerCallUnits = 1u << 20;
+
 // Where a GEMV's y goes when it is all-gathered over peer memory.
 struct GemvPeers {
   int nranks, rank;
@@ -94,8 +100,7 @@ struct GemvPeers {
 };
 int peer_group_ranks(const j4b_peer_group* g);
 int peer_gemv_targets(const j4b_peer_group* g, int channel, int64_t gathered_floats, GemvPeers* t);
-int peer_wait_copy(const j4b_peer_group* g, int channel, unsigned incr, float* out, int64_t n,
-                   cudaStream_t stream);
+int peer_wait_copy(const j4b_peer_group* g, int channel, float* out, int64_t n, cudaStream_t stream);
 
 // out[k] = sum of a[sources[p]] for p in [offsets[k], offsets[k+1]), in that order
 int launch_segment_sum(const float* a, const int64_t* offsets, const int64_t* sources, int64_t n_dst,

@@ -13,9 +13,14 @@
 //   [64, 128)      arrival counter of the calling kernel's CTAs per channel (local)
 //   [4096, 69632)  arrival counters per channel: [channel][slot], slot = chunk * 8 + source
 //   [131072, end)  data, one slice per channel, each split into two parity halves
-// Counters only grow: source s has finished step k of a channel once its counter reaches
-// (k + 1) x its arrivals per step, and the data of consecutive steps alternates halves, so a
-// rank that runs one step ahead never overwrites what a slower rank still reads.
+// Step k of a channel is complete for source s once
+//   - GEMV all-gather: s's arrival counter reaches (k + 1) x kPeerCallUnits (every call adds
+//     exactly that many units, whatever its grid);
+//   - all-reduce: the chunk's slot holds the epoch k + 1 (stored by s after its chunk's data, so
+//     a chunk that earlier calls did not use carries no stale count);
+// both compared modulo 2^32. The data of consecutive steps alternates halves, so a rank that runs
+// one step ahead never overwrites what a slower rank still reads (and no rank gets further ahead:
+// each step waits for every rank's arrival at that step).
 // Every wait is bounded (about a second); a wait that gives up sets the group's status word.
 #include <cuda_runtime.h>
 
@@ -37,28 +42,33 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// v has not yet reached target, modulo 2^32.
+__device__ __forceinline__ bool before(unsigned v, unsigned target) { return (int)(v - target) < 0; }
 
 struct PeerBases {
   uint8_t* base[kMaxPeerRanks];
 };
 
-// Waits until every source's arrival counter reaches (step + 1) x incr, then copies this rank's
-// gathered half to `out`; the last CTA advances the step counter.
+// Waits until every source's arrival counter reaches (step + 1) x kPeerCallUnits, then copies
+// this rank's gathered half to `out`; the last CTA advances the step counter.
 // Launched as a programmatic dependent of the GEMV: it may start while the GEMV still runs (it
 // reads only the arrival counters, the step counter and the gathered data the counters vouch
 // for), and it releases its own dependents at once so the next kernel's prologue -- the next
 // GEMV's weight prefetch -- overlaps the wait.
-__global__ void wait_copy_kernel(unsigned* step, unsigned* done, const unsigned* ctr, int nranks, unsigned incr,
+__global__ void wait_copy_kernel(unsigned* step, unsigned* done, const unsigned* ctr, int nranks,
                                  const float* data, int64_t half_floats, float* out, int64_t n,
                                  int* status) {
   __shared__ unsigned s_step;
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (threadIdx.x == 0) {
     const unsigned s = *(volatile unsigned*)step;
-    const unsigned target = (s + 1u) * incr;
+    const unsigned target = (s + 1u) * kPeerCallUnits;
     for (int src = 0; src < nranks; ++src) {
       uint32_t it = 0;
-      while (ld_acquire_sys(ctr + src) < target) {
+      while (before(ld_acquire_sys(ctr + src), target)) {
         if (++it > kPeerWaitLimit) {
           atomicExch(status, 1);
           break;
@@ -82,8 +92,9 @@ __global__ void wait_copy_kernel(unsigned* step, unsigned* done, const unsigned*
   }
 }
 
-// One CTA per 1024-element chunk: write the chunk into slot `rank` of every rank, count the
-// arrival, wait for every source's chunk, sum the slots in rank order.
+// One CTA per 1024-element chunk: write the chunk into slot `rank` of every rank, publish the
+// step's epoch in the chunk's counter slot at every rank, wait for every source's epoch, sum the
+// slots in rank order.
 __global__ void allreduce_kernel(PeerBases bases, int nranks, int rank, int channel, int64_t slice_floats,
                                  const float* src, int64_t n, float* out, int* status) {
   constexpr int kChunk = 1024;
@@ -106,12 +117,12 @@ __global__ void allreduce_kernel(PeerBases bases, int nranks, int rank, int chan
     __threadfence_system();
     for (int p = 0; p < nranks; ++p) {
       unsigned* ctr = reinterpret_cast<unsigned*>(bases.base[p] + kCtrOffset) + channel * kSlotsPerChannel;
-      atomicAdd_system(ctr + c * 8 + rank, 1u);
+      st_release_sys(ctr + c * 8 + rank, s + 1u);
     }
     const unsigned* mctr = reinterpret_cast<const unsigned*>(mine + kCtrOffset) + channel * kSlotsPerChannel;
     for (int q = 0; q < nranks; ++q) {
       uint32_t it = 0;
-      while (ld_acquire_sys(mctr + c * 8 + q) < s + 1u) {
+      while (before(ld_acquire_sys(mctr + c * 8 + q), s + 1u)) {
         if (++it > kPeerWaitLimit) {
           atomicExch(status, 1);
           break;
@@ -256,8 +267,7 @@ int peer_gemv_targets(const j4b_peer_group* g, int channel, int64_t gathered_flo
   return J4B_OK;
 }
 
-int peer_wait_copy(const j4b_peer_group* g, int channel, unsigned incr, float* out, int64_t n,
-                   cudaStream_t stream) {
+int peer_wait_copy(const j4b_peer_group* g, int channel, float* out, int64_t n, cudaStream_t stream) {
   uint8_t* mine = g->base[g->rank];
   const int64_t slice = peer_slice_floats(g);
   unsigned* step = reinterpret_cast<unsigned*>(mine) + channel;
@@ -274,7 +284,7 @@ int peer_wait_copy(const j4b_peer_group* g, int channel, unsigned incr, float* o
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  J4B_CUDA(cudaLaunchKernelEx(&cfg, wait_copy_kernel, step, done, ctr, g->nranks, incr, data, slice / 2, out, n,
+  J4B_CUDA(cudaLaunchKernelEx(&cfg, wait_copy_kernel, step, done, ctr, g->nranks, data, slice / 2, out, n,
                               g->status),
            "wait_copy_kernel");
   count_launch();

@@ -35,14 +35,21 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
                "r"(bytes)
                : "memory");
 }
-// 1-D bulk copy global -> this CTA's own shared memory (one destination CTA). 16-byte aligned,
-// size % 16 == 0.
-__device__ __forceinline__ void tma_load_1d(void* dst, const void* src, uint32_t bytes,
-                                            uint64_t* bar) {
+// 1-D bulk copy global -> this CTA's own shared memory (one destination CTA), 16-byte aligned,
+// size % 16 == 0, for weight bytes that one launch reads exactly once: the copy carries an L2
+// evict-first policy, so the streamed weights do not push x, y and the split-K partials (read
+// again within the launch, or by the next one) out of L2.
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+__device__ __forceinline__ void tma_load_1d_stream(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                                   uint64_t policy) {
   asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
           smem_u32(dst)),
-      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
       : "memory");
 }
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t phase) {
@@ -170,14 +177,16 @@ __device__ __forceinline__ void store_y(const GemvArgs& a, int64_t par_off, int 
 }
 
 // After this CTA's last store: the CTA barrier orders every thread's stores before thread 0's
-// system-scope fence, which orders them before the arrival counted at every rank. Called by
-// every thread of the CTA on each exit path.
+// system-scope fence, which orders them before the arrival counted at every rank. The CTAs of
+// one launch add kPeerCallUnits in total (CTA 0 the remainder), so the count per call does not
+// depend on the grid. Called by every thread of the CTA on each exit path.
 __device__ __forceinline__ void signal_peers(const GemvArgs& a) {
   if (a.nranks <= 1) return;
   __syncthreads();
   if (threadIdx.x == 0) {
+    const unsigned units = blockIdx.x == 0 ? kPeerCallUnits - (gridDim.x - 1u) : 1u;
     __threadfence_system();
-    for (int p = 0; p < a.nranks; ++p) atomicAdd_system(a.peer_ctr[p], 1u);
+    for (int p = 0; p < a.nranks; ++p) atomicAdd_system(a.peer_ctr[p], units);
   }
 }
 
@@ -587,8 +596,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) qgemv_kernel(GemvArgs a) {
     const uint32_t bytes = (uint32_t)count * chunk_bytes;
     uint64_t* bar = &full[c % kStages];
     mbar_expect_tx(bar, bytes);
-    tma_load_1d(stage_base + (c % kStages) * kStageBytes,
-                a.data + a.L.chunk_offset(split, tile0 + first), bytes, bar);
+    tma_load_1d_stream(stage_base + (c % kStages) * kStageBytes,
+                       a.data + a.L.chunk_offset(split, tile0 + first), bytes, bar, l2_evict_first_policy());
   };
 
   if (threadIdx.x == 0) {
@@ -960,6 +969,7 @@ cudaError_t launch_gemv(const j4b_qweight* w, const float* x, const float* add, 
   attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = a.cluster ? 2 : 1;
+  if (peers && cfg.gridDim.x > kPeerCallUnits) return cudaErrorInvalidConfiguration;
   if (grid_out) *grid_out = cfg.gridDim.x;
   return cudaLaunchKernelEx(&cfg, qgemv_kernel<QT, NT, PK>, a);
 }

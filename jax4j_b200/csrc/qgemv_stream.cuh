@@ -231,13 +231,15 @@ __global__ void __launch_bounds__(stream_threads<NW>(), NW == 8 ? 2 : 1) qgemv_s
   int issued = 0;  // stages issued (producer lane 0 only)
   if (warp == NW) {
     // ---------------- producer ----------------
+    const uint64_t policy = l2_evict_first_policy();
     auto issue = [&](int st) {
       const int first = st * kU, count = min(kU, ntiles - first);
       const uint32_t bytes = (uint32_t)count * chunk_bytes;
       uint64_t* bar = &full[st % R];
       seq[st % R] = st;
       mbar_expect_tx(bar, bytes);
-      tma_load_1d(ring + (st % R) * kStage, a.data + a.L.chunk_offset(split, tile0 + first), bytes, bar);
+      tma_load_1d_stream(ring + (st % R) * kStage, a.data + a.L.chunk_offset(split, tile0 + first), bytes, bar,
+                         policy);
     };
     if (lane == 0)
       for (; issued < R && issued < nstages; issued++) issue(issued);
@@ -445,6 +447,7 @@ cudaError_t launch_gemv_stream(const j4b_qweight* w, const float* x, const float
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
+  if (peers && cfg.gridDim.x > kPeerCallUnits) return cudaErrorInvalidConfiguration;
   if (grid_out) *grid_out = cfg.gridDim.x;
   return cudaLaunchKernelEx(&cfg, qgemv_stream_kernel<QT, PK, NW>, a);
 }

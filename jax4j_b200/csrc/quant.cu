@@ -816,18 +816,17 @@ extern "C" int j4b_quant_matvec_allgather(j4b_qweight_t w, j4b_buf x, j4b_buf ad
   const float* xp = (const float*)(uintptr_t)x;
   const float* ap = add ? (const float*)(uintptr_t)add : nullptr;
   const int sms = device_ctx(w->dev)->sm_count;
-  unsigned grid = 0;
   cudaError_t e = cudaErrorInvalidValue;
   switch (w->type) {
-    case J4B_Q8_0: e = gemv_dispatch<J4B_Q8_0>(w, xp, ap, nullptr, (int)batch, sms, stream, &t, &grid); break;
-    case J4B_Q4_0: e = gemv_dispatch<J4B_Q4_0>(w, xp, ap, nullptr, (int)batch, sms, stream, &t, &grid); break;
-    case J4B_Q4_K: e = gemv_dispatch<J4B_Q4_K>(w, xp, ap, nullptr, (int)batch, sms, stream, &t, &grid); break;
-    case J4B_Q6_K: e = gemv_dispatch<J4B_Q6_K>(w, xp, ap, nullptr, (int)batch, sms, stream, &t, &grid); break;
-    case J4B_Q2_0: e = gemv_dispatch<J4B_Q2_0>(w, xp, ap, nullptr, (int)batch, sms, stream, &t, &grid); break;
+    case J4B_Q8_0: e = gemv_dispatch<J4B_Q8_0>(w, xp, ap, nullptr, (int)batch, sms, stream, &t); break;
+    case J4B_Q4_0: e = gemv_dispatch<J4B_Q4_0>(w, xp, ap, nullptr, (int)batch, sms, stream, &t); break;
+    case J4B_Q4_K: e = gemv_dispatch<J4B_Q4_K>(w, xp, ap, nullptr, (int)batch, sms, stream, &t); break;
+    case J4B_Q6_K: e = gemv_dispatch<J4B_Q6_K>(w, xp, ap, nullptr, (int)batch, sms, stream, &t); break;
+    case J4B_Q2_0: e = gemv_dispatch<J4B_Q2_0>(w, xp, ap, nullptr, (int)batch, sms, stream, &t); break;
   }
   if (e != cudaSuccess) return cuda_error(e, "qgemv_kernel");
   count_launch();
-  return peer_wait_copy(g, channel, grid, (float*)(uintptr_t)y_all, gathered, stream);
+  return peer_wait_copy(g, channel, (float*)(uintptr_t)y_all, gathered, stream);
 }
 
 extern "C" int j4b_quant_gather_row(j4b_qweight_t w, int64_t row, j4b_buf out, j4b_stream s) {

@@ -24,9 +24,11 @@ from jax4j_b200 import _lib
 be = B200Backend(rank)
 pg = PeerGroup(rank, rank, world)
 s = torch_stream()
-# one K split (the epilogue stores y into every rank), and four K splits at batch 8 (the split-K
-# fold inside the all-gathering kernel, where the local GEMV folds in a separate kernel)
-for rows, cols, batch, qtype in ((96, 512, 3, 8), (256, 4096, 8, 8), (160, 2048, 1, 12)):
+# one K split (the epilogue stores y into every rank), four K splits at batch 8 (the split-K
+# fold inside the all-gathering kernel), then smaller grids after larger ones on the same channel
+# (every call adds the same count to the arrival counters, whatever its grid)
+for rows, cols, batch, qtype in ((96, 512, 3, 8), (256, 4096, 8, 8), (160, 2048, 1, 12), (96, 512, 3, 8),
+                                 (4096, 4096, 8, 8), (64, 1024, 2, 12)):
     rng = np.random.default_rng(100 + rank)
     w = (rng.standard_normal((rows, cols)) * 0.02).astype(np.float32)
     blob = be.quantize(be.upload(w, w.shape), qtype)
@@ -43,8 +45,8 @@ for rows, cols, batch, qtype in ((96, 512, 3, 8), (256, 4096, 8, 8), (160, 2048,
     dist.all_gather(parts, torch.from_numpy(mine.reshape(-1)).cuda())
     want = np.concatenate([p.cpu().numpy().reshape(batch, rows) for p in parts], axis=1)
     assert np.array_equal(got, want), ("all-gather mismatch", rows, cols, batch)
-n = 5000
-for it in range(3):
+# calls of different sizes share the channel (chunks an earlier call did not use hold no count)
+for it, n in enumerate((5000, 1000, 3000, 5000)):
     v = torch.from_numpy(np.random.default_rng(it * 10 + rank).standard_normal(n).astype(np.float32)).cuda()
     out = torch.empty(n, device="cuda")
     pg.allreduce(v.data_ptr(), n, out.data_ptr(), s)
