@@ -856,22 +856,32 @@ def measure_gemv(ctx, name, K, W, cpu_budget):
     kernel_avg_us = kernel_ms * 1e3 / K
 
     # ---- end to end through the public API: pinned host x in, y out, every step ----
+    # one GPU: the host-buffer quantMatvec (j4b_quant_matvec_host: copy in, GEMV, copy out in one
+    # C-ABI call); N GPUs: x copied in, the all-gathering GEMV, the gathered y copied out
     x_host = torch.from_numpy(np.ascontiguousarray(be.download(x))).pin_memory()
-    y_host = torch.empty(batch * rows, dtype=torch.float32).pin_memory()
-    out = be.full(0.0, (batch, rows))
+    y_host = torch.empty(world * batch * rows, dtype=torch.float32).pin_memory()
+    y_all_host = y_host
     xin = be.full(0.0, (batch, cols))
     e2e_steps = max(K, 200)
     stream = torch_stream()
-    for i in range(3):  # warm the path
-        be.quant_matvec(weights[i % copies], xin, out=out)
+
+    def e2e_step(i):
+        if world > 1:
+            _lib.call("j4b_h2d", xin.ptr, ctypes.c_void_p(x_host.data_ptr()), x_host.numel() * 4, stream)
+            peers.allgather_matvec(weights[i % copies], xin.ptr, y_all.data_ptr(), batch, stream)
+            _lib.call("j4b_d2h", ctypes.c_void_p(y_all_host.data_ptr()), y_all.data_ptr(), y_all_host.numel() * 4,
+                      stream)
+        else:
+            be.quant_matvec_host(weights[i % copies], x_host, y_host, stream)
+
+    for i in range(3):  # warm the path (the first host-buffer call allocates its staging)
+        e2e_step(i)
     ctx.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0 = time.perf_counter()
     e0.record()
     for i in range(e2e_steps):
-        _lib.call("j4b_h2d", xin.ptr, ctypes.c_void_p(x_host.data_ptr()), x_host.numel() * 4, stream)
-        be.quant_matvec(weights[i % copies], xin, out=out)
-        _lib.call("j4b_d2h", ctypes.c_void_p(y_host.data_ptr()), out.ptr, y_host.numel() * 4, stream)
+        e2e_step(i)
     e1.record()
     host_issue_s = time.perf_counter() - t0
     ctx.barrier()
@@ -897,7 +907,9 @@ def measure_gemv(ctx, name, K, W, cpu_budget):
                                    kernel_avg_us, name),
         "cpu_baseline": cpu,
         "e2e": {"value": round(e2e_value, 3), "unit": "GB/s",
-                "h2d_bytes_per_step": batch * cols * 4, "d2h_bytes_per_step": batch * rows * 4,
+                "h2d_bytes_per_step": batch * cols * 4, "d2h_bytes_per_step": world * batch * rows * 4,
+                "call": "j4b_quant_matvec_host" if world == 1 else
+                        "j4b_h2d + j4b_quant_matvec_allgather + j4b_d2h",
                 "host_issue_us_per_step": round(host_issue_s * 1e6 / e2e_steps, 2),
                 "device_us_per_step": round(e_ms * 1e3 / e2e_steps, 2)},
         "gpu_launches": K * launches,

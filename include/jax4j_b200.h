@@ -205,6 +205,12 @@ int j4b_quant_shape(j4b_qweight_t w, int* ggml_type, int64_t* rows, int64_t* col
  * fp32-accurate mode. Either way relative error ~1e-5 (bar 1e-4). */
 int j4b_quant_matvec(j4b_qweight_t w, j4b_buf x, j4b_buf add, j4b_buf y, int64_t batch,
                      j4b_stream s);
+/* The same with HOST buffers (QuantizedOps.java:26-30 as a host caller makes it: upload x, the
+ * product, download y): x [batch, cols] and y [batch, rows] f32 in host memory, batch 1..16. The
+ * copies and the GEMV are queued on the stream (asynchronous for pinned host memory); y is valid
+ * once the stream is synchronised. Device staging for x and y belongs to the weight (allocated
+ * by the first call), so calls on one weight must not overlap. */
+int j4b_quant_matvec_host(j4b_qweight_t w, const float* x, int64_t batch, float* y, j4b_stream s);
 /* Prefill projection (no reference counterpart: the reference only has the rank-1 quantMatvec):
  * y [m, rows] = x [m, cols] . W^T, f32 row-major, on the tcgen05 tensor cores. precision
  * 1 = bf16 operands (rel 1e-2); 0 or 2 = 3-term bf16 split of both operands (rel 1e-4). Q8_0,
@@ -241,7 +247,10 @@ int j4b_peer_status(j4b_peer_group* g, int* status);
  * every rank's buffer and y_all [batch, rows * nranks] receives the gathered result. batch <= 16. */
 int j4b_quant_matvec_allgather(j4b_qweight_t w, j4b_buf x, j4b_buf add, j4b_buf y_all, int64_t batch,
                                j4b_peer_group* g, int channel, j4b_stream s);
-/* out[i] = sum over ranks of src[i], summed in rank order (identical on every rank), n <= 131072. */
+/* out[i] = sum over ranks of src[i], summed in rank order (identical on every rank). Both
+ * collectives move 8-byte flagged words (value + step flag): a channel's slice of `bytes` holds
+ * two parity halves, so a gathered output (batch * rows * nranks floats) or an all-reduce
+ * (n * nranks floats) may take up to (bytes - 131072) / 16 / 16 words. */
 int j4b_peer_allreduce(j4b_peer_group* g, int channel, j4b_buf src, int64_t n, j4b_buf out,
                        j4b_stream s);
 

@@ -90,6 +90,7 @@ SIGNATURES = {
     "j4b_quant_free": [_vp],
     "j4b_quant_shape": [_vp, ctypes.POINTER(ctypes.c_int), _i64p, _i64p],
     "j4b_quant_matvec": [_vp, _u64, _u64, _u64, _i64, _vp],
+    "j4b_quant_matvec_host": [_vp, _vp, _i64, _vp, _vp],
     "j4b_quant_gather_row": [_vp, _i64, _u64, _vp],
     "j4b_quantize": [_int, _u64, _i64, _i64, _u64, _vp],
     "j4b_quant_gemm": [_vp, _u64, _u64, _i64, _int, _vp],

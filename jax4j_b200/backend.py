@@ -465,6 +465,20 @@ class B200Backend:
              batch, self.stream)
         return out
 
+    def quant_matvec_host(self, w: QuantBuffer, x_host: torch.Tensor, y_host: torch.Tensor,
+                          stream: int | None = None) -> None:
+        """quantMatvec with host buffers (j4b_quant_matvec_host): x_host [batch, cols] and y_host
+        [batch, rows] are contiguous f32 CPU tensors, pinned for asynchronous copies; y_host holds
+        the product once the stream has been synchronised. `stream` defaults to PyTorch's current
+        stream (a decode loop passes its handle once instead of looking it up every call)."""
+        rows, cols = w.shape
+        n = x_host.numel()
+        if n % cols or not 1 <= n // cols <= 16 or y_host.numel() != n // cols * rows:
+            raise ValueError(f"host quantMatvec shapes: W {w.shape}, x {tuple(x_host.shape)}, "
+                             f"y {tuple(y_host.shape)} (batch 1..16)")
+        call("j4b_quant_matvec_host", w.handle, x_host.data_ptr(), n // cols, y_host.data_ptr(),
+             self.stream if stream is None else stream)
+
     def quant_matvec_add(self, w: QuantBuffer, x: DeviceBuffer, add: DeviceBuffer):
         return self.quant_matvec(w, x, add)
 

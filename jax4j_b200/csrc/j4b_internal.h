@@ -84,20 +84,27 @@ int tc_split_rows(const float* src, int64_t rows, int64_t cols, int64_t ld, int6
 // ---- collectives over peer memory (peer.cu) ----
 constexpr int kMaxPeerRanks = 8;
 
-// Every all-gathering GEMV call adds exactly kPeerCallUnits to each rank's arrival counter of
-// its source (CTA 0 adds kPeerCallUnits - (grid - 1), every other CTA 1), whatever its grid, so
-// calls of different shapes can share a channel: source s has finished step k once its counter
-// reaches (k + 1) x kPeerCallUnits (compared modulo 2^32). A launch needs grid <= kPeerCallUnits.
-constexpr unsigned kPeerCallUnits = 1u << 20;
-
 // Where a GEMV's y goes when it is all-gathered over peer memory.
 struct GemvPeers {
   int nranks, rank;
-  float* y[kMaxPeerRanks];       // each rank's gathered buffer (the channel's data slice)
-  unsigned* ctr[kMaxPeerRanks];  // each rank's arrival counter for this rank as the source
-  const unsigned* step;          // this rank's step counter of the channel
-  int64_t half_floats;           // floats per parity half of the slice
+  unsigned long long* y[kMaxPeerRanks];  // each rank's gathered buffer (the channel's data slice)
+  const unsigned* step;                  // this rank's step counter of the channel
+  int64_t half_words;                    // flagged words per parity half of the slice
 };
+
+// A flagged word of the peer buffers: a float value in the low half, the step flag (step + 1) in
+// the high half, written and read as one 64-bit access (single-copy atomic), so a reader that
+// sees the flag of its step sees that step's value: no fence and no arrival counter between the
+// writer's data and the reader's wait.
+__device__ __forceinline__ void gather_store(unsigned long long* p, float v, unsigned flag) {
+  const unsigned long long w = ((unsigned long long)flag << 32) | __float_as_uint(v);
+  asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ unsigned long long gather_load(const unsigned long long* p) {
+  unsigned long long w;
+  asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+  return w;
+}
 int peer_group_ranks(const j4b_peer_group* g);
 int peer_gemv_targets(const j4b_peer_group* g, int channel, int64_t gathered_floats, GemvPeers* t);
 int peer_wait_copy(const j4b_peer_group* g, int channel, float* out, int64_t n, cudaStream_t stream);

@@ -8,19 +8,16 @@
 //
 // Every rank allocates one buffer (j4b_peer_alloc) and maps the others' (j4b_peer_open); a peer
 // group holds all of them. Layout of each rank's buffer:
-//   [0, 64)        step counter per channel (local; selects the parity half, advanced once per
-//                  collective call by the rank's own kernel)
-//   [64, 128)      arrival counter of the calling kernel's CTAs per channel (local)
-//   [4096, 69632)  arrival counters per channel: [channel][slot], slot = chunk * 8 + source
-//   [131072, end)  data, one slice per channel, each split into two parity halves
-// Step k of a channel is complete for source s once
-//   - GEMV all-gather: s's arrival counter reaches (k + 1) x kPeerCallUnits (every call adds
-//     exactly that many units, whatever its grid);
-//   - all-reduce: the chunk's slot holds the epoch k + 1 (stored by s after its chunk's data, so
-//     a chunk that earlier calls did not use carries no stale count);
-// both compared modulo 2^32. The data of consecutive steps alternates halves, so a rank that runs
-// one step ahead never overwrites what a slower rank still reads (and no rank gets further ahead:
-// each step waits for every rank's arrival at that step).
+//   [0, 64)        step counter per channel (local; selects the parity half and the flag, advanced
+//                  once per collective call by the rank's own kernel)
+//   [64, 128)      finished-CTA counter of the reading kernel per channel (local)
+//   [131072, end)  data, one slice per channel, each split into two parity halves of flagged
+//                  words (gather_store: value and step flag in one 64-bit store)
+// A reader of step k waits, word by word, until the flag k + 1 appears: no fence, arrival
+// counter or remote atomic sits between a writer's data and the reader. The data of consecutive
+// steps alternates halves, so a rank that runs one step ahead never overwrites what a slower rank
+// still reads, and no rank gets two steps ahead: step k + 1 of every rank waits for every rank's
+// words of step k + 1, which each rank writes only after its own step k is read.
 // Every wait is bounded (about a second); a wait that gives up sets the group's status word.
 #include <cuda_runtime.h>
 
@@ -28,116 +25,35 @@
 #include <cstring>
 
 #include "j4b_internal.h"
+#include "j4b_wait.cuh"
 
 namespace j4b {
 namespace {
 
 constexpr int kChannels = 16;
-constexpr size_t kCtrOffset = 4096, kDataOffset = 131072;
-constexpr int kSlotsPerChannel = 1024;
-constexpr uint32_t kPeerWaitLimit = 1u << 24;
-
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-// v has not yet reached target, modulo 2^32.
-__device__ __forceinline__ bool before(unsigned v, unsigned target) { return (int)(v - target) < 0; }
+constexpr size_t kDataOffset = 131072;
+constexpr uint64_t kPeerWaitNs = 1000000000ull;  // one second
 
 struct PeerBases {
   uint8_t* base[kMaxPeerRanks];
 };
 
-// Waits until every source's arrival counter reaches (step + 1) x kPeerCallUnits, then copies
-// this rank's gathered half to `out`; the last CTA advances the step counter.
-// Launched as a programmatic dependent of the GEMV: it may start while the GEMV still runs (it
-// reads only the arrival counters, the step counter and the gathered data the counters vouch
-// for), and it releases its own dependents at once so the next kernel's prologue -- the next
-// GEMV's weight prefetch -- overlaps the wait.
-__global__ void wait_copy_kernel(unsigned* step, unsigned* done, const unsigned* ctr, int nranks,
-                                 const float* data, int64_t half_floats, float* out, int64_t n,
-                                 int* status) {
-  __shared__ unsigned s_step;
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  if (threadIdx.x == 0) {
-    const unsigned s = *(volatile unsigned*)step;
-    const unsigned target = (s + 1u) * kPeerCallUnits;
-    for (int src = 0; src < nranks; ++src) {
-      uint32_t it = 0;
-      while (before(ld_acquire_sys(ctr + src), target)) {
-        if (++it > kPeerWaitLimit) {
-          atomicExch(status, 1);
-          break;
-        }
-        __nanosleep(32);
-      }
+// Waits (bounded) for the flag of step `want` in a flagged word and returns its value; on a
+// timeout sets *timed_out (and every later word of the thread is taken as it is).
+__device__ __forceinline__ float wait_word(const unsigned long long* p, unsigned want, uint64_t t0, bool& timed_out) {
+  unsigned long long w = gather_load(p);
+  while ((unsigned)(w >> 32) != want && !timed_out) {
+    if (global_ns() - t0 > kPeerWaitNs) {
+      timed_out = true;
+      break;
     }
-    s_step = s;
+    w = gather_load(p);
   }
-  __syncthreads();
-  const float* src = data + (int64_t)(s_step & 1u) * half_floats;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
-    out[i] = src[i];
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    if (atomicAdd(done, 1u) == gridDim.x - 1) {
-      *done = 0u;
-      *(volatile unsigned*)step = s_step + 1u;
-    }
-  }
+  return __uint_as_float((unsigned)w);
 }
 
-// One CTA per 1024-element chunk: write the chunk into slot `rank` of every rank, publish the
-// step's epoch in the chunk's counter slot at every rank, wait for every source's epoch, sum the
-// slots in rank order.
-__global__ void allreduce_kernel(PeerBases bases, int nranks, int rank, int channel, int64_t slice_floats,
-                                 const float* src, int64_t n, float* out, int* status) {
-  constexpr int kChunk = 1024;
-  __shared__ unsigned s_step;
-  uint8_t* mine = bases.base[rank];
-  unsigned* step = reinterpret_cast<unsigned*>(mine) + channel;
-  unsigned* done = reinterpret_cast<unsigned*>(mine + 64) + channel;
-  if (threadIdx.x == 0) s_step = *(volatile unsigned*)step;
-  __syncthreads();
-  const unsigned s = s_step;
-  const int64_t half = slice_floats / 2;
-  const int64_t par = (int64_t)(s & 1u) * half;
-  const int64_t c = blockIdx.x, i0 = c * kChunk, i1 = min(n, i0 + kChunk);
-  for (int p = 0; p < nranks; ++p) {
-    float* dst = reinterpret_cast<float*>(bases.base[p] + kDataOffset) + channel * slice_floats + par + (int64_t)rank * n;
-    for (int64_t i = i0 + threadIdx.x; i < i1; i += blockDim.x) dst[i] = src[i];
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence_system();
-    for (int p = 0; p < nranks; ++p) {
-      unsigned* ctr = reinterpret_cast<unsigned*>(bases.base[p] + kCtrOffset) + channel * kSlotsPerChannel;
-      st_release_sys(ctr + c * 8 + rank, s + 1u);
-    }
-    const unsigned* mctr = reinterpret_cast<const unsigned*>(mine + kCtrOffset) + channel * kSlotsPerChannel;
-    for (int q = 0; q < nranks; ++q) {
-      uint32_t it = 0;
-      while (before(ld_acquire_sys(mctr + c * 8 + q), s + 1u)) {
-        if (++it > kPeerWaitLimit) {
-          atomicExch(status, 1);
-          break;
-        }
-        __nanosleep(32);
-      }
-    }
-  }
-  __syncthreads();
-  const float* slots = reinterpret_cast<const float*>(mine + kDataOffset) + channel * slice_floats + par;
-  for (int64_t i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
-    float acc = slots[i];
-    for (int q = 1; q < nranks; ++q) acc = __fadd_rn(acc, slots[(int64_t)q * n + i]);
-    out[i] = acc;
-  }
+// The last CTA of the reading kernel to finish advances the channel's step counter.
+__device__ __forceinline__ void finish_step(unsigned* step, unsigned* done, unsigned s) {
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();
@@ -146,6 +62,55 @@ __global__ void allreduce_kernel(PeerBases bases, int nranks, int rank, int chan
       *(volatile unsigned*)step = s + 1u;
     }
   }
+}
+
+// Copies this rank's gathered half (every source's flagged words of this step) to `out` once the
+// flags show up, then advances the step counter. Launched as a programmatic dependent of the
+// GEMV; it lets its own dependents launch at once (the next GEMV's weight prefetch overlaps the
+// wait), and it waits for the GEMV to finish before it reads the step counter, which the previous
+// step's copy advanced (a launch two kernels back is not otherwise ordered before this one).
+__global__ void wait_copy_kernel(unsigned* step, unsigned* done, const unsigned long long* data, int64_t half_words,
+                                 float* out, int64_t n, int* status) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const unsigned s = *(volatile unsigned*)step;
+  const unsigned long long* src = data + (int64_t)(s & 1u) * half_words;
+  const uint64_t t0 = global_ns();
+  bool timed_out = false;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    out[i] = wait_word(src + i, s + 1u, t0, timed_out);
+  if (timed_out) atomicExch(status, 1);
+  finish_step(step, done, s);
+}
+
+// One CTA per 1024-element chunk: write the chunk into slot `rank` of every rank as flagged words,
+// then read slot q of every source q from this rank's buffer as its flags appear and sum the
+// slots in rank order.
+__global__ void allreduce_kernel(PeerBases bases, int nranks, int rank, int channel, int64_t slice_words,
+                                 const float* src, int64_t n, float* out, int* status) {
+  constexpr int kChunk = 1024;
+  uint8_t* mine = bases.base[rank];
+  unsigned* step = reinterpret_cast<unsigned*>(mine) + channel;
+  unsigned* done = reinterpret_cast<unsigned*>(mine + 64) + channel;
+  const unsigned s = *(volatile unsigned*)step;
+  const int64_t par = (int64_t)(s & 1u) * (slice_words / 2);
+  const int64_t i0 = (int64_t)blockIdx.x * kChunk, i1 = min(n, i0 + kChunk);
+  for (int p = 0; p < nranks; ++p) {
+    unsigned long long* dst =
+        reinterpret_cast<unsigned long long*>(bases.base[p] + kDataOffset) + channel * slice_words + par + (int64_t)rank * n;
+    for (int64_t i = i0 + threadIdx.x; i < i1; i += blockDim.x) gather_store(dst + i, src[i], s + 1u);
+  }
+  const unsigned long long* slots =
+      reinterpret_cast<const unsigned long long*>(mine + kDataOffset) + channel * slice_words + par;
+  const uint64_t t0 = global_ns();
+  bool timed_out = false;
+  for (int64_t i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
+    float acc = wait_word(slots + i, s + 1u, t0, timed_out);
+    for (int q = 1; q < nranks; ++q) acc = __fadd_rn(acc, wait_word(slots + (int64_t)q * n + i, s + 1u, t0, timed_out));
+    out[i] = acc;
+  }
+  if (timed_out) atomicExch(status, 1);
+  finish_step(step, done, s);
 }
 
 }  // namespace
@@ -247,33 +212,34 @@ namespace j4b {
 
 int peer_group_ranks(const j4b_peer_group* g) { return g->nranks; }
 
-int64_t peer_slice_floats(const j4b_peer_group* g) {
-  return (int64_t)(((g->bytes - kDataOffset) / kChannels) / 256 * 256 / 4);
+// Flagged words per channel slice (both parity halves).
+int64_t peer_slice_words(const j4b_peer_group* g) {
+  return (int64_t)(((g->bytes - kDataOffset) / kChannels) / 256 * 256 / 8);
 }
 
-// Fills the GEMV's peer targets for `channel` and launches the waiting copy after it.
+// Fills the GEMV's peer targets for `channel`.
 int peer_gemv_targets(const j4b_peer_group* g, int channel, int64_t gathered_floats, GemvPeers* t) {
   J4B_REQUIRE(channel >= 0 && channel < kChannels, "channel %d out of range", channel);
-  const int64_t slice = peer_slice_floats(g);
-  J4B_REQUIRE(2 * gathered_floats <= slice, "peer buffer slice too small for the gathered output");
+  const int64_t slice = peer_slice_words(g);
+  J4B_REQUIRE(2 * gathered_floats <= slice,
+              "peer buffer slice too small for the gathered output (%lld words per parity half, %lld needed)",
+              (long long)(slice / 2), (long long)gathered_floats);
   t->nranks = g->nranks;
   t->rank = g->rank;
-  t->half_floats = slice / 2;
+  t->half_words = slice / 2;
   t->step = reinterpret_cast<const unsigned*>(g->base[g->rank]) + channel;
-  for (int p = 0; p < g->nranks; ++p) {
-    t->y[p] = reinterpret_cast<float*>(g->base[p] + kDataOffset) + channel * slice;
-    t->ctr[p] = reinterpret_cast<unsigned*>(g->base[p] + kCtrOffset) + channel * kSlotsPerChannel + g->rank;
-  }
+  for (int p = 0; p < g->nranks; ++p)
+    t->y[p] = reinterpret_cast<unsigned long long*>(g->base[p] + kDataOffset) + channel * slice;
   return J4B_OK;
 }
 
+// Launches the waiting copy of the gathered output after the GEMV.
 int peer_wait_copy(const j4b_peer_group* g, int channel, float* out, int64_t n, cudaStream_t stream) {
   uint8_t* mine = g->base[g->rank];
-  const int64_t slice = peer_slice_floats(g);
+  const int64_t slice = peer_slice_words(g);
   unsigned* step = reinterpret_cast<unsigned*>(mine) + channel;
   unsigned* done = reinterpret_cast<unsigned*>(mine + 64) + channel;
-  const unsigned* ctr = reinterpret_cast<const unsigned*>(mine + kCtrOffset) + channel * kSlotsPerChannel;
-  const float* data = reinterpret_cast<const float*>(mine + kDataOffset) + channel * slice;
+  const unsigned long long* data = reinterpret_cast<const unsigned long long*>(mine + kDataOffset) + channel * slice;
   const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>((n + 1023) / 1024, 148));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
@@ -284,8 +250,7 @@ int peer_wait_copy(const j4b_peer_group* g, int channel, float* out, int64_t n, 
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  J4B_CUDA(cudaLaunchKernelEx(&cfg, wait_copy_kernel, step, done, ctr, g->nranks, data, slice / 2, out, n,
-                              g->status),
+  J4B_CUDA(cudaLaunchKernelEx(&cfg, wait_copy_kernel, step, done, data, slice / 2, out, n, g->status),
            "wait_copy_kernel");
   count_launch();
   return J4B_OK;
@@ -298,10 +263,9 @@ extern "C" int j4b_peer_allreduce(j4b_peer_group* g, int channel, j4b_buf src, i
   J4B_REQUIRE(g != nullptr, "null peer group");
   J4B_REQUIRE(channel >= 0 && channel < kChannels, "channel %d out of range", channel);
   J4B_REQUIRE(n >= 1 && src && out, "all-reduce needs n >= 1 and buffers");
-  J4B_REQUIRE((n + 1023) / 1024 * 8 <= kSlotsPerChannel, "all-reduce of %lld elements exceeds the counter slots",
-              (long long)n);
-  const int64_t slice = peer_slice_floats(g);
+  const int64_t slice = peer_slice_words(g);
   J4B_REQUIRE(2 * (int64_t)g->nranks * n <= slice, "peer buffer slice too small for the all-reduce");
+  J4B_REQUIRE((n + 1023) / 1024 <= 0x7fffffffLL, "all-reduce of %lld elements is too long", (long long)n);
   DeviceGuard guard(g->dev);
   cudaStream_t stream = resolve_stream(g->dev, s);
   PeerBases b;

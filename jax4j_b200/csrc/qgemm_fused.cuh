@@ -34,14 +34,28 @@ constexpr int qg_threads() { return (6 + qg_decode_warps<TERMS, N, NH>()) * 32; 
 
 // N tokens per MMA, NH accumulators of N columns each per CTA (NH = 2, N = 256: 512 tokens in bf16
 // mode, the whole TMEM, one CTA per SM; N = 64: decode-time batches).
+// Two rings: A (the decoded weight tile, written by the decoders) and B (the activation tiles,
+// TMA). The 512-token prefill tile gives B a third stage (3 x 64 KB + 2 x 16 KB): a B copy comes
+// from L2 or HBM and needs more lead than the decode of the next A tile from registers.
 template <int TERMS, int N, int NH>
 constexpr int qg_stages() { return (TERMS == 1 && N * NH <= 256) ? 2 : (TERMS == 3 && N * NH <= 128 ? 3 : 2); }
+template <int TERMS, int N, int NH>
+constexpr int qg_stages_a() { return qg_stages<TERMS, N, NH>(); }
+template <int TERMS, int N, int NH>
+constexpr int qg_stages_b() { return (TERMS == 1 && N * NH == 512) ? 3 : qg_stages<TERMS, N, NH>(); }
 constexpr uint32_t kQgABytes = kQgBM * kQgBK * 2;  // one 128 x 64 bf16 tile
 template <int N, int NH>
 constexpr uint32_t qg_b_bytes() { return (uint32_t)(NH * N) * kQgBK * 2; }
-// stage: A hi | B hi | (A lo | B lo); a B part holds the NH token boxes one after the other
+// A stage: A hi (| A lo); B stage: B hi (| B lo), a B part holding the NH token boxes in a row
+template <int TERMS>
+constexpr uint32_t qg_a_stage_bytes() { return (TERMS == 3 ? 2u : 1u) * kQgABytes; }
 template <int TERMS, int N, int NH>
-constexpr uint32_t qg_stage_bytes() { return (TERMS == 3 ? 2u : 1u) * (kQgABytes + qg_b_bytes<N, NH>()); }
+constexpr uint32_t qg_b_stage_bytes() { return (TERMS == 3 ? 2u : 1u) * qg_b_bytes<N, NH>(); }
+template <int TERMS, int N, int NH>
+constexpr uint32_t qg_ring_bytes() {
+  return qg_stages_a<TERMS, N, NH>() * qg_a_stage_bytes<TERMS>() +
+         qg_stages_b<TERMS, N, NH>() * qg_b_stage_bytes<TERMS, N, NH>();
+}
 template <int TERMS, int N, int NH>
 constexpr int qg_min_blocks() { return (TERMS == 1 && N * NH <= 256) ? 2 : 1; }
 template <int TERMS, int N, int NH>
@@ -194,16 +208,19 @@ __global__ void __launch_bounds__(qg_threads<TERMS, N, NH>(), qg_min_blocks<TERM
     qgemm_fused_kernel(const __grid_constant__ CUtensorMap x_hi, const __grid_constant__ CUtensorMap x_lo, QgArgs p) {
   constexpr int kN = N;                // tokens per MMA
   constexpr int kBN = NH * kN;         // tokens per tile (TMEM columns)
-  constexpr int kStages = qg_stages<TERMS, N, NH>();
-  constexpr uint32_t kStage = qg_stage_bytes<TERMS, N, NH>();
+  constexpr int kSA = qg_stages_a<TERMS, N, NH>();
+  constexpr int kSB = qg_stages_b<TERMS, N, NH>();
+  constexpr uint32_t kAStage = qg_a_stage_bytes<TERMS>();
+  constexpr uint32_t kBStage = qg_b_stage_bytes<TERMS, N, NH>();
   constexpr uint32_t kB = qg_b_bytes<N, NH>();
   constexpr uint32_t kBox = (uint32_t)kN * kQgBK * 2;  // one token box
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full_a = reinterpret_cast<uint64_t*>(smem + kStages * kStage);
-  uint64_t* full_b = full_a + kStages;
-  uint64_t* empty = full_b + kStages;
-  uint64_t* acc_full = empty + kStages;
+  uint64_t* full_a = reinterpret_cast<uint64_t*>(smem + qg_ring_bytes<TERMS, N, NH>());
+  uint64_t* empty_a = full_a + kSA;
+  uint64_t* full_b = empty_a + kSA;
+  uint64_t* empty_b = full_b + kSB;
+  uint64_t* acc_full = empty_b + kSB;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -217,14 +234,17 @@ __global__ void __launch_bounds__(qg_threads<TERMS, N, NH>(), qg_min_blocks<TERM
   const int kb0 = split * p.kb_per;
   const int nk = min(p.kp / kQgBK - kb0, p.kb_per);  // k-blocks of this CTA, from kb0
   float* out = p.y + (int64_t)split * p.m * p.rows;
-  auto stage_a = [&](int s, int lo) { return smem + s * kStage + (lo ? kQgABytes + kB : 0); };
-  auto stage_b = [&](int s, int lo) { return smem + s * kStage + kQgABytes + (lo ? kQgABytes + kB : 0); };
+  auto stage_a = [&](int s, int lo) { return smem + s * kAStage + (lo ? kQgABytes : 0); };
+  auto stage_b = [&](int s, int lo) { return smem + kSA * kAStage + s * kBStage + (lo ? kB : 0); };
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < kSA; ++s) {
       bar_init(&full_a[s], qg_decode_warps<TERMS, N, NH>());
+      bar_init(&empty_a[s], 1);
+    }
+    for (int s = 0; s < kSB; ++s) {
       bar_init(&full_b[s], 1);
-      bar_init(&empty[s], 1);
+      bar_init(&empty_b[s], 1);
     }
     bar_init(acc_full, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -243,9 +263,9 @@ __global__ void __launch_bounds__(qg_threads<TERMS, N, NH>(), qg_min_blocks<TERM
   if (warp == 0) {
     if (lane == 0) {  // x tiles
       for (int kb = 0; kb < nk; ++kb) {
-        const int s = kb % kStages, use = kb / kStages;
-        if (use > 0 && !bar_wait(&empty[s], (uint32_t)((use - 1) & 1))) ok = false;
-        bar_expect_tx(&full_b[s], (TERMS == 3 ? 2u : 1u) * kB);
+        const int s = kb % kSB, use = kb / kSB;
+        if (use > 0 && !bar_wait(&empty_b[s], (uint32_t)((use - 1) & 1))) ok = false;
+        bar_expect_tx(&full_b[s], kBStage);
         const int kx = (kb0 + kb) * kQgBK;
 #pragma unroll
         for (int h = 0; h < NH; ++h) {
@@ -258,12 +278,12 @@ __global__ void __launch_bounds__(qg_threads<TERMS, N, NH>(), qg_min_blocks<TERM
     if (lane == 0) {  // MMA issue
       constexpr uint32_t idesc = idesc_bf16(kQgBM, kN);
       for (int kb = 0; kb < nk; ++kb) {
-        const int s = kb % kStages, par = (kb / kStages) & 1;
-        if (!bar_wait(&full_a[s], (uint32_t)par)) ok = false;
-        if (!bar_wait(&full_b[s], (uint32_t)par)) ok = false;
+        const int sa = kb % kSA, sb = kb % kSB;
+        if (!bar_wait(&full_a[sa], (uint32_t)((kb / kSA) & 1))) ok = false;
+        if (!bar_wait(&full_b[sb], (uint32_t)((kb / kSB) & 1))) ok = false;
         tc_fence_after();
-        const uint32_t ah = saddr(stage_a(s, 0)), bh = saddr(stage_b(s, 0));
-        const uint32_t al = saddr(stage_a(s, 1)), bl = saddr(stage_b(s, 1));
+        const uint32_t ah = saddr(stage_a(sa, 0)), bh = saddr(stage_b(sb, 0));
+        const uint32_t al = saddr(stage_a(sa, 1)), bl = saddr(stage_b(sb, 1));
 #pragma unroll
         for (int k = 0; k < kQgBK / 16; ++k) {  // 16 bf16 = 32 bytes along the swizzled row
           const uint64_t dah = kmajor_sw128(ah + k * 32);
@@ -278,7 +298,8 @@ __global__ void __launch_bounds__(qg_threads<TERMS, N, NH>(), qg_min_blocks<TERM
             }
           }
         }
-        umma_commit(&empty[s]);  // the stage is free once these MMAs have read it
+        umma_commit(&empty_a[sa]);  // the stages are free once these MMAs have read them
+        umma_commit(&empty_b[sb]);
       }
       umma_commit(acc_full);
     }
@@ -317,12 +338,12 @@ __global__ void __launch_bounds__(qg_threads<TERMS, N, NH>(), qg_min_blocks<TERM
 #pragma unroll
     for (int i = 0; i < kT; ++i) qg_load<QT>(p, tile0 + i, kb0, lane, cur[i]);
     for (int kb = 0; kb < nk; ++kb) {
-      const int s = kb % kStages, use = kb / kStages;
+      const int s = kb % kSA, use = kb / kSA;
       if (kb + 1 < nk) {
 #pragma unroll
         for (int i = 0; i < kT; ++i) qg_load<QT>(p, tile0 + i, kb0 + kb + 1, lane, nxt[i]);
       }
-      if (use > 0 && !bar_wait(&empty[s], (uint32_t)((use - 1) & 1))) ok = false;
+      if (use > 0 && !bar_wait(&empty_a[s], (uint32_t)((use - 1) & 1))) ok = false;
       uint8_t* ahi = stage_a(s, 0);
       uint8_t* alo = stage_a(s, 1);
 #pragma unroll
@@ -359,7 +380,7 @@ template <int QT, int TERMS, int N, int NH>
 cudaError_t launch_qgemm_fused(const j4b_qweight* w, const CUtensorMap& xh, const CUtensorMap& xl, int m, int kp,
                                int splits, int kb_per, float* out, const float* add, cudaStream_t stream) {
   constexpr int kBN = NH * N;
-  const size_t smem = (size_t)qg_stages<TERMS, N, NH>() * qg_stage_bytes<TERMS, N, NH>() + 1024 + 256;
+  const size_t smem = (size_t)qg_ring_bytes<TERMS, N, NH>() + 1024 + 256;
   static bool attr_set[kMaxDevices] = {};
   if (w->dev < 0 || w->dev >= kMaxDevices) return cudaErrorInvalidDevice;
   if (!attr_set[w->dev]) {

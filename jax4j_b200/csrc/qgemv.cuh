@@ -157,37 +157,38 @@ struct GemvArgs {
   unsigned* arrivals;  // one counter per tile group
   int* status;         // nonzero after a bounded wait gave up
   // All-gather over peer memory (nranks > 1): this rank's rows of y go straight into every
-  // rank's gathered buffer, [batch][rows * nranks] in the parity half selected by the local step
-  // counter, and every CTA counts one arrival at every rank after its stores.
+  // rank's gathered buffer, [batch][rows * nranks] flagged words in the parity half selected by
+  // the local step counter (see gather_store).
   int nranks, rank;
-  float* peer_y[kMaxPeerRanks];
-  unsigned* peer_ctr[kMaxPeerRanks];  // at rank p: the counter of this rank as a source
+  unsigned long long* peer_y[kMaxPeerRanks];
   const unsigned* step;
-  int64_t half_floats;
+  int64_t half_words;
 };
 
+// Where this launch's outputs go in the gathered buffers: the parity half's offset and the flag
+// of this step (step + 1). Read after the dependency wait.
+struct GatherSlot {
+  int64_t off = 0;
+  unsigned flag = 0;
+};
+__device__ __forceinline__ GatherSlot gather_slot(const GemvArgs& a) {
+  GatherSlot g;
+  if (a.nranks > 1) {
+    const unsigned st = *a.step;
+    g.off = (int64_t)(st & 1u) * a.half_words;
+    g.flag = st + 1u;
+  }
+  return g;
+}
+
 // Stores one output, locally or into every rank's gathered buffer.
-__device__ __forceinline__ void store_y(const GemvArgs& a, int64_t par_off, int bcol, int64_t r, float v) {
+__device__ __forceinline__ void store_y(const GemvArgs& a, const GatherSlot& gs, int bcol, int64_t r, float v) {
   if (a.nranks <= 1) {
     a.y[(int64_t)bcol * a.rows + r] = v;
     return;
   }
-  const int64_t idx = par_off + (int64_t)bcol * (a.rows * a.nranks) + (int64_t)a.rank * a.rows + r;
-  for (int p = 0; p < a.nranks; ++p) a.peer_y[p][idx] = v;
-}
-
-// After this CTA's last store: the CTA barrier orders every thread's stores before thread 0's
-// system-scope fence, which orders them before the arrival counted at every rank. The CTAs of
-// one launch add kPeerCallUnits in total (CTA 0 the remainder), so the count per call does not
-// depend on the grid. Called by every thread of the CTA on each exit path.
-__device__ __forceinline__ void signal_peers(const GemvArgs& a) {
-  if (a.nranks <= 1) return;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const unsigned units = blockIdx.x == 0 ? kPeerCallUnits - (gridDim.x - 1u) : 1u;
-    __threadfence_system();
-    for (int p = 0; p < a.nranks; ++p) atomicAdd_system(a.peer_ctr[p], units);
-  }
+  const int64_t idx = gs.off + (int64_t)bcol * (a.rows * a.nranks) + (int64_t)a.rank * a.rows + r;
+  for (int p = 0; p < a.nranks; ++p) gather_store(a.peer_y[p] + idx, v, gs.flag);
 }
 
 constexpr int kXStride = 1024 + 4;  // floats per staged x row (padding spreads the banks)
@@ -572,7 +573,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) qgemv_kernel(GemvArgs a) {
   __shared__ int last_flag;
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  int64_t par_off = 0;  // parity half of the gathered buffer, read after the dependency wait
+  GatherSlot gslot;  // where outputs go when all-gathered; read after the dependency wait
   // 16 warps: warp w works on the 128-column chunk w % 8 of the CTA's K range, for the tiles of
   // each stage whose index has the parity w / 8.
   const int chunk = warp & 7, sub = warp >> 3;
@@ -612,7 +613,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) qgemv_kernel(GemvArgs a) {
     for (; issued < kStages && issued < ncopies; issued++) issue(issued);
   pdl_launch_dependents();
   pdl_wait();
-  if (a.nranks > 1) par_off = (int64_t)(*a.step & 1u) * a.half_floats;
+  gslot = gather_slot(a);
 
   // ---- x: the CTA's 1024-column slice of every batch row, staged once in shared memory with
   // coalesced 128-bit loads (columns past K and rows past the batch are zeros) ----
@@ -758,7 +759,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) qgemv_kernel(GemvArgs a) {
         const int64_t r = tile * 16 + row;
         if (r < a.rows && bcol < a.batch) {
           if (a.add) total += a.add[(int64_t)bcol * a.rows + r];
-          store_y(a, par_off, bcol, r, total);
+          store_y(a, gslot, bcol, r, total);
         }
       } else if (a.cluster) {
         mine[(c * kM + j) * kVals + v] = total;
@@ -777,10 +778,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) qgemv_kernel(GemvArgs a) {
         mbar_wait_bounded(&full[cc % kStages], (uint32_t)((cc / kStages) & 1));
     }
     __syncthreads();
-    if (!a.cluster) {
-      signal_peers(a);
-      return;  // cluster members still take both cluster barriers below
-    }
+    if (!a.cluster) return;  // cluster members still take both cluster barriers below
   }
 
   if (a.cluster) {
@@ -805,11 +803,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) qgemv_kernel(GemvArgs a) {
         const int64_t r = tile0 * 16 + rr;
         if (r < a.rows) {
           if (a.add) total += a.add[(int64_t)bcol * a.rows + r];
-          store_y(a, par_off, bcol, r, total);
+          store_y(a, gslot, bcol, r, total);
         }
       }
     }
-    signal_peers(a);
     return;
   }
 
@@ -818,10 +815,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) qgemv_kernel(GemvArgs a) {
     __syncthreads();
     if (threadIdx.x == 0) last_flag = atomicAdd(a.arrivals + group, 1u) == (unsigned)(a.ksplit - 1);
     __syncthreads();
-    if (!last_flag) {
-      signal_peers(a);
-      return;
-    }
+    if (!last_flag) return;
     __threadfence();
     // The last CTA of the group folds the K splits in split order (deterministic), walking the
     // outputs row-fastest; four outputs per thread per pass keep their loads in flight together.
@@ -849,13 +843,12 @@ __global__ void __launch_bounds__(kGemvThreads, 1) qgemv_kernel(GemvArgs a) {
         if (r < a.rows) {
           float v = tot[u];
           if (a.add) v += a.add[(int64_t)bcol * a.rows + r];
-          store_y(a, par_off, bcol, r, v);
+          store_y(a, gslot, bcol, r, v);
         }
       }
     }
     if (threadIdx.x == 0) a.arrivals[group] = 0u;
   }
-  signal_peers(a);
 }
 
 template <int QT, int NT, bool PK>
@@ -898,20 +891,14 @@ cudaError_t launch_gemv(const j4b_qweight* w, const float* x, const float* add, 
   a.nranks = 1;
   a.rank = 0;
   a.step = nullptr;
-  a.half_floats = 0;
-  for (int p = 0; p < kMaxPeerRanks; ++p) {
-    a.peer_y[p] = nullptr;
-    a.peer_ctr[p] = nullptr;
-  }
+  a.half_words = 0;
+  for (int p = 0; p < kMaxPeerRanks; ++p) a.peer_y[p] = nullptr;
   if (peers) {
     a.nranks = peers->nranks;
     a.rank = peers->rank;
     a.step = peers->step;
-    a.half_floats = peers->half_floats;
-    for (int p = 0; p < peers->nranks; ++p) {
-      a.peer_y[p] = peers->y[p];
-      a.peer_ctr[p] = peers->ctr[p];
-    }
+    a.half_words = peers->half_words;
+    for (int p = 0; p < peers->nranks; ++p) a.peer_y[p] = peers->y[p];
   }
   // One 16-warp CTA per SM: as many tile groups as fit next to the K splits, tiles shared out
   // evenly.
@@ -969,7 +956,6 @@ cudaError_t launch_gemv(const j4b_qweight* w, const float* x, const float* add, 
   attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = a.cluster ? 2 : 1;
-  if (peers && cfg.gridDim.x > kPeerCallUnits) return cudaErrorInvalidConfiguration;
   if (grid_out) *grid_out = cfg.gridDim.x;
   return cudaLaunchKernelEx(&cfg, qgemv_kernel<QT, NT, PK>, a);
 }

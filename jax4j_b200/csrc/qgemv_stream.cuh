@@ -11,8 +11,9 @@
 //   - the last warp is the producer: one elected lane streams the run's tile chunks (contiguous in the
 //     split-major layout) into a ring of shared-memory stages with 1-D bulk copies, each stage
 //     completing on its `full` mbarrier; it refills a stage once the warps that read it have
-//     arrived on its `empty` mbarrier. The first ring's worth is issued before the dependency
-//     wait (weights are immutable once uploaded).
+//     arrived on its `empty` mbarrier. A run that fits the ring is issued whole before the
+//     dependency wait (weights are immutable once uploaded); of a longer run, about 48 KB, and
+//     the rest once x is staged.
 //   - the compute warps first turn x's 1024-column slice into fp16 hi/lo mma fragments in shared memory
 //     (warp w converts 128-column chunk w), then each warp takes whole tiles round-robin and
 //     walks the tile's 8 chunks itself, so a tile's partial sum over the split never leaves the
@@ -66,6 +67,34 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 template <int NW>
 __device__ __forceinline__ void compute_warps_sync() {
   asm volatile("bar.sync 1, %0;" ::"n"(NW * 32) : "memory");
+}
+// Barrier 2: the compute warps arrive once x is staged; the producer waits on it before it issues
+// the stages after the first ones. Global loads queue behind the SM's bulk copies in flight, so
+// x (read only after the dependency wait) would otherwise land behind the whole ring.
+template <int NW>
+__device__ __forceinline__ void x_staged_arrive() {
+  asm volatile("bar.arrive 2, %0;" ::"n"((NW + 1) * 32) : "memory");
+}
+template <int NW>
+__device__ __forceinline__ void x_staged_wait() {
+  asm volatile("bar.sync 2, %0;" ::"n"((NW + 1) * 32) : "memory");
+}
+// Stages issued before the dependency wait when the CTA's run is longer than the ring: about
+// 48 KB, what the SM's share of HBM bandwidth brings in while the previous kernel drains; the
+// rest waits for x, which the refills need anyway. A run that fits the ring is issued whole
+// before the wait (measured: Q8_0 4096 x 4096 at batch 8, 7 tiles per CTA, 8.2 us per call whole
+// against 9.0 us with 48 KB; Q4_K 14336 x 4096 at batch 1, 24 tiles per CTA, 14.9 us with 48 KB
+// against 16.5 us with the whole ring).
+template <int QT, bool PK, int NW>
+constexpr int stream_pre_stages() {
+  constexpr int stage = stream_tiles_per_stage<QT>() * GemvTraits<QT>::kChunk;
+  constexpr int r = stream_stages<QT, PK, NW>();
+  constexpr int p = 49152 / stage;
+  return p < 1 ? 1 : (p > r ? r : p);
+}
+template <int QT, bool PK, int NW>
+__device__ __forceinline__ int stream_pre_ring(int nstages) {
+  return nstages <= stream_stages<QT, PK, NW>() ? stream_stages<QT, PK, NW>() : stream_pre_stages<QT, PK, NW>();
 }
 // Waits (bounded) until the producer has issued stage `st` into its slot: only then is the slot's
 // `full` barrier on the phase of that stage, so its parity identifies the stage. (A warp can reach
@@ -241,10 +270,12 @@ __global__ void __launch_bounds__(stream_threads<NW>(), NW == 8 ? 2 : 1) qgemv_s
       tma_load_1d_stream(ring + (st % R) * kStage, a.data + a.L.chunk_offset(split, tile0 + first), bytes, bar,
                          policy);
     };
+    const int pre = stream_pre_ring<QT, PK, NW>(nstages);
     if (lane == 0)
-      for (; issued < R && issued < nstages; issued++) issue(issued);
+      for (; issued < pre && issued < nstages; issued++) issue(issued);
     pdl_launch_dependents();
     pdl_wait();
+    x_staged_wait<NW>();
     if (lane == 0) {
       for (; issued < nstages; issued++) {
         const int slot = issued % R;
@@ -260,9 +291,9 @@ __global__ void __launch_bounds__(stream_threads<NW>(), NW == 8 ? 2 : 1) qgemv_s
     // ---------------- compute warps ----------------
     pdl_launch_dependents();
     pdl_wait();
-    int64_t par_off = 0;  // parity half of the gathered buffer (peer all-gather only)
-    if (a.nranks > 1) par_off = (int64_t)(*a.step & 1u) * a.half_floats;
+    const GatherSlot gslot = gather_slot(a);  // peer all-gather only
     if (warp < nchunks) stream_prep_x<QT, PK>(a, kc0, warp, lane, frag);
+    x_staged_arrive<NW>();
     compute_warps_sync<NW>();
 
     for (int u = warp; u < ntiles; u += NW) {
@@ -376,7 +407,7 @@ __global__ void __launch_bounds__(stream_threads<NW>(), NW == 8 ? 2 : 1) qgemv_s
         if (r < a.rows && bcol < a.batch) {
           float v = acc[i];
           if (a.add) v += a.add[(int64_t)bcol * a.rows + r];
-          store_y(a, par_off, bcol, r, v);
+          store_y(a, gslot, bcol, r, v);
         }
       }
     }
@@ -393,7 +424,6 @@ __global__ void __launch_bounds__(stream_threads<NW>(), NW == 8 ? 2 : 1) qgemv_s
     }
     __syncthreads();
   }
-  signal_peers(a);
 }
 
 template <int QT, bool PK, int NW>
@@ -429,11 +459,8 @@ cudaError_t launch_gemv_stream(const j4b_qweight* w, const float* x, const float
     a.nranks = peers->nranks;
     a.rank = peers->rank;
     a.step = peers->step;
-    a.half_floats = peers->half_floats;
-    for (int p = 0; p < peers->nranks; ++p) {
-      a.peer_y[p] = peers->y[p];
-      a.peer_ctr[p] = peers->ctr[p];
-    }
+    a.half_words = peers->half_words;
+    for (int p = 0; p < peers->nranks; ++p) a.peer_y[p] = peers->y[p];
   }
   // one CTA per SM: as many tile groups as fit next to the K splits
   const int64_t groups = std::max<int64_t>(1, std::min<int64_t>(w->rt, (int64_t)sms / w->ksplit));
@@ -447,7 +474,6 @@ cudaError_t launch_gemv_stream(const j4b_qweight* w, const float* x, const float
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  if (peers && cfg.gridDim.x > kPeerCallUnits) return cudaErrorInvalidConfiguration;
   if (grid_out) *grid_out = cfg.gridDim.x;
   return cudaLaunchKernelEx(&cfg, qgemv_stream_kernel<QT, PK, NW>, a);
 }

@@ -56,6 +56,9 @@ struct j4b_qweight {
   // weights before it waits on the kernel before it; the first GEMV after an upload therefore
   // launches without it (host-side flag, cleared at that launch).
   bool fresh;
+  // Device staging of x and y for j4b_quant_matvec_host (16 rows of each), allocated by its first
+  // call; like the split-K scratch, it serialises the calls made on one weight.
+  float* io;
 };
 
 namespace j4b {
@@ -741,6 +744,10 @@ extern "C" int j4b_quant_free(j4b_qweight_t w) {
   cudaFree(w->partials);
   cudaFree(w->arrivals);
   counters().releases += w->partials ? 3 : 2;
+  if (w->io) {
+    cudaFree(w->io);
+    counters().releases += 1;
+  }
   delete w;
   return J4B_OK;
 }
@@ -796,6 +803,32 @@ extern "C" int j4b_quant_matvec(j4b_qweight_t w, j4b_buf x, j4b_buf add, j4b_buf
     if (e != cudaSuccess) return cuda_error(e, "qgemv_kernel");
     count_launch();
   }
+  return J4B_OK;
+}
+
+// quantMatvec with host buffers: x [batch, cols] is copied in, y [batch, rows] copied out, all on
+// the stream (pinned host buffers make both copies asynchronous; the caller synchronises the
+// stream before it reads y). One call per decode step from a host loop.
+extern "C" int j4b_quant_matvec_host(j4b_qweight_t w, const float* x, int64_t batch, float* y, j4b_stream s) {
+  if (!w) return set_error(J4B_EINVAL, "null quantized weight");
+  J4B_REQUIRE(batch >= 1 && batch <= 16, "host-buffer quantMatvec takes batch 1..16, got %lld", (long long)batch);
+  J4B_REQUIRE(x && y, "quantMatvec needs x and y host buffers");
+  DeviceGuard guard(w->dev);
+  cudaStream_t stream = resolve_stream(w->dev, s);
+  const int64_t xs = (w->cols + 3) / 4 * 4;  // keeps the y staging 16-byte aligned
+  if (!w->io) {
+    J4B_CUDA(cudaMalloc(&w->io, (size_t)16 * (xs + w->rows) * sizeof(float)), "cudaMalloc(quantMatvec staging)");
+    counters().allocations += 1;
+  }
+  float* dx = w->io;
+  float* dy = w->io + 16 * xs;
+  const size_t xb = (size_t)(batch * w->cols) * sizeof(float), yb = (size_t)(batch * w->rows) * sizeof(float);
+  J4B_CUDA(cudaMemcpyAsync(dx, x, xb, cudaMemcpyHostToDevice, stream), "cudaMemcpyAsync(HtoD)");
+  counters().h2d += xb;
+  const int st = j4b_quant_matvec(w, (j4b_buf)(uintptr_t)dx, 0, (j4b_buf)(uintptr_t)dy, batch, s);
+  if (st) return st;
+  J4B_CUDA(cudaMemcpyAsync(y, dy, yb, cudaMemcpyDeviceToHost, stream), "cudaMemcpyAsync(DtoH)");
+  counters().d2h += yb;
   return J4B_OK;
 }
 

@@ -86,6 +86,28 @@ def test_reference_shaped_call_and_add(backend, oracle):
         backend.quant_matvec(w, backend.upload(np.zeros(cols - 32, np.float32), (cols - 32,)))
 
 
+def test_host_buffer_call(backend, oracle):
+    """j4b_quant_matvec_host (copy in, GEMV, copy out on the stream) equals the device-buffer
+    call bit for bit, from pinned and from pageable host memory, and rejects bad shapes."""
+    import torch
+    rows, cols = 160, 4096
+    _, blob = make(oracle, Q4_K, rows, cols, 13)
+    w = backend.upload_quantized(blob, Q4_K, (rows, cols))
+    for batch in (1, 5, 16):
+        x = np.random.default_rng(batch).standard_normal((batch, cols)).astype(np.float32)
+        want = backend.download(backend.quant_matvec(w, backend.upload(x, x.shape)))
+        for pin in (True, False):
+            xh = torch.from_numpy(x)
+            yh = torch.zeros(batch * rows, dtype=torch.float32)
+            if pin:
+                xh, yh = xh.pin_memory(), yh.pin_memory()
+            backend.quant_matvec_host(w, xh, yh)
+            backend.sync()
+            assert np.array_equal(yh.numpy().reshape(batch, rows), want.reshape(batch, rows))
+    with pytest.raises(ValueError, match="batch 1..16"):
+        backend.quant_matvec_host(w, torch.zeros(17 * cols), torch.zeros(17 * rows))
+
+
 def test_repeated_calls_are_deterministic(backend, oracle):
     """The split-K arrival counters reset themselves: back-to-back calls agree bit for bit."""
     rows, cols = 160, 4096  # 4 K ranges
