@@ -233,8 +233,8 @@ SECONDARY = ("q4_k_b1", "q4_k_b16", "rms_swiglu")
 # dominant kernel from one ncu capture of the same command, with the capture it comes from. A
 # constant of this file, not a run-time measurement: the bench itself never runs under ncu.
 TRAFFIC = {
-    "q8_0_b8": (17994496, "ncu capture of one qgemv_kernel launch (profiles/qgemv_q8_0_b8.md)"),
-    "q4_k_b1": (33096192, "ncu capture of one qgemv_kernel launch (profiles/qgemv_q4_k_b1.md)"),
+    "q8_0_b8": (17996288, "ncu capture of one qgemv_stream_kernel launch (profiles/qgemv_q8_0_b8.md)"),
+    "q4_k_b1": (33089280, "ncu capture of one qgemv_stream_kernel launch (profiles/qgemv_q4_k_b1.md)"),
     "q6_k_b1": (48293632, "ncu capture of one qgemv_kernel launch (profiles/qgemv_q6_k_b1.md)"),
     "rms_swiglu": (229038848, "ncu capture of one j4b_group0 launch (profiles/tape_rms_swiglu.md)"),
 }
@@ -856,25 +856,24 @@ def measure_gemv(ctx, name, K, W, cpu_budget):
     kernel_avg_us = kernel_ms * 1e3 / K
 
     # ---- end to end through the public API: pinned host x in, y out, every step ----
-    # one GPU: the host-buffer quantMatvec (j4b_quant_matvec_host: copy in, GEMV, copy out in one
-    # C-ABI call); N GPUs: x copied in, the all-gathering GEMV, the gathered y copied out
+    # host buffers in and out every step through the C ABI: j4b_quant_matvec_host (one GPU) or
+    # j4b_quant_matvec_allgather_host (N GPUs), recorded per weight as a plan and replayed;
+    # pinned buffers cross PCIe inside the kernels
     x_host = torch.from_numpy(np.ascontiguousarray(be.download(x))).pin_memory()
     y_host = torch.empty(world * batch * rows, dtype=torch.float32).pin_memory()
-    y_all_host = y_host
-    xin = be.full(0.0, (batch, cols))
     e2e_steps = max(K, 200)
     stream = torch_stream()
 
-    def e2e_step(i):
-        if world > 1:
-            _lib.call("j4b_h2d", xin.ptr, ctypes.c_void_p(x_host.data_ptr()), x_host.numel() * 4, stream)
-            peers.allgather_matvec(weights[i % copies], xin.ptr, y_all.data_ptr(), batch, stream)
-            _lib.call("j4b_d2h", ctypes.c_void_p(y_all_host.data_ptr()), y_all.data_ptr(), y_all_host.numel() * 4,
-                      stream)
-        else:
-            be.quant_matvec_host(weights[i % copies], x_host, y_host, stream)
+    # a decode loop records each weight's host-buffer call once and replays it every step
+    if world > 1:
+        plans = [peers.allgather_matvec_host_plan(wq, x_host, y_host, batch, stream) for wq in weights]
+    else:
+        plans = [be.quant_matvec_host_plan(wq, x_host, y_host) for wq in weights]
 
-    for i in range(3):  # warm the path (the first host-buffer call allocates its staging)
+    def e2e_step(i):
+        plans[i % copies].run(stream)
+
+    for i in range(3):  # warm the path
         e2e_step(i)
     ctx.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -893,7 +892,7 @@ def measure_gemv(ctx, name, K, W, cpu_budget):
         rate, sample, _ = cpu_matvec_rate(qtype, rows, cols, batch, 1, cpu_budget)
         cpu = {"value": round(rate, 4), "unit": "GB/s", "cores": 1, "kind": "port",
                "sample": sample + f" (host has {os.cpu_count()} cores)"}
-    del weights
+    del weights, plans
     if rank != 0:
         return None
     return {
@@ -908,8 +907,8 @@ def measure_gemv(ctx, name, K, W, cpu_budget):
         "cpu_baseline": cpu,
         "e2e": {"value": round(e2e_value, 3), "unit": "GB/s",
                 "h2d_bytes_per_step": batch * cols * 4, "d2h_bytes_per_step": world * batch * rows * 4,
-                "call": "j4b_quant_matvec_host" if world == 1 else
-                        "j4b_h2d + j4b_quant_matvec_allgather + j4b_d2h",
+                "call": "j4b_quant_matvec_host_run (a plan of j4b_quant_matvec_host" +
+                        (")" if world == 1 else " over the peer group: j4b_quant_matvec_allgather_host)"),
                 "host_issue_us_per_step": round(host_issue_s * 1e6 / e2e_steps, 2),
                 "device_us_per_step": round(e_ms * 1e3 / e2e_steps, 2)},
         "gpu_launches": K * launches,

@@ -206,10 +206,12 @@ int j4b_quant_shape(j4b_qweight_t w, int* ggml_type, int64_t* rows, int64_t* col
 int j4b_quant_matvec(j4b_qweight_t w, j4b_buf x, j4b_buf add, j4b_buf y, int64_t batch,
                      j4b_stream s);
 /* The same with HOST buffers (QuantizedOps.java:26-30 as a host caller makes it: upload x, the
- * product, download y): x [batch, cols] and y [batch, rows] f32 in host memory, batch 1..16. The
- * copies and the GEMV are queued on the stream (asynchronous for pinned host memory); y is valid
- * once the stream is synchronised. Device staging for x and y belongs to the weight (allocated
- * by the first call), so calls on one weight must not overlap. */
+ * product, download y): x [batch, cols] and y [batch, rows] f32 in host memory, batch 1..16.
+ * Everything is queued on the stream; y is valid once the stream is synchronised. Page-locked
+ * buffers (cudaHostAlloc / cudaMallocHost, e.g. torch pin_memory) are used in place: a kernel
+ * reads x over PCIe and the GEMV stores y into host memory; pageable buffers go through copies.
+ * Device staging for x belongs to the weight (allocated by the first call), so calls on one
+ * weight must not overlap. */
 int j4b_quant_matvec_host(j4b_qweight_t w, const float* x, int64_t batch, float* y, j4b_stream s);
 /* Prefill projection (no reference counterpart: the reference only has the rank-1 quantMatvec):
  * y [m, rows] = x [m, cols] . W^T, f32 row-major, on the tcgen05 tensor cores. precision
@@ -247,6 +249,20 @@ int j4b_peer_status(j4b_peer_group* g, int* status);
  * every rank's buffer and y_all [batch, rows * nranks] receives the gathered result. batch <= 16. */
 int j4b_quant_matvec_allgather(j4b_qweight_t w, j4b_buf x, j4b_buf add, j4b_buf y_all, int64_t batch,
                                j4b_peer_group* g, int channel, j4b_stream s);
+/* The same with host buffers, as j4b_quant_matvec_host: x [batch, cols] and the gathered
+ * y_all [batch, rows * nranks] in host memory (page-locked ones are read and written in place
+ * by the kernels). */
+int j4b_quant_matvec_allgather_host(j4b_qweight_t w, const float* x, int64_t batch, float* y_all,
+                                    j4b_peer_group* g, int channel, j4b_stream s);
+/* A host-buffer call (g = NULL: j4b_quant_matvec_host; else j4b_quant_matvec_allgather_host on
+ * `channel`) recorded once as a CUDA graph; each run replays it with one launch on the stream (a
+ * decode loop's per-step host cost). Buffers, weight and group are captured by address and must
+ * outlive the plan; runs of one plan, like calls on one weight, must not overlap. */
+typedef struct j4b_qplan* j4b_qplan_t;
+int j4b_quant_matvec_host_plan(j4b_qweight_t w, const float* x, int64_t batch, float* y, j4b_peer_group* g,
+                               int channel, j4b_qplan_t* out);
+int j4b_quant_matvec_host_run(j4b_qplan_t plan, j4b_stream s);
+int j4b_quant_matvec_host_plan_free(j4b_qplan_t plan);
 /* out[i] = sum over ranks of src[i], summed in rank order (identical on every rank). Both
  * collectives move 8-byte flagged words (value + step flag): a channel's slice of `bytes` holds
  * two parity halves, so a gathered output (batch * rows * nranks floats) or an all-reduce

@@ -108,6 +108,10 @@ SIGNATURES = {
     "j4b_peer_group_free": [_vp],
     "j4b_peer_status": [_vp, ctypes.POINTER(ctypes.c_int)],
     "j4b_quant_matvec_allgather": [_vp, _u64, _u64, _u64, _i64, _vp, _int, _vp],
+    "j4b_quant_matvec_allgather_host": [_vp, _vp, _i64, _vp, _vp, _int, _vp],
+    "j4b_quant_matvec_host_plan": [_vp, _vp, _i64, _vp, _vp, _int, ctypes.POINTER(_vp)],
+    "j4b_quant_matvec_host_run": [_vp, _vp],
+    "j4b_quant_matvec_host_plan_free": [_vp],
     "j4b_peer_allreduce": [_vp, _int, _u64, _i64, _u64, _vp],
     "j4b_tape_compile": [_int, _i64p, ctypes.c_size_t, ctypes.POINTER(_vp)],
     "j4b_tape_launch": [_vp, ctypes.POINTER(_u64), _int, ctypes.POINTER(_u64), _int, _vp],

@@ -67,6 +67,28 @@ class DeviceBuffer:
 
 
 @dataclass(eq=False)
+class QuantPlan:
+    """A recorded host-buffer quantMatvec (j4b_quant_matvec_host_plan); `run` replays it."""
+
+    def __init__(self, handle: int, keep: tuple, default_stream: int):
+        self.handle, self._keep, self._stream = handle, keep, default_stream
+
+    @staticmethod
+    def make(w, x_host, y_host, batch: int, group_handle, channel: int, stream: int) -> "QuantPlan":
+        h = ctypes.c_void_p()
+        call("j4b_quant_matvec_host_plan", ctypes.c_void_p(w.handle), x_host.data_ptr(), batch, y_host.data_ptr(),
+             group_handle, channel, ctypes.byref(h))
+        return QuantPlan(h.value, (w, x_host, y_host), stream)
+
+    def run(self, stream: int | None = None) -> None:
+        call("j4b_quant_matvec_host_run", self.handle, self._stream if stream is None else stream)
+
+    def __del__(self):
+        if getattr(self, "handle", None) and _lib._lib is not None:
+            _lib.load().j4b_quant_matvec_host_plan_free(ctypes.c_void_p(self.handle))
+            self.handle = None
+
+
 class QuantBuffer:
     """Opaque quantized matrix (the CpuQuantBuffer role, CpuQuantBuffer.java:10-38)."""
     handle: int
@@ -478,6 +500,17 @@ class B200Backend:
                              f"y {tuple(y_host.shape)} (batch 1..16)")
         call("j4b_quant_matvec_host", w.handle, x_host.data_ptr(), n // cols, y_host.data_ptr(),
              self.stream if stream is None else stream)
+
+    def quant_matvec_host_plan(self, w: QuantBuffer, x_host: torch.Tensor, y_host: torch.Tensor) -> "QuantPlan":
+        """quant_matvec_host recorded once (j4b_quant_matvec_host_plan): `plan.run(stream)` then
+        replays the copy-in, the GEMV and the copy-out with one graph launch. The plan keeps x_host,
+        y_host and w alive."""
+        rows, cols = w.shape
+        n = x_host.numel()
+        if n % cols or not 1 <= n // cols <= 16 or y_host.numel() != n // cols * rows:
+            raise ValueError(f"host quantMatvec shapes: W {w.shape}, x {tuple(x_host.shape)}, "
+                             f"y {tuple(y_host.shape)} (batch 1..16)")
+        return QuantPlan.make(w, x_host, y_host, n // cols, None, 0, self.stream)
 
     def quant_matvec_add(self, w: QuantBuffer, x: DeviceBuffer, add: DeviceBuffer):
         return self.quant_matvec(w, x, add)

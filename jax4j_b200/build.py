@@ -93,8 +93,16 @@ def build(force: bool = False, verbose: bool = False, extra: list[str] | None = 
         # libcuda is not linked: driver entry points are resolved at run time through the runtime,
         # so the library also loads (for planning and ABI checks) where no driver is installed
         rpath = ["-Xlinker", "-rpath=" + cuda_lib_dirs()[0]]
-        cmd = [nvcc(), *ARCH, "-shared", "-o", LIB, *objs, *libdirs, *rpath, "-lcudart", "-lnvrtc"]
-        subprocess.run(cmd, check=True)
+        # linked to a temporary name and renamed into place: a process that loads (or copies) the
+        # library meanwhile sees the old file or the new one, never a partial one
+        tmp = LIB + f".tmp{os.getpid()}"
+        cmd = [nvcc(), *ARCH, "-shared", "-o", tmp, *objs, *libdirs, *rpath, "-lcudart", "-lnvrtc"]
+        try:
+            subprocess.run(cmd, check=True)
+            os.replace(tmp, LIB)
+        finally:
+            if os.path.exists(tmp):
+                os.remove(tmp)
     return LIB
 
 

@@ -56,9 +56,10 @@ struct j4b_qweight {
   // weights before it waits on the kernel before it; the first GEMV after an upload therefore
   // launches without it (host-side flag, cleared at that launch).
   bool fresh;
-  // Device staging of x and y for j4b_quant_matvec_host (16 rows of each), allocated by its first
-  // call; like the split-K scratch, it serialises the calls made on one weight.
+  // Device staging of x and y for the host-buffer calls (16 rows of x, then y), allocated by the
+  // first one; like the split-K scratch, it serialises the calls made on one weight.
   float* io;
+  int64_t io_floats;
 };
 
 namespace j4b {
@@ -806,31 +807,54 @@ extern "C" int j4b_quant_matvec(j4b_qweight_t w, j4b_buf x, j4b_buf add, j4b_buf
   return J4B_OK;
 }
 
-// quantMatvec with host buffers: x [batch, cols] is copied in, y [batch, rows] copied out, all on
-// the stream (pinned host buffers make both copies asynchronous; the caller synchronises the
-// stream before it reads y). One call per decode step from a host loop.
-extern "C" int j4b_quant_matvec_host(j4b_qweight_t w, const float* x, int64_t batch, float* y, j4b_stream s) {
-  if (!w) return set_error(J4B_EINVAL, "null quantized weight");
-  J4B_REQUIRE(batch >= 1 && batch <= 16, "host-buffer quantMatvec takes batch 1..16, got %lld", (long long)batch);
-  J4B_REQUIRE(x && y, "quantMatvec needs x and y host buffers");
-  DeviceGuard guard(w->dev);
-  cudaStream_t stream = resolve_stream(w->dev, s);
-  const int64_t xs = (w->cols + 3) / 4 * 4;  // keeps the y staging 16-byte aligned
-  if (!w->io) {
-    J4B_CUDA(cudaMalloc(&w->io, (size_t)16 * (xs + w->rows) * sizeof(float)), "cudaMalloc(quantMatvec staging)");
-    counters().allocations += 1;
+namespace j4b {
+namespace {
+// Device address of page-locked host memory (cudaHostAlloc / cudaMallocHost, or registered as
+// mapped), or null for pageable memory.
+const void* mapped_host(const void* p) {
+  cudaPointerAttributes at;
+  if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
   }
-  float* dx = w->io;
-  float* dy = w->io + 16 * xs;
-  const size_t xb = (size_t)(batch * w->cols) * sizeof(float), yb = (size_t)(batch * w->rows) * sizeof(float);
-  J4B_CUDA(cudaMemcpyAsync(dx, x, xb, cudaMemcpyHostToDevice, stream), "cudaMemcpyAsync(HtoD)");
-  counters().h2d += xb;
-  const int st = j4b_quant_matvec(w, (j4b_buf)(uintptr_t)dx, 0, (j4b_buf)(uintptr_t)dy, batch, s);
-  if (st) return st;
-  J4B_CUDA(cudaMemcpyAsync(y, dy, yb, cudaMemcpyDeviceToHost, stream), "cudaMemcpyAsync(DtoH)");
-  counters().d2h += yb;
+  return at.type == cudaMemoryTypeHost ? at.devicePointer : nullptr;
+}
+
+// Copies n4 float4s between mapped host memory and the device staging through the SMs (one
+// float4 per thread, every read in flight at once): no copy-engine round trip. Stage-in (x, host
+// to device) issues its PCIe reads before it waits on the kernel before it (the previous step's
+// GEMV may still read the staging); stage-out (y, device to host) waits first, since the GEMV
+// before it writes what it reads, and stores whole 128-byte lines.
+template <bool kIn>
+__global__ void __launch_bounds__(256) host_stage_kernel(const float4* __restrict__ src, float4* __restrict__ dst,
+                                                         int64_t n4) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  const int64_t i = (int64_t)blockIdx.x * 256 + threadIdx.x;
+  if (!kIn) asm volatile("griddepcontrol.wait;" ::: "memory");
+  float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (i < n4) v = src[i];
+  if (kIn) asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (i < n4) dst[i] = v;
+}
+
+template <bool kIn>
+int launch_host_stage(const void* src, void* dst, int64_t n4, cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)((n4 + 255) / 256));
+  cfg.blockDim = dim3(256);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  J4B_CUDA(cudaLaunchKernelEx(&cfg, host_stage_kernel<kIn>, (const float4*)src, (float4*)dst, n4),
+           "host_stage_kernel");
+  count_launch();
   return J4B_OK;
 }
+}  // namespace
+}  // namespace j4b
 
 extern "C" int j4b_quant_matvec_allgather(j4b_qweight_t w, j4b_buf x, j4b_buf add, j4b_buf y_all,
                                           int64_t batch, j4b_peer_group* g, int channel, j4b_stream s) {
@@ -860,6 +884,176 @@ extern "C" int j4b_quant_matvec_allgather(j4b_qweight_t w, j4b_buf x, j4b_buf ad
   if (e != cudaSuccess) return cuda_error(e, "qgemv_kernel");
   count_launch();
   return peer_wait_copy(g, channel, (float*)(uintptr_t)y_all, gathered, stream);
+}
+
+// quantMatvec with host buffers: x [batch, cols] in, y [batch, rows] out, queued on the stream; the
+// caller synchronises the stream before it reads y. One call per decode step from a host loop.
+// Page-locked buffers are used in place: the SMs read x over PCIe into the weight's staging and
+// the GEMV stores y straight into host memory (copy-engine transfers of this size cost ~14 us
+// each, twice the GEMV). Pageable buffers go through stream-ordered copies.
+namespace j4b {
+namespace {
+// Device staging of the host-buffer calls: 16 rows of x, then y (`y_floats`); allocated on first
+// use, or grown (after the work still using it) for a larger gathered y.
+int ensure_io(j4b_qweight* w, int64_t y_floats) {
+  const int64_t xs = (w->cols + 3) / 4 * 4;  // keeps the y staging 16-byte aligned
+  if (w->io_floats >= 16 * xs + y_floats) return J4B_OK;
+  if (w->io) {
+    cudaFree(w->io);  // synchronises with the work still using it
+    counters().releases += 1;
+    w->io = nullptr;
+    w->io_floats = 0;
+  }
+  J4B_CUDA(cudaMalloc(&w->io, (size_t)(16 * xs + y_floats) * sizeof(float)), "cudaMalloc(quantMatvec staging)");
+  w->io_floats = 16 * xs + y_floats;
+  counters().allocations += 1;
+  return J4B_OK;
+}
+
+// Where the host buffers of one host-buffer call live: page-locked ones (both, 16-byte aligned,
+// whole float4s) are moved by the SMs, others by stream-ordered copies.
+struct HostIo {
+  const void* xd = nullptr;  // device address of x, or null
+  void* yd = nullptr;        // device address of y, or null
+  bool direct = false;
+};
+HostIo host_io(const j4b_qweight* w, const float* x, const float* y, int64_t batch, int64_t y_floats) {
+  HostIo h;
+  h.xd = mapped_host(x);
+  h.yd = const_cast<void*>(mapped_host(y));
+  h.direct = h.xd && h.yd && ((uintptr_t)h.xd & 15) == 0 && ((uintptr_t)h.yd & 15) == 0 &&
+             (batch * w->cols) % 4 == 0 && y_floats % 4 == 0;
+  return h;
+}
+
+// One host-buffer quantMatvec (g == null) or all-gathered quantMatvec on `stream`: x into the
+// staging, the GEMV into the staging, y out. The staging must already hold y_floats.
+int host_call(j4b_qweight* w, const float* x, int64_t batch, float* y, int64_t y_floats, j4b_peer_group* g,
+              int channel, const HostIo& h, cudaStream_t stream) {
+  const int64_t xs = (w->cols + 3) / 4 * 4;
+  float* dx = w->io;
+  float* dy = w->io + 16 * xs;
+  const size_t xb = (size_t)(batch * w->cols) * sizeof(float), yb = (size_t)y_floats * sizeof(float);
+  int st = h.direct ? launch_host_stage<true>(h.xd, dx, batch * w->cols / 4, stream)
+                    : (cudaMemcpyAsync(dx, x, xb, cudaMemcpyHostToDevice, stream) == cudaSuccess
+                           ? J4B_OK
+                           : cuda_error(cudaGetLastError(), "cudaMemcpyAsync(HtoD)"));
+  if (st) return st;
+  counters().h2d += xb;
+  st = g ? j4b_quant_matvec_allgather(w, (j4b_buf)(uintptr_t)dx, 0, (j4b_buf)(uintptr_t)dy, batch, g, channel,
+                                      (j4b_stream)stream)
+         : j4b_quant_matvec(w, (j4b_buf)(uintptr_t)dx, 0, (j4b_buf)(uintptr_t)dy, batch, (j4b_stream)stream);
+  if (st) return st;
+  st = h.direct ? launch_host_stage<false>(dy, h.yd, y_floats / 4, stream)
+                : (cudaMemcpyAsync(y, dy, yb, cudaMemcpyDeviceToHost, stream) == cudaSuccess
+                       ? J4B_OK
+                       : cuda_error(cudaGetLastError(), "cudaMemcpyAsync(DtoH)"));
+  if (st) return st;
+  counters().d2h += yb;
+  return J4B_OK;
+}
+}  // namespace
+}  // namespace j4b
+
+// quantMatvec with host buffers: x [batch, cols] in, y [batch, rows] out, queued on the stream; the
+// caller synchronises the stream before it reads y. Page-locked buffers are moved by the SMs (a
+// kernel reads x over PCIe into the weight's staging, another writes y back in whole lines):
+// copy-engine transfers of this size cost ~14 us each, twice the GEMV.
+extern "C" int j4b_quant_matvec_host(j4b_qweight_t w, const float* x, int64_t batch, float* y, j4b_stream s) {
+  if (!w) return set_error(J4B_EINVAL, "null quantized weight");
+  J4B_REQUIRE(batch >= 1 && batch <= 16, "host-buffer quantMatvec takes batch 1..16, got %lld", (long long)batch);
+  J4B_REQUIRE(x && y, "quantMatvec needs x and y host buffers");
+  DeviceGuard guard(w->dev);
+  const int64_t n = batch * w->rows;
+  int st = ensure_io(w, 16 * w->rows);
+  if (st) return st;
+  return host_call(w, x, batch, y, n, nullptr, 0, host_io(w, x, y, batch, n), resolve_stream(w->dev, s));
+}
+
+// The all-gathered quantMatvec with host buffers: x [batch, cols] from host memory, the gathered
+// y [batch, rows * nranks] into host memory.
+extern "C" int j4b_quant_matvec_allgather_host(j4b_qweight_t w, const float* x, int64_t batch, float* y_all,
+                                               j4b_peer_group* g, int channel, j4b_stream s) {
+  if (!w) return set_error(J4B_EINVAL, "null quantized weight");
+  J4B_REQUIRE(g != nullptr, "null peer group");
+  J4B_REQUIRE(batch >= 1 && batch <= 16, "all-gathered quantMatvec takes batch 1..16, got %lld", (long long)batch);
+  J4B_REQUIRE(x && y_all, "quantMatvec needs x and y host buffers");
+  DeviceGuard guard(w->dev);
+  const int64_t n = batch * w->rows * peer_group_ranks(g);
+  int st = ensure_io(w, 16 * w->rows * peer_group_ranks(g));
+  if (st) return st;
+  return host_call(w, x, batch, y_all, n, g, channel, host_io(w, x, y_all, batch, n), resolve_stream(w->dev, s));
+}
+
+// A host-buffer call recorded once as a CUDA graph (stage-in, GEMV, stage-out, and for a peer
+// group the gathering copy) and replayed with one launch: a decode loop's per-step host cost is
+// then one graph launch. The buffers, the weight and the group are captured by address and must
+// outlive the plan.
+struct j4b_qplan {
+  int dev = 0;
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  uint64_t launches = 0, h2d = 0, d2h = 0;
+};
+
+extern "C" int j4b_quant_matvec_host_plan(j4b_qweight_t w, const float* x, int64_t batch, float* y,
+                                          j4b_peer_group* g, int channel, j4b_qplan_t* out) {
+  if (!w) return set_error(J4B_EINVAL, "null quantized weight");
+  J4B_REQUIRE(out != nullptr, "null plan pointer");
+  J4B_REQUIRE(batch >= 1 && batch <= 16, "host-buffer quantMatvec takes batch 1..16, got %lld", (long long)batch);
+  J4B_REQUIRE(x && y, "quantMatvec needs x and y host buffers");
+  DeviceGuard guard(w->dev);
+  const int nr = g ? peer_group_ranks(g) : 1;
+  const int64_t n = batch * w->rows * nr;
+  int st = ensure_io(w, 16 * w->rows * nr);
+  if (st) return st;
+  const HostIo h = host_io(w, x, y, batch, n);
+  cudaStream_t cs = nullptr;
+  J4B_CUDA(cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking), "cudaStreamCreate(plan capture)");
+  const uint64_t l0 = counters().dispatches.load(), h0 = counters().h2d.load(), d0 = counters().d2h.load();
+  cudaGraph_t graph = nullptr;
+  cudaError_t e = cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal);
+  if (e == cudaSuccess) {
+    st = host_call(w, x, batch, y, n, g, channel, h, cs);
+    e = cudaStreamEndCapture(cs, &graph);
+  }
+  cudaStreamDestroy(cs);
+  if (st || e != cudaSuccess) {
+    if (graph) cudaGraphDestroy(graph);
+    return st ? st : cuda_error(e, "plan capture");
+  }
+  j4b_qplan* p = new j4b_qplan();
+  p->dev = w->dev;
+  p->graph = graph;
+  e = cudaGraphInstantiate(&p->exec, graph, 0);
+  if (e != cudaSuccess) {
+    cudaGraphDestroy(graph);
+    delete p;
+    return cuda_error(e, "cudaGraphInstantiate(plan)");
+  }
+  p->launches = counters().dispatches.load() - l0;
+  p->h2d = counters().h2d.load() - h0;
+  p->d2h = counters().d2h.load() - d0;
+  *out = p;
+  return J4B_OK;
+}
+
+extern "C" int j4b_quant_matvec_host_run(j4b_qplan_t p, j4b_stream s) {
+  J4B_REQUIRE(p != nullptr, "null plan");
+  J4B_CUDA(cudaGraphLaunch(p->exec, resolve_stream(p->dev, s)), "cudaGraphLaunch(plan)");
+  counters().dispatches += p->launches;
+  counters().h2d += p->h2d;
+  counters().d2h += p->d2h;
+  return J4B_OK;
+}
+
+extern "C" int j4b_quant_matvec_host_plan_free(j4b_qplan_t p) {
+  if (!p) return J4B_OK;
+  DeviceGuard guard(p->dev);
+  cudaGraphExecDestroy(p->exec);
+  cudaGraphDestroy(p->graph);
+  delete p;
+  return J4B_OK;
 }
 
 extern "C" int j4b_quant_gather_row(j4b_qweight_t w, int64_t row, j4b_buf out, j4b_stream s) {

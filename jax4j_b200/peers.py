@@ -54,6 +54,18 @@ class PeerGroup:
         call("j4b_quant_matvec_allgather", ctypes.c_void_p(w.handle), x_ptr, add_ptr, y_all_ptr, batch,
              self.handle, GATHER_CHANNEL, stream)
 
+    def allgather_matvec_host(self, w, x_host, y_all_host, batch: int, stream: int):
+        """The same with host tensors (j4b_quant_matvec_allgather_host): x_host [batch, cols] and
+        y_all_host [batch, rows * world], f32 CPU tensors (pinned ones are used in place)."""
+        call("j4b_quant_matvec_allgather_host", ctypes.c_void_p(w.handle), x_host.data_ptr(), batch,
+             y_all_host.data_ptr(), self.handle, GATHER_CHANNEL, stream)
+
+    def allgather_matvec_host_plan(self, w, x_host, y_all_host, batch: int, stream: int):
+        """allgather_matvec_host recorded once as a replayable plan (j4b_quant_matvec_host_plan);
+        every rank records and runs its plans in the same order."""
+        from .backend import QuantPlan
+        return QuantPlan.make(w, x_host, y_all_host, batch, self.handle, GATHER_CHANNEL, stream)
+
     def allreduce(self, src_ptr: int, n: int, out_ptr: int, stream: int):
         call("j4b_peer_allreduce", self.handle, ALLREDUCE_CHANNEL, src_ptr, n, out_ptr, stream)
 

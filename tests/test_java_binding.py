@@ -27,7 +27,7 @@ def c_signatures() -> dict:
         for p in (x.strip() for x in params.split(",")):
             if not p or p == "void":
                 continue
-            if "*" in p or p.split()[0] in ("j4b_stream", "j4b_qweight_t", "j4b_aad_t"):
+            if "*" in p or p.split()[0] in ("j4b_stream", "j4b_qweight_t", "j4b_aad_t", "j4b_qplan_t"):
                 kinds.append("P")
             elif p.split()[0] in ("j4b_buf", "int64_t", "uint64_t", "size_t"):
                 kinds.append("L")

@@ -45,6 +45,19 @@ for rows, cols, batch, qtype in ((96, 512, 3, 8), (256, 4096, 8, 8), (160, 2048,
     dist.all_gather(parts, torch.from_numpy(mine.reshape(-1)).cuda())
     want = np.concatenate([p.cpu().numpy().reshape(batch, rows) for p in parts], axis=1)
     assert np.array_equal(got, want), ("all-gather mismatch", rows, cols, batch)
+    # the host-buffer form: pinned x in and gathered y out, read and written by the kernels
+    xh = torch.from_numpy(x).pin_memory()
+    yh = torch.zeros(batch * rows * world).pin_memory()
+    pg.allgather_matvec_host(wq, xh, yh, batch, s)
+    torch.cuda.synchronize()
+    assert np.array_equal(yh.numpy().reshape(batch, world * rows), want), ("host all-gather", rows, cols, batch)
+    plan = pg.allgather_matvec_host_plan(wq, xh, yh, batch, s)
+    for it in range(2):
+        yh.zero_()
+        plan.run(s)
+        torch.cuda.synchronize()
+        assert np.array_equal(yh.numpy().reshape(batch, world * rows), want), ("planned all-gather", rows, cols)
+    del plan
 # calls of different sizes share the channel (chunks an earlier call did not use hold no count)
 for it, n in enumerate((5000, 1000, 3000, 5000)):
     v = torch.from_numpy(np.random.default_rng(it * 10 + rank).standard_normal(n).astype(np.float32)).cuda()

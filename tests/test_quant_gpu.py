@@ -106,6 +106,18 @@ def test_host_buffer_call(backend, oracle):
             assert np.array_equal(yh.numpy().reshape(batch, rows), want.reshape(batch, rows))
     with pytest.raises(ValueError, match="batch 1..16"):
         backend.quant_matvec_host(w, torch.zeros(17 * cols), torch.zeros(17 * rows))
+    # the recorded form replays the same call: new x values in the same buffer, new products out
+    batch = 8
+    xh = torch.zeros((batch, cols)).pin_memory()
+    yh = torch.zeros(batch * rows).pin_memory()
+    plan = backend.quant_matvec_host_plan(w, xh, yh)
+    for seed in (21, 22, 23):
+        x = np.random.default_rng(seed).standard_normal((batch, cols)).astype(np.float32)
+        xh.copy_(torch.from_numpy(x))
+        plan.run()
+        backend.sync()
+        want = backend.download(backend.quant_matvec(w, backend.upload(x, x.shape)))
+        assert np.array_equal(yh.numpy().reshape(batch, rows), want.reshape(batch, rows))
 
 
 def test_repeated_calls_are_deterministic(backend, oracle):
