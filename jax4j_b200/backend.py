@@ -66,7 +66,6 @@ class DeviceBuffer:
         return _prod(self.shape)
 
 
-@dataclass(eq=False)
 class QuantPlan:
     """A recorded host-buffer quantMatvec (j4b_quant_matvec_host_plan); `run` replays it."""
 
@@ -89,6 +88,7 @@ class QuantPlan:
             self.handle = None
 
 
+@dataclass(eq=False)
 class QuantBuffer:
     """Opaque quantized matrix (the CpuQuantBuffer role, CpuQuantBuffer.java:10-38)."""
     handle: int

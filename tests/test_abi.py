@@ -83,3 +83,14 @@ def test_backend_refuses_without_gpu():
     assert B200Backend.is_available() is False
     with pytest.raises(RuntimeError, match="CUDA device"):
         B200Backend(0)
+
+
+def test_backend_handle_types_construct_without_a_gpu():
+    """The handle wrappers the GPU paths return are plain records: constructible and inert here
+    (a zero handle frees nothing)."""
+    from jax4j_b200.backend import QuantBuffer, QuantPlan
+    q = QuantBuffer(0, 8, (2, 32))
+    assert q.shape == (2, 32) and q.qtype == 8
+    p = QuantPlan(0, (q,), 0)
+    assert p.handle == 0
+    del p, q
