@@ -367,31 +367,16 @@ __global__ void __launch_bounds__(256) gemm_short_k_kernel(const float* __restri
 }
 
 // n <= 32: one warp per row of C; lane l takes p = l, l + 32, ... and keeps n partial sums, which
-// the warp adds lane-wise (butterfly), so the sum order is fixed. With kStaged, the CTA first
-// copies B [K, n] (at most kNarrowStage floats) into shared memory, row-major, so the n reads
-// per p come from shared memory instead of n strided global loads per lane.
-constexpr int kNarrowStage = 12288;  // 48 KB
-template <bool kStaged>
+// the warp adds lane-wise (butterfly), so the sum order is fixed.
 __global__ void __launch_bounds__(256) gemm_narrow_n_kernel(const float* __restrict__ A, const float* __restrict__ B,
                                                             float* __restrict__ C, int64_t M, int64_t K, int N,
                                                             int64_t sai, int64_t sap, int64_t sbp, int64_t sbj) {
-  extern __shared__ float bs[];
   const int64_t bz = blockIdx.y;
   const int lane = threadIdx.x & 31;
   const int64_t i = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
-  const float* b = B + bz * K * N;
-  if (kStaged) {
-    for (int64_t e = threadIdx.x; e < K * N; e += 256) {
-      const int64_t p = e / N, j = e % N;
-      bs[e] = __ldg(b + p * sbp + j * sbj);
-    }
-    __syncthreads();
-    b = bs;
-    sbp = N;
-    sbj = 1;
-  }
   if (i >= M) return;
   const float* a = A + bz * M * K + i * sai;
+  const float* b = B + bz * K * N;
   float acc[32];
 #pragma unroll
   for (int j = 0; j < 32; j++) acc[j] = 0.f;
@@ -403,10 +388,8 @@ __global__ void __launch_bounds__(256) gemm_narrow_n_kernel(const float* __restr
 #pragma unroll
     for (int j = 0; j < 32; j++) {
       if (j < N) {
-        const float b0 = kStaged ? b[p * sbp + j] : __ldg(b + (p)*sbp + j * sbj);
-        const float b1 = kStaged ? b[(p + 32) * sbp + j] : __ldg(b + (p + 32) * sbp + j * sbj);
-        const float b2 = kStaged ? b[(p + 64) * sbp + j] : __ldg(b + (p + 64) * sbp + j * sbj);
-        const float b3 = kStaged ? b[(p + 96) * sbp + j] : __ldg(b + (p + 96) * sbp + j * sbj);
+        const float b0 = __ldg(b + (p)*sbp + j * sbj), b1 = __ldg(b + (p + 32) * sbp + j * sbj);
+        const float b2 = __ldg(b + (p + 64) * sbp + j * sbj), b3 = __ldg(b + (p + 96) * sbp + j * sbj);
         acc[j] = fmaf(av[0], b0, acc[j]);
         acc[j] = fmaf(av[1], b1, acc[j]);
         acc[j] = fmaf(av[2], b2, acc[j]);
@@ -419,7 +402,7 @@ __global__ void __launch_bounds__(256) gemm_narrow_n_kernel(const float* __restr
     const float* br = b + p * sbp;
 #pragma unroll
     for (int j = 0; j < 32; j++)
-      if (j < N) acc[j] = fmaf(av, kStaged ? br[j] : __ldg(br + j * sbj), acc[j]);
+      if (j < N) acc[j] = fmaf(av, __ldg(br + j * sbj), acc[j]);
   }
   float mine = 0.f;
 #pragma unroll
@@ -740,12 +723,8 @@ int matmul_strided(const float* pa, const float* pb, float* pc, int64_t batch, i
     return J4B_OK;
   }
   if (n <= 32 && batch <= 65535 && (m + 7) / 8 <= INT32_MAX) {
-    const dim3 grid((unsigned)((m + 7) / 8), (unsigned)batch);
-    if (k * n <= kNarrowStage)
-      gemm_narrow_n_kernel<true><<<grid, 256, (size_t)(k * n) * sizeof(float), stream>>>(pa, pb, pc, m, k, (int)n, sai,
-                                                                                      sap, sbp, sbj);
-    else
-      gemm_narrow_n_kernel<false><<<grid, 256, 0, stream>>>(pa, pb, pc, m, k, (int)n, sai, sap, sbp, sbj);
+    gemm_narrow_n_kernel<<<dim3((unsigned)((m + 7) / 8), (unsigned)batch), 256, 0, stream>>>(pa, pb, pc, m, k, (int)n,
+                                                                                          sai, sap, sbp, sbj);
     J4B_CHECK_LAUNCH("gemm_narrow_n_kernel");
     return J4B_OK;
   }

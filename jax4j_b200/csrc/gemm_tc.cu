@@ -55,8 +55,7 @@ constexpr uint32_t tc_stage_bytes() { return TERMS == 1 ? kTileBytes * 3 : kTile
 struct TcArgs {
   int M, N, Kp;   // Kp: K padded to a multiple of 64
   int terms;      // 1: hi.hi (bf16 mode); 3: hi.hi + hi.lo + lo.hi (fp32-accurate mode)
-  int splits, kb_per;  // K splits and 64-column k-blocks per split
-  float* C;       // with splits > 1, the partials [splits][M][ldc]
+  float* C;
   int64_t ldc;
   int* status;
 };
@@ -82,22 +81,18 @@ __global__ void __launch_bounds__(kTcThreads, TERMS == 1 ? 2 : 1)
   // row index fastest, so the CTAs resident at one time share a few A row panels and about
   // (resident / kGroupM) B column panels, which stay in L2 (row-major order would sweep all of
   // B's panels at once).
-  // With K splits the grid holds splits x tiles CTAs, the tile index fastest.
-  int m_tile, n_tile, split;
+  int m_tile, n_tile;
   {
     const int mt = (p.M + kBM - 1) / kBM;
     const int nt = (p.N + kBN - 1) / kBN;
-    const int tile = (int)(blockIdx.x % (unsigned)(mt * nt));
-    split = (int)(blockIdx.x / (unsigned)(mt * nt));
     const int per_group = kGroupM * nt;
-    const int grp = tile / per_group, idx = tile % per_group;
+    const int grp = (int)blockIdx.x / per_group, idx = (int)blockIdx.x % per_group;
     const int gm = min(kGroupM, mt - grp * kGroupM);
     m_tile = grp * kGroupM + idx % gm;
     n_tile = idx / gm;
   }
   const int m0 = m_tile * kBM, n0 = n_tile * kBN;
-  const int kb0 = split * p.kb_per;
-  const int nk = min(p.Kp / kBK - kb0, p.kb_per);  // k-blocks of this CTA, from kb0
+  const int nk = p.Kp / kBK;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -125,12 +120,11 @@ __global__ void __launch_bounds__(kTcThreads, TERMS == 1 ? 2 : 1)
         if (use > 0 && !bar_wait(&empty[s], (uint32_t)((use - 1) & 1))) ok = false;
         uint8_t* st = smem + s * kStageBytes;
         bar_expect_tx(&full[s], kStageBytes);
-        const int kx = (kb0 + kb) * kBK;
-        tma_tile(st, &a_hi, kx, m0, &full[s]);
-        tma_tile(st + kTileBytes, &b_hi, kx, n0, &full[s]);
+        tma_tile(st, &a_hi, kb * kBK, m0, &full[s]);
+        tma_tile(st + kTileBytes, &b_hi, kb * kBK, n0, &full[s]);
         if (TERMS == 3) {
-          tma_tile(st + kTileBytes + kBTile, &a_lo, kx, m0, &full[s]);
-          tma_tile(st + 2 * kTileBytes + kBTile, &b_lo, kx, n0, &full[s]);
+          tma_tile(st + kTileBytes + kBTile, &a_lo, kb * kBK, m0, &full[s]);
+          tma_tile(st + 2 * kTileBytes + kBTile, &b_lo, kb * kBK, n0, &full[s]);
         }
       }
     }
@@ -164,9 +158,7 @@ __global__ void __launch_bounds__(kTcThreads, TERMS == 1 ? 2 : 1)
     if (!bar_wait(acc_full, 0)) ok = false;
     tc_fence_after();
     const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16);
-    float* cbase = p.C + (int64_t)split * p.M * p.ldc;  // this split's partial (or C itself)
-    float* crow = cbase + (int64_t)row * p.ldc;
-    const bool vec = (p.ldc & 3) == 0 && (reinterpret_cast<uintptr_t>(cbase) & 15) == 0;
+    float* crow = p.C + (int64_t)row * p.ldc;
 #pragma unroll 1
     for (int c = 0; c < kBN; c += 8) {
       uint32_t v[8];
@@ -177,7 +169,7 @@ __global__ void __launch_bounds__(kTcThreads, TERMS == 1 ? 2 : 1)
       asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
       const int col = n0 + c;
       if (row < p.M) {
-        if (col + 8 <= p.N && vec) {
+        if (col + 8 <= p.N && (p.ldc & 3) == 0 && (reinterpret_cast<uintptr_t>(p.C) & 15) == 0) {
           float4* dst = reinterpret_cast<float4*>(crow + col);
           dst[0] = make_float4(__uint_as_float(v[0]), __uint_as_float(v[1]), __uint_as_float(v[2]), __uint_as_float(v[3]));
           dst[1] = make_float4(__uint_as_float(v[4]), __uint_as_float(v[5]), __uint_as_float(v[6]), __uint_as_float(v[7]));
@@ -249,15 +241,6 @@ __global__ void split_transpose_kernel(const float* __restrict__ b, int64_t k, i
   }
 }
 
-// C[i] = sum over splits of part[s][i], in split order.
-__global__ void tc_fold_kernel(const float* __restrict__ part, int splits, int64_t n, float* __restrict__ c) {
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-    float v = 0.f;
-    for (int s = 0; s < splits; ++s) v += __ldcg(part + s * n + i);
-    c[i] = v;
-  }
-}
-
 int* tc_status(int dev) {
   static int* status[kMaxDevices] = {};
   static std::mutex mu;
@@ -281,7 +264,7 @@ cudaError_t launch_tc(const CUtensorMap& ah, const CUtensorMap& al, const CUtens
     if (e != cudaSuccess) return e;
     configured = true;
   }
-  const int64_t tiles = (int64_t)((a.N + kBN - 1) / kBN) * ((a.M + kBM - 1) / kBM) * a.splits;
+  const int64_t tiles = (int64_t)((a.N + kBN - 1) / kBN) * ((a.M + kBM - 1) / kBM);
   if (tiles > 0x7fffffffLL) return cudaErrorInvalidValue;
   tc_gemm_kernel<TERMS><<<(unsigned)tiles, kTcThreads, smem, stream>>>(ah, al, bh, bl, a);
   return cudaGetLastError();
@@ -316,39 +299,9 @@ int tc_gemm_bf16(const __nv_bfloat16* a_hi, const __nv_bfloat16* a_lo, int64_t m
   args.C = out;
   args.ldc = n;
   args.status = status;
-  // Small outputs leave most SMs idle: the K range is then split over CTAs (at least two
-  // k-blocks each, partials bounded at 64 MB) and the partials summed in split order.
-  const int nkt = (int)(kp / kBK);
-  const int64_t tiles = ((m + kBM - 1) / kBM) * ((n + bn - 1) / bn);
-  const DeviceCtx* ctx = device_ctx(dev);
-  const int sms = ctx ? ctx->sm_count : 148;
-  int splits = 1;
-  if (tiles * 2 <= sms && nkt >= 4) {
-    splits = (int)std::min<int64_t>(nkt / 2, (sms + tiles - 1) / tiles);
-    while (splits > 1 && (int64_t)splits * m * n * 4 > (int64_t(64) << 20)) --splits;
-  }
-  args.kb_per = (nkt + splits - 1) / splits;
-  args.splits = (nkt + args.kb_per - 1) / args.kb_per;
-  void* part = nullptr;
-  if (args.splits > 1) {
-    J4B_CUDA(cudaMallocAsync(&part, (size_t)args.splits * m * n * sizeof(float), stream), "cudaMallocAsync(partials)");
-    args.C = (float*)part;
-  }
   cudaError_t e = split ? launch_tc<3>(mah, mal, mbh, mbl, args, stream) : launch_tc<1>(mah, mal, mbh, mbl, args, stream);
-  if (e != cudaSuccess) {
-    if (part) cudaFreeAsync(part, stream);
-    return cuda_error(e, "tc_gemm_kernel");
-  }
+  if (e != cudaSuccess) return cuda_error(e, "tc_gemm_kernel");
   count_launch(1);
-  if (part) {
-    const int64_t total = m * n;
-    tc_fold_kernel<<<(unsigned)std::min<int64_t>((total + 255) / 256, 4 * sms), 256, 0, stream>>>(
-        (const float*)part, args.splits, total, out);
-    e = cudaGetLastError();
-    cudaFreeAsync(part, stream);
-    if (e != cudaSuccess) return cuda_error(e, "tc_fold_kernel");
-    count_launch(1);
-  }
   return J4B_OK;
 }
 

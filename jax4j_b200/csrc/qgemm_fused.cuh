@@ -34,15 +34,22 @@ constexpr int qg_threads() { return (6 + qg_decode_warps<TERMS, N, NH>()) * 32; 
 
 // N tokens per MMA, NH accumulators of N columns each per CTA (NH = 2, N = 256: 512 tokens in bf16
 // mode, the whole TMEM, one CTA per SM; N = 64: decode-time batches).
-// Two rings of the same depth: A (the decoded weight tile, written by the decoders) and B (the
-// activation tiles, TMA). (A third B stage for the 512-token prefill tile, 224 KB of shared memory
-// against 160 KB, measured slower: 2.22 ms against 2.10 ms per 16384 x 14336 x 4096 projection.)
+// Two rings: A (the decoded weight tile, written by the decoders) and B (the activation tiles,
+// TMA). A B stage of a long prefill comes from L2 and needs more than one stage of MMAs to land,
+// so the bf16 prefill tile is 2 x 192 tokens with three B stages (48 KB each); 2 x 256 tokens
+// with two 64 KB stages left the tensor pipe 44% busy (2.1 ms per 16384 x 14336 x 4096
+// projection), and a third 64 KB stage left no room for the decoders' prefetch ring.
 template <int TERMS, int N, int NH>
 constexpr int qg_stages() { return (TERMS == 1 && N * NH <= 256) ? 2 : (TERMS == 3 && N * NH <= 128 ? 3 : 2); }
 template <int TERMS, int N, int NH>
 constexpr int qg_stages_a() { return qg_stages<TERMS, N, NH>(); }
 template <int TERMS, int N, int NH>
-constexpr int qg_stages_b() { return qg_stages<TERMS, N, NH>(); }
+constexpr int qg_stages_b() { return (TERMS == 1 && NH == 2 && N <= 192) ? 3 : qg_stages<TERMS, N, NH>(); }
+// TMEM columns allocated for NH accumulators of N columns (a power of two, at least 32)
+template <int N, int NH>
+constexpr uint32_t qg_tmem_cols() {
+  return N * NH <= 32 ? 32u : N * NH <= 64 ? 64u : N * NH <= 128 ? 128u : N * NH <= 256 ? 256u : 512u;
+}
 constexpr uint32_t kQgABytes = kQgBM * kQgBK * 2;  // one 128 x 64 bf16 tile
 template <int N, int NH>
 constexpr uint32_t qg_b_bytes() { return (uint32_t)(NH * N) * kQgBK * 2; }
@@ -61,6 +68,26 @@ constexpr int qg_min_blocks() { return (TERMS == 1 && N * NH <= 256) ? 2 : 1; }
 template <int TERMS, int N, int NH>
 constexpr int qg_decode_warps() { return qg_min_blocks<TERMS, N, NH>() == 2 ? 4 : 8; }
 
+// Decoder prefetch. A decoder's loads of its tiles' code and scale bytes come from L2/HBM and take
+// longer than one k-block of MMAs, so with one CTA per SM they go through a per-lane shared-memory
+// ring filled by cp.async, kQgPre k-blocks deep (48 bytes per lane, tile and k-block); a
+// configuration whose rings leave no room (two CTAs per SM) keeps one k-block of prefetch in
+// registers (depth 0 here).
+constexpr uint32_t kQgSlot = 48;  // bytes per lane per tile per k-block
+template <int TERMS, int N, int NH>
+constexpr uint32_t qg_pre_bytes(int depth) {
+  return (uint32_t)depth * 8u * 32u * kQgSlot;  // 8 row tiles per CTA, whatever the decoder split
+}
+template <int TERMS, int N, int NH>
+constexpr int qg_pre_depth() {
+  constexpr uint32_t kMax = 232448 - 1024 - 256;  // opt-in shared memory per block, minus slack
+  if (qg_min_blocks<TERMS, N, NH>() != 1) return 0;
+  return qg_ring_bytes<TERMS, N, NH>() + qg_pre_bytes<TERMS, N, NH>(4) <= kMax   ? 4
+         : qg_ring_bytes<TERMS, N, NH>() + qg_pre_bytes<TERMS, N, NH>(3) <= kMax ? 3
+         : qg_ring_bytes<TERMS, N, NH>() + qg_pre_bytes<TERMS, N, NH>(2) <= kMax ? 2
+                                                                                 : 0;
+}
+
 struct QgArgs {
   const uint8_t* data;
   Layout L;
@@ -71,6 +98,18 @@ struct QgArgs {
   const float* add;    // added to y (splits == 1 only; else the fold adds it)
   int* status;
 };
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int kPending>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(kPending) : "memory");
+}
 
 // One lane's bytes of one 16-row tile for one 64-column k-block (two 32-column groups).
 struct QgBytes {
@@ -105,6 +144,53 @@ __device__ __forceinline__ void qg_load(const QgArgs& a, int64_t tile, int kb, i
     const uint8_t* mp = base + meta + (gl / 8) * 256 + (g * 2) * 16;
     b.s0 = __ldg(reinterpret_cast<const uint4*>(mp));
     b.s1 = __ldg(reinterpret_cast<const uint4*>(mp + 16));
+  }
+}
+
+// The same bytes as qg_load, copied asynchronously into the lane's 48-byte slot at shared address
+// `slot`: [0, 16) the first code line, [16, 32) the second (Q8_0) or the rows' Q4_K headers of
+// row g, [32, 48) Q4_K row g + 8's headers, or the two group scale words (Q8_0, Q4_0). A tile past
+// the matrix gets zeros (plain stores, read back by the same lane).
+template <int QT>
+__device__ __forceinline__ void qg_copy(const QgArgs& a, int64_t tile, int kb, int lane, uint8_t* slot_ptr) {
+  const int g = lane >> 2;
+  const int64_t G = 2 * (int64_t)kb;
+  const int64_t s = G / 32;
+  const int gl = (int)(G % 32);
+  if (tile >= a.L.rt) {
+    uint4* z = reinterpret_cast<uint4*>(slot_ptr);
+    z[0] = z[1] = z[2] = make_uint4(0, 0, 0, 0);
+    return;
+  }
+  const uint32_t slot = (uint32_t)__cvta_generic_to_shared(slot_ptr);
+  const uint8_t* base = a.data + a.L.chunk_offset(s, tile);
+  const int64_t meta = (int64_t)a.L.groups_in_split(s) * GemvTraits<QT>::kQ;
+  if constexpr (QT == J4B_Q8_0) {
+    cp_async16(slot, base + gl * 512 + lane * 16);
+    cp_async16(slot + 16, base + (gl + 1) * 512 + lane * 16);
+    cp_async4(slot + 32, base + meta + gl * 32 + g * 4);
+    cp_async4(slot + 36, base + meta + (gl + 1) * 32 + g * 4);
+  } else if constexpr (QT == J4B_Q4_0) {
+    cp_async16(slot, base + (gl / 2) * 512 + lane * 16);
+    cp_async4(slot + 32, base + meta + gl * 32 + g * 4);
+    cp_async4(slot + 36, base + meta + (gl + 1) * 32 + g * 4);
+  } else {  // Q4_K
+    cp_async16(slot, base + (gl / 4) * 1024 + lane * 32 + (gl % 4) * 8);
+    const uint8_t* mp = base + meta + (gl / 8) * 256 + (g * 2) * 16;
+    cp_async16(slot + 16, mp);
+    cp_async16(slot + 32, mp + 16);
+  }
+}
+template <int QT>
+__device__ __forceinline__ void qg_read_slot(const uint8_t* slot, QgBytes& b) {
+  const uint4* v = reinterpret_cast<const uint4*>(slot);
+  b.q0 = v[0];
+  if constexpr (QT == J4B_Q4_K) {
+    b.s0 = v[1];
+    b.s1 = v[2];
+  } else {
+    b.q1 = v[1];
+    b.s0 = v[2];
   }
 }
 
@@ -251,7 +337,7 @@ __global__ void __launch_bounds__(qg_threads<TERMS, N, NH>(), qg_min_blocks<TERM
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(tmem_slot)),
-                 "r"(kBN));
+                 "r"(qg_tmem_cols<N, NH>()));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
   }
   tc_fence_before();
@@ -332,14 +418,39 @@ __global__ void __launch_bounds__(qg_threads<TERMS, N, NH>(), qg_min_blocks<TERM
   } else {
     // decoders: warp d owns row tiles [kT d, kT (d + 1)) of the 128-row A tile
     constexpr int kT = 8 / qg_decode_warps<TERMS, N, NH>();
+    constexpr int kPre = qg_pre_depth<TERMS, N, NH>();
     const int d = warp - 6;
     const int64_t tile0 = w0 / 16 + kT * d;
     QgBytes cur[kT], nxt[kT];
+    // the lane's slot of tile i for k-block kb in the prefetch ring (after both operand rings)
+    uint8_t* pre = smem + qg_ring_bytes<TERMS, N, NH>() + 256;
+    auto slot = [&](int kb, int i) {
+      return pre + ((uint32_t)(kb % (kPre > 0 ? kPre : 1)) * 8u + (uint32_t)(kT * d + i)) * (32u * kQgSlot) +
+             (uint32_t)lane * kQgSlot;
+    };
+    if constexpr (kPre > 0) {
+      for (int j = 0; j < kPre - 1; ++j) {
+        if (j < nk)
 #pragma unroll
-    for (int i = 0; i < kT; ++i) qg_load<QT>(p, tile0 + i, kb0, lane, cur[i]);
+          for (int i = 0; i < kT; ++i) qg_copy<QT>(p, tile0 + i, kb0 + j, lane, slot(j, i));
+        cp_async_commit();
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < kT; ++i) qg_load<QT>(p, tile0 + i, kb0, lane, cur[i]);
+    }
     for (int kb = 0; kb < nk; ++kb) {
       const int s = kb % kSA, use = kb / kSA;
-      if (kb + 1 < nk) {
+      if constexpr (kPre > 0) {
+        const int ahead = kb + kPre - 1;  // refills the slot read one iteration ago
+        if (ahead < nk)
+#pragma unroll
+          for (int i = 0; i < kT; ++i) qg_copy<QT>(p, tile0 + i, kb0 + ahead, lane, slot(ahead, i));
+        cp_async_commit();
+        cp_async_wait<kPre - 1>();  // k-block kb's copies have landed
+#pragma unroll
+        for (int i = 0; i < kT; ++i) qg_read_slot<QT>(slot(kb, i), cur[i]);
+      } else if (kb + 1 < nk) {
 #pragma unroll
         for (int i = 0; i < kT; ++i) qg_load<QT>(p, tile0 + i, kb0 + kb + 1, lane, nxt[i]);
       }
@@ -351,9 +462,12 @@ __global__ void __launch_bounds__(qg_threads<TERMS, N, NH>(), qg_min_blocks<TERM
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor-core reads
       __syncwarp();
       if (lane == 0) bar_arrive(&full_a[s]);
+      if constexpr (kPre == 0) {
 #pragma unroll
-      for (int i = 0; i < kT; ++i) cur[i] = nxt[i];
+        for (int i = 0; i < kT; ++i) cur[i] = nxt[i];
+      }
     }
+    if constexpr (kPre > 0) cp_async_wait<0>();  // nothing in flight into shared memory at exit
   }
   if (!ok) atomicExch(p.status, 1);
   tc_fence_before();
@@ -361,7 +475,7 @@ __global__ void __launch_bounds__(qg_threads<TERMS, N, NH>(), qg_min_blocks<TERM
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kBN));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(qg_tmem_cols<N, NH>()));
   }
 }
 
@@ -380,7 +494,8 @@ template <int QT, int TERMS, int N, int NH>
 cudaError_t launch_qgemm_fused(const j4b_qweight* w, const CUtensorMap& xh, const CUtensorMap& xl, int m, int kp,
                                int splits, int kb_per, float* out, const float* add, cudaStream_t stream) {
   constexpr int kBN = NH * N;
-  const size_t smem = (size_t)qg_ring_bytes<TERMS, N, NH>() + 1024 + 256;
+  const size_t smem = (size_t)qg_ring_bytes<TERMS, N, NH>() + 1024 + 256 +
+                     qg_pre_bytes<TERMS, N, NH>(qg_pre_depth<TERMS, N, NH>());
   static bool attr_set[kMaxDevices] = {};
   if (w->dev < 0 || w->dev >= kMaxDevices) return cudaErrorInvalidDevice;
   if (!attr_set[w->dev]) {
