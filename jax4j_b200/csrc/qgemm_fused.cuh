@@ -34,17 +34,17 @@ constexpr int qg_threads() { return (6 + qg_decode_warps<TERMS, N, NH>()) * 32; 
 
 // N tokens per MMA, NH accumulators of N columns each per CTA (NH = 2, N = 256: 512 tokens in bf16
 // mode, the whole TMEM, one CTA per SM; N = 64: decode-time batches).
-// Two rings: A (the decoded weight tile, written by the decoders) and B (the activation tiles,
-// TMA). A B stage of a long prefill comes from L2 and needs more than one stage of MMAs to land,
-// so the bf16 prefill tile is 2 x 192 tokens with three B stages (48 KB each); 2 x 256 tokens
-// with two 64 KB stages left the tensor pipe 44% busy (2.1 ms per 16384 x 14336 x 4096
-// projection), and a third 64 KB stage left no room for the decoders' prefetch ring.
+// Two rings of the same depth: A (the decoded weight tile, written by the decoders) and B (the
+// activation tiles, TMA). Measured on the 16384 x 14336 x 4096 bf16 prefill projection (2 x 256
+// tokens, two 64 KB B stages: 2.12 ms, tensor pipe 44% busy, shared-memory pipes ~32% busy):
+// a third B stage (224 KB, no room left for the decoders' prefetch ring) 2.22 ms; 2 x 192 tokens
+// with three 48 KB B stages 2.39 ms.
 template <int TERMS, int N, int NH>
 constexpr int qg_stages() { return (TERMS == 1 && N * NH <= 256) ? 2 : (TERMS == 3 && N * NH <= 128 ? 3 : 2); }
 template <int TERMS, int N, int NH>
 constexpr int qg_stages_a() { return qg_stages<TERMS, N, NH>(); }
 template <int TERMS, int N, int NH>
-constexpr int qg_stages_b() { return (TERMS == 1 && NH == 2 && N <= 192) ? 3 : qg_stages<TERMS, N, NH>(); }
+constexpr int qg_stages_b() { return qg_stages<TERMS, N, NH>(); }
 // TMEM columns allocated for NH accumulators of N columns (a power of two, at least 32)
 template <int N, int NH>
 constexpr uint32_t qg_tmem_cols() {

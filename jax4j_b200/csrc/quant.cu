@@ -1082,10 +1082,10 @@ int quant_gemm_fused(const j4b_qweight* w, const float* x, float* y, const float
                      int sms, cudaStream_t stream) {
   const int nk = (int)(kp / 64);
   const int n_tiles = (int)((w->rows + kQgBM - 1) / kQgBM);
-  // tokens per MMA: 64 for decode-time batches; bf16 mode 256 (one accumulator, two CTAs per SM)
-  // or 2 x 192 for long inputs; fp32-accurate mode 128 or 2 x 128
+  // tokens per MMA: 64 for decode-time batches; bf16 mode 256 (one accumulator and two CTAs per
+  // SM, or two accumulators for long inputs); fp32-accurate mode 128 or 2 x 128
   const int NH = m > 256 ? 2 : 1;
-  const int N = m <= 64 ? 64 : (terms == 1 ? (NH == 2 ? 192 : 256) : 128);
+  const int N = m <= 64 ? 64 : (terms == 1 ? 256 : 128);
   const int64_t t_tiles = (m + (int64_t)N * NH - 1) / ((int64_t)N * NH);
   // K splits: the count (at most 9, each split at least 8 k-blocks, partials at most 24 MB) whose
   // CTAs fill the SMs' slots best over whole waves, the fewest among near-equals
@@ -1128,11 +1128,11 @@ int quant_gemm_fused(const j4b_qweight* w, const float* x, float* y, const float
   case (QT * 4 + T) * 3 + 0: e = launch_qgemm_fused<QT, T, 64, 1>(w, mh, ml, mi, kpi, splits, kb_per, out, add, stream); break; \
   case (QT * 4 + T) * 3 + 1: e = launch_qgemm_fused<QT, T, NW, 1>(w, mh, ml, mi, kpi, splits, kb_per, out, add, stream); break; \
   case (QT * 4 + T) * 3 + 2: e = launch_qgemm_fused<QT, T, NW2, 2>(w, mh, ml, mi, kpi, splits, kb_per, out, add, stream); break;
-      J4B_QG_CASE(J4B_Q8_0, 1, 256, 192)
+      J4B_QG_CASE(J4B_Q8_0, 1, 256, 256)
       J4B_QG_CASE(J4B_Q8_0, 3, 128, 128)
-      J4B_QG_CASE(J4B_Q4_0, 1, 256, 192)
+      J4B_QG_CASE(J4B_Q4_0, 1, 256, 256)
       J4B_QG_CASE(J4B_Q4_0, 3, 128, 128)
-      J4B_QG_CASE(J4B_Q4_K, 1, 256, 192)
+      J4B_QG_CASE(J4B_Q4_K, 1, 256, 256)
       J4B_QG_CASE(J4B_Q4_K, 3, 128, 128)
 #undef J4B_QG_CASE
     }
