@@ -966,13 +966,9 @@ template <int QT>
 cudaError_t gemv_dispatch(const j4b_qweight* w, const float* x, const float* add, float* y,
                           int batch, int sms, cudaStream_t stream, const GemvPeers* peers = nullptr,
                           unsigned* grid_out = nullptr) {
-  static const char* variant = getenv("J4B_QGEMV_VARIANT");  // development A/B only
-  static const bool legacy = variant && variant[0] == 'l';
   const bool pdl = !w->fresh;
   const_cast<j4b_qweight*>(w)->fresh = false;
-  if (!legacy && batch <= 4) return launch_gemv_stream<QT, true, 16>(w, x, add, y, batch, sms, stream, peers, grid_out, pdl);
-  if (!legacy && batch <= 8) return launch_gemv_stream<QT, false, 16>(w, x, add, y, batch, sms, stream, peers, grid_out, pdl);
-  if (batch <= 4) return launch_gemv<QT, 1, true>(w, x, add, y, batch, sms, stream, peers, grid_out, pdl);
-  if (batch <= 8) return launch_gemv<QT, 1, false>(w, x, add, y, batch, sms, stream, peers, grid_out, pdl);
-  return launch_gemv<QT, 2, false>(w, x, add, y, batch, sms, stream, peers, grid_out, pdl);
+  if (batch <= 4) return launch_gemv_stream<QT, true, 15>(w, x, add, y, batch, sms, stream, peers, grid_out, pdl);
+  if (batch <= 8) return launch_gemv_stream<QT, false, 15>(w, x, add, y, batch, sms, stream, peers, grid_out, pdl);
+  return launch_gemv_stream<QT, false, 15, 2>(w, x, add, y, batch, sms, stream, peers, grid_out, pdl);
 }

@@ -1,23 +1,23 @@
-// Streaming dequant-GEMV for batch <= 8 (included by qgemv.cuh, inside namespace
+// Streaming dequant-GEMV for batch <= 16 (included by qgemv.cuh, inside namespace
 // j4b::<anonymous>; it reuses that file's fragment decoders tile_compute / tile_compute_pk and
-// its bulk-copy and mbarrier helpers).
+// its bulk-copy and mbarrier helpers). Batch <= 4 packs x's hi and lo halves into one 8-column
+// n-tile; 5..8 use one n-tile per half; 9..16 two n-tiles (NT = 2).
 //
-// Shape of one launch: one CTA per SM. With 8 compute warps the CTA takes at most half of an SM
-// (<= 112 KB of shared memory, 288 threads, <= 112 registers per thread), so that under
-// programmatic dependent launch the next GEMV's CTAs are resident and already streaming their
-// weights while this launch's CTAs finish their last tiles and their split-K folds; with 16 it
-// holds the whole SM with a deeper ring. A CTA owns one 1024-column K range ("split")
-// of a contiguous run of 16-row tiles:
+// Shape of one launch: one CTA per SM (15 compute warps + 1 producer warp, the whole SM's shared
+// memory for a deep ring; a half-SM variant with 8 compute warps, so that two launches' CTAs
+// co-reside, measured slower). A CTA owns one 1024-column K range ("split") of a contiguous run
+// of 16-row tiles:
 //   - the last warp is the producer: one elected lane streams the run's tile chunks (contiguous in the
 //     split-major layout) into a ring of shared-memory stages with 1-D bulk copies, each stage
 //     completing on its `full` mbarrier; it refills a stage once the warps that read it have
 //     arrived on its `empty` mbarrier. A run that fits the ring is issued whole before the
 //     dependency wait (weights are immutable once uploaded); of a longer run, about 48 KB, and
 //     the rest once x is staged.
-//   - the compute warps first turn x's 1024-column slice into fp16 hi/lo mma fragments in shared memory
-//     (warp w converts 128-column chunk w), then each warp takes whole tiles round-robin and
-//     walks the tile's 8 chunks itself, so a tile's partial sum over the split never leaves the
-//     warp's registers: no block barrier and no cross-warp reduction in the main loop.
+//   - the compute warps first turn x's 1024-column slice into fp16 hi/lo mma fragments in shared
+//     memory (one 128-column chunk of one n-tile per warp, round-robin), then each warp takes
+//     whole tiles round-robin and walks the tile's 8 chunks itself, so a tile's partial sum over
+//     the split never leaves the warp's registers: no block barrier and no cross-warp reduction
+//     in the main loop.
 //   - split-K: a warp stores its tile's partial into the weight's scratch, and the warp whose
 //     arrival completes the tile's counter adds the splits in split order (deterministic) and
 //     writes y (+ add); with one split the warp writes y directly.
@@ -25,11 +25,13 @@
 // weight's status word, lets every copy still in flight land, and returns.
 
 // NW compute warps + 1 producer warp. NW = 8: at most half an SM (112 KB of shared memory), so
-// two launches' CTAs co-reside; NW = 16: one CTA per SM with a deeper ring.
+// two launches' CTAs co-reside; NW = 15: one CTA per SM with a deeper ring, 512 threads, so the
+// compiler may give each thread 128 registers (17 warps cap it at 96 and the two-n-tile decode
+// spills).
 template <int NW>
 constexpr int stream_threads() { return (NW + 1) * 32; }
 template <int NW>
-constexpr int stream_smem_budget() { return NW == 8 ? 112 * 1024 : 220 * 1024; }
+constexpr int stream_smem_budget() { return NW <= 8 ? 112 * 1024 : 220 * 1024; }
 
 template <int QT>
 constexpr bool stream_needs_xblk() {
@@ -43,21 +45,25 @@ constexpr int stream_tiles_per_stage() {
 // Shared-memory bytes of one 128-column chunk's x fragments: packed (batch <= 4) 4 x 16 bytes
 // per lane of B fragments (+ 16 bytes of x block sums), unpacked 8 x 16 bytes (hi, lo of each
 // k-step) (+ 32 bytes of block sums).
-template <int QT, bool PK>
+// Batch 9..16 (NT = 2, unpacked only): the 8-column n-tile's block repeated for batch rows 8..15.
+template <int QT>
+constexpr int stream_frag_ntile() { return 4096 + (stream_needs_xblk<QT>() ? 1024 : 0); }
+template <int QT, bool PK, int NT = 1>
 constexpr int stream_frag_chunk() {
-  return PK ? 2048 + (stream_needs_xblk<QT>() ? 512 : 0) : 4096 + (stream_needs_xblk<QT>() ? 1024 : 0);
+  return PK ? 2048 + (stream_needs_xblk<QT>() ? 512 : 0) : NT * stream_frag_ntile<QT>();
 }
-template <int QT, bool PK, int NW>
+template <int QT, bool PK, int NW, int NT = 1>
 constexpr int stream_stages() {
   constexpr int stage = stream_tiles_per_stage<QT>() * GemvTraits<QT>::kChunk;
-  constexpr int r = (stream_smem_budget<NW>() - 8 * stream_frag_chunk<QT, PK>() - 512) / stage;
+  constexpr int r = (stream_smem_budget<NW>() - 8 * stream_frag_chunk<QT, PK, NT>() - 512) / stage;
   return r > 16 ? 16 : r;
 }
 // ring | x fragments | full[R] | empty[R] mbarriers | seq[R] stage numbers
-template <int QT, bool PK, int NW>
+template <int QT, bool PK, int NW, int NT = 1>
 constexpr int stream_smem_bytes() {
-  return stream_stages<QT, PK, NW>() * stream_tiles_per_stage<QT>() * GemvTraits<QT>::kChunk +
-         8 * stream_frag_chunk<QT, PK>() + 2 * 8 * stream_stages<QT, PK, NW>() + 4 * stream_stages<QT, PK, NW>();
+  return stream_stages<QT, PK, NW, NT>() * stream_tiles_per_stage<QT>() * GemvTraits<QT>::kChunk +
+         8 * stream_frag_chunk<QT, PK, NT>() + 2 * 8 * stream_stages<QT, PK, NW, NT>() +
+         4 * stream_stages<QT, PK, NW, NT>();
 }
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
@@ -85,16 +91,17 @@ __device__ __forceinline__ void x_staged_wait() {
 // before the wait (measured: Q8_0 4096 x 4096 at batch 8, 7 tiles per CTA, 8.2 us per call whole
 // against 9.0 us with 48 KB; Q4_K 14336 x 4096 at batch 1, 24 tiles per CTA, 14.9 us with 48 KB
 // against 16.5 us with the whole ring).
-template <int QT, bool PK, int NW>
+template <int QT, bool PK, int NW, int NT>
 constexpr int stream_pre_stages() {
   constexpr int stage = stream_tiles_per_stage<QT>() * GemvTraits<QT>::kChunk;
-  constexpr int r = stream_stages<QT, PK, NW>();
+  constexpr int r = stream_stages<QT, PK, NW, NT>();
   constexpr int p = 49152 / stage;
   return p < 1 ? 1 : (p > r ? r : p);
 }
-template <int QT, bool PK, int NW>
+template <int QT, bool PK, int NW, int NT>
 __device__ __forceinline__ int stream_pre_ring(int nstages) {
-  return nstages <= stream_stages<QT, PK, NW>() ? stream_stages<QT, PK, NW>() : stream_pre_stages<QT, PK, NW>();
+  return nstages <= stream_stages<QT, PK, NW, NT>() ? stream_stages<QT, PK, NW, NT>()
+                                                    : stream_pre_stages<QT, PK, NW, NT>();
 }
 // Waits (bounded) until the producer has issued stage `st` into its slot: only then is the slot's
 // `full` barrier on the phase of that stage, so its parity identifies the stage. (A warp can reach
@@ -119,14 +126,14 @@ __device__ __forceinline__ unsigned arrive_acq_rel(unsigned* ctr) {
   return old;
 }
 
-// Warp `c` converts x's columns [kc0 + 128c, kc0 + 128c + 128) of every batch row into the
-// chunk's fragment block (columns past K and rows past the batch are zeros).
+// Converts x's columns [kc0 + 128c, kc0 + 128c + 128) of batch rows row0.. into the fragment
+// block at dst (columns past K and rows past the batch are zeros).
 template <int QT, bool PK>
-__device__ __forceinline__ void stream_prep_x(const GemvArgs& a, int64_t kc0, int c, int lane, uint8_t* frag) {
+__device__ __forceinline__ void stream_prep_x(const GemvArgs& a, int64_t kc0, int c, int lane, uint8_t* dst,
+                                              int row0) {
   const int g = lane >> 2, t = lane & 3;
   constexpr int kXB = kXBlocks<QT>;
-  uint8_t* dst = frag + c * stream_frag_chunk<QT, PK>();
-  const int xrow = PK ? (g >> 1) : g;
+  const int xrow = row0 + (PK ? (g >> 1) : g);
   const bool row_ok = xrow < a.batch;
   const float* xr = a.x + (int64_t)xrow * a.cols;
   const int64_t kb = kc0 + c * 128 + 2 * t;
@@ -206,7 +213,8 @@ __device__ __forceinline__ void stream_prep_x(const GemvArgs& a, int64_t kc0, in
   }
 }
 
-// Output element cc of lane (g, t)'s accumulator -> (row in tile, batch column).
+// Output element cc of lane (g, t)'s accumulator -> (row in tile, batch column); unpacked element
+// cc belongs to n-tile cc / 4 (batch columns 8 (cc / 4) ..).
 template <bool PK>
 __device__ __forceinline__ void stream_coord(int lane, int cc, int& row, int& bcol) {
   const int g = lane >> 2, t = lane & 3;
@@ -214,19 +222,21 @@ __device__ __forceinline__ void stream_coord(int lane, int cc, int& row, int& bc
     row = g + 8 * cc;
     bcol = t;
   } else {
-    row = g + 8 * (cc >> 1);
-    bcol = 2 * t + (cc & 1);
+    row = g + 8 * ((cc & 3) >> 1);
+    bcol = 8 * (cc >> 2) + 2 * t + (cc & 1);
   }
 }
 
-template <int QT, bool PK, int NW>
+template <int QT, bool PK, int NW, int NT>
 __global__ void __launch_bounds__(stream_threads<NW>(), NW == 8 ? 2 : 1) qgemv_stream_kernel(GemvArgs a) {
   using T = GemvTraits<QT>;
-  constexpr int R = stream_stages<QT, PK, NW>();
+  static_assert(NT == 1 || (NT == 2 && !PK), "two n-tiles: unpacked fragments only");
+  constexpr int R = stream_stages<QT, PK, NW, NT>();
   constexpr int kU = stream_tiles_per_stage<QT>();
   constexpr int kStage = kU * T::kChunk;
-  constexpr int kFrag = stream_frag_chunk<QT, PK>();
-  constexpr int kNV = PK ? 2 : 4;  // accumulator floats per lane per tile
+  constexpr int kFrag = stream_frag_chunk<QT, PK, NT>();
+  constexpr int kFragN = stream_frag_ntile<QT>();  // one n-tile's part of an unpacked chunk
+  constexpr int kNV = PK ? 2 : 4 * NT;  // accumulator floats per lane per tile
   constexpr int kXB = kXBlocks<QT>;
   static_assert(R >= 2, "ring too small");
   extern __shared__ __align__(128) uint8_t smem[];
@@ -272,7 +282,7 @@ __global__ void __launch_bounds__(stream_threads<NW>(), NW == 8 ? 2 : 1) qgemv_s
       tma_load_1d_stream(ring + (st % R) * kStage, a.data + a.L.chunk_offset(split, tile0 + first), bytes, bar,
                          policy);
     };
-    const int pre = stream_pre_ring<QT, PK, NW>(nstages);
+    const int pre = stream_pre_ring<QT, PK, NW, NT>(nstages);
     if (lane == 0)
       for (; issued < pre && issued < nstages; issued++) issue(issued);
     pdl_launch_dependents();
@@ -294,7 +304,9 @@ __global__ void __launch_bounds__(stream_threads<NW>(), NW == 8 ? 2 : 1) qgemv_s
     pdl_launch_dependents();
     pdl_wait();
     const GatherSlot gslot = gather_slot(a);  // peer all-gather only
-    if (warp < nchunks) stream_prep_x<QT, PK>(a, kc0, warp, lane, frag);
+    // the (chunk, n-tile) blocks of x round-robin over the compute warps
+    for (int b = warp; b < 8 * NT; b += NW)
+      if ((b & 7) < nchunks) stream_prep_x<QT, PK>(a, kc0, b & 7, lane, frag + (b & 7) * kFrag + (b >> 3) * kFragN, 8 * (b >> 3));
     x_staged_arrive<NW>();
     compute_warps_sync<NW>();
 
@@ -336,33 +348,43 @@ __global__ void __launch_bounds__(stream_threads<NW>(), NW == 8 ? 2 : 1) qgemv_s
             acc[0] = r2[0];
             acc[1] = r2[1];
           } else {
-            uint32_t bh[1][8][2], bl[1][8][2];
+            uint32_t bh[NT][8][2], bl[NT][8][2];
+            float xb[NT][kXB][2];
 #pragma unroll
-            for (int j = 0; j < 8; j++) {
-              const uint4 v = *reinterpret_cast<const uint4*>(fc + (j * 32 + lane) * 16);
-              bh[0][j][0] = v.x;
-              bh[0][j][1] = v.y;
-              bl[0][j][0] = v.z;
-              bl[0][j][1] = v.w;
-            }
-            float xb[1][kXB][2];
-            if constexpr (stream_needs_xblk<QT>()) {
-              const float4 v0 = *reinterpret_cast<const float4*>(fc + 4096 + lane * 16);
-              const float4 v1 = *reinterpret_cast<const float4*>(fc + 4096 + 512 + lane * 16);
-              const float vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+            for (int n = 0; n < NT; n++) {
+              const uint8_t* fn = fc + n * kFragN;
 #pragma unroll
-              for (int q = 0; q < kXB; q++) {
-                xb[0][q][0] = vv[2 * q];
-                xb[0][q][1] = vv[2 * q + 1];
+              for (int j = 0; j < 8; j++) {
+                const uint4 v = *reinterpret_cast<const uint4*>(fn + (j * 32 + lane) * 16);
+                bh[n][j][0] = v.x;
+                bh[n][j][1] = v.y;
+                bl[n][j][0] = v.z;
+                bl[n][j][1] = v.w;
               }
-            } else {
+              if constexpr (stream_needs_xblk<QT>()) {
+                const float4 v0 = *reinterpret_cast<const float4*>(fn + 4096 + lane * 16);
+                const float4 v1 = *reinterpret_cast<const float4*>(fn + 4096 + 512 + lane * 16);
+                const float vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
 #pragma unroll
-              for (int q = 0; q < kXB; q++) xb[0][q][0] = xb[0][q][1] = 0.f;
+                for (int q = 0; q < kXB; q++) {
+                  xb[n][q][0] = vv[2 * q];
+                  xb[n][q][1] = vv[2 * q + 1];
+                }
+              } else {
+#pragma unroll
+                for (int q = 0; q < kXB; q++) xb[n][q][0] = xb[n][q][1] = 0.f;
+              }
             }
-            float r4[1][4] = {{acc[0], acc[1], acc[2], acc[3]}};
-            tile_compute<QT, 1>(base, base + meta_off, c, lane, bh, bl, xb, r4);
+            float r4[NT][4];
 #pragma unroll
-            for (int i = 0; i < 4; i++) acc[i] = r4[0][i];
+            for (int n = 0; n < NT; n++)
+#pragma unroll
+              for (int i = 0; i < 4; i++) r4[n][i] = acc[4 * n + i];
+            tile_compute<QT, NT>(base, base + meta_off, c, lane, bh, bl, xb, r4);
+#pragma unroll
+            for (int n = 0; n < NT; n++)
+#pragma unroll
+              for (int i = 0; i < 4; i++) acc[4 * n + i] = r4[n][i];
           }
         }
       }
@@ -428,15 +450,15 @@ __global__ void __launch_bounds__(stream_threads<NW>(), NW == 8 ? 2 : 1) qgemv_s
   }
 }
 
-template <int QT, bool PK, int NW>
+template <int QT, bool PK, int NW, int NT = 1>
 cudaError_t launch_gemv_stream(const j4b_qweight* w, const float* x, const float* add, float* y, int batch,
                                int sms, cudaStream_t stream, const GemvPeers* peers, unsigned* grid_out,
                                bool pdl) {
-  constexpr int smem = stream_smem_bytes<QT, PK, NW>();
+  constexpr int smem = stream_smem_bytes<QT, PK, NW, NT>();
   static bool attr_set[kMaxDevices] = {};  // function attributes are per device context
   if (w->dev < 0 || w->dev >= kMaxDevices) return cudaErrorInvalidDevice;
   if (!attr_set[w->dev]) {
-    cudaError_t e = cudaFuncSetAttribute(qgemv_stream_kernel<QT, PK, NW>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaError_t e = cudaFuncSetAttribute(qgemv_stream_kernel<QT, PK, NW, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     attr_set[w->dev] = true;
   }
@@ -477,5 +499,5 @@ cudaError_t launch_gemv_stream(const j4b_qweight* w, const float* x, const float
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
   if (grid_out) *grid_out = cfg.gridDim.x;
-  return cudaLaunchKernelEx(&cfg, qgemv_stream_kernel<QT, PK, NW>, a);
+  return cudaLaunchKernelEx(&cfg, qgemv_stream_kernel<QT, PK, NW, NT>, a);
 }
