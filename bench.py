@@ -383,7 +383,7 @@ def cpu_tape_rate(rows, cols, threads, budget_s):
 
 
 def gemv_kernel_name(batch):
-    return "qgemv_stream_kernel" if batch <= 8 else "qgemv_kernel"
+    return "qgemv_stream_kernel" if batch <= 16 else "qgemm_fused_kernel"
 
 
 def cpu_mlp_rate(batch, d_in, budget_s):

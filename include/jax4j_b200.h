@@ -199,10 +199,10 @@ int j4b_quant_upload_device(int dev, j4b_buf blocks, size_t bytes, int ggml_type
 int j4b_quant_free(j4b_qweight_t w);
 int j4b_quant_shape(j4b_qweight_t w, int* ggml_type, int64_t* rows, int64_t* cols);
 /* quantMatvec / quantMatvecAdd (QuantizedOps.java:26-30), batched: x [batch, cols] f32,
- * add [batch, rows] f32 or 0, y [batch, rows] f32. batch = 1 is the reference call. Up to 16
- * rows of x: the dequant-GEMV (fp16 fragments of the codes, x split into fp16 hi + lo, fp32
- * accumulation); more rows (Q8_0, Q4_0, Q4_K): one pass of the fused dequant-GEMM below in its
- * fp32-accurate mode. Either way relative error ~1e-5 (bar 1e-4). */
+ * add [batch, rows] f32 or 0, y [batch, rows] f32. batch = 1 is the reference call. The
+ * dequant-GEMV (fp16 fragments of the codes, x split into fp16 hi + lo, fp32 accumulation) in
+ * passes of up to 16 rows of x; from 33 rows (Q8_0) or 49 rows (Q4_0, Q4_K) one pass of the fused
+ * dequant-GEMM below in its fp32-accurate mode. Either way relative error ~1e-5 (bar 1e-4). */
 int j4b_quant_matvec(j4b_qweight_t w, j4b_buf x, j4b_buf add, j4b_buf y, int64_t batch,
                      j4b_stream s);
 /* The same with HOST buffers (QuantizedOps.java:26-30 as a host caller makes it: upload x, the

@@ -64,49 +64,114 @@ __device__ __forceinline__ void finish_step(unsigned* step, unsigned* done, unsi
   }
 }
 
+// Two consecutive flagged words (16-byte aligned) in one load; each 8-byte word is read
+// single-copy atomically, so value and flag of a word always belong together.
+__device__ __forceinline__ ulonglong2 gather_load2(const unsigned long long* p) {
+  ulonglong2 w;
+  asm volatile("ld.relaxed.sys.global.v2.b64 {%0, %1}, [%2];" : "=l"(w.x), "=l"(w.y) : "l"(p) : "memory");
+  return w;
+}
+
+constexpr int kWaitCopyThreads = 512;
+constexpr int kWaitCopyPairs = 4;  // word pairs a thread loads before it checks any of their flags
+
 // Copies this rank's gathered half (every source's flagged words of this step) to `out` once the
 // flags show up, then advances the step counter. Launched as a programmatic dependent of the
 // GEMV; it lets its own dependents launch at once (the next GEMV's weight prefetch overlaps the
 // wait), and it waits for the GEMV to finish before it reads the step counter, which the previous
 // step's copy advanced (a launch two kernels back is not otherwise ordered before this one).
-__global__ void wait_copy_kernel(unsigned* step, unsigned* done, const unsigned long long* data, int64_t half_words,
-                                 float* out, int64_t n, int* status) {
+// Each thread issues the loads of up to kWaitCopyPairs word pairs before it looks at a flag, and
+// re-reads only a pair whose flags have not arrived: the copy costs about one load round trip
+// when the peers' stores have landed.
+__global__ void __launch_bounds__(kWaitCopyThreads) wait_copy_kernel(unsigned* step, unsigned* done,
+                                                                     const unsigned long long* data,
+                                                                     int64_t half_words, float* out, int64_t n,
+                                                                     int* status) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const unsigned s = *(volatile unsigned*)step;
-  const unsigned long long* src = data + (int64_t)(s & 1u) * half_words;
+  const unsigned want = s + 1u;
+  const unsigned long long* src = data + (int64_t)(s & 1u) * half_words;  // 16-byte aligned
   const uint64_t t0 = global_ns();
   bool timed_out = false;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
-    out[i] = wait_word(src + i, s + 1u, t0, timed_out);
+  const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x, stride = (int64_t)gridDim.x * blockDim.x;
+  if (((uintptr_t)out & 7u) == 0) {
+    const int64_t npairs = n / 2;
+    float2* out2 = reinterpret_cast<float2*>(out);
+    for (int64_t p0 = tid; p0 < npairs; p0 += stride * kWaitCopyPairs) {
+      ulonglong2 w[kWaitCopyPairs];
+#pragma unroll
+      for (int u = 0; u < kWaitCopyPairs; ++u)
+        if (p0 + u * stride < npairs) w[u] = gather_load2(src + 2 * (p0 + u * stride));
+#pragma unroll
+      for (int u = 0; u < kWaitCopyPairs; ++u) {
+        const int64_t p = p0 + u * stride;
+        if (p >= npairs) break;
+        while (((unsigned)(w[u].x >> 32) != want || (unsigned)(w[u].y >> 32) != want) && !timed_out) {
+          if (global_ns() - t0 > kPeerWaitNs) {
+            timed_out = true;
+            break;
+          }
+          w[u] = gather_load2(src + 2 * p);
+        }
+        out2[p] = make_float2(__uint_as_float((unsigned)w[u].x), __uint_as_float((unsigned)w[u].y));
+      }
+    }
+    if ((n & 1) && tid == 0) out[n - 1] = wait_word(src + n - 1, want, t0, timed_out);
+  } else {
+    for (int64_t i = tid; i < n; i += stride) out[i] = wait_word(src + i, want, t0, timed_out);
+  }
   if (timed_out) atomicExch(status, 1);
   finish_step(step, done, s);
 }
 
-// One CTA per 1024-element chunk: write the chunk into slot `rank` of every rank as flagged words,
-// then read slot q of every source q from this rank's buffer as its flags appear and sum the
-// slots in rank order.
-__global__ void allreduce_kernel(PeerBases bases, int nranks, int rank, int channel, int64_t slice_words,
-                                 const float* src, int64_t n, float* out, int* status) {
-  constexpr int kChunk = 1024;
+constexpr int kAllreduceThreads = 256;
+
+// One thread per element: write it into slot `rank` of every rank as flagged words, then load slot
+// q of every source q from this rank's buffer (all loads issued before any flag is checked; a
+// slot whose flag has not arrived is re-read) and sum the slots in rank order.
+__global__ void __launch_bounds__(kAllreduceThreads) allreduce_kernel(PeerBases bases, int nranks, int rank,
+                                                                      int channel, int64_t slice_words,
+                                                                      const float* src, int64_t n, float* out,
+                                                                      int* status) {
   uint8_t* mine = bases.base[rank];
   unsigned* step = reinterpret_cast<unsigned*>(mine) + channel;
   unsigned* done = reinterpret_cast<unsigned*>(mine + 64) + channel;
   const unsigned s = *(volatile unsigned*)step;
+  const unsigned want = s + 1u;
   const int64_t par = (int64_t)(s & 1u) * (slice_words / 2);
-  const int64_t i0 = (int64_t)blockIdx.x * kChunk, i1 = min(n, i0 + kChunk);
-  for (int p = 0; p < nranks; ++p) {
-    unsigned long long* dst =
-        reinterpret_cast<unsigned long long*>(bases.base[p] + kDataOffset) + channel * slice_words + par + (int64_t)rank * n;
-    for (int64_t i = i0 + threadIdx.x; i < i1; i += blockDim.x) gather_store(dst + i, src[i], s + 1u);
-  }
-  const unsigned long long* slots =
-      reinterpret_cast<const unsigned long long*>(mine + kDataOffset) + channel * slice_words + par;
-  const uint64_t t0 = global_ns();
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   bool timed_out = false;
-  for (int64_t i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
-    float acc = wait_word(slots + i, s + 1u, t0, timed_out);
-    for (int q = 1; q < nranks; ++q) acc = __fadd_rn(acc, wait_word(slots + (int64_t)q * n + i, s + 1u, t0, timed_out));
+  if (i < n) {
+    const float v = src[i];
+#pragma unroll
+    for (int p = 0; p < kMaxPeerRanks; ++p) {
+      if (p < nranks) {
+        unsigned long long* dst = reinterpret_cast<unsigned long long*>(bases.base[p] + kDataOffset) +
+                                  channel * slice_words + par + (int64_t)rank * n;
+        gather_store(dst + i, v, want);
+      }
+    }
+    const unsigned long long* slots =
+        reinterpret_cast<const unsigned long long*>(mine + kDataOffset) + channel * slice_words + par + i;
+    unsigned long long w[kMaxPeerRanks];
+#pragma unroll
+    for (int q = 0; q < kMaxPeerRanks; ++q)
+      if (q < nranks) w[q] = gather_load(slots + (int64_t)q * n);
+    const uint64_t t0 = global_ns();
+    float acc = 0.0f;
+#pragma unroll
+    for (int q = 0; q < kMaxPeerRanks; ++q) {
+      if (q < nranks) {
+        unsigned long long wq = w[q];
+        while ((unsigned)(wq >> 32) != want && !timed_out) {
+          if (global_ns() - t0 > kPeerWaitNs) timed_out = true;
+          else wq = gather_load(slots + (int64_t)q * n);
+        }
+        const float x = __uint_as_float((unsigned)wq);
+        acc = q == 0 ? x : __fadd_rn(acc, x);
+      }
+    }
     out[i] = acc;
   }
   if (timed_out) atomicExch(status, 1);
@@ -240,10 +305,12 @@ int peer_wait_copy(const j4b_peer_group* g, int channel, float* out, int64_t n, 
   unsigned* step = reinterpret_cast<unsigned*>(mine) + channel;
   unsigned* done = reinterpret_cast<unsigned*>(mine + 64) + channel;
   const unsigned long long* data = reinterpret_cast<const unsigned long long*>(mine + kDataOffset) + channel * slice;
-  const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>((n + 1023) / 1024, 148));
+  // about one word pair per thread, up to kWaitCopyPairs pairs per thread on one CTA per SM
+  const int64_t ctas = ((n + 1) / 2 + kWaitCopyThreads - 1) / kWaitCopyThreads;
+  const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(ctas, 148));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(256);
+  cfg.blockDim = dim3(kWaitCopyThreads);
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -265,14 +332,14 @@ extern "C" int j4b_peer_allreduce(j4b_peer_group* g, int channel, j4b_buf src, i
   J4B_REQUIRE(n >= 1 && src && out, "all-reduce needs n >= 1 and buffers");
   const int64_t slice = peer_slice_words(g);
   J4B_REQUIRE(2 * (int64_t)g->nranks * n <= slice, "peer buffer slice too small for the all-reduce");
-  J4B_REQUIRE((n + 1023) / 1024 <= 0x7fffffffLL, "all-reduce of %lld elements is too long", (long long)n);
+  J4B_REQUIRE((n + kAllreduceThreads - 1) / kAllreduceThreads <= 0x7fffffffLL, "all-reduce of %lld elements is too long",
+              (long long)n);
   DeviceGuard guard(g->dev);
   cudaStream_t stream = resolve_stream(g->dev, s);
   PeerBases b;
   for (int p = 0; p < kMaxPeerRanks; ++p) b.base[p] = p < g->nranks ? g->base[p] : nullptr;
-  allreduce_kernel<<<(unsigned)((n + 1023) / 1024), 256, 0, stream>>>(b, g->nranks, g->rank, channel, slice,
-                                                                      (const float*)(uintptr_t)src, n,
-                                                                      (float*)(uintptr_t)out, g->status);
+  allreduce_kernel<<<(unsigned)((n + kAllreduceThreads - 1) / kAllreduceThreads), kAllreduceThreads, 0, stream>>>(
+      b, g->nranks, g->rank, channel, slice, (const float*)(uintptr_t)src, n, (float*)(uintptr_t)out, g->status);
   J4B_CHECK_LAUNCH("allreduce_kernel");
   return J4B_OK;
 }

@@ -22,10 +22,11 @@
 // 1 + q/16 offset, via precomputed block sums of x) is applied in fp32 on the block partials.
 // Accuracy: normwise relative error ~1e-6, inside the 1e-4 fp32-accumulate bar.
 //
-// Work split: a CTA of 8 warps owns one K range of 1024 columns (8 warp chunks of 128) and a run
-// of row tiles; each warp keeps its chunk's x fragments in registers for the whole run. Warp
-// partials are summed in shared memory; K ranges are combined by the last CTA to finish a row
-// tile (per-tile arrival counter, partials in per-weight scratch), which also applies `add`.
+// Work split (qgemv_stream.cuh): one CTA per SM owns one K range of 1024 columns and a run of row
+// tiles, streamed into shared memory by a producer warp; each compute warp owns whole tiles, so
+// a tile's partial over the K range stays in one warp's registers. K ranges are combined by the
+// warp whose arrival completes the tile's counter (partials in per-weight scratch, added in K
+// order), which also applies `add`.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -778,10 +779,13 @@ extern "C" int j4b_quant_matvec(j4b_qweight_t w, j4b_buf x, j4b_buf add, j4b_buf
   DeviceGuard guard(w->dev);
   cudaStream_t stream = resolve_stream(w->dev, s);
   const int sms = device_ctx(w->dev)->sm_count;
-  // more than 16 rows of x: one pass over the weight on the tensor cores (the fused dequant-GEMM
-  // in its fp32-accurate 3-term mode) instead of a GEMV pass per 16 rows
-  static const bool passes = getenv("J4B_QGEMV_PASSES") != nullptr;  // development A/B only
-  if (batch > 16 && !passes && (w->type == J4B_Q8_0 || w->type == J4B_Q4_0 || w->type == J4B_Q4_K) &&
+  // Larger batches: one pass over the weight on the tensor cores (the fused dequant-GEMM in its
+  // fp32-accurate 3-term mode) instead of a GEMV pass per 16 rows. Its cost is nearly flat in the
+  // batch up to 64 rows (decode-bound), so it wins only past two or three GEMV passes. Measured
+  // per call (one B200): Q4_K 14336 x 4096 GEMV 23.5 us per 16 rows, fused 81-87 us at 17-64
+  // rows; Q4_0 of that shape 21.2 against 70-75 us; Q8_0 4096 x 4096 9.9 against 22-25 us.
+  const int64_t fused_from = w->type == J4B_Q8_0 ? 33 : 49;
+  if (batch >= fused_from && (w->type == J4B_Q8_0 || w->type == J4B_Q4_0 || w->type == J4B_Q4_K) &&
       batch <= INT32_MAX) {
     w->fresh = false;
     return quant_gemm_fused(w, (const float*)(uintptr_t)x, (float*)(uintptr_t)y,

@@ -45,6 +45,11 @@ for rows, cols, batch, qtype in ((96, 512, 3, 8), (256, 4096, 8, 8), (160, 2048,
     dist.all_gather(parts, torch.from_numpy(mine.reshape(-1)).cuda())
     want = np.concatenate([p.cpu().numpy().reshape(batch, rows) for p in parts], axis=1)
     assert np.array_equal(got, want), ("all-gather mismatch", rows, cols, batch)
+    if rows == 96:  # an output 4 bytes past an 8-byte boundary: the copy's word-at-a-time path
+        y_off = torch.empty(batch * rows * world + 1, device="cuda")
+        pg.allgather_matvec(wq, xb.ptr, y_off.data_ptr() + 4, batch, s)
+        torch.cuda.synchronize()
+        assert np.array_equal(y_off[1:].cpu().numpy().reshape(batch, world * rows), want), "unaligned all-gather"
     # the host-buffer form: pinned x in and gathered y out, read and written by the kernels
     xh = torch.from_numpy(x).pin_memory()
     yh = torch.zeros(batch * rows * world).pin_memory()

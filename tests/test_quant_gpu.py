@@ -56,7 +56,7 @@ def test_device_encoder_byte_identical(backend, oracle, qtype):
 
 
 @pytest.mark.parametrize("qtype", TYPES)
-@pytest.mark.parametrize("batch", [1, 3, 8, 9, 16, 21])
+@pytest.mark.parametrize("batch", [1, 3, 8, 9, 16, 21, 40, 64])
 def test_matvec_within_tolerance(backend, oracle, qtype, batch):
     for i, (rows, cols) in enumerate(SHAPES[qtype]):
         _, blob = make(oracle, qtype, rows, cols, 300 + i)
