@@ -67,6 +67,30 @@ def test_matvec_within_tolerance(backend, oracle, qtype, batch):
         assert normwise(y, y64) <= REL, (rows, cols, batch, normwise(y, y64))
 
 
+@pytest.mark.parametrize("qtype", [Q8_0, Q4_0, Q4_K])
+@pytest.mark.parametrize("batch", [17, 33, 64])
+def test_matvec_add_at_decode_batches(backend, oracle, qtype, batch):
+    """17..64 rows of x with `add`: GEMV passes of 16 rows, or from 33 (Q8_0) / 49 (Q4_0, Q4_K)
+    rows the fused dequant-GEMM (add applied in its epilogue or in the split-K fold); ragged rows
+    and columns."""
+    rows, cols = (150, 1280) if qtype == Q4_K else (150, 1120)
+    _, blob = make(oracle, qtype, rows, cols, 900 + batch)
+    w = backend.upload_quantized(blob, qtype, (rows, cols))
+    x = np.random.default_rng(batch).standard_normal((batch, cols)).astype(np.float32)
+    add = np.random.default_rng(batch + 1).standard_normal((batch, rows)).astype(np.float32)
+    y64 = oracle.quant_matvec_f64(qtype, blob, rows, cols, x)
+    ya = backend.download(backend.quant_matvec_add(w, backend.upload(x, x.shape),
+                                                   backend.upload(add, add.shape))).reshape(batch, rows)
+    assert normwise(ya - add, y64) <= REL
+    # a long K range: partials of several K splits folded in split order
+    rows2, cols2 = 256, 8192
+    _, blob2 = make(oracle, qtype, rows2, cols2, 901)
+    w2 = backend.upload_quantized(blob2, qtype, (rows2, cols2))
+    x2 = np.random.default_rng(5).standard_normal((batch, cols2)).astype(np.float32)
+    y2 = backend.download(backend.quant_matvec(w2, backend.upload(x2, x2.shape))).reshape(batch, rows2)
+    assert normwise(y2, oracle.quant_matvec_f64(qtype, blob2, rows2, cols2, x2)) <= REL
+
+
 def test_reference_shaped_call_and_add(backend, oracle):
     """Rank-1 x is the reference's quantMatvec / quantMatvecAdd (CpuBackend.java:707-736)."""
     rows, cols = 48, 512
