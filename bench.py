@@ -233,9 +233,10 @@ SECONDARY = ("q4_k_b1", "q4_k_b16", "rms_swiglu")
 # dominant kernel from one ncu capture of the same command, with the capture it comes from. A
 # constant of this file, not a run-time measurement: the bench itself never runs under ncu.
 TRAFFIC = {
-    "q8_0_b8": (17996288, "ncu capture of one qgemv_stream_kernel launch (profiles/qgemv_q8_0_b8.md)"),
+    "q8_0_b8": (17995776, "ncu capture of one qgemv_stream_kernel launch (profiles/qgemv_q8_0_b8.md)"),
     "q4_k_b1": (33089280, "ncu capture of one qgemv_stream_kernel launch (profiles/qgemv_q4_k_b1.md)"),
-    "q6_k_b1": (48293632, "ncu capture of one qgemv_kernel launch (profiles/qgemv_q6_k_b1.md)"),
+    "q4_k_b16": (33368576, "ncu capture of one qgemv_stream_kernel launch (profiles/qgemv_q4_k_b16.md)"),
+    "q6_k_b1": (48288000, "ncu capture of one qgemv_stream_kernel launch (profiles/qgemv_q6_k_b1.md)"),
     "rms_swiglu": (229038848, "ncu capture of one j4b_group0 launch (profiles/tape_rms_swiglu.md)"),
 }
 
