@@ -1137,7 +1137,9 @@ def run_engine_gemm(args):
                        "timing": "K back-to-back calls (operand decode/conversion included), CUDA events"},
             "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
                          "frac": round(achieved / peak, 4), "traffic": None, "peak_source": peak_src,
-                         "kernel": "tc_gemm_kernel + operand conversion (the whole call)",
+                         "kernel": ("qgemm_fused_kernel + x conversion (the whole call; the weight decoded "
+                                    "inside the GEMM)" if qtype is not None
+                                    else "tc_gemm_kernel + operand conversion (the whole call)"),
                          "kernel_avg_us": round(step_ms * 1e3, 1)},
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e, 3), "unit": "TFLOP/s", "h2d_bytes_per_step": m * k * 4,
@@ -1727,7 +1729,7 @@ def run_engine_decoder(args):
         roof = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
                 "frac": round(achieved / peak, 4), "traffic": None,
                 "peak_source": "measured MEASURED_PEAKS.json bf16_tflops_sustained" if pk else "fallback 1.4 PFLOP/s",
-                "kernel": "the whole prefill step (tc_gemm_kernel projections hold ~97% of its flops)",
+                "kernel": "the whole prefill step (qgemm_fused_kernel projections hold ~97% of its flops)",
                 "kernel_avg_us": round(step_ms * 1e3, 1)}
         value = flops / (step_ms * 1e-3) / 1e12
         unit = "TFLOP/s"
