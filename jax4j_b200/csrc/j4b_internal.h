@@ -88,8 +88,12 @@ constexpr int kMaxPeerRanks = 8;
 struct GemvPeers {
   int nranks, rank;
   unsigned long long* y[kMaxPeerRanks];  // each rank's gathered buffer (the channel's data slice)
-  const unsigned* step;                  // this rank's step counter of the channel
+  unsigned* step;                        // this rank's step counter of the channel
+  unsigned* done;                        // this rank's finished-warp counter of the channel
   int64_t half_words;                    // flagged words per parity half of the slice
+  float* out;                            // the gathered output, [batch][rows * nranks]
+  int64_t gathered;                      // its floats
+  int* status;                           // the group's status word (a wait that gave up)
 };
 
 // A flagged word of the peer buffers: a float value in the low half, the step flag (step + 1) in
@@ -105,9 +109,16 @@ __device__ __forceinline__ unsigned long long gather_load(const unsigned long lo
   asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
   return w;
 }
+// Two consecutive flagged words (16-byte aligned) in one load; each 8-byte word is read
+// single-copy atomically, so value and flag of a word always belong together.
+__device__ __forceinline__ ulonglong2 gather_load2(const unsigned long long* p) {
+  ulonglong2 w;
+  asm volatile("ld.relaxed.sys.global.v2.b64 {%0, %1}, [%2];" : "=l"(w.x), "=l"(w.y) : "l"(p) : "memory");
+  return w;
+}
+constexpr uint64_t kPeerWaitNs = 1000000000ull;  // a peer's words: one second before giving up
 int peer_group_ranks(const j4b_peer_group* g);
-int peer_gemv_targets(const j4b_peer_group* g, int channel, int64_t gathered_floats, GemvPeers* t);
-int peer_wait_copy(const j4b_peer_group* g, int channel, float* out, int64_t n, cudaStream_t stream);
+int peer_gemv_targets(const j4b_peer_group* g, int channel, float* out, int64_t gathered_floats, GemvPeers* t);
 
 // out[k] = sum of a[sources[p]] for p in [offsets[k], offsets[k+1]), in that order
 int launch_segment_sum(const float* a, const int64_t* offsets, const int64_t* sources, int64_t n_dst,

@@ -2,7 +2,8 @@
 //
 // Replaces the NCCL calls of the sharded paths: the row-sharded GEMV's all-gather of y
 // (j4b_quant_matvec_allgather: the GEMV epilogue itself stores each output into every rank's
-// buffer) and the data-parallel tape's all-reduce of [dg, loss] (j4b_peer_allreduce: every rank
+// buffer, and the GEMV's warps then copy the gathered words out as their flags arrive, in the
+// same kernel) and the data-parallel tape's all-reduce of [dg, loss] (j4b_peer_allreduce: every rank
 // writes its vector into every rank's slot, then sums the slots in rank order -- deterministic,
 // identical on all ranks).
 //
@@ -10,7 +11,8 @@
 // group holds all of them. Layout of each rank's buffer:
 //   [0, 64)        step counter per channel (local; selects the parity half and the flag, advanced
 //                  once per collective call by the rank's own kernel)
-//   [64, 128)      finished-CTA counter of the reading kernel per channel (local)
+//   [64, 128)      finished-reader counter per channel (local; the reading kernel's last CTA or
+//                  warp to finish advances the step counter and resets it)
 //   [131072, end)  data, one slice per channel, each split into two parity halves of flagged
 //                  words (gather_store: value and step flag in one 64-bit store)
 // A reader of step k waits, word by word, until the flag k + 1 appears: no fence, arrival
@@ -32,25 +34,10 @@ namespace {
 
 constexpr int kChannels = 16;
 constexpr size_t kDataOffset = 131072;
-constexpr uint64_t kPeerWaitNs = 1000000000ull;  // one second
 
 struct PeerBases {
   uint8_t* base[kMaxPeerRanks];
 };
-
-// Waits (bounded) for the flag of step `want` in a flagged word and returns its value; on a
-// timeout sets *timed_out (and every later word of the thread is taken as it is).
-__device__ __forceinline__ float wait_word(const unsigned long long* p, unsigned want, uint64_t t0, bool& timed_out) {
-  unsigned long long w = gather_load(p);
-  while ((unsigned)(w >> 32) != want && !timed_out) {
-    if (global_ns() - t0 > kPeerWaitNs) {
-      timed_out = true;
-      break;
-    }
-    w = gather_load(p);
-  }
-  return __uint_as_float((unsigned)w);
-}
 
 // The last CTA of the reading kernel to finish advances the channel's step counter.
 __device__ __forceinline__ void finish_step(unsigned* step, unsigned* done, unsigned s) {
@@ -62,67 +49,6 @@ __device__ __forceinline__ void finish_step(unsigned* step, unsigned* done, unsi
       *(volatile unsigned*)step = s + 1u;
     }
   }
-}
-
-// Two consecutive flagged words (16-byte aligned) in one load; each 8-byte word is read
-// single-copy atomically, so value and flag of a word always belong together.
-__device__ __forceinline__ ulonglong2 gather_load2(const unsigned long long* p) {
-  ulonglong2 w;
-  asm volatile("ld.relaxed.sys.global.v2.b64 {%0, %1}, [%2];" : "=l"(w.x), "=l"(w.y) : "l"(p) : "memory");
-  return w;
-}
-
-constexpr int kWaitCopyThreads = 512;
-constexpr int kWaitCopyPairs = 4;  // word pairs a thread loads before it checks any of their flags
-
-// Copies this rank's gathered half (every source's flagged words of this step) to `out` once the
-// flags show up, then advances the step counter. Launched as a programmatic dependent of the
-// GEMV; it lets its own dependents launch at once (the next GEMV's weight prefetch overlaps the
-// wait), and it waits for the GEMV to finish before it reads the step counter, which the previous
-// step's copy advanced (a launch two kernels back is not otherwise ordered before this one).
-// Each thread issues the loads of up to kWaitCopyPairs word pairs before it looks at a flag, and
-// re-reads only a pair whose flags have not arrived: the copy costs about one load round trip
-// when the peers' stores have landed.
-__global__ void __launch_bounds__(kWaitCopyThreads) wait_copy_kernel(unsigned* step, unsigned* done,
-                                                                     const unsigned long long* data,
-                                                                     int64_t half_words, float* out, int64_t n,
-                                                                     int* status) {
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  const unsigned s = *(volatile unsigned*)step;
-  const unsigned want = s + 1u;
-  const unsigned long long* src = data + (int64_t)(s & 1u) * half_words;  // 16-byte aligned
-  const uint64_t t0 = global_ns();
-  bool timed_out = false;
-  const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x, stride = (int64_t)gridDim.x * blockDim.x;
-  if (((uintptr_t)out & 7u) == 0) {
-    const int64_t npairs = n / 2;
-    float2* out2 = reinterpret_cast<float2*>(out);
-    for (int64_t p0 = tid; p0 < npairs; p0 += stride * kWaitCopyPairs) {
-      ulonglong2 w[kWaitCopyPairs];
-#pragma unroll
-      for (int u = 0; u < kWaitCopyPairs; ++u)
-        if (p0 + u * stride < npairs) w[u] = gather_load2(src + 2 * (p0 + u * stride));
-#pragma unroll
-      for (int u = 0; u < kWaitCopyPairs; ++u) {
-        const int64_t p = p0 + u * stride;
-        if (p >= npairs) break;
-        while (((unsigned)(w[u].x >> 32) != want || (unsigned)(w[u].y >> 32) != want) && !timed_out) {
-          if (global_ns() - t0 > kPeerWaitNs) {
-            timed_out = true;
-            break;
-          }
-          w[u] = gather_load2(src + 2 * p);
-        }
-        out2[p] = make_float2(__uint_as_float((unsigned)w[u].x), __uint_as_float((unsigned)w[u].y));
-      }
-    }
-    if ((n & 1) && tid == 0) out[n - 1] = wait_word(src + n - 1, want, t0, timed_out);
-  } else {
-    for (int64_t i = tid; i < n; i += stride) out[i] = wait_word(src + i, want, t0, timed_out);
-  }
-  if (timed_out) atomicExch(status, 1);
-  finish_step(step, done, s);
 }
 
 constexpr int kAllreduceThreads = 256;
@@ -282,44 +208,25 @@ int64_t peer_slice_words(const j4b_peer_group* g) {
   return (int64_t)(((g->bytes - kDataOffset) / kChannels) / 256 * 256 / 8);
 }
 
-// Fills the GEMV's peer targets for `channel`.
-int peer_gemv_targets(const j4b_peer_group* g, int channel, int64_t gathered_floats, GemvPeers* t) {
+// Fills the GEMV's peer targets for `channel`: every rank's gathered buffer, this rank's step and
+// finished-warp counters, and the gathered output `out` the GEMV's warps copy into.
+int peer_gemv_targets(const j4b_peer_group* g, int channel, float* out, int64_t gathered_floats, GemvPeers* t) {
   J4B_REQUIRE(channel >= 0 && channel < kChannels, "channel %d out of range", channel);
   const int64_t slice = peer_slice_words(g);
   J4B_REQUIRE(2 * gathered_floats <= slice,
               "peer buffer slice too small for the gathered output (%lld words per parity half, %lld needed)",
               (long long)(slice / 2), (long long)gathered_floats);
+  uint8_t* mine = g->base[g->rank];
   t->nranks = g->nranks;
   t->rank = g->rank;
   t->half_words = slice / 2;
-  t->step = reinterpret_cast<const unsigned*>(g->base[g->rank]) + channel;
+  t->step = reinterpret_cast<unsigned*>(mine) + channel;
+  t->done = reinterpret_cast<unsigned*>(mine + 64) + channel;
+  t->out = out;
+  t->gathered = gathered_floats;
+  t->status = g->status;
   for (int p = 0; p < g->nranks; ++p)
     t->y[p] = reinterpret_cast<unsigned long long*>(g->base[p] + kDataOffset) + channel * slice;
-  return J4B_OK;
-}
-
-// Launches the waiting copy of the gathered output after the GEMV.
-int peer_wait_copy(const j4b_peer_group* g, int channel, float* out, int64_t n, cudaStream_t stream) {
-  uint8_t* mine = g->base[g->rank];
-  const int64_t slice = peer_slice_words(g);
-  unsigned* step = reinterpret_cast<unsigned*>(mine) + channel;
-  unsigned* done = reinterpret_cast<unsigned*>(mine + 64) + channel;
-  const unsigned long long* data = reinterpret_cast<const unsigned long long*>(mine + kDataOffset) + channel * slice;
-  // about one word pair per thread, up to kWaitCopyPairs pairs per thread on one CTA per SM
-  const int64_t ctas = ((n + 1) / 2 + kWaitCopyThreads - 1) / kWaitCopyThreads;
-  const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>(ctas, 148));
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(kWaitCopyThreads);
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  J4B_CUDA(cudaLaunchKernelEx(&cfg, wait_copy_kernel, step, done, data, slice / 2, out, n, g->status),
-           "wait_copy_kernel");
-  count_launch();
   return J4B_OK;
 }
 

@@ -138,8 +138,12 @@ struct GemvArgs {
   // the local step counter (see gather_store).
   int nranks, rank;
   unsigned long long* peer_y[kMaxPeerRanks];
-  const unsigned* step;
+  unsigned* step;       // the channel's step counter, advanced by the launch's last warp
+  unsigned* done;       // finished-warp counter of the channel
   int64_t half_words;
+  float* gout;          // the gathered output the warps copy into, [batch][rows * nranks]
+  int64_t gathered;     // its floats
+  int* pstatus;         // the peer group's status word
 };
 
 // Where this launch's outputs go in the gathered buffers: the parity half's offset and the flag

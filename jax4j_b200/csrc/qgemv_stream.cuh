@@ -213,6 +213,69 @@ __device__ __forceinline__ void stream_prep_x(const GemvArgs& a, int64_t kc0, in
   }
 }
 
+// All-gather, second half (inside the GEMV, after a warp's tiles): the warp copies its share of
+// this rank's gathered half -- every rank's outputs of this step as flagged words -- to the
+// output as the flags appear. Each thread issues the loads of up to four word pairs before it
+// checks a flag and re-reads only a pair whose flags have not arrived. The launch's last warp to
+// finish advances the channel's step counter (every warp read it, in gather_slot, before its own
+// arrival) and resets the counter of finished warps. A wait gives up after a second and marks the
+// peer group's status word.
+template <int NW>
+__device__ __forceinline__ void gather_copy(const GemvArgs& a, const GatherSlot& gs, int warp, int lane) {
+  const unsigned long long* src = a.peer_y[a.rank] + gs.off;  // 16-byte aligned
+  const int64_t nthreads = (int64_t)gridDim.x * NW * 32;
+  const int64_t tid = ((int64_t)blockIdx.x * NW + warp) * 32 + lane;
+  const unsigned want = gs.flag;
+  const uint64_t t0 = global_ns();
+  bool timed_out = false;
+  if (((uintptr_t)a.gout & 7u) == 0) {
+    const int64_t npairs = a.gathered / 2;
+    float2* out2 = reinterpret_cast<float2*>(a.gout);
+    for (int64_t p0 = tid; p0 < npairs; p0 += nthreads * 4) {
+      ulonglong2 w[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (p0 + u * nthreads < npairs) w[u] = gather_load2(src + 2 * (p0 + u * nthreads));
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int64_t p = p0 + u * nthreads;
+        if (p >= npairs) break;
+        while (((unsigned)(w[u].x >> 32) != want || (unsigned)(w[u].y >> 32) != want) && !timed_out) {
+          if (global_ns() - t0 > kPeerWaitNs) timed_out = true;
+          else w[u] = gather_load2(src + 2 * p);
+        }
+        out2[p] = make_float2(__uint_as_float((unsigned)w[u].x), __uint_as_float((unsigned)w[u].y));
+      }
+    }
+    if ((a.gathered & 1) && tid == 0) {
+      unsigned long long w = gather_load(src + a.gathered - 1);
+      while ((unsigned)(w >> 32) != want && !timed_out) {
+        if (global_ns() - t0 > kPeerWaitNs) timed_out = true;
+        else w = gather_load(src + a.gathered - 1);
+      }
+      a.gout[a.gathered - 1] = __uint_as_float((unsigned)w);
+    }
+  } else {
+    for (int64_t i = tid; i < a.gathered; i += nthreads) {
+      unsigned long long w = gather_load(src + i);
+      while ((unsigned)(w >> 32) != want && !timed_out) {
+        if (global_ns() - t0 > kPeerWaitNs) timed_out = true;
+        else w = gather_load(src + i);
+      }
+      a.gout[i] = __uint_as_float((unsigned)w);
+    }
+  }
+  if (timed_out) atomicExch(a.pstatus, 1);
+  __syncwarp();
+  if (lane == 0) {
+    __threadfence();
+    if (atomicAdd(a.done, 1u) == (unsigned)(gridDim.x * NW - 1)) {
+      *a.done = 0u;
+      *(volatile unsigned*)a.step = want;  // step + 1
+    }
+  }
+}
+
 // Output element cc of lane (g, t)'s accumulator -> (row in tile, batch column); unpacked element
 // cc belongs to n-tile cc / 4 (batch columns 8 (cc / 4) ..).
 template <bool PK>
@@ -435,6 +498,7 @@ __global__ void __launch_bounds__(stream_threads<NW>(), NW == 8 ? 2 : 1) qgemv_s
         }
       }
     }
+    if (a.nranks > 1) gather_copy<NW>(a, gslot, warp, lane);
   }
 
   if (__syncthreads_or(failed)) {
@@ -483,7 +547,11 @@ cudaError_t launch_gemv_stream(const j4b_qweight* w, const float* x, const float
     a.nranks = peers->nranks;
     a.rank = peers->rank;
     a.step = peers->step;
+    a.done = peers->done;
     a.half_words = peers->half_words;
+    a.gout = peers->out;
+    a.gathered = peers->gathered;
+    a.pstatus = peers->status;
     for (int p = 0; p < peers->nranks; ++p) a.peer_y[p] = peers->y[p];
   }
   // one CTA per SM: as many tile groups as fit next to the K splits

@@ -872,7 +872,7 @@ extern "C" int j4b_quant_matvec_allgather(j4b_qweight_t w, j4b_buf x, j4b_buf ad
   const int nranks = peer_group_ranks(g);
   const int64_t gathered = batch * w->rows * nranks;
   GemvPeers t;
-  int st = peer_gemv_targets(g, channel, gathered, &t);
+  int st = peer_gemv_targets(g, channel, (float*)(uintptr_t)y_all, gathered, &t);
   if (st) return st;
   const float* xp = (const float*)(uintptr_t)x;
   const float* ap = add ? (const float*)(uintptr_t)add : nullptr;
@@ -887,7 +887,7 @@ extern "C" int j4b_quant_matvec_allgather(j4b_qweight_t w, j4b_buf x, j4b_buf ad
   }
   if (e != cudaSuccess) return cuda_error(e, "qgemv_kernel");
   count_launch();
-  return peer_wait_copy(g, channel, (float*)(uintptr_t)y_all, gathered, stream);
+  return J4B_OK;
 }
 
 // quantMatvec with host buffers: x [batch, cols] in, y [batch, rows] out, queued on the stream; the
