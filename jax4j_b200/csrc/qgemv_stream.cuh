@@ -241,8 +241,12 @@ __device__ __forceinline__ void gather_copy(const GemvArgs& a, const GatherSlot&
         const int64_t p = p0 + u * nthreads;
         if (p >= npairs) break;
         while (((unsigned)(w[u].x >> 32) != want || (unsigned)(w[u].y >> 32) != want) && !timed_out) {
-          if (global_ns() - t0 > kPeerWaitNs) timed_out = true;
-          else w[u] = gather_load2(src + 2 * p);
+          if (global_ns() - t0 > kPeerWaitNs) {
+            timed_out = true;
+          } else {
+            __nanosleep(128);  // polls spaced out: warps still on their tiles keep the memory pipes
+            w[u] = gather_load2(src + 2 * p);
+          }
         }
         out2[p] = make_float2(__uint_as_float((unsigned)w[u].x), __uint_as_float((unsigned)w[u].y));
       }
