@@ -1168,8 +1168,7 @@ extern "C" int j4b_quant_gemm(j4b_qweight_t w, j4b_buf x, j4b_buf y, int64_t m, 
   cudaStream_t stream = resolve_stream(w->dev, s);
   const int terms = precision == 1 ? 1 : 3;
   const int64_t kp = (w->cols + 63) / 64 * 64;
-  static const bool two_pass = getenv("J4B_QGEMM_TWO_PASS") != nullptr;  // development A/B only
-  if (!two_pass && (w->type == J4B_Q8_0 || w->type == J4B_Q4_0 || w->type == J4B_Q4_K) && m <= INT32_MAX &&
+  if ((w->type == J4B_Q8_0 || w->type == J4B_Q4_0 || w->type == J4B_Q4_K) && m <= INT32_MAX &&
       w->rows <= INT32_MAX)
     return quant_gemm_fused(w, (const float*)(uintptr_t)x, (float*)(uintptr_t)y, nullptr, m, kp, terms,
                             device_ctx(w->dev)->sm_count, stream);
